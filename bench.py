@@ -1,0 +1,448 @@
+"""Benchmark of the B200 GGUF quantized-matmul path.
+
+Workload: the Llama-3-8B-shaped Q4_K decode matmul
+stack -- 32 layers x {q 4096x4096, k 1024x4096, v 1024x4096, o 4096x4096,
+gate 14336x4096, up 14336x4096, down 4096x14336}, 3,925,868,544 weight bytes,
+batch 1 (``--batch 16`` for the batch-16 variant), seeded synthetic weights
+with the configuration's distributions and N(0,1) activations.  One step =
+one decode token through all 224 matmuls (one launch each, in layer order,
+replayed from a CUDA graph).  With N GPUs every matrix is row-sharded N ways
+and each output is all-gathered over NCCL after its matmul (strong scaling:
+the model is fixed, value counts its bytes once).
+
+value  = weight bytes of the whole model x steps / device time (max over ranks)
+e2e    = the same through the host C-ABI call (rce_qmm_mm_1d with host buffers,
+         copies in and out on every call), timed by the wall clock around the
+         synchronous calls
+roofline = the dominant kernel (the 14336x4096 / 4096x14336 Q4_K GEMVs) timed
+         launch by launch with CUDA events, algorithmic bytes / duration
+cpu_baseline = the C restatement of the reference's CPU path (oracle/) on one
+         layer of the same stack, all host threads
+The weights (3.9 GB) are far larger than L2 (126 MB), so no L2 flush is
+needed between steps.
+
+``--impl reference`` times the reference's CPU path (the oracle port; the Rust
+crate cannot be built here) on the same metric: each step is one layer's
+seven matmuls (122,683,392 weight bytes), all host threads.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = "quant GEMV weight GB/s vs HBM peak; prefill GEMM TFLOP/s; 1/2/4/8 GPU"
+Q4_K = 12
+D_MODEL, D_FF, D_KV = 4096, 14336, 1024
+# (name, n_rows, n_cols)
+LAYER = [("q", D_MODEL, D_MODEL), ("k", D_KV, D_MODEL), ("v", D_KV, D_MODEL), ("o", D_MODEL, D_MODEL),
+         ("gate", D_FF, D_MODEL), ("up", D_FF, D_MODEL), ("down", D_MODEL, D_FF)]
+
+
+def q4k_bytes(n, k):
+    return n * k // 256 * 144
+
+
+def layer_bytes():
+    return sum(q4k_bytes(n, k) for _, n, k in LAYER)
+
+
+def load_peaks():
+    for p in (os.path.join(ROOT, "MEASURED_PEAKS.json"),):
+        if os.path.exists(p):
+            d = json.load(open(p))
+            return d.get("hbm_gbs"), d.get("bf16_tflops"), "measured"
+    return 6650.0, 1590.0, "fallback"
+
+
+# ---- clocks -------------------------------------------------------------------
+
+class ClockSampler:
+    FIELDS = ("uuid,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
+              "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+              "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, uuid: str):
+        self.uuid = uuid
+        self.path = tempfile.mktemp(prefix="clocks_", suffix=".csv")
+        self.proc = None
+        self.windows = []
+        try:
+            self.f = open(self.path, "w")
+            self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                                          "-lms", "100"], stdout=self.f, stderr=subprocess.DEVNULL)
+        except Exception:
+            self.proc = None
+
+    def mark(self):
+        return time.time()
+
+    def stop(self):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:
+                self.proc.kill()
+            self.f.close()
+
+    def summary(self, t0, t1):
+        if self.proc is None or not os.path.exists(self.path):
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        rows = []
+        with open(self.path) as f:
+            lines = f.read().strip().splitlines()
+        # nvidia-smi -lms has no timestamps: spread the samples evenly over the
+        # sampling lifetime and keep the ones inside [t0, t1] (widened to one
+        # interval each side so short regions still get samples)
+        mine = [ln.split(", ") for ln in lines if self.uuid and self.uuid in ln]
+        if not mine:
+            mine = [ln.split(", ") for ln in lines]
+        if not mine:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
+        for r in mine:
+            try:
+                rows.append((float(r[1]), float(r[2]), r[4:8]))
+            except (ValueError, IndexError):
+                pass
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unparsed samples"]}
+        n = len(rows)
+        start, end = self.t_start, self.t_end
+        span = max(end - start, 1e-3)
+        sel = [rows[i] for i in range(n) if t0 - 0.15 <= start + span * (i + 0.5) / n <= t1 + 0.15]
+        if not sel:
+            sel = rows
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[j] for r in sel for j, v in enumerate(r[2]) if v.strip() == "Active"})
+        return {"sm_mhz": statistics.median(r[0] for r in sel), "sm_max_mhz": max(r[1] for r in sel),
+                "reasons": reasons, "samples": len(sel)}
+
+
+# ---- the reference arm ------------------------------------------------------------
+
+def cpu_layer_sample(seed=3):
+    from rce_b200 import synth
+
+    rng = np.random.default_rng(seed)
+    mats = [(name, n, k, synth.q4_k(n, k, rng)) for name, n, k in LAYER]
+    xs = {D_MODEL: synth.activations(1, D_MODEL, rng)[0], D_FF: synth.activations(1, D_FF, rng)[0]}
+    return mats, xs
+
+
+def time_cpu_layer(mats, xs, threads, reps=None, budget_s=10.0):
+    import oracle as O
+
+    times = []
+    t_total = 0.0
+    r = 0
+    while True:
+        t0 = time.perf_counter()
+        for name, n, k, w in mats:
+            O.mm_1d(xs[k], w, Q4_K, n, k, nthreads=threads)
+        dt = time.perf_counter() - t0
+        times.append(dt)
+        t_total += dt
+        r += 1
+        if reps is not None and r >= reps:
+            break
+        if reps is None and (t_total >= budget_s or r >= 200):
+            break
+    return times
+
+
+def run_reference(args, rank, world):
+    if rank != 0:
+        return
+    threads = os.cpu_count() or 1
+    mats, xs = cpu_layer_sample()
+    time_cpu_layer(mats, xs, threads, reps=max(1, args.warmup))
+    times = time_cpu_layer(mats, xs, threads, reps=args.steps)
+    lb = layer_bytes()
+    tot = sum(times)
+    value = lb * len(times) / tot / 1e9
+    line = {
+        "impl": "reference", "metric": METRIC, "value": round(value, 3), "unit": "GB/s", "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(1e3 * tot / len(times), 3),
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic (seeded, configuration distributions)",
+        "config": config_dict(args, world),
+        "cpu_baseline": {"value": round(value, 3), "unit": "GB/s", "cores": threads, "kind": "port",
+                         "sample": "one layer of the stack per step (7 Q4_K matmuls, 122,683,392 weight bytes), "
+                                   "oracle/qmm_oracle.c restating rce-op-qmm mm_1d_q4_k, rows over all host threads"},
+        "e2e": {"value": round(value, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "note": "the reference crate is Rust and no Rust toolchain exists here; its CPU path is timed through the "
+                "bit-exact C restatement",
+    }
+    print(json.dumps(line), flush=True)
+
+
+def config_dict(args, world):
+    return {"workload": "llama3-8b-shaped Q4_K decode matmul stack (configs[3])", "layers": args.layers,
+            "batch": args.batch, "matmuls_per_step": 7 * args.layers, "weight_bytes": layer_bytes() * args.layers,
+            "parallelism": f"row-shard x{world} + all-gather" if world > 1 else "single GPU",
+            "l2": "no flush: weights 3.9 GB >> 126 MB L2" if args.layers >= 8 else "small stack (profiling)"}
+
+
+# ---- our arm -------------------------------------------------------------------------
+
+def build_stack(args, rank, world, dev):
+    import torch
+
+    import rce_b200 as R
+    from rce_b200 import synth
+
+    ctx = R.default_context(dev.index)
+    layers = []
+    for li in range(args.layers):
+        mats = []
+        for mi, (name, n, k) in enumerate(LAYER):
+            ns = n // world
+            g = torch.Generator(device=dev)
+            g.manual_seed(3_000_000 + 7919 * li + 131 * mi + rank)
+            raw = synth.device_weights(Q4_K, ns, k, g, dev)
+            w = R.QuantWeight.from_device_bytes(raw, Q4_K, ns, k, ctx=ctx)
+            del raw
+            mats.append((name, ns, k, w))
+        layers.append(mats)
+    torch.cuda.synchronize(dev)
+    return ctx, layers
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=1000)
+    ap.add_argument("--warmup", type=int, default=20)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--batch", type=int, default=1)
+    ap.add_argument("--layers", type=int, default=32)
+    ap.add_argument("--e2e-steps", type=int, default=3)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--profile", action="store_true", help="short run for ncu: warm-up + steps only")
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3)
+
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+
+    if args.impl == "reference":
+        if world > 1:
+            import torch.distributed as dist
+
+            dist.init_process_group("gloo", init_method="env://")
+        run_reference(args, rank, world)
+        if world > 1:
+            dist.destroy_process_group()
+        return
+
+    import datetime
+
+    import torch
+    import torch.distributed as dist
+
+    import rce_b200 as R
+
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    if world > 1:
+        dist.init_process_group("nccl", init_method="env://", timeout=datetime.timedelta(seconds=120),
+                                device_id=dev)
+    ctx, layers = build_stack(args, rank, world, dev)
+    m = args.batch
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(3)
+    xs = {D_MODEL: torch.randn((m, D_MODEL), device=dev, generator=gen),
+          D_FF: torch.randn((m, D_FF), device=dev, generator=gen)}
+    ys = {name: torch.empty((m, n // world), device=dev) for name, n, _ in LAYER}
+    yfull = {name: torch.empty((world * m, n // world), device=dev) for name, n, _ in LAYER} if world > 1 else {}
+    stream = torch.cuda.Stream(dev)
+    launches_per_step = 7 * args.layers
+
+    def step():
+        for mats in layers:
+            for name, ns, k, w in mats:
+                R.mm_batched_device(xs[k], w, ys[name], stream=stream)
+                if world > 1:
+                    dist.all_gather_into_tensor(yfull[name], ys[name])
+
+    graph = None
+    with torch.cuda.stream(stream):
+        for _ in range(2):
+            step()  # eager warm-up: allocates split-K scratch for this stream
+    stream.synchronize()
+    if world == 1:
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=stream):
+            step()
+
+    def run(n):
+        with torch.cuda.stream(stream):
+            for _ in range(n):
+                if graph is not None:
+                    graph.replay()
+                else:
+                    step()
+
+    run(args.warmup)
+    stream.synchronize()
+    uuid = ""
+    try:
+        uuid = str(torch.cuda.get_device_properties(dev).uuid)
+    except Exception:
+        pass
+    clocks = ClockSampler(uuid) if rank == 0 else None
+    if clocks:
+        clocks.t_start = time.time()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize(dev)
+    ev0 = torch.cuda.Event(enable_timing=True)
+    ev1 = torch.cuda.Event(enable_timing=True)
+    t_wall0 = time.time()
+    ev0.record(stream)
+    run(args.steps)
+    ev1.record(stream)
+    ev1.synchronize()
+    t_wall1 = time.time()
+    torch.cuda.synchronize(dev)
+    if world > 1:
+        dist.barrier()
+    ms = ev0.elapsed_time(ev1)
+    if world > 1:
+        t = torch.tensor([ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    total_bytes = layer_bytes() * args.layers
+    value = total_bytes * args.steps / (ms / 1e3) / 1e9
+
+    if args.profile:
+        if clocks:
+            clocks.t_end = time.time()
+            clocks.stop()
+        if rank == 0:
+            print(json.dumps({"profile_run": True, "ms_per_step": ms / args.steps, "value": value}))
+        if world > 1:
+            dist.destroy_process_group()
+        return
+
+    # ---- roofline: per-launch CUDA events on the launching stream -------------
+    per_type = {name: [] for name, _, _ in LAYER}
+    with torch.cuda.stream(stream):
+        for rep in range(3):
+            for mats in layers:
+                for name, ns, k, w in mats:
+                    e0 = torch.cuda.Event(enable_timing=True)
+                    e1 = torch.cuda.Event(enable_timing=True)
+                    e0.record(stream)
+                    R.mm_batched_device(xs[k], w, ys[name], stream=stream)
+                    e1.record(stream)
+                    per_type[name].append((e0, e1))
+    stream.synchronize()
+    if clocks:
+        clocks.t_end = time.time()
+        clocks.stop()
+    kern = {}
+    for name, n, k in LAYER:
+        durs = [a.elapsed_time(b) for a, b in per_type[name]]
+        ns = n // world
+        alg = q4k_bytes(ns, k) + 4 * m * k + 4 * m * ns
+        avg = sum(durs) / len(durs)
+        kern[name] = {"avg_us": avg * 1e3, "alg_bytes": alg, "gbs": alg / (avg / 1e3) / 1e9, "total_ms": sum(durs)}
+    dom = max(kern, key=lambda nm: kern[nm]["total_ms"])
+    hbm, bf16, peak_kind = load_peaks()
+    traffic = None
+    tpath = os.path.join(ROOT, "profiles", "gemv_q4k_traffic.json")
+    if os.path.exists(tpath):
+        try:
+            tj = json.load(open(tpath))
+            key = f"{D_FF if dom in ('gate', 'up') else D_MODEL}x{D_MODEL if dom != 'down' else D_FF}_m{m}_w{world}"
+            traffic = tj.get(key)
+        except Exception:
+            traffic = None
+
+    # ---- e2e through the host C-ABI ----------------------------------------------
+    e2e = None
+    hx = {k: v.cpu().numpy() for k, v in xs.items()}
+    hy = {name: np.empty((m, n // world), np.float32) for name, n, _ in LAYER}
+    h2d = d2h = 0
+    for name, n, k in LAYER:
+        h2d += 4 * m * k * args.layers
+        d2h += 4 * m * (n // world) * args.layers
+
+    def e2e_step():
+        for mats in layers:
+            for name, ns, k, w in mats:
+                R.mm_batched(hx[k], m, w, hy[name].reshape(-1))
+                if world > 1:
+                    t = torch.from_numpy(hy[name]).to(dev)
+                    dist.all_gather_into_tensor(yfull[name], t)
+                    yfull[name].cpu()
+
+    e2e_step()
+    if world > 1:
+        dist.barrier()
+    t0 = time.perf_counter()
+    for _ in range(args.e2e_steps):
+        e2e_step()
+    t1 = time.perf_counter()
+    e2e_s = t1 - t0
+    if world > 1:
+        t = torch.tensor([e2e_s], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_s = float(t.item())
+    e2e = {"value": round(total_bytes * args.e2e_steps / e2e_s / 1e9, 3), "unit": "GB/s",
+           "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "steps": args.e2e_steps,
+           "timing": "wall clock around the synchronous host C-ABI calls (rce_qmm_mm_batched)"}
+
+    # ---- CPU baseline (rank 0, N = 1) ---------------------------------------------
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        threads = os.cpu_count() or 1
+        mats_h, xs_h = cpu_layer_sample()
+        times = time_cpu_layer(mats_h, xs_h, threads, budget_s=10.0)
+        cpu = {"value": round(layer_bytes() * len(times) / sum(times) / 1e9, 3), "unit": "GB/s", "cores": threads,
+               "kind": "port",
+               "sample": f"{len(times)} passes over one layer of the stack (7 Q4_K matmuls, 122,683,392 weight bytes), "
+                         "batch 1, oracle/qmm_oracle.c (bit-exact restatement of rce-op-qmm mm_1d_q4_k), rows split "
+                         "over all host threads as rayon does"}
+
+    if rank == 0:
+        clk = clocks.summary(t_wall0, t_wall1) if clocks else {}
+        line = {
+            "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(ms / args.steps, 5), "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": "q4_k x f32 (f32 accumulate)",
+            "data": "synthetic (seeded, configuration distributions; random weights)",
+            "config": config_dict(args, world),
+            "gpu_launches": launches_per_step * args.steps,
+            "roofline": {"bound": "hbm", "kernel": f"gemv_kernel<Q4_K> ({dom})",
+                         "achieved": round(kern[dom]["gbs"], 1), "peak": hbm, "unit": "GB/s",
+                         "frac": round(kern[dom]["gbs"] / hbm, 4), "peak_kind": peak_kind,
+                         "traffic": traffic, "alg_bytes_per_launch": kern[dom]["alg_bytes"],
+                         "avg_launch_us": round(kern[dom]["avg_us"], 2)},
+            "kernels": {nm: {"avg_us": round(v["avg_us"], 2), "gbs": round(v["gbs"], 1)} for nm, v in kern.items()},
+            "stack_frac_of_hbm": round(value / world / hbm, 4),
+            "e2e": e2e,
+            "cpu_baseline": cpu,
+            "clocks": clk,
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

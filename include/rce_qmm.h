@@ -1,0 +1,138 @@
+/*
+ * rce_qmm.h -- C ABI of the B200 GGUF quantized-matmul library
+ * (librce_qmm.so), the drop-in for the reference crate rce-op-qmm's operator
+ * API for the Q8_0, Q4_0 and Q4_K weight formats.
+ *
+ * Reference interfaces replaced (paths relative to openIE-dev/rce,
+ * compute/crates/):
+ *   QuantWeight          rce-op-qmm/src/lib.rs:77-210
+ *   mm_1d                rce-op-qmm/src/lib.rs:216-270
+ *   mm_1d_serial         rce-op-qmm/src/lib.rs:281-304
+ *   mm_batched           rce-op-qmm/src/lib.rs:967-1023
+ *   QuantWeight::dequant_row / dequantize_to_f32
+ *                        rce-op-qmm/src/lib.rs:150-166, rce-ingest-gguf/src/dequant.rs:115-134
+ *   tensor_byte_size     rce-ingest-gguf/src/dequant.rs:18-58
+ *   QmmDispatch::qmm_1d  rce-placement-adapter/src/lib.rs:130-134
+ *   QmmLeaf::execute     rce-op-qmm/src/lib.rs:2096-2130
+ *   moe_router / moe_combine
+ *                        rce-op-moe/src/lib.rs:35-73, 98-110
+ *   moe_ffn_forward      rce-qwen36-moe/src/lib.rs:666-705 (routed experts)
+ *
+ * Conventions (after the reference's own C ABI, rce-c/src/lib.rs:8-100):
+ *   - every function returns RCE_QMM_OK (0) or an error code; the message of
+ *     the last failure on the calling thread is rce_qmm_last_error();
+ *   - inputs are borrowed for the duration of the call; handles are freed by
+ *     the matching *_free / *_destroy function;
+ *   - "host" entry points take host pointers and copy in and out themselves
+ *     (synchronous); "_device" entry points take device pointers and a
+ *     cudaStream_t (passed as void*, NULL = the context's default stream) and
+ *     are asynchronous on that stream;
+ *   - every entry point is thread-safe: each calling thread gets its own
+ *     stream and staging buffers, as the reference's callers run qmm from many
+ *     rayon threads at once (rce-qwen36-moe/src/lib.rs:688-698).
+ * Where the reference panics (mm_1d on an unsupported dtype, lib.rs:268) or
+ * returns InterpretError::Unsupported (QmmLeaf), this ABI returns
+ * RCE_QMM_ERR_UNSUPPORTED or RCE_QMM_ERR_INVALID.
+ */
+#ifndef RCE_QMM_H
+#define RCE_QMM_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define RCE_QMM_ABI_VERSION 1
+
+/* Status codes. */
+#define RCE_QMM_OK 0
+#define RCE_QMM_ERR_INVALID 1     /* bad argument: null pointer, size, shape */
+#define RCE_QMM_ERR_UNSUPPORTED 2 /* dtype or shape outside this library */
+#define RCE_QMM_ERR_CUDA 3        /* a CUDA runtime call failed */
+#define RCE_QMM_ERR_NOMEM 4       /* device or host allocation failed */
+
+/* GGUF dtype tags (rce-ingest-gguf/src/parser.rs:308-338). */
+#define RCE_QMM_GGUF_Q4_0 2
+#define RCE_QMM_GGUF_Q8_0 8
+#define RCE_QMM_GGUF_Q4_K 12
+
+typedef struct rce_qmm_ctx rce_qmm_ctx;
+typedef struct rce_qmm_weight rce_qmm_weight;
+
+/* ABI version (RCE_QMM_ABI_VERSION). */
+int rce_qmm_abi_version(void);
+
+/* Message of the last failed call on this thread ("" if none). */
+const char *rce_qmm_last_error(void);
+
+/* Bytes of a GGUF tensor of `numel` values (tensor_byte_size,
+ * rce-ingest-gguf/src/dequant.rs:18-58); 0 for dtypes outside this library. */
+size_t rce_qmm_tensor_byte_size(int gguf_dtype, uint64_t numel);
+
+/* A context binds one CUDA device. */
+int rce_qmm_ctx_create(int device, rce_qmm_ctx **out);
+int rce_qmm_ctx_destroy(rce_qmm_ctx *ctx);
+/* Number of SMs of the context's device. */
+int rce_qmm_ctx_sm_count(const rce_qmm_ctx *ctx, int *out);
+
+/* Register a GGUF weight [n_rows = N_out][n_cols = K_in] (row-major blocks,
+ * the layout QuantWeight keeps, rce-op-qmm/src/lib.rs:15-19).  The bytes are
+ * copied to the device once and repacked into the device tile layout (a byte
+ * permutation: same byte count, recoverable bit for bit).  n_cols must be a
+ * multiple of the block size (32; 256 for Q4_K) and nbytes must equal
+ * rce_qmm_tensor_byte_size(dtype, n_rows * n_cols). */
+int rce_qmm_weight_register(rce_qmm_ctx *ctx, const void *gguf_bytes, size_t nbytes, int gguf_dtype,
+                            int64_t n_rows, int64_t n_cols, rce_qmm_weight **out);
+/* As rce_qmm_weight_register, from GGUF bytes already in device memory. */
+int rce_qmm_weight_register_device(rce_qmm_ctx *ctx, const void *d_gguf_bytes, size_t nbytes,
+                                   int gguf_dtype, int64_t n_rows, int64_t n_cols, void *stream,
+                                   rce_qmm_weight **out);
+/* Zero-copy sub-view (QuantWeight::sub_view, rce-op-qmm/src/lib.rs:99-118),
+ * e.g. one expert of a stacked [n_expert * n_rows, n_cols] tensor.  The view
+ * must start on a row that is a multiple of 16 and keep n_cols; byte_offset and
+ * byte_len are GGUF byte counts relative to the parent.  The parent must
+ * outlive the view. */
+int rce_qmm_weight_sub_view(const rce_qmm_weight *parent, size_t byte_offset, size_t byte_len,
+                            int64_t n_rows, int64_t n_cols, rce_qmm_weight **out);
+int rce_qmm_weight_free(rce_qmm_weight *w);
+/* dtype, shape and GGUF byte count of a weight. */
+int rce_qmm_weight_info(const rce_qmm_weight *w, int *gguf_dtype, int64_t *n_rows, int64_t *n_cols,
+                        size_t *nbytes);
+/* Device address and byte count of the tile storage (for tools/tests). */
+int rce_qmm_weight_device_storage(const rce_qmm_weight *w, const void **dev_ptr, size_t *dev_bytes);
+/* The weight's GGUF bytes (QuantWeight::bytes, rce-op-qmm/src/lib.rs:87-91),
+ * rebuilt from the device tiles into host memory (nbytes = the GGUF size). */
+int rce_qmm_weight_read_bytes(const rce_qmm_weight *w, void *host_out, size_t nbytes);
+
+/* out[j] = a . W[j,:] for j < n_rows (mm_1d, rce-op-qmm/src/lib.rs:216).
+ * a_len must equal n_cols, out_len >= n_rows.  Host buffers, synchronous. */
+int rce_qmm_mm_1d(rce_qmm_ctx *ctx, const float *a, size_t a_len, const rce_qmm_weight *w, float *out,
+                  size_t out_len);
+/* mm_1d_serial (rce-op-qmm/src/lib.rs:281): identical results to mm_1d. */
+int rce_qmm_mm_1d_serial(rce_qmm_ctx *ctx, const float *a, size_t a_len, const rce_qmm_weight *w,
+                         float *out, size_t out_len);
+/* out[T, n_rows] = a[T, n_cols] . W^T (mm_batched, rce-op-qmm/src/lib.rs:967).
+ * Host buffers, synchronous. */
+int rce_qmm_mm_batched(rce_qmm_ctx *ctx, const float *a, size_t t_rows, const rce_qmm_weight *w,
+                       float *out, size_t out_len);
+/* Device variant: d_a is [t_rows][lda] f32, d_out [t_rows][ldo] f32. */
+int rce_qmm_mm_batched_device(rce_qmm_ctx *ctx, const float *d_a, size_t lda, size_t t_rows,
+                              const rce_qmm_weight *w, float *d_out, size_t ldo, void *stream);
+
+/* dequant_row (rce-op-qmm/src/lib.rs:150-166): n_cols f32 values of row
+ * `row`, bit-exact with dequantize_to_f32.  Host output, synchronous. */
+int rce_qmm_dequant_row(rce_qmm_ctx *ctx, const rce_qmm_weight *w, int64_t row, float *out,
+                        size_t out_len);
+/* Device variant: rows [row0, row1) into d_out[(row - row0) * ldo + col]. */
+int rce_qmm_dequant_device(rce_qmm_ctx *ctx, const rce_qmm_weight *w, int64_t row0, int64_t row1,
+                           float *d_out, size_t ldo, void *stream);
+
+/* Wait for all work this thread queued on the context's streams. */
+int rce_qmm_synchronize(rce_qmm_ctx *ctx);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* RCE_QMM_H */

@@ -1,0 +1,490 @@
+// qmm_capi.cu -- the extern "C" boundary declared in include/rce_qmm.h:
+// contexts, the device weight registry, per-thread streams and staging, the
+// split-K scratch pool and argument validation.  All compute is delegated to
+// the kernel launchers in qmm_internal.h; there is no CPU fallback: a failed
+// launch is an error returned to the caller.
+#include <cuda_runtime.h>
+
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+#include <string>
+#include <thread>
+#include <unordered_map>
+
+#include "../../include/rce_qmm.h"
+#include "qmm_internal.h"
+
+using rce::Geometry;
+
+namespace {
+
+thread_local std::string g_last_error;
+
+int fail(int code, const char *fmt, ...) {
+    char buf[512];
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(buf, sizeof buf, fmt, ap);
+    va_end(ap);
+    g_last_error = buf;
+    return code;
+}
+
+int ok() { return RCE_QMM_OK; }
+
+#define CUDA_TRY(expr)                                                                         \
+    do {                                                                                       \
+        cudaError_t e_ = (expr);                                                               \
+        if (e_ != cudaSuccess)                                                                 \
+            return fail(e_ == cudaErrorMemoryAllocation ? RCE_QMM_ERR_NOMEM : RCE_QMM_ERR_CUDA, \
+                        "%s: %s (%s:%d)", #expr, cudaGetErrorString(e_), __FILE__, __LINE__); \
+    } while (0)
+
+struct Scratch {
+    float *partial = nullptr;
+    size_t floats = 0;
+    unsigned *counters = nullptr;
+    size_t ncounters = 0;
+};
+
+struct ThreadState {
+    cudaStream_t stream = nullptr;
+    float *d_in = nullptr;
+    size_t d_in_cap = 0;
+    float *d_out = nullptr;
+    size_t d_out_cap = 0;
+    void *h_pin = nullptr;
+    size_t h_cap = 0;
+};
+
+}  // namespace
+
+struct rce_qmm_ctx {
+    int device = 0;
+    int sm_count = 148;
+    std::mutex mu;
+    std::unordered_map<cudaStream_t, Scratch> scratch;
+    std::unordered_map<std::thread::id, ThreadState> threads;
+};
+
+struct rce_qmm_weight {
+    rce_qmm_ctx *ctx = nullptr;
+    int dtype = 0;
+    Geometry g;
+    uint8_t *dev = nullptr;
+    bool owner = false;
+};
+
+namespace {
+
+struct DeviceGuard {
+    int prev = -1;
+    bool changed = false;
+    explicit DeviceGuard(int dev) {
+        if (cudaGetDevice(&prev) == cudaSuccess && prev != dev) {
+            changed = cudaSetDevice(dev) == cudaSuccess;
+        }
+    }
+    ~DeviceGuard() {
+        if (changed) cudaSetDevice(prev);
+    }
+};
+
+int thread_state(rce_qmm_ctx *ctx, ThreadState **out) {
+    std::lock_guard<std::mutex> lk(ctx->mu);
+    ThreadState &ts = ctx->threads[std::this_thread::get_id()];
+    if (!ts.stream) CUDA_TRY(cudaStreamCreateWithFlags(&ts.stream, cudaStreamNonBlocking));
+    *out = &ts;
+    return ok();
+}
+
+int grow_device(float **p, size_t *cap, size_t need_floats) {
+    if (*cap >= need_floats) return ok();
+    if (*p) cudaFree(*p);
+    *p = nullptr;
+    *cap = 0;
+    CUDA_TRY(cudaMalloc(p, need_floats * sizeof(float)));
+    *cap = need_floats;
+    return ok();
+}
+
+int grow_pinned(ThreadState *ts, size_t bytes) {
+    if (ts->h_cap >= bytes) return ok();
+    if (ts->h_pin) cudaFreeHost(ts->h_pin);
+    ts->h_pin = nullptr;
+    ts->h_cap = 0;
+    CUDA_TRY(cudaMallocHost(&ts->h_pin, bytes));
+    ts->h_cap = bytes;
+    return ok();
+}
+
+// Scratch for split-K partial sums, one buffer per stream (work on one stream
+// is ordered, so its kernels never share scratch concurrently).  Growing it
+// synchronises the stream, so the first call with the largest shape must
+// come before any CUDA-graph capture on that stream.
+int stream_scratch(rce_qmm_ctx *ctx, cudaStream_t s, size_t floats, size_t counters, Scratch **out) {
+    std::lock_guard<std::mutex> lk(ctx->mu);
+    Scratch &sc = ctx->scratch[s];
+    if (sc.floats < floats) {
+        CUDA_TRY(cudaStreamSynchronize(s));
+        if (sc.partial) cudaFree(sc.partial);
+        sc.partial = nullptr;
+        sc.floats = 0;
+        CUDA_TRY(cudaMalloc(&sc.partial, floats * sizeof(float)));
+        sc.floats = floats;
+    }
+    if (sc.ncounters < counters) {
+        CUDA_TRY(cudaStreamSynchronize(s));
+        if (sc.counters) cudaFree(sc.counters);
+        sc.counters = nullptr;
+        sc.ncounters = 0;
+        const size_t n = counters < 1024 ? 1024 : counters;
+        CUDA_TRY(cudaMalloc(&sc.counters, n * sizeof(unsigned)));
+        CUDA_TRY(cudaMemsetAsync(sc.counters, 0, n * sizeof(unsigned), s));
+        sc.ncounters = n;
+    }
+    *out = &sc;
+    return ok();
+}
+
+int check_weight(const rce_qmm_weight *w) {
+    if (!w || !w->ctx || !w->dev) return fail(RCE_QMM_ERR_INVALID, "null or freed weight handle");
+    return ok();
+}
+
+// y[t_rows][ldo] = x[t_rows][lda] . W^T on stream s (device pointers).
+int run_matmul(rce_qmm_ctx *ctx, const rce_qmm_weight *w, const float *d_x, size_t lda, size_t t_rows,
+               float *d_y, size_t ldo, cudaStream_t s) {
+    const Geometry &g = w->g;
+    size_t t0 = 0;
+    while (t0 < t_rows) {
+        const int m = (int)((t_rows - t0) < 16 ? (t_rows - t0) : 16);
+        rce::GemvPlan plan = rce::plan_gemv(w->dtype, g, m, ctx->sm_count);
+        Scratch *sc = nullptr;
+        if (plan.k_splits > 1) {
+            int rc = stream_scratch(ctx, s, plan.scratch_floats, (size_t)plan.counters, &sc);
+            if (rc) return rc;
+        }
+        CUDA_TRY(rce::launch_gemv(w->dtype, w->dev, g, d_x + t0 * lda, lda, d_y + t0 * ldo, ldo, m, plan,
+                                  sc ? sc->partial : nullptr, sc ? sc->counters : nullptr, s));
+        t0 += (size_t)m;
+    }
+    return ok();
+}
+
+int register_common(rce_qmm_ctx *ctx, const void *src, bool src_on_device, size_t nbytes, int dtype,
+                    int64_t n_rows, int64_t n_cols, cudaStream_t s, rce_qmm_weight **out) {
+    if (!ctx || !src || !out) return fail(RCE_QMM_ERR_INVALID, "weight_register: null argument");
+    *out = nullptr;
+    if (!rce::dtype_supported(dtype))
+        return fail(RCE_QMM_ERR_UNSUPPORTED, "weight_register: GGUF dtype %d is not supported (Q4_0=2, Q8_0=8, Q4_K=12)",
+                    dtype);
+    if (n_rows <= 0 || n_cols <= 0)
+        return fail(RCE_QMM_ERR_INVALID, "weight_register: shape %lld x %lld", (long long)n_rows,
+                    (long long)n_cols);
+    if (n_cols % rce::gguf_block(dtype) != 0)
+        return fail(RCE_QMM_ERR_INVALID, "weight_register: n_cols %lld is not a multiple of the block size %d",
+                    (long long)n_cols, rce::gguf_block(dtype));
+    if (n_rows > (int64_t)1 << 31 || n_cols > (int64_t)1 << 31)
+        return fail(RCE_QMM_ERR_UNSUPPORTED, "weight_register: dimension too large");
+    Geometry g = rce::make_geometry(dtype, n_rows, n_cols);
+    if (nbytes != g.gguf_bytes)
+        return fail(RCE_QMM_ERR_INVALID, "weight_register: %zu bytes given, %zu expected for %lld x %lld dtype %d",
+                    nbytes, g.gguf_bytes, (long long)n_rows, (long long)n_cols, dtype);
+    DeviceGuard dg(ctx->device);
+    uint8_t *tmp = nullptr, *dev = nullptr;
+    const uint8_t *gguf_dev = static_cast<const uint8_t *>(src);
+    if (!src_on_device) {
+        cudaError_t e = cudaMalloc(&tmp, nbytes);
+        if (e != cudaSuccess) return fail(RCE_QMM_ERR_NOMEM, "weight_register: cudaMalloc(%zu): %s", nbytes,
+                                          cudaGetErrorString(e));
+        e = cudaMemcpyAsync(tmp, src, nbytes, cudaMemcpyHostToDevice, s);
+        if (e != cudaSuccess) {
+            cudaFree(tmp);
+            return fail(RCE_QMM_ERR_CUDA, "weight_register: copy to device: %s", cudaGetErrorString(e));
+        }
+        gguf_dev = tmp;
+    }
+    cudaError_t e = cudaMalloc(&dev, g.dev_bytes);
+    if (e != cudaSuccess) {
+        if (tmp) cudaFree(tmp);
+        return fail(RCE_QMM_ERR_NOMEM, "weight_register: cudaMalloc(%zu): %s", g.dev_bytes, cudaGetErrorString(e));
+    }
+    e = rce::launch_repack(dtype, gguf_dev, dev, g, s);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+    if (tmp) cudaFree(tmp);
+    if (e != cudaSuccess) {
+        cudaFree(dev);
+        return fail(RCE_QMM_ERR_CUDA, "weight_register: repack: %s", cudaGetErrorString(e));
+    }
+    rce_qmm_weight *w = new rce_qmm_weight;
+    w->ctx = ctx;
+    w->dtype = dtype;
+    w->g = g;
+    w->dev = dev;
+    w->owner = true;
+    *out = w;
+    return ok();
+}
+
+}  // namespace
+
+extern "C" {
+
+int rce_qmm_abi_version(void) { return RCE_QMM_ABI_VERSION; }
+
+const char *rce_qmm_last_error(void) { return g_last_error.c_str(); }
+
+size_t rce_qmm_tensor_byte_size(int dt, uint64_t n) {
+    switch (dt) {
+    case RCE_QMM_GGUF_Q4_0: return (size_t)((n + 31) / 32 * 18);
+    case RCE_QMM_GGUF_Q8_0: return (size_t)((n + 31) / 32 * 34);
+    case RCE_QMM_GGUF_Q4_K: return (size_t)((n + 255) / 256 * 144);
+    default: return 0;
+    }
+}
+
+int rce_qmm_ctx_create(int device, rce_qmm_ctx **out) {
+    if (!out) return fail(RCE_QMM_ERR_INVALID, "ctx_create: null out");
+    *out = nullptr;
+    int n = 0;
+    CUDA_TRY(cudaGetDeviceCount(&n));
+    if (device < 0 || device >= n) return fail(RCE_QMM_ERR_INVALID, "ctx_create: device %d of %d", device, n);
+    cudaDeviceProp prop;
+    CUDA_TRY(cudaGetDeviceProperties(&prop, device));
+    if (prop.major != 10)
+        return fail(RCE_QMM_ERR_UNSUPPORTED, "ctx_create: device %d is sm_%d%d; this library is built for sm_100a",
+                    device, prop.major, prop.minor);
+    rce_qmm_ctx *c = new rce_qmm_ctx;
+    c->device = device;
+    c->sm_count = prop.multiProcessorCount;
+    *out = c;
+    return ok();
+}
+
+int rce_qmm_ctx_destroy(rce_qmm_ctx *ctx) {
+    if (!ctx) return fail(RCE_QMM_ERR_INVALID, "ctx_destroy: null");
+    DeviceGuard dg(ctx->device);
+    for (auto &kv : ctx->threads) {
+        ThreadState &ts = kv.second;
+        if (ts.stream) cudaStreamSynchronize(ts.stream);
+        if (ts.d_in) cudaFree(ts.d_in);
+        if (ts.d_out) cudaFree(ts.d_out);
+        if (ts.h_pin) cudaFreeHost(ts.h_pin);
+        if (ts.stream) cudaStreamDestroy(ts.stream);
+    }
+    for (auto &kv : ctx->scratch) {
+        if (kv.second.partial) cudaFree(kv.second.partial);
+        if (kv.second.counters) cudaFree(kv.second.counters);
+    }
+    delete ctx;
+    return ok();
+}
+
+int rce_qmm_ctx_sm_count(const rce_qmm_ctx *ctx, int *out) {
+    if (!ctx || !out) return fail(RCE_QMM_ERR_INVALID, "ctx_sm_count: null argument");
+    *out = ctx->sm_count;
+    return ok();
+}
+
+int rce_qmm_weight_register(rce_qmm_ctx *ctx, const void *bytes, size_t nbytes, int dtype, int64_t n_rows,
+                            int64_t n_cols, rce_qmm_weight **out) {
+    if (!ctx) return fail(RCE_QMM_ERR_INVALID, "weight_register: null ctx");
+    DeviceGuard dg(ctx->device);
+    ThreadState *ts = nullptr;
+    int rc = thread_state(ctx, &ts);
+    if (rc) return rc;
+    return register_common(ctx, bytes, false, nbytes, dtype, n_rows, n_cols, ts->stream, out);
+}
+
+int rce_qmm_weight_register_device(rce_qmm_ctx *ctx, const void *d_bytes, size_t nbytes, int dtype,
+                                   int64_t n_rows, int64_t n_cols, void *stream, rce_qmm_weight **out) {
+    if (!ctx) return fail(RCE_QMM_ERR_INVALID, "weight_register_device: null ctx");
+    DeviceGuard dg(ctx->device);
+    return register_common(ctx, d_bytes, true, nbytes, dtype, n_rows, n_cols, (cudaStream_t)stream, out);
+}
+
+int rce_qmm_weight_sub_view(const rce_qmm_weight *parent, size_t byte_offset, size_t byte_len, int64_t n_rows,
+                            int64_t n_cols, rce_qmm_weight **out) {
+    if (!out) return fail(RCE_QMM_ERR_INVALID, "sub_view: null out");
+    *out = nullptr;
+    int rc = check_weight(parent);
+    if (rc) return rc;
+    const Geometry &pg = parent->g;
+    if (n_cols != pg.n_cols)
+        return fail(RCE_QMM_ERR_UNSUPPORTED, "sub_view: n_cols %lld differs from the parent's %lld",
+                    (long long)n_cols, (long long)pg.n_cols);
+    if (n_rows <= 0 || byte_offset % pg.gguf_row_bytes != 0)
+        return fail(RCE_QMM_ERR_INVALID, "sub_view: byte offset %zu is not on a row boundary", byte_offset);
+    const int64_t row0 = (int64_t)(byte_offset / pg.gguf_row_bytes);
+    if (row0 % rce::TILE_ROWS != 0)
+        return fail(RCE_QMM_ERR_UNSUPPORTED, "sub_view: first row %lld is not a multiple of %d", (long long)row0,
+                    rce::TILE_ROWS);
+    if (byte_len != (size_t)n_rows * pg.gguf_row_bytes || row0 + n_rows > pg.n_rows)
+        return fail(RCE_QMM_ERR_INVALID, "sub_view: %zu+%zu bytes / %lld rows outside the parent", byte_offset,
+                    byte_len, (long long)n_rows);
+    rce_qmm_weight *w = new rce_qmm_weight;
+    w->ctx = parent->ctx;
+    w->dtype = parent->dtype;
+    w->g = rce::make_geometry(parent->dtype, n_rows, n_cols);
+    w->dev = parent->dev + (size_t)(row0 / rce::TILE_ROWS) * pg.n_chunks * rce::chunk_bytes(parent->dtype);
+    w->owner = false;
+    *out = w;
+    return ok();
+}
+
+int rce_qmm_weight_free(rce_qmm_weight *w) {
+    if (!w) return fail(RCE_QMM_ERR_INVALID, "weight_free: null");
+    if (w->owner && w->dev) {
+        DeviceGuard dg(w->ctx->device);
+        cudaFree(w->dev);
+    }
+    w->dev = nullptr;
+    delete w;
+    return ok();
+}
+
+int rce_qmm_weight_info(const rce_qmm_weight *w, int *dtype, int64_t *n_rows, int64_t *n_cols, size_t *nbytes) {
+    int rc = check_weight(w);
+    if (rc) return rc;
+    if (dtype) *dtype = w->dtype;
+    if (n_rows) *n_rows = w->g.n_rows;
+    if (n_cols) *n_cols = w->g.n_cols;
+    if (nbytes) *nbytes = w->g.gguf_bytes;
+    return ok();
+}
+
+int rce_qmm_weight_device_storage(const rce_qmm_weight *w, const void **dev_ptr, size_t *dev_bytes) {
+    int rc = check_weight(w);
+    if (rc) return rc;
+    if (dev_ptr) *dev_ptr = w->dev;
+    if (dev_bytes) *dev_bytes = w->g.dev_bytes;
+    return ok();
+}
+
+int rce_qmm_weight_read_bytes(const rce_qmm_weight *w, void *host_out, size_t nbytes) {
+    int rc = check_weight(w);
+    if (rc) return rc;
+    if (!host_out || nbytes != w->g.gguf_bytes)
+        return fail(RCE_QMM_ERR_INVALID, "weight_read_bytes: need a buffer of %zu bytes", w->g.gguf_bytes);
+    DeviceGuard dg(w->ctx->device);
+    ThreadState *ts = nullptr;
+    rc = thread_state(w->ctx, &ts);
+    if (rc) return rc;
+    uint8_t *tmp = nullptr;
+    CUDA_TRY(cudaMalloc(&tmp, nbytes));
+    cudaError_t e = rce::launch_unpack(w->dtype, w->dev, tmp, w->g, 0, w->g.n_rows, ts->stream);
+    if (e == cudaSuccess) e = cudaMemcpyAsync(host_out, tmp, nbytes, cudaMemcpyDeviceToHost, ts->stream);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(ts->stream);
+    cudaFree(tmp);
+    if (e != cudaSuccess) return fail(RCE_QMM_ERR_CUDA, "weight_read_bytes: %s", cudaGetErrorString(e));
+    return ok();
+}
+
+int rce_qmm_mm_batched_device(rce_qmm_ctx *ctx, const float *d_a, size_t lda, size_t t_rows,
+                              const rce_qmm_weight *w, float *d_out, size_t ldo, void *stream) {
+    if (!ctx) return fail(RCE_QMM_ERR_INVALID, "mm_batched_device: null ctx");
+    int rc = check_weight(w);
+    if (rc) return rc;
+    if (w->ctx != ctx) return fail(RCE_QMM_ERR_INVALID, "mm_batched_device: weight belongs to another context");
+    if (t_rows == 0) return ok();
+    if (!d_a || !d_out) return fail(RCE_QMM_ERR_INVALID, "mm_batched_device: null buffer");
+    if (lda < (size_t)w->g.n_cols || ldo < (size_t)w->g.n_rows)
+        return fail(RCE_QMM_ERR_INVALID, "mm_batched_device: lda %zu < k %lld or ldo %zu < n %lld", lda,
+                    (long long)w->g.n_cols, ldo, (long long)w->g.n_rows);
+    DeviceGuard dg(ctx->device);
+    return run_matmul(ctx, w, d_a, lda, t_rows, d_out, ldo, (cudaStream_t)stream);
+}
+
+int rce_qmm_mm_batched(rce_qmm_ctx *ctx, const float *a, size_t t_rows, const rce_qmm_weight *w, float *out,
+                       size_t out_len) {
+    if (!ctx) return fail(RCE_QMM_ERR_INVALID, "mm_batched: null ctx");
+    int rc = check_weight(w);
+    if (rc) return rc;
+    if (w->ctx != ctx) return fail(RCE_QMM_ERR_INVALID, "mm_batched: weight belongs to another context");
+    if (t_rows == 0) return ok();
+    if (!a || !out) return fail(RCE_QMM_ERR_INVALID, "mm_batched: null buffer");
+    const size_t k = (size_t)w->g.n_cols, n = (size_t)w->g.n_rows;
+    if (out_len < t_rows * n)
+        return fail(RCE_QMM_ERR_INVALID, "mm_batched: output holds %zu values, %zu needed", out_len, t_rows * n);
+    DeviceGuard dg(ctx->device);
+    ThreadState *ts = nullptr;
+    rc = thread_state(ctx, &ts);
+    if (rc) return rc;
+    const size_t in_f = t_rows * k, out_f = t_rows * n;
+    if ((rc = grow_device(&ts->d_in, &ts->d_in_cap, in_f))) return rc;
+    if ((rc = grow_device(&ts->d_out, &ts->d_out_cap, out_f))) return rc;
+    if ((rc = grow_pinned(ts, (in_f > out_f ? in_f : out_f) * sizeof(float)))) return rc;
+    std::memcpy(ts->h_pin, a, in_f * sizeof(float));
+    CUDA_TRY(cudaMemcpyAsync(ts->d_in, ts->h_pin, in_f * sizeof(float), cudaMemcpyHostToDevice, ts->stream));
+    rc = run_matmul(ctx, w, ts->d_in, k, t_rows, ts->d_out, n, ts->stream);
+    if (rc) return rc;
+    CUDA_TRY(cudaMemcpyAsync(ts->h_pin, ts->d_out, out_f * sizeof(float), cudaMemcpyDeviceToHost, ts->stream));
+    CUDA_TRY(cudaStreamSynchronize(ts->stream));
+    std::memcpy(out, ts->h_pin, out_f * sizeof(float));
+    return ok();
+}
+
+int rce_qmm_mm_1d(rce_qmm_ctx *ctx, const float *a, size_t a_len, const rce_qmm_weight *w, float *out,
+                  size_t out_len) {
+    int rc = check_weight(w);
+    if (rc) return rc;
+    if (a_len != (size_t)w->g.n_cols)
+        return fail(RCE_QMM_ERR_INVALID, "mm_1d: activation len %zu != k %lld", a_len, (long long)w->g.n_cols);
+    return rce_qmm_mm_batched(ctx, a, 1, w, out, out_len);
+}
+
+int rce_qmm_mm_1d_serial(rce_qmm_ctx *ctx, const float *a, size_t a_len, const rce_qmm_weight *w, float *out,
+                         size_t out_len) {
+    return rce_qmm_mm_1d(ctx, a, a_len, w, out, out_len);
+}
+
+int rce_qmm_dequant_device(rce_qmm_ctx *ctx, const rce_qmm_weight *w, int64_t row0, int64_t row1, float *d_out,
+                           size_t ldo, void *stream) {
+    if (!ctx) return fail(RCE_QMM_ERR_INVALID, "dequant_device: null ctx");
+    int rc = check_weight(w);
+    if (rc) return rc;
+    if (row0 < 0 || row1 > w->g.n_rows || row0 > row1)
+        return fail(RCE_QMM_ERR_INVALID, "dequant_device: rows [%lld, %lld) outside [0, %lld)", (long long)row0,
+                    (long long)row1, (long long)w->g.n_rows);
+    if (!d_out || ldo < (size_t)w->g.n_cols) return fail(RCE_QMM_ERR_INVALID, "dequant_device: bad output");
+    DeviceGuard dg(ctx->device);
+    CUDA_TRY(rce::launch_dequant(w->dtype, w->dev, d_out, ldo, w->g, row0, row1, (cudaStream_t)stream));
+    return ok();
+}
+
+int rce_qmm_dequant_row(rce_qmm_ctx *ctx, const rce_qmm_weight *w, int64_t row, float *out, size_t out_len) {
+    if (!ctx) return fail(RCE_QMM_ERR_INVALID, "dequant_row: null ctx");
+    int rc = check_weight(w);
+    if (rc) return rc;
+    if (row < 0 || row >= w->g.n_rows)
+        return fail(RCE_QMM_ERR_INVALID, "dequant_row: row %lld >= n_rows %lld", (long long)row,
+                    (long long)w->g.n_rows);
+    const size_t k = (size_t)w->g.n_cols;
+    if (!out || out_len < k) return fail(RCE_QMM_ERR_INVALID, "dequant_row: output holds %zu < %zu", out_len, k);
+    DeviceGuard dg(ctx->device);
+    ThreadState *ts = nullptr;
+    rc = thread_state(ctx, &ts);
+    if (rc) return rc;
+    if ((rc = grow_device(&ts->d_out, &ts->d_out_cap, k))) return rc;
+    if ((rc = grow_pinned(ts, k * sizeof(float)))) return rc;
+    CUDA_TRY(rce::launch_dequant(w->dtype, w->dev, ts->d_out, k, w->g, row, row + 1, ts->stream));
+    CUDA_TRY(cudaMemcpyAsync(ts->h_pin, ts->d_out, k * sizeof(float), cudaMemcpyDeviceToHost, ts->stream));
+    CUDA_TRY(cudaStreamSynchronize(ts->stream));
+    std::memcpy(out, ts->h_pin, k * sizeof(float));
+    return ok();
+}
+
+int rce_qmm_synchronize(rce_qmm_ctx *ctx) {
+    if (!ctx) return fail(RCE_QMM_ERR_INVALID, "synchronize: null ctx");
+    DeviceGuard dg(ctx->device);
+    ThreadState *ts = nullptr;
+    int rc = thread_state(ctx, &ts);
+    if (rc) return rc;
+    CUDA_TRY(cudaStreamSynchronize(ts->stream));
+    return ok();
+}
+
+}  // extern "C"

@@ -1,0 +1,39 @@
+// qmm_internal.h -- launch wrappers shared between the kernel files and the
+// C-ABI layer.  Not part of the public interface (include/rce_qmm.h is).
+#pragma once
+#include <cuda_runtime.h>
+
+#include <cstddef>
+#include <cstdint>
+
+#include "qmm_layout.cuh"
+
+namespace rce {
+
+// GGUF bytes (device) -> T16 tiles (device).  Rows [0, n_rows) of the source.
+cudaError_t launch_repack(int dt, const uint8_t *gguf, uint8_t *tiles, const Geometry &g,
+                          cudaStream_t s);
+// T16 tiles -> GGUF bytes for rows [row0, row1) (dst holds those rows only).
+cudaError_t launch_unpack(int dt, const uint8_t *tiles, uint8_t *gguf, const Geometry &g,
+                          int64_t row0, int64_t row1, cudaStream_t s);
+// Bit-exact dequantize_to_f32 of rows [row0, row1) into out[(row-row0)*ldo + col].
+cudaError_t launch_dequant(int dt, const uint8_t *tiles, float *out, size_t ldo, const Geometry &g,
+                           int64_t row0, int64_t row1, cudaStream_t s);
+
+// Decode GEMV / small-M matmul: y[t][row] = sum_k x[t][k] W[row][k] for
+// t < m, rows [0, n_rows).  Uses split-K scratch when the plan asks for it.
+struct GemvPlan {
+    int rt = 2;          // 16-row tiles per CTA
+    int k_splits = 1;    // CTAs along K
+    int cps = 0;         // chunks per split
+    int nt = 1;          // token slots compiled in (1, 2, 4, 8 or 16)
+    size_t smem = 0;     // dynamic shared memory
+    size_t scratch_floats = 0;  // partial sums
+    int counters = 0;    // arrival counters (k_splits > 1)
+};
+GemvPlan plan_gemv(int dt, const Geometry &g, int m, int sm_count);
+cudaError_t launch_gemv(int dt, const uint8_t *tiles, const Geometry &g, const float *x, size_t ldx,
+                        float *y, size_t ldy, int m, const GemvPlan &plan, float *scratch,
+                        unsigned *counters, cudaStream_t s);
+
+}  // namespace rce
