@@ -14,6 +14,7 @@
 #include <unordered_map>
 
 #include "../../include/rce_qmm.h"
+#include "qmm_handles.h"
 #include "qmm_internal.h"
 
 using rce::Geometry;
@@ -42,40 +43,12 @@ int ok() { return RCE_QMM_OK; }
                         "%s: %s (%s:%d)", #expr, cudaGetErrorString(e_), __FILE__, __LINE__); \
     } while (0)
 
-struct Scratch {
-    float *partial = nullptr;
-    size_t floats = 0;
-    unsigned *counters = nullptr;
-    size_t ncounters = 0;
-};
-
-struct ThreadState {
-    cudaStream_t stream = nullptr;
-    float *d_in = nullptr;
-    size_t d_in_cap = 0;
-    float *d_out = nullptr;
-    size_t d_out_cap = 0;
-    void *h_pin = nullptr;
-    size_t h_cap = 0;
-};
-
 }  // namespace
 
-struct rce_qmm_ctx {
-    int device = 0;
-    int sm_count = 148;
-    std::mutex mu;
-    std::unordered_map<cudaStream_t, Scratch> scratch;
-    std::unordered_map<std::thread::id, ThreadState> threads;
-};
-
-struct rce_qmm_weight {
-    rce_qmm_ctx *ctx = nullptr;
-    int dtype = 0;
-    Geometry g;
-    uint8_t *dev = nullptr;
-    bool owner = false;
-};
+int rce_qmm_set_error(int code, const char *msg) {
+    g_last_error = msg;
+    return code;
+}
 
 namespace {
 
@@ -92,9 +65,9 @@ struct DeviceGuard {
     }
 };
 
-int thread_state(rce_qmm_ctx *ctx, ThreadState **out) {
+int thread_state(rce_qmm_ctx *ctx, RceThreadState **out) {
     std::lock_guard<std::mutex> lk(ctx->mu);
-    ThreadState &ts = ctx->threads[std::this_thread::get_id()];
+    RceThreadState &ts = ctx->threads[std::this_thread::get_id()];
     if (!ts.stream) CUDA_TRY(cudaStreamCreateWithFlags(&ts.stream, cudaStreamNonBlocking));
     *out = &ts;
     return ok();
@@ -110,7 +83,7 @@ int grow_device(float **p, size_t *cap, size_t need_floats) {
     return ok();
 }
 
-int grow_pinned(ThreadState *ts, size_t bytes) {
+int grow_pinned(RceThreadState *ts, size_t bytes) {
     if (ts->h_cap >= bytes) return ok();
     if (ts->h_pin) cudaFreeHost(ts->h_pin);
     ts->h_pin = nullptr;
@@ -124,9 +97,9 @@ int grow_pinned(ThreadState *ts, size_t bytes) {
 // is ordered, so its kernels never share scratch concurrently).  Growing it
 // synchronises the stream, so the first call with the largest shape must
 // come before any CUDA-graph capture on that stream.
-int stream_scratch(rce_qmm_ctx *ctx, cudaStream_t s, size_t floats, size_t counters, Scratch **out) {
+int stream_scratch(rce_qmm_ctx *ctx, cudaStream_t s, size_t floats, size_t counters, RceScratch **out) {
     std::lock_guard<std::mutex> lk(ctx->mu);
-    Scratch &sc = ctx->scratch[s];
+    RceScratch &sc = ctx->scratch[s];
     if (sc.floats < floats) {
         CUDA_TRY(cudaStreamSynchronize(s));
         if (sc.partial) cudaFree(sc.partial);
@@ -162,7 +135,7 @@ int run_matmul(rce_qmm_ctx *ctx, const rce_qmm_weight *w, const float *d_x, size
     while (t0 < t_rows) {
         const int m = (int)((t_rows - t0) < 16 ? (t_rows - t0) : 16);
         rce::GemvPlan plan = rce::plan_gemv(w->dtype, g, m, ctx->sm_count);
-        Scratch *sc = nullptr;
+        RceScratch *sc = nullptr;
         if (plan.k_splits > 1) {
             int rc = stream_scratch(ctx, s, plan.scratch_floats, (size_t)plan.counters, &sc);
             if (rc) return rc;
@@ -268,7 +241,7 @@ int rce_qmm_ctx_destroy(rce_qmm_ctx *ctx) {
     if (!ctx) return fail(RCE_QMM_ERR_INVALID, "ctx_destroy: null");
     DeviceGuard dg(ctx->device);
     for (auto &kv : ctx->threads) {
-        ThreadState &ts = kv.second;
+        RceThreadState &ts = kv.second;
         if (ts.stream) cudaStreamSynchronize(ts.stream);
         if (ts.d_in) cudaFree(ts.d_in);
         if (ts.d_out) cudaFree(ts.d_out);
@@ -293,7 +266,7 @@ int rce_qmm_weight_register(rce_qmm_ctx *ctx, const void *bytes, size_t nbytes, 
                             int64_t n_cols, rce_qmm_weight **out) {
     if (!ctx) return fail(RCE_QMM_ERR_INVALID, "weight_register: null ctx");
     DeviceGuard dg(ctx->device);
-    ThreadState *ts = nullptr;
+    RceThreadState *ts = nullptr;
     int rc = thread_state(ctx, &ts);
     if (rc) return rc;
     return register_common(ctx, bytes, false, nbytes, dtype, n_rows, n_cols, ts->stream, out);
@@ -370,7 +343,7 @@ int rce_qmm_weight_read_bytes(const rce_qmm_weight *w, void *host_out, size_t nb
     if (!host_out || nbytes != w->g.gguf_bytes)
         return fail(RCE_QMM_ERR_INVALID, "weight_read_bytes: need a buffer of %zu bytes", w->g.gguf_bytes);
     DeviceGuard dg(w->ctx->device);
-    ThreadState *ts = nullptr;
+    RceThreadState *ts = nullptr;
     rc = thread_state(w->ctx, &ts);
     if (rc) return rc;
     uint8_t *tmp = nullptr;
@@ -410,7 +383,7 @@ int rce_qmm_mm_batched(rce_qmm_ctx *ctx, const float *a, size_t t_rows, const rc
     if (out_len < t_rows * n)
         return fail(RCE_QMM_ERR_INVALID, "mm_batched: output holds %zu values, %zu needed", out_len, t_rows * n);
     DeviceGuard dg(ctx->device);
-    ThreadState *ts = nullptr;
+    RceThreadState *ts = nullptr;
     rc = thread_state(ctx, &ts);
     if (rc) return rc;
     const size_t in_f = t_rows * k, out_f = t_rows * n;
@@ -465,7 +438,7 @@ int rce_qmm_dequant_row(rce_qmm_ctx *ctx, const rce_qmm_weight *w, int64_t row, 
     const size_t k = (size_t)w->g.n_cols;
     if (!out || out_len < k) return fail(RCE_QMM_ERR_INVALID, "dequant_row: output holds %zu < %zu", out_len, k);
     DeviceGuard dg(ctx->device);
-    ThreadState *ts = nullptr;
+    RceThreadState *ts = nullptr;
     rc = thread_state(ctx, &ts);
     if (rc) return rc;
     if ((rc = grow_device(&ts->d_out, &ts->d_out_cap, k))) return rc;
@@ -480,7 +453,7 @@ int rce_qmm_dequant_row(rce_qmm_ctx *ctx, const rce_qmm_weight *w, int64_t row, 
 int rce_qmm_synchronize(rce_qmm_ctx *ctx) {
     if (!ctx) return fail(RCE_QMM_ERR_INVALID, "synchronize: null ctx");
     DeviceGuard dg(ctx->device);
-    ThreadState *ts = nullptr;
+    RceThreadState *ts = nullptr;
     int rc = thread_state(ctx, &ts);
     if (rc) return rc;
     CUDA_TRY(cudaStreamSynchronize(ts->stream));

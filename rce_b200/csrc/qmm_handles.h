@@ -1,0 +1,46 @@
+// qmm_handles.h -- definitions of the opaque C-ABI handles, shared by the
+// translation units that implement include/rce_qmm.h.
+#pragma once
+#include <cuda_runtime.h>
+
+#include <mutex>
+#include <thread>
+#include <unordered_map>
+
+#include "qmm_layout.cuh"
+
+struct RceScratch {
+    float *partial = nullptr;
+    size_t floats = 0;
+    unsigned *counters = nullptr;
+    size_t ncounters = 0;
+};
+
+struct RceThreadState {
+    cudaStream_t stream = nullptr;
+    float *d_in = nullptr;
+    size_t d_in_cap = 0;
+    float *d_out = nullptr;
+    size_t d_out_cap = 0;
+    void *h_pin = nullptr;
+    size_t h_cap = 0;
+};
+
+struct rce_qmm_ctx {
+    int device = 0;
+    int sm_count = 148;
+    std::mutex mu;
+    std::unordered_map<cudaStream_t, RceScratch> scratch;
+    std::unordered_map<std::thread::id, RceThreadState> threads;
+};
+
+struct rce_qmm_weight {
+    rce_qmm_ctx *ctx = nullptr;
+    int dtype = 0;
+    rce::Geometry g;
+    uint8_t *dev = nullptr;
+    bool owner = false;
+};
+
+// Records `msg` as the calling thread's rce_qmm_last_error() and returns code.
+int rce_qmm_set_error(int code, const char *msg);
