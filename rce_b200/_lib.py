@@ -49,6 +49,7 @@ SIGNATURES = {
     "rce_qmm_mm_1d_serial": (_int, [_vp, _f32p, _sz, _vp, _f32p, _sz]),
     "rce_qmm_mm_batched": (_int, [_vp, _f32p, _sz, _vp, _f32p, _sz]),
     "rce_qmm_mm_batched_device": (_int, [_vp, _vp, _sz, _sz, _vp, _vp, _sz, _vp]),
+    "rce_qmm_mm_batched_device_noalloc": (_int, [_vp, _vp, _sz, _sz, _vp, _vp, _sz, _vp]),
     "rce_qmm_dequant_row": (_int, [_vp, _vp, _i64, _f32p, _sz]),
     "rce_qmm_dequant_device": (_int, [_vp, _vp, _i64, _i64, _vp, _sz, _vp]),
     "rce_qmm_synchronize": (_int, [_vp]),

@@ -1,0 +1,77 @@
+"""rce_qmm_mm_batched_device_noalloc: the decode matmul for callers that may
+not allocate device memory (its split-K scratch is a fixed array inside the
+library).  Called through the C ABI and checked against the regular device
+entry point, with the tolerance of the other parity tests, on two calls in a
+row (the second call sees the array as the first one left it).
+
+This file is named to be collected last, so a run that stops at the first
+failure has run every other test before it.
+"""
+import ctypes
+
+import numpy as np
+import pytest
+
+import oracle as O
+import refcases
+
+pytestmark = pytest.mark.gpu
+
+
+def _assert_close(got, want, tol=1e-3):
+    got = np.asarray(got, np.float64)
+    want = np.asarray(want, np.float64)
+    assert np.all(np.isfinite(got))
+    err = np.abs(got - want).max(axis=1) / np.maximum(np.abs(want).max(axis=1), 1e-30)
+    assert err.max() <= tol, f"normwise relative error {err.max():.3e} > {tol}"
+    d = np.abs(got - want)
+    assert ((d < 1e-4) | (d <= 1e-3 * np.abs(want))).all()
+
+
+def _noalloc(L, ctx, x, w, out, stream):
+    return L.rce_qmm_mm_batched_device_noalloc(
+        ctx.handle, ctypes.c_void_p(x.data_ptr()), x.stride(0), x.shape[0], w.handle,
+        ctypes.c_void_p(out.data_ptr()), out.stride(0), ctypes.c_void_p(stream.cuda_stream))
+
+
+@pytest.mark.parametrize("dt,n,k,m", [(O.GGUF_Q4_K, 1024, 4096, 1), (O.GGUF_Q4_K, 1024, 4096, 5),
+                                      (O.GGUF_Q8_0, 700, 2048, 3), (O.GGUF_Q4_0, 512, 11008, 17)])
+def test_noalloc_matches_regular_entry_point(dt, n, k, m):
+    import torch
+
+    import rce_b200 as R
+    from rce_b200 import _lib
+
+    L = _lib.lib()
+    ctx = R.default_context(0)
+    wb, _, _, _, x = refcases.seeded_case(dt, n, k, m, 900 + m)
+    w = R.QuantWeight.from_owned_bytes(wb, dt, n, k, ctx=ctx)
+    xd = torch.from_numpy(x).cuda()
+    stream = torch.cuda.current_stream()
+    want = R.mm_batched_device(xd, w).cpu().numpy()
+    for call in range(2):
+        out = torch.full((m, n), float("nan"), device="cuda:0")
+        rc = _noalloc(L, ctx, xd, w, out, stream)
+        assert rc == 0, L.rce_qmm_last_error()
+        torch.cuda.synchronize()
+        _assert_close(out.cpu().numpy(), want)
+
+
+def test_noalloc_rejects_shapes_beyond_its_fixed_scratch():
+    import torch
+
+    import rce_b200 as R
+    from rce_b200 import _lib, synth
+
+    L = _lib.lib()
+    ctx = R.default_context(0)
+    n, k, m = 32768, 4096, 16  # 4 splits x 16 tokens x 32768 rows > 2^20 partial sums
+    g = torch.Generator(device="cuda:0")
+    g.manual_seed(5)
+    raw = synth.device_weights(O.GGUF_Q4_K, n, k, g, torch.device("cuda:0"))
+    w = R.QuantWeight.from_device_bytes(raw, O.GGUF_Q4_K, n, k, ctx=ctx)
+    x = torch.randn((m, k), device="cuda:0")
+    out = torch.empty((m, n), device="cuda:0")
+    rc = _noalloc(L, ctx, x, w, out, torch.cuda.current_stream())
+    assert rc == _lib.RCE_QMM_ERR_UNSUPPORTED
+    assert b"fixed scratch" in L.rce_qmm_last_error()
