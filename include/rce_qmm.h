@@ -52,6 +52,7 @@ extern "C" {
 #define RCE_QMM_ERR_UNSUPPORTED 2 /* dtype or shape outside this library */
 #define RCE_QMM_ERR_CUDA 3        /* a CUDA runtime call failed */
 #define RCE_QMM_ERR_NOMEM 4       /* device or host allocation failed */
+#define RCE_QMM_ERR_TIMEOUT 5     /* a bounded wait inside a kernel expired */
 
 /* GGUF dtype tags (rce-ingest-gguf/src/parser.rs:308-338). */
 #define RCE_QMM_GGUF_Q4_0 2
@@ -125,7 +126,7 @@ int rce_qmm_mm_batched_device(rce_qmm_ctx *ctx, const float *d_a, size_t lda, si
  * memory (a custom allocator owning the device, a serving loop that forbids
  * cudaMalloc after start-up).  No counterpart in the reference: its CPU path
  * never allocates device memory.  The split-K scratch comes from a fixed
- * 4 MiB array inside the library (held by every GPU that loads it) instead of
+ * 1 MiB array inside the library (held by every GPU that loads it) instead of
  * a per-stream allocation; this call performs no cudaMalloc/cudaFree.
  * Shapes whose split needs more than that array are rejected with
  * RCE_QMM_ERR_UNSUPPORTED.  All calls on a device share the array: calls whose
@@ -141,6 +142,13 @@ int rce_qmm_dequant_row(rce_qmm_ctx *ctx, const rce_qmm_weight *w, int64_t row, 
 /* Device variant: rows [row0, row1) into d_out[(row - row0) * ldo + col]. */
 int rce_qmm_dequant_device(rce_qmm_ctx *ctx, const rce_qmm_weight *w, int64_t row0, int64_t row1,
                            float *d_out, size_t ldo, void *stream);
+
+/* The context's kernel error word: 0, or the code a kernel recorded when one
+ * of its bounded waits expired (its outputs are then invalid).  Host entry
+ * points check it themselves and return RCE_QMM_ERR_TIMEOUT; after
+ * asynchronous _device calls, synchronise the stream and read it here.
+ * clear != 0 re-arms it. */
+int rce_qmm_device_error(rce_qmm_ctx *ctx, int *code, int clear);
 
 /* Wait for all work this thread queued on the context's streams. */
 int rce_qmm_synchronize(rce_qmm_ctx *ctx);

@@ -18,6 +18,7 @@ RCE_QMM_ERR_INVALID = 1
 RCE_QMM_ERR_UNSUPPORTED = 2
 RCE_QMM_ERR_CUDA = 3
 RCE_QMM_ERR_NOMEM = 4
+RCE_QMM_ERR_TIMEOUT = 5
 
 _lib = None
 _lock = threading.Lock()
@@ -52,6 +53,7 @@ SIGNATURES = {
     "rce_qmm_mm_batched_device_noalloc": (_int, [_vp, _vp, _sz, _sz, _vp, _vp, _sz, _vp]),
     "rce_qmm_dequant_row": (_int, [_vp, _vp, _i64, _f32p, _sz]),
     "rce_qmm_dequant_device": (_int, [_vp, _vp, _i64, _i64, _vp, _sz, _vp]),
+    "rce_qmm_device_error": (_int, [_vp, _c.POINTER(_int), _int]),
     "rce_qmm_synchronize": (_int, [_vp]),
 }
 

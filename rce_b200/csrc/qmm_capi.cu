@@ -122,6 +122,16 @@ int stream_scratch(rce_qmm_ctx *ctx, cudaStream_t s, size_t floats, size_t count
     return ok();
 }
 
+// After the caller's stream has been synchronised: turn a kernel-reported
+// error (a bounded wait that expired) into a status, and re-arm the word.
+int take_kernel_error(rce_qmm_ctx *ctx) {
+    const int code = *reinterpret_cast<volatile int *>(ctx->err_host);
+    if (code == 0) return ok();
+    *reinterpret_cast<volatile int *>(ctx->err_host) = 0;
+    return fail(RCE_QMM_ERR_TIMEOUT, "a kernel's bounded wait expired (device error code %d); its results are invalid",
+                code);
+}
+
 int check_weight(const rce_qmm_weight *w) {
     if (!w || !w->ctx || !w->dev) return fail(RCE_QMM_ERR_INVALID, "null or freed weight handle");
     return ok();
@@ -133,7 +143,8 @@ int run_matmul(rce_qmm_ctx *ctx, const rce_qmm_weight *w, const float *d_x, size
     const Geometry &g = w->g;
     size_t t0 = 0;
     while (t0 < t_rows) {
-        const int m = (int)((t_rows - t0) < 16 ? (t_rows - t0) : 16);
+        const size_t left = t_rows - t0;
+        const int m = (int)(left < (size_t)rce::kGemvMaxTokens ? left : (size_t)rce::kGemvMaxTokens);
         rce::GemvPlan plan = rce::plan_gemv(w->dtype, g, m, ctx->sm_count);
         RceScratch *sc = nullptr;
         if (plan.k_splits > 1) {
@@ -141,7 +152,7 @@ int run_matmul(rce_qmm_ctx *ctx, const rce_qmm_weight *w, const float *d_x, size
             if (rc) return rc;
         }
         CUDA_TRY(rce::launch_gemv(w->dtype, w->dev, g, d_x + t0 * lda, lda, d_y + t0 * ldo, ldo, m, plan,
-                                  sc ? sc->partial : nullptr, sc ? sc->counters : nullptr, s));
+                                  sc ? sc->partial : nullptr, sc ? sc->counters : nullptr, ctx->err_dev, s));
         t0 += (size_t)m;
     }
     return ok();
@@ -230,9 +241,20 @@ int rce_qmm_ctx_create(int device, rce_qmm_ctx **out) {
     if (prop.major != 10)
         return fail(RCE_QMM_ERR_UNSUPPORTED, "ctx_create: device %d is sm_%d%d; this library is built for sm_100a",
                     device, prop.major, prop.minor);
+    DeviceGuard dg(device);
+    int *err_host = nullptr, *err_dev = nullptr;
+    CUDA_TRY(cudaHostAlloc(&err_host, sizeof(int), cudaHostAllocMapped | cudaHostAllocPortable));
+    *err_host = 0;
+    cudaError_t e = cudaHostGetDevicePointer(&err_dev, err_host, 0);
+    if (e != cudaSuccess) {
+        cudaFreeHost(err_host);
+        return fail(RCE_QMM_ERR_CUDA, "ctx_create: mapped error word: %s", cudaGetErrorString(e));
+    }
     rce_qmm_ctx *c = new rce_qmm_ctx;
     c->device = device;
     c->sm_count = prop.multiProcessorCount;
+    c->err_host = err_host;
+    c->err_dev = err_dev;
     *out = c;
     return ok();
 }
@@ -252,6 +274,7 @@ int rce_qmm_ctx_destroy(rce_qmm_ctx *ctx) {
         if (kv.second.partial) cudaFree(kv.second.partial);
         if (kv.second.counters) cudaFree(kv.second.counters);
     }
+    if (ctx->err_host) cudaFreeHost(ctx->err_host);
     delete ctx;
     return ok();
 }
@@ -396,6 +419,7 @@ int rce_qmm_mm_batched(rce_qmm_ctx *ctx, const float *a, size_t t_rows, const rc
     if (rc) return rc;
     CUDA_TRY(cudaMemcpyAsync(ts->h_pin, ts->d_out, out_f * sizeof(float), cudaMemcpyDeviceToHost, ts->stream));
     CUDA_TRY(cudaStreamSynchronize(ts->stream));
+    if ((rc = take_kernel_error(ctx))) return rc;
     std::memcpy(out, ts->h_pin, out_f * sizeof(float));
     return ok();
 }
@@ -447,6 +471,13 @@ int rce_qmm_dequant_row(rce_qmm_ctx *ctx, const rce_qmm_weight *w, int64_t row, 
     CUDA_TRY(cudaMemcpyAsync(ts->h_pin, ts->d_out, k * sizeof(float), cudaMemcpyDeviceToHost, ts->stream));
     CUDA_TRY(cudaStreamSynchronize(ts->stream));
     std::memcpy(out, ts->h_pin, k * sizeof(float));
+    return ok();
+}
+
+int rce_qmm_device_error(rce_qmm_ctx *ctx, int *code, int clear) {
+    if (!ctx || !code) return fail(RCE_QMM_ERR_INVALID, "device_error: null argument");
+    *code = *reinterpret_cast<volatile int *>(ctx->err_host);
+    if (clear) *reinterpret_cast<volatile int *>(ctx->err_host) = 0;
     return ok();
 }
 

@@ -29,6 +29,10 @@ struct RceThreadState {
 struct rce_qmm_ctx {
     int device = 0;
     int sm_count = 148;
+    // Error word the kernels write when a bounded wait expires: mapped,
+    // pinned host memory, so the host reads it without a copy.
+    int *err_host = nullptr;
+    int *err_dev = nullptr;
     std::mutex mu;
     std::unordered_map<cudaStream_t, RceScratch> scratch;
     std::unordered_map<std::thread::id, RceThreadState> threads;

@@ -20,13 +20,18 @@ cudaError_t launch_unpack(int dt, const uint8_t *tiles, uint8_t *gguf, const Geo
 cudaError_t launch_dequant(int dt, const uint8_t *tiles, float *out, size_t ldo, const Geometry &g,
                            int64_t row0, int64_t row1, cudaStream_t s);
 
-// Decode GEMV / small-M matmul: y[t][row] = sum_k x[t][k] W[row][k] for
-// t < m, rows [0, n_rows).  Uses split-K scratch when the plan asks for it.
+// Decode GEMV / small-M matmul: y[t][row] = sum_k x[t][k] W[row][k], for
+// t < m <= kGemvMaxTokens, rows [0, n_rows).  Uses split-K scratch when the
+// plan asks for it.  `err` (device-visible int) receives a non-zero code if a
+// bounded wait inside the kernel expires.
+constexpr int kGemvMaxTokens = 4;
 struct GemvPlan {
-    int rt = 2;          // 16-row tiles per CTA
+    int rt = 1;          // 16-row tiles per CTA
     int k_splits = 1;    // CTAs along K
     int cps = 0;         // chunks per split
-    int nt = 1;          // token slots compiled in (1, 2, 4, 8 or 16)
+    int nt = 1;          // token slots compiled in (1, 2 or 4)
+    int stages = 4;      // TMA ring depth per warp
+    int window = 16;     // chunks per activation-table window
     size_t smem = 0;     // dynamic shared memory
     size_t scratch_floats = 0;  // partial sums
     int counters = 0;    // arrival counters (k_splits > 1)
@@ -34,6 +39,9 @@ struct GemvPlan {
 GemvPlan plan_gemv(int dt, const Geometry &g, int m, int sm_count);
 cudaError_t launch_gemv(int dt, const uint8_t *tiles, const Geometry &g, const float *x, size_t ldx,
                         float *y, size_t ldy, int m, const GemvPlan &plan, float *scratch,
-                        unsigned *counters, cudaStream_t s);
+                        unsigned *counters, int *err, cudaStream_t s);
+
+// Kernel error codes written to the context's error word.
+constexpr int kKernelErrWaitTimeout = 1;
 
 }  // namespace rce

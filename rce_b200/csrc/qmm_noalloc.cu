@@ -8,11 +8,14 @@
 // routine.
 //
 // Limits and sharing:
-//  * the array holds kNoAllocPartialFloats split-K partial sums (4 MiB) and
-//    kNoAllocCounters arrival counters (16 KiB); every GPU that loads the
-//    library keeps them until the process exits.  A shape whose split needs
-//    more (k_splits x min(t_rows, 16) x 16 * ceil(n_rows / 16) floats) is
-//    rejected with RCE_QMM_ERR_UNSUPPORTED before anything is launched;
+//  * the array holds kNoAllocPartialFloats split-K partial sums (1 MiB) and
+//    kNoAllocCounters arrival counters (4 KiB); every GPU that loads the
+//    library keeps them until the process exits.  The planner splits K only
+//    for weights of fewer than ~148 row blocks, so a split needs at most
+//    ~2 x 148 x 16 rows x 4 tokens partial sums, well inside the array; a
+//    shape that would need more (k_splits x min(t_rows, 4) x 16 *
+//    ceil(n_rows / 16) floats) is rejected with RCE_QMM_ERR_UNSUPPORTED
+//    before anything is launched;
 //  * all calls on a device share the one array and it keeps the last call's
 //    contents: each call clears the counters it uses before its kernels, and
 //    calls whose work overlaps on the GPU (different streams, or different
@@ -32,8 +35,8 @@
 
 namespace {
 
-constexpr size_t kNoAllocPartialFloats = size_t(1) << 20;  // 4 MiB of f32 partial sums
-constexpr size_t kNoAllocCounters = 4096;                  // 16 KiB of arrival counters
+constexpr size_t kNoAllocPartialFloats = size_t(1) << 18;  // 1 MiB of f32 partial sums
+constexpr size_t kNoAllocCounters = 1024;                  // 4 KiB of arrival counters
 
 // In host code these names are host-side stand-ins, not device addresses:
 // only the addresses from cudaGetSymbolAddress may be passed to a kernel.
@@ -107,7 +110,7 @@ extern "C" int rce_qmm_mm_batched_device_noalloc(rce_qmm_ctx *ctx, const float *
     CurrentDevice cd(ctx->device);
     if (cd.status != cudaSuccess)
         return err(RCE_QMM_ERR_CUDA, "mm_batched_device_noalloc: set device: %s", cudaGetErrorString(cd.status));
-    const int m_max = (int)(t_rows < 16 ? t_rows : 16);
+    const int m_max = (int)(t_rows < (size_t)rce::kGemvMaxTokens ? t_rows : (size_t)rce::kGemvMaxTokens);
     const rce::GemvPlan worst = rce::plan_gemv(w->dtype, g, m_max, ctx->sm_count);
     if (worst.k_splits > 1 &&
         (worst.scratch_floats > kNoAllocPartialFloats || (size_t)worst.counters > kNoAllocCounters))
@@ -127,11 +130,12 @@ extern "C" int rce_qmm_mm_batched_device_noalloc(rce_qmm_ctx *ctx, const float *
             return err(RCE_QMM_ERR_CUDA, "mm_batched_device_noalloc: clear counters: %s", cudaGetErrorString(e));
     }
     for (size_t t0 = 0; t0 < t_rows;) {
-        const int m = (int)((t_rows - t0) < 16 ? (t_rows - t0) : 16);
+        const size_t left = t_rows - t0;
+        const int m = (int)(left < (size_t)rce::kGemvMaxTokens ? left : (size_t)rce::kGemvMaxTokens);
         const rce::GemvPlan plan = rce::plan_gemv(w->dtype, g, m, ctx->sm_count);
         cudaError_t e = rce::launch_gemv(w->dtype, w->dev, g, d_a + t0 * lda, lda, d_out + t0 * ldo, ldo, m, plan,
                                          plan.k_splits > 1 ? partials : nullptr,
-                                         plan.k_splits > 1 ? counters : nullptr, s);
+                                         plan.k_splits > 1 ? counters : nullptr, ctx->err_dev, s);
         if (e != cudaSuccess)
             return err(RCE_QMM_ERR_CUDA, "mm_batched_device_noalloc: launch: %s", cudaGetErrorString(e));
         t0 += (size_t)m;

@@ -54,6 +54,13 @@ class Context:
     def synchronize(self) -> None:
         check(lib().rce_qmm_synchronize(self._h))
 
+    def device_error(self, clear: bool = True) -> int:
+        """The kernel error word (0 = none): non-zero when a bounded wait
+        inside a kernel expired; read it after synchronising the stream."""
+        code = ctypes.c_int()
+        check(lib().rce_qmm_device_error(self._h, ctypes.byref(code), int(bool(clear))))
+        return code.value
+
     def close(self) -> None:
         if self._h is not None and self._h.value:
             lib().rce_qmm_ctx_destroy(self._h)
