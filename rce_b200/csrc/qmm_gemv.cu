@@ -559,11 +559,11 @@ __global__ void __launch_bounds__(256, 2) gemv_kernel(GemvArgs p) {
     }
 }
 
-// Opt each kernel instantiation in to the device's full shared memory once
-// per device (a host-side attribute; not a stream operation).
+// Opt a kernel in to the device's full shared memory once per device (a
+// host-side attribute; not a stream operation).  `done` is the caller's
+// per-kernel record of the devices already set.
 template <typename Kern>
-cudaError_t ensure_smem_optin(Kern kern) {
-    static std::atomic<unsigned long long> done{0};
+cudaError_t ensure_smem_optin(Kern kern, std::atomic<unsigned long long> &done) {
     int dev = 0;
     cudaError_t e = cudaGetDevice(&dev);
     if (e != cudaSuccess) return e;
@@ -583,8 +583,9 @@ cudaError_t ensure_smem_optin(Kern kern) {
 
 template <int DT, int NT, int RT>
 cudaError_t launch_one(const GemvArgs &a, dim3 grid, size_t smem, cudaStream_t s) {
+    static std::atomic<unsigned long long> done{0};  // one per instantiation
     auto kern = gemv_kernel<DT, NT, RT>;
-    cudaError_t e = ensure_smem_optin(kern);
+    cudaError_t e = ensure_smem_optin(kern, done);
     if (e != cudaSuccess) return e;
     kern<<<grid, 256, smem, s>>>(a);
     return cudaGetLastError();
