@@ -93,8 +93,9 @@ int grow_pinned(RceThreadState *ts, size_t bytes) {
     return ok();
 }
 
-// Scratch for split-K partial sums, one buffer per stream (work on one stream
-// is ordered, so its kernels never share scratch concurrently).  Growing it
+// Scratch for split-K partial sums when a split is too wide for one cluster,
+// one buffer per stream (work on one stream is ordered, so its kernels never
+// share scratch concurrently).  Growing it
 // synchronises the stream, so the first call with the largest shape must
 // come before any CUDA-graph capture on that stream.
 int stream_scratch(rce_qmm_ctx *ctx, cudaStream_t s, size_t floats, size_t counters, RceScratch **out) {
@@ -147,7 +148,7 @@ int run_matmul(rce_qmm_ctx *ctx, const rce_qmm_weight *w, const float *d_x, size
         const int m = (int)(left < (size_t)rce::kGemvMaxTokens ? left : (size_t)rce::kGemvMaxTokens);
         rce::GemvPlan plan = rce::plan_gemv(w->dtype, g, m, ctx->sm_count);
         RceScratch *sc = nullptr;
-        if (plan.k_splits > 1) {
+        if (plan.scratch_floats > 0) {
             int rc = stream_scratch(ctx, s, plan.scratch_floats, (size_t)plan.counters, &sc);
             if (rc) return rc;
         }

@@ -8,26 +8,24 @@
 //  * Each warp owns one 16-row tile and a strided subset of its 256-column
 //    chunks.  Its lane 0 streams the chunks into a private shared-memory ring
 //    with TMA bulk copies (cp.async.bulk + mbarrier complete_tx), S chunks
-//    ahead, so ~70 KB per CTA are in flight from the first instruction on
-//    and no registers are spent on loads in flight.  Every wait on an
-//    mbarrier is bounded (%globaltimer); on expiry the kernel records an
-//    error word, waits (bounded) for its own copies and finishes.
-//  * Dequantisation stays in registers and stays exact: the quant codes are
-//    turned into fp16 integers (q, q-8 or the signed byte) with lop3/prmt
-//    magic-number tricks, which are exact for |q| <= 2048.  The block scales
-//    are applied in f32 after the dot product of each 32-value sub-block, so
-//    no weight is ever rounded.
-//  * The dot products run on the tensor cores (mma.sync m16n8k16, f32
-//    accumulate) as a throughput device: a CUDA-core FFMA loop would need
-//    ~3 ALU ops per weight, more than the SM issues at HBM speed for 4-bit
-//    formats.  Each lane feeds one column group g (its two sub-blocks), and
-//    the activation operand is block-diagonal: column 2g holds the fp16 "hi"
-//    part of x and column 2g+1 the "lo" remainder, so D[r][2g] + D[r][2g+1]
-//    is the sub-block dot product with ~22 significant bits of x.
-//  * x is scaled per token by a power of two (exact) so hi/lo stay inside
-//    fp16's range; the scale is undone on the f32 partial sums.
-//  * Q4_K's min term uses per-sub-block activation sums (the "asum hoist"),
-//    one FFMA per sub-block instead of one per weight.
+//    ahead, so ~70 KB per CTA are in flight from the first instruction on.
+//    Every wait on an mbarrier is bounded (%globaltimer); on expiry the
+//    kernel records an error word, waits (bounded) for its own copies and
+//    finishes.
+//  * The dot products are exact integer arithmetic on the tensor cores
+//    (mma.sync m16n8k32, u8/s8 x s8 -> s32).  The weight codes are the A
+//    operand as they are stored: Q8_0's int8 bytes need no unpacking at all,
+//    Q4_K/Q4_0 nibbles one and/shift per 4 codes.  Activations become a
+//    fixed-point integer per token, x * 2^e rounded to 28 bits with the power
+//    of two chosen from the CTA's slice of x, split into four balanced int8
+//    digits; the B operand is block-diagonal so that lane g's columns hold
+//    digits of its own column group (tile A digits 0-1, tile B digits 2-3).
+//    Each digit pair's 32-value sub-block sum is exact in s32; the two pairs
+//    meet in f32 and the block scales (d, d*sc, dmin*m) are applied once per
+//    sub-block, so no weight is rounded and x keeps 2^-27 of its slice
+//    maximum (below f32's own rounding of the reference's sums).
+//  * Q4_K's min term and Q4_0's -8 offset use per-sub-block sums of the
+//    integer activations (the "asum hoist"): one op per sub-block.
 //  * The activation table (the B fragments) is built per window of chunks
 //    with vectorised loads while the first weight copies are in flight.
 //  * The grid puts 1-8 tiles in a CTA so that all CTAs are resident in one
@@ -58,7 +56,7 @@ struct GemvArgs {
     Geometry g;
     size_t ldx, ldy;
     int m, cps, k_splits, n_pad;
-    int stages, window, x_vec4;
+    int stages, red_mode, x_vec4;
 };
 
 // ---- PTX helpers ---------------------------------------------------------------
@@ -117,37 +115,21 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint32_t bar, uint32_t parity)
     }
 }
 
-// (a & mask) | orv
-__device__ __forceinline__ uint32_t lop3_ao(uint32_t a, uint32_t mask, uint32_t orv) {
-    uint32_t r;
-    asm("lop3.b32 %0, %1, %2, %3, 0xEA;" : "=r"(r) : "r"(a), "r"(mask), "r"(orv));
-    return r;
-}
-
-__device__ __forceinline__ uint32_t hsub2(uint32_t a, uint32_t b) {
-    uint32_t r;
-    asm("sub.rn.f16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
-    return r;
-}
-
-__device__ __forceinline__ uint32_t hfma2(uint32_t a, uint32_t b, uint32_t c) {
-    uint32_t r;
-    asm("fma.rn.f16x2 %0, %1, %2, %3;" : "=r"(r) : "r"(a), "r"(b), "r"(c));
-    return r;
-}
-
-__device__ __forceinline__ uint32_t prmt(uint32_t a, uint32_t b, uint32_t sel) {
-    uint32_t r;
-    asm("prmt.b32 %0, %1, %2, %3;" : "=r"(r) : "r"(a), "r"(b), "r"(sel));
-    return r;
-}
-
-__device__ __forceinline__ void mma16816(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
-    asm volatile(
-        "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
-        "{%0,%1,%2,%3};"
-        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
-        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+// D(s32) += A(16x32, u8 or s8) x B(32x8, s8), exact.
+template <bool A_SIGNED>
+__device__ __forceinline__ void imma16832(int (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+    if (A_SIGNED)
+        asm volatile(
+            "mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+            "{%0,%1,%2,%3};"
+            : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
+            : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+    else
+        asm volatile(
+            "mma.sync.aligned.m16n8k32.row.col.s32.u8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+            "{%0,%1,%2,%3};"
+            : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
+            : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
 }
 
 __device__ __forceinline__ uint32_t comp(const uint4 &v, int i) {
@@ -185,47 +167,37 @@ __device__ __forceinline__ void load_chunk(ChunkRegs<DT> &c, const uint8_t *slot
     }
 }
 
-// The exact fp16 operand of step j (16 columns) for rows r (a0, a2) and
-// r + 8 (a1, a3).  a0/a1 hold columns (e0, e2) and a2/a3 (e1, e3) of the
-// lane's four columns 64 g + 4 j + (0..3) -- see qmm_layout.cuh.
+// The A operand of step s (0..7) for rows r (a0: columns 64g + 8s + 0..3,
+// a2: + 4..7) and r + 8 (a1, a3): the stored codes, one byte per value.
+// Sub-block (unit) 2g + (s >> 2); see qmm_layout.cuh for where the bytes sit.
 template <int DT>
-__device__ __forceinline__ void make_a(const ChunkRegs<DT> &c, int j, uint32_t (&a)[4]) {
-    const int h = j >> 3, jj = j & 7;
+__device__ __forceinline__ void make_a(const ChunkRegs<DT> &c, int s, uint32_t (&a)[4]) {
+    const int h = s >> 2, ss = s & 3;
     if (DT == GGUF_Q4_K) {
-        const uint32_t wr = comp(c.q[jj >> 2], jj & 3);
-        const uint32_t w8 = comp(c.q[2 + (jj >> 2)], jj & 3);
-        if (h == 0) {  // low nibbles: fp16(1024 + q) - 1024
-            a[0] = hsub2(lop3_ao(wr, 0x000F000Fu, 0x64006400u), 0x64006400u);
-            a[2] = hsub2(lop3_ao(wr >> 8, 0x000F000Fu, 0x64006400u), 0x64006400u);
-            a[1] = hsub2(lop3_ao(w8, 0x000F000Fu, 0x64006400u), 0x64006400u);
-            a[3] = hsub2(lop3_ao(w8 >> 8, 0x000F000Fu, 0x64006400u), 0x64006400u);
-        } else {  // high nibbles: fp16(1024 + 16q) / 16 - 64
-            a[0] = hfma2(lop3_ao(wr, 0x00F000F0u, 0x64006400u), 0x2C002C00u, 0xD400D400u);
-            a[2] = hfma2(lop3_ao(wr >> 8, 0x00F000F0u, 0x64006400u), 0x2C002C00u, 0xD400D400u);
-            a[1] = hfma2(lop3_ao(w8, 0x00F000F0u, 0x64006400u), 0x2C002C00u, 0xD400D400u);
-            a[3] = hfma2(lop3_ao(w8 >> 8, 0x00F000F0u, 0x64006400u), 0x2C002C00u, 0xD400D400u);
-        }
+        // group g's 32 qs bytes per row: words 2ss, 2ss+1; low nibbles are
+        // sub-block 2g, high nibbles sub-block 2g+1
+        const uint32_t r0 = comp(c.q[ss >> 1], (2 * ss) & 3), r1 = comp(c.q[ss >> 1], (2 * ss + 1) & 3);
+        const uint32_t e0 = comp(c.q[2 + (ss >> 1)], (2 * ss) & 3), e1 = comp(c.q[2 + (ss >> 1)], (2 * ss + 1) & 3);
+        const int sh = 4 * h;
+        a[0] = (r0 >> sh) & 0x0F0F0F0Fu;
+        a[2] = (r1 >> sh) & 0x0F0F0F0Fu;
+        a[1] = (e0 >> sh) & 0x0F0F0F0Fu;
+        a[3] = (e1 >> sh) & 0x0F0F0F0Fu;
     } else if (DT == GGUF_Q4_0) {
-        const uint32_t wr = comp(c.q[h], jj & 3);
-        const uint32_t w8 = comp(c.q[2 + h], jj & 3);
-        if ((jj >> 2) == 0) {  // low nibbles: fp16(1024 + n) - 1032 = n - 8
-            a[0] = hsub2(lop3_ao(wr, 0x000F000Fu, 0x64006400u), 0x64086408u);
-            a[2] = hsub2(lop3_ao(wr >> 8, 0x000F000Fu, 0x64006400u), 0x64086408u);
-            a[1] = hsub2(lop3_ao(w8, 0x000F000Fu, 0x64006400u), 0x64086408u);
-            a[3] = hsub2(lop3_ao(w8 >> 8, 0x000F000Fu, 0x64006400u), 0x64086408u);
-        } else {  // high nibbles: fp16(1024 + 16n) / 16 - 72 = n - 8
-            a[0] = hfma2(lop3_ao(wr, 0x00F000F0u, 0x64006400u), 0x2C002C00u, 0xD480D480u);
-            a[2] = hfma2(lop3_ao(wr >> 8, 0x00F000F0u, 0x64006400u), 0x2C002C00u, 0xD480D480u);
-            a[1] = hfma2(lop3_ao(w8, 0x00F000F0u, 0x64006400u), 0x2C002C00u, 0xD480D480u);
-            a[3] = hfma2(lop3_ao(w8 >> 8, 0x00F000F0u, 0x64006400u), 0x2C002C00u, 0xD480D480u);
-        }
-    } else {  // Q8_0: byte ^ 0x80 = q + 128; fp16(1024 + q + 128) - 1152 = q
-        const uint32_t wr = comp(c.q[2 * h + (jj >> 2)], jj & 3) ^ 0x80808080u;
-        const uint32_t w8 = comp(c.q[4 + 2 * h + (jj >> 2)], jj & 3) ^ 0x80808080u;
-        a[0] = hsub2(prmt(wr, 0x64646464u, 0x4240u), 0x64806480u);
-        a[2] = hsub2(prmt(wr, 0x64646464u, 0x4341u), 0x64806480u);
-        a[1] = hsub2(prmt(w8, 0x64646464u, 0x4240u), 0x64806480u);
-        a[3] = hsub2(prmt(w8, 0x64646464u, 0x4341u), 0x64806480u);
+        // block 2g + h: bytes 0..15; low nibbles are values 0..15, high 16..31
+        const int wp = (ss & 1) * 2, sh = 4 * (ss >> 1);
+        const uint32_t r0 = comp(c.q[h], wp), r1 = comp(c.q[h], wp + 1);
+        const uint32_t e0 = comp(c.q[2 + h], wp), e1 = comp(c.q[2 + h], wp + 1);
+        a[0] = (r0 >> sh) & 0x0F0F0F0Fu;
+        a[2] = (r1 >> sh) & 0x0F0F0F0Fu;
+        a[1] = (e0 >> sh) & 0x0F0F0F0Fu;
+        a[3] = (e1 >> sh) & 0x0F0F0F0Fu;
+    } else {
+        // block 2g + h: 32 int8 values, words 2ss, 2ss+1
+        a[0] = comp(c.q[2 * h + (ss >> 1)], (2 * ss) & 3);
+        a[2] = comp(c.q[2 * h + (ss >> 1)], (2 * ss + 1) & 3);
+        a[1] = comp(c.q[4 + 2 * h + (ss >> 1)], (2 * ss) & 3);
+        a[3] = comp(c.q[4 + 2 * h + (ss >> 1)], (2 * ss + 1) & 3);
     }
 }
 
@@ -243,11 +215,14 @@ __device__ __forceinline__ void q4k_header(const uint4 &hd, int g, float &d1, fl
     m2 = dmin * (float)((v >> 18) & 63u);
 }
 
+// One chunk: 8 steps, two sub-blocks (units) per lane.  bp[t] points at the
+// lane's B fragments of this chunk for token t (or at the zero block);
+// sint/sflt at the chunk's per-unit integer activation sums.
 template <int DT, int NT>
-__device__ __forceinline__ void process_chunk(const ChunkRegs<DT> &c, float (&acc)[NT][2],
-                                              const uint2 *__restrict__ tbl, int tok_stride,
-                                              const float *__restrict__ asum, int asum_stride, int m,
-                                              int lane, bool bact, int boff) {
+__device__ __forceinline__ void process_chunk(const ChunkRegs<DT> &c, float (&acc)[NT][2], const uint2 *const (&bp)[NT],
+                                              const int *__restrict__ sint, const float *__restrict__ sflt,
+                                              int s_stride, int lane) {
+    constexpr bool SIGNED = DT == GGUF_Q8_0;
     const int g = lane & 3;
     float ds[2][2], mn[2][2];
     if (DT == GGUF_Q4_K) {
@@ -261,36 +236,44 @@ __device__ __forceinline__ void process_chunk(const ChunkRegs<DT> &c, float (&ac
     }
 #pragma unroll
     for (int h = 0; h < 2; h++) {
-        float d[NT][4];
+        int da[NT][4], db[NT][4];
 #pragma unroll
-        for (int t = 0; t < NT; t++) d[t][0] = d[t][1] = d[t][2] = d[t][3] = 0.f;
+        for (int t = 0; t < NT; t++)
 #pragma unroll
-        for (int jj = 0; jj < 8; jj++) {
-            const int j = 8 * h + jj;
+            for (int i = 0; i < 4; i++) da[t][i] = db[t][i] = 0;
+#pragma unroll
+        for (int ss = 0; ss < 4; ss++) {
+            const int s = 4 * h + ss;
             uint32_t a[4];
-            make_a<DT>(c, j, a);
+            make_a<DT>(c, s, a);
 #pragma unroll
             for (int t = 0; t < NT; t++) {
-                if (t < m) {
-                    uint2 b = tbl[t * tok_stride + j * 8 + boff];
-                    if (!bact) b = make_uint2(0u, 0u);
-                    mma16816(d[t], a, b.x, b.y);
-                }
+                // xy: tile A (digit 0 in col 2g, digit 1 in col 2g+1); zw: tile B (digits 2, 3)
+                const uint4 b = *reinterpret_cast<const uint4 *>(bp[t] + s * 16);
+                imma16832<SIGNED>(da[t], a, b.x, b.y);
+                imma16832<SIGNED>(db[t], a, b.z, b.w);
             }
         }
 #pragma unroll
         for (int t = 0; t < NT; t++) {
-            acc[t][0] = fmaf(ds[h][0], d[t][0] + d[t][1], acc[t][0]);
-            acc[t][1] = fmaf(ds[h][1], d[t][2] + d[t][3], acc[t][1]);
-        }
-    }
-    if (DT == GGUF_Q4_K) {
-#pragma unroll
-        for (int t = 0; t < NT; t++) {
-            if (t < m) {
-                const float2 s = *reinterpret_cast<const float2 *>(asum + t * asum_stride + 2 * g);
-                acc[t][0] -= fmaf(mn[0][0], s.x, mn[1][0] * s.y);
-                acc[t][1] -= fmaf(mn[0][1], s.x, mn[1][1] * s.y);
+            // digit pairs: lo = d1*2^7 + d0, hi = d3*2^7 + d2 (each exact in s32)
+            int lo0 = da[t][1] * 128 + da[t][0], hi0 = db[t][1] * 128 + db[t][0];  // row r
+            int lo1 = da[t][3] * 128 + da[t][2], hi1 = db[t][3] * 128 + db[t][2];  // row r + 8
+            if (DT == GGUF_Q4_0) {  // sum (n - 8) X = sum n X - 8 sum X, per digit pair
+                const int2 sx = *reinterpret_cast<const int2 *>(sint + (t * s_stride + 2 * g + h) * 2);
+                lo0 -= 8 * sx.x;
+                lo1 -= 8 * sx.x;
+                hi0 -= 8 * sx.y;
+                hi1 -= 8 * sx.y;
+            }
+            const float v0 = fmaf((float)hi0, 16384.f, (float)lo0);
+            const float v1 = fmaf((float)hi1, 16384.f, (float)lo1);
+            acc[t][0] = fmaf(ds[h][0], v0, acc[t][0]);
+            acc[t][1] = fmaf(ds[h][1], v1, acc[t][1]);
+            if (DT == GGUF_Q4_K) {  // - dmin*m * sum X
+                const float sx = sflt[t * s_stride + 2 * g + h];
+                acc[t][0] = fmaf(-mn[h][0], sx, acc[t][0]);
+                acc[t][1] = fmaf(-mn[h][1], sx, acc[t][1]);
             }
         }
     }
@@ -298,26 +281,35 @@ __device__ __forceinline__ void process_chunk(const ChunkRegs<DT> &c, float (&ac
 
 // Shared-memory carve-up, identical on host and device.
 struct SmemLayout {
-    size_t mbar, ring, tbl, qsum, asum, red, scl, total;
+    size_t mbar, zero, ring, xs, tbl, ssum, sint, sflt, red, scl, total;
 };
 
 __host__ __device__ inline size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
 
-__host__ __device__ inline SmemLayout smem_layout(int dt, int nt, int m, int stages, int window) {
+constexpr int kXBar = 8 * kMaxStages;  // index of the activation-staging mbarrier
+
+__host__ __device__ inline SmemLayout smem_layout(int dt, int nt, int stages, int cps) {
     SmemLayout L;
     size_t o = 0;
     L.mbar = o;
-    o += 8 * kMaxStages * 8;
+    o += (kXBar + 1) * 8;
+    o = align_up(o, 16);
+    L.zero = o;
+    o += 1024;
     o = align_up(o, 128);
     L.ring = o;
     o += (size_t)8 * stages * chunk_bytes(dt);
     o = align_up(o, 16);
+    L.xs = o;
+    o += (size_t)nt * cps * CHUNK_K * 4;
     L.tbl = o;
-    o += (size_t)m * window * 128 * 8;
-    L.qsum = o;
-    o += (size_t)m * window * 64 * 4;
-    L.asum = o;
-    o += (size_t)m * window * 8 * 4;
+    o += (size_t)nt * cps * 128 * 8;
+    L.ssum = o;
+    o += (size_t)nt * cps * 32 * 8;
+    L.sint = o;
+    o += (size_t)nt * cps * 8 * 8;
+    L.sflt = o;
+    o += (size_t)nt * cps * 8 * 4;
     L.red = o;
     o += (size_t)8 * nt * 16 * 4;
     L.scl = o;
@@ -326,61 +318,117 @@ __host__ __device__ inline SmemLayout smem_layout(int dt, int nt, int m, int sta
     return L;
 }
 
+// Balanced base-128 digits of a fixed-point activation |X| <= 2^27:
+// X = d3*2^21 + d2*2^14 + d1*2^7 + d0, each digit in [-64, 64].
+__device__ __forceinline__ void digits4(int X, int (&d)[4]) {
+    d[0] = ((X + 64) & 127) - 64;
+    int r = (X - d[0]) >> 7;
+    d[1] = ((r + 64) & 127) - 64;
+    r = (r - d[1]) >> 7;
+    d[2] = ((r + 64) & 127) - 64;
+    d[3] = (r - d[2]) >> 7;
+}
+
+__device__ __forceinline__ uint32_t pack4(int b0, int b1, int b2, int b3) {
+    return (uint32_t)(b0 & 0xFF) | ((uint32_t)(b1 & 0xFF) << 8) | ((uint32_t)(b2 & 0xFF) << 16) |
+           ((uint32_t)(b3 & 0xFF) << 24);
+}
+
+__device__ __forceinline__ void cluster_sync() {
+    asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
+// A float in the shared memory of cluster CTA `rank`, at the offset of `local`.
+__device__ __forceinline__ float ld_cluster(const float *local, uint32_t rank) {
+    uint32_t remote;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(remote) : "r"(smem_u32(local)), "r"(rank));
+    float v;
+    asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(remote) : "memory");
+    return v;
+}
+
+// Cross-CTA reduction of split-K partial sums.
+enum : int { kRedNone = 0, kRedCluster = 1, kRedScratch = 2 };
+
 template <int DT, int NT, int RT>
 __global__ void __launch_bounds__(256, 2) gemv_kernel(GemvArgs p) {
     constexpr int KQ = 8 / RT;
     constexpr int CB = chunk_bytes(DT);
+    constexpr int FIXED_BITS = 27;  // |x * scale| < 2^27: four int8 digits
     extern __shared__ __align__(128) uint8_t smem[];
-    const int m = p.m, S = p.stages, W = p.window;
-    const SmemLayout L = smem_layout(DT, NT, m, S, W);
+    const int m = p.m, S = p.stages, cps = p.cps;
+    const SmemLayout L = smem_layout(DT, NT, S, cps);
     uint64_t *mbar = reinterpret_cast<uint64_t *>(smem + L.mbar);
+    const uint2 *zero = reinterpret_cast<const uint2 *>(smem + L.zero);
     uint8_t *ring = smem + L.ring;
-    uint2 *tbl = reinterpret_cast<uint2 *>(smem + L.tbl);    // [m][W][16 steps][8]
-    float *qsum = reinterpret_cast<float *>(smem + L.qsum);  // [m][W][4 groups][16 steps]
-    float *asum = reinterpret_cast<float *>(smem + L.asum);  // [m][W][8 sub-blocks]
-    float *red = reinterpret_cast<float *>(smem + L.red);    // [8 warps][NT][16]
-    float *scl = reinterpret_cast<float *>(smem + L.scl);    // [NT] scale, [NT] inverse
+    float *xs = reinterpret_cast<float *>(smem + L.xs);     // [NT][cps * 256] this CTA's slice of x
+    uint2 *tbl = reinterpret_cast<uint2 *>(smem + L.tbl);   // [NT][cps][8 steps][4 groups][2 parts][2 tiles]
+    int2 *ssum = reinterpret_cast<int2 *>(smem + L.ssum);   // [NT][cps][4 groups][8 steps] (lo, hi pair sums)
+    int *sint = reinterpret_cast<int *>(smem + L.sint);     // [NT][cps][8 units][2]
+    float *sflt = reinterpret_cast<float *>(smem + L.sflt); // [NT][cps][8 units]
+    float *red = reinterpret_cast<float *>(smem + L.red);   // [8 warps][NT][16]
+    float *scl = reinterpret_cast<float *>(smem + L.scl);   // [NT] scale, [NT] inverse
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
 
-    const int cps = p.cps;
     const int c0 = blockIdx.y * cps;
     const int nc = min(cps, p.g.n_chunks - c0);
     const int rt_local = warp % RT, kq = warp / RT;
     const int tile = blockIdx.x * RT + rt_local;
     const bool tile_ok = tile < p.g.n_tiles;
-    // chunks of this warp: kq, kq + KQ, ... (< nc), the i-th in ring slot i % S
+    // chunks of this warp: kq, kq + KQ, ... (< nc)
     const int nw = (tile_ok && kq < nc) ? (nc - kq + KQ - 1) / KQ : 0;
     const uint8_t *gsrc = p.w + ((size_t)(tile_ok ? tile : 0) * p.g.n_chunks + c0) * CB;
     const uint32_t mb0 = smem_u32(mbar + warp * kMaxStages);
     const uint32_t ring0 = smem_u32(ring + (size_t)warp * S * CB);
+    const uint32_t xbar = smem_u32(mbar + kXBar);
+    const int64_t k_lo = (int64_t)c0 * CHUNK_K;
+    const int64_t k_hi = min((int64_t)(c0 + nc) * CHUNK_K, p.g.n_cols);
+    const int xn = (int)(k_hi - k_lo);  // activations of this slice (a multiple of 32)
 
-    // Weight copies do not depend on x: start them before anything else.
+    // Weight copies and the activation slice do not depend on each other:
+    // start them all before anything else.
     if (lane == 0) {
         for (int s = 0; s < S; s++) mbar_init(mb0 + 8 * s, 1);
+        if (warp == 0) mbar_init(xbar, 1);
         fence_mbar_init();
         for (int i = 0; i < min(S, nw); i++)
             bulk_load(ring0 + i * CB, gsrc + (size_t)(kq + i * KQ) * CB, CB, mb0 + 8 * i);
+        if (warp == 0 && p.x_vec4) {
+            asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(xbar),
+                         "r"((uint32_t)(m * xn * 4))
+                         : "memory");
+            for (int t = 0; t < m; t++)
+                asm volatile(
+                    "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                        smem_u32(xs + t * cps * CHUNK_K)),
+                    "l"(p.x + t * p.ldx + k_lo), "r"((uint32_t)(xn * 4)), "r"(xbar)
+                    : "memory");
+        }
     }
-    __syncwarp();
+    reinterpret_cast<uint32_t *>(smem + L.zero)[tid] = 0u;  // 256 x 4 B
+    if (!p.x_vec4) {  // unaligned activations: plain loads
+        for (int t = 0; t < m; t++)
+            for (int k = tid; k < xn; k += 256) xs[t * cps * CHUNK_K + k] = p.x[t * p.ldx + k_lo + k];
+    }
+    for (int t = m; t < NT; t++)  // padding tokens are zero
+        for (int k = tid; k < xn; k += 256) xs[t * cps * CHUNK_K + k] = 0.f;
+    __syncthreads();  // barrier inits visible before anyone waits
+    bool failed = false;
+    if (p.x_vec4 && !mbar_wait_bounded(xbar, 0u)) failed = true;
 
-    // Per-token power-of-two scale for this CTA's column slice.
-    const int64_t k_lo = (int64_t)c0 * CHUNK_K;
-    const int64_t k_hi = min((int64_t)(c0 + nc) * CHUNK_K, p.g.n_cols);
+    // Per-token power-of-two scale for this CTA's column slice: x * scale
+    // lies inside +-2^FIXED_BITS.
 #pragma unroll
     for (int t = 0; t < NT; t++) {
         float mx = 0.f;
-        if (t < m) {
-            const float *xr = p.x + t * p.ldx;
-            for (int64_t k = k_lo + 4 * tid; k < k_hi; k += 1024) {
-                float4 v;
-                if (p.x_vec4) {
-                    v = *reinterpret_cast<const float4 *>(xr + k);
-                } else {
-                    v = make_float4(xr[k], xr[k + 1], xr[k + 2], xr[k + 3]);
-                }
-                mx = fmaxf(mx, fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w))));
-            }
+        bool fin = true;
+        const float4 *xr = reinterpret_cast<const float4 *>(xs + t * cps * CHUNK_K);
+        for (int k4 = tid; k4 < xn / 4; k4 += 256) {
+            const float4 v = xr[k4];
+            mx = fmaxf(mx, fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w))));
+            fin = fin && isfinite(v.x) && isfinite(v.y) && isfinite(v.z) && isfinite(v.w);
         }
+        if (!fin) mx = INFINITY;
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
         if (lane == 0) red[warp * NT + t] = mx;
@@ -390,112 +438,121 @@ __global__ void __launch_bounds__(256, 2) gemv_kernel(GemvArgs p) {
         float v = 0.f;
         for (int w = 0; w < 8; w++) v = fmaxf(v, red[w * NT + tid]);
         float s = 1.f, inv = 1.f;
-        if (v > 0.f && isfinite(v)) {
+        if (!isfinite(v)) {
+            s = 0.f;  // non-finite activations: the outputs become NaN
+            inv = __int_as_float(0x7fc00000);
+        } else if (v > 0.f) {
             int e;
             frexpf(v, &e);  // v < 2^e
             e = max(-100, min(100, e));
-            s = ldexpf(1.f, 14 - e);
-            inv = ldexpf(1.f, e - 14);
+            s = ldexpf(1.f, FIXED_BITS - e);
+            inv = ldexpf(1.f, e - FIXED_BITS);
         }
         scl[tid] = s;
         scl[NT + tid] = inv;
     }
+    __syncthreads();
+
+    // Activation table: per (token, chunk, group gg, step s) the digits of the
+    // 8 values 64 gg + 8 s + 0..7 as B fragments, and their pair sums.
+    for (int idx = tid; idx < NT * nc * 32; idx += 256) {
+        const int t = idx / (nc * 32), rem = idx % (nc * 32);
+        const int c = rem >> 5, q = rem & 31, gg = q >> 3, s = q & 7;
+        const int k = c * CHUNK_K + 64 * gg + 8 * s;
+        float v[8];
+        if (k < xn) {
+            const float4 f0 = *reinterpret_cast<const float4 *>(xs + t * cps * CHUNK_K + k);
+            const float4 f1 = *reinterpret_cast<const float4 *>(xs + t * cps * CHUNK_K + k + 4);
+            v[0] = f0.x; v[1] = f0.y; v[2] = f0.z; v[3] = f0.w;
+            v[4] = f1.x; v[5] = f1.y; v[6] = f1.z; v[7] = f1.w;
+        } else {
+#pragma unroll
+            for (int e = 0; e < 8; e++) v[e] = 0.f;
+        }
+        const float sc = scl[t];
+        int dg[8][4];
+        int slo = 0, shi = 0;
+#pragma unroll
+        for (int e = 0; e < 8; e++) {
+            digits4(__float2int_rn(v[e] * sc), dg[e]);
+            slo += dg[e][1] * 128 + dg[e][0];
+            shi += dg[e][3] * 128 + dg[e][2];
+        }
+        uint4 *dst = reinterpret_cast<uint4 *>(tbl + (size_t)(t * cps + c) * 128 + s * 16 + gg * 4);
+        // part 0 (col 2g): tile A digit 0, tile B digit 2; part 1 (col 2g+1): digits 1, 3
+        dst[0] = make_uint4(pack4(dg[0][0], dg[1][0], dg[2][0], dg[3][0]), pack4(dg[4][0], dg[5][0], dg[6][0], dg[7][0]),
+                            pack4(dg[0][2], dg[1][2], dg[2][2], dg[3][2]), pack4(dg[4][2], dg[5][2], dg[6][2], dg[7][2]));
+        dst[1] = make_uint4(pack4(dg[0][1], dg[1][1], dg[2][1], dg[3][1]), pack4(dg[4][1], dg[5][1], dg[6][1], dg[7][1]),
+                            pack4(dg[0][3], dg[1][3], dg[2][3], dg[3][3]), pack4(dg[4][3], dg[5][3], dg[6][3], dg[7][3]));
+        ssum[((t * cps + c) * 4 + gg) * 8 + s] = make_int2(slo, shi);
+    }
+    if (DT != GGUF_Q8_0) {
+        __syncthreads();
+        // unit u = group u/2, steps 4 (u%2) .. +3
+        for (int idx = tid; idx < NT * nc * 8; idx += 256) {
+            const int t = idx / (nc * 8), rem = idx % (nc * 8), c = rem >> 3, u = rem & 7;
+            const int2 *src = ssum + ((t * cps + c) * 4 + (u >> 1)) * 8 + 4 * (u & 1);
+            const int lo = src[0].x + src[1].x + src[2].x + src[3].x;
+            const int hi = src[0].y + src[1].y + src[2].y + src[3].y;
+            sint[((t * cps + c) * 8 + u) * 2] = lo;
+            sint[((t * cps + c) * 8 + u) * 2 + 1] = hi;
+            sflt[(t * cps + c) * 8 + u] = fmaf((float)hi, 16384.f, (float)lo);
+        }
+    }
+    __syncthreads();
 
     float acc[NT][2];
 #pragma unroll
     for (int t = 0; t < NT; t++) acc[t][0] = acc[t][1] = 0.f;
+    // B fragments: lane (n = lane / 4, k-group lane % 4) reads column n; the
+    // block-diagonal operand is non-zero only where n / 2 == k-group.
     const bool bact = (lane >> 3) == (lane & 3);
-    const int boff = (lane & 3) * 2 + ((lane >> 2) & 1);
-    int i = 0;          // next chunk of this warp
-    bool failed = false;
-
-    for (int win0 = 0; win0 < nc; win0 += W) {
-        const int wn = min(W, nc - win0);
-        __syncthreads();  // scales ready; the previous window's table is no longer read
-        // Activation table for chunks [win0, win0 + wn): per (token, chunk,
-        // step j, group g, part) one uint2 = the B fragment (x[e0], x[e2]),
-        // (x[e1], x[e3]) as fp16, part 0 = hi, part 1 = lo remainder.
-        for (int idx = tid; idx < m * wn * 64; idx += 256) {
-            const int t = idx / (wn * 64), rem = idx % (wn * 64);
-            const int c = rem >> 6, q = rem & 63, gg = q >> 4, j = q & 15;
-            const int64_t k = (int64_t)(c0 + win0 + c) * CHUNK_K + 64 * gg + 4 * j;
-            const float s = scl[t];
-            float v[4] = {0.f, 0.f, 0.f, 0.f};
-            if (k < p.g.n_cols) {
-                const float *xr = p.x + t * p.ldx + k;
-                if (p.x_vec4) {
-                    const float4 f = *reinterpret_cast<const float4 *>(xr);
-                    v[0] = f.x;
-                    v[1] = f.y;
-                    v[2] = f.z;
-                    v[3] = f.w;
-                } else {
-                    v[0] = xr[0];
-                    v[1] = xr[1];
-                    v[2] = xr[2];
-                    v[3] = xr[3];
-                }
-            }
-            __half hi[4], lo[4];
-            float sum = 0.f;
-#pragma unroll
-            for (int e = 0; e < 4; e++) {
-                const float vs = v[e] * s;
-                sum += vs;
-                hi[e] = __float2half_rn(vs);
-                lo[e] = __float2half_rn(vs - __half2float(hi[e]));
-            }
-            uint2 *dst = tbl + ((size_t)(t * W + c) * 16 + j) * 8 + gg * 2;
-            dst[0] = make_uint2(__half_as_ushort(hi[0]) | ((uint32_t)__half_as_ushort(hi[2]) << 16),
-                                __half_as_ushort(hi[1]) | ((uint32_t)__half_as_ushort(hi[3]) << 16));
-            dst[1] = make_uint2(__half_as_ushort(lo[0]) | ((uint32_t)__half_as_ushort(lo[2]) << 16),
-                                __half_as_ushort(lo[1]) | ((uint32_t)__half_as_ushort(lo[3]) << 16));
-            qsum[(t * W + c) * 64 + gg * 16 + j] = sum;
+    const int boff = (lane & 3) * 4 + ((lane >> 2) & 1) * 2;
+    int i = 0, slot = 0;
+    uint32_t phase = 0;
+    while (!failed && i < nw) {
+        const int cl = kq + i * KQ;
+        if (!mbar_wait_bounded(mb0 + 8 * slot, phase)) {
+            failed = true;
+            break;
         }
-        if (DT == GGUF_Q4_K) {
-            __syncthreads();
-            // sub-block u of a chunk = group u/2, steps 8 (u%2) .. +7
-            for (int idx = tid; idx < m * wn * 8; idx += 256) {
-                const int t = idx / (wn * 8), rem = idx % (wn * 8), c = rem >> 3, u = rem & 7;
-                const float *qs = qsum + (t * W + c) * 64 + (u >> 1) * 16 + 8 * (u & 1);
-                float s = 0.f;
-#pragma unroll
-                for (int jj = 0; jj < 8; jj++) s += qs[jj];
-                asum[(t * W + c) * 8 + u] = s;
-            }
+        ChunkRegs<DT> cur;
+        load_chunk<DT>(cur, ring + ((size_t)warp * S + slot) * CB, lane);
+        __syncwarp();
+        if (lane == 0 && i + S < nw) {
+            fence_proxy_async();  // this slot's reads happen before the copy that refills it
+            bulk_load(ring0 + slot * CB, gsrc + (size_t)(kq + (i + S) * KQ) * CB, CB, mb0 + 8 * slot);
         }
-        __syncthreads();
-
-        while (!failed && i < nw && kq + i * KQ < win0 + wn) {
-            const int cl = kq + i * KQ;
-            const int slot = i % S;
-            if (!mbar_wait_bounded(mb0 + 8 * slot, (uint32_t)((i / S) & 1))) {
-                failed = true;
-                break;
-            }
-            ChunkRegs<DT> cur;
-            load_chunk<DT>(cur, ring + ((size_t)warp * S + slot) * CB, lane);
-            __syncwarp();
-            if (lane == 0 && i + S < nw) {
-                fence_proxy_async();  // this slot's reads happen before the copy that refills it
-                bulk_load(ring0 + slot * CB, gsrc + (size_t)(kq + (i + S) * KQ) * CB, CB, mb0 + 8 * slot);
-            }
-            process_chunk<DT, NT>(cur, acc, tbl + (size_t)(cl - win0) * 128, W * 128, asum + (cl - win0) * 8, W * 8,
-                                  m, lane, bact, boff);
-            i++;
+        const uint2 *bp[NT];
+#pragma unroll
+        for (int t = 0; t < NT; t++) bp[t] = bact ? tbl + (size_t)(t * cps + cl) * 128 + boff : zero;
+        process_chunk<DT, NT>(cur, acc, bp, sint + cl * 16, sflt + cl * 8, cps * 8, lane);
+        i++;
+        if (++slot == S) {
+            slot = 0;
+            phase ^= 1u;
         }
     }
     if (failed) {
         // Report, then let this warp's copies in flight land before exiting.
         if (lane == 0) {
             *reinterpret_cast<volatile int *>(p.err) = kKernelErrWaitTimeout;
-            for (int j = i; j < min(nw, i + S); j++) mbar_wait_bounded(mb0 + 8 * (j % S), (uint32_t)((j / S) & 1));
+            int sl = slot;
+            uint32_t ph = phase;
+            for (int j = i; j < min(nw, i + S); j++) {
+                mbar_wait_bounded(mb0 + 8 * sl, ph);
+                if (++sl == S) {
+                    sl = 0;
+                    ph ^= 1u;
+                }
+            }
+            if (warp == 0 && p.x_vec4) mbar_wait_bounded(xbar, 0u);
         }
         __syncwarp();
     }
 
     // Sum the four column groups of each row (lanes 4r .. 4r+3), then the KQ
-    // warps of each tile in a fixed order.
+    // warps of each tile in a fixed order, and undo the activation scale.
     __syncthreads();
 #pragma unroll
     for (int t = 0; t < NT; t++) {
@@ -510,21 +567,41 @@ __global__ void __launch_bounds__(256, 2) gemv_kernel(GemvArgs p) {
         }
     }
     __syncthreads();
-    for (int idx = tid; idx < RT * m * 16; idx += 256) {
-        const int rtl = idx / (m * 16), rem = idx % (m * 16), t = rem >> 4, r16 = rem & 15;
+    // part[rtl][t][r16] = this CTA's partial sums; reuses the front of xs
+    float *part = xs;
+    for (int idx = tid; idx < RT * NT * 16; idx += 256) {
+        const int rtl = idx / (NT * 16), rem = idx % (NT * 16), t = rem >> 4, r16 = rem & 15;
         float v = 0.f;
 #pragma unroll
         for (int q = 0; q < KQ; q++) v += red[((rtl + q * RT) * NT + t) * 16 + r16];
         v *= scl[NT + t];
         const int64_t row = (int64_t)(blockIdx.x * RT + rtl) * 16 + r16;
-        if (row < p.g.n_rows) {
+        if (p.red_mode == kRedCluster) {
+            part[idx] = v;
+        } else if (t < m && row < p.g.n_rows) {
             if (p.k_splits == 1)
                 p.y[t * p.ldy + row] = v;
             else
                 p.partial[((size_t)blockIdx.y * m + t) * p.n_pad + row] = v;
         }
     }
-    if (p.k_splits > 1) {
+    if (p.red_mode == kRedCluster) {
+        // The k_splits CTAs of this row block form one cluster (ranks =
+        // blockIdx.y); rank 0 adds their partial sums in rank order.
+        cluster_sync();
+        if (blockIdx.y == 0) {
+            for (int idx = tid; idx < RT * NT * 16; idx += 256) {
+                const int rtl = idx / (NT * 16), rem = idx % (NT * 16), t = rem >> 4, r16 = rem & 15;
+                const int64_t row = (int64_t)(blockIdx.x * RT + rtl) * 16 + r16;
+                if (t < m && row < p.g.n_rows) {
+                    float v = 0.f;
+                    for (int q = 0; q < p.k_splits; q++) v += ld_cluster(part + idx, (uint32_t)q);
+                    p.y[t * p.ldy + row] = v;
+                }
+            }
+        }
+        cluster_sync();  // keep every CTA's shared memory alive until rank 0 has read it
+    } else if (p.red_mode == kRedScratch) {
         __shared__ int is_last;
         __threadfence();
         __syncthreads();
@@ -587,8 +664,21 @@ cudaError_t launch_one(const GemvArgs &a, dim3 grid, size_t smem, cudaStream_t s
     auto kern = gemv_kernel<DT, NT, RT>;
     cudaError_t e = ensure_smem_optin(kern, done);
     if (e != cudaSuccess) return e;
-    kern<<<grid, 256, smem, s>>>(a);
-    return cudaGetLastError();
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = dim3(256, 1, 1);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    if (a.red_mode == kRedCluster) {
+        attr[0].id = cudaLaunchAttributeClusterDimension;
+        attr[0].val.clusterDim.x = 1;
+        attr[0].val.clusterDim.y = grid.y;
+        attr[0].val.clusterDim.z = 1;
+        cfg.attrs = attr;
+        cfg.numAttrs = 1;
+    }
+    return cudaLaunchKernelEx(&cfg, kern, a);
 }
 
 template <int DT, int RT>
@@ -617,33 +707,56 @@ cudaError_t launch_rt(int rt, int nt, const GemvArgs &a, dim3 grid, size_t smem,
 GemvPlan plan_gemv(int dt, const Geometry &g, int m, int sm_count) {
     GemvPlan p;
     p.nt = m <= 1 ? 1 : m <= 2 ? 2 : 4;
-    // Tiles per CTA: the fewest that keep every CTA resident in one wave (two
-    // CTAs per SM).  Split K across CTAs only if the rows leave SMs idle.
-    const int wave = 2 * sm_count;
-    int rt = 1;
-    while (rt < 8 && (g.n_tiles + rt - 1) / rt > wave) rt *= 2;
-    p.rt = rt;
-    const int kq = 8 / rt;
-    const int rows_ctas = (g.n_tiles + rt - 1) / rt;
-    int ks = 1;
-    if (rows_ctas < sm_count) {
-        ks = (sm_count + rows_ctas - 1) / rows_ctas;
+    // The activation slice and its table take nt x cps x 2 KB of shared
+    // memory: at most 8 chunks per CTA.  Nothing below depends on m, so a
+    // token's result is the same whatever the batch.
+    const int cps_cap = 8;
+    const int ks_min = (g.n_chunks + cps_cap - 1) / cps_cap;
+    // Tiles per CTA and the K split: the largest tile count (one warp per
+    // tile: the CTA's activation table serves 8 tiles) whose grid still
+    // covers every SM, within one resident wave (two CTAs per SM).
+    int best_rt = 1, best_ks = ks_min, best_ctas = -1;
+    for (int rt = 8; rt >= 1; rt /= 2) {
+        const int kq = 8 / rt;
+        const int rows = (g.n_tiles + rt - 1) / rt;
+        int ks = (2 * sm_count) / rows;
         if (ks > 8) ks = 8;
-        const int max_ks = g.n_chunks / kq;  // at least one chunk per warp
-        if (ks > max_ks) ks = max_ks < 1 ? 1 : max_ks;
+        if (ks > g.n_chunks / kq) ks = g.n_chunks / kq;  // at least one chunk per warp
+        if (ks < ks_min) ks = ks_min;
+        if (ks < 1) ks = 1;
+        const int cps = (g.n_chunks + ks - 1) / ks;
+        ks = (g.n_chunks + cps - 1) / cps;
+        const int ctas = rows * ks;
+        if (ctas > best_ctas) {
+            best_rt = rt;
+            best_ks = ks;
+            best_ctas = ctas;
+        }
+        if (ctas >= sm_count) break;
     }
-    p.cps = (g.n_chunks + ks - 1) / ks;
+    p.rt = best_rt;
+    p.cps = (g.n_chunks + best_ks - 1) / best_ks;
     p.k_splits = (g.n_chunks + p.cps - 1) / p.cps;
-    p.stages = dt == GGUF_Q8_0 ? 2 : (p.nt <= 2 ? 4 : 2);
-    int w = 16 / p.nt;
-    if (w < kq) w = kq;
-    w = (w + kq - 1) / kq * kq;
-    if (w > p.cps) w = p.cps;
-    p.window = w;
-    p.smem = smem_layout(dt, p.nt, m, p.stages, p.window).total;
-    if (p.k_splits > 1) {
+    p.red_mode = p.k_splits == 1 ? kRedNone : (p.k_splits <= 8 ? kRedCluster : kRedScratch);
+    // TMA ring depth: as deep as shared memory allows for two CTAs per SM
+    p.stages = kMaxStages;
+    while (p.stages > 2 && smem_layout(dt, p.nt, p.stages, p.cps).total > 110 * 1024) p.stages--;
+    (void)m;
+    p.window = p.cps;
+    p.smem = smem_layout(dt, p.nt, p.stages, p.cps).total;
+    if (p.red_mode == kRedScratch) {
         p.scratch_floats = (size_t)p.k_splits * m * g.n_tiles * 16;
-        p.counters = rows_ctas;
+        p.counters = (g.n_tiles + p.rt - 1) / p.rt;
+    }
+    return p;
+}
+
+GemvPlan plan_gemv_scratch(int dt, const Geometry &g, int m, int sm_count) {
+    GemvPlan p = plan_gemv(dt, g, m, sm_count);
+    if (p.red_mode == kRedCluster) {
+        p.red_mode = kRedScratch;
+        p.scratch_floats = (size_t)p.k_splits * m * g.n_tiles * 16;
+        p.counters = (g.n_tiles + p.rt - 1) / p.rt;
     }
     return p;
 }
@@ -652,7 +765,8 @@ cudaError_t launch_gemv(int dt, const uint8_t *tiles, const Geometry &g, const f
                         float *y, size_t ldy, int m, const GemvPlan &plan, float *scratch,
                         unsigned *counters, int *err, cudaStream_t s) {
     if (m <= 0 || g.n_rows <= 0) return cudaSuccess;
-    if (m > plan.nt || m > 4) return cudaErrorInvalidValue;
+    if (m > plan.nt || m > kGemvMaxTokens) return cudaErrorInvalidValue;
+    if (plan.red_mode == kRedScratch && (!scratch || !counters)) return cudaErrorInvalidValue;
     GemvArgs a;
     a.w = tiles;
     a.x = x;
@@ -668,7 +782,7 @@ cudaError_t launch_gemv(int dt, const uint8_t *tiles, const Geometry &g, const f
     a.k_splits = plan.k_splits;
     a.n_pad = g.n_tiles * 16;
     a.stages = plan.stages;
-    a.window = plan.window;
+    a.red_mode = plan.red_mode;
     a.x_vec4 = ((ldx & 3) == 0 && (reinterpret_cast<uintptr_t>(x) & 15) == 0) ? 1 : 0;
     dim3 grid((g.n_tiles + plan.rt - 1) / plan.rt, plan.k_splits);
     switch (dt) {

@@ -31,12 +31,16 @@ struct GemvPlan {
     int cps = 0;         // chunks per split
     int nt = 1;          // token slots compiled in (1, 2 or 4)
     int stages = 4;      // TMA ring depth per warp
-    int window = 16;     // chunks per activation-table window
+    int window = 16;     // chunks of activations staged per CTA
+    int red_mode = 0;    // split-K reduction: 0 none, 1 cluster shared memory, 2 global scratch
     size_t smem = 0;     // dynamic shared memory
     size_t scratch_floats = 0;  // partial sums
     int counters = 0;    // arrival counters (k_splits > 1)
 };
 GemvPlan plan_gemv(int dt, const Geometry &g, int m, int sm_count);
+// The same plan with any K split reduced through global scratch (for callers
+// that supply their own scratch) instead of cluster shared memory.
+GemvPlan plan_gemv_scratch(int dt, const Geometry &g, int m, int sm_count);
 cudaError_t launch_gemv(int dt, const uint8_t *tiles, const Geometry &g, const float *x, size_t ldx,
                         float *y, size_t ldy, int m, const GemvPlan &plan, float *scratch,
                         unsigned *counters, int *err, cudaStream_t s);

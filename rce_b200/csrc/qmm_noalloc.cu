@@ -1,21 +1,21 @@
 // qmm_noalloc.cu -- rce_qmm_mm_batched_device_noalloc, the decode matmul for
 // callers that cannot allocate device memory: a custom allocator that owns
 // all of the device's memory, a serving loop that forbids cudaMalloc after
-// start-up, or a host that only hands us pointers it already owns.  The
-// regular device entry point allocates its split-K scratch on a stream's
-// first use; this one takes that scratch from a fixed array compiled into the
-// library instead, and calls no cudaMalloc, cudaFree or allocating library
-// routine.
+// start-up, or a host that only hands us pointers it already owns.  When it
+// splits K across CTAs, this entry point always adds the partial sums through
+// a fixed array compiled into the library (the regular entry point uses
+// cluster shared memory, or for the widest splits a per-stream scratch it
+// allocates on first use); it calls no cudaMalloc, cudaFree or allocating
+// library routine.
 //
 // Limits and sharing:
 //  * the array holds kNoAllocPartialFloats split-K partial sums (1 MiB) and
 //    kNoAllocCounters arrival counters (4 KiB); every GPU that loads the
-//    library keeps them until the process exits.  The planner splits K only
-//    for weights of fewer than ~148 row blocks, so a split needs at most
-//    ~2 x 148 x 16 rows x 4 tokens partial sums, well inside the array; a
-//    shape that would need more (k_splits x min(t_rows, 4) x 16 *
-//    ceil(n_rows / 16) floats) is rejected with RCE_QMM_ERR_UNSUPPORTED
-//    before anything is launched;
+//    library keeps them until the process exits.  A split needs
+//    k_splits x min(t_rows, 4) x 16 * ceil(n_rows / 16) floats; the planner
+//    splits K only while the row blocks alone leave SMs idle, so the decode
+//    shapes need well under the limit, and a shape that would need more is
+//    rejected with RCE_QMM_ERR_UNSUPPORTED before anything is launched;
 //  * all calls on a device share the one array and it keeps the last call's
 //    contents: each call clears the counters it uses before its kernels, and
 //    calls whose work overlaps on the GPU (different streams, or different
@@ -111,8 +111,8 @@ extern "C" int rce_qmm_mm_batched_device_noalloc(rce_qmm_ctx *ctx, const float *
     if (cd.status != cudaSuccess)
         return err(RCE_QMM_ERR_CUDA, "mm_batched_device_noalloc: set device: %s", cudaGetErrorString(cd.status));
     const int m_max = (int)(t_rows < (size_t)rce::kGemvMaxTokens ? t_rows : (size_t)rce::kGemvMaxTokens);
-    const rce::GemvPlan worst = rce::plan_gemv(w->dtype, g, m_max, ctx->sm_count);
-    if (worst.k_splits > 1 &&
+    const rce::GemvPlan worst = rce::plan_gemv_scratch(w->dtype, g, m_max, ctx->sm_count);
+    if (worst.scratch_floats > 0 &&
         (worst.scratch_floats > kNoAllocPartialFloats || (size_t)worst.counters > kNoAllocCounters))
         return err(RCE_QMM_ERR_UNSUPPORTED,
                    "mm_batched_device_noalloc: a %lld x %lld weight with %d tokens per pass needs %zu split-K partial "
@@ -124,7 +124,7 @@ extern "C" int rce_qmm_mm_batched_device_noalloc(rce_qmm_ctx *ctx, const float *
     int rc = noalloc_addresses(ctx->device, &partials, &counters);
     if (rc) return rc;
     cudaStream_t s = static_cast<cudaStream_t>(stream);
-    if (worst.k_splits > 1) {
+    if (worst.scratch_floats > 0) {
         cudaError_t e = cudaMemsetAsync(counters, 0, (size_t)worst.counters * sizeof(unsigned), s);
         if (e != cudaSuccess)
             return err(RCE_QMM_ERR_CUDA, "mm_batched_device_noalloc: clear counters: %s", cudaGetErrorString(e));
@@ -132,10 +132,10 @@ extern "C" int rce_qmm_mm_batched_device_noalloc(rce_qmm_ctx *ctx, const float *
     for (size_t t0 = 0; t0 < t_rows;) {
         const size_t left = t_rows - t0;
         const int m = (int)(left < (size_t)rce::kGemvMaxTokens ? left : (size_t)rce::kGemvMaxTokens);
-        const rce::GemvPlan plan = rce::plan_gemv(w->dtype, g, m, ctx->sm_count);
+        const rce::GemvPlan plan = rce::plan_gemv_scratch(w->dtype, g, m, ctx->sm_count);
         cudaError_t e = rce::launch_gemv(w->dtype, w->dev, g, d_a + t0 * lda, lda, d_out + t0 * ldo, ldo, m, plan,
-                                         plan.k_splits > 1 ? partials : nullptr,
-                                         plan.k_splits > 1 ? counters : nullptr, ctx->err_dev, s);
+                                         plan.scratch_floats > 0 ? partials : nullptr,
+                                         plan.scratch_floats > 0 ? counters : nullptr, ctx->err_dev, s);
         if (e != cudaSuccess)
             return err(RCE_QMM_ERR_CUDA, "mm_batched_device_noalloc: launch: %s", cudaGetErrorString(e));
         t0 += (size_t)m;
