@@ -16,14 +16,15 @@
 //    (mma.sync m16n8k32, u8/s8 x s8 -> s32).  The weight codes are the A
 //    operand as they are stored: Q8_0's int8 bytes need no unpacking at all,
 //    Q4_K/Q4_0 nibbles one and/shift per 4 codes.  Activations become a
-//    fixed-point integer per token, x * 2^e rounded to 28 bits with the power
-//    of two chosen from the CTA's slice of x, split into four balanced int8
-//    digits; the B operand is block-diagonal so that lane g's columns hold
-//    digits of its own column group (tile A digits 0-1, tile B digits 2-3).
-//    Each digit pair's 32-value sub-block sum is exact in s32; the two pairs
-//    meet in f32 and the block scales (d, d*sc, dmin*m) are applied once per
-//    sub-block, so no weight is rounded and x keeps 2^-27 of its slice
-//    maximum (below f32's own rounding of the reference's sums).
+//    fixed-point integer per token, X = x * 2^e rounded to 31 bits with the
+//    power of two chosen from the CTA's slice of x, whose four balanced
+//    base-256 digits are simply the bytes of (X + 0x80808080) ^ 0x80808080;
+//    the B operand is block-diagonal so that lane g's columns hold digits of
+//    its own column group (tile A digits 0-1, tile B digits 2-3).  Each digit
+//    pair's 32-value sub-block sum is exact in s32; the two pairs meet in f32
+//    and the block scales (d, d*sc, dmin*m) are applied once per sub-block,
+//    so no weight is rounded and x keeps 2^-30 of its slice maximum (below
+//    f32's own rounding of the reference's sums).
 //  * Q4_K's min term and Q4_0's -8 offset use per-sub-block sums of the
 //    integer activations (the "asum hoist"): one op per sub-block.
 //  * The activation table (the B fragments) is built per window of chunks
@@ -113,6 +114,12 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint32_t bar, uint32_t parity)
         if (mbar_try_wait(bar, parity)) return true;
         if (globaltimer() - t0 > kWaitLimitNs) return false;
     }
+}
+
+__device__ __forceinline__ uint32_t prmt(uint32_t a, uint32_t b, uint32_t sel) {
+    uint32_t r;
+    asm("prmt.b32 %0, %1, %2, %3;" : "=r"(r) : "r"(a), "r"(b), "r"(sel));
+    return r;
 }
 
 // D(s32) += A(16x32, u8 or s8) x B(32x8, s8), exact.
@@ -256,9 +263,9 @@ __device__ __forceinline__ void process_chunk(const ChunkRegs<DT> &c, float (&ac
         }
 #pragma unroll
         for (int t = 0; t < NT; t++) {
-            // digit pairs: lo = d1*2^7 + d0, hi = d3*2^7 + d2 (each exact in s32)
-            int lo0 = da[t][1] * 128 + da[t][0], hi0 = db[t][1] * 128 + db[t][0];  // row r
-            int lo1 = da[t][3] * 128 + da[t][2], hi1 = db[t][3] * 128 + db[t][2];  // row r + 8
+            // digit pairs: lo = d1*2^8 + d0, hi = d3*2^8 + d2 (each exact in s32)
+            int lo0 = da[t][1] * 256 + da[t][0], hi0 = db[t][1] * 256 + db[t][0];  // row r
+            int lo1 = da[t][3] * 256 + da[t][2], hi1 = db[t][3] * 256 + db[t][2];  // row r + 8
             if (DT == GGUF_Q4_0) {  // sum (n - 8) X = sum n X - 8 sum X, per digit pair
                 const int2 sx = *reinterpret_cast<const int2 *>(sint + (t * s_stride + 2 * g + h) * 2);
                 lo0 -= 8 * sx.x;
@@ -266,8 +273,8 @@ __device__ __forceinline__ void process_chunk(const ChunkRegs<DT> &c, float (&ac
                 hi0 -= 8 * sx.y;
                 hi1 -= 8 * sx.y;
             }
-            const float v0 = fmaf((float)hi0, 16384.f, (float)lo0);
-            const float v1 = fmaf((float)hi1, 16384.f, (float)lo1);
+            const float v0 = fmaf((float)hi0, 65536.f, (float)lo0);
+            const float v1 = fmaf((float)hi1, 65536.f, (float)lo1);
             acc[t][0] = fmaf(ds[h][0], v0, acc[t][0]);
             acc[t][1] = fmaf(ds[h][1], v1, acc[t][1]);
             if (DT == GGUF_Q4_K) {  // - dmin*m * sum X
@@ -318,20 +325,19 @@ __host__ __device__ inline SmemLayout smem_layout(int dt, int nt, int stages, in
     return L;
 }
 
-// Balanced base-128 digits of a fixed-point activation |X| <= 2^27:
-// X = d3*2^21 + d2*2^14 + d1*2^7 + d0, each digit in [-64, 64].
-__device__ __forceinline__ void digits4(int X, int (&d)[4]) {
-    d[0] = ((X + 64) & 127) - 64;
-    int r = (X - d[0]) >> 7;
-    d[1] = ((r + 64) & 127) - 64;
-    r = (r - d[1]) >> 7;
-    d[2] = ((r + 64) & 127) - 64;
-    d[3] = (r - d[2]) >> 7;
-}
+// Balanced base-256 digits of a fixed-point activation |X| < 2^30: with
+// Y = X + 0x80808080 (mod 2^32) the bytes of Y are d_i + 128, so the bytes of
+// Y ^ 0x80808080 are the int8 digits d_i of X = sum d_i 256^i.
+__device__ __forceinline__ uint32_t biased(int X) { return (uint32_t)X + 0x80808080u; }
 
-__device__ __forceinline__ uint32_t pack4(int b0, int b1, int b2, int b3) {
-    return (uint32_t)(b0 & 0xFF) | ((uint32_t)(b1 & 0xFF) << 8) | ((uint32_t)(b2 & 0xFF) << 16) |
-           ((uint32_t)(b3 & 0xFF) << 24);
+// 4x4 byte transpose: out[d] = byte d of w0, w1, w2, w3 (low to high).
+__device__ __forceinline__ void transpose4(uint32_t w0, uint32_t w1, uint32_t w2, uint32_t w3, uint32_t (&o)[4]) {
+    const uint32_t t0 = prmt(w0, w1, 0x5140u), t1 = prmt(w0, w1, 0x7362u);
+    const uint32_t t2 = prmt(w2, w3, 0x5140u), t3 = prmt(w2, w3, 0x7362u);
+    o[0] = prmt(t0, t2, 0x5410u);
+    o[1] = prmt(t0, t2, 0x7632u);
+    o[2] = prmt(t1, t3, 0x5410u);
+    o[3] = prmt(t1, t3, 0x7632u);
 }
 
 __device__ __forceinline__ void cluster_sync() {
@@ -354,7 +360,7 @@ template <int DT, int NT, int RT>
 __global__ void __launch_bounds__(256, 2) gemv_kernel(GemvArgs p) {
     constexpr int KQ = 8 / RT;
     constexpr int CB = chunk_bytes(DT);
-    constexpr int FIXED_BITS = 27;  // |x * scale| < 2^27: four int8 digits
+    constexpr int FIXED_BITS = 30;  // |x * scale| < 2^30: four balanced int8 digits
     extern __shared__ __align__(128) uint8_t smem[];
     const int m = p.m, S = p.stages, cps = p.cps;
     const SmemLayout L = smem_layout(DT, NT, S, cps);
@@ -391,9 +397,7 @@ __global__ void __launch_bounds__(256, 2) gemv_kernel(GemvArgs p) {
         for (int s = 0; s < S; s++) mbar_init(mb0 + 8 * s, 1);
         if (warp == 0) mbar_init(xbar, 1);
         fence_mbar_init();
-        for (int i = 0; i < min(S, nw); i++)
-            bulk_load(ring0 + i * CB, gsrc + (size_t)(kq + i * KQ) * CB, CB, mb0 + 8 * i);
-        if (warp == 0 && p.x_vec4) {
+        if (warp == 0 && p.x_vec4) {  // the activations first: every warp waits on them
             asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(xbar),
                          "r"((uint32_t)(m * xn * 4))
                          : "memory");
@@ -404,6 +408,8 @@ __global__ void __launch_bounds__(256, 2) gemv_kernel(GemvArgs p) {
                     "l"(p.x + t * p.ldx + k_lo), "r"((uint32_t)(xn * 4)), "r"(xbar)
                     : "memory");
         }
+        for (int i = 0; i < min(S, nw); i++)
+            bulk_load(ring0 + i * CB, gsrc + (size_t)(kq + i * KQ) * CB, CB, mb0 + 8 * i);
     }
     reinterpret_cast<uint32_t *>(smem + L.zero)[tid] = 0u;  // 256 x 4 B
     if (!p.x_vec4) {  // unaligned activations: plain loads
@@ -470,21 +476,23 @@ __global__ void __launch_bounds__(256, 2) gemv_kernel(GemvArgs p) {
             for (int e = 0; e < 8; e++) v[e] = 0.f;
         }
         const float sc = scl[t];
-        int dg[8][4];
-        int slo = 0, shi = 0;
+        uint32_t y[8];
+        uint32_t slo = 0, shi = 0;
 #pragma unroll
         for (int e = 0; e < 8; e++) {
-            digits4(__float2int_rn(v[e] * sc), dg[e]);
-            slo += dg[e][1] * 128 + dg[e][0];
-            shi += dg[e][3] * 128 + dg[e][2];
+            y[e] = biased(__float2int_rn(v[e] * sc));
+            slo += y[e] & 0xFFFFu;  // d1*256 + d0 + 0x8080
+            shi += y[e] >> 16;      // d3*256 + d2 + 0x8080
+            y[e] ^= 0x80808080u;    // the digit bytes
         }
+        uint32_t a[4], b[4];
+        transpose4(y[0], y[1], y[2], y[3], a);
+        transpose4(y[4], y[5], y[6], y[7], b);
         uint4 *dst = reinterpret_cast<uint4 *>(tbl + (size_t)(t * cps + c) * 128 + s * 16 + gg * 4);
         // part 0 (col 2g): tile A digit 0, tile B digit 2; part 1 (col 2g+1): digits 1, 3
-        dst[0] = make_uint4(pack4(dg[0][0], dg[1][0], dg[2][0], dg[3][0]), pack4(dg[4][0], dg[5][0], dg[6][0], dg[7][0]),
-                            pack4(dg[0][2], dg[1][2], dg[2][2], dg[3][2]), pack4(dg[4][2], dg[5][2], dg[6][2], dg[7][2]));
-        dst[1] = make_uint4(pack4(dg[0][1], dg[1][1], dg[2][1], dg[3][1]), pack4(dg[4][1], dg[5][1], dg[6][1], dg[7][1]),
-                            pack4(dg[0][3], dg[1][3], dg[2][3], dg[3][3]), pack4(dg[4][3], dg[5][3], dg[6][3], dg[7][3]));
-        ssum[((t * cps + c) * 4 + gg) * 8 + s] = make_int2(slo, shi);
+        dst[0] = make_uint4(a[0], b[0], a[2], b[2]);
+        dst[1] = make_uint4(a[1], b[1], a[3], b[3]);
+        ssum[((t * cps + c) * 4 + gg) * 8 + s] = make_int2((int)slo - 8 * 0x8080, (int)shi - 8 * 0x8080);
     }
     if (DT != GGUF_Q8_0) {
         __syncthreads();
@@ -496,7 +504,7 @@ __global__ void __launch_bounds__(256, 2) gemv_kernel(GemvArgs p) {
             const int hi = src[0].y + src[1].y + src[2].y + src[3].y;
             sint[((t * cps + c) * 8 + u) * 2] = lo;
             sint[((t * cps + c) * 8 + u) * 2 + 1] = hi;
-            sflt[(t * cps + c) * 8 + u] = fmaf((float)hi, 16384.f, (float)lo);
+            sflt[(t * cps + c) * 8 + u] = fmaf((float)hi, 65536.f, (float)lo);
         }
     }
     __syncthreads();
