@@ -29,6 +29,11 @@
 //    integer activations (the "asum hoist"): one op per sub-block.
 //  * The activation table (the B fragments) is built per window of chunks
 //    with vectorised loads while the first weight copies are in flight.
+//  * Launched with programmatic stream serialization: a kernel's CTAs start
+//    while the previous kernel on the stream drains, issue their weight
+//    copies (which depend on nothing), and only then wait for the previous
+//    grid (griddepcontrol.wait) before touching the activations or writing
+//    outputs.  Each CTA signals its dependents once its main loop is done.
 //  * The grid puts 1-8 tiles in a CTA so that all CTAs are resident in one
 //    wave; K is split across CTAs only when the rows alone cannot occupy the
 //    SMs.  Split partial sums go to scratch and the last CTA to arrive for a
@@ -397,7 +402,13 @@ __global__ void __launch_bounds__(256, 2) gemv_kernel(GemvArgs p) {
         for (int s = 0; s < S; s++) mbar_init(mb0 + 8 * s, 1);
         if (warp == 0) mbar_init(xbar, 1);
         fence_mbar_init();
-        if (warp == 0 && p.x_vec4) {  // the activations first: every warp waits on them
+        for (int i = 0; i < min(S, nw); i++)
+            bulk_load(ring0 + i * CB, gsrc + (size_t)(kq + i * KQ) * CB, CB, mb0 + 8 * i);
+    }
+    // The activations may be the previous kernel's output: wait for it.
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    if (lane == 0) {
+        if (warp == 0 && p.x_vec4) {
             asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(xbar),
                          "r"((uint32_t)(m * xn * 4))
                          : "memory");
@@ -408,8 +419,6 @@ __global__ void __launch_bounds__(256, 2) gemv_kernel(GemvArgs p) {
                     "l"(p.x + t * p.ldx + k_lo), "r"((uint32_t)(xn * 4)), "r"(xbar)
                     : "memory");
         }
-        for (int i = 0; i < min(S, nw); i++)
-            bulk_load(ring0 + i * CB, gsrc + (size_t)(kq + i * KQ) * CB, CB, mb0 + 8 * i);
     }
     reinterpret_cast<uint32_t *>(smem + L.zero)[tid] = 0u;  // 256 x 4 B
     if (!p.x_vec4) {  // unaligned activations: plain loads
@@ -562,6 +571,7 @@ __global__ void __launch_bounds__(256, 2) gemv_kernel(GemvArgs p) {
     // Sum the four column groups of each row (lanes 4r .. 4r+3), then the KQ
     // warps of each tile in a fixed order, and undo the activation scale.
     __syncthreads();
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 #pragma unroll
     for (int t = 0; t < NT; t++) {
         float v0 = acc[t][0], v1 = acc[t][1];
@@ -677,15 +687,20 @@ cudaError_t launch_one(const GemvArgs &a, dim3 grid, size_t smem, cudaStream_t s
     cfg.blockDim = dim3(256, 1, 1);
     cfg.dynamicSmemBytes = smem;
     cfg.stream = s;
-    cudaLaunchAttribute attr[1];
+    cudaLaunchAttribute attr[2];
+    unsigned n = 0;
+    attr[n].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[n].val.programmaticStreamSerializationAllowed = 1;
+    n++;
     if (a.red_mode == kRedCluster) {
-        attr[0].id = cudaLaunchAttributeClusterDimension;
-        attr[0].val.clusterDim.x = 1;
-        attr[0].val.clusterDim.y = grid.y;
-        attr[0].val.clusterDim.z = 1;
-        cfg.attrs = attr;
-        cfg.numAttrs = 1;
+        attr[n].id = cudaLaunchAttributeClusterDimension;
+        attr[n].val.clusterDim.x = 1;
+        attr[n].val.clusterDim.y = grid.y;
+        attr[n].val.clusterDim.z = 1;
+        n++;
     }
+    cfg.attrs = attr;
+    cfg.numAttrs = n;
     return cudaLaunchKernelEx(&cfg, kern, a);
 }
 
