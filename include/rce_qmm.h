@@ -77,6 +77,16 @@ int rce_qmm_ctx_create(int device, rce_qmm_ctx **out);
 int rce_qmm_ctx_destroy(rce_qmm_ctx *ctx);
 /* Number of SMs of the context's device. */
 int rce_qmm_ctx_sm_count(const rce_qmm_ctx *ctx, int *out);
+/* mm_batched (host and device) runs the tensor-core prefill GEMM for batches
+ * of at least `n` tokens (default 16): weights dequantised to fp16 and
+ * activations rounded to fp16 with a per-token power-of-two scale, f32
+ * accumulation, within the 1e-3 normwise bar but not bit-identical to mm_1d.
+ * Smaller batches take the decode path, whose results per token are
+ * bit-identical to mm_1d whatever the batch, as the reference's mm_batched
+ * guarantees (rce-op-qmm/src/lib.rs:2575-2616).  n = 0 keeps every batch on
+ * the decode path. */
+int rce_qmm_ctx_set_prefill_min_tokens(rce_qmm_ctx *ctx, int n);
+int rce_qmm_ctx_get_prefill_min_tokens(const rce_qmm_ctx *ctx, int *n);
 
 /* Register a GGUF weight [n_rows = N_out][n_cols = K_in] (row-major blocks,
  * the layout QuantWeight keeps, rce-op-qmm/src/lib.rs:15-19).  The bytes are

@@ -39,6 +39,8 @@ SIGNATURES = {
     "rce_qmm_ctx_create": (_int, [_int, _vpp]),
     "rce_qmm_ctx_destroy": (_int, [_vp]),
     "rce_qmm_ctx_sm_count": (_int, [_vp, _c.POINTER(_int)]),
+    "rce_qmm_ctx_set_prefill_min_tokens": (_int, [_vp, _int]),
+    "rce_qmm_ctx_get_prefill_min_tokens": (_int, [_vp, _c.POINTER(_int)]),
     "rce_qmm_weight_register": (_int, [_vp, _vp, _sz, _int, _i64, _i64, _vpp]),
     "rce_qmm_weight_register_device": (_int, [_vp, _vp, _sz, _int, _i64, _i64, _vp, _vpp]),
     "rce_qmm_weight_sub_view": (_int, [_vp, _sz, _sz, _i64, _i64, _vpp]),

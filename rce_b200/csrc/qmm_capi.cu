@@ -138,10 +138,33 @@ int check_weight(const rce_qmm_weight *w) {
     return ok();
 }
 
+// Prefill GEMM workspace for stream s (grown like the split-K scratch).
+int stream_gemm_ws(rce_qmm_ctx *ctx, cudaStream_t s, size_t bytes, void **out) {
+    std::lock_guard<std::mutex> lk(ctx->mu);
+    RceScratch &sc = ctx->scratch[s];
+    if (sc.gemm_ws_bytes < bytes) {
+        CUDA_TRY(cudaStreamSynchronize(s));
+        if (sc.gemm_ws) cudaFree(sc.gemm_ws);
+        sc.gemm_ws = nullptr;
+        sc.gemm_ws_bytes = 0;
+        CUDA_TRY(cudaMalloc(&sc.gemm_ws, bytes));
+        sc.gemm_ws_bytes = bytes;
+    }
+    *out = sc.gemm_ws;
+    return ok();
+}
+
 // y[t_rows][ldo] = x[t_rows][lda] . W^T on stream s (device pointers).
 int run_matmul(rce_qmm_ctx *ctx, const rce_qmm_weight *w, const float *d_x, size_t lda, size_t t_rows,
                float *d_y, size_t ldo, cudaStream_t s) {
     const Geometry &g = w->g;
+    if (ctx->prefill_min_tokens > 0 && t_rows >= (size_t)ctx->prefill_min_tokens && t_rows <= (size_t)INT32_MAX) {
+        void *ws = nullptr;
+        int rc = stream_gemm_ws(ctx, s, rce::gemm_workspace_bytes(g, (int)t_rows), &ws);
+        if (rc) return rc;
+        CUDA_TRY(rce::launch_gemm(w->dtype, w->dev, g, d_x, lda, d_y, ldo, (int)t_rows, ws, ctx->err_dev, s));
+        return ok();
+    }
     size_t t0 = 0;
     while (t0 < t_rows) {
         const size_t left = t_rows - t0;
@@ -274,9 +297,22 @@ int rce_qmm_ctx_destroy(rce_qmm_ctx *ctx) {
     for (auto &kv : ctx->scratch) {
         if (kv.second.partial) cudaFree(kv.second.partial);
         if (kv.second.counters) cudaFree(kv.second.counters);
+        if (kv.second.gemm_ws) cudaFree(kv.second.gemm_ws);
     }
     if (ctx->err_host) cudaFreeHost(ctx->err_host);
     delete ctx;
+    return ok();
+}
+
+int rce_qmm_ctx_set_prefill_min_tokens(rce_qmm_ctx *ctx, int n) {
+    if (!ctx || n < 0) return fail(RCE_QMM_ERR_INVALID, "ctx_set_prefill_min_tokens: null ctx or negative count");
+    ctx->prefill_min_tokens = n;
+    return ok();
+}
+
+int rce_qmm_ctx_get_prefill_min_tokens(const rce_qmm_ctx *ctx, int *n) {
+    if (!ctx || !n) return fail(RCE_QMM_ERR_INVALID, "ctx_get_prefill_min_tokens: null argument");
+    *n = ctx->prefill_min_tokens;
     return ok();
 }
 

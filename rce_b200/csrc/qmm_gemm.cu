@@ -1,0 +1,562 @@
+// qmm_gemm.cu -- prefill matmul on the 5th-generation tensor cores (tcgen05).
+//
+// Y[t][row] = sum_k X[t][k] * W[row][k] for t_rows tokens, W a registered
+// GGUF weight in the T16 layout (qmm_layout.cuh).  Same operator as the
+// reference's mm_batched (rce-op-qmm/src/lib.rs:967-1023), which for these
+// formats is t_rows independent mm_1d calls.
+//
+// Numerics: the weights are dequantised exactly in f32 (d*sc*q - dmin*m, as
+// dequantize_to_f32 computes them) and rounded once to fp16; activations are
+// scaled per token by a power of two (exact) so that |x * s| < 2^14 and
+// rounded to fp16; products accumulate in f32 in tensor memory.  fp16 (11
+// significant bits) instead of bf16 (8) keeps the output within the 1e-3
+// normwise bar for Q4_K, at the same tensor-core rate.
+//
+// Structure (one CTA = 128 weight rows x BN tokens, all of K):
+//   prep kernel: X (f32) -> Xh (fp16, [t_rows][K]) and 1/s per token;
+//   warp 0     : producer -- TMA bulk copies of the packed T16 chunks (8
+//                tiles x 256 columns per slot) and TMA tensor loads of the
+//                128B-swizzled Xh tile of each 64-column k-block;
+//   warps 1-4  : dequantise one weight row each into the A tile (fp16,
+//                K-major, 128-byte swizzle), then run the epilogue
+//                (tcgen05.ld from tensor memory, scale, store);
+//   warp 5     : one thread issues tcgen05.mma (kind::f16, M=128, N=BN,
+//                K=16 per instruction) into f32 accumulators in tensor
+//                memory and frees each stage with tcgen05.commit.
+// Every mbarrier wait is bounded (%globaltimer, 1 s); on expiry the CTA
+// records the kernel error word and unwinds without further waits that
+// could block, releasing its tensor memory.
+#include <cuda.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+#include <atomic>
+#include <mutex>
+
+#include "qmm_internal.h"
+
+namespace rce {
+namespace {
+
+constexpr unsigned long long kWaitNs = 1000000000ull;
+constexpr int kBK = 64;                // k-block (one 128-byte swizzle row of fp16)
+constexpr int kBM = 128;               // weight rows per CTA (UMMA M)
+constexpr int kStages = 3;             // A/B k-block stages
+constexpr int kPSlots = 2;             // packed-chunk slots
+constexpr int kThreads = 192;          // 6 warps
+
+__device__ __forceinline__ uint32_t smem_u32(const void *p) {
+    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+__device__ __forceinline__ unsigned long long gtimer() {
+    unsigned long long t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+__device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count));
+}
+__device__ __forceinline__ void mbar_arrive(uint32_t bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
+}
+__device__ __forceinline__ void mbar_expect_tx(uint32_t bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ bool mbar_try(uint32_t bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\tselp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(bar), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+// Bounded wait; false if the phase did not complete within kWaitNs.
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity) {
+    if (mbar_try(bar, parity)) return true;
+    const unsigned long long t0 = gtimer();
+    while (!mbar_try(bar, parity))
+        if (gtimer() - t0 > kWaitNs) return false;
+    return true;
+}
+__device__ __forceinline__ void bulk_g2s(uint32_t dst, const void *src, uint32_t bytes, uint32_t bar) {
+    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst),
+                 "l"(src), "r"(bytes), "r"(bar)
+                 : "memory");
+}
+__device__ __forceinline__ void tma_2d(uint32_t dst, const CUtensorMap *map, int x, int y, uint32_t bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::
+            "r"(dst),
+        "l"(map), "r"(x), "r"(y), "r"(bar)
+        : "memory");
+}
+
+// UMMA shared-memory descriptor: K-major, 128-byte swizzle, 8-row groups
+// 1024 bytes apart (SBO), version 1.
+__device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr) {
+    uint64_t d = 0;
+    d |= (uint64_t)((saddr >> 4) & 0x3FFF);
+    d |= (uint64_t)1 << 16;                 // LBO (unused for swizzled K-major)
+    d |= (uint64_t)(1024 >> 4) << 32;       // SBO
+    d |= (uint64_t)1 << 46;                 // descriptor version
+    d |= (uint64_t)2 << 61;                 // SWIZZLE_128B
+    return d;
+}
+
+// Instruction descriptor: D f32, A/B fp16, both K-major, M = 128, N = n.
+__device__ __forceinline__ uint32_t idesc_f16(int n) {
+    return (1u << 4) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(kBM >> 4) << 24);
+}
+
+__device__ __forceinline__ void umma_f16(uint32_t tmem_d, uint64_t da, uint64_t db, uint32_t idesc, uint32_t acc) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
+        "l"(da), "l"(db), "r"(idesc), "r"(acc)
+        : "memory");
+}
+__device__ __forceinline__ void umma_commit(uint32_t bar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar)
+                 : "memory");
+}
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+__device__ __forceinline__ float h2f(uint32_t bits16) {
+    return __half2float(__ushort_as_half((unsigned short)(bits16 & 0xFFFF)));
+}
+
+__device__ __forceinline__ uint32_t pack_h2(float lo, float hi) {
+    const __half2 h = __floats2half2_rn(lo, hi);
+    return *reinterpret_cast<const uint32_t *>(&h);
+}
+
+struct GemmArgs {
+    const uint8_t *w;
+    float *y;
+    const float *inv_scale;  // per token
+    int *err;
+    Geometry g;
+    size_t ldy;
+    int t_rows;
+    int bn;
+};
+
+// Dequantise this thread's weight row for k-block j (0..3) of the chunk in
+// `slot` (8 tiles x CB bytes): 64 fp16 values into row `row` of A (K-major,
+// 128-byte swizzle).  Values are computed exactly in f32 as the reference's
+// dequantize_to_f32 does, then rounded once to fp16.
+template <int DT>
+__device__ __forceinline__ void dequant_row(const uint8_t *slot, int row, int j, uint8_t *a_tile) {
+    constexpr int CB = chunk_bytes(DT);
+    const int tile = row >> 4, r16 = row & 15, r = r16 & 7, rh = r16 >> 3;
+    const int lane = 4 * r + j;
+    const uint8_t *ch = slot + tile * CB;
+    float v[64];
+    if (DT == GGUF_Q4_K) {
+        const uint4 hd = *reinterpret_cast<const uint4 *>(ch + 2048 + r16 * 16);
+        const float d = h2f(hd.x), dmin = h2f(hd.x >> 16);
+        const uint32_t lo = j < 2 ? hd.y : (j == 2 ? hd.z : hd.w);
+        const uint32_t hi = j < 2 ? hd.z : (j == 2 ? hd.w : 0u);
+        const uint32_t sh = j == 0 ? 0u : (j == 1 ? 24u : (j == 2 ? 16u : 8u));
+        const uint32_t f = __funnelshift_r(lo, hi, sh) & 0xFFFFFFu;
+        const float d1 = d * (float)(f & 63u), m1 = dmin * (float)((f >> 6) & 63u);
+        const float d2 = d * (float)((f >> 12) & 63u), m2 = dmin * (float)((f >> 18) & 63u);
+#pragma unroll
+        for (int h = 0; h < 2; h++) {
+            const uint4 q = *reinterpret_cast<const uint4 *>(ch + ((2 * rh + h) * 32 + lane) * 16);
+            const uint32_t w[4] = {q.x, q.y, q.z, q.w};
+#pragma unroll
+            for (int b = 0; b < 16; b++) {
+                const uint32_t byte = (w[b >> 2] >> (8 * (b & 3))) & 0xFFu;
+                v[16 * h + b] = __fsub_rn(__fmul_rn(d1, (float)(byte & 15u)), m1);
+                v[32 + 16 * h + b] = __fsub_rn(__fmul_rn(d2, (float)(byte >> 4)), m2);
+            }
+        }
+    } else {
+        const uint2 sc = *reinterpret_cast<const uint2 *>(ch + quant_bytes(DT) + lane * 8);
+        const float dd[2] = {h2f(rh ? sc.y : sc.x), h2f((rh ? sc.y : sc.x) >> 16)};
+        if (DT == GGUF_Q4_0) {
+#pragma unroll
+            for (int h = 0; h < 2; h++) {
+                const uint4 q = *reinterpret_cast<const uint4 *>(ch + ((2 * rh + h) * 32 + lane) * 16);
+                const uint32_t w[4] = {q.x, q.y, q.z, q.w};
+#pragma unroll
+                for (int b = 0; b < 16; b++) {
+                    const uint32_t byte = (w[b >> 2] >> (8 * (b & 3))) & 0xFFu;
+                    v[32 * h + b] = __fmul_rn((float)((int)(byte & 15u) - 8), dd[h]);
+                    v[32 * h + 16 + b] = __fmul_rn((float)((int)(byte >> 4) - 8), dd[h]);
+                }
+            }
+        } else {
+#pragma unroll
+            for (int p = 0; p < 4; p++) {
+                const uint4 q = *reinterpret_cast<const uint4 *>(ch + ((4 * rh + p) * 32 + lane) * 16);
+                const uint32_t w[4] = {q.x, q.y, q.z, q.w};
+#pragma unroll
+                for (int b = 0; b < 16; b++) {
+                    const int8_t s = (int8_t)((w[b >> 2] >> (8 * (b & 3))) & 0xFFu);
+                    v[16 * p + b] = __fmul_rn((float)s, dd[p >> 1]);
+                }
+            }
+        }
+    }
+    // row `row` of the 128 x 64 fp16 tile: 8-row atoms of 1024 bytes, 16-byte
+    // chunk c of row r at ((c ^ (r & 7)) * 16)
+    uint8_t *dst = a_tile + (row >> 3) * 1024 + (row & 7) * 128;
+#pragma unroll
+    for (int c = 0; c < 8; c++) {
+        uint4 o;
+        o.x = pack_h2(v[8 * c + 0], v[8 * c + 1]);
+        o.y = pack_h2(v[8 * c + 2], v[8 * c + 3]);
+        o.z = pack_h2(v[8 * c + 4], v[8 * c + 5]);
+        o.w = pack_h2(v[8 * c + 6], v[8 * c + 7]);
+        *reinterpret_cast<uint4 *>(dst + ((c ^ (row & 7)) * 16)) = o;
+    }
+}
+
+struct GemmSmem {
+    size_t packed, a, b, bars, tmem_slot, total;
+};
+
+__host__ __device__ inline GemmSmem gemm_smem(int dt, int bn) {
+    GemmSmem L;
+    size_t o = 0;
+    L.a = o;  // 1024-aligned stages
+    o += (size_t)kStages * kBM * kBK * 2;
+    L.b = o;
+    o += (size_t)kStages * bn * kBK * 2;
+    L.packed = o;
+    o += (size_t)kPSlots * 8 * chunk_bytes(dt);
+    o = (o + 15) / 16 * 16;
+    L.bars = o;
+    o += 32 * 8;
+    L.tmem_slot = o;
+    o += 16;
+    L.total = o + 1024;  // slack to align the base to 1024
+    return L;
+}
+
+template <int DT>
+__global__ void __launch_bounds__(kThreads, 1)
+    gemm_kernel(const __grid_constant__ CUtensorMap xmap, GemmArgs p) {
+    constexpr int CB = chunk_bytes(DT);
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    const int bn = p.bn;
+    const GemmSmem L = gemm_smem(DT, bn);
+    uint8_t *a_st = smem + L.a;
+    uint8_t *b_st = smem + L.b;
+    uint8_t *pk = smem + L.packed;
+    uint64_t *bars = reinterpret_cast<uint64_t *>(smem + L.bars);
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(smem + L.tmem_slot);
+    // barriers: [0,2) packed full, [2,4) packed empty, [4,7) A full, [7,10) B
+    // full, [10,13) stage free (MMA done with A and B), 13 accumulator full
+    const uint32_t bar0 = smem_u32(bars);
+    auto PF = [&](int s) { return bar0 + 8 * (0 + s); };
+    auto PE = [&](int s) { return bar0 + 8 * (2 + s); };
+    auto AF = [&](int s) { return bar0 + 8 * (4 + s); };
+    auto BF = [&](int s) { return bar0 + 8 * (7 + s); };
+    auto SF = [&](int s) { return bar0 + 8 * (10 + s); };
+    const uint32_t ACC = bar0 + 8 * 13;
+
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int tile0 = blockIdx.x * 8;  // first 16-row tile of this CTA
+    const int ntiles = min(8, p.g.n_tiles - tile0);
+    const int tok0 = blockIdx.y * bn;
+    const int nchunks = p.g.n_chunks;
+    const int nkb = nchunks * 4;
+
+    if (tid == 0) {
+        for (int s = 0; s < kPSlots; s++) {
+            mbar_init(PF(s), 1);
+            mbar_init(PE(s), 128);
+        }
+        for (int s = 0; s < kStages; s++) {
+            mbar_init(AF(s), 128);
+            mbar_init(BF(s), 1);
+            mbar_init(SF(s), 1);
+        }
+        mbar_init(ACC, 1);
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    if (warp == 5) {  // tensor memory for the bn f32 accumulator columns
+        const uint32_t ncols = bn <= 32 ? 32 : (bn <= 64 ? 64 : (bn <= 128 ? 128 : 256));
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                     "r"(ncols)
+                     : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+    // The activations (Xh) come from the prep kernel just before this one.
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    bool ok = true;
+
+    if (warp == 0) {
+        if (lane == 0) {
+            // producer: packed chunk c -> slot c % 2; k-block kb -> stage kb % 3
+            int c_next = 0, kb_issued = 0;
+            for (int kb = 0; kb < nkb && ok; kb++) {
+                const int c = kb >> 2;
+                while (c_next <= c + 1 && c_next < nchunks && ok) {  // keep one chunk ahead
+                    const int s = c_next % kPSlots, use = c_next / kPSlots;
+                    if (use > 0 && !mbar_wait(PE(s), (use - 1) & 1)) {
+                        ok = false;
+                        break;
+                    }
+                    mbar_expect_tx(PF(s), (uint32_t)(ntiles * CB));
+                    for (int t = 0; t < ntiles; t++)
+                        bulk_g2s(smem_u32(pk + (size_t)(s * 8 + t) * CB),
+                                 p.w + ((size_t)(tile0 + t) * nchunks + c_next) * CB, CB, PF(s));
+                    c_next++;
+                }
+                if (!ok) break;
+                const int st = kb % kStages, use = kb / kStages;
+                if (use > 0 && !mbar_wait(SF(st), (use - 1) & 1)) {
+                    ok = false;
+                    break;
+                }
+                mbar_expect_tx(BF(st), (uint32_t)(bn * kBK * 2));
+                tma_2d(smem_u32(b_st + (size_t)st * bn * kBK * 2), &xmap, kb * kBK, tok0, BF(st));
+                kb_issued = kb + 1;
+            }
+            if (!ok) {  // let every copy this thread issued land before the CTA exits
+                for (int kb = max(0, kb_issued - kStages); kb < kb_issued; kb++)
+                    mbar_wait(BF(kb % kStages), (kb / kStages) & 1);
+                for (int c = max(0, c_next - kPSlots); c < c_next; c++) mbar_wait(PF(c % kPSlots), (c / kPSlots) & 1);
+            }
+        }
+    } else if (warp <= 4) {
+        // dequantisers: thread row = 0..127
+        const int row = tid - 32;
+        for (int kb = 0; kb < nkb && ok; kb++) {
+            const int c = kb >> 2, j = kb & 3, s = c % kPSlots;
+            if (j == 0 && !mbar_wait(PF(s), (c / kPSlots) & 1)) {
+                ok = false;
+                break;
+            }
+            const int st = kb % kStages, use = kb / kStages;
+            if (use > 0 && !mbar_wait(SF(st), (use - 1) & 1)) {
+                ok = false;
+                break;
+            }
+            uint8_t *a_tile = a_st + (size_t)st * kBM * kBK * 2;
+            if (row < ntiles * 16) {
+                dequant_row<DT>(pk + (size_t)s * 8 * CB, row, j, a_tile);
+            } else {  // rows past the weight: zeros
+                uint8_t *dst = a_tile + (row >> 3) * 1024 + (row & 7) * 128;
+#pragma unroll
+                for (int q = 0; q < 8; q++) *reinterpret_cast<uint4 *>(dst + 16 * q) = make_uint4(0, 0, 0, 0);
+            }
+            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // generic writes -> tensor-core reads
+            mbar_arrive(AF(st));
+            if (j == 3) mbar_arrive(PE(s));  // this chunk is no longer read
+        }
+    } else {
+        // MMA issuer
+        const uint32_t idesc = idesc_f16(bn);
+        for (int kb = 0; kb < nkb && ok; kb++) {
+            const int st = kb % kStages, use = kb / kStages;
+            if (!mbar_wait(AF(st), use & 1) || !mbar_wait(BF(st), use & 1)) {
+                ok = false;
+                break;
+            }
+            tc_fence_after();
+            if (lane == 0) {
+                const uint32_t a0 = smem_u32(a_st + (size_t)st * kBM * kBK * 2);
+                const uint32_t b0 = smem_u32(b_st + (size_t)st * bn * kBK * 2);
+#pragma unroll
+                for (int k = 0; k < kBK / 16; k++)  // 16 fp16 = 32 bytes per instruction
+                    umma_f16(tmem, sw128_desc(a0 + 32 * k), sw128_desc(b0 + 32 * k), idesc, (kb | k) ? 1u : 0u);
+                umma_commit(SF(st));
+            }
+            __syncwarp();
+        }
+        if (lane == 0) umma_commit(ACC);  // fires once every MMA above has completed
+        __syncwarp();
+    }
+
+    // epilogue: warps 1-4 own tensor-memory lanes 32 * (warp % 4) .. + 31
+    if (warp >= 1 && warp <= 4) {
+        if (ok && !mbar_wait(ACC, 0)) ok = false;
+        tc_fence_after();
+        const int lane_base = 32 * (warp & 3);
+        const int row = tile0 * 16 + lane_base + lane;
+        if (ok) {
+            for (int c0 = 0; c0 < bn; c0 += 32) {
+                uint32_t r[32];
+                asm volatile(
+                    "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+                    "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+                    : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+                      "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]),
+                      "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]),
+                      "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]),
+                      "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+                    : "r"(tmem + ((uint32_t)lane_base << 16) + (uint32_t)c0));
+                asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+                if (row < p.g.n_rows) {
+#pragma unroll
+                    for (int i = 0; i < 32; i++) {
+                        const int t = tok0 + c0 + i;
+                        if (t < p.t_rows) p.y[(size_t)t * p.ldy + row] = __uint_as_float(r[i]) * p.inv_scale[t];
+                    }
+                }
+            }
+        }
+    }
+    if (!ok && lane == 0) *reinterpret_cast<volatile int *>(p.err) = kKernelErrWaitTimeout;
+    tc_fence_before();
+    __syncthreads();
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+    if (warp == 5) {
+        const uint32_t ncols = bn <= 32 ? 32 : (bn <= 64 ? 64 : (bn <= 128 ? 128 : 256));
+        mbar_wait(ACC, 0);  // no MMA may still write the accumulator (returns at once when done)
+        tc_fence_after();
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(ncols) : "memory");
+    }
+}
+
+// X f32 [t][ldx] -> Xh fp16 [t][k] with x * 2^e, |x * 2^e| < 2^14, and 1/2^e.
+__global__ void __launch_bounds__(256) prep_kernel(const float *x, size_t ldx, int k, __half *xh, float *inv) {
+    const int t = blockIdx.x;
+    const float *xr = x + (size_t)t * ldx;
+    float mx = 0.f;
+    bool fin = true;
+    for (int i = threadIdx.x; i < k; i += 256) {
+        const float v = xr[i];
+        mx = fmaxf(mx, fabsf(v));
+        fin = fin && isfinite(v);
+    }
+    if (!fin) mx = INFINITY;
+    __shared__ float red[8];
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = mx;
+    __syncthreads();
+    float v = 0.f;
+    for (int w = 0; w < 8; w++) v = fmaxf(v, red[w]);
+    float s = 1.f, is = 1.f;
+    if (!isfinite(v)) {
+        s = 0.f;
+        is = __int_as_float(0x7fc00000);
+    } else if (v > 0.f) {
+        int e;
+        frexpf(v, &e);
+        e = max(-100, min(100, e));
+        s = ldexpf(1.f, 14 - e);
+        is = ldexpf(1.f, e - 14);
+    }
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+    __half *o = xh + (size_t)t * k;
+    for (int i = threadIdx.x; i < k; i += 256) o[i] = __float2half_rn(xr[i] * s);
+    if (threadIdx.x == 0) inv[t] = is;
+}
+
+using EncodeTiled = CUresult (*)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *, const cuuint64_t *,
+                                 const cuuint64_t *, const cuuint32_t *, const cuuint32_t *, CUtensorMapInterleave,
+                                 CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiled encode_fn() {
+    static std::once_flag once;
+    static EncodeTiled fn = nullptr;
+    std::call_once(once, [] {
+        void *p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<EncodeTiled>(p);
+    });
+    return fn;
+}
+
+template <int DT>
+cudaError_t launch_dt(const CUtensorMap &map, const GemmArgs &a, dim3 grid, size_t smem, cudaStream_t s) {
+    static std::atomic<unsigned long long> done{0};
+    auto kern = gemm_kernel<DT>;
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    const unsigned long long bit = dev < 64 ? (1ull << dev) : 0ull;
+    if (!bit || !(done.load() & bit)) {
+        int optin = 0;
+        e = cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
+        if (e != cudaSuccess) return e;
+        cudaFuncAttributes fa;
+        e = cudaFuncGetAttributes(&fa, kern);
+        if (e != cudaSuccess) return e;
+        e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, optin - (int)fa.sharedSizeBytes);
+        if (e != cudaSuccess) return e;
+        if (bit) done.fetch_or(bit);
+    }
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = dim3(kThreads, 1, 1);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kern, map, a);
+}
+
+}  // namespace
+
+int gemm_bn(int t_rows) {
+    if (t_rows >= 256) return 256;
+    int bn = (t_rows + 15) / 16 * 16;
+    return bn < 16 ? 16 : bn;
+}
+
+size_t gemm_workspace_bytes(const Geometry &g, int t_rows) {
+    const size_t xh = (size_t)t_rows * g.n_cols * 2;
+    return (xh + 255) / 256 * 256 + (size_t)t_rows * 4;
+}
+
+cudaError_t launch_gemm(int dt, const uint8_t *tiles, const Geometry &g, const float *x, size_t ldx, float *y,
+                        size_t ldy, int t_rows, void *workspace, int *err, cudaStream_t s) {
+    if (t_rows <= 0 || g.n_rows <= 0) return cudaSuccess;
+    EncodeTiled enc = encode_fn();
+    if (!enc) return cudaErrorNotSupported;
+    __half *xh = static_cast<__half *>(workspace);
+    const size_t xh_bytes = ((size_t)t_rows * g.n_cols * 2 + 255) / 256 * 256;
+    float *inv = reinterpret_cast<float *>(static_cast<uint8_t *>(workspace) + xh_bytes);
+    prep_kernel<<<t_rows, 256, 0, s>>>(x, ldx, (int)g.n_cols, xh, inv);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return e;
+    const int bn = gemm_bn(t_rows);
+    CUtensorMap map;
+    const cuuint64_t dims[2] = {(cuuint64_t)g.n_cols, (cuuint64_t)t_rows};
+    const cuuint64_t strides[1] = {(cuuint64_t)g.n_cols * 2};
+    const cuuint32_t box[2] = {(cuuint32_t)kBK, (cuuint32_t)bn};
+    const cuuint32_t estr[2] = {1, 1};
+    CUresult r = enc(&map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, xh, dims, strides, box, estr,
+                     CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                     CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return cudaErrorInvalidValue;
+    GemmArgs a;
+    a.w = tiles;
+    a.y = y;
+    a.inv_scale = inv;
+    a.err = err;
+    a.g = g;
+    a.ldy = ldy;
+    a.t_rows = t_rows;
+    a.bn = bn;
+    const size_t smem = gemm_smem(dt, bn).total;
+    dim3 grid((g.n_tiles + 7) / 8, (t_rows + bn - 1) / bn);
+    switch (dt) {
+    case GGUF_Q4_K: return launch_dt<GGUF_Q4_K>(map, a, grid, smem, s);
+    case GGUF_Q4_0: return launch_dt<GGUF_Q4_0>(map, a, grid, smem, s);
+    case GGUF_Q8_0: return launch_dt<GGUF_Q8_0>(map, a, grid, smem, s);
+    default: return cudaErrorInvalidValue;
+    }
+}
+
+}  // namespace rce

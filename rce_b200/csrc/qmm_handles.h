@@ -14,6 +14,8 @@ struct RceScratch {
     size_t floats = 0;
     unsigned *counters = nullptr;
     size_t ncounters = 0;
+    void *gemm_ws = nullptr;  // prefill GEMM workspace (fp16 activations, token scales)
+    size_t gemm_ws_bytes = 0;
 };
 
 struct RceThreadState {
@@ -33,6 +35,9 @@ struct rce_qmm_ctx {
     // pinned host memory, so the host reads it without a copy.
     int *err_host = nullptr;
     int *err_dev = nullptr;
+    // mm_batched runs the tensor-core prefill GEMM from this many tokens on
+    // (0: never; every token then takes the exact decode path).
+    int prefill_min_tokens = 16;
     std::mutex mu;
     std::unordered_map<cudaStream_t, RceScratch> scratch;
     std::unordered_map<std::thread::id, RceThreadState> threads;

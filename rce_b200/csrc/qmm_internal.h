@@ -45,6 +45,13 @@ cudaError_t launch_gemv(int dt, const uint8_t *tiles, const Geometry &g, const f
                         float *y, size_t ldy, int m, const GemvPlan &plan, float *scratch,
                         unsigned *counters, int *err, cudaStream_t s);
 
+// Prefill matmul on tcgen05 (fp16 operands, f32 accumulation in tensor
+// memory) for t_rows tokens at once.  `workspace` holds
+// gemm_workspace_bytes() bytes (the fp16 activations and per-token scales).
+size_t gemm_workspace_bytes(const Geometry &g, int t_rows);
+cudaError_t launch_gemm(int dt, const uint8_t *tiles, const Geometry &g, const float *x, size_t ldx, float *y,
+                        size_t ldy, int t_rows, void *workspace, int *err, cudaStream_t s);
+
 // Kernel error codes written to the context's error word.
 constexpr int kKernelErrWaitTimeout = 1;
 

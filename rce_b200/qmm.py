@@ -54,6 +54,18 @@ class Context:
     def synchronize(self) -> None:
         check(lib().rce_qmm_synchronize(self._h))
 
+    @property
+    def prefill_min_tokens(self) -> int:
+        """Batches of at least this many tokens run the tensor-core prefill
+        GEMM (fp16 operands); smaller ones the exact decode path; 0 = never."""
+        n = ctypes.c_int()
+        check(lib().rce_qmm_ctx_get_prefill_min_tokens(self._h, ctypes.byref(n)))
+        return n.value
+
+    @prefill_min_tokens.setter
+    def prefill_min_tokens(self, n: int) -> None:
+        check(lib().rce_qmm_ctx_set_prefill_min_tokens(self._h, int(n)))
+
     def device_error(self, clear: bool = True) -> int:
         """The kernel error word (0 = none): non-zero when a bounded wait
         inside a kernel expired; read it after synchronising the stream."""

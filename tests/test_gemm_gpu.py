@@ -1,0 +1,87 @@
+"""The tensor-core prefill GEMM (tcgen05, fp16 operands, f32 accumulation in
+tensor memory) that mm_batched uses for batches of at least
+ctx.prefill_min_tokens tokens.
+
+Bar: max normwise relative error per output row <= 1e-3 (the path's contract
+for final float outputs), against the oracle (the reference's f32 CPU path)
+and against a torch fp32 matmul of the bit-exact dequantised weights.
+"""
+import numpy as np
+import pytest
+
+import oracle as O
+import refcases
+import rce_b200 as R
+
+pytestmark = pytest.mark.gpu
+
+Q4_0, Q8_0, Q4_K = O.GGUF_Q4_0, O.GGUF_Q8_0, O.GGUF_Q4_K
+
+
+def norm_err(got, want):
+    got = np.asarray(got, np.float64)
+    want = np.asarray(want, np.float64)
+    return float((np.abs(got - want).max(axis=1) / np.maximum(np.abs(want).max(axis=1), 1e-30)).max())
+
+
+def test_prefill_threshold_option(ctx):
+    saved = ctx.prefill_min_tokens
+    assert saved == 16
+    ctx.prefill_min_tokens = 0
+    assert ctx.prefill_min_tokens == 0
+    ctx.prefill_min_tokens = saved
+    with pytest.raises(R.QmmError):
+        ctx.prefill_min_tokens = -1
+
+
+@pytest.mark.parametrize("dt", [Q4_K, Q4_0, Q8_0])
+@pytest.mark.parametrize("n,k,m", [(128, 256, 16), (200, 1024, 17), (1000, 4096, 40), (300, 2048, 256),
+                                   (513, 1024, 300), (256, 4096, 512)])
+def test_gemm_against_oracle(ctx, dt, n, k, m):
+    if dt != Q4_K and k % 256:
+        pytest.skip("shape")
+    w, _, _, _, x = refcases.seeded_case(dt, n, k, m, 1000 + n + m)
+    qw = R.QuantWeight.from_owned_bytes(w, dt, n, k, ctx=ctx)
+    assert m >= ctx.prefill_min_tokens
+    got = R.mm_batched(x, m, qw).reshape(m, n)
+    assert ctx.device_error() == 0
+    want = O.mm_batched(x, m, w, dt, n, k, nthreads=8)
+    e = norm_err(got, want)
+    print(f"dtype {dt} {n}x{k} m={m}: normwise rel err {e:.3e}")
+    assert e <= 1e-3
+
+
+def test_gemm_against_torch_fp32(ctx):
+    import torch
+
+    n, k, m = 640, 4096, 192
+    w, _, _, _, x = refcases.seeded_case(Q4_K, n, k, m, 77)
+    qw = R.QuantWeight.from_owned_bytes(w, Q4_K, n, k, ctx=ctx)
+    wd = R.dequant_device(qw)                       # bit-exact f32 weights
+    xd = torch.from_numpy(x).cuda()
+    ref = (xd.double() @ wd.double().T).float()     # fp32-exact reference of the same op
+    got = R.mm_batched_device(xd, qw)
+    torch.cuda.synchronize()
+    e = norm_err(got.cpu().numpy(), ref.cpu().numpy())
+    print(f"tcgen05 GEMM vs torch fp64-accumulated reference: {e:.3e}")
+    assert e <= 1e-3
+
+
+def test_gemm_full_width_rows_subset(ctx):
+    # the prefill configuration's weight (14336 x 4096 Q4_K, seed 2) at 128
+    # tokens, checked on a subset of rows against the oracle
+    import torch
+    from rce_b200 import synth
+
+    rng = np.random.default_rng(2)
+    n, k, m = 14336, 4096, 128
+    w = synth.weights(Q4_K, n, k, rng)
+    x = synth.activations(m, k, rng)
+    qw = R.QuantWeight.from_owned_bytes(w, Q4_K, n, k, ctx=ctx)
+    got = R.mm_batched_device(torch.from_numpy(x).cuda(), qw).cpu().numpy()
+    rows = np.r_[0:64, 7000:7064, n - 64:n]
+    want = np.stack([np.concatenate([O.mm_1d_rows(x[t], w, Q4_K, n, k, a, a + 64, nthreads=8)
+                                     for a in (0, 7000, n - 64)]) for t in range(m)])
+    e = norm_err(got[:, rows], want)
+    print(f"14336x4096 Q4_K m=128 (rows subset): normwise rel err {e:.3e}")
+    assert e <= 1e-3

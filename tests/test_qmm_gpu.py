@@ -29,16 +29,24 @@ def norm_rel_err(got, want):
     return float((err / scale).max())
 
 
-def assert_close(got, want, tol=NORM_TOL):
+def assert_close(got, want, tol=NORM_TOL, elementwise=True):
+    """Normwise bar always; the per-element idiom for the exact decode path
+    (the fp16 prefill GEMM is held to the normwise bar only)."""
     got = np.asarray(got, np.float32)
     want = np.asarray(want, np.float32)
     assert np.all(np.isfinite(got))
     e = norm_rel_err(got, want)
     assert e <= tol, f"normwise relative error {e:.3e} > {tol}"
-    d = np.abs(got.astype(np.float64) - want.astype(np.float64))
-    ok = (d < 1e-4) | (d <= 1e-3 * np.abs(want.astype(np.float64)))
-    assert ok.all(), f"{(~ok).sum()} elements outside abs<1e-4||rel<1e-3; worst {d.max():.3e}"
+    if elementwise:
+        d = np.abs(got.astype(np.float64) - want.astype(np.float64))
+        ok = (d < 1e-4) | (d <= 1e-3 * np.abs(want.astype(np.float64)))
+        assert ok.all(), f"{(~ok).sum()} elements outside abs<1e-4||rel<1e-3; worst {d.max():.3e}"
     return e
+
+
+def exact_path(ctx, m):
+    """True when a batch of m tokens takes the exact decode path."""
+    return ctx.prefill_min_tokens == 0 or m < ctx.prefill_min_tokens
 
 
 def register(ctx, w, dt, n, k):
@@ -81,7 +89,7 @@ def test_seeded_configs_against_golden(ctx, golden, case):
     w, _, _, _, x = refcases.seeded_case(dt, n, k, m, seed)
     qw = register(ctx, w, dt, n, k)
     got = R.mm_batched(x, m, qw).reshape(m, n)
-    e = assert_close(got, golden[f"{name}__y"])
+    e = assert_close(got, golden[f"{name}__y"], elementwise=exact_path(ctx, m))
     print(f"{name}: normwise rel err {e:.3e}")
 
 
@@ -91,11 +99,16 @@ def test_batched_is_bit_identical_to_per_row(ctx, dt):
     n, k, t = 200, 1024, 21
     w, _, _, _, x = refcases.seeded_case(dt, n, k, t, 31)
     qw = register(ctx, w, dt, n, k)
-    got = R.mm_batched(x, t, qw).reshape(t, n)
-    for r in range(t):
-        assert np.array_equal(got[r].view(np.uint32), R.mm_1d(x[r], qw).view(np.uint32)), r
-    again = R.mm_batched(x, t, qw).reshape(t, n)
-    assert np.array_equal(got.view(np.uint32), again.view(np.uint32))
+    saved = ctx.prefill_min_tokens
+    ctx.prefill_min_tokens = 0  # every batch on the exact decode path
+    try:
+        got = R.mm_batched(x, t, qw).reshape(t, n)
+        for r in range(t):
+            assert np.array_equal(got[r].view(np.uint32), R.mm_1d(x[r], qw).view(np.uint32)), r
+        again = R.mm_batched(x, t, qw).reshape(t, n)
+        assert np.array_equal(got.view(np.uint32), again.view(np.uint32))
+    finally:
+        ctx.prefill_min_tokens = saved
 
 
 @pytest.mark.parametrize("dt", [Q8_0, Q4_0, Q4_K])
@@ -125,7 +138,7 @@ def test_token_counts(ctx, dt, m):
     w, _, _, _, x = refcases.seeded_case(dt, n, k, m, 7 * m)
     qw = register(ctx, w, dt, n, k)
     got = R.mm_batched(x, m, qw).reshape(m, n)
-    assert_close(got, O.mm_batched(x, m, w, dt, n, k))
+    assert_close(got, O.mm_batched(x, m, w, dt, n, k), elementwise=exact_path(ctx, m))
 
 
 @pytest.mark.parametrize("dt", [Q8_0, Q4_0, Q4_K])
@@ -203,6 +216,7 @@ def test_device_path_and_strided_rows(ctx):
     n, k, m = 300, 4096, 6
     w, _, _, _, x = refcases.seeded_case(Q4_K, n, k, m, 77)
     qw = register(ctx, w, Q4_K, n, k)
+    assert exact_path(ctx, m)
     xb = torch.zeros((m, k + 64), dtype=torch.float32, device="cuda:0")
     xb[:, :k] = torch.from_numpy(x).cuda()
     out = torch.full((m, n + 3), float("nan"), device="cuda:0")
