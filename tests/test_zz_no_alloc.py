@@ -49,7 +49,12 @@ def test_noalloc_matches_regular_entry_point(dt, n, k, m):
     w = R.QuantWeight.from_owned_bytes(wb, dt, n, k, ctx=ctx)
     xd = torch.from_numpy(x).cuda()
     stream = torch.cuda.current_stream()
-    want = R.mm_batched_device(xd, w).cpu().numpy()
+    saved = ctx.prefill_min_tokens
+    ctx.prefill_min_tokens = 0  # the regular entry point's decode path, which this one mirrors
+    try:
+        want = R.mm_batched_device(xd, w).cpu().numpy()
+    finally:
+        ctx.prefill_min_tokens = saved
     for call in range(2):
         out = torch.full((m, n), float("nan"), device="cuda:0")
         rc = _noalloc(L, ctx, xd, w, out, stream)
