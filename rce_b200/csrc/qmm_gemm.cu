@@ -143,6 +143,35 @@ struct GemmArgs {
     int bn;
 };
 
+// Packed f32x2 arithmetic (two lanes of f32 per instruction).
+__device__ __forceinline__ unsigned long long f2pack(float lo, float hi) {
+    return (unsigned long long)__float_as_uint(lo) | ((unsigned long long)__float_as_uint(hi) << 32);
+}
+__device__ __forceinline__ unsigned long long f2add(unsigned long long a, unsigned long long b) {
+    unsigned long long r;
+    asm("add.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+    return r;
+}
+__device__ __forceinline__ unsigned long long f2fma(unsigned long long a, unsigned long long b, unsigned long long c) {
+    unsigned long long r;
+    asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(a), "l"(b), "l"(c));
+    return r;
+}
+// fp16x2 of the two f32 lanes (round to nearest even).
+__device__ __forceinline__ uint32_t f2_to_h2(unsigned long long v) {
+    return pack_h2(__uint_as_float((uint32_t)v), __uint_as_float((uint32_t)(v >> 32)));
+}
+
+// Two codes -> their values as f32 pair: exact integer c via the exponent
+// bias (0x4B000000 | c is 2^23 + c), minus `bias`, then value = c' * scale -
+// offset in one fused rounding (the product is exact, as in the reference's
+// d1 * q - min1, which rounds once at the subtraction).
+__device__ __forceinline__ uint32_t dq_pair(uint32_t c0, uint32_t c1, unsigned long long bias, unsigned long long sc,
+                                            unsigned long long off) {
+    const unsigned long long f = f2pack(__uint_as_float(0x4B000000u | c0), __uint_as_float(0x4B000000u | c1));
+    return f2_to_h2(f2fma(f2add(f, bias), sc, off));
+}
+
 // Dequantise this thread's weight row for k-block j (0..3) of the chunk in
 // `slot` (8 tiles x CB bytes): 64 fp16 values into row `row` of A (K-major,
 // 128-byte swizzle).  Values are computed exactly in f32 as the reference's
@@ -153,7 +182,7 @@ __device__ __forceinline__ void dequant_row(const uint8_t *slot, int row, int j,
     const int tile = row >> 4, r16 = row & 15, r = r16 & 7, rh = r16 >> 3;
     const int lane = 4 * r + j;
     const uint8_t *ch = slot + tile * CB;
-    float v[64];
+    uint32_t h[32];  // 64 fp16 values, in order
     if (DT == GGUF_Q4_K) {
         const uint4 hd = *reinterpret_cast<const uint4 *>(ch + 2048 + r16 * 16);
         const float d = h2f(hd.x), dmin = h2f(hd.x >> 16);
@@ -163,41 +192,50 @@ __device__ __forceinline__ void dequant_row(const uint8_t *slot, int row, int j,
         const uint32_t f = __funnelshift_r(lo, hi, sh) & 0xFFFFFFu;
         const float d1 = d * (float)(f & 63u), m1 = dmin * (float)((f >> 6) & 63u);
         const float d2 = d * (float)((f >> 12) & 63u), m2 = dmin * (float)((f >> 18) & 63u);
+        const unsigned long long bias = f2pack(-8388608.f, -8388608.f);
+        const unsigned long long s1 = f2pack(d1, d1), o1 = f2pack(-m1, -m1);
+        const unsigned long long s2 = f2pack(d2, d2), o2 = f2pack(-m2, -m2);
 #pragma unroll
-        for (int h = 0; h < 2; h++) {
-            const uint4 q = *reinterpret_cast<const uint4 *>(ch + ((2 * rh + h) * 32 + lane) * 16);
+        for (int hh = 0; hh < 2; hh++) {
+            const uint4 q = *reinterpret_cast<const uint4 *>(ch + ((2 * rh + hh) * 32 + lane) * 16);
             const uint32_t w[4] = {q.x, q.y, q.z, q.w};
 #pragma unroll
-            for (int b = 0; b < 16; b++) {
-                const uint32_t byte = (w[b >> 2] >> (8 * (b & 3))) & 0xFFu;
-                v[16 * h + b] = __fsub_rn(__fmul_rn(d1, (float)(byte & 15u)), m1);
-                v[32 + 16 * h + b] = __fsub_rn(__fmul_rn(d2, (float)(byte >> 4)), m2);
+            for (int b = 0; b < 16; b += 2) {
+                const uint32_t x = w[b >> 2] >> (8 * (b & 3));  // bytes b, b+1 in the low half
+                h[(16 * hh + b) >> 1] = dq_pair(x & 15u, (x >> 8) & 15u, bias, s1, o1);
+                h[(32 + 16 * hh + b) >> 1] = dq_pair((x >> 4) & 15u, (x >> 12) & 15u, bias, s2, o2);
             }
         }
     } else {
         const uint2 sc = *reinterpret_cast<const uint2 *>(ch + quant_bytes(DT) + lane * 8);
-        const float dd[2] = {h2f(rh ? sc.y : sc.x), h2f((rh ? sc.y : sc.x) >> 16)};
+        const uint32_t sw = rh ? sc.y : sc.x;
+        const float dd[2] = {h2f(sw), h2f(sw >> 16)};
+        const unsigned long long zero = f2pack(0.f, 0.f);
         if (DT == GGUF_Q4_0) {
+            const unsigned long long bias = f2pack(-8388616.f, -8388616.f);  // 2^23 + 8
 #pragma unroll
-            for (int h = 0; h < 2; h++) {
-                const uint4 q = *reinterpret_cast<const uint4 *>(ch + ((2 * rh + h) * 32 + lane) * 16);
+            for (int hh = 0; hh < 2; hh++) {
+                const unsigned long long sd = f2pack(dd[hh], dd[hh]);
+                const uint4 q = *reinterpret_cast<const uint4 *>(ch + ((2 * rh + hh) * 32 + lane) * 16);
                 const uint32_t w[4] = {q.x, q.y, q.z, q.w};
 #pragma unroll
-                for (int b = 0; b < 16; b++) {
-                    const uint32_t byte = (w[b >> 2] >> (8 * (b & 3))) & 0xFFu;
-                    v[32 * h + b] = __fmul_rn((float)((int)(byte & 15u) - 8), dd[h]);
-                    v[32 * h + 16 + b] = __fmul_rn((float)((int)(byte >> 4) - 8), dd[h]);
+                for (int b = 0; b < 16; b += 2) {
+                    const uint32_t x = w[b >> 2] >> (8 * (b & 3));
+                    h[(32 * hh + b) >> 1] = dq_pair(x & 15u, (x >> 8) & 15u, bias, sd, zero);
+                    h[(32 * hh + 16 + b) >> 1] = dq_pair((x >> 4) & 15u, (x >> 12) & 15u, bias, sd, zero);
                 }
             }
         } else {
+            const unsigned long long bias = f2pack(-8388736.f, -8388736.f);  // 2^23 + 128
 #pragma unroll
             for (int p = 0; p < 4; p++) {
+                const unsigned long long sd = f2pack(dd[p >> 1], dd[p >> 1]);
                 const uint4 q = *reinterpret_cast<const uint4 *>(ch + ((4 * rh + p) * 32 + lane) * 16);
-                const uint32_t w[4] = {q.x, q.y, q.z, q.w};
+                const uint32_t w[4] = {q.x ^ 0x80808080u, q.y ^ 0x80808080u, q.z ^ 0x80808080u, q.w ^ 0x80808080u};
 #pragma unroll
-                for (int b = 0; b < 16; b++) {
-                    const int8_t s = (int8_t)((w[b >> 2] >> (8 * (b & 3))) & 0xFFu);
-                    v[16 * p + b] = __fmul_rn((float)s, dd[p >> 1]);
+                for (int b = 0; b < 16; b += 2) {
+                    const uint32_t x = w[b >> 2] >> (8 * (b & 3));  // byte ^ 0x80 = q + 128
+                    h[(16 * p + b) >> 1] = dq_pair(x & 255u, (x >> 8) & 255u, bias, sd, zero);
                 }
             }
         }
@@ -206,14 +244,9 @@ __device__ __forceinline__ void dequant_row(const uint8_t *slot, int row, int j,
     // chunk c of row r at ((c ^ (r & 7)) * 16)
     uint8_t *dst = a_tile + (row >> 3) * 1024 + (row & 7) * 128;
 #pragma unroll
-    for (int c = 0; c < 8; c++) {
-        uint4 o;
-        o.x = pack_h2(v[8 * c + 0], v[8 * c + 1]);
-        o.y = pack_h2(v[8 * c + 2], v[8 * c + 3]);
-        o.z = pack_h2(v[8 * c + 4], v[8 * c + 5]);
-        o.w = pack_h2(v[8 * c + 6], v[8 * c + 7]);
-        *reinterpret_cast<uint4 *>(dst + ((c ^ (row & 7)) * 16)) = o;
-    }
+    for (int c = 0; c < 8; c++)
+        *reinterpret_cast<uint4 *>(dst + ((c ^ (row & 7)) * 16)) =
+            make_uint4(h[4 * c], h[4 * c + 1], h[4 * c + 2], h[4 * c + 3]);
 }
 
 struct GemmSmem {
