@@ -12,17 +12,21 @@
 // significant bits) instead of bf16 (8) keeps the output within the 1e-3
 // normwise bar for Q4_K, at the same tensor-core rate.
 //
-// Structure (one CTA = 128 weight rows x BN tokens, all of K):
+// Structure (one CTA = 128 weight rows x BN tokens, all of K; BN up to 512,
+// i.e. two N = 256 accumulators filling tensor memory, so that a weight
+// tile is dequantised once per 512 tokens):
 //   prep kernel: X (f32) -> Xh (fp16, [t_rows][K]) and 1/s per token;
-//   warp 0     : producer -- TMA bulk copies of the packed T16 chunks (8
-//                tiles x 256 columns per slot) and TMA tensor loads of the
-//                128B-swizzled Xh tile of each 64-column k-block;
-//   warps 1-4  : dequantise one weight row each into the A tile (fp16,
-//                K-major, 128-byte swizzle), then run the epilogue
-//                (tcgen05.ld from tensor memory, scale, store);
-//   warp 5     : one thread issues tcgen05.mma (kind::f16, M=128, N=BN,
+//   warp 0     : TMA bulk copies of the packed T16 chunks (8 tiles x 256
+//                columns per slot, 2-4 slots as shared memory allows);
+//   warps 1-16 : dequantise a quarter weight row each (16 values) into the
+//                A tile (fp16, K-major, 128-byte swizzle), then run the
+//                epilogue (tcgen05.ld from tensor memory, scale, store);
+//                four warps per scheduler hide each other's latency;
+//   warp 17    : one thread issues tcgen05.mma (kind::f16, M=128, N<=256,
 //                K=16 per instruction) into f32 accumulators in tensor
-//                memory and frees each stage with tcgen05.commit.
+//                memory and frees each stage with tcgen05.commit;
+//   warp 18    : TMA tensor loads of the 128B-swizzled Xh tile of each
+//                64-column k-block (after the prep kernel, via PDL).
 // Every mbarrier wait is bounded (%globaltimer, 1 s); on expiry the CTA
 // records the kernel error word and unwinds without further waits that
 // could block, releasing its tensor memory.
@@ -41,9 +45,11 @@ namespace {
 constexpr unsigned long long kWaitNs = 1000000000ull;
 constexpr int kBK = 64;                // k-block (one 128-byte swizzle row of fp16)
 constexpr int kBM = 128;               // weight rows per CTA (UMMA M)
-constexpr int kStages = 3;             // A/B k-block stages
-constexpr int kPSlots = 2;             // packed-chunk slots
-constexpr int kThreads = 192;          // 6 warps
+constexpr int kDqWarps = 16;           // dequantiser warps (four threads per weight row)
+constexpr int kWeightWarp = 0;         // TMA bulk copies of the packed weight chunks
+constexpr int kMmaWarp = kDqWarps + 1;  // tcgen05.alloc / mma / dealloc
+constexpr int kActWarp = kDqWarps + 2;  // TMA tensor loads of the activation k-blocks
+constexpr int kThreads = 32 * (kDqWarps + 3);
 
 __device__ __forceinline__ uint32_t smem_u32(const void *p) {
     return static_cast<uint32_t>(__cvta_generic_to_shared(p));
@@ -172,17 +178,24 @@ __device__ __forceinline__ uint32_t dq_pair(uint32_t c0, uint32_t c1, unsigned l
     return f2_to_h2(f2fma(f2add(f, bias), sc, off));
 }
 
-// Dequantise this thread's weight row for k-block j (0..3) of the chunk in
-// `slot` (8 tiles x CB bytes): 64 fp16 values into row `row` of A (K-major,
-// 128-byte swizzle).  Values are computed exactly in f32 as the reference's
-// dequantize_to_f32 does, then rounded once to fp16.
+// Dequantise quarter `qr` of this thread's weight row for k-block j (0..3)
+// of the chunk in `slot` (8 tiles x CB bytes): 16 of the row's 64 fp16
+// values into row `row` of A (K-major, 128-byte swizzle).  Values are
+// computed exactly in f32 as the reference's dequantize_to_f32 does, then
+// rounded once to fp16.
+//   Q4_K: group j's qs bytes 8 qr .. 8 qr + 7, i.e. values 8 qr .. (low
+//         nibbles, A chunk qr) and 32 + 8 qr .. (high nibbles, chunk 4 + qr);
+//   Q4_0: block 2 j + qr / 2, bytes 8 (qr & 1) ..: low nibbles -> chunk
+//         4 (qr >> 1) + (qr & 1), high nibbles -> 2 more;
+//   Q8_0: block 2 j + qr / 2, values 16 (qr & 1) .. -> chunks 2 qr, 2 qr + 1.
 template <int DT>
-__device__ __forceinline__ void dequant_row(const uint8_t *slot, int row, int j, uint8_t *a_tile) {
+__device__ __forceinline__ void dequant_quarter(const uint8_t *slot, int row, int qr, int j, uint8_t *a_tile) {
     constexpr int CB = chunk_bytes(DT);
     const int tile = row >> 4, r16 = row & 15, r = r16 & 7, rh = r16 >> 3;
-    const int lane = 4 * r + j;
+    const int lane = 4 * r + j, hf = qr >> 1;
     const uint8_t *ch = slot + tile * CB;
-    uint32_t h[32];  // 64 fp16 values, in order
+    uint32_t h[8];  // 16 fp16 values
+    int c0, c1;     // the two 16-byte A chunks (8 values each) they fill
     if (DT == GGUF_Q4_K) {
         const uint4 hd = *reinterpret_cast<const uint4 *>(ch + 2048 + r16 * 16);
         const float d = h2f(hd.x), dmin = h2f(hd.x >> 16);
@@ -195,73 +208,78 @@ __device__ __forceinline__ void dequant_row(const uint8_t *slot, int row, int j,
         const unsigned long long bias = f2pack(-8388608.f, -8388608.f);
         const unsigned long long s1 = f2pack(d1, d1), o1 = f2pack(-m1, -m1);
         const unsigned long long s2 = f2pack(d2, d2), o2 = f2pack(-m2, -m2);
+        const uint2 q = *reinterpret_cast<const uint2 *>(ch + ((2 * rh + hf) * 32 + lane) * 16 + 8 * (qr & 1));
+        const uint32_t w[2] = {q.x, q.y};
 #pragma unroll
-        for (int hh = 0; hh < 2; hh++) {
-            const uint4 q = *reinterpret_cast<const uint4 *>(ch + ((2 * rh + hh) * 32 + lane) * 16);
-            const uint32_t w[4] = {q.x, q.y, q.z, q.w};
-#pragma unroll
-            for (int b = 0; b < 16; b += 2) {
-                const uint32_t x = w[b >> 2] >> (8 * (b & 3));  // bytes b, b+1 in the low half
-                h[(16 * hh + b) >> 1] = dq_pair(x & 15u, (x >> 8) & 15u, bias, s1, o1);
-                h[(32 + 16 * hh + b) >> 1] = dq_pair((x >> 4) & 15u, (x >> 12) & 15u, bias, s2, o2);
-            }
+        for (int b = 0; b < 8; b += 2) {
+            const uint32_t x = w[b >> 2] >> (8 * (b & 3));  // bytes b, b+1 in the low half
+            h[b >> 1] = dq_pair(x & 15u, (x >> 8) & 15u, bias, s1, o1);
+            h[4 + (b >> 1)] = dq_pair((x >> 4) & 15u, (x >> 12) & 15u, bias, s2, o2);
         }
+        c0 = qr;
+        c1 = 4 + qr;
     } else {
         const uint2 sc = *reinterpret_cast<const uint2 *>(ch + quant_bytes(DT) + lane * 8);
         const uint32_t sw = rh ? sc.y : sc.x;
-        const float dd[2] = {h2f(sw), h2f(sw >> 16)};
-        const unsigned long long zero = f2pack(0.f, 0.f);
+        const float dd = h2f(sw >> (16 * hf));
+        const unsigned long long zero = f2pack(0.f, 0.f), sd = f2pack(dd, dd);
         if (DT == GGUF_Q4_0) {
             const unsigned long long bias = f2pack(-8388616.f, -8388616.f);  // 2^23 + 8
+            const uint2 q =
+                *reinterpret_cast<const uint2 *>(ch + ((2 * rh + hf) * 32 + lane) * 16 + 8 * (qr & 1));
+            const uint32_t w[2] = {q.x, q.y};
 #pragma unroll
-            for (int hh = 0; hh < 2; hh++) {
-                const unsigned long long sd = f2pack(dd[hh], dd[hh]);
-                const uint4 q = *reinterpret_cast<const uint4 *>(ch + ((2 * rh + hh) * 32 + lane) * 16);
-                const uint32_t w[4] = {q.x, q.y, q.z, q.w};
-#pragma unroll
-                for (int b = 0; b < 16; b += 2) {
-                    const uint32_t x = w[b >> 2] >> (8 * (b & 3));
-                    h[(32 * hh + b) >> 1] = dq_pair(x & 15u, (x >> 8) & 15u, bias, sd, zero);
-                    h[(32 * hh + 16 + b) >> 1] = dq_pair((x >> 4) & 15u, (x >> 12) & 15u, bias, sd, zero);
-                }
+            for (int b = 0; b < 8; b += 2) {
+                const uint32_t x = w[b >> 2] >> (8 * (b & 3));
+                h[b >> 1] = dq_pair(x & 15u, (x >> 8) & 15u, bias, sd, zero);
+                h[4 + (b >> 1)] = dq_pair((x >> 4) & 15u, (x >> 12) & 15u, bias, sd, zero);
             }
+            c0 = 4 * hf + (qr & 1);
+            c1 = c0 + 2;
         } else {
             const unsigned long long bias = f2pack(-8388736.f, -8388736.f);  // 2^23 + 128
+            const uint4 q = *reinterpret_cast<const uint4 *>(ch + ((4 * rh + qr) * 32 + lane) * 16);
+            const uint32_t w[4] = {q.x ^ 0x80808080u, q.y ^ 0x80808080u, q.z ^ 0x80808080u, q.w ^ 0x80808080u};
 #pragma unroll
-            for (int p = 0; p < 4; p++) {
-                const unsigned long long sd = f2pack(dd[p >> 1], dd[p >> 1]);
-                const uint4 q = *reinterpret_cast<const uint4 *>(ch + ((4 * rh + p) * 32 + lane) * 16);
-                const uint32_t w[4] = {q.x ^ 0x80808080u, q.y ^ 0x80808080u, q.z ^ 0x80808080u, q.w ^ 0x80808080u};
-#pragma unroll
-                for (int b = 0; b < 16; b += 2) {
-                    const uint32_t x = w[b >> 2] >> (8 * (b & 3));  // byte ^ 0x80 = q + 128
-                    h[(16 * p + b) >> 1] = dq_pair(x & 255u, (x >> 8) & 255u, bias, sd, zero);
-                }
+            for (int b = 0; b < 16; b += 2) {
+                const uint32_t x = w[b >> 2] >> (8 * (b & 3));  // byte ^ 0x80 = q + 128
+                h[b >> 1] = dq_pair(x & 255u, (x >> 8) & 255u, bias, sd, zero);
             }
+            c0 = 2 * qr;
+            c1 = c0 + 1;
         }
     }
     // row `row` of the 128 x 64 fp16 tile: 8-row atoms of 1024 bytes, 16-byte
     // chunk c of row r at ((c ^ (r & 7)) * 16)
     uint8_t *dst = a_tile + (row >> 3) * 1024 + (row & 7) * 128;
-#pragma unroll
-    for (int c = 0; c < 8; c++)
-        *reinterpret_cast<uint4 *>(dst + ((c ^ (row & 7)) * 16)) =
-            make_uint4(h[4 * c], h[4 * c + 1], h[4 * c + 2], h[4 * c + 3]);
+    *reinterpret_cast<uint4 *>(dst + ((c0 ^ (row & 7)) * 16)) = make_uint4(h[0], h[1], h[2], h[3]);
+    *reinterpret_cast<uint4 *>(dst + ((c1 ^ (row & 7)) * 16)) = make_uint4(h[4], h[5], h[6], h[7]);
 }
 
+// Shared-memory plan of one CTA for token-tile width bn.
 struct GemmSmem {
-    size_t packed, a, b, bars, tmem_slot, total;
+    size_t a, b, packed, bars, tmem_slot, total;
+    int a_stages, b_stages, pslots;
 };
 
 __host__ __device__ inline GemmSmem gemm_smem(int dt, int bn) {
+    constexpr size_t kLimit = 227 * 1024;  // dynamic shared memory per CTA (opt-in)
     GemmSmem L;
+    L.a_stages = 3;
+    L.b_stages = bn > 256 ? 2 : 3;
+    const size_t a_bytes = (size_t)L.a_stages * kBM * kBK * 2;
+    const size_t b_bytes = (size_t)L.b_stages * bn * kBK * 2;
+    const size_t slot = (size_t)8 * chunk_bytes(dt);
+    const size_t fixed = a_bytes + b_bytes + 32 * 8 + 16 + 1024;
+    size_t ps = fixed < kLimit ? (kLimit - fixed) / slot : 0;
+    L.pslots = ps > 4 ? 4 : (int)ps;
     size_t o = 0;
     L.a = o;  // 1024-aligned stages
-    o += (size_t)kStages * kBM * kBK * 2;
+    o += a_bytes;
     L.b = o;
-    o += (size_t)kStages * bn * kBK * 2;
+    o += b_bytes;
     L.packed = o;
-    o += (size_t)kPSlots * 8 * chunk_bytes(dt);
+    o += (size_t)L.pslots * slot;
     o = (o + 15) / 16 * 16;
     L.bars = o;
     o += 32 * 8;
@@ -269,6 +287,10 @@ __host__ __device__ inline GemmSmem gemm_smem(int dt, int bn) {
     o += 16;
     L.total = o + 1024;  // slack to align the base to 1024
     return L;
+}
+
+__host__ __device__ inline uint32_t tmem_cols(int bn) {
+    return bn <= 32 ? 32u : (bn <= 64 ? 64u : (bn <= 128 ? 128u : (bn <= 256 ? 256u : 512u)));
 }
 
 template <int DT>
@@ -279,20 +301,22 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     const int bn = p.bn;
     const GemmSmem L = gemm_smem(DT, bn);
+    const int NA = L.a_stages, NB = L.b_stages, NP = L.pslots;
     uint8_t *a_st = smem + L.a;
     uint8_t *b_st = smem + L.b;
     uint8_t *pk = smem + L.packed;
     uint64_t *bars = reinterpret_cast<uint64_t *>(smem + L.bars);
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(smem + L.tmem_slot);
-    // barriers: [0,2) packed full, [2,4) packed empty, [4,7) A full, [7,10) B
-    // full, [10,13) stage free (MMA done with A and B), 13 accumulator full
+    // barriers: [0,4) packed full, [4,8) packed empty, [8,11) A full,
+    // [11,14) A free, [14,17) B full, [17,20) B free, 20 accumulator full
     const uint32_t bar0 = smem_u32(bars);
     auto PF = [&](int s) { return bar0 + 8 * (0 + s); };
-    auto PE = [&](int s) { return bar0 + 8 * (2 + s); };
-    auto AF = [&](int s) { return bar0 + 8 * (4 + s); };
-    auto BF = [&](int s) { return bar0 + 8 * (7 + s); };
-    auto SF = [&](int s) { return bar0 + 8 * (10 + s); };
-    const uint32_t ACC = bar0 + 8 * 13;
+    auto PE = [&](int s) { return bar0 + 8 * (4 + s); };
+    auto AF = [&](int s) { return bar0 + 8 * (8 + s); };
+    auto AE = [&](int s) { return bar0 + 8 * (11 + s); };
+    auto BF = [&](int s) { return bar0 + 8 * (14 + s); };
+    auto BE = [&](int s) { return bar0 + 8 * (17 + s); };
+    const uint32_t ACC = bar0 + 8 * 20;
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int tile0 = blockIdx.x * 8;  // first 16-row tile of this CTA
@@ -300,22 +324,25 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int tok0 = blockIdx.y * bn;
     const int nchunks = p.g.n_chunks;
     const int nkb = nchunks * 4;
+    const uint32_t ncols = tmem_cols(bn);
 
     if (tid == 0) {
-        for (int s = 0; s < kPSlots; s++) {
+        for (int s = 0; s < NP; s++) {
             mbar_init(PF(s), 1);
-            mbar_init(PE(s), 128);
+            mbar_init(PE(s), kDqWarps);
         }
-        for (int s = 0; s < kStages; s++) {
-            mbar_init(AF(s), 128);
+        for (int s = 0; s < NA; s++) {
+            mbar_init(AF(s), kDqWarps);
+            mbar_init(AE(s), 1);
+        }
+        for (int s = 0; s < NB; s++) {
             mbar_init(BF(s), 1);
-            mbar_init(SF(s), 1);
+            mbar_init(BE(s), 1);
         }
         mbar_init(ACC, 1);
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
-    if (warp == 5) {  // tensor memory for the bn f32 accumulator columns
-        const uint32_t ncols = bn <= 32 ? 32 : (bn <= 64 ? 64 : (bn <= 128 ? 128 : 256));
+    if (warp == kMmaWarp) {  // tensor memory for the bn f32 accumulator columns
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
                      "r"(ncols)
                      : "memory");
@@ -325,116 +352,154 @@ __global__ void __launch_bounds__(kThreads, 1)
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
-    // The activations (Xh) come from the prep kernel just before this one.
-    asm volatile("griddepcontrol.wait;" ::: "memory");
     bool ok = true;
 
-    if (warp == 0) {
+    if (warp == kWeightWarp) {
+        // packed T16 chunks (the weights do not depend on the previous kernel)
         if (lane == 0) {
-            // producer: packed chunk c -> slot c % 2; k-block kb -> stage kb % 3
-            int c_next = 0, kb_issued = 0;
-            for (int kb = 0; kb < nkb && ok; kb++) {
-                const int c = kb >> 2;
-                while (c_next <= c + 1 && c_next < nchunks && ok) {  // keep one chunk ahead
-                    const int s = c_next % kPSlots, use = c_next / kPSlots;
-                    if (use > 0 && !mbar_wait(PE(s), (use - 1) & 1)) {
-                        ok = false;
-                        break;
-                    }
-                    mbar_expect_tx(PF(s), (uint32_t)(ntiles * CB));
-                    for (int t = 0; t < ntiles; t++)
-                        bulk_g2s(smem_u32(pk + (size_t)(s * 8 + t) * CB),
-                                 p.w + ((size_t)(tile0 + t) * nchunks + c_next) * CB, CB, PF(s));
-                    c_next++;
+            // stage s and phase ph of chunk c, advanced without division
+            int c = 0, s = 0;
+            uint32_t ph = 0;
+            for (; c < nchunks; c++) {
+                if (c >= NP && !mbar_wait(PE(s), ph ^ 1)) {
+                    ok = false;
+                    break;
                 }
-                if (!ok) break;
-                const int st = kb % kStages, use = kb / kStages;
-                if (use > 0 && !mbar_wait(SF(st), (use - 1) & 1)) {
+                mbar_expect_tx(PF(s), (uint32_t)(ntiles * CB));
+                for (int t = 0; t < ntiles; t++)
+                    bulk_g2s(smem_u32(pk + (size_t)(s * 8 + t) * CB), p.w + ((size_t)(tile0 + t) * nchunks + c) * CB,
+                             CB, PF(s));
+                if (++s == NP) {
+                    s = 0;
+                    ph ^= 1;
+                }
+            }
+            if (!ok)  // let every copy this thread issued land before the CTA exits
+                for (int u = max(0, c - NP); u < c; u++) mbar_wait(PF(u % NP), (u / NP) & 1);
+        }
+    } else if (warp == kActWarp) {
+        // activation k-blocks: the prep kernel just before this one writes Xh
+        asm volatile("griddepcontrol.wait;" ::: "memory");
+        if (lane == 0) {
+            int kb = 0, st = 0;
+            uint32_t ph = 0;
+            for (; kb < nkb; kb++) {
+                if (kb >= NB && !mbar_wait(BE(st), ph ^ 1)) {
                     ok = false;
                     break;
                 }
                 mbar_expect_tx(BF(st), (uint32_t)(bn * kBK * 2));
-                tma_2d(smem_u32(b_st + (size_t)st * bn * kBK * 2), &xmap, kb * kBK, tok0, BF(st));
-                kb_issued = kb + 1;
+                uint8_t *dst = b_st + (size_t)st * bn * kBK * 2;
+                for (int r0 = 0; r0 < bn; r0 += 256)  // a tensor-map box is at most 256 rows
+                    tma_2d(smem_u32(dst + (size_t)r0 * kBK * 2), &xmap, kb * kBK, tok0 + r0, BF(st));
+                if (++st == NB) {
+                    st = 0;
+                    ph ^= 1;
+                }
             }
-            if (!ok) {  // let every copy this thread issued land before the CTA exits
-                for (int kb = max(0, kb_issued - kStages); kb < kb_issued; kb++)
-                    mbar_wait(BF(kb % kStages), (kb / kStages) & 1);
-                for (int c = max(0, c_next - kPSlots); c < c_next; c++) mbar_wait(PF(c % kPSlots), (c / kPSlots) & 1);
-            }
+            if (!ok)
+                for (int u = max(0, kb - NB); u < kb; u++) mbar_wait(BF(u % NB), (u / NB) & 1);
         }
-    } else if (warp <= 4) {
-        // dequantisers: thread row = 0..127
-        const int row = tid - 32;
+    } else if (warp >= 1 && warp <= kDqWarps) {
+        // dequantisers: four threads per weight row
+        const int row = (tid - 32) >> 2, qr = (tid - 32) & 3;
+        int s = 0, st = 0;  // packed slot and A stage, with their phases
+        uint32_t sph = 0, aph = 0;
         for (int kb = 0; kb < nkb && ok; kb++) {
-            const int c = kb >> 2, j = kb & 3, s = c % kPSlots;
-            if (j == 0 && !mbar_wait(PF(s), (c / kPSlots) & 1)) {
+            const int j = kb & 3;
+            if (j == 0 && !mbar_wait(PF(s), sph)) {
                 ok = false;
                 break;
             }
-            const int st = kb % kStages, use = kb / kStages;
-            if (use > 0 && !mbar_wait(SF(st), (use - 1) & 1)) {
+            if (kb >= NA && !mbar_wait(AE(st), aph ^ 1)) {
                 ok = false;
                 break;
             }
             uint8_t *a_tile = a_st + (size_t)st * kBM * kBK * 2;
             if (row < ntiles * 16) {
-                dequant_row<DT>(pk + (size_t)s * 8 * CB, row, j, a_tile);
+                dequant_quarter<DT>(pk + (size_t)s * 8 * CB, row, qr, j, a_tile);
             } else {  // rows past the weight: zeros
-                uint8_t *dst = a_tile + (row >> 3) * 1024 + (row & 7) * 128;
-#pragma unroll
-                for (int q = 0; q < 8; q++) *reinterpret_cast<uint4 *>(dst + 16 * q) = make_uint4(0, 0, 0, 0);
+                uint8_t *dst = a_tile + (row >> 3) * 1024 + (row & 7) * 128 + 32 * qr;
+                *reinterpret_cast<uint4 *>(dst) = make_uint4(0, 0, 0, 0);
+                *reinterpret_cast<uint4 *>(dst + 16) = make_uint4(0, 0, 0, 0);
             }
             asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // generic writes -> tensor-core reads
-            mbar_arrive(AF(st));
-            if (j == 3) mbar_arrive(PE(s));  // this chunk is no longer read
-        }
-    } else {
-        // MMA issuer
-        const uint32_t idesc = idesc_f16(bn);
-        for (int kb = 0; kb < nkb && ok; kb++) {
-            const int st = kb % kStages, use = kb / kStages;
-            if (!mbar_wait(AF(st), use & 1) || !mbar_wait(BF(st), use & 1)) {
-                ok = false;
-                break;
-            }
-            tc_fence_after();
-            if (lane == 0) {
-                const uint32_t a0 = smem_u32(a_st + (size_t)st * kBM * kBK * 2);
-                const uint32_t b0 = smem_u32(b_st + (size_t)st * bn * kBK * 2);
-#pragma unroll
-                for (int k = 0; k < kBK / 16; k++)  // 16 fp16 = 32 bytes per instruction
-                    umma_f16(tmem, sw128_desc(a0 + 32 * k), sw128_desc(b0 + 32 * k), idesc, (kb | k) ? 1u : 0u);
-                umma_commit(SF(st));
-            }
             __syncwarp();
+            if (lane == 0) {  // one arrival per warp
+                mbar_arrive(AF(st));
+                if (j == 3) mbar_arrive(PE(s));  // this chunk is no longer read
+            }
+            if (++st == NA) {
+                st = 0;
+                aph ^= 1;
+            }
+            if (j == 3 && ++s == NP) {
+                s = 0;
+                sph ^= 1;
+            }
         }
-        if (lane == 0) umma_commit(ACC);  // fires once every MMA above has completed
+    } else if (warp == kMmaWarp) {
+        // MMA issuer: per k-block, bn / 256 (at least one) accumulators of
+        // up to 256 columns, 4 instructions of K = 16 each
+        // lane 0 alone; descriptors advance by 32 bytes (2 in the >> 4 address
+        // field) per K = 16 step and by a whole stage per stage
+        const int nsub = bn > 256 ? bn / 256 : 1, nw = bn > 256 ? 256 : bn;
+        const uint32_t idesc = idesc_f16(nw);
+        if (lane == 0) {
+            const uint64_t da0 = sw128_desc(smem_u32(a_st)), db0 = sw128_desc(smem_u32(b_st));
+            const uint64_t a_step = (uint64_t)(kBM * kBK * 2) >> 4, b_step = (uint64_t)(bn * kBK * 2) >> 4;
+            const uint64_t h_step = (uint64_t)(256 * kBK * 2) >> 4;
+            int sa = 0, sb = 0;
+            uint32_t aph = 0, bph = 0;
+            for (int kb = 0; kb < nkb; kb++) {
+                if (!mbar_wait(AF(sa), aph) || !mbar_wait(BF(sb), bph)) {
+                    ok = false;
+                    break;
+                }
+                tc_fence_after();
+                const uint64_t da = da0 + (uint64_t)sa * a_step, db = db0 + (uint64_t)sb * b_step;
+                for (int h = 0; h < nsub; h++) {
+#pragma unroll
+                    for (int k = 0; k < kBK / 16; k++)  // 16 fp16 = 32 bytes per instruction
+                        umma_f16(tmem + (uint32_t)(h * 256), da + 2 * k, db + (uint64_t)h * h_step + 2 * k, idesc,
+                                 (kb | k) ? 1u : 0u);
+                }
+                umma_commit(AE(sa));
+                umma_commit(BE(sb));
+                if (++sa == NA) {
+                    sa = 0;
+                    aph ^= 1;
+                }
+                if (++sb == NB) {
+                    sb = 0;
+                    bph ^= 1;
+                }
+            }
+            umma_commit(ACC);  // fires once every MMA above has completed
+        }
         __syncwarp();
     }
 
-    // epilogue: warps 1-4 own tensor-memory lanes 32 * (warp % 4) .. + 31
-    if (warp >= 1 && warp <= 4) {
+    // epilogue: dequantiser warp w owns tensor-memory lanes 32 * (w % 4) ..
+    // + 31 (the only lanes a warp may read) and one of four column groups
+    if (warp >= 1 && warp <= kDqWarps) {
         if (ok && !mbar_wait(ACC, 0)) ok = false;
         tc_fence_after();
         const int lane_base = 32 * (warp & 3);
+        const int cpg = (bn / 8 + 3) / 4 * 8;  // columns per group, a multiple of 8
+        const int c_begin = ((warp - 1) >> 2) * cpg, c_end = min(bn, c_begin + cpg);
         const int row = tile0 * 16 + lane_base + lane;
         if (ok) {
-            for (int c0 = 0; c0 < bn; c0 += 32) {
-                uint32_t r[32];
-                asm volatile(
-                    "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
-                    "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
-                    : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
-                      "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]),
-                      "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]),
-                      "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]),
-                      "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
-                    : "r"(tmem + ((uint32_t)lane_base << 16) + (uint32_t)c0));
+            for (int c0 = c_begin; c0 < c_end; c0 += 8) {
+                uint32_t r[8];
+                asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
+                             : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+                               "=r"(r[7])
+                             : "r"(tmem + ((uint32_t)lane_base << 16) + (uint32_t)c0));
                 asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
                 if (row < p.g.n_rows) {
 #pragma unroll
-                    for (int i = 0; i < 32; i++) {
+                    for (int i = 0; i < 8; i++) {
                         const int t = tok0 + c0 + i;
                         if (t < p.t_rows) p.y[(size_t)t * p.ldy + row] = __uint_as_float(r[i]) * p.inv_scale[t];
                     }
@@ -446,8 +511,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     tc_fence_before();
     __syncthreads();
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
-    if (warp == 5) {
-        const uint32_t ncols = bn <= 32 ? 32 : (bn <= 64 ? 64 : (bn <= 128 ? 128 : 256));
+    if (warp == kMmaWarp) {
         mbar_wait(ACC, 0);  // no MMA may still write the accumulator (returns at once when done)
         tc_fence_after();
         asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(ncols) : "memory");
@@ -541,7 +605,11 @@ cudaError_t launch_dt(const CUtensorMap &map, const GemmArgs &a, dim3 grid, size
 
 }  // namespace
 
-int gemm_bn(int t_rows) {
+int gemm_bn(int dt, int t_rows) {
+    // 512 tokens: two N = 256 accumulators fill tensor memory, so each weight
+    // tile is dequantised once per 512 tokens (Q8_0's larger chunks leave
+    // no room for the 2 x 64 KB activation stages)
+    if (t_rows >= 512 && dt != GGUF_Q8_0) return 512;
     if (t_rows >= 256) return 256;
     int bn = (t_rows + 15) / 16 * 16;
     return bn < 16 ? 16 : bn;
@@ -563,11 +631,11 @@ cudaError_t launch_gemm(int dt, const uint8_t *tiles, const Geometry &g, const f
     prep_kernel<<<t_rows, 256, 0, s>>>(x, ldx, (int)g.n_cols, xh, inv);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return e;
-    const int bn = gemm_bn(t_rows);
+    const int bn = gemm_bn(dt, t_rows);
     CUtensorMap map;
     const cuuint64_t dims[2] = {(cuuint64_t)g.n_cols, (cuuint64_t)t_rows};
     const cuuint64_t strides[1] = {(cuuint64_t)g.n_cols * 2};
-    const cuuint32_t box[2] = {(cuuint32_t)kBK, (cuuint32_t)bn};
+    const cuuint32_t box[2] = {(cuuint32_t)kBK, (cuuint32_t)(bn < 256 ? bn : 256)};
     const cuuint32_t estr[2] = {1, 1};
     CUresult r = enc(&map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, xh, dims, strides, box, estr,
                      CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
@@ -582,7 +650,9 @@ cudaError_t launch_gemm(int dt, const uint8_t *tiles, const Geometry &g, const f
     a.ldy = ldy;
     a.t_rows = t_rows;
     a.bn = bn;
-    const size_t smem = gemm_smem(dt, bn).total;
+    const GemmSmem lay = gemm_smem(dt, bn);
+    if (lay.pslots < 2) return cudaErrorInvalidConfiguration;
+    const size_t smem = lay.total;
     dim3 grid((g.n_tiles + 7) / 8, (t_rows + bn - 1) / bn);
     switch (dt) {
     case GGUF_Q4_K: return launch_dt<GGUF_Q4_K>(map, a, grid, smem, s);
