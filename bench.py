@@ -18,6 +18,12 @@ roofline = the dominant kernel (the 14336x4096 / 4096x14336 Q4_K GEMVs) timed
          launch by launch with CUDA events, algorithmic bytes / duration
 cpu_baseline = the C restatement of the reference's CPU path (oracle/) on one
          layer of the same stack, all host threads
+prefill  = BASELINE configs[2]: Q4_K 14336x4096 weight (row-sharded N ways),
+         M = 1, 16, 128, 512 f32 activations through mm_batched_device (the
+         tcgen05 GEMM from ctx.prefill_min_tokens = 16 tokens on, the GEMV
+         below); four distinct weights per pass (132 MB > L2) replayed from a
+         CUDA graph, CUDA events; TFLOP/s = 2 M N K / time, against the
+         measured bf16 dense peak
 The weights (3.9 GB) are far larger than L2 (126 MB), so no L2 flush is
 needed between steps.
 
@@ -194,6 +200,75 @@ def config_dict(args, world):
             "l2": "no flush: weights 3.9 GB >> 126 MB L2" if args.layers >= 8 else "small stack (profiling)"}
 
 
+# ---- prefill GEMM ---------------------------------------------------------
+
+PREFILL_N, PREFILL_K, PREFILL_MS = D_FF, D_MODEL, (1, 16, 128, 512)
+
+
+def prefill_section(args, rank, world, dev, stream, ctx):
+    import torch
+    import torch.distributed as dist
+
+    import rce_b200 as R
+    from rce_b200 import synth
+
+    ns = PREFILL_N // world
+    ws = []
+    for i in range(4):
+        g = torch.Generator(device=dev)
+        g.manual_seed(2_000_000 + 97 * i + rank)
+        raw = synth.device_weights(Q4_K, ns, PREFILL_K, g, dev)
+        ws.append(R.QuantWeight.from_device_bytes(raw, Q4_K, ns, PREFILL_K, ctx=ctx))
+        del raw
+    out = {}
+    for m in PREFILL_MS:
+        g = torch.Generator(device=dev)
+        g.manual_seed(2)
+        x = torch.randn((m, PREFILL_K), device=dev, generator=g)
+        y = torch.empty((m, ns), device=dev)
+        yall = torch.empty((world * m, ns), device=dev) if world > 1 else None
+
+        def one():
+            for w in ws:
+                R.mm_batched_device(x, w, y, stream=stream)
+                if world > 1:
+                    dist.all_gather_into_tensor(yall, y)
+
+        with torch.cuda.stream(stream):
+            for _ in range(3):
+                one()
+        stream.synchronize()
+        graph = None
+        if world == 1:
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph, stream=stream):
+                one()
+        reps = 20
+        with torch.cuda.stream(stream):
+            for _ in range(3):
+                graph.replay() if graph is not None else one()
+            if world > 1:
+                dist.barrier()
+            torch.cuda.synchronize(dev)
+            e0 = torch.cuda.Event(enable_timing=True)
+            e1 = torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            for _ in range(reps):
+                graph.replay() if graph is not None else one()
+            e1.record(stream)
+        e1.synchronize()
+        ms = e0.elapsed_time(e1) / (reps * len(ws))
+        if world > 1:
+            t = torch.tensor([ms], device=dev)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            ms = float(t.item())
+        flops = 2.0 * m * PREFILL_N * PREFILL_K
+        out[f"m{m}"] = {"us": round(ms * 1e3, 2), "tflops": round(flops / (ms / 1e3) / 1e12, 1),
+                        "path": "tcgen05 GEMM" if m >= ctx.prefill_min_tokens else "GEMV"}
+        del graph
+    return out
+
+
 # ---- our arm -------------------------------------------------------------------------
 
 def build_stack(args, rank, world, dev):
@@ -230,6 +305,8 @@ def main():
     ap.add_argument("--e2e-steps", type=int, default=3)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--profile", action="store_true", help="short run for ncu: warm-up + steps only")
+    ap.add_argument("--profile-prefill", type=int, default=0, metavar="M",
+                    help="for ncu: only the configs[2] prefill matmul at M tokens, warm-up + steps launches")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
 
@@ -256,6 +333,21 @@ def main():
 
     dev = torch.device("cuda", local)
     torch.cuda.set_device(dev)
+    if args.profile_prefill:
+        from rce_b200 import synth
+
+        ctx = R.default_context(dev.index)
+        g = torch.Generator(device=dev)
+        g.manual_seed(2)
+        raw = synth.device_weights(Q4_K, PREFILL_N, PREFILL_K, g, dev)
+        w = R.QuantWeight.from_device_bytes(raw, Q4_K, PREFILL_N, PREFILL_K, ctx=ctx)
+        x = torch.randn((args.profile_prefill, PREFILL_K), device=dev, generator=g)
+        y = torch.empty((args.profile_prefill, PREFILL_N), device=dev)
+        for _ in range(args.warmup + args.steps):
+            R.mm_batched_device(x, w, y)
+        torch.cuda.synchronize(dev)
+        print(json.dumps({"profile_prefill": args.profile_prefill, "launches": args.warmup + args.steps}))
+        return
     if world > 1:
         dist.init_process_group("nccl", init_method="env://", timeout=datetime.timedelta(seconds=120),
                                 device_id=dev)
@@ -379,6 +471,8 @@ def main():
         except Exception:
             traffic = None
 
+    prefill = prefill_section(args, rank, world, dev, stream, ctx)
+
     # ---- e2e through the host C-ABI ----------------------------------------------
     e2e = None
     hx = {k: v.cpu().numpy() for k, v in xs.items()}
@@ -442,6 +536,14 @@ def main():
                          "avg_launch_us": round(kern[dom]["avg_us"], 2)},
             "kernels": {nm: {"avg_us": round(v["avg_us"], 2), "gbs": round(v["gbs"], 1)} for nm, v in kern.items()},
             "stack_frac_of_hbm": round(value / world / hbm, 4),
+            "prefill_gemm": {
+                "workload": f"configs[2]: Q4_K {PREFILL_N}x{PREFILL_K} weight, M f32 activations, fp16 operands, "
+                            "f32 accumulation in tensor memory",
+                "per_m": prefill,
+                "roofline": {"bound": "tensor", "m": 512, "achieved": prefill["m512"]["tflops"], "peak": bf16,
+                             "unit": "TFLOP/s", "frac": round(prefill["m512"]["tflops"] / bf16 / max(world, 1), 4),
+                             "peak_kind": f"{peak_kind} bf16 dense (burst)"},
+            },
             "e2e": e2e,
             "cpu_baseline": cpu,
             "clocks": clk,
