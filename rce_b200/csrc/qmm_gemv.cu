@@ -298,13 +298,13 @@ struct SmemLayout {
 
 __host__ __device__ inline size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
 
-constexpr int kXBar = 8 * kMaxStages;  // index of the activation-staging mbarrier
+constexpr int kNumBars = 8 * kMaxStages;  // one weight-ring mbarrier per warp and stage
 
 __host__ __device__ inline SmemLayout smem_layout(int dt, int nt, int stages, int cps) {
     SmemLayout L;
     size_t o = 0;
     L.mbar = o;
-    o += (kXBar + 1) * 8;
+    o += kNumBars * 8;
     o = align_up(o, 16);
     L.zero = o;
     o += 1024;
@@ -391,59 +391,57 @@ __global__ void __launch_bounds__(256, 2) gemv_kernel(GemvArgs p) {
     const uint8_t *gsrc = p.w + ((size_t)(tile_ok ? tile : 0) * p.g.n_chunks + c0) * CB;
     const uint32_t mb0 = smem_u32(mbar + warp * kMaxStages);
     const uint32_t ring0 = smem_u32(ring + (size_t)warp * S * CB);
-    const uint32_t xbar = smem_u32(mbar + kXBar);
     const int64_t k_lo = (int64_t)c0 * CHUNK_K;
     const int64_t k_hi = min((int64_t)(c0 + nc) * CHUNK_K, p.g.n_cols);
     const int xn = (int)(k_hi - k_lo);  // activations of this slice (a multiple of 32)
 
-    // Weight copies and the activation slice do not depend on each other:
-    // start them all before anything else.
+    // The weight copies depend on nothing: start them before anything else.
     if (lane == 0) {
         for (int s = 0; s < S; s++) mbar_init(mb0 + 8 * s, 1);
-        if (warp == 0) mbar_init(xbar, 1);
         fence_mbar_init();
         for (int i = 0; i < min(S, nw); i++)
             bulk_load(ring0 + i * CB, gsrc + (size_t)(kq + i * KQ) * CB, CB, mb0 + 8 * i);
     }
     // The activations may be the previous kernel's output: wait for it.
     asm volatile("griddepcontrol.wait;" ::: "memory");
-    if (lane == 0) {
-        if (warp == 0 && p.x_vec4) {
-            asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(xbar),
-                         "r"((uint32_t)(m * xn * 4))
-                         : "memory");
-            for (int t = 0; t < m; t++)
-                asm volatile(
-                    "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
-                        smem_u32(xs + t * cps * CHUNK_K)),
-                    "l"(p.x + t * p.ldx + k_lo), "r"((uint32_t)(xn * 4)), "r"(xbar)
-                    : "memory");
-        }
-    }
+    // The CTA's activation slice comes in through ordinary coalesced loads
+    // (the load/store path), not the TMA queue, which is busy with the weight
+    // prefetch; each thread tracks the maximum of what it loaded.
     reinterpret_cast<uint32_t *>(smem + L.zero)[tid] = 0u;  // 256 x 4 B
-    if (!p.x_vec4) {  // unaligned activations: plain loads
-        for (int t = 0; t < m; t++)
-            for (int k = tid; k < xn; k += 256) xs[t * cps * CHUNK_K + k] = p.x[t * p.ldx + k_lo + k];
+    float xmax[NT];
+#pragma unroll
+    for (int t = 0; t < NT; t++) {
+        float mx = 0.f;
+        bool fin = true;
+        float *xd = xs + t * cps * CHUNK_K;
+        if (t >= m) {  // padding tokens are zero
+            for (int k = tid; k < xn; k += 256) xd[k] = 0.f;
+        } else if (p.x_vec4) {
+            const float4 *src = reinterpret_cast<const float4 *>(p.x + t * p.ldx + k_lo);
+            for (int k4 = tid; k4 < xn / 4; k4 += 256) {
+                const float4 v = src[k4];
+                reinterpret_cast<float4 *>(xd)[k4] = v;
+                mx = fmaxf(mx, fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w))));
+                fin = fin && isfinite(v.x) && isfinite(v.y) && isfinite(v.z) && isfinite(v.w);
+            }
+        } else {  // unaligned activations: scalar loads
+            for (int k = tid; k < xn; k += 256) {
+                const float v = p.x[t * p.ldx + k_lo + k];
+                xd[k] = v;
+                mx = fmaxf(mx, fabsf(v));
+                fin = fin && isfinite(v);
+            }
+        }
+        xmax[t] = fin ? mx : INFINITY;
     }
-    for (int t = m; t < NT; t++)  // padding tokens are zero
-        for (int k = tid; k < xn; k += 256) xs[t * cps * CHUNK_K + k] = 0.f;
     __syncthreads();  // barrier inits visible before anyone waits
     bool failed = false;
-    if (p.x_vec4 && !mbar_wait_bounded(xbar, 0u)) failed = true;
 
     // Per-token power-of-two scale for this CTA's column slice: x * scale
     // lies inside +-2^FIXED_BITS.
 #pragma unroll
     for (int t = 0; t < NT; t++) {
-        float mx = 0.f;
-        bool fin = true;
-        const float4 *xr = reinterpret_cast<const float4 *>(xs + t * cps * CHUNK_K);
-        for (int k4 = tid; k4 < xn / 4; k4 += 256) {
-            const float4 v = xr[k4];
-            mx = fmaxf(mx, fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w))));
-            fin = fin && isfinite(v.x) && isfinite(v.y) && isfinite(v.z) && isfinite(v.w);
-        }
-        if (!fin) mx = INFINITY;
+        float mx = xmax[t];
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
         if (lane == 0) red[warp * NT + t] = mx;
@@ -563,7 +561,6 @@ __global__ void __launch_bounds__(256, 2) gemv_kernel(GemvArgs p) {
                     ph ^= 1u;
                 }
             }
-            if (warp == 0 && p.x_vec4) mbar_wait_bounded(xbar, 0u);
         }
         __syncwarp();
     }
