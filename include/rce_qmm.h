@@ -163,6 +163,38 @@ int rce_qmm_device_error(rce_qmm_ctx *ctx, int *code, int clear);
 /* Wait for all work this thread queued on the context's streams. */
 int rce_qmm_synchronize(rce_qmm_ctx *ctx);
 
+/* ---- expert-grouped MoE FFN ---------------------------------------------- */
+
+/* moe_router (rce-op-moe/src/lib.rs:35-73) on given router logits, on the
+ * device: for each of t_rows tokens, softmax over n_experts (<= 256) logits
+ * at d_logits[t * ld_logits], the top_k largest probabilities (ties to the
+ * lower expert index) into d_idx[t * top_k + j] / d_w[...], renormalised to
+ * sum 1 when normalize != 0.  Asynchronous on `stream`. */
+int rce_qmm_moe_route_device(rce_qmm_ctx *ctx, const float *d_logits, size_t ld_logits, size_t t_rows,
+                             int n_experts, int top_k, int normalize, int32_t *d_idx, float *d_w, void *stream);
+
+/* The expert-grouped SwiGLU FFN of moe_ffn_forward
+ * (rce-qwen36-moe/src/lib.rs:666-705) with moe_router / moe_combine
+ * (rce-op-moe/src/lib.rs:35-110): route every token as
+ * rce_qmm_moe_route_device does (normalised), then for each routed expert e
+ * g = W_gate[e] x, u = W_up[e] x, h = silu(g) * u, y = W_down[e] h, and
+ * out[t] = sum over route slots j, in order, of w_j * y_j.  Experts outside
+ * [expert_begin, expert_end) are skipped (their slots add nothing), so with
+ * the experts placed across GPUs the sum of every GPU's output is the full
+ * FFN (for top_k <= 2 bit for bit: adding zeros and swapping two terms
+ * round alike).  gate/up/down hold n_experts weight handles each (entries
+ * outside the local range may be NULL); gate/up are [d_ff x d_model], down
+ * [d_model x d_ff].  Each expert's rows run through mm_batched's dispatch
+ * (the decode GEMV below prefill_min_tokens rows, the tensor-core GEMM
+ * above).  Device buffers; the call synchronises `stream` once (to size
+ * the per-expert matmuls) and grows a per-stream workspace on first use.
+ * d_idx / d_w (optional, [t_rows][top_k]) receive the routes. */
+int rce_qmm_moe_ffn_device(rce_qmm_ctx *ctx, const float *d_x, size_t ldx, size_t t_rows,
+                           const float *d_logits, size_t ld_logits, int n_experts, int top_k,
+                           int expert_begin, int expert_end, const rce_qmm_weight *const *gate,
+                           const rce_qmm_weight *const *up, const rce_qmm_weight *const *down, float *d_out,
+                           size_t ldo, int32_t *d_idx, float *d_w, void *stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -56,6 +56,9 @@ SIGNATURES = {
     "rce_qmm_dequant_row": (_int, [_vp, _vp, _i64, _f32p, _sz]),
     "rce_qmm_dequant_device": (_int, [_vp, _vp, _i64, _i64, _vp, _sz, _vp]),
     "rce_qmm_device_error": (_int, [_vp, _c.POINTER(_int), _int]),
+    "rce_qmm_moe_route_device": (_int, [_vp, _vp, _sz, _sz, _int, _int, _int, _vp, _vp, _vp]),
+    "rce_qmm_moe_ffn_device": (_int, [_vp, _vp, _sz, _sz, _vp, _sz, _int, _int, _int, _int, _vp, _vp, _vp, _vp,
+                                       _sz, _vp, _vp, _vp]),
     "rce_qmm_synchronize": (_int, [_vp]),
 }
 

@@ -182,6 +182,32 @@ int run_matmul(rce_qmm_ctx *ctx, const rce_qmm_weight *w, const float *d_x, size
     return ok();
 }
 
+// MoE FFN workspace for stream s (grown like the split-K scratch) and its
+// pinned host mirror of the per-expert row offsets.
+int stream_moe_ws(rce_qmm_ctx *ctx, cudaStream_t s, size_t bytes, size_t host_n, void **ws, int32_t **host) {
+    std::lock_guard<std::mutex> lk(ctx->mu);
+    RceScratch &sc = ctx->scratch[s];
+    if (sc.moe_ws_bytes < bytes) {
+        CUDA_TRY(cudaStreamSynchronize(s));
+        if (sc.moe_ws) cudaFree(sc.moe_ws);
+        sc.moe_ws = nullptr;
+        sc.moe_ws_bytes = 0;
+        CUDA_TRY(cudaMalloc(&sc.moe_ws, bytes));
+        sc.moe_ws_bytes = bytes;
+    }
+    if (sc.moe_host_n < host_n) {
+        CUDA_TRY(cudaStreamSynchronize(s));
+        if (sc.moe_host) cudaFreeHost(sc.moe_host);
+        sc.moe_host = nullptr;
+        sc.moe_host_n = 0;
+        CUDA_TRY(cudaMallocHost(&sc.moe_host, host_n * sizeof(int32_t)));
+        sc.moe_host_n = host_n;
+    }
+    *ws = sc.moe_ws;
+    *host = sc.moe_host;
+    return ok();
+}
+
 int register_common(rce_qmm_ctx *ctx, const void *src, bool src_on_device, size_t nbytes, int dtype,
                     int64_t n_rows, int64_t n_cols, cudaStream_t s, rce_qmm_weight **out) {
     if (!ctx || !src || !out) return fail(RCE_QMM_ERR_INVALID, "weight_register: null argument");
@@ -298,6 +324,8 @@ int rce_qmm_ctx_destroy(rce_qmm_ctx *ctx) {
         if (kv.second.partial) cudaFree(kv.second.partial);
         if (kv.second.counters) cudaFree(kv.second.counters);
         if (kv.second.gemm_ws) cudaFree(kv.second.gemm_ws);
+        if (kv.second.moe_ws) cudaFree(kv.second.moe_ws);
+        if (kv.second.moe_host) cudaFreeHost(kv.second.moe_host);
     }
     if (ctx->err_host) cudaFreeHost(ctx->err_host);
     delete ctx;
@@ -525,6 +553,128 @@ int rce_qmm_synchronize(rce_qmm_ctx *ctx) {
     int rc = thread_state(ctx, &ts);
     if (rc) return rc;
     CUDA_TRY(cudaStreamSynchronize(ts->stream));
+    return ok();
+}
+
+int rce_qmm_moe_route_device(rce_qmm_ctx *ctx, const float *d_logits, size_t ld_logits, size_t t_rows,
+                             int n_experts, int top_k, int normalize, int32_t *d_idx, float *d_w, void *stream) {
+    if (!ctx) return fail(RCE_QMM_ERR_INVALID, "moe_route_device: null ctx");
+    if (n_experts < 1 || n_experts > 256 || top_k < 1 || top_k > n_experts)
+        return fail(RCE_QMM_ERR_INVALID, "moe_route_device: n_experts %d (1..256), top_k %d (1..n_experts)",
+                    n_experts, top_k);
+    if (t_rows == 0) return ok();
+    if (!d_logits || !d_idx || !d_w || ld_logits < (size_t)n_experts || t_rows > (size_t)INT32_MAX)
+        return fail(RCE_QMM_ERR_INVALID, "moe_route_device: null buffer, ld_logits < n_experts or too many rows");
+    DeviceGuard dg(ctx->device);
+    CUDA_TRY(rce::launch_moe_route(d_logits, ld_logits, (int)t_rows, n_experts, top_k, normalize, d_idx, d_w,
+                                   (cudaStream_t)stream));
+    return ok();
+}
+
+int rce_qmm_moe_ffn_device(rce_qmm_ctx *ctx, const float *d_x, size_t ldx, size_t t_rows,
+                           const float *d_logits, size_t ld_logits, int n_experts, int top_k,
+                           int expert_begin, int expert_end, const rce_qmm_weight *const *gate,
+                           const rce_qmm_weight *const *up, const rce_qmm_weight *const *down, float *d_out,
+                           size_t ldo, int32_t *d_idx, float *d_w, void *stream) {
+    if (!ctx) return fail(RCE_QMM_ERR_INVALID, "moe_ffn_device: null ctx");
+    if (n_experts < 1 || n_experts > 256 || top_k < 1 || top_k > n_experts)
+        return fail(RCE_QMM_ERR_INVALID, "moe_ffn_device: n_experts %d (1..256), top_k %d (1..n_experts)",
+                    n_experts, top_k);
+    if (expert_begin < 0 || expert_end > n_experts || expert_begin >= expert_end)
+        return fail(RCE_QMM_ERR_INVALID, "moe_ffn_device: expert range [%d, %d) of %d", expert_begin, expert_end,
+                    n_experts);
+    if (!gate || !up || !down) return fail(RCE_QMM_ERR_INVALID, "moe_ffn_device: null weight array");
+    // shapes: every local expert's gate/up are [d_ff x d_model], down [d_model x d_ff]
+    const rce_qmm_weight *g0 = gate[expert_begin];
+    int rc = check_weight(g0);
+    if (rc) return rc;
+    const int64_t d_model = g0->g.n_cols, d_ff = g0->g.n_rows;
+    for (int e = expert_begin; e < expert_end; e++) {
+        const rce_qmm_weight *ws[3] = {gate[e], up[e], down[e]};
+        for (int q = 0; q < 3; q++) {
+            rc = check_weight(ws[q]);
+            if (rc) return rc;
+            if (ws[q]->ctx != ctx) return fail(RCE_QMM_ERR_INVALID, "moe_ffn_device: weight of another context");
+        }
+        if (gate[e]->g.n_rows != d_ff || gate[e]->g.n_cols != d_model || up[e]->g.n_rows != d_ff ||
+            up[e]->g.n_cols != d_model || down[e]->g.n_rows != d_model || down[e]->g.n_cols != d_ff)
+            return fail(RCE_QMM_ERR_INVALID,
+                        "moe_ffn_device: expert %d: gate/up must be [%lld x %lld] and down [%lld x %lld]", e,
+                        (long long)d_ff, (long long)d_model, (long long)d_model, (long long)d_ff);
+    }
+    if (t_rows == 0) return ok();
+    if (!d_x || !d_logits || !d_out) return fail(RCE_QMM_ERR_INVALID, "moe_ffn_device: null buffer");
+    if (ldx < (size_t)d_model || ldo < (size_t)d_model || ld_logits < (size_t)n_experts)
+        return fail(RCE_QMM_ERR_INVALID, "moe_ffn_device: ldx %zu / ldo %zu < d_model %lld or ld_logits %zu < %d",
+                    ldx, ldo, (long long)d_model, ld_logits, n_experts);
+    if (t_rows * (size_t)top_k > (size_t)INT32_MAX / 2)
+        return fail(RCE_QMM_ERR_INVALID, "moe_ffn_device: too many tokens");
+    DeviceGuard dg(ctx->device);
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    const int n_local = expert_end - expert_begin;
+    const size_t P = t_rows * (size_t)top_k;
+    auto al = [](size_t v) { return (v + 255) / 256 * 256; };
+    size_t o = 0;
+    const size_t o_idx = o;
+    o += al(P * 4);
+    const size_t o_w = o;
+    o += al(P * 4);
+    const size_t o_pos = o;
+    o += al(P * 4);
+    const size_t o_tok = o;
+    o += al(P * 4);
+    const size_t o_off = o;
+    o += al((size_t)(n_local + 1) * 4);
+    const size_t o_xg = o;
+    o += al(P * (size_t)d_model * 4);
+    const size_t o_g = o;
+    o += al(P * (size_t)d_ff * 4);
+    const size_t o_u = o;
+    o += al(P * (size_t)d_ff * 4);
+    const size_t o_y = o;
+    o += al(P * (size_t)d_model * 4);
+    void *wsv = nullptr;
+    int32_t *host_off = nullptr;
+    rc = stream_moe_ws(ctx, s, o, (size_t)n_local + 1, &wsv, &host_off);
+    if (rc) return rc;
+    uint8_t *ws = static_cast<uint8_t *>(wsv);
+    int32_t *idx = d_idx ? d_idx : reinterpret_cast<int32_t *>(ws + o_idx);
+    float *wt = d_w ? d_w : reinterpret_cast<float *>(ws + o_w);
+    int32_t *pos = reinterpret_cast<int32_t *>(ws + o_pos);
+    int32_t *tok = reinterpret_cast<int32_t *>(ws + o_tok);
+    int32_t *off = reinterpret_cast<int32_t *>(ws + o_off);
+    float *xg = reinterpret_cast<float *>(ws + o_xg);
+    float *gb = reinterpret_cast<float *>(ws + o_g);
+    float *ub = reinterpret_cast<float *>(ws + o_u);
+    float *yb = reinterpret_cast<float *>(ws + o_y);
+
+    CUDA_TRY(rce::launch_moe_route(d_logits, ld_logits, (int)t_rows, n_experts, top_k, 1, idx, wt, s));
+    CUDA_TRY(rce::launch_moe_plan(idx, (int)P, top_k, expert_begin, expert_end, off, pos, tok, s));
+    // the per-expert row counts size the matmuls below
+    CUDA_TRY(cudaMemcpyAsync(host_off, off, (size_t)(n_local + 1) * 4, cudaMemcpyDeviceToHost, s));
+    CUDA_TRY(cudaStreamSynchronize(s));
+    const int rows = host_off[n_local];
+    if (rows > 0) {
+        CUDA_TRY(rce::launch_moe_gather(d_x, ldx, tok, rows, (int)d_model, xg, s));
+        for (int i = 0; i < n_local; i++) {
+            const size_t r0 = (size_t)host_off[i], n = (size_t)(host_off[i + 1] - host_off[i]);
+            if (n == 0) continue;
+            const int e = expert_begin + i;
+            rc = run_matmul(ctx, gate[e], xg + r0 * d_model, (size_t)d_model, n, gb + r0 * d_ff, (size_t)d_ff, s);
+            if (rc) return rc;
+            rc = run_matmul(ctx, up[e], xg + r0 * d_model, (size_t)d_model, n, ub + r0 * d_ff, (size_t)d_ff, s);
+            if (rc) return rc;
+        }
+        CUDA_TRY(rce::launch_swiglu(gb, ub, gb, (size_t)rows * d_ff, s));
+        for (int i = 0; i < n_local; i++) {
+            const size_t r0 = (size_t)host_off[i], n = (size_t)(host_off[i + 1] - host_off[i]);
+            if (n == 0) continue;
+            rc = run_matmul(ctx, down[expert_begin + i], gb + r0 * d_ff, (size_t)d_ff, n, yb + r0 * d_model,
+                            (size_t)d_model, s);
+            if (rc) return rc;
+        }
+    }
+    CUDA_TRY(rce::launch_moe_combine(yb, (int)d_model, pos, wt, (int)t_rows, top_k, d_out, ldo, s));
     return ok();
 }
 

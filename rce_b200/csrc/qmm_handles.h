@@ -16,6 +16,10 @@ struct RceScratch {
     size_t ncounters = 0;
     void *gemm_ws = nullptr;  // prefill GEMM workspace (fp16 activations, token scales)
     size_t gemm_ws_bytes = 0;
+    void *moe_ws = nullptr;   // MoE FFN workspace (routes, rows, activations per row)
+    size_t moe_ws_bytes = 0;
+    int32_t *moe_host = nullptr;  // pinned copy of the per-expert row offsets
+    size_t moe_host_n = 0;
 };
 
 struct RceThreadState {

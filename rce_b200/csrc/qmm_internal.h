@@ -52,6 +52,22 @@ size_t gemm_workspace_bytes(const Geometry &g, int t_rows);
 cudaError_t launch_gemm(int dt, const uint8_t *tiles, const Geometry &g, const float *x, size_t ldx, float *y,
                         size_t ldy, int t_rows, void *workspace, int *err, cudaStream_t s);
 
+// MoE pieces (qmm_moe.cu).  route: per token softmax / top_k / renormalise
+// of router logits [t_rows][ld] into idx, w [t_rows][top_k] (n_experts <=
+// 256).  plan: rows for the (token, slot) pairs whose expert lies in
+// [e_begin, e_end), grouped by expert: offsets [n_local + 1], pos [pairs]
+// (-1: not local), token [rows].  gather: xg[row] = x[token[row]].
+// swiglu: h = silu(g) * u.  combine: out[t] = sum_j w[t][j] y[pos[t][j]].
+cudaError_t launch_moe_route(const float *logits, size_t ld, int t_rows, int n_experts, int top_k, int normalize,
+                             int32_t *idx, float *w, cudaStream_t s);
+cudaError_t launch_moe_plan(const int32_t *idx, int pairs, int top_k, int e_begin, int e_end, int32_t *offsets,
+                            int32_t *pos, int32_t *token, cudaStream_t s);
+cudaError_t launch_moe_gather(const float *x, size_t ldx, const int32_t *token, int rows, int d_model, float *xg,
+                              cudaStream_t s);
+cudaError_t launch_swiglu(const float *g, const float *u, float *h, size_t n, cudaStream_t s);
+cudaError_t launch_moe_combine(const float *y, int d_model, const int32_t *pos, const float *w, int t_rows, int top_k,
+                               float *out, size_t ldo, cudaStream_t s);
+
 // Kernel error codes written to the context's error word.
 constexpr int kKernelErrWaitTimeout = 1;
 

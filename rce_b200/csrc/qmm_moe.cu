@@ -1,0 +1,188 @@
+// qmm_moe.cu -- the device side of the expert-grouped MoE FFN: routing,
+// grouping of (token, route slot) pairs by expert, the gather of their
+// activations, the SwiGLU product between the gate/up and down matmuls, and
+// the weighted combine.  The matmuls themselves are the library's quantized
+// matmul (qmm_gemv.cu / qmm_gemm.cu) over each expert's rows.
+//
+// Reference: moe_router and moe_combine (rce-op-moe/src/lib.rs:35-110) and
+// the SwiGLU expert FFN moe_ffn_forward (rce-qwen36-moe/src/lib.rs:666-705,
+// silu :649-656).
+#include <cuda_runtime.h>
+
+#include <cstdint>
+
+#include "qmm_internal.h"
+
+namespace rce {
+namespace {
+
+// One thread per token: softmax over all experts (max subtracted), the
+// top_k largest probabilities (ties to the lower expert index), optionally
+// renormalised to sum 1 -- the arithmetic of moe_router
+// (rce-op-moe/src/lib.rs:49-72): exp of (l - max), a left-to-right f32 sum,
+// one IEEE division per probability, the selected weights summed in rank
+// order.  exp is the device expf (the reference uses the platform libm; the
+// two may differ in the last bit).
+__global__ void route_kernel(const float *logits, size_t ld, int t_rows, int n_experts, int top_k, int normalize,
+                             int32_t *idx, float *w) {
+    const int t = blockIdx.x * blockDim.x + threadIdx.x;
+    if (t >= t_rows) return;
+    const float *l = logits + (size_t)t * ld;
+    float mx = -INFINITY;
+    for (int e = 0; e < n_experts; e++) mx = fmaxf(mx, l[e]);
+    float sum = 0.f;
+    for (int e = 0; e < n_experts; e++) sum = sum + expf(l[e] - mx);
+    // top_k by repeated selection of the largest remaining probability;
+    // each probability is recomputed exactly as above (same operands, same
+    // rounding), so no per-expert array is needed
+    uint32_t taken[8] = {0, 0, 0, 0, 0, 0, 0, 0};  // bit set of chosen experts (n_experts <= 256)
+    float s = 0.f;
+    for (int j = 0; j < top_k; j++) {
+        int best = -1;
+        float bp = 0.f;
+        for (int e = 0; e < n_experts; e++) {
+            if (taken[e >> 5] & (1u << (e & 31))) continue;
+            float p = expf(l[e] - mx);
+            if (sum > 0.f) p = p / sum;
+            if (best < 0 || p > bp) {  // strictly greater: ties keep the lower index
+                best = e;
+                bp = p;
+            }
+        }
+        taken[best >> 5] |= 1u << (best & 31);
+        idx[(size_t)t * top_k + j] = best;
+        w[(size_t)t * top_k + j] = bp;
+    }
+    if (normalize) {
+        for (int j = 0; j < top_k; j++) s = s + w[(size_t)t * top_k + j];
+        if (s > 0.f)
+            for (int j = 0; j < top_k; j++) w[(size_t)t * top_k + j] = w[(size_t)t * top_k + j] / s;
+    }
+}
+
+// One CTA: rows for the (token, slot) pairs routed to experts [e_begin,
+// e_end), grouped by expert.  offsets[i] = first row of local expert i
+// (offsets[n_local] = rows in all); pos[pair] = its row or -1; token[row] =
+// the pair's token.  The order of rows inside an expert is not defined (it
+// does not change any result: every row of a matmul is computed on its own).
+__global__ void __launch_bounds__(1024) plan_kernel(const int32_t *idx, int pairs, int top_k, int e_begin,
+                                                    int e_end, int32_t *offsets, int32_t *pos, int32_t *token) {
+    extern __shared__ int32_t cnt[];  // [n_local + 1]
+    const int n_local = e_end - e_begin;
+    for (int i = threadIdx.x; i <= n_local; i += blockDim.x) cnt[i] = 0;
+    __syncthreads();
+    for (int p = threadIdx.x; p < pairs; p += blockDim.x) {
+        const int e = idx[p];
+        pos[p] = (e >= e_begin && e < e_end) ? atomicAdd(&cnt[e - e_begin], 1) : -1;
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        int run = 0;
+        for (int i = 0; i < n_local; i++) {
+            const int c = cnt[i];
+            cnt[i] = run;
+            offsets[i] = run;
+            run += c;
+        }
+        offsets[n_local] = run;
+    }
+    __syncthreads();
+    for (int p = threadIdx.x; p < pairs; p += blockDim.x) {
+        const int e = idx[p];
+        if (e >= e_begin && e < e_end) {
+            const int row = cnt[e - e_begin] + pos[p];
+            pos[p] = row;
+            token[row] = p / top_k;
+        }
+    }
+}
+
+// xg[row] = x[token[row]], d_model floats per row.
+__global__ void gather_kernel(const float *x, size_t ldx, const int32_t *token, int rows, int d_model, float *xg) {
+    const int r = blockIdx.y;
+    if (r >= rows) return;
+    const float *src = x + (size_t)token[r] * ldx;
+    float *dst = xg + (size_t)r * d_model;
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < d_model; i += gridDim.x * blockDim.x) dst[i] = src[i];
+}
+
+// silu as moe_ffn_forward's expert computes it (rce-qwen36-moe/src/lib.rs:649-656):
+// x / (1 + exp(-x)) for x >= 0, x e^x / (1 + e^x) below, each operation
+// rounded on its own.
+__device__ __forceinline__ float silu_ref(float x) {
+    if (x >= 0.f) {
+        const float den = __fadd_rn(1.f, expf(-x));
+        return __fdiv_rn(x, den);
+    }
+    const float e = expf(x);
+    const float num = __fmul_rn(x, e);
+    const float den = __fadd_rn(1.f, e);
+    return __fdiv_rn(num, den);
+}
+
+// h = silu(g) * u, element by element (h may be g).
+__global__ void swiglu_kernel(const float *g, const float *u, float *h, size_t n) {
+    for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x)
+        h[i] = __fmul_rn(silu_ref(g[i]), u[i]);
+}
+
+// out[t] = sum over route slots j (in order, from 0) of w[t][j] * y[pos[t][j]],
+// slots whose expert is not local skipped (moe_combine, rce-op-moe/src/lib.rs:98-110).
+__global__ void combine_kernel(const float *y, int d_model, const int32_t *pos, const float *w, int top_k,
+                               float *out, size_t ldo) {
+    const int t = blockIdx.y;
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < d_model; i += gridDim.x * blockDim.x) {
+        float acc = 0.f;
+        for (int j = 0; j < top_k; j++) {
+            const int r = pos[(size_t)t * top_k + j];
+            if (r >= 0) acc = __fadd_rn(acc, __fmul_rn(w[(size_t)t * top_k + j], y[(size_t)r * d_model + i]));
+        }
+        out[(size_t)t * ldo + i] = acc;
+    }
+}
+
+}  // namespace
+
+cudaError_t launch_moe_route(const float *logits, size_t ld, int t_rows, int n_experts, int top_k, int normalize,
+                             int32_t *idx, float *w, cudaStream_t s) {
+    if (t_rows <= 0) return cudaSuccess;
+    if (n_experts < 1 || n_experts > 256 || top_k < 1 || top_k > n_experts) return cudaErrorInvalidValue;
+    route_kernel<<<(t_rows + 127) / 128, 128, 0, s>>>(logits, ld, t_rows, n_experts, top_k, normalize, idx, w);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_moe_plan(const int32_t *idx, int pairs, int top_k, int e_begin, int e_end, int32_t *offsets,
+                            int32_t *pos, int32_t *token, cudaStream_t s) {
+    const int n_local = e_end - e_begin;
+    if (pairs <= 0 || n_local < 1) return cudaErrorInvalidValue;
+    const size_t smem = (size_t)(n_local + 1) * sizeof(int32_t);
+    if (smem > 48 * 1024) return cudaErrorInvalidValue;
+    plan_kernel<<<1, 1024, smem, s>>>(idx, pairs, top_k, e_begin, e_end, offsets, pos, token);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_moe_gather(const float *x, size_t ldx, const int32_t *token, int rows, int d_model, float *xg,
+                              cudaStream_t s) {
+    if (rows <= 0) return cudaSuccess;
+    dim3 grid((d_model + 255) / 256 < 8 ? (d_model + 255) / 256 : 8, rows);
+    gather_kernel<<<grid, 256, 0, s>>>(x, ldx, token, rows, d_model, xg);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_swiglu(const float *g, const float *u, float *h, size_t n, cudaStream_t s) {
+    if (n == 0) return cudaSuccess;
+    size_t blocks = (n + 255) / 256;
+    if (blocks > 4096) blocks = 4096;
+    swiglu_kernel<<<(unsigned)blocks, 256, 0, s>>>(g, u, h, n);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_moe_combine(const float *y, int d_model, const int32_t *pos, const float *w, int t_rows, int top_k,
+                               float *out, size_t ldo, cudaStream_t s) {
+    if (t_rows <= 0) return cudaSuccess;
+    dim3 grid((d_model + 255) / 256 < 8 ? (d_model + 255) / 256 : 8, t_rows);
+    combine_kernel<<<grid, 256, 0, s>>>(y, d_model, pos, w, top_k, out, ldo);
+    return cudaGetLastError();
+}
+
+}  // namespace rce

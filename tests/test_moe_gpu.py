@@ -1,0 +1,184 @@
+"""The expert-grouped MoE FFN on the device (rce_qmm_moe_route_device,
+rce_qmm_moe_ffn_device) against the oracle's restatement of moe_router /
+moe_combine (rce-op-moe/src/lib.rs:35-110) and moe_ffn_forward
+(rce-qwen36-moe/src/lib.rs:666-705).
+
+Bars:
+- routes: the same experts in the same rank order; weights within a few
+  units in the last place (the device expf and the host libm exp may differ
+  in the last bit);
+- exact path (prefill_min_tokens = 0, every expert's rows through the
+  decode GEMV): per token max|got - want| / max|want| <= 1e-5;
+- default path (experts with >= 16 rows through the fp16 tensor-core GEMM):
+  max-norm error over the whole output <= 1e-3, and within 2.5e-4 of a model
+  of fp16 operands with exact accumulation (per-token relative L2 errors are
+  printed: tokens whose two experts' outputs cancel have a tail of a few
+  1e-3, which that model reproduces);
+- experts split into ranges: the ranges' outputs add up to the full output
+  bit for bit (top-2).
+"""
+import numpy as np
+import pytest
+
+import oracle as O
+import rce_b200 as R
+from rce_b200 import synth
+
+pytestmark = pytest.mark.gpu
+
+Q4_K, Q8_0, Q4_0 = O.GGUF_Q4_K, O.GGUF_Q8_0, O.GGUF_Q4_0
+
+
+def _setup(dt, n_experts, d_model, d_ff, t_rows, seed):
+    rng = np.random.default_rng(seed)
+    gate = [synth.weights(dt, d_ff, d_model, rng) for _ in range(n_experts)]
+    up = [synth.weights(dt, d_ff, d_model, rng) for _ in range(n_experts)]
+    down = [synth.weights(dt, d_model, d_ff, rng) for _ in range(n_experts)]
+    x = synth.activations(t_rows, d_model, rng)
+    logits = rng.standard_normal((t_rows, n_experts)).astype(np.float32)
+    return gate, up, down, x, logits
+
+
+def _device(ctx, dt, gate, up, down, d_model, d_ff):
+    g = [R.QuantWeight.from_owned_bytes(b, dt, d_ff, d_model, ctx=ctx) for b in gate]
+    u = [R.QuantWeight.from_owned_bytes(b, dt, d_ff, d_model, ctx=ctx) for b in up]
+    d = [R.QuantWeight.from_owned_bytes(b, dt, d_model, d_ff, ctx=ctx) for b in down]
+    return g, u, d
+
+
+@pytest.mark.parametrize("n_experts,top_k,normalize", [(8, 2, True), (128, 8, True), (16, 4, False), (3, 1, True)])
+def test_route_matches_oracle(n_experts, top_k, normalize):
+    import torch
+
+    rng = np.random.default_rng(40 + n_experts)
+    logits = rng.standard_normal((300, n_experts)).astype(np.float32)
+    idx, w = R.moe_route_device(torch.from_numpy(logits).cuda(), top_k, normalize)
+    idx, w = idx.cpu().numpy(), w.cpu().numpy()
+    for t in range(logits.shape[0]):
+        ri, rw = O.moe_softmax_topk(logits[t], top_k, normalize)
+        assert list(idx[t]) == list(ri), f"token {t}"
+        np.testing.assert_allclose(w[t], rw, rtol=4e-7, atol=0)
+    dec = R.decisions(torch.from_numpy(idx), torch.from_numpy(w))
+    assert len(dec) == 300 and dec[0].expert_indices == list(idx[0])
+
+
+def _ffn(ctx, dt, n_experts, top_k, d_model, d_ff, t_rows, seed, **kw):
+    import torch
+
+    gate, up, down, x, logits = _setup(dt, n_experts, d_model, d_ff, t_rows, seed)
+    want = O.moe_ffn(x, logits, top_k, np.stack(gate), np.stack(up), np.stack(down), dt, d_ff, nthreads=8)
+    g, u, d = _device(ctx, dt, gate, up, down, d_model, d_ff)
+    got, idx, w = R.moe_ffn_device(torch.from_numpy(x).cuda(), torch.from_numpy(logits).cuda(), top_k, g, u, d,
+                                   return_routes=True, **kw)
+    torch.cuda.synchronize()
+    assert ctx.device_error() == 0
+    return got.cpu().numpy(), want, (g, u, d, x, logits)
+
+
+@pytest.mark.parametrize("dt", [Q4_K, Q8_0, Q4_0])
+def test_ffn_exact_path_matches_oracle(ctx, dt):
+    saved = ctx.prefill_min_tokens
+    ctx.prefill_min_tokens = 0
+    try:
+        got, want, _ = _ffn(ctx, dt, 4, 2, 256, 512, 37, 7 + dt)
+    finally:
+        ctx.prefill_min_tokens = saved
+    err = np.abs(got - want).max(axis=1) / np.abs(want).max(axis=1)
+    print(f"MoE exact path dtype {dt}: per-token normwise {err.max():.3e}")
+    assert err.max() <= 1e-5
+
+
+def _fp16_operand_model(dt, gate, up, down, x, logits, top_k, d_model, d_ff):
+    """The FFN as the tensor-core path computes it: each matmul's activation
+    row scaled by a power of two and rounded to fp16, the dequantised weights
+    rounded to fp16, products accumulated exactly (f64), SwiGLU in f32."""
+    Wg = [O.dequant(b, dt, d_ff * d_model).reshape(d_ff, d_model) for b in gate]
+    Wu = [O.dequant(b, dt, d_ff * d_model).reshape(d_ff, d_model) for b in up]
+    Wd = [O.dequant(b, dt, d_model * d_ff).reshape(d_model, d_ff) for b in down]
+    h16 = lambda W: W.astype(np.float16).astype(np.float64)  # noqa: E731
+
+    def r16(a):
+        a = np.asarray(a, np.float32)
+        e = np.frexp(np.abs(a).max(axis=-1, keepdims=True))[1]
+        s = np.ldexp(np.float32(1.0), 14 - e).astype(np.float32)
+        return (a * s).astype(np.float16).astype(np.float64) / s
+
+    Wg, Wu, Wd = [h16(w) for w in Wg], [h16(w) for w in Wu], [h16(w) for w in Wd]
+    out = np.zeros((x.shape[0], d_model))
+    for t in range(x.shape[0]):
+        idx, w = O.moe_softmax_topk(logits[t], top_k, True)
+        for j in range(top_k):
+            e = idx[j]
+            xr = r16(x[t][None])[0]
+            g = (Wg[e] @ xr).astype(np.float32)
+            u = (Wu[e] @ xr).astype(np.float32)
+            with np.errstate(over="ignore"):
+                h = (g / (np.float32(1) + np.exp(-g))) * u
+            out[t] += np.float64(w[j]) * (Wd[e] @ r16(h[None])[0])
+    return out
+
+
+@pytest.mark.parametrize("dt", [Q4_K, Q8_0])
+def test_ffn_gemm_path_matches_oracle(ctx, dt):
+    # 4 experts, 200 tokens x top-2: every expert gets far more than 16 rows
+    assert ctx.prefill_min_tokens == 16
+    d_model, d_ff = 512, 1024
+    got, want, (g, u, d, x, logits) = _ffn(ctx, dt, 4, 2, d_model, d_ff, 200, 11 + dt)
+    gate, up, down, _, _ = _setup(dt, 4, d_model, d_ff, 200, 11 + dt)
+    scale = np.abs(want).max()
+    tensor = np.abs(got.astype(np.float64) - want).max() / scale
+    l2 = np.linalg.norm(got - want, axis=1) / np.linalg.norm(want, axis=1)
+    model = _fp16_operand_model(dt, gate, up, down, x, logits, 2, d_model, d_ff)
+    vs_model = np.abs(got - model).max() / scale
+    print(f"MoE GEMM path dtype {dt}: max-norm {tensor:.3e}; per-token L2 median {np.median(l2):.3e}, "
+          f"max {l2.max():.3e}; vs the fp16-operand model {vs_model:.3e}")
+    assert tensor <= 1e-3
+    # the tensor-core path is "fp16 operands, exact accumulation" up to f32
+    # accumulation and the last bit of exp inside silu, which can flip the
+    # fp16 rounding of an intermediate (the per-token L2 tail above is that
+    # operand rounding on tokens whose expert outputs cancel)
+    assert vs_model <= 2.5e-4
+
+
+def test_expert_ranges_add_up_bit_for_bit(ctx):
+    import torch
+
+    saved = ctx.prefill_min_tokens
+    ctx.prefill_min_tokens = 0
+    try:
+        full, _, (g, u, d, x, logits) = _ffn(ctx, Q4_K, 4, 2, 256, 512, 23, 99)
+        xd, ld = torch.from_numpy(x).cuda(), torch.from_numpy(logits).cuda()
+        parts = [R.moe_ffn_device(xd, ld, 2, g, u, d, expert_range=r).cpu().numpy() for r in [(0, 1), (1, 3), (3, 4)]]
+    finally:
+        ctx.prefill_min_tokens = saved
+    # each token's two routed experts: one range holds both, or two ranges one each
+    assert np.array_equal(parts[0] + parts[1] + parts[2], full)
+
+
+def test_ffn_mixtral_shape_token_subset(ctx):
+    # configs[4]'s expert shape (gate/up 14336 x 4096, down 4096 x 14336,
+    # Q4_K) with 4 experts and 8 tokens (the exact path), checked against the
+    # oracle
+    saved = ctx.prefill_min_tokens
+    ctx.prefill_min_tokens = 0
+    try:
+        got, want, _ = _ffn(ctx, Q4_K, 4, 2, 4096, 14336, 8, 4)
+    finally:
+        ctx.prefill_min_tokens = saved
+    err = np.abs(got - want).max(axis=1) / np.abs(want).max(axis=1)
+    print(f"MoE Mixtral expert shape, 8 tokens: per-token normwise {err.max():.3e}")
+    assert err.max() <= 1e-5
+
+
+def test_bad_arguments_are_errors(ctx):
+    import torch
+
+    gate, up, down, x, logits = _setup(Q4_K, 2, 256, 512, 4, 3)
+    g, u, d = _device(ctx, Q4_K, gate, up, down, 256, 512)
+    xd, ld = torch.from_numpy(x).cuda(), torch.from_numpy(logits).cuda()
+    with pytest.raises(R.QmmError):
+        R.moe_ffn_device(xd, ld, 3, g, u, d)          # top_k > n_experts
+    with pytest.raises(R.QmmError):
+        R.moe_ffn_device(xd, ld, 1, g, d, u)          # up/down shapes swapped
+    with pytest.raises(R.QmmError):
+        R.moe_ffn_device(xd, ld, 1, g, u, d, expert_range=(1, 1))
