@@ -269,6 +269,76 @@ def prefill_section(args, rank, world, dev, stream, ctx):
     return out
 
 
+# ---- MoE FFN ------------------------------------------------------------
+
+MOE_E, MOE_K, MOE_T = 8, 2, 256
+
+
+def moe_section(args, rank, world, dev, stream, ctx):
+    """Mixtral-shaped MoE FFN: 8 experts of Q4_K gate/up 14336x4096 and down
+    4096x14336, 256 tokens, top-2 from softmax of N(0,1) router logits.
+    Experts are placed world-ways (8/world per GPU); every GPU routes all
+    tokens, runs its experts' rows, and the outputs are summed over NCCL."""
+    import torch
+    import torch.distributed as dist
+
+    import rce_b200 as R
+    from rce_b200 import synth
+
+    if MOE_E % world:
+        return None
+    per = MOE_E // world
+    lo, hi = rank * per, (rank + 1) * per
+    gate, up, down = [None] * MOE_E, [None] * MOE_E, [None] * MOE_E
+    for e in range(lo, hi):
+        for lst, (n, k), salt in ((gate, (D_FF, D_MODEL), 1), (up, (D_FF, D_MODEL), 2), (down, (D_MODEL, D_FF), 3)):
+            g = torch.Generator(device=dev)
+            g.manual_seed(4_000_000 + 1009 * e + salt)
+            raw = synth.device_weights(Q4_K, n, k, g, dev)
+            lst[e] = R.QuantWeight.from_device_bytes(raw, Q4_K, n, k, ctx=ctx)
+            del raw
+    g = torch.Generator(device=dev)
+    g.manual_seed(4)
+    x = torch.randn((MOE_T, D_MODEL), device=dev, generator=g)
+    logits = torch.randn((MOE_T, MOE_E), device=dev, generator=g)
+    out = torch.empty((MOE_T, D_MODEL), device=dev)
+
+    def one():
+        R.moe_ffn_device(x, logits, MOE_K, gate, up, down, expert_range=(lo, hi), out=out, stream=stream)
+        if world > 1:
+            dist.all_reduce(out)
+
+    with torch.cuda.stream(stream):
+        for _ in range(3):
+            one()
+    stream.synchronize()
+    reps = 10
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize(dev)
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(stream):
+        e0.record(stream)
+        for _ in range(reps):
+            one()
+        e1.record(stream)
+    e1.synchronize()
+    ms = e0.elapsed_time(e1) / reps
+    if world > 1:
+        t = torch.tensor([ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    flops = 2.0 * MOE_T * MOE_K * 3 * D_FF * D_MODEL
+    wbytes = MOE_E * (2 * q4k_bytes(D_FF, D_MODEL) + q4k_bytes(D_MODEL, D_FF))
+    return {"workload": "configs[4]: Mixtral-shaped MoE FFN, 8 experts x Q4_K gate/up 14336x4096 + down 4096x14336, "
+                        "256 tokens, top-2 of softmax(N(0,1) logits), renormalised",
+            "placement": f"{per} experts per GPU" + (", outputs summed with NCCL all-reduce" if world > 1 else ""),
+            "ms": round(ms, 4), "tokens_per_s": round(MOE_T / (ms / 1e3), 1),
+            "tflops": round(flops / (ms / 1e3) / 1e12, 1), "weight_gbs": round(wbytes / (ms / 1e3) / 1e9, 1),
+            "timing": "CUDA events around whole calls (each call synchronises once to size the expert matmuls)"}
+
+
 # ---- our arm -------------------------------------------------------------------------
 
 def build_stack(args, rank, world, dev):
@@ -472,6 +542,7 @@ def main():
             traffic = None
 
     prefill = prefill_section(args, rank, world, dev, stream, ctx)
+    moe = moe_section(args, rank, world, dev, stream, ctx)
 
     # ---- e2e through the host C-ABI ----------------------------------------------
     e2e = None
@@ -544,6 +615,7 @@ def main():
                              "unit": "TFLOP/s", "frac": round(prefill["m512"]["tflops"] / bf16 / max(world, 1), 4),
                              "peak_kind": f"{peak_kind} bf16 dense (burst)"},
             },
+            "moe_ffn": moe,
             "e2e": e2e,
             "cpu_baseline": cpu,
             "clocks": clk,

@@ -18,10 +18,10 @@
 //   prep kernel: X (f32) -> Xh (fp16, [t_rows][K]) and 1/s per token;
 //   warp 0     : TMA bulk copies of the packed T16 chunks (8 tiles x 256
 //                columns per slot, 2-4 slots as shared memory allows);
-//   warps 1-16 : dequantise a quarter weight row each (16 values) into the
-//                A tile (fp16, K-major, 128-byte swizzle), then run the
+//   warps 1-16 : dequantisers in two groups of eight that take alternate
+//                k-blocks, half a weight row per thread (32 values), into
+//                the A tile (fp16, K-major, 128-byte swizzle); then the
 //                epilogue (tcgen05.ld from tensor memory, scale, store);
-//                four warps per scheduler hide each other's latency;
 //   warp 17    : one thread issues tcgen05.mma (kind::f16, M=128, N<=256,
 //                K=16 per instruction) into f32 accumulators in tensor
 //                memory and frees each stage with tcgen05.commit;
@@ -47,9 +47,10 @@ constexpr int kBK = 64;                // k-block (one 128-byte swizzle row of f
 constexpr int kBM = 128;               // weight rows per CTA (UMMA M)
 constexpr int kDqWarps = 16;           // dequantiser warps (four threads per weight row)
 constexpr int kWeightWarp = 0;         // TMA bulk copies of the packed weight chunks
-constexpr int kMmaWarp = kDqWarps + 1;  // tcgen05.alloc / mma / dealloc
-constexpr int kActWarp = kDqWarps + 2;  // TMA tensor loads of the activation k-blocks
-constexpr int kThreads = 32 * (kDqWarps + 3);
+constexpr int kMaxMmaWarps = 1;       // tcgen05.mma issuers (K split between them; see mma_warps)
+constexpr int kMmaWarp = kDqWarps + 1;  // the first; also tcgen05.alloc / dealloc
+constexpr int kActWarp = kDqWarps + 1 + kMaxMmaWarps;  // TMA tensor loads of the activation k-blocks
+constexpr int kThreads = 32 * (kActWarp + 1);
 
 __device__ __forceinline__ uint32_t smem_u32(const void *p) {
     return static_cast<uint32_t>(__cvta_generic_to_shared(p));
@@ -262,27 +263,39 @@ struct GemmSmem {
     int a_stages, b_stages, pslots;
 };
 
+constexpr int kMaxA = 8, kMaxB = 4, kMaxP = 4;  // ring depth limits (barrier slots)
+
 __host__ __device__ inline GemmSmem gemm_smem(int dt, int bn) {
+    // Rings as deep as 227 KB allow: the dequantiser <-> MMA hand-off takes
+    // a few thousand cycles, so the A ring should span several k-blocks;
+    // the activation ring shrinks as its stages grow with bn.
     constexpr size_t kLimit = 227 * 1024;  // dynamic shared memory per CTA (opt-in)
     GemmSmem L;
-    L.a_stages = 3;
-    L.b_stages = bn > 256 ? 2 : 3;
-    const size_t a_bytes = (size_t)L.a_stages * kBM * kBK * 2;
+    L.b_stages = bn > 256 ? 2 : (bn > 128 ? 3 : kMaxB);
+    const size_t a_stage = (size_t)kBM * kBK * 2;
     const size_t b_bytes = (size_t)L.b_stages * bn * kBK * 2;
     const size_t slot = (size_t)8 * chunk_bytes(dt);
-    const size_t fixed = a_bytes + b_bytes + 32 * 8 + 16 + 1024;
-    size_t ps = fixed < kLimit ? (kLimit - fixed) / slot : 0;
-    L.pslots = ps > 4 ? 4 : (int)ps;
+    const size_t misc = 64 * 8 + 16 + 1024;
+    L.pslots = 2;
+    size_t avail = kLimit > b_bytes + misc + 2 * slot ? kLimit - b_bytes - misc - 2 * slot : 0;
+    int na = (int)(avail / a_stage);
+    if (na > kMaxA) na = kMaxA;
+    // leftover room buys a third and fourth weight slot
+    while (L.pslots < kMaxP && na >= 3 && (size_t)na * a_stage + slot <= avail) {
+        L.pslots++;
+        avail -= slot;
+    }
+    L.a_stages = na < 2 ? 2 : na;
     size_t o = 0;
     L.a = o;  // 1024-aligned stages
-    o += a_bytes;
+    o += (size_t)L.a_stages * a_stage;
     L.b = o;
     o += b_bytes;
     L.packed = o;
     o += (size_t)L.pslots * slot;
     o = (o + 15) / 16 * 16;
     L.bars = o;
-    o += 32 * 8;
+    o += 64 * 8;
     L.tmem_slot = o;
     o += 16;
     L.total = o + 1024;  // slack to align the base to 1024
@@ -292,6 +305,13 @@ __host__ __device__ inline GemmSmem gemm_smem(int dt, int bn) {
 __host__ __device__ inline uint32_t tmem_cols(int bn) {
     return bn <= 32 ? 32u : (bn <= 64 ? 64u : (bn <= 128 ? 128u : (bn <= 256 ? 256u : 512u)));
 }
+
+// MMA issuer warps for token-tile width bn: k-blocks are dealt round-robin
+// to this many warps, each with its own accumulator (bn columns of tensor
+// memory each, 512 in all), and the epilogue adds them.  One issuer keeps
+// up with the rest of the pipeline at every bn measured (a second to fourth
+// issuer changed nothing at 16-128 tokens), so the split is kept at one.
+__host__ __device__ inline int mma_warps(int bn) { return (void)bn, 1; }
 
 template <int DT>
 __global__ void __launch_bounds__(kThreads, 1)
@@ -307,16 +327,16 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint8_t *pk = smem + L.packed;
     uint64_t *bars = reinterpret_cast<uint64_t *>(smem + L.bars);
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(smem + L.tmem_slot);
-    // barriers: [0,4) packed full, [4,8) packed empty, [8,11) A full,
-    // [11,14) A free, [14,17) B full, [17,20) B free, 20 accumulator full
+    // barriers: packed full / empty [kMaxP each], A full / empty [kMaxA
+    // each], B full / empty [kMaxB each], accumulator full
     const uint32_t bar0 = smem_u32(bars);
     auto PF = [&](int s) { return bar0 + 8 * (0 + s); };
-    auto PE = [&](int s) { return bar0 + 8 * (4 + s); };
-    auto AF = [&](int s) { return bar0 + 8 * (8 + s); };
-    auto AE = [&](int s) { return bar0 + 8 * (11 + s); };
-    auto BF = [&](int s) { return bar0 + 8 * (14 + s); };
-    auto BE = [&](int s) { return bar0 + 8 * (17 + s); };
-    const uint32_t ACC = bar0 + 8 * 20;
+    auto PE = [&](int s) { return bar0 + 8 * (kMaxP + s); };
+    auto AF = [&](int s) { return bar0 + 8 * (2 * kMaxP + s); };
+    auto AE = [&](int s) { return bar0 + 8 * (2 * kMaxP + kMaxA + s); };
+    auto BF = [&](int s) { return bar0 + 8 * (2 * kMaxP + 2 * kMaxA + s); };
+    auto BE = [&](int s) { return bar0 + 8 * (2 * kMaxP + 2 * kMaxA + kMaxB + s); };
+    const uint32_t ACC = bar0 + 8 * (2 * kMaxP + 2 * kMaxA + 2 * kMaxB);
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int tile0 = blockIdx.x * 8;  // first 16-row tile of this CTA
@@ -324,7 +344,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int tok0 = blockIdx.y * bn;
     const int nchunks = p.g.n_chunks;
     const int nkb = nchunks * 4;
-    const uint32_t ncols = tmem_cols(bn);
+    const int MW = mma_warps(bn);
+    const uint32_t acc_cols = tmem_cols(bn), ncols = acc_cols * (uint32_t)MW;
 
     if (tid == 0) {
         for (int s = 0; s < NP; s++) {
@@ -332,14 +353,14 @@ __global__ void __launch_bounds__(kThreads, 1)
             mbar_init(PE(s), kDqWarps);
         }
         for (int s = 0; s < NA; s++) {
-            mbar_init(AF(s), kDqWarps);
+            mbar_init(AF(s), kDqWarps / 2);  // one group fills a stage
             mbar_init(AE(s), 1);
         }
         for (int s = 0; s < NB; s++) {
             mbar_init(BF(s), 1);
             mbar_init(BE(s), 1);
         }
-        mbar_init(ACC, 1);
+        mbar_init(ACC, MW);  // each MMA warp's final commit
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
     if (warp == kMmaWarp) {  // tensor memory for the bn f32 accumulator columns
@@ -401,15 +422,26 @@ __global__ void __launch_bounds__(kThreads, 1)
                 for (int u = max(0, kb - NB); u < kb; u++) mbar_wait(BF(u % NB), (u / NB) & 1);
         }
     } else if (warp >= 1 && warp <= kDqWarps) {
-        // dequantisers: four threads per weight row
-        const int row = (tid - 32) >> 2, qr = (tid - 32) & 3;
-        int s = 0, st = 0;  // packed slot and A stage, with their phases
+        // dequantisers: two groups of eight warps take alternate k-blocks
+        // (each warp has two k-blocks' time for its chain of waits, loads,
+        // arithmetic and stores); two threads per weight row, 32 values each
+        const int grp = (warp - 1) / (kDqWarps / 2);
+        const int gt = tid - 32 - grp * (kDqWarps / 2) * 32;
+        const int row = gt >> 1, hf = gt & 1;
+        int s = 0, st = grp, cur_c = -1;  // packed slot and A stage, with their phases
         uint32_t sph = 0, aph = 0;
-        for (int kb = 0; kb < nkb && ok; kb++) {
-            const int j = kb & 3;
-            if (j == 0 && !mbar_wait(PF(s), sph)) {
-                ok = false;
-                break;
+        for (int kb = grp; kb < nkb && ok; kb += 2) {
+            const int c = kb >> 2, j = kb & 3;
+            if (c != cur_c) {  // the next chunk (one at a time: kb advances by 2 of its 4)
+                if (cur_c >= 0 && ++s == NP) {
+                    s = 0;
+                    sph ^= 1;
+                }
+                cur_c = c;
+                if (!mbar_wait(PF(s), sph)) {
+                    ok = false;
+                    break;
+                }
             }
             if (kb >= NA && !mbar_wait(AE(st), aph ^ 1)) {
                 ok = false;
@@ -417,41 +449,42 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
             uint8_t *a_tile = a_st + (size_t)st * kBM * kBK * 2;
             if (row < ntiles * 16) {
-                dequant_quarter<DT>(pk + (size_t)s * 8 * CB, row, qr, j, a_tile);
+                dequant_quarter<DT>(pk + (size_t)s * 8 * CB, row, 2 * hf, j, a_tile);
+                dequant_quarter<DT>(pk + (size_t)s * 8 * CB, row, 2 * hf + 1, j, a_tile);
             } else {  // rows past the weight: zeros
-                uint8_t *dst = a_tile + (row >> 3) * 1024 + (row & 7) * 128 + 32 * qr;
-                *reinterpret_cast<uint4 *>(dst) = make_uint4(0, 0, 0, 0);
-                *reinterpret_cast<uint4 *>(dst + 16) = make_uint4(0, 0, 0, 0);
+                uint8_t *dst = a_tile + (row >> 3) * 1024 + (row & 7) * 128 + 64 * hf;
+#pragma unroll
+                for (int q = 0; q < 4; q++) *reinterpret_cast<uint4 *>(dst + 16 * q) = make_uint4(0, 0, 0, 0);
             }
             asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // generic writes -> tensor-core reads
             __syncwarp();
             if (lane == 0) {  // one arrival per warp
                 mbar_arrive(AF(st));
-                if (j == 3) mbar_arrive(PE(s));  // this chunk is no longer read
+                if (j == 2 + grp) mbar_arrive(PE(s));  // this group is done with the chunk
             }
-            if (++st == NA) {
-                st = 0;
+            st += 2;
+            if (st >= NA) {
+                st -= NA;
                 aph ^= 1;
             }
-            if (j == 3 && ++s == NP) {
-                s = 0;
-                sph ^= 1;
-            }
         }
-    } else if (warp == kMmaWarp) {
-        // MMA issuer: per k-block, bn / 256 (at least one) accumulators of
-        // up to 256 columns, 4 instructions of K = 16 each
-        // lane 0 alone; descriptors advance by 32 bytes (2 in the >> 4 address
-        // field) per K = 16 step and by a whole stage per stage
+    } else if (warp >= kMmaWarp && warp < kMmaWarp + MW) {
+        // MMA issuer w takes k-blocks w, w + MW, ... into its own accumulator
+        // (columns w * acc_cols ..); per k-block, bn / 256 (at least one)
+        // sub-accumulators of up to 256 columns, 4 instructions of K = 16.
+        // One lane issues; descriptors advance by 32 bytes (2 in the >> 4
+        // address field) per K = 16 step and by a whole stage per stage.
+        const int w = warp - kMmaWarp;
         const int nsub = bn > 256 ? bn / 256 : 1, nw = bn > 256 ? 256 : bn;
         const uint32_t idesc = idesc_f16(nw);
+        const uint32_t acc = tmem + (uint32_t)w * acc_cols;
         if (lane == 0) {
             const uint64_t da0 = sw128_desc(smem_u32(a_st)), db0 = sw128_desc(smem_u32(b_st));
             const uint64_t a_step = (uint64_t)(kBM * kBK * 2) >> 4, b_step = (uint64_t)(bn * kBK * 2) >> 4;
             const uint64_t h_step = (uint64_t)(256 * kBK * 2) >> 4;
-            int sa = 0, sb = 0;
+            int sa = w, sb = w;  // stages of k-block kb = w (MW <= NA, NB)
             uint32_t aph = 0, bph = 0;
-            for (int kb = 0; kb < nkb; kb++) {
+            for (int kb = w; kb < nkb; kb += MW) {
                 if (!mbar_wait(AF(sa), aph) || !mbar_wait(BF(sb), bph)) {
                     ok = false;
                     break;
@@ -461,21 +494,23 @@ __global__ void __launch_bounds__(kThreads, 1)
                 for (int h = 0; h < nsub; h++) {
 #pragma unroll
                     for (int k = 0; k < kBK / 16; k++)  // 16 fp16 = 32 bytes per instruction
-                        umma_f16(tmem + (uint32_t)(h * 256), da + 2 * k, db + (uint64_t)h * h_step + 2 * k, idesc,
-                                 (kb | k) ? 1u : 0u);
+                        umma_f16(acc + (uint32_t)(h * 256), da + 2 * k, db + (uint64_t)h * h_step + 2 * k, idesc,
+                                 (kb != w || k) ? 1u : 0u);
                 }
                 umma_commit(AE(sa));
                 umma_commit(BE(sb));
-                if (++sa == NA) {
-                    sa = 0;
+                sa += MW;
+                if (sa >= NA) {
+                    sa -= NA;
                     aph ^= 1;
                 }
-                if (++sb == NB) {
-                    sb = 0;
+                sb += MW;
+                if (sb >= NB) {
+                    sb -= NB;
                     bph ^= 1;
                 }
             }
-            umma_commit(ACC);  // fires once every MMA above has completed
+            umma_commit(ACC);  // arrives once this warp's MMAs above have completed
         }
         __syncwarp();
     }
@@ -491,17 +526,22 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int row = tile0 * 16 + lane_base + lane;
         if (ok) {
             for (int c0 = c_begin; c0 < c_end; c0 += 8) {
-                uint32_t r[8];
-                asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
-                             : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
-                               "=r"(r[7])
-                             : "r"(tmem + ((uint32_t)lane_base << 16) + (uint32_t)c0));
-                asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+                float v[8];
+                for (int w = 0; w < MW; w++) {  // the issuers' accumulators, added in order
+                    uint32_t r[8];
+                    asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
+                                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+                                   "=r"(r[7])
+                                 : "r"(tmem + ((uint32_t)lane_base << 16) + (uint32_t)w * acc_cols + (uint32_t)c0));
+                    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+                    for (int i = 0; i < 8; i++) v[i] = w ? v[i] + __uint_as_float(r[i]) : __uint_as_float(r[i]);
+                }
                 if (row < p.g.n_rows) {
 #pragma unroll
                     for (int i = 0; i < 8; i++) {
                         const int t = tok0 + c0 + i;
-                        if (t < p.t_rows) p.y[(size_t)t * p.ldy + row] = __uint_as_float(r[i]) * p.inv_scale[t];
+                        if (t < p.t_rows) p.y[(size_t)t * p.ldy + row] = v[i] * p.inv_scale[t];
                     }
                 }
             }
