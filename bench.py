@@ -7,8 +7,11 @@ batch 1 (``--batch 16`` for the batch-16 variant), seeded synthetic weights
 with the configuration's distributions and N(0,1) activations.  One step =
 one decode token through all 224 matmuls (one launch each, in layer order,
 replayed from a CUDA graph).  With N GPUs every matrix is row-sharded N ways
-and each output is all-gathered over NCCL after its matmul (strong scaling:
-the model is fixed, value counts its bytes once).
+and each output is all-gathered by the matmul itself: its kernel stores the
+rows, as {value, epoch} words, into every other GPU's receive buffer over
+NVLink; the step ends with each GPU unpacking the seven outputs (waiting
+for every word of the step's last epochs) -- strong scaling: the model is
+fixed, value counts its bytes once.
 
 value  = weight bytes of the whole model x steps / device time (max over ranks)
 e2e    = the same through the host C-ABI call (rce_qmm_mm_1d with host buffers,
@@ -205,7 +208,7 @@ def config_dict(args, world):
 PREFILL_N, PREFILL_K, PREFILL_MS = D_FF, D_MODEL, (1, 16, 128, 512)
 
 
-def prefill_section(args, rank, world, dev, stream, ctx):
+def prefill_section(args, rank, world, dev, stream, ctx, pg=None):
     import torch
     import torch.distributed as dist
 
@@ -226,13 +229,16 @@ def prefill_section(args, rank, world, dev, stream, ctx):
         g.manual_seed(2)
         x = torch.randn((m, PREFILL_K), device=dev, generator=g)
         y = torch.empty((m, ns), device=dev)
-        yall = torch.empty((world * m, ns), device=dev) if world > 1 else None
+        if world > 1:
+            pg.output(f"prefill{m}", m, PREFILL_N)
 
         def one():
             for w in ws:
-                R.mm_batched_device(x, w, y, stream=stream)
                 if world > 1:
-                    dist.all_gather_into_tensor(yall, y)
+                    pg.mm(x, w, f"prefill{m}", rank * ns, stream=stream)
+                    pg.gather(f"prefill{m}", stream=stream)
+                else:
+                    R.mm_batched_device(x, w, y, stream=stream)
 
         with torch.cuda.stream(stream):
             for _ in range(3):
@@ -422,6 +428,11 @@ def main():
         dist.init_process_group("nccl", init_method="env://", timeout=datetime.timedelta(seconds=120),
                                 device_id=dev)
     ctx, layers = build_stack(args, rank, world, dev)
+    pg = None
+    if world > 1:
+        from rce_b200.shard import PeerGroup, torch_exchange
+
+        pg = PeerGroup(ctx, world, rank, torch_exchange())
     m = args.batch
     gen = torch.Generator(device=dev)
     gen.manual_seed(3)
@@ -429,25 +440,36 @@ def main():
           D_FF: torch.randn((m, D_FF), device=dev, generator=gen)}
     ys = {name: torch.empty((m, n // world), device=dev) for name, n, _ in LAYER}
     yfull = {name: torch.empty((world * m, n // world), device=dev) for name, n, _ in LAYER} if world > 1 else {}
+    if world > 1:
+        for name, n, _ in LAYER:
+            pg.output(name, m, n)
     stream = torch.cuda.Stream(dev)
-    launches_per_step = 7 * args.layers
+    launches_per_step = 7 * args.layers + (8 if world > 1 else 0)
 
     def step():
+        if world > 1:
+            pg.begin_step(7 * args.layers, stream=stream)
         for mats in layers:
             for name, ns, k, w in mats:
-                R.mm_batched_device(xs[k], w, ys[name], stream=stream)
                 if world > 1:
-                    dist.all_gather_into_tensor(yfull[name], ys[name])
+                    pg.mm(xs[k], w, name, rank * ns, stream=stream)
+                else:
+                    R.mm_batched_device(xs[k], w, ys[name], stream=stream)
+        if world > 1:
+            for name, _, _ in LAYER:
+                pg.gather(name, stream=stream)
 
     graph = None
     with torch.cuda.stream(stream):
         for _ in range(2):
             step()  # eager warm-up: allocates split-K scratch for this stream
     stream.synchronize()
-    if world == 1:
-        graph = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(graph, stream=stream):
-            step()
+    if world > 1:
+        dist.barrier()
+    # the whole step (at N > 1 with its gathers and the final wait) as one CUDA graph
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=stream):
+        step()
 
     def run(n):
         with torch.cuda.stream(stream):
@@ -495,9 +517,16 @@ def main():
             clocks.stop()
         if rank == 0:
             print(json.dumps({"profile_run": True, "ms_per_step": ms / args.steps, "value": value}))
+        del graph
+        torch.cuda.synchronize(dev)
         if world > 1:
+            dist.barrier()
+            pg.close()
+            dist.barrier()
             dist.destroy_process_group()
         return
+    del graph
+    torch.cuda.synchronize(dev)
 
     # ---- roofline: per kernel type, the 32 layers' launches back to back in a
     # CUDA graph, timed with CUDA events on the launching stream ----------------
@@ -541,7 +570,9 @@ def main():
         except Exception:
             traffic = None
 
-    prefill = prefill_section(args, rank, world, dev, stream, ctx)
+    if pg is not None:
+        pg.end_step()  # absolute epochs for the eager legs below
+    prefill = prefill_section(args, rank, world, dev, stream, ctx, pg)
     moe = moe_section(args, rank, world, dev, stream, ctx)
 
     # ---- e2e through the host C-ABI ----------------------------------------------
@@ -622,6 +653,9 @@ def main():
         }
         print(json.dumps(line), flush=True)
     if world > 1:
+        torch.cuda.synchronize(dev)
+        dist.barrier()
+        pg.close()
         dist.barrier()
         dist.destroy_process_group()
 

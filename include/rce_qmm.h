@@ -163,6 +163,52 @@ int rce_qmm_device_error(rce_qmm_ctx *ctx, int *code, int clear);
 /* Wait for all work this thread queued on the context's streams. */
 int rce_qmm_synchronize(rce_qmm_ctx *ctx);
 
+/* ---- row sharding over GPUs, all-gather fused over peer memory ------------ */
+
+/* The reference splits a matmul's rows over the threads of one host (rayon
+ * in mm_1d_q4_0 / mm_1d_q8_0 / mm_1d_q4_k, rce-op-qmm/src/lib.rs:502, 654,
+ * 742: rows are independent, so the split changes no result).  Its
+ * multi-GPU counterpart here shards rows over the GPUs of one node and
+ * gathers the outputs with NVLink stores from the matmul itself.  These
+ * entry points have no counterpart in the reference.
+ *
+ * Device memory that the other processes of the node can map: `bytes`
+ * zeroed bytes at *d_ptr, and its 64-byte CUDA IPC handle in ipc_handle. */
+int rce_qmm_peer_alloc(rce_qmm_ctx *ctx, size_t bytes, void **d_ptr, void *ipc_handle);
+int rce_qmm_peer_free(rce_qmm_ctx *ctx, void *d_ptr);
+/* Map another process's rce_qmm_peer_alloc buffer (its 64-byte handle). */
+int rce_qmm_peer_open(rce_qmm_ctx *ctx, const void *ipc_handle, void **d_ptr);
+int rce_qmm_peer_close(rce_qmm_ctx *ctx, void *d_ptr);
+
+/* mm_batched for rank `rank` of `world` (2..8) holding rows [row_offset,
+ * row_offset + w.n_rows) of a row-sharded weight.  The rows' outputs go to
+ * this rank's full output d_y ([t_rows][ldy], at row_offset) and, as 8-byte
+ * words {value, epoch} written over NVLink, into every other rank's
+ * receive buffer d_ll[r] (t_rows x ldy words, as addressable in this
+ * context; rce_qmm_peer_alloc memory) at the same place.  No fence, flag or
+ * collective: a receiver knows a word has arrived when it carries the
+ * epoch it expects (rce_qmm_peer_unpack).  Use a new epoch for every call
+ * that writes a given receive buffer (epochs only grow; 0 is never valid). */
+int rce_qmm_mm_batched_device_gather(rce_qmm_ctx *ctx, const float *d_a, size_t lda, size_t t_rows,
+                                     const rce_qmm_weight *w, int world, int rank, int64_t row_offset,
+                                     float *d_y, size_t ldy, unsigned long long *const *d_ll, unsigned epoch,
+                                     const unsigned *d_epoch_base, void *stream);
+/* Complete a gathered output on this rank: wait (bounded, 1 s; an expired
+ * wait sets the device error word) until every word of d_ll in rows
+ * [0, t_rows) and columns [0, n) outside this rank's [own0, own1) carries
+ * `epoch` or a later one, and copy those values into d_y.  (A later epoch
+ * means a later call already overwrote that word: keep peers from running
+ * ahead into a buffer that is still being unpacked when its values matter,
+ * e.g. with alternating buffers.) */
+int rce_qmm_peer_unpack(rce_qmm_ctx *ctx, const unsigned long long *d_ll, float *d_y, size_t ldy, size_t t_rows,
+                        int64_t n, int64_t own0, int64_t own1, unsigned epoch, const unsigned *d_epoch_base,
+                        void *stream);
+/* d_epoch_base (optional, device memory): when given, the epochs of the two
+ * calls above are relative to *d_epoch_base, read on the device, so that
+ * calls captured in a CUDA graph use new epochs on every replay; advance it
+ * (on the stream, before the replayed calls) with: */
+int rce_qmm_peer_epoch_advance(rce_qmm_ctx *ctx, unsigned *d_epoch_base, unsigned delta, void *stream);
+
 /* ---- expert-grouped MoE FFN ---------------------------------------------- */
 
 /* moe_router (rce-op-moe/src/lib.rs:35-73) on given router logits, on the

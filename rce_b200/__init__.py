@@ -18,5 +18,6 @@ from .qmm import (  # noqa: F401
     mm_batched_device,
 )
 from .moe import RouterDecision, decisions, moe_ffn_device, moe_route_device, split_experts  # noqa: F401
+from .shard import PeerGroup, row_shards, torch_exchange  # noqa: F401
 
 __version__ = "0.1.0"

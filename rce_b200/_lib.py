@@ -56,6 +56,14 @@ SIGNATURES = {
     "rce_qmm_dequant_row": (_int, [_vp, _vp, _i64, _f32p, _sz]),
     "rce_qmm_dequant_device": (_int, [_vp, _vp, _i64, _i64, _vp, _sz, _vp]),
     "rce_qmm_device_error": (_int, [_vp, _c.POINTER(_int), _int]),
+    "rce_qmm_peer_alloc": (_int, [_vp, _sz, _c.POINTER(_vp), _vp]),
+    "rce_qmm_peer_free": (_int, [_vp, _vp]),
+    "rce_qmm_peer_open": (_int, [_vp, _vp, _c.POINTER(_vp)]),
+    "rce_qmm_peer_close": (_int, [_vp, _vp]),
+    "rce_qmm_mm_batched_device_gather": (_int, [_vp, _vp, _sz, _sz, _vp, _int, _int, _i64, _vp, _sz, _vp, _c.c_uint,
+                                                 _vp, _vp]),
+    "rce_qmm_peer_unpack": (_int, [_vp, _vp, _vp, _sz, _sz, _i64, _i64, _i64, _c.c_uint, _vp, _vp]),
+    "rce_qmm_peer_epoch_advance": (_int, [_vp, _vp, _c.c_uint, _vp]),
     "rce_qmm_moe_route_device": (_int, [_vp, _vp, _sz, _sz, _int, _int, _int, _vp, _vp, _vp]),
     "rce_qmm_moe_ffn_device": (_int, [_vp, _vp, _sz, _sz, _vp, _sz, _int, _int, _int, _int, _vp, _vp, _vp, _vp,
                                        _sz, _vp, _vp, _vp]),

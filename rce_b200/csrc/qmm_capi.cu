@@ -556,6 +556,120 @@ int rce_qmm_synchronize(rce_qmm_ctx *ctx) {
     return ok();
 }
 
+int rce_qmm_peer_alloc(rce_qmm_ctx *ctx, size_t bytes, void **d_ptr, void *ipc_handle) {
+    if (!ctx || !d_ptr || !ipc_handle || bytes == 0) return fail(RCE_QMM_ERR_INVALID, "peer_alloc: bad arguments");
+    DeviceGuard dg(ctx->device);
+    void *p = nullptr;
+    CUDA_TRY(cudaMalloc(&p, bytes));
+    cudaError_t e = cudaMemset(p, 0, bytes);
+    cudaIpcMemHandle_t h;
+    if (e == cudaSuccess) e = cudaIpcGetMemHandle(&h, p);
+    if (e != cudaSuccess) {
+        cudaFree(p);
+        return fail(RCE_QMM_ERR_CUDA, "peer_alloc: %s", cudaGetErrorString(e));
+    }
+    memcpy(ipc_handle, &h, sizeof(h));
+    *d_ptr = p;
+    return ok();
+}
+
+int rce_qmm_peer_free(rce_qmm_ctx *ctx, void *d_ptr) {
+    if (!ctx || !d_ptr) return fail(RCE_QMM_ERR_INVALID, "peer_free: null");
+    DeviceGuard dg(ctx->device);
+    CUDA_TRY(cudaFree(d_ptr));
+    return ok();
+}
+
+int rce_qmm_peer_open(rce_qmm_ctx *ctx, const void *ipc_handle, void **d_ptr) {
+    if (!ctx || !ipc_handle || !d_ptr) return fail(RCE_QMM_ERR_INVALID, "peer_open: null");
+    DeviceGuard dg(ctx->device);
+    cudaIpcMemHandle_t h;
+    memcpy(&h, ipc_handle, sizeof(h));
+    CUDA_TRY(cudaIpcOpenMemHandle(d_ptr, h, cudaIpcMemLazyEnablePeerAccess));
+    return ok();
+}
+
+int rce_qmm_peer_close(rce_qmm_ctx *ctx, void *d_ptr) {
+    if (!ctx || !d_ptr) return fail(RCE_QMM_ERR_INVALID, "peer_close: null");
+    DeviceGuard dg(ctx->device);
+    CUDA_TRY(cudaIpcCloseMemHandle(d_ptr));
+    return ok();
+}
+
+int rce_qmm_mm_batched_device_gather(rce_qmm_ctx *ctx, const float *d_a, size_t lda, size_t t_rows,
+                                     const rce_qmm_weight *w, int world, int rank, int64_t row_offset,
+                                     float *d_y, size_t ldy, unsigned long long *const *d_ll, unsigned epoch,
+                                     const unsigned *d_epoch_base, void *stream) {
+    if (!ctx) return fail(RCE_QMM_ERR_INVALID, "mm_batched_device_gather: null ctx");
+    int rc = check_weight(w);
+    if (rc) return rc;
+    if (w->ctx != ctx) return fail(RCE_QMM_ERR_INVALID, "mm_batched_device_gather: weight of another context");
+    if (world < 2 || world > rce::kMaxPeers || rank < 0 || rank >= world)
+        return fail(RCE_QMM_ERR_INVALID, "mm_batched_device_gather: world %d (2..%d), rank %d", world,
+                    rce::kMaxPeers, rank);
+    if (t_rows == 0) return ok();
+    if (!d_a || !d_y || !d_ll || row_offset < 0 || lda < (size_t)w->g.n_cols ||
+        ldy < (size_t)(row_offset + w->g.n_rows))
+        return fail(RCE_QMM_ERR_INVALID, "mm_batched_device_gather: null buffer, lda < k or ldy < row_offset + n");
+    for (int r = 0; r < world; r++)
+        if (r != rank && !d_ll[r]) return fail(RCE_QMM_ERR_INVALID, "mm_batched_device_gather: null d_ll[%d]", r);
+    if (epoch == 0 && !d_epoch_base) return fail(RCE_QMM_ERR_INVALID, "mm_batched_device_gather: epoch 0");
+    DeviceGuard dg(ctx->device);
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    rce::GatherArgs ga;
+    ga.world = world;
+    ga.rank = rank;
+    ga.row_off = row_offset;
+    for (int r = 0; r < world; r++) ga.ll[r] = d_ll[r];
+    ga.epoch = epoch;
+    ga.epoch_base = d_epoch_base;
+    const Geometry &g = w->g;
+    float *y_own = d_y + row_offset;
+    if (ctx->prefill_min_tokens > 0 && t_rows >= (size_t)ctx->prefill_min_tokens && t_rows <= (size_t)INT32_MAX) {
+        rc = run_matmul(ctx, w, d_a, lda, t_rows, y_own, ldy, s);
+        if (rc) return rc;
+        CUDA_TRY(rce::launch_gather_push(ga, d_y, (int)t_rows, g.n_rows, ldy, s));
+        return ok();
+    }
+    for (size_t t0 = 0; t0 < t_rows;) {
+        const size_t left = t_rows - t0;
+        const int m = (int)(left < (size_t)rce::kGemvMaxTokens ? left : (size_t)rce::kGemvMaxTokens);
+        rce::GemvPlan plan = rce::plan_gemv(w->dtype, g, m, ctx->sm_count);
+        RceScratch *sc = nullptr;
+        if (plan.scratch_floats > 0) {
+            rc = stream_scratch(ctx, s, plan.scratch_floats, (size_t)plan.counters, &sc);
+            if (rc) return rc;
+        }
+        rce::GatherArgs gp = ga;
+        for (int r = 0; r < world; r++) gp.ll[r] = d_ll[r] ? d_ll[r] + t0 * ldy : nullptr;
+        CUDA_TRY(rce::launch_gemv(w->dtype, w->dev, g, d_a + t0 * lda, lda, y_own + t0 * ldy, ldy, m, plan,
+                                  sc ? sc->partial : nullptr, sc ? sc->counters : nullptr, ctx->err_dev, s, &gp));
+        t0 += (size_t)m;
+    }
+    return ok();
+}
+
+int rce_qmm_peer_unpack(rce_qmm_ctx *ctx, const unsigned long long *d_ll, float *d_y, size_t ldy, size_t t_rows,
+                        int64_t n, int64_t own0, int64_t own1, unsigned epoch, const unsigned *d_epoch_base,
+                        void *stream) {
+    if (!ctx) return fail(RCE_QMM_ERR_INVALID, "peer_unpack: null ctx");
+    if (t_rows == 0) return ok();
+    if (!d_ll || !d_y || n <= 0 || (size_t)n > ldy || own0 < 0 || own0 > own1 || own1 > n || t_rows > (size_t)INT32_MAX)
+        return fail(RCE_QMM_ERR_INVALID, "peer_unpack: bad buffers or ranges");
+    if (epoch == 0 && !d_epoch_base) return fail(RCE_QMM_ERR_INVALID, "peer_unpack: epoch 0");
+    DeviceGuard dg(ctx->device);
+    CUDA_TRY(rce::launch_gather_unpack(d_ll, d_y, (int)t_rows, n, ldy, own0, own1, epoch, d_epoch_base, ctx->err_dev,
+                                       static_cast<cudaStream_t>(stream)));
+    return ok();
+}
+
+int rce_qmm_peer_epoch_advance(rce_qmm_ctx *ctx, unsigned *d_epoch_base, unsigned delta, void *stream) {
+    if (!ctx || !d_epoch_base) return fail(RCE_QMM_ERR_INVALID, "peer_epoch_advance: null");
+    DeviceGuard dg(ctx->device);
+    CUDA_TRY(rce::launch_epoch_advance(d_epoch_base, delta, static_cast<cudaStream_t>(stream)));
+    return ok();
+}
+
 int rce_qmm_moe_route_device(rce_qmm_ctx *ctx, const float *d_logits, size_t ld_logits, size_t t_rows,
                              int n_experts, int top_k, int normalize, int32_t *d_idx, float *d_w, void *stream) {
     if (!ctx) return fail(RCE_QMM_ERR_INVALID, "moe_route_device: null ctx");

@@ -44,6 +44,7 @@
 
 #include <atomic>
 
+#include "qmm_gather.cuh"
 #include "qmm_internal.h"
 
 namespace rce {
@@ -63,6 +64,7 @@ struct GemvArgs {
     size_t ldx, ldy;
     int m, cps, k_splits, n_pad;
     int stages, red_mode, x_vec4;
+    GatherArgs ga;  // fused all-gather over peer memory (ga.world > 1)
 };
 
 // ---- PTX helpers ---------------------------------------------------------------
@@ -150,6 +152,13 @@ __device__ __forceinline__ uint32_t comp(const uint4 &v, int i) {
 
 __device__ __forceinline__ float h2f(uint32_t bits16) {
     return __half2float(__ushort_as_half((unsigned short)(bits16 & 0xFFFF)));
+}
+
+// One output value: to y, and with the fused all-gather also to every other
+// rank's receive buffer (at this rank's rows of the full output).
+__device__ __forceinline__ void put_y(const GemvArgs &p, int t, int64_t row, float v, unsigned epoch) {
+    p.y[t * p.ldy + row] = v;
+    if (p.ga.world > 1) gather_send(p.ga, (size_t)t * p.ldy + (size_t)p.ga.row_off + (size_t)row, v, epoch);
 }
 
 template <int DT>
@@ -404,6 +413,7 @@ __global__ void __launch_bounds__(256, 2) gemv_kernel(GemvArgs p) {
     }
     // The activations may be the previous kernel's output: wait for it.
     asm volatile("griddepcontrol.wait;" ::: "memory");
+    const unsigned gepoch = p.ga.world > 1 ? gather_epoch(p.ga) : 0u;
     // The CTA's activation slice comes in through ordinary coalesced loads
     // (the load/store path), not the TMA queue, which is busy with the weight
     // prefetch; each thread tracks the maximum of what it loaded.
@@ -595,7 +605,7 @@ __global__ void __launch_bounds__(256, 2) gemv_kernel(GemvArgs p) {
             part[idx] = v;
         } else if (t < m && row < p.g.n_rows) {
             if (p.k_splits == 1)
-                p.y[t * p.ldy + row] = v;
+                put_y(p, t, row, v, gepoch);
             else
                 p.partial[((size_t)blockIdx.y * m + t) * p.n_pad + row] = v;
         }
@@ -611,7 +621,7 @@ __global__ void __launch_bounds__(256, 2) gemv_kernel(GemvArgs p) {
                 if (t < m && row < p.g.n_rows) {
                     float v = 0.f;
                     for (int q = 0; q < p.k_splits; q++) v += ld_cluster(part + idx, (uint32_t)q);
-                    p.y[t * p.ldy + row] = v;
+                    put_y(p, t, row, v, gepoch);
                 }
             }
         }
@@ -643,7 +653,7 @@ __global__ void __launch_bounds__(256, 2) gemv_kernel(GemvArgs p) {
                         v += a3;
                     }
                     for (; ks < p.k_splits; ks++) v += __ldcg(src + (size_t)ks * stride);
-                    p.y[t * p.ldy + row] = v;
+                    put_y(p, t, row, v, gepoch);
                 }
             }
             if (tid == 0) p.counters[blockIdx.x] = 0u;
@@ -783,8 +793,9 @@ GemvPlan plan_gemv_scratch(int dt, const Geometry &g, int m, int sm_count) {
 
 cudaError_t launch_gemv(int dt, const uint8_t *tiles, const Geometry &g, const float *x, size_t ldx,
                         float *y, size_t ldy, int m, const GemvPlan &plan, float *scratch,
-                        unsigned *counters, int *err, cudaStream_t s) {
+                        unsigned *counters, int *err, cudaStream_t s, const GatherArgs *ga) {
     if (m <= 0 || g.n_rows <= 0) return cudaSuccess;
+    if (ga && ga->world > kMaxPeers) return cudaErrorInvalidValue;
     if (m > plan.nt || m > kGemvMaxTokens) return cudaErrorInvalidValue;
     if (plan.red_mode == kRedScratch && (!scratch || !counters)) return cudaErrorInvalidValue;
     GemvArgs a;
@@ -804,6 +815,7 @@ cudaError_t launch_gemv(int dt, const uint8_t *tiles, const Geometry &g, const f
     a.stages = plan.stages;
     a.red_mode = plan.red_mode;
     a.x_vec4 = ((ldx & 3) == 0 && (reinterpret_cast<uintptr_t>(x) & 15) == 0) ? 1 : 0;
+    if (ga) a.ga = *ga;
     dim3 grid((g.n_tiles + plan.rt - 1) / plan.rt, plan.k_splits);
     switch (dt) {
     case GGUF_Q4_K: return launch_rt<GGUF_Q4_K>(plan.rt, plan.nt, a, grid, plan.smem, s);

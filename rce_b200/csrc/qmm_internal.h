@@ -20,6 +20,21 @@ cudaError_t launch_unpack(int dt, const uint8_t *tiles, uint8_t *gguf, const Geo
 cudaError_t launch_dequant(int dt, const uint8_t *tiles, float *out, size_t ldo, const Geometry &g,
                            int64_t row0, int64_t row1, cudaStream_t s);
 
+// Fused all-gather of a row-sharded output over peer memory (see
+// qmm_gather.cuh): rank `rank` of `world` computes rows [row_off, row_off +
+// n) of the output, stores them in its own y, and stores each value with
+// the call's epoch, as one 8-byte word, into every other rank's receive
+// buffer ll[r] (t rows x ldy words, as addressable here) at the same place.
+// The epoch is `epoch` (+ *epoch_base when set, read on the device).
+constexpr int kMaxPeers = 8;
+struct GatherArgs {
+    int world = 1, rank = 0;
+    int64_t row_off = 0;
+    unsigned long long *ll[kMaxPeers] = {};
+    unsigned epoch = 0;
+    const unsigned *epoch_base = nullptr;
+};
+
 // Decode GEMV / small-M matmul: y[t][row] = sum_k x[t][k] W[row][k], for
 // t < m <= kGemvMaxTokens, rows [0, n_rows).  Uses split-K scratch when the
 // plan asks for it.  `err` (device-visible int) receives a non-zero code if a
@@ -43,7 +58,19 @@ GemvPlan plan_gemv(int dt, const Geometry &g, int m, int sm_count);
 GemvPlan plan_gemv_scratch(int dt, const Geometry &g, int m, int sm_count);
 cudaError_t launch_gemv(int dt, const uint8_t *tiles, const Geometry &g, const float *x, size_t ldx,
                         float *y, size_t ldy, int m, const GemvPlan &plan, float *scratch,
-                        unsigned *counters, int *err, cudaStream_t s);
+                        unsigned *counters, int *err, cudaStream_t s, const GatherArgs *ga = nullptr);
+// Gather helpers.  push: for kernels that write only locally (the prefill
+// GEMM), store rows [0, t_rows) x [row_off, row_off + n) of y (leading
+// dimension ldy) into the peers' receive buffers.  unpack: wait (bounded)
+// until this rank's receive buffer `ll` holds epoch e (+ *epoch_base) in
+// every word of the rows other ranks own -- rows [0, t_rows), columns
+// [0, n) except [own0, own1) -- and copy those values into y.
+cudaError_t launch_gather_push(const GatherArgs &ga, const float *y, int t_rows, int64_t n, size_t ldy,
+                               cudaStream_t s);
+cudaError_t launch_gather_unpack(const unsigned long long *ll, float *y, int t_rows, int64_t n, size_t ldy,
+                                 int64_t own0, int64_t own1, unsigned epoch, const unsigned *epoch_base, int *err,
+                                 cudaStream_t s);
+cudaError_t launch_epoch_advance(unsigned *epoch_base, unsigned delta, cudaStream_t s);
 
 // Prefill matmul on tcgen05 (fp16 operands, f32 accumulation in tensor
 // memory) for t_rows tokens at once.  `workspace` holds

@@ -1,0 +1,181 @@
+"""Row sharding of the quantized matmul over the GPUs of one node, with the
+output all-gather fused into the matmul (NVLink stores of {value, epoch}
+words into peer-mapped receive buffers; librce_qmm.so's
+rce_qmm_mm_batched_device_gather and rce_qmm_peer_unpack).
+
+Rows of a GGUF weight are independent -- the reference splits them over host
+threads with rayon (rce-op-qmm/src/lib.rs:502, 654, 742) -- so a row shard
+per GPU gives, row for row, the single-GPU result.  One process per GPU;
+torch.distributed (any backend) only exchanges the buffers' IPC handles.
+"""
+from __future__ import annotations
+
+import ctypes
+from typing import Dict, List, Optional, Tuple
+
+from ._lib import check, lib
+from .qmm import Context, QuantWeight, _check_weight, _stream_handle
+
+TILE_ROWS = 16  # shards start on a 16-row tile of the device layout
+
+
+def row_shards(n_rows: int, world: int) -> List[Tuple[int, int]]:
+    """[row0, row1) of each rank: whole 16-row tiles, as even as possible,
+    rank order, covering [0, n_rows)."""
+    if world < 1:
+        raise ValueError("world must be >= 1")
+    tiles = (n_rows + TILE_ROWS - 1) // TILE_ROWS
+    out = []
+    for r in range(world):
+        t0 = tiles * r // world
+        t1 = tiles * (r + 1) // world
+        out.append((min(n_rows, t0 * TILE_ROWS), min(n_rows, t1 * TILE_ROWS)))
+    return out
+
+
+class PeerGroup:
+    """The buffers one rank shares with the others for gathered outputs: per
+    output name, this rank's full output (a torch tensor) and a receive
+    buffer of 8-byte {value, epoch} words that the other ranks write over
+    NVLink.  `exchange` is a callable (obj -> list of every rank's obj, in
+    rank order), e.g. torch_exchange()."""
+
+    def __init__(self, ctx: Context, world: int, rank: int, exchange):
+        if not 2 <= world <= 8:
+            raise ValueError("world must be 2..8")
+        self.ctx, self.world, self.rank, self._exchange = ctx, world, rank, exchange
+        self.epoch = 0
+        self._own: List[int] = []          # own allocations (device pointers)
+        self._opened: List[int] = []       # peers' allocations mapped here
+        self.outputs: Dict[str, list] = {}  # name -> [y, ll array, t_rows, n_rows, own0, own1]
+        # step mode: epochs relative to a device counter that begin_step
+        # advances, so calls captured in a CUDA graph use fresh epochs on
+        # every replay
+        self._base = None
+        self._rel = None
+
+    def _shared(self, nbytes: int) -> List[int]:
+        ptr = ctypes.c_void_p()
+        handle = ctypes.create_string_buffer(64)
+        check(lib().rce_qmm_peer_alloc(self.ctx.handle, nbytes, ctypes.byref(ptr), handle))
+        self._own.append(ptr.value)
+        handles = self._exchange(handle.raw)
+        ptrs = []
+        for r, h in enumerate(handles):
+            if r == self.rank:
+                ptrs.append(ptr.value)
+                continue
+            p = ctypes.c_void_p()
+            check(lib().rce_qmm_peer_open(self.ctx.handle, ctypes.create_string_buffer(h, 64), ctypes.byref(p)))
+            self._opened.append(p.value)
+            ptrs.append(p.value)
+        return ptrs
+
+    def output(self, name: str, t_rows: int, n_rows: int):
+        """Create the gathered output `name` ([t_rows, n_rows] f32; collective:
+        every rank creates the same names in the same order)."""
+        import torch
+
+        if name not in self.outputs:
+            ll = self._shared(8 * t_rows * n_rows)
+            y = torch.zeros((t_rows, n_rows), dtype=torch.float32, device=f"cuda:{self.ctx.device}")
+            self.outputs[name] = [y, (ctypes.c_void_p * self.world)(*ll), t_rows, n_rows, 0, 0]
+        return self.outputs[name][0]
+
+    def view(self, name: str):
+        """This rank's full output `name` (complete after gather(name))."""
+        return self.outputs[name][0]
+
+    def _next_epoch(self):
+        if self._rel is not None:
+            self._rel += 1
+            return self._rel, ctypes.c_void_p(self._base.data_ptr())
+        self.epoch = (self.epoch + 1) & 0xFFFFFFFF or 1
+        return self.epoch, None
+
+    def mm(self, x, w: QuantWeight, name: str, row_offset: int, stream=None) -> int:
+        """x [T, K] (CUDA f32) times this rank's row shard w (rows
+        [row_offset, row_offset + w.n_rows) of the full weight): this rank's
+        rows of output `name`, sent to every rank.  Returns the epoch to
+        pass to gather()."""
+        _check_weight(w)
+        o = self.outputs[name]
+        y, arr, t_rows, n_rows = o[0], o[1], o[2], o[3]
+        if x.shape[0] > t_rows or x.shape[1] != w.n_cols or row_offset + w.n_rows > n_rows:
+            raise ValueError("shape mismatch with the gathered output")
+        o[4], o[5] = row_offset, row_offset + w.n_rows
+        epoch, base = self._next_epoch()
+        check(lib().rce_qmm_mm_batched_device_gather(
+            self.ctx.handle, ctypes.c_void_p(x.data_ptr()), x.stride(0), x.shape[0], w.handle, self.world, self.rank,
+            int(row_offset), ctypes.c_void_p(y.data_ptr()), n_rows, arr, epoch, base, _stream_handle(stream, x.device)))
+        if len(o) == 6:
+            o.append(epoch)
+        else:
+            o[6] = epoch
+        return epoch
+
+    def gather(self, name: str, epoch: Optional[int] = None, t_rows: Optional[int] = None, stream=None):
+        """Complete output `name` on this rank: wait (on `stream`, bounded)
+        for the other ranks' rows of the call with `epoch` (default: the
+        latest mm into `name`) and copy them in.  Returns the tensor."""
+        o = self.outputs[name]
+        y, arr, n_rows, own0, own1 = o[0], o[1], o[3], o[4], o[5]
+        epoch = o[6] if epoch is None else epoch
+        base = ctypes.c_void_p(self._base.data_ptr()) if self._rel is not None else None
+        rows = o[2] if t_rows is None else t_rows
+        check(lib().rce_qmm_peer_unpack(self.ctx.handle, ctypes.c_void_p(arr[self.rank]), ctypes.c_void_p(y.data_ptr()),
+                                        n_rows, rows, n_rows, int(own0), int(own1), int(epoch), base,
+                                        _stream_handle(stream, y.device)))
+        return y
+
+    def begin_step(self, calls: int, stream=None) -> None:
+        """Start a step of at most `calls` mm calls whose epochs are relative
+        to a device counter advanced here by `calls` -- capture begin_step,
+        the calls and the gathers in one CUDA graph and every replay uses
+        new epochs.  Every rank must use the same `calls` and call sequence."""
+        import torch
+
+        if self._base is None:
+            self._base = torch.zeros(1, dtype=torch.int32, device=f"cuda:{self.ctx.device}")
+        self._rel = 0
+        check(lib().rce_qmm_peer_epoch_advance(self.ctx.handle, ctypes.c_void_p(self._base.data_ptr()), int(calls),
+                                               _stream_handle(stream, self._base.device)))
+
+    def end_step(self) -> None:
+        """Leave step mode: later calls use absolute epochs again."""
+        self._rel = None
+
+    def close(self) -> None:
+        for p in self._opened:
+            lib().rce_qmm_peer_close(self.ctx.handle, ctypes.c_void_p(p))
+        for p in self._own:
+            lib().rce_qmm_peer_free(self.ctx.handle, ctypes.c_void_p(p))
+        self._opened, self._own, self.outputs = [], [], {}
+
+
+def _wrap_device(ptr: int, shape, device: int):
+    """A torch view of device memory owned elsewhere (kept alive by the
+    PeerGroup)."""
+    import torch
+
+    class _Mem:
+        def __init__(self, p, n):
+            self.__cuda_array_interface__ = {"shape": (n,), "typestr": "<f4", "data": (p, False), "version": 3}
+
+    n = 1
+    for d in shape:
+        n *= d
+    with torch.cuda.device(device):
+        return torch.as_tensor(_Mem(ptr, n), device=f"cuda:{device}").view(*shape)
+
+
+def torch_exchange(group=None):
+    """An `exchange` for PeerGroup over torch.distributed."""
+    import torch.distributed as dist
+
+    def ex(obj):
+        out = [None] * dist.get_world_size(group)
+        dist.all_gather_object(out, obj, group=group)
+        return out
+
+    return ex

@@ -1,0 +1,109 @@
+"""The row-sharded matmul with its all-gather fused over peer memory
+(rce_qmm_mm_batched_device_gather + rce_qmm_peer_unpack), on two GPUs: one
+process per GPU, gloo only to exchange the peer buffers' IPC handles.  Every
+rank's gathered output must equal, bit for bit, the concatenation of each
+shard's own matmul (same shapes, same kernels); a second matmul reading the
+first's gathered output, the tensor-core GEMM route (20 tokens, shard pushed
+to the peers after the GEMM), and a second round through the same buffers
+(new epochs), likewise.  Skipped with fewer than two GPUs."""
+import os
+import socket
+
+import numpy as np
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+
+def _free_port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    p = s.getsockname()[1]
+    s.close()
+    return p
+
+
+def _rank_main(rank, world, port, q):
+    import torch
+    import torch.distributed as dist
+
+    import oracle as O
+    import rce_b200 as R
+    from rce_b200 import synth
+    from rce_b200.shard import PeerGroup, row_shards, torch_exchange
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    res = {}
+    pg = None
+    try:
+        torch.cuda.set_device(rank)
+        ctx = R.Context(rank)
+        dt = O.GGUF_Q4_K
+        n1, n2, k = 1024, 512, 2048
+        w1 = synth.weights(dt, n1, k, np.random.default_rng(1))
+        w2 = synth.weights(dt, n2, n1, np.random.default_rng(2))
+
+        def shards(wb, n, kk):
+            rb = kk // 256 * 144
+            return [(r0, R.QuantWeight.from_owned_bytes(wb[r0 * rb:r1 * rb], dt, r1 - r0, kk, ctx=ctx))
+                    for r0, r1 in row_shards(n, world)]
+
+        s1, s2 = shards(w1, n1, k), shards(w2, n2, n1)
+        pg = PeerGroup(ctx, world, rank, torch_exchange())
+        for t_rows, tag in ((3, "gemv"), (20, "gemm")):
+            pg.output(f"y1{tag}", t_rows, n1)
+            pg.output(f"y2{tag}", t_rows, n2)
+            ok = []
+            for rnd in range(2):  # the second round reuses the buffers with new epochs
+                x = torch.from_numpy(synth.activations(t_rows, k, np.random.default_rng(3 + t_rows + rnd))).cuda()
+                pg.mm(x, s1[rank][1], f"y1{tag}", s1[rank][0])
+                y1 = pg.gather(f"y1{tag}")
+                pg.mm(y1, s2[rank][1], f"y2{tag}", s2[rank][0])
+                y2 = pg.gather(f"y2{tag}")
+                torch.cuda.synchronize()
+                got1, got2 = y1.cpu().numpy(), y2.cpu().numpy()
+                want1 = torch.cat([R.mm_batched_device(x, w) for _, w in s1], dim=1)
+                want2 = torch.cat([R.mm_batched_device(want1, w) for _, w in s2], dim=1)
+                torch.cuda.synchronize()
+                ok.append(bool(np.array_equal(got1, want1.cpu().numpy())) and
+                          bool(np.array_equal(got2, want2.cpu().numpy())))
+                dist.barrier()  # a peer may not overwrite y2's words before this rank has read them
+            res[tag] = tuple(ok)
+        res["device_error"] = ctx.device_error()
+        dist.barrier()
+    except Exception as e:  # reported to the parent, never a hang
+        res["error"] = repr(e)
+    finally:
+        if pg is not None:
+            try:
+                dist.barrier()
+            except Exception:
+                pass
+            pg.close()
+        dist.destroy_process_group()
+    q.put((rank, res))
+
+
+def test_fused_gather_two_gpus():
+    import multiprocessing as mp
+
+    import torch
+
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_rank_main, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = dict(q.get(timeout=300) for _ in procs)
+    for p in procs:
+        p.join(timeout=60)
+    for r in range(2):
+        assert "error" not in res[r], res[r]
+        assert res[r]["gemv"] == (True, True), res
+        assert res[r]["gemm"] == (True, True), res
+        assert res[r]["device_error"] == 0
