@@ -135,13 +135,11 @@ int rce_qmm_mm_batched_device(rce_qmm_ctx *ctx, const float *d_a, size_t lda, si
 /* As rce_qmm_mm_batched_device, for callers that cannot allocate device
  * memory (a custom allocator owning the device, a serving loop that forbids
  * cudaMalloc after start-up).  No counterpart in the reference: its CPU path
- * never allocates device memory.  The split-K scratch comes from a fixed
- * 1 MiB array inside the library (held by every GPU that loads it) instead of
- * a per-stream allocation; this call performs no cudaMalloc/cudaFree.
- * Shapes whose split needs more than that array are rejected with
- * RCE_QMM_ERR_UNSUPPORTED.  All calls on a device share the array: calls whose
- * work overlaps on the GPU race on it.  The first call on a device looks up
- * the array's address, so make it before any stream capture. */
+ * never allocates device memory.  Every batch runs through the decode GEMV
+ * (passes of up to 4 tokens), which needs no device workspace: this call
+ * performs no cudaMalloc/cudaFree and may be captured in a CUDA graph.  A
+ * weight too large for the GEMV's shared-memory plan is rejected with
+ * RCE_QMM_ERR_UNSUPPORTED. */
 int rce_qmm_mm_batched_device_noalloc(rce_qmm_ctx *ctx, const float *d_a, size_t lda, size_t t_rows,
                                       const rce_qmm_weight *w, float *d_out, size_t ldo, void *stream);
 

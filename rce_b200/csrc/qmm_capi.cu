@@ -93,36 +93,6 @@ int grow_pinned(RceThreadState *ts, size_t bytes) {
     return ok();
 }
 
-// Scratch for split-K partial sums when a split is too wide for one cluster,
-// one buffer per stream (work on one stream is ordered, so its kernels never
-// share scratch concurrently).  Growing it
-// synchronises the stream, so the first call with the largest shape must
-// come before any CUDA-graph capture on that stream.
-int stream_scratch(rce_qmm_ctx *ctx, cudaStream_t s, size_t floats, size_t counters, RceScratch **out) {
-    std::lock_guard<std::mutex> lk(ctx->mu);
-    RceScratch &sc = ctx->scratch[s];
-    if (sc.floats < floats) {
-        CUDA_TRY(cudaStreamSynchronize(s));
-        if (sc.partial) cudaFree(sc.partial);
-        sc.partial = nullptr;
-        sc.floats = 0;
-        CUDA_TRY(cudaMalloc(&sc.partial, floats * sizeof(float)));
-        sc.floats = floats;
-    }
-    if (sc.ncounters < counters) {
-        CUDA_TRY(cudaStreamSynchronize(s));
-        if (sc.counters) cudaFree(sc.counters);
-        sc.counters = nullptr;
-        sc.ncounters = 0;
-        const size_t n = counters < 1024 ? 1024 : counters;
-        CUDA_TRY(cudaMalloc(&sc.counters, n * sizeof(unsigned)));
-        CUDA_TRY(cudaMemsetAsync(sc.counters, 0, n * sizeof(unsigned), s));
-        sc.ncounters = n;
-    }
-    *out = &sc;
-    return ok();
-}
-
 // After the caller's stream has been synchronised: turn a kernel-reported
 // error (a bounded wait that expired) into a status, and re-arm the word.
 int take_kernel_error(rce_qmm_ctx *ctx) {
@@ -169,14 +139,9 @@ int run_matmul(rce_qmm_ctx *ctx, const rce_qmm_weight *w, const float *d_x, size
     while (t0 < t_rows) {
         const size_t left = t_rows - t0;
         const int m = (int)(left < (size_t)rce::kGemvMaxTokens ? left : (size_t)rce::kGemvMaxTokens);
-        rce::GemvPlan plan = rce::plan_gemv(w->dtype, g, m, ctx->sm_count);
-        RceScratch *sc = nullptr;
-        if (plan.scratch_floats > 0) {
-            int rc = stream_scratch(ctx, s, plan.scratch_floats, (size_t)plan.counters, &sc);
-            if (rc) return rc;
-        }
-        CUDA_TRY(rce::launch_gemv(w->dtype, w->dev, g, d_x + t0 * lda, lda, d_y + t0 * ldo, ldo, m, plan,
-                                  sc ? sc->partial : nullptr, sc ? sc->counters : nullptr, ctx->err_dev, s));
+        const rce::GemvPlan plan = rce::plan_gemv(w->dtype, g, m, ctx->sm_count);
+        CUDA_TRY(rce::launch_gemv(w->dtype, w->dev, g, d_x + t0 * lda, lda, d_y + t0 * ldo, ldo, m, plan, ctx->err_dev,
+                                  s));
         t0 += (size_t)m;
     }
     return ok();
@@ -321,8 +286,6 @@ int rce_qmm_ctx_destroy(rce_qmm_ctx *ctx) {
         if (ts.stream) cudaStreamDestroy(ts.stream);
     }
     for (auto &kv : ctx->scratch) {
-        if (kv.second.partial) cudaFree(kv.second.partial);
-        if (kv.second.counters) cudaFree(kv.second.counters);
         if (kv.second.gemm_ws) cudaFree(kv.second.gemm_ws);
         if (kv.second.moe_ws) cudaFree(kv.second.moe_ws);
         if (kv.second.moe_host) cudaFreeHost(kv.second.moe_host);
@@ -634,16 +597,11 @@ int rce_qmm_mm_batched_device_gather(rce_qmm_ctx *ctx, const float *d_a, size_t 
     for (size_t t0 = 0; t0 < t_rows;) {
         const size_t left = t_rows - t0;
         const int m = (int)(left < (size_t)rce::kGemvMaxTokens ? left : (size_t)rce::kGemvMaxTokens);
-        rce::GemvPlan plan = rce::plan_gemv(w->dtype, g, m, ctx->sm_count);
-        RceScratch *sc = nullptr;
-        if (plan.scratch_floats > 0) {
-            rc = stream_scratch(ctx, s, plan.scratch_floats, (size_t)plan.counters, &sc);
-            if (rc) return rc;
-        }
+        const rce::GemvPlan plan = rce::plan_gemv(w->dtype, g, m, ctx->sm_count);
         rce::GatherArgs gp = ga;
         for (int r = 0; r < world; r++) gp.ll[r] = d_ll[r] ? d_ll[r] + t0 * ldy : nullptr;
-        CUDA_TRY(rce::launch_gemv(w->dtype, w->dev, g, d_a + t0 * lda, lda, y_own + t0 * ldy, ldy, m, plan,
-                                  sc ? sc->partial : nullptr, sc ? sc->counters : nullptr, ctx->err_dev, s, &gp));
+        CUDA_TRY(rce::launch_gemv(w->dtype, w->dev, g, d_a + t0 * lda, lda, y_own + t0 * ldy, ldy, m, plan, ctx->err_dev,
+                                  s, &gp));
         t0 += (size_t)m;
     }
     return ok();

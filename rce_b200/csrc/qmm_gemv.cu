@@ -5,39 +5,39 @@
 // up to f32 summation order.
 //
 // Design (HBM-bound; every weight byte is read once):
-//  * Each warp owns one 16-row tile and a strided subset of its 256-column
-//    chunks.  Its lane 0 streams the chunks into a private shared-memory ring
+//  * Work split: clusters of two CTAs (one CTA of 16 warps per SM).  Cluster
+//    c owns a block of whole 16-row tiles, so no sum leaves the cluster; the
+//    block's units (tile x 256-column chunk) are cut into 32 equal runs of
+//    consecutive units, one per warp, so every warp of the grid streams the
+//    same number of chunks (see "Work split" below).
+//  * Each warp's lane 0 streams its chunks into a private shared-memory ring
 //    with TMA bulk copies (cp.async.bulk + mbarrier complete_tx), S chunks
-//    ahead, so ~70 KB per CTA are in flight from the first instruction on.
-//    Every wait on an mbarrier is bounded (%globaltimer); on expiry the
-//    kernel records an error word, waits (bounded) for its own copies and
-//    finishes.
+//    ahead.  Every wait on an mbarrier is bounded (%globaltimer); on expiry
+//    the kernel records an error word, waits (bounded) for its own copies
+//    and finishes.
 //  * The dot products are exact integer arithmetic on the tensor cores
 //    (mma.sync m16n8k32, u8/s8 x s8 -> s32).  The weight codes are the A
 //    operand as they are stored: Q8_0's int8 bytes need no unpacking at all,
-//    Q4_K/Q4_0 nibbles one and/shift per 4 codes.  Activations become a
-//    fixed-point integer per token, X = x * 2^e rounded to 31 bits with the
-//    power of two chosen from the CTA's slice of x, whose four balanced
-//    base-256 digits are simply the bytes of (X + 0x80808080) ^ 0x80808080;
-//    the B operand is block-diagonal so that lane g's columns hold digits of
-//    its own column group (tile A digits 0-1, tile B digits 2-3).  Each digit
-//    pair's 32-value sub-block sum is exact in s32; the two pairs meet in f32
-//    and the block scales (d, d*sc, dmin*m) are applied once per sub-block,
-//    so no weight is rounded and x keeps 2^-30 of its slice maximum (below
-//    f32's own rounding of the reference's sums).
+//    Q4_K/Q4_0 nibbles one mask per 4 codes.  Activations become a
+//    fixed-point integer per token and chunk, X = x * 2^e rounded to 31 bits
+//    with the power of two chosen from the chunk's maximum, whose four
+//    balanced base-256 digits are simply the bytes of (X + 0x80808080) ^
+//    0x80808080; the B operand is block-diagonal so that lane g's columns
+//    hold digits of its own column group.  Sub-block sums are exact in s32;
+//    Q4_K keeps them integer through the whole super-block (sc and m are
+//    integers) and meets d and dmin once per chunk in f64; sums across
+//    chunks run in f64 and are rounded to f32 once per segment, so x keeps
+//    2^-30 of its chunk maximum and the weights are never rounded.
 //  * Q4_K's min term and Q4_0's -8 offset use per-sub-block sums of the
-//    integer activations (the "asum hoist"): one op per sub-block.
-//  * The activation table (the B fragments) is built per window of chunks
-//    with vectorised loads while the first weight copies are in flight.
+//    integer activations (one product per sub-block).
+//  * The activation table (the B fragments) covers the CTA's window of
+//    chunks; its loads are issued before most of the weight prefetch.
 //  * Launched with programmatic stream serialization: a kernel's CTAs start
-//    while the previous kernel on the stream drains, issue their weight
-//    copies (which depend on nothing), and only then wait for the previous
-//    grid (griddepcontrol.wait) before touching the activations or writing
-//    outputs.  Each CTA signals its dependents once its main loop is done.
-//  * The grid puts 1-8 tiles in a CTA so that all CTAs are resident in one
-//    wave; K is split across CTAs only when the rows alone cannot occupy the
-//    SMs.  Split partial sums go to scratch and the last CTA to arrive for a
-//    row block adds them in split order (deterministic).
+//    while the previous kernel on the stream drains, issue their first
+//    weight copies (which depend on nothing), and only then wait for the
+//    previous grid (griddepcontrol.wait) before touching the activations or
+//    writing outputs.  Each CTA signals its dependents once its main loop is
+//    done.
 // The plan depends on the weight's shape only, never on the batch, so each
 // token's result is bit-identical whatever the batch size.
 #include <cuda_fp16.h>
@@ -57,14 +57,14 @@ struct GemvArgs {
     const uint8_t *w;
     const float *x;
     float *y;
-    float *partial;
-    unsigned *counters;
     int *err;
     Geometry g;
     size_t ldx, ldy;
-    int m, cps, k_splits, n_pad;
-    int stages, red_mode, x_vec4;
-    GatherArgs ga;  // fused all-gather over peer memory (ga.world > 1)
+    int m, stages, pre, x_vec4;
+    int n_clusters;  // clusters of kClusterCtas CTAs; cluster c owns a block of whole tiles
+    int panels;      // 1 or 2 (the work split)
+    int win, kmax;   // shared-memory maxima: table chunks, slots per warp
+    GatherArgs ga;   // fused all-gather over peer memory (ga.world > 1)
 };
 
 // ---- PTX helpers ---------------------------------------------------------------
@@ -87,10 +87,6 @@ __device__ __forceinline__ void fence_mbar_init() {
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
 }
 
-__device__ __forceinline__ void fence_proxy_async() {
-    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-}
-
 // Expect `bytes` of transactions on `bar` and copy `bytes` from global `src`
 // into shared `dst`; the copy's completion completes the transactions.
 __device__ __forceinline__ void bulk_load(uint32_t dst, const void *src, uint32_t bytes, uint32_t bar) {
@@ -98,6 +94,18 @@ __device__ __forceinline__ void bulk_load(uint32_t dst, const void *src, uint32_
     asm volatile(
         "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst),
         "l"(src), "r"(bytes), "r"(bar)
+        : "memory");
+}
+
+// bulk_load preceded by fence_proxy_async, by the lanes with `pred` only
+// (predicated, not a branch).
+__device__ __forceinline__ void bulk_refill(bool pred, uint32_t dst, const void *src, uint32_t bytes, uint32_t bar) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tsetp.ne.u32 p, %4, 0;\n\t"
+        "@p fence.proxy.async.shared::cta;\n\t"
+        "@p mbarrier.arrive.expect_tx.shared::cta.b64 _, [%3], %2;\n\t"
+        "@p cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];\n\t}" ::"r"(dst),
+        "l"(src), "r"(bytes), "r"(bar), "r"((uint32_t)pred)
         : "memory");
 }
 
@@ -129,21 +137,32 @@ __device__ __forceinline__ uint32_t prmt(uint32_t a, uint32_t b, uint32_t sel) {
     return r;
 }
 
-// D(s32) += A(16x32, u8 or s8) x B(32x8, s8), exact.
-template <bool A_SIGNED>
+// D(s32) += A(16x32, u8 or s8) x B(32x8, s8), exact; ZERO: D = A x B.
+template <bool A_SIGNED, bool ZERO = false>
 __device__ __forceinline__ void imma16832(int (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
-    if (A_SIGNED)
-        asm volatile(
-            "mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
-            "{%0,%1,%2,%3};"
-            : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
-            : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
-    else
-        asm volatile(
-            "mma.sync.aligned.m16n8k32.row.col.s32.u8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
-            "{%0,%1,%2,%3};"
-            : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
-            : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+    if (ZERO) {
+        if (A_SIGNED)
+            asm("mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+                "{%10,%10,%10,%10};"
+                : "=r"(d[0]), "=r"(d[1]), "=r"(d[2]), "=r"(d[3])
+                : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1), "r"(0));
+        else
+            asm("mma.sync.aligned.m16n8k32.row.col.s32.u8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+                "{%10,%10,%10,%10};"
+                : "=r"(d[0]), "=r"(d[1]), "=r"(d[2]), "=r"(d[3])
+                : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1), "r"(0));
+    } else {
+        if (A_SIGNED)
+            asm("mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+                "{%0,%1,%2,%3};"
+                : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
+                : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+        else
+            asm("mma.sync.aligned.m16n8k32.row.col.s32.u8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+                "{%0,%1,%2,%3};"
+                : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
+                : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+    }
 }
 
 __device__ __forceinline__ uint32_t comp(const uint4 &v, int i) {
@@ -174,13 +193,21 @@ struct ChunkRegs {
 
 // One chunk's lane data from its shared-memory ring slot (conflict-free:
 // lanes read consecutive 16-byte pieces).
+// Q4_K: h0/h1 = {d | dmin << 16, the two header words holding lane group
+// g's 24 bits of (sc, m) fields} of rows r and r + 8; `hw` is the byte
+// offset of the first of those words within a row's 16-byte header
+// (4 + 4 * (3g / 4)).  For g = 3 the second word lies past the row's header
+// (the next row's, or the bytes after the chunk) and is never used.
 template <int DT>
-__device__ __forceinline__ void load_chunk(ChunkRegs<DT> &c, const uint8_t *slot, int lane) {
+__device__ __forceinline__ void load_chunk(ChunkRegs<DT> &c, const uint8_t *slot, int lane, int hw) {
 #pragma unroll
     for (int i = 0; i < Fmt<DT>::NQ; i++) c.q[i] = *reinterpret_cast<const uint4 *>(slot + (i * 32 + lane) * 16);
     if (DT == GGUF_Q4_K) {
-        c.h0 = *reinterpret_cast<const uint4 *>(slot + 2048 + (lane >> 2) * 16);
-        c.h1 = *reinterpret_cast<const uint4 *>(slot + 2048 + ((lane >> 2) + 8) * 16);
+        const uint8_t *h0 = slot + 2048 + (lane >> 2) * 16, *h1 = h0 + 8 * 16;
+        c.h0 = make_uint4(*reinterpret_cast<const uint32_t *>(h0), *reinterpret_cast<const uint32_t *>(h0 + hw),
+                          *reinterpret_cast<const uint32_t *>(h0 + hw + 4), 0u);
+        c.h1 = make_uint4(*reinterpret_cast<const uint32_t *>(h1), *reinterpret_cast<const uint32_t *>(h1 + hw),
+                          *reinterpret_cast<const uint32_t *>(h1 + hw + 4), 0u);
     } else {
         const uint2 s = *reinterpret_cast<const uint2 *>(slot + quant_bytes(DT) + lane * 8);
         c.h0 = make_uint4(s.x, s.y, 0u, 0u);
@@ -199,11 +226,13 @@ __device__ __forceinline__ void make_a(const ChunkRegs<DT> &c, int s, uint32_t (
         // sub-block 2g, high nibbles sub-block 2g+1
         const uint32_t r0 = comp(c.q[ss >> 1], (2 * ss) & 3), r1 = comp(c.q[ss >> 1], (2 * ss + 1) & 3);
         const uint32_t e0 = comp(c.q[2 + (ss >> 1)], (2 * ss) & 3), e1 = comp(c.q[2 + (ss >> 1)], (2 * ss + 1) & 3);
-        const int sh = 4 * h;
-        a[0] = (r0 >> sh) & 0x0F0F0F0Fu;
-        a[2] = (r1 >> sh) & 0x0F0F0F0Fu;
-        a[1] = (e0 >> sh) & 0x0F0F0F0Fu;
-        a[3] = (e1 >> sh) & 0x0F0F0F0Fu;
+        // (sub-block 2g+1 as 16 * code, unshifted: its sums are divided by 16
+        // after the chain, exactly)
+        const uint32_t mk = h == 0 ? 0x0F0F0F0Fu : 0xF0F0F0F0u;
+        a[0] = r0 & mk;
+        a[2] = r1 & mk;
+        a[1] = e0 & mk;
+        a[3] = e1 & mk;
     } else if (DT == GGUF_Q4_0) {
         // block 2g + h: bytes 0..15; low nibbles are values 0..15, high 16..31
         const int wp = (ss & 1) * 2, sh = 4 * (ss >> 1);
@@ -222,121 +251,130 @@ __device__ __forceinline__ void make_a(const ChunkRegs<DT> &c, int s, uint32_t (
     }
 }
 
-// Q4_K header fields for lane group g: d*sc and dmin*m of sub-blocks 2g, 2g+1.
-__device__ __forceinline__ void q4k_header(const uint4 &hd, int g, float &d1, float &m1, float &d2,
-                                           float &m2) {
-    const float d = h2f(hd.x), dmin = h2f(hd.x >> 16);
-    const uint32_t lo = g < 2 ? hd.y : (g == 2 ? hd.z : hd.w);
-    const uint32_t hi = g < 2 ? hd.z : (g == 2 ? hd.w : 0u);
-    const uint32_t sh = g == 0 ? 0u : (g == 1 ? 24u : (g == 2 ? 16u : 8u));
-    const uint32_t v = __funnelshift_r(lo, hi, sh) & 0xFFFFFFu;
-    d1 = d * (float)(v & 63u);
-    m1 = dmin * (float)((v >> 6) & 63u);
-    d2 = d * (float)((v >> 12) & 63u);
-    m2 = dmin * (float)((v >> 18) & 63u);
+// Q4_K header fields of lane group g (sub-blocks 2g, 2g+1) from the words
+// load_chunk picked: sc[h], m[h] (6-bit integers); `sh` = 24g mod 32.
+__device__ __forceinline__ void q4k_fields(const uint4 &hd, uint32_t sh, int (&sc)[2], int (&mn)[2]) {
+    const uint32_t v = __funnelshift_r(hd.y, hd.z, sh);
+    sc[0] = (int)(v & 63u);
+    mn[0] = (int)((v >> 6) & 63u);
+    sc[1] = (int)((v >> 12) & 63u);
+    mn[1] = (int)((v >> 18) & 63u);
 }
 
 // One chunk: 8 steps, two sub-blocks (units) per lane.  bp[t] points at the
 // lane's B fragments of this chunk for token t (or at the zero block);
-// sint/sflt at the chunk's per-unit integer activation sums.
+// sint at the chunk's per-unit integer activation sums (low and high digit
+// pairs); isc[t] is the chunk's activation scale for token t; `sh` is the
+// lane group's Q4_K field shift.
+//
+// Q4_K: a chunk is one super-block, so the lane's two sub-blocks share d and
+// dmin and the sums stay integers up to the chunk's end: with X the
+// fixed-point activations, Iq = sum_h sc_h * sum q X and Im = sum_h m_h *
+// sum X, each held as two int32 digit-pair halves (|sc * sum q X| < 2^30 per
+// half; two sub-blocks < 2^31), then d * Iq - dmin * Im in f64 (exact up to
+// 2^-53).  Q4_0 / Q8_0 scale every 32-value block by its own f16 d, so their
+// sub-block sums meet the scale one by one (f64).  Sums across chunks run in
+// f64, so cancelling terms keep their bits.
 template <int DT, int NT>
-__device__ __forceinline__ void process_chunk(const ChunkRegs<DT> &c, float (&acc)[NT][2], const uint2 *const (&bp)[NT],
-                                              const int *__restrict__ sint, const float *__restrict__ sflt,
-                                              int s_stride, int lane) {
+__device__ __forceinline__ void process_chunk(const ChunkRegs<DT> &c, double (&acc)[NT][2], const uint2 *const (&bp)[NT],
+                                              const int *__restrict__ sint, int s_stride, const float (&isc)[NT],
+                                              uint32_t sh, int lane) {
     constexpr bool SIGNED = DT == GGUF_Q8_0;
     const int g = lane & 3;
-    float ds[2][2], mn[2][2];
+    int sc[2][2], mn[2][2];  // Q4_K: [row r / r+8][sub-block h]
+    float ds[2][2];          // Q4_0 / Q8_0: [sub-block h][row r / r+8]
     if (DT == GGUF_Q4_K) {
-        q4k_header(c.h0, g, ds[0][0], mn[0][0], ds[1][0], mn[1][0]);
-        q4k_header(c.h1, g, ds[0][1], mn[0][1], ds[1][1], mn[1][1]);
+        q4k_fields(c.h0, sh, sc[0], mn[0]);
+        q4k_fields(c.h1, sh, sc[1], mn[1]);
     } else {
         ds[0][0] = h2f(c.h0.x);
         ds[1][0] = h2f(c.h0.x >> 16);
         ds[0][1] = h2f(c.h0.y);
         ds[1][1] = h2f(c.h0.y >> 16);
     }
+    int iq[NT][2][2], im[NT][2][2];  // Q4_K: [token][row][low / high digit-pair half]
 #pragma unroll
-    for (int h = 0; h < 2; h++) {
-        int da[NT][4], db[NT][4];
+    for (int t = 0; t < NT; t++)
 #pragma unroll
-        for (int t = 0; t < NT; t++)
+        for (int r = 0; r < 2; r++) iq[t][r][0] = iq[t][r][1] = im[t][r][0] = im[t][r][1] = 0;
+    // the MMAs: per sub-block h and token, two chains (digits 0-1, 2-3) of four
+    // steps; with few tokens both sub-blocks' chains are interleaved
+    constexpr int HB = NT <= 2 ? 2 : 1;  // sub-blocks whose chains run together
+    int da[2][NT][4], db[2][NT][4];
 #pragma unroll
-            for (int i = 0; i < 4; i++) da[t][i] = db[t][i] = 0;
+    for (int h0 = 0; h0 < 2; h0 += HB) {
 #pragma unroll
-        for (int ss = 0; ss < 4; ss++) {
-            const int s = 4 * h + ss;
-            uint32_t a[4];
-            make_a<DT>(c, s, a);
+        for (int ss = 0; ss < 4; ss++)
+#pragma unroll
+            for (int hh = 0; hh < HB; hh++) {
+                const int h = h0 + hh, s = 4 * h + ss;
+                uint32_t a[4];
+                make_a<DT>(c, s, a);
+#pragma unroll
+                for (int t = 0; t < NT; t++) {
+                    // xy: tile A (digit 0 in col 2g, digit 1 in col 2g+1); zw: tile B (digits 2, 3)
+                    const uint4 b = *reinterpret_cast<const uint4 *>(bp[t] + s * 16);
+                    if (ss == 0) {
+                        imma16832<SIGNED, true>(da[h][t], a, b.x, b.y);
+                        imma16832<SIGNED, true>(db[h][t], a, b.z, b.w);
+                    } else {
+                        imma16832<SIGNED>(da[h][t], a, b.x, b.y);
+                        imma16832<SIGNED>(db[h][t], a, b.z, b.w);
+                    }
+                }
+            }
+#pragma unroll
+        for (int hh = 0; hh < HB; hh++) {
+            const int h = h0 + hh;
 #pragma unroll
             for (int t = 0; t < NT; t++) {
-                // xy: tile A (digit 0 in col 2g, digit 1 in col 2g+1); zw: tile B (digits 2, 3)
-                const uint4 b = *reinterpret_cast<const uint4 *>(bp[t] + s * 16);
-                imma16832<SIGNED>(da[t], a, b.x, b.y);
-                imma16832<SIGNED>(db[t], a, b.z, b.w);
-            }
-        }
-#pragma unroll
-        for (int t = 0; t < NT; t++) {
-            // digit pairs: lo = d1*2^8 + d0, hi = d3*2^8 + d2 (each exact in s32)
-            int lo0 = da[t][1] * 256 + da[t][0], hi0 = db[t][1] * 256 + db[t][0];  // row r
-            int lo1 = da[t][3] * 256 + da[t][2], hi1 = db[t][3] * 256 + db[t][2];  // row r + 8
-            if (DT == GGUF_Q4_0) {  // sum (n - 8) X = sum n X - 8 sum X, per digit pair
+                // digit pairs: lo = d1*2^8 + d0, hi = d3*2^8 + d2 (each exact in s32)
+                int lo0 = da[h][t][1] * 256 + da[h][t][0], hi0 = db[h][t][1] * 256 + db[h][t][0];  // row r
+                int lo1 = da[h][t][3] * 256 + da[h][t][2], hi1 = db[h][t][3] * 256 + db[h][t][2];  // row r + 8
                 const int2 sx = *reinterpret_cast<const int2 *>(sint + (t * s_stride + 2 * g + h) * 2);
-                lo0 -= 8 * sx.x;
-                lo1 -= 8 * sx.x;
-                hi0 -= 8 * sx.y;
-                hi1 -= 8 * sx.y;
-            }
-            const float v0 = fmaf((float)hi0, 65536.f, (float)lo0);
-            const float v1 = fmaf((float)hi1, 65536.f, (float)lo1);
-            acc[t][0] = fmaf(ds[h][0], v0, acc[t][0]);
-            acc[t][1] = fmaf(ds[h][1], v1, acc[t][1]);
-            if (DT == GGUF_Q4_K) {  // - dmin*m * sum X
-                const float sx = sflt[t * s_stride + 2 * g + h];
-                acc[t][0] = fmaf(-mn[h][0], sx, acc[t][0]);
-                acc[t][1] = fmaf(-mn[h][1], sx, acc[t][1]);
+                if (DT == GGUF_Q4_K) {
+                    if (h == 1) {  // 16 * code (make_a): exact multiples of 16
+                        lo0 >>= 4;
+                        hi0 >>= 4;
+                        lo1 >>= 4;
+                        hi1 >>= 4;
+                    }
+                    iq[t][0][0] += sc[0][h] * lo0;
+                    iq[t][0][1] += sc[0][h] * hi0;
+                    iq[t][1][0] += sc[1][h] * lo1;
+                    iq[t][1][1] += sc[1][h] * hi1;
+                    im[t][0][0] += mn[0][h] * sx.x;
+                    im[t][0][1] += mn[0][h] * sx.y;
+                    im[t][1][0] += mn[1][h] * sx.x;
+                    im[t][1][1] += mn[1][h] * sx.y;
+                } else {
+                    if (DT == GGUF_Q4_0) {  // sum (n - 8) X = sum n X - 8 sum X, per digit pair
+                        lo0 -= 8 * sx.x;
+                        lo1 -= 8 * sx.x;
+                        hi0 -= 8 * sx.y;
+                        hi1 -= 8 * sx.y;
+                    }
+                    // isc[t] (a power of two) turns the chunk's fixed point back into x
+                    const double v0 = fma((double)hi0, 65536.0, (double)lo0);
+                    const double v1 = fma((double)hi1, 65536.0, (double)lo1);
+                    acc[t][0] = fma((double)(ds[h][0] * isc[t]), v0, acc[t][0]);
+                    acc[t][1] = fma((double)(ds[h][1] * isc[t]), v1, acc[t][1]);
+                }
             }
         }
     }
-}
-
-// Shared-memory carve-up, identical on host and device.
-struct SmemLayout {
-    size_t mbar, zero, ring, xs, tbl, ssum, sint, sflt, red, scl, total;
-};
-
-__host__ __device__ inline size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
-
-constexpr int kNumBars = 8 * kMaxStages;  // one weight-ring mbarrier per warp and stage
-
-__host__ __device__ inline SmemLayout smem_layout(int dt, int nt, int stages, int cps) {
-    SmemLayout L;
-    size_t o = 0;
-    L.mbar = o;
-    o += kNumBars * 8;
-    o = align_up(o, 16);
-    L.zero = o;
-    o += 1024;
-    o = align_up(o, 128);
-    L.ring = o;
-    o += (size_t)8 * stages * chunk_bytes(dt);
-    o = align_up(o, 16);
-    L.xs = o;
-    o += (size_t)nt * cps * CHUNK_K * 4;
-    L.tbl = o;
-    o += (size_t)nt * cps * 128 * 8;
-    L.ssum = o;
-    o += (size_t)nt * cps * 32 * 8;
-    L.sint = o;
-    o += (size_t)nt * cps * 8 * 8;
-    L.sflt = o;
-    o += (size_t)nt * cps * 8 * 4;
-    L.red = o;
-    o += (size_t)8 * nt * 16 * 4;
-    L.scl = o;
-    o += (size_t)2 * nt * 4;
-    L.total = align_up(o, 16);
-    return L;
+    if (DT == GGUF_Q4_K) {
+        const float d0 = h2f(c.h0.x), m0 = h2f(c.h0.x >> 16), d1 = h2f(c.h1.x), m1 = h2f(c.h1.x >> 16);
+#pragma unroll
+        for (int t = 0; t < NT; t++) {
+            const double q0 = (double)((long long)iq[t][0][1] * 65536 + iq[t][0][0]);
+            const double q1 = (double)((long long)iq[t][1][1] * 65536 + iq[t][1][0]);
+            const double s0 = (double)((long long)im[t][0][1] * 65536 + im[t][0][0]);
+            const double s1 = (double)((long long)im[t][1][1] * 65536 + im[t][1][0]);
+            acc[t][0] = fma((double)(d0 * isc[t]), q0, fma((double)(-m0 * isc[t]), s0, acc[t][0]));
+            acc[t][1] = fma((double)(d1 * isc[t]), q1, fma((double)(-m1 * isc[t]), s1, acc[t][1]));
+        }
+    }
 }
 
 // Balanced base-256 digits of a fixed-point activation |X| < 2^30: with
@@ -357,142 +395,266 @@ __device__ __forceinline__ void transpose4(uint32_t w0, uint32_t w1, uint32_t w2
 __device__ __forceinline__ void cluster_sync() {
     asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
 }
+// The two halves of a cluster barrier that orders nothing: arrive early,
+// wait where the other CTAs must have started.
+__device__ __forceinline__ void cluster_arrive_relaxed() {
+    asm volatile("barrier.cluster.arrive.relaxed.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void cluster_wait() { asm volatile("barrier.cluster.wait.aligned;" ::: "memory"); }
 
-// A float in the shared memory of cluster CTA `rank`, at the offset of `local`.
-__device__ __forceinline__ float ld_cluster(const float *local, uint32_t rank) {
-    uint32_t remote;
-    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(remote) : "r"(smem_u32(local)), "r"(rank));
-    float v;
-    asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(remote) : "memory");
-    return v;
+// ---- Work split ------------------------------------------------------------------
+//
+// Clusters of two CTAs (the two SMs of a TPC).  Cluster c owns the whole tiles
+// [tile0, tile0 + nt), so no sum leaves the cluster.  Its nt x n_chunks units
+// (one 16-row tile x one 256-column chunk) are ordered in runs -- run r < nt
+// is tile r's chunks [0, pw0), run nt + r (two panels only) tile r's chunks
+// [pw0, n_chunks) -- and cut into 32 equal ranges, one per warp of the
+// cluster.  With two panels (pw0 = ceil(n_chunks / 2); clusters of few
+// tiles) CTA 0 covers about the first half of K of every tile and CTA 1 the
+// second, so each CTA stages the activations of half of K; with one panel
+// (many tiles per cluster) each CTA covers half of the tiles.  A warp adds
+// the units of one run (a segment) in registers.  A segment that is a whole
+// tile goes straight to y; any other goes to slot [warp][k] (k: the
+// segment's place among the warp's) of the CTA that finalises the tile
+// (local tile i -> CTA i % 2), over DSMEM, and after one cluster barrier that
+// CTA adds the tile's segments in chunk order.  The split depends on the
+// weight's shape and the SM count only, never on the batch.
+
+constexpr int kWarps = 16;        // warps per CTA (one CTA per SM)
+constexpr int kClusterCtas = 2;   // CTAs per cluster
+constexpr int kClusterWarps = kWarps * kClusterCtas;
+constexpr int kTwoPanelMaxTiles = 15;  // two panels while clusters hold at most this many tiles
+constexpr int kTableBatch = 2;         // activation-table items a warp loads before the ring's rest
+
+struct Split {
+    int nt, n_chunks, pw0, pw1;  // tiles, chunks, run lengths of panel 0 and panel 1 (0: one panel)
+    uint32_t U;                  // units
+    __host__ __device__ Split(int nt_, int n_chunks_, int panels) {
+        nt = nt_;
+        n_chunks = n_chunks_;
+        pw0 = panels == 2 ? (n_chunks_ + 1) / 2 : n_chunks_;
+        pw1 = n_chunks_ - pw0;
+        U = (uint32_t)nt_ * (uint32_t)n_chunks_;
+    }
+    __host__ __device__ uint32_t warp_u0(uint32_t g) const { return g * U / kClusterWarps; }
+    // the non-empty warp whose range holds unit u
+    __host__ __device__ uint32_t warp_of(uint32_t u) const { return ((u + 1) * kClusterWarps + U - 1) / U - 1; }
+    __host__ __device__ uint32_t run_of(uint32_t u) const {
+        const uint32_t first = (uint32_t)nt * pw0;
+        return u < first ? u / pw0 : nt + (u - first) / pw1;
+    }
+    __host__ __device__ uint32_t run_start(uint32_t r) const {
+        return r < (uint32_t)nt ? r * pw0 : (uint32_t)nt * pw0 + (r - nt) * pw1;
+    }
+    __host__ __device__ uint32_t run_len(uint32_t r) const { return r < (uint32_t)nt ? pw0 : pw1; }
+    __host__ __device__ int run_tile(uint32_t r) const { return r < (uint32_t)nt ? (int)r : (int)(r - nt); }
+    __host__ __device__ int run_chunk0(uint32_t r) const { return r < (uint32_t)nt ? 0 : pw0; }
+    __host__ __device__ int runs_per_tile() const { return pw1 > 0 ? 2 : 1; }
+    // the slot of warp g's segment k (one panel: whole-tile segments have none)
+    __host__ __device__ int slot_of(int k) const { return pw1 > 0 ? k : (k == 0 ? 0 : 1); }
+    // A contiguous cover [lo, lo + n) of the chunks of units [u0, u1).
+    __host__ __device__ void window(uint32_t u0, uint32_t u1, int &lo, int &n) const {
+        if (u1 <= u0) {
+            lo = 0;
+            n = 0;
+            return;
+        }
+        const uint32_t ra = run_of(u0), rb = run_of(u1 - 1);
+        const int ca = run_chunk0(ra) + (int)(u0 - run_start(ra)), cb = run_chunk0(rb) + (int)(u1 - 1 - run_start(rb));
+        const bool pa = ra >= (uint32_t)nt, pb = rb >= (uint32_t)nt;
+        int hi;
+        if (ra == rb) {  // one run
+            lo = ca;
+            hi = cb;
+        } else if (pa == pb) {  // several runs of one panel: the whole panel
+            lo = pa ? pw0 : 0;
+            hi = pa ? n_chunks - 1 : pw0 - 1;
+        } else {  // the tail of panel 0 and the head of panel 1
+            lo = ra == (uint32_t)nt - 1 ? ca : 0;
+            hi = rb == (uint32_t)nt ? cb : n_chunks - 1;
+        }
+        n = hi - lo + 1;
+    }
+};
+
+// The tiles of cluster c: [tile0, tile0 + n).
+__host__ __device__ inline void cluster_tiles(int c, int n_clusters, int n_tiles, int &tile0, int &n) {
+    tile0 = (int)((int64_t)c * n_tiles / n_clusters);
+    n = (int)((int64_t)(c + 1) * n_tiles / n_clusters) - tile0;
 }
 
-// Cross-CTA reduction of split-K partial sums.
-enum : int { kRedNone = 0, kRedCluster = 1, kRedScratch = 2 };
+// Walks consecutive units without division (one division to start).
+struct UnitIter {
+    uint32_t run, left;  // current run, units left in it
+    int tile, chunk;
+    __host__ __device__ __forceinline__ void init(uint32_t u, const Split &sp) {
+        run = sp.run_of(u);
+        const uint32_t off = u - sp.run_start(run);
+        left = sp.run_len(run) - off;
+        tile = sp.run_tile(run);
+        chunk = sp.run_chunk0(run) + (int)off;
+    }
+    __host__ __device__ __forceinline__ void next(const Split &sp) {
+        chunk++;
+        if (--left == 0) {
+            run++;
+            left = sp.run_len(run);
+            tile = sp.run_tile(run);
+            chunk = sp.run_chunk0(run);
+        }
+    }
+};
 
-template <int DT, int NT, int RT>
-__global__ void __launch_bounds__(256, 2) gemv_kernel(GemvArgs p) {
-    constexpr int KQ = 8 / RT;
+// Shared memory of one CTA.  Identical in the two CTAs of a cluster (slots
+// are addressed remotely at the local offset), so it is sized from the
+// plan's maxima, not from the CTA's own window.
+struct SmemLayout {
+    size_t mbar, zero, ring, tbl, sint, inv, slot, total;
+};
+
+__host__ __device__ inline size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
+
+__host__ __device__ inline SmemLayout smem_layout(int dt, int nt, int stages, int win, int kmax) {
+    SmemLayout L;
+    size_t o = 0;
+    L.mbar = o;
+    o += (size_t)kWarps * kMaxStages * 8;
+    o = align_up(o, 16);
+    L.zero = o;
+    o += 1024;
+    o = align_up(o, 128);
+    L.ring = o;
+    o += (size_t)kWarps * stages * chunk_bytes(dt);
+    o = align_up(o, 16);
+    L.tbl = o;
+    o += (size_t)nt * win * 128 * 8;
+    L.sint = o;
+    o += (size_t)nt * win * 8 * 8;
+    L.inv = o;
+    o += (size_t)nt * win * 4;
+    o = align_up(o, 16);
+    L.slot = o;
+    o += (size_t)kClusterWarps * kmax * nt * 16 * 4;
+    L.total = align_up(o, 16);
+    return L;
+}
+
+__device__ __forceinline__ uint32_t cluster_rank() {
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+    return r;
+}
+__device__ __forceinline__ uint32_t map_shared(const void *local, uint32_t rank) {
+    uint32_t remote;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(remote) : "r"(smem_u32(local)), "r"(rank));
+    return remote;
+}
+__device__ __forceinline__ void st_cluster_f32(uint32_t addr, float v) {
+    asm volatile("st.shared::cluster.f32 [%0], %1;" ::"r"(addr), "f"(v) : "memory");
+}
+
+// Decode GEMV over clusters of two CTAs (the work split above).  Each warp
+// streams its units' chunks through a private TMA ring.  A token's result is
+// the same sum in the same order whatever the batch.
+template <int DT, int NT>
+__global__ void __launch_bounds__(kWarps * 32, 1) gemv_kernel(GemvArgs p) {
     constexpr int CB = chunk_bytes(DT);
     constexpr int FIXED_BITS = 30;  // |x * scale| < 2^30: four balanced int8 digits
     extern __shared__ __align__(128) uint8_t smem[];
-    const int m = p.m, S = p.stages, cps = p.cps;
-    const SmemLayout L = smem_layout(DT, NT, S, cps);
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    // The peer CTA's shared memory is written only after the wait below.
+    cluster_arrive_relaxed();
+    const int m = p.m, S = p.stages, C = p.g.n_chunks;
+    const int rank = (int)cluster_rank();
+    const int cl = blockIdx.x / kClusterCtas;
+    int T0 = 0, NTc = 0;
+    cluster_tiles(cl, p.n_clusters, p.g.n_tiles, T0, NTc);
+    const Split sp(NTc, C, p.panels);
+    int wlo = 0, nwin = 0;
+    sp.window(sp.warp_u0(rank * kWarps), sp.warp_u0((rank + 1) * kWarps), wlo, nwin);
+    const SmemLayout L = smem_layout(DT, NT, S, p.win, p.kmax);
     uint64_t *mbar = reinterpret_cast<uint64_t *>(smem + L.mbar);
     const uint2 *zero = reinterpret_cast<const uint2 *>(smem + L.zero);
     uint8_t *ring = smem + L.ring;
-    float *xs = reinterpret_cast<float *>(smem + L.xs);     // [NT][cps * 256] this CTA's slice of x
-    uint2 *tbl = reinterpret_cast<uint2 *>(smem + L.tbl);   // [NT][cps][8 steps][4 groups][2 parts][2 tiles]
-    int2 *ssum = reinterpret_cast<int2 *>(smem + L.ssum);   // [NT][cps][4 groups][8 steps] (lo, hi pair sums)
-    int *sint = reinterpret_cast<int *>(smem + L.sint);     // [NT][cps][8 units][2]
-    float *sflt = reinterpret_cast<float *>(smem + L.sflt); // [NT][cps][8 units]
-    float *red = reinterpret_cast<float *>(smem + L.red);   // [8 warps][NT][16]
-    float *scl = reinterpret_cast<float *>(smem + L.scl);   // [NT] scale, [NT] inverse
-    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    uint2 *tbl = reinterpret_cast<uint2 *>(smem + L.tbl);    // [NT][nwin][8 steps][4 groups][2 parts][2 tiles]
+    int *sint = reinterpret_cast<int *>(smem + L.sint);      // [NT][nwin][8 units][2]
+    float *inv = reinterpret_cast<float *>(smem + L.inv);    // [NT][nwin]
+    float *slot = reinterpret_cast<float *>(smem + L.slot);  // [32 warps][kmax][NT][16]
 
-    const int c0 = blockIdx.y * cps;
-    const int nc = min(cps, p.g.n_chunks - c0);
-    const int rt_local = warp % RT, kq = warp / RT;
-    const int tile = blockIdx.x * RT + rt_local;
-    const bool tile_ok = tile < p.g.n_tiles;
-    // chunks of this warp: kq, kq + KQ, ... (< nc)
-    const int nw = (tile_ok && kq < nc) ? (nc - kq + KQ - 1) / KQ : 0;
-    const uint8_t *gsrc = p.w + ((size_t)(tile_ok ? tile : 0) * p.g.n_chunks + c0) * CB;
+    // this warp's units
+    const uint32_t gw = (uint32_t)(rank * kWarps + warp);
+    const uint32_t u0 = sp.warp_u0(gw), u1 = sp.warp_u0(gw + 1);
+    const int nu = (int)(u1 - u0);
     const uint32_t mb0 = smem_u32(mbar + warp * kMaxStages);
     const uint32_t ring0 = smem_u32(ring + (size_t)warp * S * CB);
-    const int64_t k_lo = (int64_t)c0 * CHUNK_K;
-    const int64_t k_hi = min((int64_t)(c0 + nc) * CHUNK_K, p.g.n_cols);
-    const int xn = (int)(k_hi - k_lo);  // activations of this slice (a multiple of 32)
+    UnitIter issue;  // the next unit to copy into the ring
+    if (nu > 0) issue.init(u0, sp);
+    auto src_next = [&]() {
+        const uint8_t *src = p.w + ((size_t)(T0 + issue.tile) * C + issue.chunk) * CB;
+        issue.next(sp);
+        return src;
+    };
 
-    // The weight copies depend on nothing: start them before anything else.
+    // The weight copies depend on nothing: start p.pre of them before waiting
+    // for the previous kernel (more would queue ahead of the activation loads).
+    const int first = min(S, nu), pre = min(p.pre, first);
     if (lane == 0) {
         for (int s = 0; s < S; s++) mbar_init(mb0 + 8 * s, 1);
         fence_mbar_init();
-        for (int i = 0; i < min(S, nw); i++)
-            bulk_load(ring0 + i * CB, gsrc + (size_t)(kq + i * KQ) * CB, CB, mb0 + 8 * i);
+        for (int i = 0; i < pre; i++) bulk_load(ring0 + i * CB, src_next(), CB, mb0 + 8 * i);
     }
+    if (tid < 256) reinterpret_cast<uint32_t *>(smem + L.zero)[tid] = 0u;  // 1 KB
     // The activations may be the previous kernel's output: wait for it.
     asm volatile("griddepcontrol.wait;" ::: "memory");
     const unsigned gepoch = p.ga.world > 1 ? gather_epoch(p.ga) : 0u;
-    // The CTA's activation slice comes in through ordinary coalesced loads
-    // (the load/store path), not the TMA queue, which is busy with the weight
-    // prefetch; each thread tracks the maximum of what it loaded.
-    reinterpret_cast<uint32_t *>(smem + L.zero)[tid] = 0u;  // 256 x 4 B
-    float xmax[NT];
+
+    // Activation table: warp item (token t, window chunk j); lane = group gg
+    // (64 columns) x step s (8 columns).  The chunk's power of two comes from
+    // its own maximum, so no other warp is involved.  The first kTableBatch
+    // items' activations are loaded before the rest of the ring is requested,
+    // so that those loads are not queued behind the weight copies.
+    const int gg = lane >> 3, st = lane & 7;
+    auto load_item = [&](int item, float (&v)[8]) {
+        const int t = item / nwin, j = item - t * nwin;
+        const int64_t k = (int64_t)(wlo + j) * CHUNK_K + 64 * gg + 8 * st;
 #pragma unroll
-    for (int t = 0; t < NT; t++) {
+        for (int e = 0; e < 8; e++) v[e] = 0.f;
+        if (t < m && k < p.g.n_cols) {
+            const float *src = p.x + (size_t)t * p.ldx + k;
+            if (p.x_vec4) {
+                const float4 f0 = *reinterpret_cast<const float4 *>(src);
+                const float4 f1 = *reinterpret_cast<const float4 *>(src + 4);
+                v[0] = f0.x; v[1] = f0.y; v[2] = f0.z; v[3] = f0.w;
+                v[4] = f1.x; v[5] = f1.y; v[6] = f1.z; v[7] = f1.w;
+            } else {
+#pragma unroll
+                for (int e = 0; e < 8; e++) v[e] = src[e];
+            }
+        }
+    };
+    auto build_item = [&](int item, const float (&v)[8]) {
+        const int t = item / nwin, j = item - t * nwin;
         float mx = 0.f;
         bool fin = true;
-        float *xd = xs + t * cps * CHUNK_K;
-        if (t >= m) {  // padding tokens are zero
-            for (int k = tid; k < xn; k += 256) xd[k] = 0.f;
-        } else if (p.x_vec4) {
-            const float4 *src = reinterpret_cast<const float4 *>(p.x + t * p.ldx + k_lo);
-            for (int k4 = tid; k4 < xn / 4; k4 += 256) {
-                const float4 v = src[k4];
-                reinterpret_cast<float4 *>(xd)[k4] = v;
-                mx = fmaxf(mx, fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w))));
-                fin = fin && isfinite(v.x) && isfinite(v.y) && isfinite(v.z) && isfinite(v.w);
-            }
-        } else {  // unaligned activations: scalar loads
-            for (int k = tid; k < xn; k += 256) {
-                const float v = p.x[t * p.ldx + k_lo + k];
-                xd[k] = v;
-                mx = fmaxf(mx, fabsf(v));
-                fin = fin && isfinite(v);
-            }
-        }
-        xmax[t] = fin ? mx : INFINITY;
-    }
-    __syncthreads();  // barrier inits visible before anyone waits
-    bool failed = false;
-
-    // Per-token power-of-two scale for this CTA's column slice: x * scale
-    // lies inside +-2^FIXED_BITS.
 #pragma unroll
-    for (int t = 0; t < NT; t++) {
-        float mx = xmax[t];
+        for (int e = 0; e < 8; e++) {
+            mx = fmaxf(mx, fabsf(v[e]));
+            fin = fin && isfinite(v[e]);
+        }
+        if (!fin) mx = INFINITY;
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-        if (lane == 0) red[warp * NT + t] = mx;
-    }
-    __syncthreads();
-    if (tid < NT) {
-        float v = 0.f;
-        for (int w = 0; w < 8; w++) v = fmaxf(v, red[w * NT + tid]);
-        float s = 1.f, inv = 1.f;
-        if (!isfinite(v)) {
-            s = 0.f;  // non-finite activations: the outputs become NaN
-            inv = __int_as_float(0x7fc00000);
-        } else if (v > 0.f) {
+        float sc = 1.f, is = 1.f;
+        if (!isfinite(mx)) {
+            sc = 0.f;  // non-finite activations: the outputs become NaN
+            is = __int_as_float(0x7fc00000);
+        } else if (mx > 0.f) {
             int e;
-            frexpf(v, &e);  // v < 2^e
+            frexpf(mx, &e);  // mx < 2^e
             e = max(-100, min(100, e));
-            s = ldexpf(1.f, FIXED_BITS - e);
-            inv = ldexpf(1.f, e - FIXED_BITS);
+            sc = ldexpf(1.f, FIXED_BITS - e);
+            is = ldexpf(1.f, e - FIXED_BITS);
         }
-        scl[tid] = s;
-        scl[NT + tid] = inv;
-    }
-    __syncthreads();
-
-    // Activation table: per (token, chunk, group gg, step s) the digits of the
-    // 8 values 64 gg + 8 s + 0..7 as B fragments, and their pair sums.
-    for (int idx = tid; idx < NT * nc * 32; idx += 256) {
-        const int t = idx / (nc * 32), rem = idx % (nc * 32);
-        const int c = rem >> 5, q = rem & 31, gg = q >> 3, s = q & 7;
-        const int k = c * CHUNK_K + 64 * gg + 8 * s;
-        float v[8];
-        if (k < xn) {
-            const float4 f0 = *reinterpret_cast<const float4 *>(xs + t * cps * CHUNK_K + k);
-            const float4 f1 = *reinterpret_cast<const float4 *>(xs + t * cps * CHUNK_K + k + 4);
-            v[0] = f0.x; v[1] = f0.y; v[2] = f0.z; v[3] = f0.w;
-            v[4] = f1.x; v[5] = f1.y; v[6] = f1.z; v[7] = f1.w;
-        } else {
-#pragma unroll
-            for (int e = 0; e < 8; e++) v[e] = 0.f;
-        }
-        const float sc = scl[t];
         uint32_t y[8];
         uint32_t slo = 0, shi = 0;
 #pragma unroll
@@ -505,158 +667,169 @@ __global__ void __launch_bounds__(256, 2) gemv_kernel(GemvArgs p) {
         uint32_t a[4], b[4];
         transpose4(y[0], y[1], y[2], y[3], a);
         transpose4(y[4], y[5], y[6], y[7], b);
-        uint4 *dst = reinterpret_cast<uint4 *>(tbl + (size_t)(t * cps + c) * 128 + s * 16 + gg * 4);
+        uint4 *dst = reinterpret_cast<uint4 *>(tbl + (size_t)(t * nwin + j) * 128 + st * 16 + gg * 4);
         // part 0 (col 2g): tile A digit 0, tile B digit 2; part 1 (col 2g+1): digits 1, 3
         dst[0] = make_uint4(a[0], b[0], a[2], b[2]);
         dst[1] = make_uint4(a[1], b[1], a[3], b[3]);
-        ssum[((t * cps + c) * 4 + gg) * 8 + s] = make_int2((int)slo - 8 * 0x8080, (int)shi - 8 * 0x8080);
-    }
-    if (DT != GGUF_Q8_0) {
-        __syncthreads();
-        // unit u = group u/2, steps 4 (u%2) .. +3
-        for (int idx = tid; idx < NT * nc * 8; idx += 256) {
-            const int t = idx / (nc * 8), rem = idx % (nc * 8), c = rem >> 3, u = rem & 7;
-            const int2 *src = ssum + ((t * cps + c) * 4 + (u >> 1)) * 8 + 4 * (u & 1);
-            const int lo = src[0].x + src[1].x + src[2].x + src[3].x;
-            const int hi = src[0].y + src[1].y + src[2].y + src[3].y;
-            sint[((t * cps + c) * 8 + u) * 2] = lo;
-            sint[((t * cps + c) * 8 + u) * 2 + 1] = hi;
-            sflt[(t * cps + c) * 8 + u] = fmaf((float)hi, 65536.f, (float)lo);
+        // per-unit (32 values = steps 4h .. 4h+3 of group gg) integer sums
+        int lo = (int)slo - 8 * 0x8080, hi = (int)shi - 8 * 0x8080;
+        lo += __shfl_xor_sync(0xffffffffu, lo, 1);
+        hi += __shfl_xor_sync(0xffffffffu, hi, 1);
+        lo += __shfl_xor_sync(0xffffffffu, lo, 2);
+        hi += __shfl_xor_sync(0xffffffffu, hi, 2);
+        if ((st & 3) == 0) {
+            const int u = 2 * gg + (st >> 2);
+            sint[((t * nwin + j) * 8 + u) * 2] = lo;
+            sint[((t * nwin + j) * 8 + u) * 2 + 1] = hi;
         }
-    }
-    __syncthreads();
-
-    float acc[NT][2];
+        if (lane == 0) inv[t * nwin + j] = is;
+    };
+    const int n_items = NT * nwin;
+    float xv[kTableBatch][8];
 #pragma unroll
-    for (int t = 0; t < NT; t++) acc[t][0] = acc[t][1] = 0.f;
+    for (int b = 0; b < kTableBatch; b++)
+        if (warp + b * kWarps < n_items) load_item(warp + b * kWarps, xv[b]);
+    // the rest of the ring
+    if (lane == 0)
+        for (int i = pre; i < first; i++) bulk_load(ring0 + i * CB, src_next(), CB, mb0 + 8 * i);
+#pragma unroll
+    for (int b = 0; b < kTableBatch; b++)
+        if (warp + b * kWarps < n_items) build_item(warp + b * kWarps, xv[b]);
+    for (int item = warp + kTableBatch * kWarps; item < n_items; item += kWarps) {
+        float v[8];
+        load_item(item, v);
+        build_item(item, v);
+    }
+    // the table visible to the CTA; the peer CTA started
+    __syncthreads();
+    cluster_wait();
+
     // B fragments: lane (n = lane / 4, k-group lane % 4) reads column n; the
     // block-diagonal operand is non-zero only where n / 2 == k-group.
     const bool bact = (lane >> 3) == (lane & 3);
+    const int hw = 4 + 4 * ((3 * (lane & 3)) >> 2);      // Q4_K header words of this lane's group
+    const uint32_t hsh = (uint32_t)(24 * (lane & 3)) & 31u;
     const int boff = (lane & 3) * 4 + ((lane >> 2) & 1) * 2;
-    int i = 0, slot = 0;
+    int slt = 0, issued = first, failed_at = nu;
     uint32_t phase = 0;
-    while (!failed && i < nw) {
-        const int cl = kq + i * KQ;
-        if (!mbar_wait_bounded(mb0 + 8 * slot, phase)) {
-            failed = true;
+    double acc[NT][2];
+#pragma unroll
+    for (int t = 0; t < NT; t++) acc[t][0] = acc[t][1] = 0.0;
+    UnitIter un;  // the unit being processed
+    if (nu > 0) un.init(u0, sp);
+    int seg_k = 0;                 // segment number within this warp
+    uint32_t seg_u0 = u0;          // first unit of the segment
+    const uint8_t *wclu = p.w + (size_t)T0 * C * CB;  // the cluster's first tile
+    const uint8_t *myring = ring + (size_t)warp * S * CB;
+    for (int i = 0; i < nu; i++) {
+        if (!mbar_wait_bounded(mb0 + 8 * slt, phase)) {
+            failed_at = i;
             break;
         }
+        const int j = un.chunk - wlo;
         ChunkRegs<DT> cur;
-        load_chunk<DT>(cur, ring + ((size_t)warp * S + slot) * CB, lane);
+        load_chunk<DT>(cur, myring + slt * CB, lane, hw);
         __syncwarp();
-        if (lane == 0 && i + S < nw) {
-            fence_proxy_async();  // this slot's reads happen before the copy that refills it
-            bulk_load(ring0 + slot * CB, gsrc + (size_t)(kq + (i + S) * KQ) * CB, CB, mb0 + 8 * slot);
+        if (i + S < nu) {  // refill the slot (lane 0; the branch is warp-uniform)
+            const uint8_t *src = wclu + ((size_t)issue.tile * C + issue.chunk) * CB;
+            issue.next(sp);
+            // this slot's reads happen before the copy that refills it
+            bulk_refill(lane == 0, ring0 + slt * CB, src, CB, mb0 + 8 * slt);
+            issued++;
         }
         const uint2 *bp[NT];
+        float isc[NT];
 #pragma unroll
-        for (int t = 0; t < NT; t++) bp[t] = bact ? tbl + (size_t)(t * cps + cl) * 128 + boff : zero;
-        process_chunk<DT, NT>(cur, acc, bp, sint + cl * 16, sflt + cl * 8, cps * 8, lane);
-        i++;
-        if (++slot == S) {
-            slot = 0;
+        for (int t = 0; t < NT; t++) {
+            bp[t] = bact ? tbl + (size_t)(t * nwin + j) * 128 + boff : zero;
+            isc[t] = inv[t * nwin + j];
+        }
+        process_chunk<DT, NT>(cur, acc, bp, sint + j * 16, nwin * 8, isc, hsh, lane);
+        const int seg_tile = un.tile;
+        const uint32_t seg_run = un.run;
+        un.next(sp);
+        if (i + 1 == nu || un.run != seg_run) {
+            // the segment's row sums: add the four column groups (lanes 4r .. 4r+3)
+            const uint32_t seg_u1 = u0 + i + 1;
+            const bool whole = sp.pw1 == 0 && seg_u0 == sp.run_start(seg_run) && seg_u1 - seg_u0 == sp.run_len(seg_run);
+            const int owner = seg_tile % kClusterCtas;
+            const uint32_t rb = map_shared(slot + ((size_t)gw * p.kmax + sp.slot_of(seg_k)) * NT * 16, (uint32_t)owner);
+#pragma unroll
+            for (int t = 0; t < NT; t++) {
+                double d0 = acc[t][0], d1 = acc[t][1];
+                d0 += __shfl_xor_sync(0xffffffffu, d0, 1);
+                d1 += __shfl_xor_sync(0xffffffffu, d1, 1);
+                d0 += __shfl_xor_sync(0xffffffffu, d0, 2);
+                d1 += __shfl_xor_sync(0xffffffffu, d1, 2);
+                const float v0 = (float)d0, v1 = (float)d1;
+                if ((lane & 3) == 0) {
+                    const int r = lane >> 2;
+                    if (whole) {  // the tile's only segment: straight to y
+                        const int64_t row = (int64_t)(T0 + seg_tile) * 16 + r;
+                        if (t < m && row < p.g.n_rows) put_y(p, t, row, v0, gepoch);
+                        if (t < m && row + 8 < p.g.n_rows) put_y(p, t, row + 8, v1, gepoch);
+                    } else if (sp.slot_of(seg_k) < p.kmax) {
+                        st_cluster_f32(rb + 4 * (t * 16 + r), v0);
+                        st_cluster_f32(rb + 4 * (t * 16 + r + 8), v1);
+                    }
+                }
+                acc[t][0] = acc[t][1] = 0.0;
+            }
+            seg_k++;
+            seg_u0 = seg_u1;
+        }
+        if (++slt == S) {
+            slt = 0;
             phase ^= 1u;
         }
     }
-    if (failed) {
-        // Report, then let this warp's copies in flight land before exiting.
+    if (failed_at < nu) {
+        // Report, then let this warp's copies in flight (numbers failed_at ..
+        // issued - 1; copy n sits in slot n % S, phase n / S) land.
         if (lane == 0) {
             *reinterpret_cast<volatile int *>(p.err) = kKernelErrWaitTimeout;
-            int sl = slot;
-            uint32_t ph = phase;
-            for (int j = i; j < min(nw, i + S); j++) {
-                mbar_wait_bounded(mb0 + 8 * sl, ph);
-                if (++sl == S) {
-                    sl = 0;
-                    ph ^= 1u;
-                }
-            }
+            for (int n = failed_at; n < issued; n++) mbar_wait_bounded(mb0 + 8 * (n % S), (uint32_t)((n / S) & 1));
         }
         __syncwarp();
     }
-
-    // Sum the four column groups of each row (lanes 4r .. 4r+3), then the KQ
-    // warps of each tile in a fixed order, and undo the activation scale.
-    __syncthreads();
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+    // every partial of the cluster in place (the last cluster-wide access)
+    cluster_sync();
+
+    // finalise this CTA's tiles that have more than one segment: the segments
+    // run by run, warp by warp, i.e. in chunk order
+    const int runs = sp.runs_per_tile();
+    for (int tl = rank + kClusterCtas * warp; tl < NTc; tl += kClusterCtas * kWarps) {
+        uint32_t ga[2], gb[2];
+        int ka[2];  // the segment number, within warp ga[h], of its piece of run h
 #pragma unroll
-    for (int t = 0; t < NT; t++) {
-        float v0 = acc[t][0], v1 = acc[t][1];
-        v0 += __shfl_xor_sync(0xffffffffu, v0, 1);
-        v0 += __shfl_xor_sync(0xffffffffu, v0, 2);
-        v1 += __shfl_xor_sync(0xffffffffu, v1, 1);
-        v1 += __shfl_xor_sync(0xffffffffu, v1, 2);
-        if ((lane & 3) == 0) {
-            red[(warp * NT + t) * 16 + (lane >> 2)] = v0;
-            red[(warp * NT + t) * 16 + (lane >> 2) + 8] = v1;
-        }
-    }
-    __syncthreads();
-    // part[rtl][t][r16] = this CTA's partial sums; reuses the front of xs
-    float *part = xs;
-    for (int idx = tid; idx < RT * NT * 16; idx += 256) {
-        const int rtl = idx / (NT * 16), rem = idx % (NT * 16), t = rem >> 4, r16 = rem & 15;
-        float v = 0.f;
-#pragma unroll
-        for (int q = 0; q < KQ; q++) v += red[((rtl + q * RT) * NT + t) * 16 + r16];
-        v *= scl[NT + t];
-        const int64_t row = (int64_t)(blockIdx.x * RT + rtl) * 16 + r16;
-        if (p.red_mode == kRedCluster) {
-            part[idx] = v;
-        } else if (t < m && row < p.g.n_rows) {
-            if (p.k_splits == 1)
-                put_y(p, t, row, v, gepoch);
-            else
-                p.partial[((size_t)blockIdx.y * m + t) * p.n_pad + row] = v;
-        }
-    }
-    if (p.red_mode == kRedCluster) {
-        // The k_splits CTAs of this row block form one cluster (ranks =
-        // blockIdx.y); rank 0 adds their partial sums in rank order.
-        cluster_sync();
-        if (blockIdx.y == 0) {
-            for (int idx = tid; idx < RT * NT * 16; idx += 256) {
-                const int rtl = idx / (NT * 16), rem = idx % (NT * 16), t = rem >> 4, r16 = rem & 15;
-                const int64_t row = (int64_t)(blockIdx.x * RT + rtl) * 16 + r16;
-                if (t < m && row < p.g.n_rows) {
-                    float v = 0.f;
-                    for (int q = 0; q < p.k_splits; q++) v += ld_cluster(part + idx, (uint32_t)q);
-                    put_y(p, t, row, v, gepoch);
-                }
+        for (int h = 0; h < 2; h++) {
+            if (h < runs) {
+                const uint32_t run = (uint32_t)tl + (uint32_t)h * NTc;
+                const uint32_t a = sp.run_start(run);
+                ga[h] = sp.warp_of(a);
+                gb[h] = sp.warp_of(a + sp.run_len(run) - 1);
+                ka[h] = (int)(run - sp.run_of(sp.warp_u0(ga[h])));
             }
         }
-        cluster_sync();  // keep every CTA's shared memory alive until rank 0 has read it
-    } else if (p.red_mode == kRedScratch) {
-        __shared__ int is_last;
-        __threadfence();
-        __syncthreads();
-        if (tid == 0) is_last = atomicAdd(&p.counters[blockIdx.x], 1u) == (unsigned)(p.k_splits - 1);
-        __syncthreads();
-        if (is_last) {
-            __threadfence();
-            for (int idx = tid; idx < RT * m * 16; idx += 256) {
-                const int rtl = idx / (m * 16), rem = idx % (m * 16), t = rem >> 4, r16 = rem & 15;
-                const int64_t row = (int64_t)(blockIdx.x * RT + rtl) * 16 + r16;
-                if (row < p.g.n_rows) {
-                    const float *src = p.partial + (size_t)t * p.n_pad + row;
-                    const size_t stride = (size_t)m * p.n_pad;
-                    float v = 0.f;
-                    int ks = 0;
-                    for (; ks + 4 <= p.k_splits; ks += 4) {  // four loads in flight, summed in split order
-                        const float a0 = __ldcg(src + (size_t)ks * stride);
-                        const float a1 = __ldcg(src + (size_t)(ks + 1) * stride);
-                        const float a2 = __ldcg(src + (size_t)(ks + 2) * stride);
-                        const float a3 = __ldcg(src + (size_t)(ks + 3) * stride);
-                        v += a0;
-                        v += a1;
-                        v += a2;
-                        v += a3;
-                    }
-                    for (; ks < p.k_splits; ks++) v += __ldcg(src + (size_t)ks * stride);
-                    put_y(p, t, row, v, gepoch);
-                }
+        if (runs == 1 && ga[0] == gb[0]) continue;  // one segment: written directly
+        float v[2] = {0.f, 0.f};                  // q = lane, lane + 32 (q = t * 16 + r)
+#pragma unroll
+        for (int h = 0; h < 2; h++)
+            for (uint32_t g = ga[h]; h < runs && g <= gb[h]; g++) {
+                if (sp.warp_u0(g + 1) == sp.warp_u0(g)) continue;  // no units
+                const int sl = sp.slot_of(g == ga[h] ? ka[h] : 0);
+                if (sl >= p.kmax) continue;
+                const float *src = slot + ((size_t)g * p.kmax + sl) * NT * 16;
+#pragma unroll
+                for (int e = 0; e < 2; e++)
+                    if (lane + 32 * e < NT * 16) v[e] += src[lane + 32 * e];
             }
-            if (tid == 0) p.counters[blockIdx.x] = 0u;
+#pragma unroll
+        for (int e = 0; e < 2; e++) {
+            const int q = lane + 32 * e, t = q >> 4, r = q & 15;
+            const int64_t row = (int64_t)(T0 + tl) * 16 + r;
+            if (q < NT * 16 && t < m && row < p.g.n_rows) put_y(p, t, row, v[e], gepoch);
         }
     }
 }
@@ -683,146 +856,139 @@ cudaError_t ensure_smem_optin(Kern kern, std::atomic<unsigned long long> &done) 
     return e;
 }
 
-template <int DT, int NT, int RT>
-cudaError_t launch_one(const GemvArgs &a, dim3 grid, size_t smem, cudaStream_t s) {
+template <int DT, int NT>
+cudaError_t launch_one(const GemvArgs &a, size_t smem, cudaStream_t s) {
     static std::atomic<unsigned long long> done{0};  // one per instantiation
-    auto kern = gemv_kernel<DT, NT, RT>;
+    auto kern = gemv_kernel<DT, NT>;
     cudaError_t e = ensure_smem_optin(kern, done);
     if (e != cudaSuccess) return e;
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = grid;
-    cfg.blockDim = dim3(256, 1, 1);
+    cfg.gridDim = dim3(a.n_clusters * kClusterCtas, 1, 1);
+    cfg.blockDim = dim3(kWarps * 32, 1, 1);
     cfg.dynamicSmemBytes = smem;
     cfg.stream = s;
     cudaLaunchAttribute attr[2];
-    unsigned n = 0;
-    attr[n].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    attr[n].val.programmaticStreamSerializationAllowed = 1;
-    n++;
-    if (a.red_mode == kRedCluster) {
-        attr[n].id = cudaLaunchAttributeClusterDimension;
-        attr[n].val.clusterDim.x = 1;
-        attr[n].val.clusterDim.y = grid.y;
-        attr[n].val.clusterDim.z = 1;
-        n++;
-    }
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    attr[1].id = cudaLaunchAttributeClusterDimension;
+    attr[1].val.clusterDim.x = kClusterCtas;
+    attr[1].val.clusterDim.y = 1;
+    attr[1].val.clusterDim.z = 1;
     cfg.attrs = attr;
-    cfg.numAttrs = n;
+    cfg.numAttrs = 2;
     return cudaLaunchKernelEx(&cfg, kern, a);
 }
 
-template <int DT, int RT>
-cudaError_t launch_nt(int nt, const GemvArgs &a, dim3 grid, size_t smem, cudaStream_t s) {
+template <int DT>
+cudaError_t launch_nt(int nt, const GemvArgs &a, size_t smem, cudaStream_t s) {
     switch (nt) {
-    case 1: return launch_one<DT, 1, RT>(a, grid, smem, s);
-    case 2: return launch_one<DT, 2, RT>(a, grid, smem, s);
-    case 4: return launch_one<DT, 4, RT>(a, grid, smem, s);
+    case 1: return launch_one<DT, 1>(a, smem, s);
+    case 2: return launch_one<DT, 2>(a, smem, s);
+    case 4: return launch_one<DT, 4>(a, smem, s);
     default: return cudaErrorInvalidValue;
     }
 }
 
-template <int DT>
-cudaError_t launch_rt(int rt, int nt, const GemvArgs &a, dim3 grid, size_t smem, cudaStream_t s) {
-    switch (rt) {
-    case 1: return launch_nt<DT, 1>(nt, a, grid, smem, s);
-    case 2: return launch_nt<DT, 2>(nt, a, grid, smem, s);
-    case 4: return launch_nt<DT, 4>(nt, a, grid, smem, s);
-    case 8: return launch_nt<DT, 8>(nt, a, grid, smem, s);
-    default: return cudaErrorInvalidValue;
+constexpr size_t kSmemBudget = 225 * 1024;
+
+}  // namespace
+
+namespace {
+
+// The plan of one work-split choice (panels = 1 or 2).
+GemvPlan plan_split(int dt, const Geometry &g, int m, int nc, int panels) {
+    GemvPlan p;
+    p.clusters = nc;
+    p.panels = panels;
+    const int nt_min = g.n_tiles / nc, nt_max = (g.n_tiles + nc - 1) / nc;
+    // the largest table window of any CTA and the most segments of any warp
+    // (clusters hold nt_min or nt_max tiles)
+    int win = 1, kmax = 2;
+    for (int nt : {nt_min, nt_max}) {
+        const Split sp(nt, g.n_chunks, panels);
+        for (int r = 0; r < kClusterCtas; r++) {
+            int lo = 0, n = 0;
+            sp.window(sp.warp_u0(r * kWarps), sp.warp_u0((r + 1) * kWarps), lo, n);
+            if (n > win) win = n;
+        }
+        if (panels == 2)
+            for (uint32_t w = 0; w < (uint32_t)kClusterWarps; w++) {
+                const uint32_t u0 = sp.warp_u0(w), u1 = sp.warp_u0(w + 1);
+                if (u1 > u0) {
+                    const int k = (int)(sp.run_of(u1 - 1) - sp.run_of(u0)) + 1;
+                    if (k > kmax) kmax = k;
+                }
+            }
     }
+    p.window = win;
+    p.kmax = kmax;
+    // tokens per launch: the batch's slot count, fewer when the activation
+    // table would not fit next to a 2-stage ring
+    p.nt = m <= 1 ? 1 : m <= 2 ? 2 : 4;
+    while (p.nt > 1 && smem_layout(dt, p.nt, 2, win, kmax).total > kSmemBudget) p.nt /= 2;
+    // TMA ring: as deep as the shared memory left over allows (2..4 stages)
+    p.stages = kMaxStages;
+    while (p.stages > 2 && smem_layout(dt, p.nt, p.stages, win, kmax).total > kSmemBudget) p.stages--;
+    p.smem = smem_layout(dt, p.nt, p.stages, win, kmax).total;
+    return p;
 }
 
 }  // namespace
 
 GemvPlan plan_gemv(int dt, const Geometry &g, int m, int sm_count) {
-    GemvPlan p;
-    p.nt = m <= 1 ? 1 : m <= 2 ? 2 : 4;
-    // The activation slice and its table take nt x cps x 2 KB of shared
-    // memory: at most 8 chunks per CTA.  Nothing below depends on m, so a
-    // token's result is the same whatever the batch.
-    const int cps_cap = 8;
-    const int ks_min = (g.n_chunks + cps_cap - 1) / cps_cap;
-    // Tiles per CTA and the K split: the largest tile count (one warp per
-    // tile: the CTA's activation table serves 8 tiles) whose grid still
-    // covers every SM, within one resident wave (two CTAs per SM).
-    int best_rt = 1, best_ks = ks_min, best_ctas = -1;
-    for (int rt = 8; rt >= 1; rt /= 2) {
-        const int kq = 8 / rt;
-        const int rows = (g.n_tiles + rt - 1) / rt;
-        int ks = (2 * sm_count) / rows;
-        if (ks > 8) ks = 8;
-        if (ks > g.n_chunks / kq) ks = g.n_chunks / kq;  // at least one chunk per warp
-        if (ks < ks_min) ks = ks_min;
-        if (ks < 1) ks = 1;
-        const int cps = (g.n_chunks + ks - 1) / ks;
-        ks = (g.n_chunks + cps - 1) / cps;
-        const int ctas = rows * ks;
-        if (ctas > best_ctas) {
-            best_rt = rt;
-            best_ks = ks;
-            best_ctas = ctas;
-        }
-        if (ctas >= sm_count) break;
-    }
-    p.rt = best_rt;
-    p.cps = (g.n_chunks + best_ks - 1) / best_ks;
-    p.k_splits = (g.n_chunks + p.cps - 1) / p.cps;
-    p.red_mode = p.k_splits == 1 ? kRedNone : (p.k_splits <= 8 ? kRedCluster : kRedScratch);
-    // TMA ring depth: as deep as shared memory allows for two CTAs per SM
-    p.stages = kMaxStages;
-    while (p.stages > 2 && smem_layout(dt, p.nt, p.stages, p.cps).total > 110 * 1024) p.stages--;
-    (void)m;
-    p.window = p.cps;
-    p.smem = smem_layout(dt, p.nt, p.stages, p.cps).total;
-    if (p.red_mode == kRedScratch) {
-        p.scratch_floats = (size_t)p.k_splits * m * g.n_tiles * 16;
-        p.counters = (g.n_tiles + p.rt - 1) / p.rt;
-    }
-    return p;
-}
-
-GemvPlan plan_gemv_scratch(int dt, const Geometry &g, int m, int sm_count) {
-    GemvPlan p = plan_gemv(dt, g, m, sm_count);
-    if (p.red_mode == kRedCluster) {
-        p.red_mode = kRedScratch;
-        p.scratch_floats = (size_t)p.k_splits * m * g.n_tiles * 16;
-        p.counters = (g.n_tiles + p.rt - 1) / p.rt;
-    }
+    // one cluster per TPC, never more clusters than tiles
+    int nc = sm_count / kClusterCtas;
+    if (nc > g.n_tiles) nc = g.n_tiles;
+    if (nc < 1) nc = 1;
+    const int nt_max = (g.n_tiles + nc - 1) / nc;
+    const bool two = g.n_chunks >= 2;
+    GemvPlan p = plan_split(dt, g, m, nc, (nt_max <= kTwoPanelMaxTiles && two) ? 2 : 1);
+    // many tiles per cluster and a long K: halve the table with two panels
+    if (p.smem > kSmemBudget && p.panels == 1 && two) p = plan_split(dt, g, m, nc, 2);
     return p;
 }
 
 cudaError_t launch_gemv(int dt, const uint8_t *tiles, const Geometry &g, const float *x, size_t ldx,
-                        float *y, size_t ldy, int m, const GemvPlan &plan, float *scratch,
-                        unsigned *counters, int *err, cudaStream_t s, const GatherArgs *ga) {
+                        float *y, size_t ldy, int m, const GemvPlan &plan, int *err, cudaStream_t s,
+                        const GatherArgs *ga) {
     if (m <= 0 || g.n_rows <= 0) return cudaSuccess;
+    if (m > kGemvMaxTokens || plan.nt < 1) return cudaErrorInvalidValue;
     if (ga && ga->world > kMaxPeers) return cudaErrorInvalidValue;
-    if (m > plan.nt || m > kGemvMaxTokens) return cudaErrorInvalidValue;
-    if (plan.red_mode == kRedScratch && (!scratch || !counters)) return cudaErrorInvalidValue;
+    // 32-bit unit arithmetic in the kernel
+    if (plan.smem > 227 * 1024 || (uint64_t)g.n_tiles * g.n_chunks >= (1ull << 26)) return cudaErrorNotSupported;
     GemvArgs a;
     a.w = tiles;
-    a.x = x;
-    a.y = y;
-    a.partial = scratch;
-    a.counters = counters;
     a.err = err;
     a.g = g;
     a.ldx = ldx;
     a.ldy = ldy;
-    a.m = m;
-    a.cps = plan.cps;
-    a.k_splits = plan.k_splits;
-    a.n_pad = g.n_tiles * 16;
     a.stages = plan.stages;
-    a.red_mode = plan.red_mode;
+    a.pre = plan.stages;
+    a.n_clusters = plan.clusters;
+    a.panels = plan.panels;
+    a.win = plan.window;
+    a.kmax = plan.kmax;
     a.x_vec4 = ((ldx & 3) == 0 && (reinterpret_cast<uintptr_t>(x) & 15) == 0) ? 1 : 0;
-    if (ga) a.ga = *ga;
-    dim3 grid((g.n_tiles + plan.rt - 1) / plan.rt, plan.k_splits);
-    switch (dt) {
-    case GGUF_Q4_K: return launch_rt<GGUF_Q4_K>(plan.rt, plan.nt, a, grid, plan.smem, s);
-    case GGUF_Q4_0: return launch_rt<GGUF_Q4_0>(plan.rt, plan.nt, a, grid, plan.smem, s);
-    case GGUF_Q8_0: return launch_rt<GGUF_Q8_0>(plan.rt, plan.nt, a, grid, plan.smem, s);
-    default: return cudaErrorInvalidValue;
+    // token groups of plan.nt (one launch when the table fits the batch)
+    for (int t0 = 0; t0 < m; t0 += plan.nt) {
+        a.x = x + (size_t)t0 * ldx;
+        a.y = y + (size_t)t0 * ldy;
+        a.m = m - t0 < plan.nt ? m - t0 : plan.nt;
+        if (ga) {
+            a.ga = *ga;
+            for (int r = 0; r < ga->world; r++)
+                if (a.ga.ll[r]) a.ga.ll[r] += (size_t)t0 * ldy;
+        }
+        cudaError_t e;
+        switch (dt) {
+        case GGUF_Q4_K: e = launch_nt<GGUF_Q4_K>(plan.nt, a, plan.smem, s); break;
+        case GGUF_Q4_0: e = launch_nt<GGUF_Q4_0>(plan.nt, a, plan.smem, s); break;
+        case GGUF_Q8_0: e = launch_nt<GGUF_Q8_0>(plan.nt, a, plan.smem, s); break;
+        default: return cudaErrorInvalidValue;
+        }
+        if (e != cudaSuccess) return e;
     }
+    return cudaSuccess;
 }
 
 }  // namespace rce

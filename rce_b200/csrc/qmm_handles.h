@@ -10,10 +10,6 @@
 #include "qmm_layout.cuh"
 
 struct RceScratch {
-    float *partial = nullptr;
-    size_t floats = 0;
-    unsigned *counters = nullptr;
-    size_t ncounters = 0;
     void *gemm_ws = nullptr;  // prefill GEMM workspace (fp16 activations, token scales)
     size_t gemm_ws_bytes = 0;
     void *moe_ws = nullptr;   // MoE FFN workspace (routes, rows, activations per row)

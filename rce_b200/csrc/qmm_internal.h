@@ -36,29 +36,22 @@ struct GatherArgs {
 };
 
 // Decode GEMV / small-M matmul: y[t][row] = sum_k x[t][k] W[row][k], for
-// t < m <= kGemvMaxTokens, rows [0, n_rows).  Uses split-K scratch when the
-// plan asks for it.  `err` (device-visible int) receives a non-zero code if a
-// bounded wait inside the kernel expires.
+// t < m <= kGemvMaxTokens, rows [0, n_rows).  `err` (device-visible int)
+// receives a non-zero code if a bounded wait inside the kernel expires.
 constexpr int kGemvMaxTokens = 4;
 struct GemvPlan {
-    int rt = 1;          // 16-row tiles per CTA
-    int k_splits = 1;    // CTAs along K
-    int cps = 0;         // chunks per split
-    int nt = 1;          // token slots compiled in (1, 2 or 4)
+    int clusters = 1;    // clusters of two CTAs, each owning a block of whole tiles
+    int panels = 1;      // K halves a cluster's units are ordered by (1 or 2)
+    int kmax = 2;        // partial-sum slots per warp
+    int nt = 1;          // token slots compiled in (1, 2 or 4); larger batches take several launches
     int stages = 4;      // TMA ring depth per warp
-    int window = 16;     // chunks of activations staged per CTA
-    int red_mode = 0;    // split-K reduction: 0 none, 1 cluster shared memory, 2 global scratch
+    int window = 16;     // chunks of activations staged per CTA (the largest)
     size_t smem = 0;     // dynamic shared memory
-    size_t scratch_floats = 0;  // partial sums
-    int counters = 0;    // arrival counters (k_splits > 1)
 };
 GemvPlan plan_gemv(int dt, const Geometry &g, int m, int sm_count);
-// The same plan with any K split reduced through global scratch (for callers
-// that supply their own scratch) instead of cluster shared memory.
-GemvPlan plan_gemv_scratch(int dt, const Geometry &g, int m, int sm_count);
 cudaError_t launch_gemv(int dt, const uint8_t *tiles, const Geometry &g, const float *x, size_t ldx,
-                        float *y, size_t ldy, int m, const GemvPlan &plan, float *scratch,
-                        unsigned *counters, int *err, cudaStream_t s, const GatherArgs *ga = nullptr);
+                        float *y, size_t ldy, int m, const GemvPlan &plan, int *err, cudaStream_t s,
+                        const GatherArgs *ga = nullptr);
 // Gather helpers.  push: for kernels that write only locally (the prefill
 // GEMM), store rows [0, t_rows) x [row_off, row_off + n) of y (leading
 // dimension ldy) into the peers' receive buffers.  unpack: wait (bounded)

@@ -1,8 +1,8 @@
 """rce_qmm_mm_batched_device_noalloc: the decode matmul for callers that may
-not allocate device memory (its split-K scratch is a fixed array inside the
-library).  Called through the C ABI and checked against the regular device
-entry point, with the tolerance of the other parity tests, on two calls in a
-row (the second call sees the array as the first one left it).
+not allocate device memory (every batch through the decode GEMV, which needs
+no device workspace).  Called through the C ABI and checked against the
+regular device entry point, with the tolerance of the other parity tests, on
+two calls in a row.
 
 This file is named to be collected last, so a run that stops at the first
 failure has run every other test before it.
@@ -34,7 +34,8 @@ def _noalloc(L, ctx, x, w, out, stream):
         ctypes.c_void_p(out.data_ptr()), out.stride(0), ctypes.c_void_p(stream.cuda_stream))
 
 
-# shapes with few row blocks, so the planner splits K and the fixed scratch is used
+# shapes with few row blocks (clusters of one or two tiles) and batches above
+# the GEMV's 4-token pass, one above the GEMM threshold
 @pytest.mark.parametrize("dt,n,k,m", [(O.GGUF_Q4_K, 1024, 4096, 1), (O.GGUF_Q4_K, 1024, 4096, 5),
                                       (O.GGUF_Q8_0, 700, 4096, 3), (O.GGUF_Q4_0, 512, 11008, 17)])
 def test_noalloc_matches_regular_entry_point(dt, n, k, m):
@@ -63,4 +64,6 @@ def test_noalloc_matches_regular_entry_point(dt, n, k, m):
         code = ctypes.c_int()
         assert L.rce_qmm_device_error(ctx.handle, ctypes.byref(code), 1) == 0 and code.value == 0
         _assert_close(out.cpu().numpy(), want)
+        # the same GEMV with the same plan: bit for bit
+        assert np.array_equal(out.cpu().numpy(), want)
 
