@@ -5,8 +5,10 @@ stack -- 32 layers x {q 4096x4096, k 1024x4096, v 1024x4096, o 4096x4096,
 gate 14336x4096, up 14336x4096, down 4096x14336}, 3,925,868,544 weight bytes,
 batch 1 (``--batch 16`` for the batch-16 variant), seeded synthetic weights
 with the configuration's distributions and N(0,1) activations.  One step =
-one decode token through all 224 matmuls (one launch each, in layer order,
-replayed from a CUDA graph).  With N GPUs every matrix is row-sharded N ways
+one decode token through all 224 matmuls in layer order, replayed from a
+CUDA graph; on one GPU the matrices that read the same activation share a
+launch (q, k, v and gate, up through rce_qmm_mm_batched_device_multi: 4
+launches per layer; ``--no-group`` for one launch per matrix).  With N GPUs every matrix is row-sharded N ways
 and each output is all-gathered by the matmul itself: its kernel stores the
 rows, as {value, epoch} words, into every other GPU's receive buffer over
 NVLink; the step ends with each GPU unpacking the seven outputs (waiting
@@ -56,6 +58,9 @@ D_MODEL, D_FF, D_KV = 4096, 14336, 1024
 # (name, n_rows, n_cols)
 LAYER = [("q", D_MODEL, D_MODEL), ("k", D_KV, D_MODEL), ("v", D_KV, D_MODEL), ("o", D_MODEL, D_MODEL),
          ("gate", D_FF, D_MODEL), ("up", D_FF, D_MODEL), ("down", D_MODEL, D_FF)]
+# matrices that read the same activation run as one launch on one GPU
+# (rce_qmm_mm_batched_device_multi): attention q, k, v and FFN gate, up
+GROUPS = [("q", "k", "v"), ("o",), ("gate", "up"), ("down",)]
 
 
 def q4k_bytes(n, k):
@@ -198,7 +203,8 @@ def run_reference(args, rank, world):
 
 def config_dict(args, world):
     return {"workload": "llama3-8b-shaped Q4_K decode matmul stack (configs[3])", "layers": args.layers,
-            "batch": args.batch, "matmuls_per_step": 7 * args.layers, "weight_bytes": layer_bytes() * args.layers,
+            "batch": args.batch, "matmuls_per_step": 7 * args.layers,
+            "launches_per_layer": (len(GROUPS) if world == 1 and not args.no_group else 7), "weight_bytes": layer_bytes() * args.layers,
             "parallelism": f"row-shard x{world} + all-gather" if world > 1 else "single GPU",
             "l2": "no flush: weights 3.9 GB >> 126 MB L2" if args.layers >= 8 else "small stack (profiling)"}
 
@@ -380,6 +386,8 @@ def main():
     ap.add_argument("--layers", type=int, default=32)
     ap.add_argument("--e2e-steps", type=int, default=3)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-group", action="store_true",
+                    help="one launch per matrix (no grouped q/k/v and gate/up launches)")
     ap.add_argument("--profile", action="store_true", help="short run for ncu: warm-up + steps only")
     ap.add_argument("--profile-prefill", type=int, default=0, metavar="M",
                     help="for ncu: only the configs[2] prefill matmul at M tokens, warm-up + steps launches")
@@ -444,12 +452,22 @@ def main():
         for name, n, _ in LAYER:
             pg.output(name, m, n)
     stream = torch.cuda.Stream(dev)
-    launches_per_step = 7 * args.layers + (8 if world > 1 else 0)
+    grouped = world == 1 and not args.no_group
+    launches_per_step = (len(GROUPS) if grouped else 7) * args.layers + (8 if world > 1 else 0)
 
     def step():
         if world > 1:
             pg.begin_step(7 * args.layers, stream=stream)
         for mats in layers:
+            if grouped:
+                by = {name: (ns, k, w) for name, ns, k, w in mats}
+                for grp in GROUPS:
+                    k = by[grp[0]][1]
+                    if len(grp) == 1:
+                        R.mm_batched_device(xs[k], by[grp[0]][2], ys[grp[0]], stream=stream)
+                    else:
+                        R.mm_multi_device(xs[k], [by[nm][2] for nm in grp], [ys[nm] for nm in grp], stream=stream)
+                continue
             for name, ns, k, w in mats:
                 if world > 1:
                     pg.mm(xs[k], w, name, rank * ns, stream=stream)
@@ -462,7 +480,7 @@ def main():
     graph = None
     with torch.cuda.stream(stream):
         for _ in range(2):
-            step()  # eager warm-up: allocates split-K scratch for this stream
+            step()  # eager warm-up: allocates per-stream workspaces before capture
     stream.synchronize()
     if world > 1:
         dist.barrier()
@@ -555,6 +573,34 @@ def main():
         kern[name] = {"avg_us": avg_ms * 1e3, "alg_bytes": alg, "gbs": alg / (avg_ms / 1e3) / 1e9,
                       "total_ms": avg_ms * args.layers}
         del g_t
+    # the grouped launches of the step, timed the same way
+    groups = {}
+    if grouped:
+        for grp in GROUPS:
+            if len(grp) == 1:
+                continue
+            g_t = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g_t, stream=stream):
+                for mats in layers:
+                    by = {nm: (ns, kk, w) for nm, ns, kk, w in mats}
+                    R.mm_multi_device(xs[by[grp[0]][1]], [by[nm][2] for nm in grp], [ys[nm] for nm in grp],
+                                      stream=stream)
+            with torch.cuda.stream(stream):
+                for _ in range(3):
+                    g_t.replay()
+                e0 = torch.cuda.Event(enable_timing=True)
+                e1 = torch.cuda.Event(enable_timing=True)
+                reps = 10
+                e0.record(stream)
+                for _ in range(reps):
+                    g_t.replay()
+                e1.record(stream)
+            e1.synchronize()
+            avg_ms = e0.elapsed_time(e1) / (reps * args.layers)
+            dims = {nm: (n, k) for nm, n, k in LAYER}
+            alg = sum(q4k_bytes(dims[nm][0], dims[nm][1]) + 4 * m * dims[nm][0] for nm in grp) + 4 * m * dims[grp[0]][1]
+            groups["+".join(grp)] = {"avg_us": round(avg_ms * 1e3, 2), "gbs": round(alg / (avg_ms / 1e3) / 1e9, 1)}
+            del g_t
     if clocks:
         clocks.t_end = time.time()
         clocks.stop()
@@ -637,6 +683,7 @@ def main():
                          "traffic": traffic, "alg_bytes_per_launch": kern[dom]["alg_bytes"],
                          "avg_launch_us": round(kern[dom]["avg_us"], 2)},
             "kernels": {nm: {"avg_us": round(v["avg_us"], 2), "gbs": round(v["gbs"], 1)} for nm, v in kern.items()},
+            "grouped_launches": groups,
             "stack_frac_of_hbm": round(value / world / hbm, 4),
             "prefill_gemm": {
                 "workload": f"configs[2]: Q4_K {PREFILL_N}x{PREFILL_K} weight, M f32 activations, fp16 operands, "

@@ -132,6 +132,21 @@ int rce_qmm_mm_batched(rce_qmm_ctx *ctx, const float *a, size_t t_rows, const rc
 int rce_qmm_mm_batched_device(rce_qmm_ctx *ctx, const float *d_a, size_t lda, size_t t_rows,
                               const rce_qmm_weight *w, float *d_out, size_t ldo, void *stream);
 
+/* n_w (1..4) rce_qmm_mm_batched_device calls that share their activations,
+ * in one launch: d_outs[i] ([t_rows][ldos[i]] f32) = d_a . ws[i]^T.  The
+ * weights must have the same dtype and n_cols.  No counterpart in the
+ * reference (it runs mm_batched per weight, rce-op-qmm/src/lib.rs); serving
+ * code uses it for matrices that read the same input (attention q, k, v; FFN
+ * gate, up), whose tiles the decode GEMV then splits over the GPU as one
+ * matrix.  Batches of prefill_min_tokens or more run the tensor-core GEMM per
+ * weight.  Per-weight results equal rce_qmm_mm_batched_device's to the
+ * tolerance of the decode path (the summation order follows the group's
+ * split); within a group, every token's result is independent of the batch
+ * size. */
+int rce_qmm_mm_batched_device_multi(rce_qmm_ctx *ctx, const float *d_a, size_t lda, size_t t_rows,
+                                    const rce_qmm_weight *const *ws, size_t n_w, float *const *d_outs,
+                                    const size_t *ldos, void *stream);
+
 /* As rce_qmm_mm_batched_device, for callers that cannot allocate device
  * memory (a custom allocator owning the device, a serving loop that forbids
  * cudaMalloc after start-up).  No counterpart in the reference: its CPU path

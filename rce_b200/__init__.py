@@ -16,6 +16,7 @@ from .qmm import (  # noqa: F401
     mm_1d_serial,
     mm_batched,
     mm_batched_device,
+    mm_multi_device,
 )
 from .moe import RouterDecision, decisions, moe_ffn_device, moe_route_device, split_experts  # noqa: F401
 from .shard import PeerGroup, row_shards, torch_exchange  # noqa: F401

@@ -108,7 +108,10 @@ int check_weight(const rce_qmm_weight *w) {
     return ok();
 }
 
-// Prefill GEMM workspace for stream s (grown like the split-K scratch).
+// Prefill GEMM workspace for stream s, one per stream (work on one stream is
+// ordered, so its kernels never share it concurrently).  Growing it
+// synchronises the stream, so the first call with the largest shape must
+// come before any CUDA-graph capture on that stream.
 int stream_gemm_ws(rce_qmm_ctx *ctx, cudaStream_t s, size_t bytes, void **out) {
     std::lock_guard<std::mutex> lk(ctx->mu);
     RceScratch &sc = ctx->scratch[s];
@@ -147,7 +150,7 @@ int run_matmul(rce_qmm_ctx *ctx, const rce_qmm_weight *w, const float *d_x, size
     return ok();
 }
 
-// MoE FFN workspace for stream s (grown like the split-K scratch) and its
+// MoE FFN workspace for stream s (grown like the GEMM workspace) and its
 // pinned host mirror of the per-expert row offsets.
 int stream_moe_ws(rce_qmm_ctx *ctx, cudaStream_t s, size_t bytes, size_t host_n, void **ws, int32_t **host) {
     std::lock_guard<std::mutex> lk(ctx->mu);
@@ -420,6 +423,56 @@ int rce_qmm_mm_batched_device(rce_qmm_ctx *ctx, const float *d_a, size_t lda, si
                     (long long)w->g.n_cols, ldo, (long long)w->g.n_rows);
     DeviceGuard dg(ctx->device);
     return run_matmul(ctx, w, d_a, lda, t_rows, d_out, ldo, (cudaStream_t)stream);
+}
+
+int rce_qmm_mm_batched_device_multi(rce_qmm_ctx *ctx, const float *d_a, size_t lda, size_t t_rows,
+                                    const rce_qmm_weight *const *ws, size_t n_w, float *const *d_outs,
+                                    const size_t *ldos, void *stream) {
+    if (!ctx) return fail(RCE_QMM_ERR_INVALID, "mm_batched_device_multi: null ctx");
+    if (!ws || !d_outs || !ldos || n_w < 1 || n_w > (size_t)rce::kGemvMaxGroup)
+        return fail(RCE_QMM_ERR_INVALID, "mm_batched_device_multi: need 1..%d weights, outputs and strides",
+                    rce::kGemvMaxGroup);
+    for (size_t i = 0; i < n_w; i++) {
+        int rc = check_weight(ws[i]);
+        if (rc) return rc;
+        if (ws[i]->ctx != ctx) return fail(RCE_QMM_ERR_INVALID, "mm_batched_device_multi: weight %zu belongs to another context", i);
+        if (ws[i]->dtype != ws[0]->dtype || ws[i]->g.n_cols != ws[0]->g.n_cols)
+            return fail(RCE_QMM_ERR_INVALID, "mm_batched_device_multi: weight %zu differs from weight 0 in dtype or k", i);
+        if (!d_outs[i] || ldos[i] < (size_t)ws[i]->g.n_rows)
+            return fail(RCE_QMM_ERR_INVALID, "mm_batched_device_multi: output %zu null or ldo %zu < n %lld", i, ldos[i],
+                        (long long)ws[i]->g.n_rows);
+    }
+    if (t_rows == 0) return ok();
+    if (!d_a || lda < (size_t)ws[0]->g.n_cols)
+        return fail(RCE_QMM_ERR_INVALID, "mm_batched_device_multi: null activations or lda %zu < k %lld", lda,
+                    (long long)ws[0]->g.n_cols);
+    DeviceGuard dg(ctx->device);
+    cudaStream_t s = (cudaStream_t)stream;
+    if (ctx->prefill_min_tokens > 0 && t_rows >= (size_t)ctx->prefill_min_tokens) {
+        // the tensor-core GEMM, one weight at a time
+        for (size_t i = 0; i < n_w; i++) {
+            int rc = run_matmul(ctx, ws[i], d_a, lda, t_rows, d_outs[i], ldos[i], s);
+            if (rc) return rc;
+        }
+        return ok();
+    }
+    rce::GemvGroup grp;
+    grp.n = (int)n_w;
+    for (size_t i = 0; i < n_w; i++) {
+        grp.w[i] = ws[i]->dev;
+        grp.g[i] = ws[i]->g;
+        grp.ldy[i] = ldos[i];
+    }
+    const rce::Geometry gg = rce::group_geometry(grp);
+    for (size_t t0 = 0; t0 < t_rows;) {
+        const size_t left = t_rows - t0;
+        const int m = (int)(left < (size_t)rce::kGemvMaxTokens ? left : (size_t)rce::kGemvMaxTokens);
+        const rce::GemvPlan plan = rce::plan_gemv(ws[0]->dtype, gg, m, ctx->sm_count);
+        for (size_t i = 0; i < n_w; i++) grp.y[i] = d_outs[i] + t0 * ldos[i];
+        CUDA_TRY(rce::launch_gemv_group(ws[0]->dtype, grp, d_a + t0 * lda, lda, m, plan, ctx->err_dev, s));
+        t0 += (size_t)m;
+    }
+    return ok();
 }
 
 int rce_qmm_mm_batched(rce_qmm_ctx *ctx, const float *a, size_t t_rows, const rce_qmm_weight *w, float *out,

@@ -53,13 +53,20 @@ namespace {
 constexpr int kMaxStages = 4;
 constexpr unsigned long long kWaitLimitNs = 1000000000ull;  // 1 s per wait
 
+// Up to kGemvMaxGroup weights with the same dtype and K, read by one launch:
+// their tiles are numbered one after the other (weight i's tiles start at
+// tile0[i]) and split over the grid as one matrix.
 struct GemvArgs {
-    const uint8_t *w;
+    const uint8_t *w[kGemvMaxGroup];
+    float *y[kGemvMaxGroup];
+    size_t ldy[kGemvMaxGroup];
+    int64_t n_rows[kGemvMaxGroup];
+    int tile0[kGemvMaxGroup];
+    int n_w;
     const float *x;
-    float *y;
     int *err;
-    Geometry g;
-    size_t ldx, ldy;
+    Geometry g;  // n_tiles: all weights' tiles; n_chunks, n_cols: shared
+    size_t ldx;
     int m, stages, pre, x_vec4;
     int n_clusters;  // clusters of kClusterCtas CTAs; cluster c owns a block of whole tiles
     int panels;      // 1 or 2 (the work split)
@@ -175,9 +182,28 @@ __device__ __forceinline__ float h2f(uint32_t bits16) {
 
 // One output value: to y, and with the fused all-gather also to every other
 // rank's receive buffer (at this rank's rows of the full output).
-__device__ __forceinline__ void put_y(const GemvArgs &p, int t, int64_t row, float v, unsigned epoch) {
-    p.y[t * p.ldy + row] = v;
-    if (p.ga.world > 1) gather_send(p.ga, (size_t)t * p.ldy + (size_t)p.ga.row_off + (size_t)row, v, epoch);
+// The weight of global tile `tile`.
+__device__ __forceinline__ int group_of(const GemvArgs &p, int tile) {
+    int wi = 0;
+#pragma unroll
+    for (int i = 1; i < kGemvMaxGroup; i++) wi += (i < p.n_w && tile >= p.tile0[i]) ? 1 : 0;
+    return wi;
+}
+
+// Chunk `chunk` of global tile `tile`.
+__device__ __forceinline__ const uint8_t *tile_src(const GemvArgs &p, int tile, int chunk, int cb) {
+    const int wi = group_of(p, tile);
+    return p.w[wi] + ((size_t)(tile - p.tile0[wi]) * p.g.n_chunks + chunk) * cb;
+}
+
+// Output row r (0..15) of global tile `tile`, token t (< m): into its
+// weight's y, and to the peers when the output is gathered (one weight).
+__device__ __forceinline__ void put_y(const GemvArgs &p, int t, int tile, int r, float v, unsigned epoch) {
+    const int wi = group_of(p, tile);
+    const int64_t row = (int64_t)(tile - p.tile0[wi]) * 16 + r;
+    if (row >= p.n_rows[wi]) return;
+    p.y[wi][t * p.ldy[wi] + row] = v;
+    if (p.ga.world > 1) gather_send(p.ga, (size_t)t * p.ldy[0] + (size_t)p.ga.row_off + (size_t)row, v, epoch);
 }
 
 template <int DT>
@@ -590,7 +616,7 @@ __global__ void __launch_bounds__(kWarps * 32, 1) gemv_kernel(GemvArgs p) {
     UnitIter issue;  // the next unit to copy into the ring
     if (nu > 0) issue.init(u0, sp);
     auto src_next = [&]() {
-        const uint8_t *src = p.w + ((size_t)(T0 + issue.tile) * C + issue.chunk) * CB;
+        const uint8_t *src = tile_src(p, T0 + issue.tile, issue.chunk, CB);
         issue.next(sp);
         return src;
     };
@@ -719,7 +745,6 @@ __global__ void __launch_bounds__(kWarps * 32, 1) gemv_kernel(GemvArgs p) {
     if (nu > 0) un.init(u0, sp);
     int seg_k = 0;                 // segment number within this warp
     uint32_t seg_u0 = u0;          // first unit of the segment
-    const uint8_t *wclu = p.w + (size_t)T0 * C * CB;  // the cluster's first tile
     const uint8_t *myring = ring + (size_t)warp * S * CB;
     for (int i = 0; i < nu; i++) {
         if (!mbar_wait_bounded(mb0 + 8 * slt, phase)) {
@@ -731,7 +756,7 @@ __global__ void __launch_bounds__(kWarps * 32, 1) gemv_kernel(GemvArgs p) {
         load_chunk<DT>(cur, myring + slt * CB, lane, hw);
         __syncwarp();
         if (i + S < nu) {  // refill the slot (lane 0; the branch is warp-uniform)
-            const uint8_t *src = wclu + ((size_t)issue.tile * C + issue.chunk) * CB;
+            const uint8_t *src = tile_src(p, T0 + issue.tile, issue.chunk, CB);
             issue.next(sp);
             // this slot's reads happen before the copy that refills it
             bulk_refill(lane == 0, ring0 + slt * CB, src, CB, mb0 + 8 * slt);
@@ -765,9 +790,10 @@ __global__ void __launch_bounds__(kWarps * 32, 1) gemv_kernel(GemvArgs p) {
                 if ((lane & 3) == 0) {
                     const int r = lane >> 2;
                     if (whole) {  // the tile's only segment: straight to y
-                        const int64_t row = (int64_t)(T0 + seg_tile) * 16 + r;
-                        if (t < m && row < p.g.n_rows) put_y(p, t, row, v0, gepoch);
-                        if (t < m && row + 8 < p.g.n_rows) put_y(p, t, row + 8, v1, gepoch);
+                        if (t < m) {
+                            put_y(p, t, T0 + seg_tile, r, v0, gepoch);
+                            put_y(p, t, T0 + seg_tile, r + 8, v1, gepoch);
+                        }
                     } else if (sp.slot_of(seg_k) < p.kmax) {
                         st_cluster_f32(rb + 4 * (t * 16 + r), v0);
                         st_cluster_f32(rb + 4 * (t * 16 + r + 8), v1);
@@ -828,8 +854,7 @@ __global__ void __launch_bounds__(kWarps * 32, 1) gemv_kernel(GemvArgs p) {
 #pragma unroll
         for (int e = 0; e < 2; e++) {
             const int q = lane + 32 * e, t = q >> 4, r = q & 15;
-            const int64_t row = (int64_t)(T0 + tl) * 16 + r;
-            if (q < NT * 16 && t < m && row < p.g.n_rows) put_y(p, t, row, v[e], gepoch);
+            if (q < NT * 16 && t < m) put_y(p, t, T0 + tl, r, v[e], gepoch);
         }
     }
 }
@@ -948,20 +973,32 @@ GemvPlan plan_gemv(int dt, const Geometry &g, int m, int sm_count) {
     return p;
 }
 
-cudaError_t launch_gemv(int dt, const uint8_t *tiles, const Geometry &g, const float *x, size_t ldx,
-                        float *y, size_t ldy, int m, const GemvPlan &plan, int *err, cudaStream_t s,
-                        const GatherArgs *ga) {
-    if (m <= 0 || g.n_rows <= 0) return cudaSuccess;
-    if (m > kGemvMaxTokens || plan.nt < 1) return cudaErrorInvalidValue;
-    if (ga && ga->world > kMaxPeers) return cudaErrorInvalidValue;
+cudaError_t launch_gemv_group(int dt, const GemvGroup &grp, const float *x, size_t ldx, int m,
+                              const GemvPlan &plan, int *err, cudaStream_t s, const GatherArgs *ga) {
+    if (m <= 0) return cudaSuccess;
+    if (m > kGemvMaxTokens || plan.nt < 1 || grp.n < 1 || grp.n > kGemvMaxGroup) return cudaErrorInvalidValue;
+    if (ga && (ga->world > kMaxPeers || (ga->world > 1 && grp.n != 1))) return cudaErrorInvalidValue;
+    const Geometry g = group_geometry(grp);
     // 32-bit unit arithmetic in the kernel
     if (plan.smem > 227 * 1024 || (uint64_t)g.n_tiles * g.n_chunks >= (1ull << 26)) return cudaErrorNotSupported;
+    if (g.n_tiles == 0) return cudaSuccess;
     GemvArgs a;
-    a.w = tiles;
+    a.n_w = grp.n;
+    float *ybase[kGemvMaxGroup];
+    for (int i = 0; i < kGemvMaxGroup; i++) {
+        const int k = i < grp.n ? i : 0;  // unused entries repeat weight 0
+        a.w[i] = grp.w[k];
+        a.n_rows[i] = grp.g[k].n_rows;
+        a.ldy[i] = grp.ldy[k];
+        ybase[i] = grp.y[k];
+    }
+    for (int i = 0, t = 0; i < kGemvMaxGroup; i++) {
+        a.tile0[i] = t;
+        if (i < grp.n) t += (int)grp.g[i].n_tiles;
+    }
     a.err = err;
     a.g = g;
     a.ldx = ldx;
-    a.ldy = ldy;
     a.stages = plan.stages;
     a.pre = plan.stages;
     a.n_clusters = plan.clusters;
@@ -972,12 +1009,12 @@ cudaError_t launch_gemv(int dt, const uint8_t *tiles, const Geometry &g, const f
     // token groups of plan.nt (one launch when the table fits the batch)
     for (int t0 = 0; t0 < m; t0 += plan.nt) {
         a.x = x + (size_t)t0 * ldx;
-        a.y = y + (size_t)t0 * ldy;
+        for (int i = 0; i < kGemvMaxGroup; i++) a.y[i] = ybase[i] + (size_t)t0 * a.ldy[i];
         a.m = m - t0 < plan.nt ? m - t0 : plan.nt;
         if (ga) {
             a.ga = *ga;
             for (int r = 0; r < ga->world; r++)
-                if (a.ga.ll[r]) a.ga.ll[r] += (size_t)t0 * ldy;
+                if (a.ga.ll[r]) a.ga.ll[r] += (size_t)t0 * a.ldy[0];
         }
         cudaError_t e;
         switch (dt) {
@@ -989,6 +1026,28 @@ cudaError_t launch_gemv(int dt, const uint8_t *tiles, const Geometry &g, const f
         if (e != cudaSuccess) return e;
     }
     return cudaSuccess;
+}
+
+Geometry group_geometry(const GemvGroup &grp) {
+    Geometry g = grp.g[0];
+    int64_t tiles = 0;
+    for (int i = 0; i < grp.n; i++) tiles += grp.g[i].n_tiles;
+    g.n_tiles = tiles;
+    g.n_rows = tiles * 16;
+    return g;
+}
+
+cudaError_t launch_gemv(int dt, const uint8_t *tiles, const Geometry &g, const float *x, size_t ldx,
+                        float *y, size_t ldy, int m, const GemvPlan &plan, int *err, cudaStream_t s,
+                        const GatherArgs *ga) {
+    if (g.n_rows <= 0) return cudaSuccess;
+    GemvGroup grp;
+    grp.n = 1;
+    grp.w[0] = tiles;
+    grp.g[0] = g;
+    grp.y[0] = y;
+    grp.ldy[0] = ldy;
+    return launch_gemv_group(dt, grp, x, ldx, m, plan, err, s, ga);
 }
 
 }  // namespace rce

@@ -52,6 +52,23 @@ GemvPlan plan_gemv(int dt, const Geometry &g, int m, int sm_count);
 cudaError_t launch_gemv(int dt, const uint8_t *tiles, const Geometry &g, const float *x, size_t ldx,
                         float *y, size_t ldy, int m, const GemvPlan &plan, int *err, cudaStream_t s,
                         const GatherArgs *ga = nullptr);
+// Up to kGemvMaxGroup weights with the same dtype and K (n_cols) read by one
+// launch, each into its own output (y[i]: [m][ldy[i]]).  The grid splits the
+// weights' tiles as one matrix, so small matrices sharing an activation
+// (attention q, k, v; FFN gate, up) cost one launch.  Plan it with
+// plan_gemv(dt, group_geometry(grp), m, sm_count).  A gathered output (ga
+// with world > 1) takes one weight only.
+constexpr int kGemvMaxGroup = 4;
+struct GemvGroup {
+    int n = 0;
+    const uint8_t *w[kGemvMaxGroup] = {};
+    Geometry g[kGemvMaxGroup] = {};
+    float *y[kGemvMaxGroup] = {};
+    size_t ldy[kGemvMaxGroup] = {};
+};
+Geometry group_geometry(const GemvGroup &grp);
+cudaError_t launch_gemv_group(int dt, const GemvGroup &grp, const float *x, size_t ldx, int m,
+                              const GemvPlan &plan, int *err, cudaStream_t s, const GatherArgs *ga = nullptr);
 // Gather helpers.  push: for kernels that write only locally (the prefill
 // GEMM), store rows [0, t_rows) x [row_off, row_off + n) of y (leading
 // dimension ldy) into the peers' receive buffers.  unpack: wait (bounded)

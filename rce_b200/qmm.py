@@ -312,6 +312,40 @@ def mm_batched_device(x, w: QuantWeight, out=None, stream=None):
     return out
 
 
+def mm_multi_device(x, weights, outs=None, stream=None):
+    """Several ``mm_batched_device`` calls sharing ``x``, in one launch
+    (``rce_qmm_mm_batched_device_multi``): 1-4 weights of one dtype and K,
+    e.g. attention q, k, v or FFN gate, up.  Returns the list of outputs
+    ([T, N_i] each; ``outs`` may supply them)."""
+    import torch
+
+    weights = list(weights)
+    if not 1 <= len(weights) <= 4:
+        raise ValueError("mm_multi_device takes 1 to 4 weights")
+    for w in weights:
+        _check_weight(w)
+    if x.dim() == 1:
+        x = x.view(1, -1)
+    if x.dtype != torch.float32 or not x.is_cuda or x.stride(1) != 1:
+        raise ValueError("x must be a CUDA float32 tensor with unit column stride")
+    t_rows, k = x.shape
+    for w in weights:
+        if k != w.n_cols:
+            raise ValueError(f"activation len {k} ≠ k {w.n_cols}")
+    if outs is None:
+        outs = [torch.empty((t_rows, w.n_rows), dtype=torch.float32, device=x.device) for w in weights]
+    outs = list(outs)
+    if len(outs) != len(weights) or any(o.stride(-1) != 1 for o in outs):
+        raise ValueError("one output with unit column stride per weight")
+    n = len(weights)
+    hs = (ctypes.c_void_p * n)(*[w.handle for w in weights])
+    ys = (ctypes.c_void_p * n)(*[o.data_ptr() for o in outs])
+    lds = (ctypes.c_size_t * n)(*[o.stride(0) if o.dim() == 2 else w.n_rows for o, w in zip(outs, weights)])
+    check(lib().rce_qmm_mm_batched_device_multi(weights[0].ctx.handle, ctypes.c_void_p(x.data_ptr()), x.stride(0),
+                                                t_rows, hs, n, ys, lds, _stream_handle(stream, x.device)))
+    return outs
+
+
 def dequant_device(w: QuantWeight, row0: int = 0, row1: Optional[int] = None, out=None, stream=None):
     """Bit-exact dequantisation of rows [row0, row1) into a CUDA f32 tensor."""
     import torch
