@@ -53,6 +53,25 @@ namespace {
 constexpr int kMaxStages = 4;
 constexpr unsigned long long kWaitLimitNs = 1000000000ull;  // 1 s per wait
 
+// x / d for 0 <= x < 2^31 as a multiply and a shift (Granlund and
+// Montgomery, "Division by invariant integers using multiplication", 1994,
+// Theorem 4.2 with N = 31: m = ceil(2^(31+l) / d), l = ceil(log2 d)).
+struct FastDiv {
+    uint32_t m = 1u << 31, s = 31;  // d = 1
+};
+__host__ inline FastDiv make_fastdiv(uint32_t d) {
+    FastDiv f;
+    if (d <= 1) return f;
+    uint32_t l = 0;
+    while ((1ull << l) < d) l++;
+    f.m = (uint32_t)(((1ull << (31 + l)) + d - 1) / d);
+    f.s = 31 + l;
+    return f;
+}
+__host__ __device__ __forceinline__ uint32_t udiv(uint32_t x, const FastDiv &f) {
+    return (uint32_t)(((uint64_t)x * f.m) >> f.s);
+}
+
 // Up to kGemvMaxGroup weights with the same dtype and K, read by one launch:
 // their tiles are numbered one after the other (weight i's tiles start at
 // tile0[i]) and split over the grid as one matrix.
@@ -70,6 +89,8 @@ struct GemvArgs {
     int m, stages, pre, x_vec4;
     int n_clusters;  // clusters of kClusterCtas CTAs; cluster c owns a block of whole tiles
     int panels;      // 1 or 2 (the work split)
+    int tiles_base, tiles_extra;   // clusters c < tiles_extra hold tiles_base + 1 tiles
+    FastDiv fd_pw0, fd_pw1, fd_u[2];  // division by the run lengths and by the units of a cluster (base, base + 1)
     int win, kmax;   // shared-memory maxima: table chunks, slots per warp
     GatherArgs ga;   // fused all-gather over peer memory (ga.world > 1)
 };
@@ -452,22 +473,38 @@ constexpr int kClusterWarps = kWarps * kClusterCtas;
 constexpr int kTwoPanelMaxTiles = 15;  // two panels while clusters hold at most this many tiles
 constexpr int kTableBatch = 2;         // activation-table items a warp loads before the ring's rest
 
+// The unit order of a cluster of nt tiles (units < 2^25, so every numerator
+// below is < 2^31).  The divisions by pw0, pw1 and U are multiplies by the
+// plan's precomputed FastDivs.
 struct Split {
     int nt, n_chunks, pw0, pw1;  // tiles, chunks, run lengths of panel 0 and panel 1 (0: one panel)
     uint32_t U;                  // units
-    __host__ __device__ Split(int nt_, int n_chunks_, int panels) {
+    FastDiv d0, d1, dU;          // division by pw0, pw1, U
+    __host__ __device__ Split(int nt_, int n_chunks_, int panels, const FastDiv &f0, const FastDiv &f1,
+                              const FastDiv &fU) {
         nt = nt_;
         n_chunks = n_chunks_;
-        pw0 = panels == 2 ? (n_chunks_ + 1) / 2 : n_chunks_;
+        pw0 = panel0_width(n_chunks_, panels);
         pw1 = n_chunks_ - pw0;
         U = (uint32_t)nt_ * (uint32_t)n_chunks_;
+        d0 = f0;
+        d1 = f1;
+        dU = fU;
+    }
+    __host__ __device__ static int panel0_width(int n_chunks, int panels) {
+        return panels == 2 ? (n_chunks + 1) / 2 : n_chunks;
+    }
+    __host__ static Split make(int nt, int n_chunks, int panels) {
+        const int p0 = panel0_width(n_chunks, panels);
+        return Split(nt, n_chunks, panels, make_fastdiv((uint32_t)p0), make_fastdiv((uint32_t)(n_chunks - p0)),
+                     make_fastdiv((uint32_t)nt * (uint32_t)n_chunks));
     }
     __host__ __device__ uint32_t warp_u0(uint32_t g) const { return g * U / kClusterWarps; }
     // the non-empty warp whose range holds unit u
-    __host__ __device__ uint32_t warp_of(uint32_t u) const { return ((u + 1) * kClusterWarps + U - 1) / U - 1; }
+    __host__ __device__ uint32_t warp_of(uint32_t u) const { return udiv((u + 1) * kClusterWarps + U - 1, dU) - 1; }
     __host__ __device__ uint32_t run_of(uint32_t u) const {
         const uint32_t first = (uint32_t)nt * pw0;
-        return u < first ? u / pw0 : nt + (u - first) / pw1;
+        return u < first ? udiv(u, d0) : nt + udiv(u - first, d1);
     }
     __host__ __device__ uint32_t run_start(uint32_t r) const {
         return r < (uint32_t)nt ? r * pw0 : (uint32_t)nt * pw0 + (r - nt) * pw1;
@@ -503,10 +540,10 @@ struct Split {
     }
 };
 
-// The tiles of cluster c: [tile0, tile0 + n).
-__host__ __device__ inline void cluster_tiles(int c, int n_clusters, int n_tiles, int &tile0, int &n) {
-    tile0 = (int)((int64_t)c * n_tiles / n_clusters);
-    n = (int)((int64_t)(c + 1) * n_tiles / n_clusters) - tile0;
+// The tiles of cluster c: [tile0, tile0 + n); clusters c < extra hold base + 1.
+__host__ __device__ inline void cluster_tiles(int c, int base, int extra, int &tile0, int &n) {
+    tile0 = c * base + (c < extra ? c : extra);
+    n = base + (c < extra ? 1 : 0);
 }
 
 // Walks consecutive units without division (one division to start).
@@ -520,14 +557,15 @@ struct UnitIter {
         tile = sp.run_tile(run);
         chunk = sp.run_chunk0(run) + (int)off;
     }
+    __host__ __device__ __forceinline__ void next_run(const Split &sp) {
+        run++;
+        left = sp.run_len(run);
+        tile = sp.run_tile(run);
+        chunk = sp.run_chunk0(run);
+    }
     __host__ __device__ __forceinline__ void next(const Split &sp) {
         chunk++;
-        if (--left == 0) {
-            run++;
-            left = sp.run_len(run);
-            tile = sp.run_tile(run);
-            chunk = sp.run_chunk0(run);
-        }
+        if (--left == 0) next_run(sp);
     }
 };
 
@@ -594,8 +632,8 @@ __global__ void __launch_bounds__(kWarps * 32, 1) gemv_kernel(GemvArgs p) {
     const int rank = (int)cluster_rank();
     const int cl = blockIdx.x / kClusterCtas;
     int T0 = 0, NTc = 0;
-    cluster_tiles(cl, p.n_clusters, p.g.n_tiles, T0, NTc);
-    const Split sp(NTc, C, p.panels);
+    cluster_tiles(cl, p.tiles_base, p.tiles_extra, T0, NTc);
+    const Split sp(NTc, C, p.panels, p.fd_pw0, p.fd_pw1, p.fd_u[cl < p.tiles_extra ? 1 : 0]);
     int wlo = 0, nwin = 0;
     sp.window(sp.warp_u0(rank * kWarps), sp.warp_u0((rank + 1) * kWarps), wlo, nwin);
     const SmemLayout L = smem_layout(DT, NT, S, p.win, p.kmax);
@@ -640,8 +678,7 @@ __global__ void __launch_bounds__(kWarps * 32, 1) gemv_kernel(GemvArgs p) {
     // items' activations are loaded before the rest of the ring is requested,
     // so that those loads are not queued behind the weight copies.
     const int gg = lane >> 3, st = lane & 7;
-    auto load_item = [&](int item, float (&v)[8]) {
-        const int t = item / nwin, j = item - t * nwin;
+    auto load_item = [&](int t, int j, float (&v)[8]) {
         const int64_t k = (int64_t)(wlo + j) * CHUNK_K + 64 * gg + 8 * st;
 #pragma unroll
         for (int e = 0; e < 8; e++) v[e] = 0.f;
@@ -658,28 +695,24 @@ __global__ void __launch_bounds__(kWarps * 32, 1) gemv_kernel(GemvArgs p) {
             }
         }
     };
-    auto build_item = [&](int item, const float (&v)[8]) {
-        const int t = item / nwin, j = item - t * nwin;
-        float mx = 0.f;
-        bool fin = true;
+    auto build_item = [&](int t, int j, const float (&v)[8]) {
+        // the chunk's largest magnitude, as bits (ordered like the values;
+        // inf and NaN above every finite value)
+        uint32_t mb = 0;
 #pragma unroll
-        for (int e = 0; e < 8; e++) {
-            mx = fmaxf(mx, fabsf(v[e]));
-            fin = fin && isfinite(v[e]);
-        }
-        if (!fin) mx = INFINITY;
+        for (int e = 0; e < 8; e++) mb = max(mb, __float_as_uint(v[e]) & 0x7FFFFFFFu);
 #pragma unroll
-        for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+        for (int o = 16; o > 0; o >>= 1) mb = max(mb, __shfl_xor_sync(0xffffffffu, mb, o));
         float sc = 1.f, is = 1.f;
-        if (!isfinite(mx)) {
+        if (mb >= 0x7F800000u) {
             sc = 0.f;  // non-finite activations: the outputs become NaN
             is = __int_as_float(0x7fc00000);
-        } else if (mx > 0.f) {
-            int e;
-            frexpf(mx, &e);  // mx < 2^e
-            e = max(-100, min(100, e));
-            sc = ldexpf(1.f, FIXED_BITS - e);
-            is = ldexpf(1.f, e - FIXED_BITS);
+        } else if (mb != 0u) {
+            // max < 2^e (e from the exponent field); below 2^-96 the scale
+            // stays 2^126 so that it and its inverse are normal floats
+            const int e = max((int)(mb >> 23) - 126, -96);
+            sc = __uint_as_float((uint32_t)(127 + FIXED_BITS - e) << 23);  // 2^(30 - e)
+            is = __uint_as_float((uint32_t)(127 - FIXED_BITS + e) << 23);  // 2^(e - 30)
         }
         uint32_t y[8];
         uint32_t slo = 0, shi = 0;
@@ -710,21 +743,38 @@ __global__ void __launch_bounds__(kWarps * 32, 1) gemv_kernel(GemvArgs p) {
         }
         if (lane == 0) inv[t * nwin + j] = is;
     };
-    const int n_items = NT * nwin;
+    // this warp's items: (t, j) for every token slot t and j = warp, warp + 16, ...
+    int it_t = 0, it_j = warp;
+    auto item_next = [&]() {
+        it_j += kWarps;
+        if (it_j >= nwin) {
+            it_j = warp;
+            it_t++;
+        }
+    };
+    if (it_j >= nwin) it_t = NT;  // no items
     float xv[kTableBatch][8];
+    int bt[kTableBatch], bj[kTableBatch];
 #pragma unroll
-    for (int b = 0; b < kTableBatch; b++)
-        if (warp + b * kWarps < n_items) load_item(warp + b * kWarps, xv[b]);
+    for (int b = 0; b < kTableBatch; b++) {
+        bt[b] = it_t;
+        bj[b] = it_j;
+        if (it_t < NT) {
+            load_item(it_t, it_j, xv[b]);
+            item_next();
+        }
+    }
     // the rest of the ring
     if (lane == 0)
         for (int i = pre; i < first; i++) bulk_load(ring0 + i * CB, src_next(), CB, mb0 + 8 * i);
 #pragma unroll
     for (int b = 0; b < kTableBatch; b++)
-        if (warp + b * kWarps < n_items) build_item(warp + b * kWarps, xv[b]);
-    for (int item = warp + kTableBatch * kWarps; item < n_items; item += kWarps) {
+        if (bt[b] < NT) build_item(bt[b], bj[b], xv[b]);
+    while (it_t < NT) {
         float v[8];
-        load_item(item, v);
-        build_item(item, v);
+        load_item(it_t, it_j, v);
+        build_item(it_t, it_j, v);
+        item_next();
     }
     // the table visible to the CTA; the peer CTA started
     __syncthreads();
@@ -741,73 +791,81 @@ __global__ void __launch_bounds__(kWarps * 32, 1) gemv_kernel(GemvArgs p) {
     double acc[NT][2];
 #pragma unroll
     for (int t = 0; t < NT; t++) acc[t][0] = acc[t][1] = 0.0;
-    UnitIter un;  // the unit being processed
-    if (nu > 0) un.init(u0, sp);
-    int seg_k = 0;                 // segment number within this warp
-    uint32_t seg_u0 = u0;          // first unit of the segment
     const uint8_t *myring = ring + (size_t)warp * S * CB;
-    for (int i = 0; i < nu; i++) {
-        if (!mbar_wait_bounded(mb0 + 8 * slt, phase)) {
-            failed_at = i;
-            break;
-        }
-        const int j = un.chunk - wlo;
-        ChunkRegs<DT> cur;
-        load_chunk<DT>(cur, myring + slt * CB, lane, hw);
-        __syncwarp();
-        if (i + S < nu) {  // refill the slot (lane 0; the branch is warp-uniform)
-            const uint8_t *src = tile_src(p, T0 + issue.tile, issue.chunk, CB);
-            issue.next(sp);
-            // this slot's reads happen before the copy that refills it
-            bulk_refill(lane == 0, ring0 + slt * CB, src, CB, mb0 + 8 * slt);
-            issued++;
-        }
-        const uint2 *bp[NT];
-        float isc[NT];
-#pragma unroll
-        for (int t = 0; t < NT; t++) {
-            bp[t] = bact ? tbl + (size_t)(t * nwin + j) * 128 + boff : zero;
-            isc[t] = inv[t * nwin + j];
-        }
-        process_chunk<DT, NT>(cur, acc, bp, sint + j * 16, nwin * 8, isc, hsh, lane);
-        const int seg_tile = un.tile;
-        const uint32_t seg_run = un.run;
-        un.next(sp);
-        if (i + 1 == nu || un.run != seg_run) {
-            // the segment's row sums: add the four column groups (lanes 4r .. 4r+3)
-            const uint32_t seg_u1 = u0 + i + 1;
-            const bool whole = sp.pw1 == 0 && seg_u0 == sp.run_start(seg_run) && seg_u1 - seg_u0 == sp.run_len(seg_run);
-            const int owner = seg_tile % kClusterCtas;
-            const uint32_t rb = map_shared(slot + ((size_t)gw * p.kmax + sp.slot_of(seg_k)) * NT * 16, (uint32_t)owner);
+    // refill state: the source of the next copy and the units left in its run
+    // (consecutive chunks of a run are consecutive in memory)
+    const uint8_t *rsrc = first < nu ? tile_src(p, T0 + issue.tile, issue.chunk, CB) : nullptr;
+    uint32_t rleft = issue.left;
+    // Segments: this warp's units of one run each.
+    UnitIter un;  // first unit of the current segment
+    if (nu > 0) un.init(u0, sp);
+    int done = 0;
+    for (int seg_k = 0; done < nu; seg_k++) {
+        const int seg_len = min(nu - done, (int)un.left);
+        const int j0 = un.chunk - wlo;
+        for (int e = 0; e < seg_len; e++) {
+            if (!mbar_wait_bounded(mb0 + 8 * slt, phase)) {
+                failed_at = done + e;
+                break;
+            }
+            const int j = j0 + e;
+            ChunkRegs<DT> cur;
+            load_chunk<DT>(cur, myring + slt * CB, lane, hw);
+            __syncwarp();
+            if (done + e + S < nu) {  // refill the slot (lane 0; the branch is warp-uniform)
+                // this slot's reads happen before the copy that refills it
+                bulk_refill(lane == 0, ring0 + slt * CB, rsrc, CB, mb0 + 8 * slt);
+                issued++;
+                rsrc += CB;
+                if (--rleft == 0 && done + e + S + 1 < nu) {
+                    issue.next_run(sp);
+                    rsrc = tile_src(p, T0 + issue.tile, issue.chunk, CB);
+                    rleft = issue.left;
+                }
+            }
+            const uint2 *bp[NT];
+            float isc[NT];
 #pragma unroll
             for (int t = 0; t < NT; t++) {
-                double d0 = acc[t][0], d1 = acc[t][1];
-                d0 += __shfl_xor_sync(0xffffffffu, d0, 1);
-                d1 += __shfl_xor_sync(0xffffffffu, d1, 1);
-                d0 += __shfl_xor_sync(0xffffffffu, d0, 2);
-                d1 += __shfl_xor_sync(0xffffffffu, d1, 2);
-                const float v0 = (float)d0, v1 = (float)d1;
-                if ((lane & 3) == 0) {
-                    const int r = lane >> 2;
-                    if (whole) {  // the tile's only segment: straight to y
-                        if (t < m) {
-                            put_y(p, t, T0 + seg_tile, r, v0, gepoch);
-                            put_y(p, t, T0 + seg_tile, r + 8, v1, gepoch);
-                        }
-                    } else if (sp.slot_of(seg_k) < p.kmax) {
-                        st_cluster_f32(rb + 4 * (t * 16 + r), v0);
-                        st_cluster_f32(rb + 4 * (t * 16 + r + 8), v1);
-                    }
-                }
-                acc[t][0] = acc[t][1] = 0.0;
+                bp[t] = bact ? tbl + (size_t)(t * nwin + j) * 128 + boff : zero;
+                isc[t] = inv[t * nwin + j];
             }
-            seg_k++;
-            seg_u0 = seg_u1;
+            process_chunk<DT, NT>(cur, acc, bp, sint + j * 16, nwin * 8, isc, hsh, lane);
+            if (++slt == S) {
+                slt = 0;
+                phase ^= 1u;
+            }
         }
-        if (++slt == S) {
-            slt = 0;
-            phase ^= 1u;
+        if (failed_at < nu) break;
+        // the segment's row sums: add the four column groups (lanes 4r .. 4r+3)
+        const int seg_tile = un.tile;
+        const bool whole = sp.pw1 == 0 && seg_len == (int)sp.run_len(un.run) && un.chunk == sp.run_chunk0(un.run);
+        const int owner = seg_tile % kClusterCtas;
+        const uint32_t rb = map_shared(slot + ((size_t)gw * p.kmax + sp.slot_of(seg_k)) * NT * 16, (uint32_t)owner);
+#pragma unroll
+        for (int t = 0; t < NT; t++) {
+            double d0 = acc[t][0], d1 = acc[t][1];
+            d0 += __shfl_xor_sync(0xffffffffu, d0, 1);
+            d1 += __shfl_xor_sync(0xffffffffu, d1, 1);
+            d0 += __shfl_xor_sync(0xffffffffu, d0, 2);
+            d1 += __shfl_xor_sync(0xffffffffu, d1, 2);
+            const float v0 = (float)d0, v1 = (float)d1;
+            if ((lane & 3) == 0) {
+                const int r = lane >> 2;
+                if (whole) {  // the tile's only segment: straight to y
+                    if (t < m) {
+                        put_y(p, t, T0 + seg_tile, r, v0, gepoch);
+                        put_y(p, t, T0 + seg_tile, r + 8, v1, gepoch);
+                    }
+                } else if (sp.slot_of(seg_k) < p.kmax) {
+                    st_cluster_f32(rb + 4 * (t * 16 + r), v0);
+                    st_cluster_f32(rb + 4 * (t * 16 + r + 8), v1);
+                }
+            }
+            acc[t][0] = acc[t][1] = 0.0;
         }
+        done += seg_len;
+        if (done < nu) un.next_run(sp);
     }
     if (failed_at < nu) {
         // Report, then let this warp's copies in flight (numbers failed_at ..
@@ -930,7 +988,7 @@ GemvPlan plan_split(int dt, const Geometry &g, int m, int nc, int panels) {
     // (clusters hold nt_min or nt_max tiles)
     int win = 1, kmax = 2;
     for (int nt : {nt_min, nt_max}) {
-        const Split sp(nt, g.n_chunks, panels);
+        const Split sp = Split::make(nt, g.n_chunks, panels);
         for (int r = 0; r < kClusterCtas; r++) {
             int lo = 0, n = 0;
             sp.window(sp.warp_u0(r * kWarps), sp.warp_u0((r + 1) * kWarps), lo, n);
@@ -979,8 +1037,8 @@ cudaError_t launch_gemv_group(int dt, const GemvGroup &grp, const float *x, size
     if (m > kGemvMaxTokens || plan.nt < 1 || grp.n < 1 || grp.n > kGemvMaxGroup) return cudaErrorInvalidValue;
     if (ga && (ga->world > kMaxPeers || (ga->world > 1 && grp.n != 1))) return cudaErrorInvalidValue;
     const Geometry g = group_geometry(grp);
-    // 32-bit unit arithmetic in the kernel
-    if (plan.smem > 227 * 1024 || (uint64_t)g.n_tiles * g.n_chunks >= (1ull << 26)) return cudaErrorNotSupported;
+    // 32-bit unit arithmetic in the kernel (numerators < 2^31)
+    if (plan.smem > 227 * 1024 || (uint64_t)g.n_tiles * g.n_chunks >= (1ull << 25)) return cudaErrorNotSupported;
     if (g.n_tiles == 0) return cudaSuccess;
     GemvArgs a;
     a.n_w = grp.n;
@@ -1005,6 +1063,15 @@ cudaError_t launch_gemv_group(int dt, const GemvGroup &grp, const float *x, size
     a.panels = plan.panels;
     a.win = plan.window;
     a.kmax = plan.kmax;
+    a.tiles_base = (int)(g.n_tiles / plan.clusters);
+    a.tiles_extra = (int)(g.n_tiles % plan.clusters);
+    {
+        const int p0 = Split::panel0_width((int)g.n_chunks, plan.panels);
+        a.fd_pw0 = make_fastdiv((uint32_t)p0);
+        a.fd_pw1 = make_fastdiv((uint32_t)(g.n_chunks - p0));
+        a.fd_u[0] = make_fastdiv((uint32_t)(a.tiles_base * g.n_chunks));
+        a.fd_u[1] = make_fastdiv((uint32_t)((a.tiles_base + 1) * g.n_chunks));
+    }
     a.x_vec4 = ((ldx & 3) == 0 && (reinterpret_cast<uintptr_t>(x) & 15) == 0) ? 1 : 0;
     // token groups of plan.nt (one launch when the table fits the batch)
     for (int t0 = 0; t0 < m; t0 += plan.nt) {
