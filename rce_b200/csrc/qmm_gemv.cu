@@ -322,11 +322,62 @@ __device__ __forceinline__ void q4k_fields(const uint4 &hd, uint32_t sh, int (&s
 // 2^-53).  Q4_0 / Q8_0 scale every 32-value block by its own f16 d, so their
 // sub-block sums meet the scale one by one (f64).  Sums across chunks run in
 // f64, so cancelling terms keep their bits.
+// The digit sums of one chunk: per sub-block h and token t, da (digits 0, 1)
+// and db (digits 2, 3) of rows r (entries 0, 1) and r + 8 (entries 2, 3).
+template <int NT>
+struct ChunkSums {
+    int da[2][NT][4], db[2][NT][4];
+};
+
+// Phase 1 of a chunk: the MMAs.  Per sub-block h and token, two chains
+// (digits 0-1, 2-3) of four steps; with few tokens both sub-blocks' chains
+// run together.  bp[t] points at the lane's B fragments of this chunk for
+// token t (or at the zero block).
 template <int DT, int NT>
-__device__ __forceinline__ void process_chunk(const ChunkRegs<DT> &c, double (&acc)[NT][2], const uint2 *const (&bp)[NT],
-                                              const int *__restrict__ sint, int s_stride, const float (&isc)[NT],
-                                              uint32_t sh, int lane) {
+__device__ __forceinline__ void chunk_mma(const ChunkRegs<DT> &c, const uint2 *const (&bp)[NT], ChunkSums<NT> &r) {
     constexpr bool SIGNED = DT == GGUF_Q8_0;
+    constexpr int HB = NT <= 2 ? 2 : 1;  // sub-blocks whose chains run together
+#pragma unroll
+    for (int h0 = 0; h0 < 2; h0 += HB)
+#pragma unroll
+        for (int ss = 0; ss < 4; ss++)
+#pragma unroll
+            for (int hh = 0; hh < HB; hh++) {
+                const int h = h0 + hh, s = 4 * h + ss;
+                uint32_t a[4];
+                make_a<DT>(c, s, a);
+#pragma unroll
+                for (int t = 0; t < NT; t++) {
+                    // xy: tile A (digit 0 in col 2g, digit 1 in col 2g+1); zw: tile B (digits 2, 3)
+                    const uint4 b = *reinterpret_cast<const uint4 *>(bp[t] + s * 16);
+                    if (ss == 0) {
+                        imma16832<SIGNED, true>(r.da[h][t], a, b.x, b.y);
+                        imma16832<SIGNED, true>(r.db[h][t], a, b.z, b.w);
+                    } else {
+                        imma16832<SIGNED>(r.da[h][t], a, b.x, b.y);
+                        imma16832<SIGNED>(r.db[h][t], a, b.z, b.w);
+                    }
+                }
+            }
+}
+
+// Phase 2 of a chunk: the sums meet the scales.  sint points at the chunk's
+// per-unit integer activation sums (low and high digit pairs); isc[t] is the
+// chunk's activation scale for token t; `sh` is the lane group's Q4_K field
+// shift.
+//
+// Q4_K: a chunk is one super-block, so the lane's two sub-blocks share d and
+// dmin and the sums stay integers up to the chunk's end: with X the
+// fixed-point activations, Iq = sum_h sc_h * sum q X and Im = sum_h m_h *
+// sum X, each held as two int32 digit-pair halves (|sc * sum q X| < 2^30 per
+// half; two sub-blocks < 2^31), then d * Iq - dmin * Im in f64 (exact up to
+// 2^-53).  Q4_0 / Q8_0 scale every 32-value block by its own f16 d, so their
+// sub-block sums meet the scale one by one (f64).  Sums across chunks run in
+// f64, so cancelling terms keep their bits.
+template <int DT, int NT>
+__device__ __forceinline__ void chunk_epilogue(const ChunkRegs<DT> &c, const ChunkSums<NT> &r, double (&acc)[NT][2],
+                                               const int *__restrict__ sint, int s_stride, const float (&isc)[NT],
+                                               uint32_t sh, int lane) {
     const int g = lane & 3;
     int sc[2][2], mn[2][2];  // Q4_K: [row r / r+8][sub-block h]
     float ds[2][2];          // Q4_0 / Q8_0: [sub-block h][row r / r+8]
@@ -343,70 +394,42 @@ __device__ __forceinline__ void process_chunk(const ChunkRegs<DT> &c, double (&a
 #pragma unroll
     for (int t = 0; t < NT; t++)
 #pragma unroll
-        for (int r = 0; r < 2; r++) iq[t][r][0] = iq[t][r][1] = im[t][r][0] = im[t][r][1] = 0;
-    // the MMAs: per sub-block h and token, two chains (digits 0-1, 2-3) of four
-    // steps; with few tokens both sub-blocks' chains are interleaved
-    constexpr int HB = NT <= 2 ? 2 : 1;  // sub-blocks whose chains run together
-    int da[2][NT][4], db[2][NT][4];
+        for (int w = 0; w < 2; w++) iq[t][w][0] = iq[t][w][1] = im[t][w][0] = im[t][w][1] = 0;
 #pragma unroll
-    for (int h0 = 0; h0 < 2; h0 += HB) {
+    for (int h = 0; h < 2; h++) {
 #pragma unroll
-        for (int ss = 0; ss < 4; ss++)
-#pragma unroll
-            for (int hh = 0; hh < HB; hh++) {
-                const int h = h0 + hh, s = 4 * h + ss;
-                uint32_t a[4];
-                make_a<DT>(c, s, a);
-#pragma unroll
-                for (int t = 0; t < NT; t++) {
-                    // xy: tile A (digit 0 in col 2g, digit 1 in col 2g+1); zw: tile B (digits 2, 3)
-                    const uint4 b = *reinterpret_cast<const uint4 *>(bp[t] + s * 16);
-                    if (ss == 0) {
-                        imma16832<SIGNED, true>(da[h][t], a, b.x, b.y);
-                        imma16832<SIGNED, true>(db[h][t], a, b.z, b.w);
-                    } else {
-                        imma16832<SIGNED>(da[h][t], a, b.x, b.y);
-                        imma16832<SIGNED>(db[h][t], a, b.z, b.w);
-                    }
+        for (int t = 0; t < NT; t++) {
+            // digit pairs: lo = d1*2^8 + d0, hi = d3*2^8 + d2 (each exact in s32)
+            int lo0 = r.da[h][t][1] * 256 + r.da[h][t][0], hi0 = r.db[h][t][1] * 256 + r.db[h][t][0];  // row r
+            int lo1 = r.da[h][t][3] * 256 + r.da[h][t][2], hi1 = r.db[h][t][3] * 256 + r.db[h][t][2];  // row r + 8
+            const int2 sx = *reinterpret_cast<const int2 *>(sint + (t * s_stride + 2 * g + h) * 2);
+            if (DT == GGUF_Q4_K) {
+                if (h == 1) {  // 16 * code (make_a): exact multiples of 16
+                    lo0 >>= 4;
+                    hi0 >>= 4;
+                    lo1 >>= 4;
+                    hi1 >>= 4;
                 }
-            }
-#pragma unroll
-        for (int hh = 0; hh < HB; hh++) {
-            const int h = h0 + hh;
-#pragma unroll
-            for (int t = 0; t < NT; t++) {
-                // digit pairs: lo = d1*2^8 + d0, hi = d3*2^8 + d2 (each exact in s32)
-                int lo0 = da[h][t][1] * 256 + da[h][t][0], hi0 = db[h][t][1] * 256 + db[h][t][0];  // row r
-                int lo1 = da[h][t][3] * 256 + da[h][t][2], hi1 = db[h][t][3] * 256 + db[h][t][2];  // row r + 8
-                const int2 sx = *reinterpret_cast<const int2 *>(sint + (t * s_stride + 2 * g + h) * 2);
-                if (DT == GGUF_Q4_K) {
-                    if (h == 1) {  // 16 * code (make_a): exact multiples of 16
-                        lo0 >>= 4;
-                        hi0 >>= 4;
-                        lo1 >>= 4;
-                        hi1 >>= 4;
-                    }
-                    iq[t][0][0] += sc[0][h] * lo0;
-                    iq[t][0][1] += sc[0][h] * hi0;
-                    iq[t][1][0] += sc[1][h] * lo1;
-                    iq[t][1][1] += sc[1][h] * hi1;
-                    im[t][0][0] += mn[0][h] * sx.x;
-                    im[t][0][1] += mn[0][h] * sx.y;
-                    im[t][1][0] += mn[1][h] * sx.x;
-                    im[t][1][1] += mn[1][h] * sx.y;
-                } else {
-                    if (DT == GGUF_Q4_0) {  // sum (n - 8) X = sum n X - 8 sum X, per digit pair
-                        lo0 -= 8 * sx.x;
-                        lo1 -= 8 * sx.x;
-                        hi0 -= 8 * sx.y;
-                        hi1 -= 8 * sx.y;
-                    }
-                    // isc[t] (a power of two) turns the chunk's fixed point back into x
-                    const double v0 = fma((double)hi0, 65536.0, (double)lo0);
-                    const double v1 = fma((double)hi1, 65536.0, (double)lo1);
-                    acc[t][0] = fma((double)(ds[h][0] * isc[t]), v0, acc[t][0]);
-                    acc[t][1] = fma((double)(ds[h][1] * isc[t]), v1, acc[t][1]);
+                iq[t][0][0] += sc[0][h] * lo0;
+                iq[t][0][1] += sc[0][h] * hi0;
+                iq[t][1][0] += sc[1][h] * lo1;
+                iq[t][1][1] += sc[1][h] * hi1;
+                im[t][0][0] += mn[0][h] * sx.x;
+                im[t][0][1] += mn[0][h] * sx.y;
+                im[t][1][0] += mn[1][h] * sx.x;
+                im[t][1][1] += mn[1][h] * sx.y;
+            } else {
+                if (DT == GGUF_Q4_0) {  // sum (n - 8) X = sum n X - 8 sum X, per digit pair
+                    lo0 -= 8 * sx.x;
+                    lo1 -= 8 * sx.x;
+                    hi0 -= 8 * sx.y;
+                    hi1 -= 8 * sx.y;
                 }
+                // isc[t] (a power of two) turns the chunk's fixed point back into x
+                const double v0 = fma((double)hi0, 65536.0, (double)lo0);
+                const double v1 = fma((double)hi1, 65536.0, (double)lo1);
+                acc[t][0] = fma((double)(ds[h][0] * isc[t]), v0, acc[t][0]);
+                acc[t][1] = fma((double)(ds[h][1] * isc[t]), v1, acc[t][1]);
             }
         }
     }
@@ -796,50 +819,43 @@ __global__ void __launch_bounds__(kWarps * 32, 1) gemv_kernel(GemvArgs p) {
     // (consecutive chunks of a run are consecutive in memory)
     const uint8_t *rsrc = first < nu ? tile_src(p, T0 + issue.tile, issue.chunk, CB) : nullptr;
     uint32_t rleft = issue.left;
-    // Segments: this warp's units of one run each.
-    UnitIter un;  // first unit of the current segment
-    if (nu > 0) un.init(u0, sp);
-    int done = 0;
-    for (int seg_k = 0; done < nu; seg_k++) {
-        const int seg_len = min(nu - done, (int)un.left);
-        const int j0 = un.chunk - wlo;
-        for (int e = 0; e < seg_len; e++) {
-            if (!mbar_wait_bounded(mb0 + 8 * slt, phase)) {
-                failed_at = done + e;
-                break;
-            }
-            const int j = j0 + e;
-            ChunkRegs<DT> cur;
-            load_chunk<DT>(cur, myring + slt * CB, lane, hw);
-            __syncwarp();
-            if (done + e + S < nu) {  // refill the slot (lane 0; the branch is warp-uniform)
-                // this slot's reads happen before the copy that refills it
-                bulk_refill(lane == 0, ring0 + slt * CB, rsrc, CB, mb0 + 8 * slt);
-                issued++;
-                rsrc += CB;
-                if (--rleft == 0 && done + e + S + 1 < nu) {
-                    issue.next_run(sp);
-                    rsrc = tile_src(p, T0 + issue.tile, issue.chunk, CB);
-                    rleft = issue.left;
-                }
-            }
-            const uint2 *bp[NT];
-            float isc[NT];
-#pragma unroll
-            for (int t = 0; t < NT; t++) {
-                bp[t] = bact ? tbl + (size_t)(t * nwin + j) * 128 + boff : zero;
-                isc[t] = inv[t * nwin + j];
-            }
-            process_chunk<DT, NT>(cur, acc, bp, sint + j * 16, nwin * 8, isc, hsh, lane);
-            if (++slt == S) {
-                slt = 0;
-                phase ^= 1u;
+    // After unit i's slot is read: refill it with unit i + S (lane 0; the
+    // branch is warp-uniform) and step to the next slot.
+    auto refill = [&](int i) {
+        if (i + S < nu) {
+            // this slot's reads happen before the copy that refills it
+            bulk_refill(lane == 0, ring0 + slt * CB, rsrc, CB, mb0 + 8 * slt);
+            issued++;
+            rsrc += CB;
+            if (--rleft == 0 && i + S + 1 < nu) {
+                issue.next_run(sp);
+                rsrc = tile_src(p, T0 + issue.tile, issue.chunk, CB);
+                rleft = issue.left;
             }
         }
-        if (failed_at < nu) break;
-        // the segment's row sums: add the four column groups (lanes 4r .. 4r+3)
+        if (++slt == S) {
+            slt = 0;
+            phase ^= 1u;
+        }
+    };
+    auto table_bp = [&](int j, const uint2 *(&bp)[NT]) {
+#pragma unroll
+        for (int t = 0; t < NT; t++) bp[t] = bact ? tbl + (size_t)(t * nwin + j) * 128 + boff : zero;
+    };
+    auto table_isc = [&](int j, float (&isc)[NT]) {
+#pragma unroll
+        for (int t = 0; t < NT; t++) isc[t] = inv[t * nwin + j];
+    };
+    // Segments: this warp's units of one run each; the current one starts at
+    // chunk seg_c0 of run un.run and has seg_len units, seg_left still to end.
+    UnitIter un;
+    if (nu > 0) un.init(u0, sp);
+    int seg_k = 0, seg_len = nu > 0 ? min(nu, (int)un.left) : 0, seg_left = seg_len, seg_c0 = un.chunk;
+    // the segment's row sums: add the four column groups (lanes 4r .. 4r+3)
+    // and send them to the tile's slot, or to y when the segment is the tile
+    auto end_segment = [&]() {
         const int seg_tile = un.tile;
-        const bool whole = sp.pw1 == 0 && seg_len == (int)sp.run_len(un.run) && un.chunk == sp.run_chunk0(un.run);
+        const bool whole = sp.pw1 == 0 && seg_len == (int)sp.run_len(un.run) && seg_c0 == sp.run_chunk0(un.run);
         const int owner = seg_tile % kClusterCtas;
         const uint32_t rb = map_shared(slot + ((size_t)gw * p.kmax + sp.slot_of(seg_k)) * NT * 16, (uint32_t)owner);
 #pragma unroll
@@ -864,8 +880,104 @@ __global__ void __launch_bounds__(kWarps * 32, 1) gemv_kernel(GemvArgs p) {
             }
             acc[t][0] = acc[t][1] = 0.0;
         }
-        done += seg_len;
-        if (done < nu) un.next_run(sp);
+    };
+    if constexpr (NT == 1) {
+        // A one-chunk pipeline: unit i's epilogue runs beside unit i + 1's MMAs.
+        int jcur = un.chunk - wlo;  // table index of the unit in `cur`
+        ChunkRegs<DT> cur;
+        ChunkSums<NT> sums;
+        if (nu > 0) {
+            if (mbar_wait_bounded(mb0 + 8 * slt, phase)) {
+                load_chunk<DT>(cur, myring + slt * CB, lane, hw);
+                __syncwarp();
+                refill(0);
+                const uint2 *bp[NT];
+                table_bp(jcur, bp);
+                chunk_mma<DT, NT>(cur, bp, sums);
+            } else {
+                failed_at = 0;
+            }
+        }
+        for (int i = 0; i + 1 < nu && failed_at == nu; i++) {
+            const bool seg_end = seg_left == 1;
+            const int jn = seg_end ? sp.run_chunk0(un.run + 1) - wlo : jcur + 1;
+            if (!mbar_wait_bounded(mb0 + 8 * slt, phase)) {
+                failed_at = i + 1;
+                break;
+            }
+            ChunkRegs<DT> nxt;
+            load_chunk<DT>(nxt, myring + slt * CB, lane, hw);
+            __syncwarp();
+            refill(i + 1);
+            {
+                float isc[NT];
+                table_isc(jcur, isc);
+                chunk_epilogue<DT, NT>(cur, sums, acc, sint + jcur * 16, nwin * 8, isc, hsh, lane);
+            }
+            ChunkSums<NT> nsums;
+            {
+                const uint2 *bp[NT];
+                table_bp(jn, bp);
+                chunk_mma<DT, NT>(nxt, bp, nsums);
+            }
+            if (seg_end) {
+                end_segment();
+                seg_k++;
+                un.next_run(sp);
+                seg_len = min(nu - (i + 1), (int)un.left);
+                seg_left = seg_len;
+                seg_c0 = un.chunk;
+            } else {
+                seg_left--;
+            }
+            cur = nxt;
+            sums = nsums;
+            jcur = jn;
+        }
+        if (failed_at == nu && nu > 0) {
+            float isc[NT];
+            table_isc(jcur, isc);
+            chunk_epilogue<DT, NT>(cur, sums, acc, sint + jcur * 16, nwin * 8, isc, hsh, lane);
+            end_segment();
+        }
+    } else {
+        // one chunk at a time (more tokens leave no registers for a pipeline)
+        int j = un.chunk - wlo;
+        for (int i = 0; i < nu; i++) {
+            if (!mbar_wait_bounded(mb0 + 8 * slt, phase)) {
+                failed_at = i;
+                break;
+            }
+            ChunkRegs<DT> cur;
+            load_chunk<DT>(cur, myring + slt * CB, lane, hw);
+            __syncwarp();
+            refill(i);
+            ChunkSums<NT> sums;
+            {
+                const uint2 *bp[NT];
+                table_bp(j, bp);
+                chunk_mma<DT, NT>(cur, bp, sums);
+            }
+            {
+                float isc[NT];
+                table_isc(j, isc);
+                chunk_epilogue<DT, NT>(cur, sums, acc, sint + j * 16, nwin * 8, isc, hsh, lane);
+            }
+            if (seg_left == 1) {
+                end_segment();
+                if (i + 1 < nu) {
+                    seg_k++;
+                    un.next_run(sp);
+                    seg_len = min(nu - (i + 1), (int)un.left);
+                    seg_left = seg_len;
+                    seg_c0 = un.chunk;
+                    j = un.chunk - wlo;
+                }
+            } else {
+                seg_left--;
+                j++;
+            }
+        }
     }
     if (failed_at < nu) {
         // Report, then let this warp's copies in flight (numbers failed_at ..
@@ -1058,7 +1170,7 @@ cudaError_t launch_gemv_group(int dt, const GemvGroup &grp, const float *x, size
     a.g = g;
     a.ldx = ldx;
     a.stages = plan.stages;
-    a.pre = plan.stages;
+    a.pre = plan.stages < 2 ? plan.stages : 2;
     a.n_clusters = plan.clusters;
     a.panels = plan.panels;
     a.win = plan.window;
