@@ -204,7 +204,7 @@ def run_reference(args, rank, world):
 def config_dict(args, world):
     return {"workload": "llama3-8b-shaped Q4_K decode matmul stack (configs[3])", "layers": args.layers,
             "batch": args.batch, "matmuls_per_step": 7 * args.layers,
-            "launches_per_layer": (len(GROUPS) if world == 1 and not args.no_group else 7), "weight_bytes": layer_bytes() * args.layers,
+            "launches_per_layer": (len(GROUPS) if not args.no_group else 7), "weight_bytes": layer_bytes() * args.layers,
             "parallelism": f"row-shard x{world} + all-gather" if world > 1 else "single GPU",
             "l2": "no flush: weights 3.9 GB >> 126 MB L2" if args.layers >= 8 else "small stack (profiling)"}
 
@@ -452,18 +452,22 @@ def main():
         for name, n, _ in LAYER:
             pg.output(name, m, n)
     stream = torch.cuda.Stream(dev)
-    grouped = world == 1 and not args.no_group
-    launches_per_step = (len(GROUPS) if grouped else 7) * args.layers + (8 if world > 1 else 0)
+    grouped = not args.no_group
+    per_layer = len(GROUPS) if grouped else 7
+    launches_per_step = per_layer * args.layers + (8 if world > 1 else 0)
 
     def step():
         if world > 1:
-            pg.begin_step(7 * args.layers, stream=stream)
+            pg.begin_step(per_layer * args.layers, stream=stream)
         for mats in layers:
             if grouped:
                 by = {name: (ns, k, w) for name, ns, k, w in mats}
                 for grp in GROUPS:
                     k = by[grp[0]][1]
-                    if len(grp) == 1:
+                    if world > 1:
+                        pg.mm_multi(xs[k], [by[nm][2] for nm in grp], list(grp), [rank * by[nm][0] for nm in grp],
+                                    stream=stream)
+                    elif len(grp) == 1:
                         R.mm_batched_device(xs[k], by[grp[0]][2], ys[grp[0]], stream=stream)
                     else:
                         R.mm_multi_device(xs[k], [by[nm][2] for nm in grp], [ys[nm] for nm in grp], stream=stream)
@@ -597,7 +601,7 @@ def main():
                 e1.record(stream)
             e1.synchronize()
             avg_ms = e0.elapsed_time(e1) / (reps * args.layers)
-            dims = {nm: (n, k) for nm, n, k in LAYER}
+            dims = {nm: (n // world, k) for nm, n, k in LAYER}  # this GPU's shards
             alg = sum(q4k_bytes(dims[nm][0], dims[nm][1]) + 4 * m * dims[nm][0] for nm in grp) + 4 * m * dims[grp[0]][1]
             groups["+".join(grp)] = {"avg_us": round(avg_ms * 1e3, 2), "gbs": round(alg / (avg_ms / 1e3) / 1e9, 1)}
             del g_t

@@ -206,6 +206,17 @@ int rce_qmm_mm_batched_device_gather(rce_qmm_ctx *ctx, const float *d_a, size_t 
                                      const rce_qmm_weight *w, int world, int rank, int64_t row_offset,
                                      float *d_y, size_t ldy, unsigned long long *const *d_ll, unsigned epoch,
                                      const unsigned *d_epoch_base, void *stream);
+/* rce_qmm_mm_batched_device_gather for 1..4 weights that share their
+ * activations (one launch, as rce_qmm_mm_batched_device_multi): weight i's
+ * rows go to d_ys[i] (+ row_offsets[i], leading dimension ldys[i]) and, as
+ * {value, epoch} words, to every other rank's receive buffer
+ * d_lls[i * world + r].  One epoch for all the outputs of the call. */
+int rce_qmm_mm_batched_device_multi_gather(rce_qmm_ctx *ctx, const float *d_a, size_t lda, size_t t_rows,
+                                           const rce_qmm_weight *const *ws, size_t n_w, int world, int rank,
+                                           const int64_t *row_offsets, float *const *d_ys, const size_t *ldys,
+                                           unsigned long long *const *d_lls, unsigned epoch,
+                                           const unsigned *d_epoch_base, void *stream);
+
 /* Complete a gathered output on this rank: wait (bounded, 1 s; an expired
  * wait sets the device error word) until every word of d_ll in rows
  * [0, t_rows) and columns [0, n) outside this rank's [own0, own1) carries

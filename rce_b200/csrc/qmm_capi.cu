@@ -660,6 +660,79 @@ int rce_qmm_mm_batched_device_gather(rce_qmm_ctx *ctx, const float *d_a, size_t 
     return ok();
 }
 
+int rce_qmm_mm_batched_device_multi_gather(rce_qmm_ctx *ctx, const float *d_a, size_t lda, size_t t_rows,
+                                           const rce_qmm_weight *const *ws, size_t n_w, int world, int rank,
+                                           const int64_t *row_offsets, float *const *d_ys, const size_t *ldys,
+                                           unsigned long long *const *d_lls, unsigned epoch,
+                                           const unsigned *d_epoch_base, void *stream) {
+    if (!ctx) return fail(RCE_QMM_ERR_INVALID, "mm_batched_device_multi_gather: null ctx");
+    if (!ws || !row_offsets || !d_ys || !ldys || !d_lls || n_w < 1 || n_w > (size_t)rce::kGemvMaxGroup)
+        return fail(RCE_QMM_ERR_INVALID, "mm_batched_device_multi_gather: need 1..%d weights with offsets, outputs, "
+                    "strides and receive buffers", rce::kGemvMaxGroup);
+    if (world < 2 || world > rce::kMaxPeers || rank < 0 || rank >= world)
+        return fail(RCE_QMM_ERR_INVALID, "mm_batched_device_multi_gather: world %d (2..%d), rank %d", world,
+                    rce::kMaxPeers, rank);
+    if (epoch == 0 && !d_epoch_base) return fail(RCE_QMM_ERR_INVALID, "mm_batched_device_multi_gather: epoch 0");
+    for (size_t i = 0; i < n_w; i++) {
+        int rc = check_weight(ws[i]);
+        if (rc) return rc;
+        if (ws[i]->ctx != ctx)
+            return fail(RCE_QMM_ERR_INVALID, "mm_batched_device_multi_gather: weight %zu of another context", i);
+        if (ws[i]->dtype != ws[0]->dtype || ws[i]->g.n_cols != ws[0]->g.n_cols)
+            return fail(RCE_QMM_ERR_INVALID, "mm_batched_device_multi_gather: weight %zu differs in dtype or k", i);
+        if (!d_ys[i] || row_offsets[i] < 0 || ldys[i] < (size_t)(row_offsets[i] + ws[i]->g.n_rows))
+            return fail(RCE_QMM_ERR_INVALID, "mm_batched_device_multi_gather: output %zu null or ldy < row_offset + n", i);
+        for (int r = 0; r < world; r++)
+            if (r != rank && !d_lls[i * world + r])
+                return fail(RCE_QMM_ERR_INVALID, "mm_batched_device_multi_gather: null receive buffer %zu/%d", i, r);
+    }
+    if (t_rows == 0) return ok();
+    if (!d_a || lda < (size_t)ws[0]->g.n_cols)
+        return fail(RCE_QMM_ERR_INVALID, "mm_batched_device_multi_gather: null activations or lda < k");
+    DeviceGuard dg(ctx->device);
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    rce::GatherArgs ga[rce::kGemvMaxGroup];
+    for (size_t i = 0; i < n_w; i++) {
+        ga[i].world = world;
+        ga[i].rank = rank;
+        ga[i].row_off = row_offsets[i];
+        for (int r = 0; r < world; r++) ga[i].ll[r] = d_lls[i * world + r];
+        ga[i].epoch = epoch;
+        ga[i].epoch_base = d_epoch_base;
+    }
+    if (ctx->prefill_min_tokens > 0 && t_rows >= (size_t)ctx->prefill_min_tokens && t_rows <= (size_t)INT32_MAX) {
+        // the tensor-core GEMM per weight, each output pushed to the peers after it
+        for (size_t i = 0; i < n_w; i++) {
+            int rc = run_matmul(ctx, ws[i], d_a, lda, t_rows, d_ys[i] + row_offsets[i], ldys[i], s);
+            if (rc) return rc;
+            CUDA_TRY(rce::launch_gather_push(ga[i], d_ys[i], (int)t_rows, ws[i]->g.n_rows, ldys[i], s));
+        }
+        return ok();
+    }
+    rce::GemvGroup grp;
+    grp.n = (int)n_w;
+    for (size_t i = 0; i < n_w; i++) {
+        grp.w[i] = ws[i]->dev;
+        grp.g[i] = ws[i]->g;
+        grp.ldy[i] = ldys[i];
+    }
+    const rce::Geometry gg = rce::group_geometry(grp);
+    for (size_t t0 = 0; t0 < t_rows;) {
+        const size_t left = t_rows - t0;
+        const int m = (int)(left < (size_t)rce::kGemvMaxTokens ? left : (size_t)rce::kGemvMaxTokens);
+        const rce::GemvPlan plan = rce::plan_gemv(ws[0]->dtype, gg, m, ctx->sm_count);
+        rce::GatherArgs gp[rce::kGemvMaxGroup];
+        for (size_t i = 0; i < n_w; i++) {
+            grp.y[i] = d_ys[i] + row_offsets[i] + t0 * ldys[i];
+            gp[i] = ga[i];
+            for (int r = 0; r < world; r++) gp[i].ll[r] = ga[i].ll[r] ? ga[i].ll[r] + t0 * ldys[i] : nullptr;
+        }
+        CUDA_TRY(rce::launch_gemv_group(ws[0]->dtype, grp, d_a + t0 * lda, lda, m, plan, ctx->err_dev, s, gp));
+        t0 += (size_t)m;
+    }
+    return ok();
+}
+
 int rce_qmm_peer_unpack(rce_qmm_ctx *ctx, const unsigned long long *d_ll, float *d_y, size_t ldy, size_t t_rows,
                         int64_t n, int64_t own0, int64_t own1, unsigned epoch, const unsigned *d_epoch_base,
                         void *stream) {

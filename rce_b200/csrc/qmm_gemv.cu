@@ -92,7 +92,7 @@ struct GemvArgs {
     int tiles_base, tiles_extra;   // clusters c < tiles_extra hold tiles_base + 1 tiles
     FastDiv fd_pw0, fd_pw1, fd_u[2];  // division by the run lengths and by the units of a cluster (base, base + 1)
     int win, kmax;   // shared-memory maxima: table chunks, slots per warp
-    GatherArgs ga;   // fused all-gather over peer memory (ga.world > 1)
+    GatherArgs ga[kGemvMaxGroup];  // fused all-gather over peer memory (ga[0].world > 1), per weight
 };
 
 // ---- PTX helpers ---------------------------------------------------------------
@@ -224,7 +224,8 @@ __device__ __forceinline__ void put_y(const GemvArgs &p, int t, int tile, int r,
     const int64_t row = (int64_t)(tile - p.tile0[wi]) * 16 + r;
     if (row >= p.n_rows[wi]) return;
     p.y[wi][t * p.ldy[wi] + row] = v;
-    if (p.ga.world > 1) gather_send(p.ga, (size_t)t * p.ldy[0] + (size_t)p.ga.row_off + (size_t)row, v, epoch);
+    if (p.ga[0].world > 1)
+        gather_send(p.ga[wi], (size_t)t * p.ldy[wi] + (size_t)p.ga[wi].row_off + (size_t)row, v, epoch);
 }
 
 template <int DT>
@@ -693,7 +694,7 @@ __global__ void __launch_bounds__(kWarps * 32, 1) gemv_kernel(GemvArgs p) {
     if (tid < 256) reinterpret_cast<uint32_t *>(smem + L.zero)[tid] = 0u;  // 1 KB
     // The activations may be the previous kernel's output: wait for it.
     asm volatile("griddepcontrol.wait;" ::: "memory");
-    const unsigned gepoch = p.ga.world > 1 ? gather_epoch(p.ga) : 0u;
+    const unsigned gepoch = p.ga[0].world > 1 ? gather_epoch(p.ga[0]) : 0u;
 
     // Activation table: warp item (token t, window chunk j); lane = group gg
     // (64 columns) x step s (8 columns).  The chunk's power of two comes from
@@ -1147,7 +1148,7 @@ cudaError_t launch_gemv_group(int dt, const GemvGroup &grp, const float *x, size
                               const GemvPlan &plan, int *err, cudaStream_t s, const GatherArgs *ga) {
     if (m <= 0) return cudaSuccess;
     if (m > kGemvMaxTokens || plan.nt < 1 || grp.n < 1 || grp.n > kGemvMaxGroup) return cudaErrorInvalidValue;
-    if (ga && (ga->world > kMaxPeers || (ga->world > 1 && grp.n != 1))) return cudaErrorInvalidValue;
+    if (ga && ga[0].world > kMaxPeers) return cudaErrorInvalidValue;
     const Geometry g = group_geometry(grp);
     // 32-bit unit arithmetic in the kernel (numerators < 2^31)
     if (plan.smem > 227 * 1024 || (uint64_t)g.n_tiles * g.n_chunks >= (1ull << 25)) return cudaErrorNotSupported;
@@ -1191,9 +1192,11 @@ cudaError_t launch_gemv_group(int dt, const GemvGroup &grp, const float *x, size
         for (int i = 0; i < kGemvMaxGroup; i++) a.y[i] = ybase[i] + (size_t)t0 * a.ldy[i];
         a.m = m - t0 < plan.nt ? m - t0 : plan.nt;
         if (ga) {
-            a.ga = *ga;
-            for (int r = 0; r < ga->world; r++)
-                if (a.ga.ll[r]) a.ga.ll[r] += (size_t)t0 * a.ldy[0];
+            for (int i = 0; i < grp.n; i++) {
+                a.ga[i] = ga[i];
+                for (int r = 0; r < ga[i].world; r++)
+                    if (a.ga[i].ll[r]) a.ga[i].ll[r] += (size_t)t0 * a.ldy[i];
+            }
         }
         cudaError_t e;
         switch (dt) {

@@ -56,8 +56,9 @@ cudaError_t launch_gemv(int dt, const uint8_t *tiles, const Geometry &g, const f
 // launch, each into its own output (y[i]: [m][ldy[i]]).  The grid splits the
 // weights' tiles as one matrix, so small matrices sharing an activation
 // (attention q, k, v; FFN gate, up) cost one launch.  Plan it with
-// plan_gemv(dt, group_geometry(grp), m, sm_count).  A gathered output (ga
-// with world > 1) takes one weight only.
+// plan_gemv(dt, group_geometry(grp), m, sm_count).  Gathered outputs: ga
+// holds one GatherArgs per weight (same world, rank and epoch; each its own
+// row offset and receive buffers), or is null.
 constexpr int kGemvMaxGroup = 4;
 struct GemvGroup {
     int n = 0;

@@ -114,6 +114,40 @@ class PeerGroup:
             o[6] = epoch
         return epoch
 
+    def mm_multi(self, x, weights, names, row_offsets, stream=None) -> int:
+        """mm() for 1-4 row shards that read the same x (weights of one dtype
+        and K, e.g. attention q, k, v), in one launch
+        (rce_qmm_mm_batched_device_multi_gather): shard i into output
+        names[i] at row_offsets[i].  One epoch for all the outputs (returned;
+        gather() each name as usual)."""
+        weights, names, row_offsets = list(weights), list(names), [int(r) for r in row_offsets]
+        if not (1 <= len(weights) <= 4 and len(names) == len(weights) == len(row_offsets)):
+            raise ValueError("mm_multi takes 1 to 4 weights, one output name and row offset each")
+        outs = []
+        for w, name, r0 in zip(weights, names, row_offsets):
+            _check_weight(w)
+            o = self.outputs[name]
+            if x.shape[0] > o[2] or x.shape[1] != w.n_cols or r0 + w.n_rows > o[3]:
+                raise ValueError(f"shape mismatch with the gathered output {name}")
+            outs.append(o)
+        epoch, base = self._next_epoch()
+        n = len(weights)
+        hs = (ctypes.c_void_p * n)(*[w.handle for w in weights])
+        offs = (ctypes.c_int64 * n)(*row_offsets)
+        ys = (ctypes.c_void_p * n)(*[o[0].data_ptr() for o in outs])
+        lds = (ctypes.c_size_t * n)(*[o[3] for o in outs])
+        lls = (ctypes.c_void_p * (n * self.world))(*[o[1][r] for o in outs for r in range(self.world)])
+        check(lib().rce_qmm_mm_batched_device_multi_gather(
+            self.ctx.handle, ctypes.c_void_p(x.data_ptr()), x.stride(0), x.shape[0], hs, n, self.world, self.rank,
+            offs, ys, lds, lls, epoch, base, _stream_handle(stream, x.device)))
+        for o, w, r0 in zip(outs, weights, row_offsets):
+            o[4], o[5] = r0, r0 + w.n_rows
+            if len(o) == 6:
+                o.append(epoch)
+            else:
+                o[6] = epoch
+        return epoch
+
     def gather(self, name: str, epoch: Optional[int] = None, t_rows: Optional[int] = None, stream=None):
         """Complete output `name` on this rank: wait (on `stream`, bounded)
         for the other ranks' rows of the call with `epoch` (default: the

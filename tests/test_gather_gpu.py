@@ -5,7 +5,9 @@ rank's gathered output must equal, bit for bit, the concatenation of each
 shard's own matmul (same shapes, same kernels); a second matmul reading the
 first's gathered output, the tensor-core GEMM route (20 tokens, shard pushed
 to the peers after the GEMM), and a second round through the same buffers
-(new epochs), likewise.  Skipped with fewer than two GPUs."""
+(new epochs), likewise; and two shards sharing x gathered from one grouped
+launch (rce_qmm_mm_batched_device_multi_gather) against each rank's grouped
+device call, at 1, 3 and 20 tokens.  Skipped with fewer than two GPUs."""
 import os
 import socket
 
@@ -71,6 +73,25 @@ def _rank_main(rank, world, port, q):
                           bool(np.array_equal(got2, want2.cpu().numpy())))
                 dist.barrier()  # a peer may not overwrite y2's words before this rank has read them
             res[tag] = tuple(ok)
+        # grouped: two shards sharing x in one launch (q/k/v-style), two rounds
+        w3 = synth.weights(dt, 512, k, np.random.default_rng(7))
+        s3 = shards(w3, 512, k)
+        okg = []
+        for t_rows in (1, 3, 20):
+            pg.output(f"ga{t_rows}", t_rows, n1)
+            pg.output(f"gb{t_rows}", t_rows, 512)
+            for rnd in range(2):
+                x = torch.from_numpy(synth.activations(t_rows, k, np.random.default_rng(50 + t_rows + rnd))).cuda()
+                pg.mm_multi(x, [s1[rank][1], s3[rank][1]], [f"ga{t_rows}", f"gb{t_rows}"], [s1[rank][0], s3[rank][0]])
+                ya, yb = pg.gather(f"ga{t_rows}"), pg.gather(f"gb{t_rows}")
+                torch.cuda.synchronize()
+                got_a, got_b = ya.cpu().numpy(), yb.cpu().numpy()
+                per = [R.mm_multi_device(x, [s1[r][1], s3[r][1]]) for r in range(world)]
+                want_a = torch.cat([p_[0] for p_ in per], dim=1).cpu().numpy()
+                want_b = torch.cat([p_[1] for p_ in per], dim=1).cpu().numpy()
+                okg.append(bool(np.array_equal(got_a, want_a)) and bool(np.array_equal(got_b, want_b)))
+                dist.barrier()
+        res["group"] = tuple(okg)
         res["device_error"] = ctx.device_error()
         dist.barrier()
     except Exception as e:  # reported to the parent, never a hang
@@ -106,4 +127,5 @@ def test_fused_gather_two_gpus():
         assert "error" not in res[r], res[r]
         assert res[r]["gemv"] == (True, True), res
         assert res[r]["gemm"] == (True, True), res
+        assert res[r]["group"] == (True,) * 6, res
         assert res[r]["device_error"] == 0
