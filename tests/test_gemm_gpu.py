@@ -55,7 +55,8 @@ def test_prefill_threshold_option(ctx):
 
 
 @pytest.mark.parametrize("dt", [Q4_K, Q4_0, Q8_0])
-@pytest.mark.parametrize("n,k,m", [(128, 256, 16), (200, 1024, 17), (1000, 4096, 40), (300, 2048, 256),
+@pytest.mark.parametrize("n,k,m", [(128, 256, 16), (200, 1024, 17), (1000, 4096, 40), (2048, 4096, 64),
+                                   (520, 14336, 100), (300, 2048, 128), (300, 2048, 256),
                                    (513, 1024, 300), (256, 4096, 512), (384, 2048, 600), (144, 1024, 1100)])
 def test_gemm_against_oracle(ctx, dt, n, k, m):
     if dt != Q4_K and k % 256:
@@ -67,6 +68,26 @@ def test_gemm_against_oracle(ctx, dt, n, k, m):
     assert ctx.device_error() == 0
     want = O.mm_batched(x, m, w, dt, n, k, nthreads=8)
     check(got, want, f"dtype {dt} {n}x{k} m={m}")
+
+
+def test_small_m_repeatable_between_large_calls(ctx):
+    # a small batch gives the same bits on every call, also when a large
+    # batch on the same stream reuses the per-stream workspace in between
+    import torch
+
+    n, k = 4096, 4096
+    w, _, _, _, x = refcases.seeded_case(Q4_K, n, k, 300, 31)
+    qw = R.QuantWeight.from_owned_bytes(w, Q4_K, n, k, ctx=ctx)
+    xs = torch.from_numpy(x[:24]).cuda()
+    xl = torch.from_numpy(x).cuda()
+    first = R.mm_batched_device(xs, qw).cpu().numpy()
+    for _ in range(3):
+        R.mm_batched_device(xl, qw)
+        again = R.mm_batched_device(xs, qw).cpu().numpy()
+        assert np.array_equal(first, again)
+    assert ctx.device_error() == 0
+    want = O.mm_batched(x[:24], 24, w, Q4_K, n, k, nthreads=8)
+    check(first, want, "small-M 4096x4096 m=24")
 
 
 def test_gemm_against_torch_fp32(ctx):
