@@ -2,7 +2,7 @@
 Q8_0, Q4_0 and Q4_K formats, a drop-in for the reference crate rce-op-qmm's
 operator API.  Compute runs in librce_qmm.so (include/rce_qmm.h); this
 package is the host-side mirror of the reference interface."""
-from .gguf import GgufDtype, tensor_byte_size  # noqa: F401
+from .gguf import GgufDtype, GgufFile, GgufParseError, tensor_byte_size  # noqa: F401
 from .qmm import (  # noqa: F401
     Context,
     CudaQmm,
