@@ -235,38 +235,45 @@ def prefill_section(args, rank, world, dev, stream, ctx, pg=None):
         g.manual_seed(2)
         x = torch.randn((m, PREFILL_K), device=dev, generator=g)
         y = torch.empty((m, ns), device=dev)
+        names = [f"prefill{m}_{i}" for i in range(len(ws))]
         if world > 1:
-            pg.output(f"prefill{m}", m, PREFILL_N)
+            for nm in names:
+                pg.output(nm, m, PREFILL_N)
 
         def one():
-            for w in ws:
-                if world > 1:
-                    pg.mm(x, w, f"prefill{m}", rank * ns, stream=stream)
-                    pg.gather(f"prefill{m}", stream=stream)
-                else:
+            if world > 1:
+                # every shard's matmul first, then the gathers: weight i's
+                # outputs cross NVLink while weight i + 1's GEMM runs
+                pg.begin_step(len(ws), stream=stream)
+                for w, nm in zip(ws, names):
+                    pg.mm(x, w, nm, rank * ns, stream=stream)
+                for nm in names:
+                    pg.gather(nm, stream=stream)
+            else:
+                for w in ws:
                     R.mm_batched_device(x, w, y, stream=stream)
 
         with torch.cuda.stream(stream):
             for _ in range(3):
                 one()
         stream.synchronize()
-        graph = None
-        if world == 1:
-            graph = torch.cuda.CUDAGraph()
-            with torch.cuda.graph(graph, stream=stream):
-                one()
+        if world > 1:
+            dist.barrier()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=stream):
+            one()
         reps = 20
         with torch.cuda.stream(stream):
             for _ in range(3):
-                graph.replay() if graph is not None else one()
+                graph.replay()
+            torch.cuda.synchronize(dev)
             if world > 1:
                 dist.barrier()
-            torch.cuda.synchronize(dev)
             e0 = torch.cuda.Event(enable_timing=True)
             e1 = torch.cuda.Event(enable_timing=True)
             e0.record(stream)
             for _ in range(reps):
-                graph.replay() if graph is not None else one()
+                graph.replay()
             e1.record(stream)
         e1.synchronize()
         ms = e0.elapsed_time(e1) / (reps * len(ws))
@@ -278,6 +285,8 @@ def prefill_section(args, rank, world, dev, stream, ctx, pg=None):
         out[f"m{m}"] = {"us": round(ms * 1e3, 2), "tflops": round(flops / (ms / 1e3) / 1e12, 1),
                         "path": "tcgen05 GEMM" if m >= ctx.prefill_min_tokens else "GEMV"}
         del graph
+    if pg is not None:
+        pg.end_step()
     return out
 
 

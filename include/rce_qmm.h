@@ -217,6 +217,26 @@ int rce_qmm_mm_batched_device_multi_gather(rce_qmm_ctx *ctx, const float *d_a, s
                                            unsigned long long *const *d_lls, unsigned epoch,
                                            const unsigned *d_epoch_base, void *stream);
 
+/* Bulk mode of the gathered matmul, for large outputs (prefill batches; no
+ * counterpart in the reference): the matmul per weight (the tensor-core
+ * GEMM from prefill_min_tokens tokens), then this rank's rows as plain f32
+ * into every other rank's bulk buffer d_bulks[i * world + r] at the same
+ * [t][ldys[i]] positions, then one flag per peer (slot `rank` of the u32
+ * flags at byte flag_offsets[i] of the peer's buffer, after the values)
+ * released at system scope with the call's epoch.  Half the NVLink bytes of
+ * the {value, epoch} words.  The receiver calls rce_qmm_peer_unpack_bulk. */
+int rce_qmm_mm_batched_device_multi_gather_bulk(rce_qmm_ctx *ctx, const float *d_a, size_t lda, size_t t_rows,
+                                                const rce_qmm_weight *const *ws, size_t n_w, int world, int rank,
+                                                const int64_t *row_offsets, float *const *d_ys, const size_t *ldys,
+                                                float *const *d_bulks, const size_t *flag_offsets, unsigned epoch,
+                                                const unsigned *d_epoch_base, void *stream);
+/* Wait (bounded) until every other rank's flag in this rank's bulk buffer
+ * carries the epoch (or a later one), then copy their rows (columns [0, n)
+ * except [own0, own1)) of the [t_rows][ldy] values into d_y. */
+int rce_qmm_peer_unpack_bulk(rce_qmm_ctx *ctx, const float *d_bulk, size_t flag_offset, float *d_y, size_t ldy,
+                             size_t t_rows, int64_t n, int64_t own0, int64_t own1, int world, int rank, unsigned epoch,
+                             const unsigned *d_epoch_base, void *stream);
+
 /* Complete a gathered output on this rank: wait (bounded, 1 s; an expired
  * wait sets the device error word) until every word of d_ll in rows
  * [0, t_rows) and columns [0, n) outside this rank's [own0, own1) carries

@@ -56,6 +56,10 @@ SIGNATURES = {
     "rce_qmm_mm_batched_device_multi": (_int, [_vp, _vp, _sz, _sz, _vp, _sz, _vp, _vp, _vp]),
     "rce_qmm_mm_batched_device_multi_gather": (_int, [_vp, _vp, _sz, _sz, _vp, _sz, _int, _int, _vp, _vp, _vp, _vp,
                                                       _c.c_uint, _vp, _vp]),
+    "rce_qmm_mm_batched_device_multi_gather_bulk": (_int, [_vp, _vp, _sz, _sz, _vp, _sz, _int, _int, _vp, _vp, _vp,
+                                                           _vp, _vp, _c.c_uint, _vp, _vp]),
+    "rce_qmm_peer_unpack_bulk": (_int, [_vp, _vp, _sz, _vp, _sz, _sz, _i64, _i64, _i64, _int, _int, _c.c_uint, _vp,
+                                        _vp]),
     "rce_qmm_dequant_row": (_int, [_vp, _vp, _i64, _f32p, _sz]),
     "rce_qmm_dequant_device": (_int, [_vp, _vp, _i64, _i64, _vp, _sz, _vp]),
     "rce_qmm_device_error": (_int, [_vp, _c.POINTER(_int), _int]),

@@ -733,6 +733,67 @@ int rce_qmm_mm_batched_device_multi_gather(rce_qmm_ctx *ctx, const float *d_a, s
     return ok();
 }
 
+int rce_qmm_mm_batched_device_multi_gather_bulk(rce_qmm_ctx *ctx, const float *d_a, size_t lda, size_t t_rows,
+                                                const rce_qmm_weight *const *ws, size_t n_w, int world, int rank,
+                                                const int64_t *row_offsets, float *const *d_ys, const size_t *ldys,
+                                                float *const *d_bulks, const size_t *flag_offsets, unsigned epoch,
+                                                const unsigned *d_epoch_base, void *stream) {
+    if (!ctx) return fail(RCE_QMM_ERR_INVALID, "mm_batched_device_multi_gather_bulk: null ctx");
+    if (!ws || !row_offsets || !d_ys || !ldys || !d_bulks || !flag_offsets || n_w < 1 ||
+        n_w > (size_t)rce::kGemvMaxGroup)
+        return fail(RCE_QMM_ERR_INVALID, "mm_batched_device_multi_gather_bulk: need 1..%d weights with offsets, "
+                    "outputs, strides, bulk buffers and flag offsets", rce::kGemvMaxGroup);
+    if (world < 2 || world > rce::kMaxPeers || rank < 0 || rank >= world)
+        return fail(RCE_QMM_ERR_INVALID, "mm_batched_device_multi_gather_bulk: world %d (2..%d), rank %d", world,
+                    rce::kMaxPeers, rank);
+    if (epoch == 0 && !d_epoch_base) return fail(RCE_QMM_ERR_INVALID, "mm_batched_device_multi_gather_bulk: epoch 0");
+    if (t_rows > 65535) return fail(RCE_QMM_ERR_INVALID, "mm_batched_device_multi_gather_bulk: t_rows > 65535");
+    for (size_t i = 0; i < n_w; i++) {
+        int rc = check_weight(ws[i]);
+        if (rc) return rc;
+        if (ws[i]->ctx != ctx)
+            return fail(RCE_QMM_ERR_INVALID, "mm_batched_device_multi_gather_bulk: weight %zu of another context", i);
+        if (ws[i]->g.n_cols != ws[0]->g.n_cols)
+            return fail(RCE_QMM_ERR_INVALID, "mm_batched_device_multi_gather_bulk: weight %zu differs in k", i);
+        if (!d_ys[i] || row_offsets[i] < 0 || ldys[i] < (size_t)(row_offsets[i] + ws[i]->g.n_rows) ||
+            flag_offsets[i] % 4 || flag_offsets[i] < t_rows * ldys[i] * sizeof(float))
+            return fail(RCE_QMM_ERR_INVALID, "mm_batched_device_multi_gather_bulk: output %zu null, ldy < row_offset "
+                        "+ n, or flags inside the values", i);
+        for (int r = 0; r < world; r++)
+            if (r != rank && !d_bulks[i * world + r])
+                return fail(RCE_QMM_ERR_INVALID, "mm_batched_device_multi_gather_bulk: null bulk buffer %zu/%d", i, r);
+    }
+    if (t_rows == 0) return ok();
+    if (!d_a || lda < (size_t)ws[0]->g.n_cols)
+        return fail(RCE_QMM_ERR_INVALID, "mm_batched_device_multi_gather_bulk: null activations or lda < k");
+    DeviceGuard dg(ctx->device);
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    for (size_t i = 0; i < n_w; i++) {
+        int rc = run_matmul(ctx, ws[i], d_a, lda, t_rows, d_ys[i] + row_offsets[i], ldys[i], s);
+        if (rc) return rc;
+        CUDA_TRY(rce::launch_gather_push_bulk(world, rank, d_bulks + i * world, flag_offsets[i], d_ys[i], (int)t_rows,
+                                              row_offsets[i], ws[i]->g.n_rows, ldys[i], epoch, d_epoch_base, s));
+    }
+    return ok();
+}
+
+int rce_qmm_peer_unpack_bulk(rce_qmm_ctx *ctx, const float *d_bulk, size_t flag_offset, float *d_y, size_t ldy,
+                             size_t t_rows, int64_t n, int64_t own0, int64_t own1, int world, int rank, unsigned epoch,
+                             const unsigned *d_epoch_base, void *stream) {
+    if (!ctx) return fail(RCE_QMM_ERR_INVALID, "peer_unpack_bulk: null ctx");
+    if (t_rows == 0) return ok();
+    if (!d_bulk || !d_y || n <= 0 || (size_t)n > ldy || own0 < 0 || own0 > own1 || own1 > n || t_rows > 65535 ||
+        flag_offset % 4 || flag_offset < t_rows * ldy * sizeof(float))
+        return fail(RCE_QMM_ERR_INVALID, "peer_unpack_bulk: bad buffers or ranges");
+    if (world < 2 || world > rce::kMaxPeers || rank < 0 || rank >= world)
+        return fail(RCE_QMM_ERR_INVALID, "peer_unpack_bulk: world %d, rank %d", world, rank);
+    if (epoch == 0 && !d_epoch_base) return fail(RCE_QMM_ERR_INVALID, "peer_unpack_bulk: epoch 0");
+    DeviceGuard dg(ctx->device);
+    CUDA_TRY(rce::launch_gather_unpack_bulk(d_bulk, flag_offset, d_y, (int)t_rows, n, ldy, own0, own1, world, rank,
+                                            epoch, d_epoch_base, ctx->err_dev, static_cast<cudaStream_t>(stream)));
+    return ok();
+}
+
 int rce_qmm_peer_unpack(rce_qmm_ctx *ctx, const unsigned long long *d_ll, float *d_y, size_t ldy, size_t t_rows,
                         int64_t n, int64_t own0, int64_t own1, unsigned epoch, const unsigned *d_epoch_base,
                         void *stream) {

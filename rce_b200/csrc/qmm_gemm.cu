@@ -671,7 +671,23 @@ cudaError_t launch_gemm(int dt, const uint8_t *tiles, const Geometry &g, const f
     prep_kernel<<<t_rows, 256, 0, s>>>(x, ldx, (int)g.n_cols, xh, inv);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return e;
-    const int bn = gemm_bn(dt, t_rows);
+    int bn = gemm_bn(dt, t_rows);
+    {
+        // a narrower token tile when the row blocks alone leave most SMs idle
+        // (row shards on several GPUs): more CTAs, each weight tile
+        // dequantised once per bn tokens instead of once per 512
+        static std::atomic<int> sms_cache[64];
+        int dev = 0, sms = 148;
+        if (cudaGetDevice(&dev) == cudaSuccess && dev >= 0 && dev < 64) {
+            sms = sms_cache[dev].load();
+            if (sms <= 0) {
+                if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) sms = 148;
+                sms_cache[dev].store(sms);
+            }
+        }
+        const long rbs = (g.n_tiles + 7) / 8;
+        while (bn > 64 && rbs * ((t_rows + bn - 1) / bn) * 10 < (long)sms * 6) bn /= 2;
+    }
     CUtensorMap map;
     const cuuint64_t dims[2] = {(cuuint64_t)g.n_cols, (cuuint64_t)t_rows};
     const cuuint64_t strides[1] = {(cuuint64_t)g.n_cols * 2};

@@ -82,6 +82,17 @@ cudaError_t launch_gather_unpack(const unsigned long long *ll, float *y, int t_r
                                  int64_t own0, int64_t own1, unsigned epoch, const unsigned *epoch_base, int *err,
                                  cudaStream_t s);
 cudaError_t launch_epoch_advance(unsigned *epoch_base, unsigned delta, cudaStream_t s);
+// Bulk mode (large outputs): push rows [row_off, row_off + n_own) of
+// y[t_rows][ldy] as plain f32 into every peer's bulk buffer (same
+// positions), then release flag slot `rank` of each peer's flags (at byte
+// flag_off of its buffer) with the call's epoch; unpack waits (bounded) for
+// every other rank's flag and copies their rows.
+cudaError_t launch_gather_push_bulk(int world, int rank, float *const *peer_bufs, size_t flag_off, const float *y,
+                                    int t_rows, int64_t row_off, int64_t n_own, size_t ldy, unsigned epoch,
+                                    const unsigned *epoch_base, cudaStream_t s);
+cudaError_t launch_gather_unpack_bulk(const float *buf, size_t flag_off, float *y, int t_rows, int64_t n, size_t ldy,
+                                      int64_t own0, int64_t own1, int world, int rank, unsigned epoch,
+                                      const unsigned *epoch_base, int *err, cudaStream_t s);
 
 // Prefill matmul on tcgen05 (fp16 operands, f32 accumulation in tensor
 // memory) for t_rows tokens at once.  `workspace` holds

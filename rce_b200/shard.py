@@ -1,7 +1,8 @@
 """Row sharding of the quantized matmul over the GPUs of one node, with the
 output all-gather fused into the matmul (NVLink stores of {value, epoch}
-words into peer-mapped receive buffers; librce_qmm.so's
-rce_qmm_mm_batched_device_gather and rce_qmm_peer_unpack).
+words into peer-mapped receive buffers, or for prefill batches plain values
+and one release flag per peer; librce_qmm.so's
+rce_qmm_mm_batched_device_multi_gather[_bulk] and rce_qmm_peer_unpack[_bulk]).
 
 Rows of a GGUF weight are independent -- the reference splits them over host
 threads with rayon (rce-op-qmm/src/lib.rs:502, 654, 742) -- so a row shard
@@ -33,12 +34,30 @@ def row_shards(n_rows: int, world: int) -> List[Tuple[int, int]]:
     return out
 
 
+BULK_MIN_TOKENS = 16  # outputs this tall also get a bulk buffer (plain values, one flag per peer)
+
+
+class _Output:
+    """One gathered output: this rank's full y, the peers' receive buffers
+    of {value, epoch} words, optionally the bulk buffers, and what the last
+    matmul into it was (its epoch, this rank's rows, the mode)."""
+
+    def __init__(self, y, ll, t_rows, n_rows, bulk=None, flag_off=0):
+        self.y, self.ll, self.t_rows, self.n_rows = y, ll, t_rows, n_rows
+        self.bulk, self.flag_off = bulk, flag_off
+        self.own0 = self.own1 = 0
+        self.epoch = None
+        self.bulk_mode = False
+
+
 class PeerGroup:
     """The buffers one rank shares with the others for gathered outputs: per
-    output name, this rank's full output (a torch tensor) and a receive
-    buffer of 8-byte {value, epoch} words that the other ranks write over
-    NVLink.  `exchange` is a callable (obj -> list of every rank's obj, in
-    rank order), e.g. torch_exchange()."""
+    output name, this rank's full output (a torch tensor), a receive buffer
+    of 8-byte {value, epoch} words that the other ranks write over NVLink
+    (decode-sized calls), and for outputs of BULK_MIN_TOKENS or more tokens
+    a bulk buffer of plain values plus one release flag per peer (prefill
+    calls; half the NVLink bytes).  `exchange` is a callable (obj -> list of
+    every rank's obj, in rank order), e.g. torch_exchange()."""
 
     def __init__(self, ctx: Context, world: int, rank: int, exchange):
         if not 2 <= world <= 8:
@@ -47,7 +66,7 @@ class PeerGroup:
         self.epoch = 0
         self._own: List[int] = []          # own allocations (device pointers)
         self._opened: List[int] = []       # peers' allocations mapped here
-        self.outputs: Dict[str, list] = {}  # name -> [y, ll array, t_rows, n_rows, own0, own1]
+        self.outputs: Dict[str, _Output] = {}
         # step mode: epochs relative to a device counter that begin_step
         # advances, so calls captured in a CUDA graph use fresh epochs on
         # every replay
@@ -78,13 +97,17 @@ class PeerGroup:
 
         if name not in self.outputs:
             ll = self._shared(8 * t_rows * n_rows)
+            bulk, flag_off = None, 0
+            if t_rows >= BULK_MIN_TOKENS:
+                flag_off = (4 * t_rows * n_rows + 63) // 64 * 64
+                bulk = (ctypes.c_void_p * self.world)(*self._shared(flag_off + 64))
             y = torch.zeros((t_rows, n_rows), dtype=torch.float32, device=f"cuda:{self.ctx.device}")
-            self.outputs[name] = [y, (ctypes.c_void_p * self.world)(*ll), t_rows, n_rows, 0, 0]
-        return self.outputs[name][0]
+            self.outputs[name] = _Output(y, (ctypes.c_void_p * self.world)(*ll), t_rows, n_rows, bulk, flag_off)
+        return self.outputs[name].y
 
     def view(self, name: str):
         """This rank's full output `name` (complete after gather(name))."""
-        return self.outputs[name][0]
+        return self.outputs[name].y
 
     def _next_epoch(self):
         if self._rel is not None:
@@ -93,33 +116,25 @@ class PeerGroup:
         self.epoch = (self.epoch + 1) & 0xFFFFFFFF or 1
         return self.epoch, None
 
+    def _bulk_call(self, x, outs) -> bool:
+        pmt = self.ctx.prefill_min_tokens
+        return pmt > 0 and x.shape[0] >= pmt and all(o.bulk is not None for o in outs)
+
     def mm(self, x, w: QuantWeight, name: str, row_offset: int, stream=None) -> int:
         """x [T, K] (CUDA f32) times this rank's row shard w (rows
         [row_offset, row_offset + w.n_rows) of the full weight): this rank's
         rows of output `name`, sent to every rank.  Returns the epoch to
         pass to gather()."""
-        _check_weight(w)
-        o = self.outputs[name]
-        y, arr, t_rows, n_rows = o[0], o[1], o[2], o[3]
-        if x.shape[0] > t_rows or x.shape[1] != w.n_cols or row_offset + w.n_rows > n_rows:
-            raise ValueError("shape mismatch with the gathered output")
-        o[4], o[5] = row_offset, row_offset + w.n_rows
-        epoch, base = self._next_epoch()
-        check(lib().rce_qmm_mm_batched_device_gather(
-            self.ctx.handle, ctypes.c_void_p(x.data_ptr()), x.stride(0), x.shape[0], w.handle, self.world, self.rank,
-            int(row_offset), ctypes.c_void_p(y.data_ptr()), n_rows, arr, epoch, base, _stream_handle(stream, x.device)))
-        if len(o) == 6:
-            o.append(epoch)
-        else:
-            o[6] = epoch
-        return epoch
+        return self.mm_multi(x, [w], [name], [row_offset], stream=stream)
 
     def mm_multi(self, x, weights, names, row_offsets, stream=None) -> int:
         """mm() for 1-4 row shards that read the same x (weights of one dtype
         and K, e.g. attention q, k, v), in one launch
-        (rce_qmm_mm_batched_device_multi_gather): shard i into output
-        names[i] at row_offsets[i].  One epoch for all the outputs (returned;
-        gather() each name as usual)."""
+        (rce_qmm_mm_batched_device_multi_gather; batches of
+        ctx.prefill_min_tokens or more tokens into outputs with a bulk buffer:
+        rce_qmm_mm_batched_device_multi_gather_bulk).  Shard i goes into
+        output names[i] at row_offsets[i].  One epoch for all the outputs
+        (returned; gather() each name as usual)."""
         weights, names, row_offsets = list(weights), list(names), [int(r) for r in row_offsets]
         if not (1 <= len(weights) <= 4 and len(names) == len(weights) == len(row_offsets)):
             raise ValueError("mm_multi takes 1 to 4 weights, one output name and row offset each")
@@ -127,25 +142,30 @@ class PeerGroup:
         for w, name, r0 in zip(weights, names, row_offsets):
             _check_weight(w)
             o = self.outputs[name]
-            if x.shape[0] > o[2] or x.shape[1] != w.n_cols or r0 + w.n_rows > o[3]:
+            if x.shape[0] > o.t_rows or x.shape[1] != w.n_cols or r0 + w.n_rows > o.n_rows:
                 raise ValueError(f"shape mismatch with the gathered output {name}")
             outs.append(o)
         epoch, base = self._next_epoch()
         n = len(weights)
         hs = (ctypes.c_void_p * n)(*[w.handle for w in weights])
         offs = (ctypes.c_int64 * n)(*row_offsets)
-        ys = (ctypes.c_void_p * n)(*[o[0].data_ptr() for o in outs])
-        lds = (ctypes.c_size_t * n)(*[o[3] for o in outs])
-        lls = (ctypes.c_void_p * (n * self.world))(*[o[1][r] for o in outs for r in range(self.world)])
-        check(lib().rce_qmm_mm_batched_device_multi_gather(
-            self.ctx.handle, ctypes.c_void_p(x.data_ptr()), x.stride(0), x.shape[0], hs, n, self.world, self.rank,
-            offs, ys, lds, lls, epoch, base, _stream_handle(stream, x.device)))
+        ys = (ctypes.c_void_p * n)(*[o.y.data_ptr() for o in outs])
+        lds = (ctypes.c_size_t * n)(*[o.n_rows for o in outs])
+        bulk = self._bulk_call(x, outs)
+        s = _stream_handle(stream, x.device)
+        if bulk:
+            bufs = (ctypes.c_void_p * (n * self.world))(*[o.bulk[r] for o in outs for r in range(self.world)])
+            flags = (ctypes.c_size_t * n)(*[o.flag_off for o in outs])
+            check(lib().rce_qmm_mm_batched_device_multi_gather_bulk(
+                self.ctx.handle, ctypes.c_void_p(x.data_ptr()), x.stride(0), x.shape[0], hs, n, self.world,
+                self.rank, offs, ys, lds, bufs, flags, epoch, base, s))
+        else:
+            lls = (ctypes.c_void_p * (n * self.world))(*[o.ll[r] for o in outs for r in range(self.world)])
+            check(lib().rce_qmm_mm_batched_device_multi_gather(
+                self.ctx.handle, ctypes.c_void_p(x.data_ptr()), x.stride(0), x.shape[0], hs, n, self.world,
+                self.rank, offs, ys, lds, lls, epoch, base, s))
         for o, w, r0 in zip(outs, weights, row_offsets):
-            o[4], o[5] = r0, r0 + w.n_rows
-            if len(o) == 6:
-                o.append(epoch)
-            else:
-                o[6] = epoch
+            o.own0, o.own1, o.epoch, o.bulk_mode = r0, r0 + w.n_rows, epoch, bulk
         return epoch
 
     def gather(self, name: str, epoch: Optional[int] = None, t_rows: Optional[int] = None, stream=None):
@@ -153,14 +173,19 @@ class PeerGroup:
         for the other ranks' rows of the call with `epoch` (default: the
         latest mm into `name`) and copy them in.  Returns the tensor."""
         o = self.outputs[name]
-        y, arr, n_rows, own0, own1 = o[0], o[1], o[3], o[4], o[5]
-        epoch = o[6] if epoch is None else epoch
+        epoch = o.epoch if epoch is None else epoch
         base = ctypes.c_void_p(self._base.data_ptr()) if self._rel is not None else None
-        rows = o[2] if t_rows is None else t_rows
-        check(lib().rce_qmm_peer_unpack(self.ctx.handle, ctypes.c_void_p(arr[self.rank]), ctypes.c_void_p(y.data_ptr()),
-                                        n_rows, rows, n_rows, int(own0), int(own1), int(epoch), base,
-                                        _stream_handle(stream, y.device)))
-        return y
+        rows = o.t_rows if t_rows is None else t_rows
+        s = _stream_handle(stream, o.y.device)
+        if o.bulk_mode:
+            check(lib().rce_qmm_peer_unpack_bulk(self.ctx.handle, ctypes.c_void_p(o.bulk[self.rank]), o.flag_off,
+                                                 ctypes.c_void_p(o.y.data_ptr()), o.n_rows, rows, o.n_rows,
+                                                 int(o.own0), int(o.own1), self.world, self.rank, int(epoch), base, s))
+        else:
+            check(lib().rce_qmm_peer_unpack(self.ctx.handle, ctypes.c_void_p(o.ll[self.rank]),
+                                            ctypes.c_void_p(o.y.data_ptr()), o.n_rows, rows, o.n_rows, int(o.own0),
+                                            int(o.own1), int(epoch), base, s))
+        return o.y
 
     def begin_step(self, calls: int, stream=None) -> None:
         """Start a step of at most `calls` mm calls whose epochs are relative

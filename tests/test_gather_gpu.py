@@ -1,11 +1,13 @@
 """The row-sharded matmul with its all-gather fused over peer memory
-(rce_qmm_mm_batched_device_gather + rce_qmm_peer_unpack), on two GPUs: one
-process per GPU, gloo only to exchange the peer buffers' IPC handles.  Every
-rank's gathered output must equal, bit for bit, the concatenation of each
-shard's own matmul (same shapes, same kernels); a second matmul reading the
-first's gathered output, the tensor-core GEMM route (20 tokens, shard pushed
-to the peers after the GEMM), and a second round through the same buffers
-(new epochs), likewise; and two shards sharing x gathered from one grouped
+(rce_qmm_mm_batched_device_multi_gather + rce_qmm_peer_unpack), on two GPUs:
+one process per GPU, gloo only to exchange the peer buffers' IPC handles.
+Every rank's gathered output must equal, bit for bit, the concatenation of
+each shard's own matmul (same shapes, same kernels); a second matmul reading
+the first's gathered output, the tensor-core GEMM route (20 tokens: the bulk
+mode, plain values and one release flag per peer,
+rce_qmm_mm_batched_device_multi_gather_bulk + rce_qmm_peer_unpack_bulk), and
+a second round through the same buffers (new epochs), likewise; and two
+shards sharing x gathered from one grouped
 launch (rce_qmm_mm_batched_device_multi_gather) against each rank's grouped
 device call, at 1, 3 and 20 tokens.  Skipped with fewer than two GPUs."""
 import os
