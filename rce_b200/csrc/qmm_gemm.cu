@@ -257,6 +257,110 @@ __device__ __forceinline__ void dequant_quarter(const uint8_t *slot, int row, in
     *reinterpret_cast<uint4 *>(dst + ((c1 ^ (row & 7)) * 16)) = make_uint4(h[4], h[5], h[6], h[7]);
 }
 
+// A thread's half of weight row `row` (32 of the 64 values of each k-block),
+// the rows' scales decoded once per chunk.  Same values as dequant_quarter
+// (exact f32, rounded once to fp16); per k-block one 16-byte load of the
+// codes and, for Q4_K, no header work at all.
+template <int DT>
+struct RowHalf {
+    const uint8_t *ch;  // this row's 16-row tile in the packed chunk
+    int row, hf, r16, r, rh;
+    unsigned long long s[4][2], o[4][2];  // Q4_K: [k-block j][sub-block 2j, 2j+1] scale and -offset pairs
+
+    __device__ __forceinline__ void begin(const uint8_t *slot, int row_, int hf_) {
+        constexpr int CB = chunk_bytes(DT);
+        row = row_;
+        hf = hf_;
+        const int tile = row >> 4;
+        r16 = row & 15;
+        r = r16 & 7;
+        rh = r16 >> 3;
+        ch = slot + tile * CB;
+        if (DT == GGUF_Q4_K) {
+            const uint4 hd = *reinterpret_cast<const uint4 *>(ch + 2048 + r16 * 16);
+            const float d = h2f(hd.x), dmin = h2f(hd.x >> 16);
+#pragma unroll
+            for (int j = 0; j < 4; j++) {
+                const uint32_t lo = j < 2 ? hd.y : (j == 2 ? hd.z : hd.w);
+                const uint32_t hi = j < 2 ? hd.z : (j == 2 ? hd.w : 0u);
+                const uint32_t sh = j == 0 ? 0u : (j == 1 ? 24u : (j == 2 ? 16u : 8u));
+                const uint32_t f = __funnelshift_r(lo, hi, sh) & 0xFFFFFFu;
+                const float d1 = d * (float)(f & 63u), m1 = dmin * (float)((f >> 6) & 63u);
+                const float d2 = d * (float)((f >> 12) & 63u), m2 = dmin * (float)((f >> 18) & 63u);
+                s[j][0] = f2pack(d1, d1);
+                o[j][0] = f2pack(-m1, -m1);
+                s[j][1] = f2pack(d2, d2);
+                o[j][1] = f2pack(-m2, -m2);
+            }
+        }
+    }
+
+    // k-block J of the chunk into row `row` of A (K-major, 128-byte swizzle)
+    template <int J>
+    __device__ __forceinline__ void kblock(uint8_t *a_tile) const {
+        const int lane = 4 * r + J;
+        uint32_t h[16];  // 32 fp16 values
+        int cc[4];       // the four 16-byte A chunks they fill
+        if (DT == GGUF_Q4_K) {
+            const uint4 q = *reinterpret_cast<const uint4 *>(ch + ((2 * rh + hf) * 32 + lane) * 16);
+            const uint32_t w[4] = {q.x, q.y, q.z, q.w};
+            const unsigned long long bias = f2pack(-8388608.f, -8388608.f);
+#pragma unroll
+            for (int qq = 0; qq < 2; qq++)  // quarter 2 hf + qq: bytes 8 qq .. 8 qq + 7
+#pragma unroll
+                for (int b = 0; b < 8; b += 2) {
+                    const uint32_t x = w[2 * qq + (b >> 2)] >> (8 * (b & 3));
+                    h[8 * qq + (b >> 1)] = dq_pair(x & 15u, (x >> 8) & 15u, bias, s[J][0], o[J][0]);
+                    h[8 * qq + 4 + (b >> 1)] = dq_pair((x >> 4) & 15u, (x >> 12) & 15u, bias, s[J][1], o[J][1]);
+                }
+            cc[0] = 2 * hf;
+            cc[1] = 4 + 2 * hf;
+            cc[2] = 2 * hf + 1;
+            cc[3] = 5 + 2 * hf;
+        } else {
+#pragma unroll
+            for (int qq = 0; qq < 2; qq++) {
+                const int qr = 2 * hf + qq;
+                const uint2 sc = *reinterpret_cast<const uint2 *>(ch + quant_bytes(DT) + lane * 8);
+                const uint32_t sw = rh ? sc.y : sc.x;
+                const float dd = h2f(sw >> (16 * hf));
+                const unsigned long long zero = f2pack(0.f, 0.f), sd = f2pack(dd, dd);
+                if (DT == GGUF_Q4_0) {
+                    const unsigned long long bias = f2pack(-8388616.f, -8388616.f);  // 2^23 + 8
+                    const uint2 q =
+                        *reinterpret_cast<const uint2 *>(ch + ((2 * rh + hf) * 32 + lane) * 16 + 8 * (qr & 1));
+                    const uint32_t w[2] = {q.x, q.y};
+#pragma unroll
+                    for (int b = 0; b < 8; b += 2) {
+                        const uint32_t x = w[b >> 2] >> (8 * (b & 3));
+                        h[8 * qq + (b >> 1)] = dq_pair(x & 15u, (x >> 8) & 15u, bias, sd, zero);
+                        h[8 * qq + 4 + (b >> 1)] = dq_pair((x >> 4) & 15u, (x >> 12) & 15u, bias, sd, zero);
+                    }
+                    cc[2 * qq] = 4 * hf + (qr & 1);
+                    cc[2 * qq + 1] = cc[2 * qq] + 2;
+                } else {
+                    const unsigned long long bias = f2pack(-8388736.f, -8388736.f);  // 2^23 + 128
+                    const uint4 q = *reinterpret_cast<const uint4 *>(ch + ((4 * rh + qr) * 32 + lane) * 16);
+                    const uint32_t w[4] = {q.x ^ 0x80808080u, q.y ^ 0x80808080u, q.z ^ 0x80808080u,
+                                           q.w ^ 0x80808080u};
+#pragma unroll
+                    for (int b = 0; b < 16; b += 2) {
+                        const uint32_t x = w[b >> 2] >> (8 * (b & 3));  // byte ^ 0x80 = q + 128
+                        h[8 * qq + (b >> 1)] = dq_pair(x & 255u, (x >> 8) & 255u, bias, sd, zero);
+                    }
+                    cc[2 * qq] = 2 * qr;
+                    cc[2 * qq + 1] = 2 * qr + 1;
+                }
+            }
+        }
+        uint8_t *dst = a_tile + (row >> 3) * 1024 + (row & 7) * 128;
+#pragma unroll
+        for (int i = 0; i < 4; i++)
+            *reinterpret_cast<uint4 *>(dst + ((cc[i] ^ (row & 7)) * 16)) =
+                make_uint4(h[4 * i], h[4 * i + 1], h[4 * i + 2], h[4 * i + 3]);
+    }
+};
+
 // Shared-memory plan of one CTA for token-tile width bn.
 struct GemmSmem {
     size_t a, b, packed, bars, tmem_slot, total;
@@ -312,6 +416,58 @@ __host__ __device__ inline uint32_t tmem_cols(int bn) {
 // up with the rest of the pipeline at every bn measured (a second to fourth
 // issuer changed nothing at 16-128 tokens), so the split is kept at one.
 __host__ __device__ inline int mma_warps(int bn) { return (void)bn, 1; }
+
+// One dequantiser group's loop (group G takes k-blocks j = G and G + 2 of
+// every chunk); returns false if a bounded wait expired.
+template <int DT, int G>
+__device__ __forceinline__ bool dequant_group(const GemmArgs &p, uint8_t *pk, uint8_t *a_st, uint32_t bar0, int row,
+                                              int hf, int ntiles, int nchunks, int NP, int NA, int lane) {
+    constexpr int CB = chunk_bytes(DT);
+    auto PF = [&](int s) { return bar0 + 8 * (0 + s); };
+    auto PE = [&](int s) { return bar0 + 8 * (kMaxP + s); };
+    auto AF = [&](int s) { return bar0 + 8 * (2 * kMaxP + s); };
+    auto AE = [&](int s) { return bar0 + 8 * (2 * kMaxP + kMaxA + s); };
+    int s = 0, st = G;  // packed slot and A stage, with their phases
+    uint32_t sph = 0, aph = 0;
+    const bool live = row < ntiles * 16;
+    for (int c = 0; c < nchunks; c++) {
+        if (!mbar_wait(PF(s), sph)) return false;
+        RowHalf<DT> rw;
+        if (live) rw.begin(pk + (size_t)s * 8 * CB, row, hf);
+#pragma unroll
+        for (int jj = 0; jj < 2; jj++) {
+            const int kb = 4 * c + G + 2 * jj;
+            if (kb >= NA && !mbar_wait(AE(st), aph ^ 1)) return false;
+            uint8_t *a_tile = a_st + (size_t)st * kBM * kBK * 2;
+            if (live) {
+                if (jj == 0)
+                    rw.template kblock<G>(a_tile);
+                else
+                    rw.template kblock<G + 2>(a_tile);
+            } else {  // rows past the weight: zeros
+                uint8_t *dst = a_tile + (row >> 3) * 1024 + (row & 7) * 128 + 64 * hf;
+#pragma unroll
+                for (int q = 0; q < 4; q++) *reinterpret_cast<uint4 *>(dst + 16 * q) = make_uint4(0, 0, 0, 0);
+            }
+            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // generic writes -> tensor-core reads
+            __syncwarp();
+            if (lane == 0) {  // one arrival per warp
+                mbar_arrive(AF(st));
+                if (jj == 1) mbar_arrive(PE(s));  // this group is done with the chunk
+            }
+            st += 2;
+            if (st >= NA) {
+                st -= NA;
+                aph ^= 1;
+            }
+        }
+        if (++s == NP) {
+            s = 0;
+            sph ^= 1;
+        }
+    }
+    return true;
+}
 
 template <int DT>
 __global__ void __launch_bounds__(kThreads, 1)
@@ -428,46 +584,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int grp = (warp - 1) / (kDqWarps / 2);
         const int gt = tid - 32 - grp * (kDqWarps / 2) * 32;
         const int row = gt >> 1, hf = gt & 1;
-        int s = 0, st = grp, cur_c = -1;  // packed slot and A stage, with their phases
-        uint32_t sph = 0, aph = 0;
-        for (int kb = grp; kb < nkb && ok; kb += 2) {
-            const int c = kb >> 2, j = kb & 3;
-            if (c != cur_c) {  // the next chunk (one at a time: kb advances by 2 of its 4)
-                if (cur_c >= 0 && ++s == NP) {
-                    s = 0;
-                    sph ^= 1;
-                }
-                cur_c = c;
-                if (!mbar_wait(PF(s), sph)) {
-                    ok = false;
-                    break;
-                }
-            }
-            if (kb >= NA && !mbar_wait(AE(st), aph ^ 1)) {
-                ok = false;
-                break;
-            }
-            uint8_t *a_tile = a_st + (size_t)st * kBM * kBK * 2;
-            if (row < ntiles * 16) {
-                dequant_quarter<DT>(pk + (size_t)s * 8 * CB, row, 2 * hf, j, a_tile);
-                dequant_quarter<DT>(pk + (size_t)s * 8 * CB, row, 2 * hf + 1, j, a_tile);
-            } else {  // rows past the weight: zeros
-                uint8_t *dst = a_tile + (row >> 3) * 1024 + (row & 7) * 128 + 64 * hf;
-#pragma unroll
-                for (int q = 0; q < 4; q++) *reinterpret_cast<uint4 *>(dst + 16 * q) = make_uint4(0, 0, 0, 0);
-            }
-            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // generic writes -> tensor-core reads
-            __syncwarp();
-            if (lane == 0) {  // one arrival per warp
-                mbar_arrive(AF(st));
-                if (j == 2 + grp) mbar_arrive(PE(s));  // this group is done with the chunk
-            }
-            st += 2;
-            if (st >= NA) {
-                st -= NA;
-                aph ^= 1;
-            }
-        }
+        if (grp == 0)
+            ok = dequant_group<DT, 0>(p, pk, a_st, bar0, row, hf, ntiles, nchunks, NP, NA, lane);
+        else
+            ok = dequant_group<DT, 1>(p, pk, a_st, bar0, row, hf, ntiles, nchunks, NP, NA, lane);
     } else if (warp >= kMmaWarp && warp < kMmaWarp + MW) {
         // MMA issuer w takes k-blocks w, w + MW, ... into its own accumulator
         // (columns w * acc_cols ..); per k-block, bn / 256 (at least one)
