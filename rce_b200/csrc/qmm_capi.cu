@@ -892,6 +892,12 @@ int rce_qmm_moe_ffn_device(rce_qmm_ctx *ctx, const float *d_x, size_t ldx, size_
     o += al(P * (size_t)d_ff * 4);
     const size_t o_y = o;
     o += al(P * (size_t)d_model * 4);
+    const size_t o_xh2 = o;  // grouped path: fp16 SwiGLU outputs and both inputs' row scales
+    o += al(P * (size_t)d_ff * 2);
+    const size_t o_inv = o;
+    o += al(P * 4);
+    const size_t o_inv2 = o;
+    o += al(P * 4);
     void *wsv = nullptr;
     int32_t *host_off = nullptr;
     rc = stream_moe_ws(ctx, s, o, (size_t)n_local + 1, &wsv, &host_off);
@@ -909,6 +915,47 @@ int rce_qmm_moe_ffn_device(rce_qmm_ctx *ctx, const float *d_x, size_t ldx, size_
 
     CUDA_TRY(rce::launch_moe_route(d_logits, ld_logits, (int)t_rows, n_experts, top_k, 1, idx, wt, s));
     CUDA_TRY(rce::launch_moe_plan(idx, (int)P, top_k, expert_begin, expert_end, off, pos, tok, s));
+    // Prefill-sized batches: every local expert's gate and up in one grouped
+    // tensor-core launch, the down matmuls in another, the row counts read
+    // on the device (no host synchronisation; the call can be captured in a
+    // CUDA graph).  Smaller batches, prefill_min_tokens = 0 (the exact
+    // path) and experts of mixed formats: each expert's matmuls on their own,
+    // sized by the row counts copied to the host.
+    bool grouped = ctx->prefill_min_tokens > 0 && t_rows >= (size_t)ctx->prefill_min_tokens;
+    for (int e = expert_begin; e < expert_end && grouped; e++)
+        grouped = gate[e]->dtype == g0->dtype && up[e]->dtype == g0->dtype &&
+                  down[e]->dtype == down[expert_begin]->dtype;
+    if (grouped) {
+        constexpr int kG = rce::kGemmMaxGroup;
+        const int32_t *n_rows = off + n_local;
+        const int max_rows = (int)t_rows;  // a token picks an expert at most once
+        const int rows_hint = (int)(P * (size_t)n_local / (size_t)n_experts);
+        void *xh = ws + o_xg, *xh2 = ws + o_xh2;
+        float *inv = reinterpret_cast<float *>(ws + o_inv), *inv2 = reinterpret_cast<float *>(ws + o_inv2);
+        const uint8_t *wz[kG];
+        float *yz[kG];
+        int sz[kG];
+        CUDA_TRY(rce::launch_moe_gather_prep(d_x, ldx, tok, n_rows, (int)P, (int)d_model, xh, inv, s));
+        for (int i0 = 0; i0 < n_local; i0 += kG / 2) {  // entries 2i, 2i + 1: gate and up of local expert i
+            int n = 0;
+            for (int i = i0; i < n_local && i < i0 + kG / 2; i++) {
+                wz[n] = gate[expert_begin + i]->dev, yz[n] = gb, sz[n++] = i;
+                wz[n] = up[expert_begin + i]->dev, yz[n] = ub, sz[n++] = i;
+            }
+            CUDA_TRY(rce::launch_gemm_grouped(g0->dtype, wz, yz, sz, n, g0->g, xh, inv, (int)P, rows_hint, off,
+                                              n_local, max_rows, (size_t)d_ff, ctx->err_dev, s));
+        }
+        CUDA_TRY(rce::launch_moe_swiglu_prep(gb, ub, (size_t)d_ff, n_rows, (int)P, (int)d_ff, xh2, inv2, s));
+        const rce_qmm_weight *d0 = down[expert_begin];
+        for (int i0 = 0; i0 < n_local; i0 += kG) {
+            int n = 0;
+            for (int i = i0; i < n_local && i < i0 + kG; i++) wz[n] = down[expert_begin + i]->dev, yz[n] = yb, sz[n++] = i;
+            CUDA_TRY(rce::launch_gemm_grouped(d0->dtype, wz, yz, sz, n, d0->g, xh2, inv2, (int)P, rows_hint, off,
+                                              n_local, max_rows, (size_t)d_model, ctx->err_dev, s));
+        }
+        CUDA_TRY(rce::launch_moe_combine(yb, (int)d_model, pos, wt, (int)t_rows, top_k, d_out, ldo, s));
+        return ok();
+    }
     // the per-expert row counts size the matmuls below
     CUDA_TRY(cudaMemcpyAsync(host_off, off, (size_t)(n_local + 1) * 4, cudaMemcpyDeviceToHost, s));
     CUDA_TRY(cudaStreamSynchronize(s));

@@ -36,8 +36,10 @@
 
 #include <atomic>
 #include <mutex>
+#include <type_traits>
 
 #include "qmm_internal.h"
+#include "qmm_prep.cuh"
 
 namespace rce {
 namespace {
@@ -148,6 +150,7 @@ struct GemmArgs {
     size_t ldy;
     int t_rows;
     int bn;
+    int box_rows;  // rows of one activation TMA box
 };
 
 // Packed f32x2 arithmetic (two lanes of f32 per instruction).
@@ -179,88 +182,10 @@ __device__ __forceinline__ uint32_t dq_pair(uint32_t c0, uint32_t c1, unsigned l
     return f2_to_h2(f2fma(f2add(f, bias), sc, off));
 }
 
-// Dequantise quarter `qr` of this thread's weight row for k-block j (0..3)
-// of the chunk in `slot` (8 tiles x CB bytes): 16 of the row's 64 fp16
-// values into row `row` of A (K-major, 128-byte swizzle).  Values are
-// computed exactly in f32 as the reference's dequantize_to_f32 does, then
-// rounded once to fp16.
-//   Q4_K: group j's qs bytes 8 qr .. 8 qr + 7, i.e. values 8 qr .. (low
-//         nibbles, A chunk qr) and 32 + 8 qr .. (high nibbles, chunk 4 + qr);
-//   Q4_0: block 2 j + qr / 2, bytes 8 (qr & 1) ..: low nibbles -> chunk
-//         4 (qr >> 1) + (qr & 1), high nibbles -> 2 more;
-//   Q8_0: block 2 j + qr / 2, values 16 (qr & 1) .. -> chunks 2 qr, 2 qr + 1.
-template <int DT>
-__device__ __forceinline__ void dequant_quarter(const uint8_t *slot, int row, int qr, int j, uint8_t *a_tile) {
-    constexpr int CB = chunk_bytes(DT);
-    const int tile = row >> 4, r16 = row & 15, r = r16 & 7, rh = r16 >> 3;
-    const int lane = 4 * r + j, hf = qr >> 1;
-    const uint8_t *ch = slot + tile * CB;
-    uint32_t h[8];  // 16 fp16 values
-    int c0, c1;     // the two 16-byte A chunks (8 values each) they fill
-    if (DT == GGUF_Q4_K) {
-        const uint4 hd = *reinterpret_cast<const uint4 *>(ch + 2048 + r16 * 16);
-        const float d = h2f(hd.x), dmin = h2f(hd.x >> 16);
-        const uint32_t lo = j < 2 ? hd.y : (j == 2 ? hd.z : hd.w);
-        const uint32_t hi = j < 2 ? hd.z : (j == 2 ? hd.w : 0u);
-        const uint32_t sh = j == 0 ? 0u : (j == 1 ? 24u : (j == 2 ? 16u : 8u));
-        const uint32_t f = __funnelshift_r(lo, hi, sh) & 0xFFFFFFu;
-        const float d1 = d * (float)(f & 63u), m1 = dmin * (float)((f >> 6) & 63u);
-        const float d2 = d * (float)((f >> 12) & 63u), m2 = dmin * (float)((f >> 18) & 63u);
-        const unsigned long long bias = f2pack(-8388608.f, -8388608.f);
-        const unsigned long long s1 = f2pack(d1, d1), o1 = f2pack(-m1, -m1);
-        const unsigned long long s2 = f2pack(d2, d2), o2 = f2pack(-m2, -m2);
-        const uint2 q = *reinterpret_cast<const uint2 *>(ch + ((2 * rh + hf) * 32 + lane) * 16 + 8 * (qr & 1));
-        const uint32_t w[2] = {q.x, q.y};
-#pragma unroll
-        for (int b = 0; b < 8; b += 2) {
-            const uint32_t x = w[b >> 2] >> (8 * (b & 3));  // bytes b, b+1 in the low half
-            h[b >> 1] = dq_pair(x & 15u, (x >> 8) & 15u, bias, s1, o1);
-            h[4 + (b >> 1)] = dq_pair((x >> 4) & 15u, (x >> 12) & 15u, bias, s2, o2);
-        }
-        c0 = qr;
-        c1 = 4 + qr;
-    } else {
-        const uint2 sc = *reinterpret_cast<const uint2 *>(ch + quant_bytes(DT) + lane * 8);
-        const uint32_t sw = rh ? sc.y : sc.x;
-        const float dd = h2f(sw >> (16 * hf));
-        const unsigned long long zero = f2pack(0.f, 0.f), sd = f2pack(dd, dd);
-        if (DT == GGUF_Q4_0) {
-            const unsigned long long bias = f2pack(-8388616.f, -8388616.f);  // 2^23 + 8
-            const uint2 q =
-                *reinterpret_cast<const uint2 *>(ch + ((2 * rh + hf) * 32 + lane) * 16 + 8 * (qr & 1));
-            const uint32_t w[2] = {q.x, q.y};
-#pragma unroll
-            for (int b = 0; b < 8; b += 2) {
-                const uint32_t x = w[b >> 2] >> (8 * (b & 3));
-                h[b >> 1] = dq_pair(x & 15u, (x >> 8) & 15u, bias, sd, zero);
-                h[4 + (b >> 1)] = dq_pair((x >> 4) & 15u, (x >> 12) & 15u, bias, sd, zero);
-            }
-            c0 = 4 * hf + (qr & 1);
-            c1 = c0 + 2;
-        } else {
-            const unsigned long long bias = f2pack(-8388736.f, -8388736.f);  // 2^23 + 128
-            const uint4 q = *reinterpret_cast<const uint4 *>(ch + ((4 * rh + qr) * 32 + lane) * 16);
-            const uint32_t w[4] = {q.x ^ 0x80808080u, q.y ^ 0x80808080u, q.z ^ 0x80808080u, q.w ^ 0x80808080u};
-#pragma unroll
-            for (int b = 0; b < 16; b += 2) {
-                const uint32_t x = w[b >> 2] >> (8 * (b & 3));  // byte ^ 0x80 = q + 128
-                h[b >> 1] = dq_pair(x & 255u, (x >> 8) & 255u, bias, sd, zero);
-            }
-            c0 = 2 * qr;
-            c1 = c0 + 1;
-        }
-    }
-    // row `row` of the 128 x 64 fp16 tile: 8-row atoms of 1024 bytes, 16-byte
-    // chunk c of row r at ((c ^ (r & 7)) * 16)
-    uint8_t *dst = a_tile + (row >> 3) * 1024 + (row & 7) * 128;
-    *reinterpret_cast<uint4 *>(dst + ((c0 ^ (row & 7)) * 16)) = make_uint4(h[0], h[1], h[2], h[3]);
-    *reinterpret_cast<uint4 *>(dst + ((c1 ^ (row & 7)) * 16)) = make_uint4(h[4], h[5], h[6], h[7]);
-}
-
 // A thread's half of weight row `row` (32 of the 64 values of each k-block),
-// the rows' scales decoded once per chunk.  Same values as dequant_quarter
-// (exact f32, rounded once to fp16); per k-block one 16-byte load of the
-// codes and, for Q4_K, no header work at all.
+// the rows' scales decoded once per chunk.  Values are exact in f32 (as the
+// reference's dequantize_to_f32 computes them) and rounded once to fp16; per
+// k-block one 16-byte load of the codes and, for Q4_K, no header work.
 template <int DT>
 struct RowHalf {
     const uint8_t *ch;  // this row's 16-row tile in the packed chunk
@@ -469,10 +394,24 @@ __device__ __forceinline__ bool dequant_group(const GemmArgs &p, uint8_t *pk, ui
     return true;
 }
 
-template <int DT>
+// Expert-grouped launch: blockIdx.z selects entry z, which multiplies
+// weight w[z] by the activation rows [off[set[z]], off[set[z] + 1]) into the
+// same rows of y[z].  The row ranges are read on the device (written by an
+// earlier kernel), so the host never waits for them; CTAs whose token tile
+// lies past their entry's rows exit at once.
+struct GemmGroup {
+    const uint8_t *w[kGemmMaxGroup];
+    float *y[kGemmMaxGroup];
+    int set[kGemmMaxGroup];
+    const int32_t *off;
+};
+struct NoGroup {};
+
+template <int DT, class Grp>
 __global__ void __launch_bounds__(kThreads, 1)
-    gemm_kernel(const __grid_constant__ CUtensorMap xmap, GemmArgs p) {
+    gemm_kernel(const __grid_constant__ CUtensorMap xmap, const GemmArgs p, const __grid_constant__ Grp q) {
     constexpr int CB = chunk_bytes(DT);
+    constexpr bool kGrouped = std::is_same<Grp, GemmGroup>::value;
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     const int bn = p.bn;
@@ -497,7 +436,23 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int tile0 = blockIdx.x * 8;  // first 16-row tile of this CTA
     const int ntiles = min(8, p.g.n_tiles - tile0);
+    // this CTA's weight, output and activation rows t_begin + tok0 ..
+    const uint8_t *wt = p.w;
+    float *yo = p.y;
+    int t_begin = 0, t_count = p.t_rows;
+    if constexpr (kGrouped) {
+        const int z = blockIdx.z;
+        wt = q.w[z];
+        yo = q.y[z];
+        t_begin = q.off[q.set[z]];
+        t_count = q.off[q.set[z] + 1] - t_begin;
+    }
     const int tok0 = blockIdx.y * bn;
+    if (tok0 >= t_count) return;  // the whole CTA, before any barrier or tensor memory
+    const int live = min(bn, t_count - tok0);  // tokens of this tile
+    // activation rows loaded per k-block (whole boxes) and MMA width
+    const int b_rows = kGrouped ? (live + p.box_rows - 1) / p.box_rows * p.box_rows : bn;
+    const int ncol = kGrouped ? (live + 15) / 16 * 16 : bn;
     const int nchunks = p.g.n_chunks;
     const int nkb = nchunks * 4;
     const int MW = mma_warps(bn);
@@ -544,7 +499,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 }
                 mbar_expect_tx(PF(s), (uint32_t)(ntiles * CB));
                 for (int t = 0; t < ntiles; t++)
-                    bulk_g2s(smem_u32(pk + (size_t)(s * 8 + t) * CB), p.w + ((size_t)(tile0 + t) * nchunks + c) * CB,
+                    bulk_g2s(smem_u32(pk + (size_t)(s * 8 + t) * CB), wt + ((size_t)(tile0 + t) * nchunks + c) * CB,
                              CB, PF(s));
                 if (++s == NP) {
                     s = 0;
@@ -565,10 +520,10 @@ __global__ void __launch_bounds__(kThreads, 1)
                     ok = false;
                     break;
                 }
-                mbar_expect_tx(BF(st), (uint32_t)(bn * kBK * 2));
+                mbar_expect_tx(BF(st), (uint32_t)(b_rows * kBK * 2));
                 uint8_t *dst = b_st + (size_t)st * bn * kBK * 2;
-                for (int r0 = 0; r0 < bn; r0 += 256)  // a tensor-map box is at most 256 rows
-                    tma_2d(smem_u32(dst + (size_t)r0 * kBK * 2), &xmap, kb * kBK, tok0 + r0, BF(st));
+                for (int r0 = 0; r0 < b_rows; r0 += p.box_rows)  // a tensor-map box is at most 256 rows
+                    tma_2d(smem_u32(dst + (size_t)r0 * kBK * 2), &xmap, kb * kBK, t_begin + tok0 + r0, BF(st));
                 if (++st == NB) {
                     st = 0;
                     ph ^= 1;
@@ -595,7 +550,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         // One lane issues; descriptors advance by 32 bytes (2 in the >> 4
         // address field) per K = 16 step and by a whole stage per stage.
         const int w = warp - kMmaWarp;
-        const int nsub = bn > 256 ? bn / 256 : 1, nw = bn > 256 ? 256 : bn;
+        const int nsub = ncol > 256 ? ncol / 256 : 1, nw = ncol > 256 ? 256 : ncol;
         const uint32_t idesc = idesc_f16(nw);
         const uint32_t acc = tmem + (uint32_t)w * acc_cols;
         if (lane == 0) {
@@ -641,8 +596,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (ok && !mbar_wait(ACC, 0)) ok = false;
         tc_fence_after();
         const int lane_base = 32 * (warp & 3);
-        const int cpg = (bn / 8 + 3) / 4 * 8;  // columns per group, a multiple of 8
-        const int c_begin = ((warp - 1) >> 2) * cpg, c_end = min(bn, c_begin + cpg);
+        const int cpg = (ncol / 8 + 3) / 4 * 8;  // columns per group, a multiple of 8
+        const int c_begin = ((warp - 1) >> 2) * cpg, c_end = min(ncol, c_begin + cpg);
         const int row = tile0 * 16 + lane_base + lane;
         if (ok) {
             for (int c0 = c_begin; c0 < c_end; c0 += 8) {
@@ -660,8 +615,8 @@ __global__ void __launch_bounds__(kThreads, 1)
                 if (row < p.g.n_rows) {
 #pragma unroll
                     for (int i = 0; i < 8; i++) {
-                        const int t = tok0 + c0 + i;
-                        if (t < p.t_rows) p.y[(size_t)t * p.ldy + row] = v[i] * p.inv_scale[t];
+                        const int t = t_begin + tok0 + c0 + i;
+                        if (c0 + i < live) yo[(size_t)t * p.ldy + row] = v[i] * p.inv_scale[t];
                     }
                 }
             }
@@ -679,39 +634,11 @@ __global__ void __launch_bounds__(kThreads, 1)
 }
 
 // X f32 [t][ldx] -> Xh fp16 [t][k] with x * 2^e, |x * 2^e| < 2^14, and 1/2^e.
-__global__ void __launch_bounds__(256) prep_kernel(const float *x, size_t ldx, int k, __half *xh, float *inv) {
+__global__ void __launch_bounds__(kPrepThreads) prep_kernel(const float *x, size_t ldx, int k, __half *xh,
+                                                             float *inv) {
     const int t = blockIdx.x;
     const float *xr = x + (size_t)t * ldx;
-    float mx = 0.f;
-    bool fin = true;
-    for (int i = threadIdx.x; i < k; i += 256) {
-        const float v = xr[i];
-        mx = fmaxf(mx, fabsf(v));
-        fin = fin && isfinite(v);
-    }
-    if (!fin) mx = INFINITY;
-    __shared__ float red[8];
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = mx;
-    __syncthreads();
-    float v = 0.f;
-    for (int w = 0; w < 8; w++) v = fmaxf(v, red[w]);
-    float s = 1.f, is = 1.f;
-    if (!isfinite(v)) {
-        s = 0.f;
-        is = __int_as_float(0x7fc00000);
-    } else if (v > 0.f) {
-        int e;
-        frexpf(v, &e);
-        e = max(-100, min(100, e));
-        s = ldexpf(1.f, 14 - e);
-        is = ldexpf(1.f, e - 14);
-    }
-    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
-    __half *o = xh + (size_t)t * k;
-    for (int i = threadIdx.x; i < k; i += 256) o[i] = __float2half_rn(xr[i] * s);
-    if (threadIdx.x == 0) inv[t] = is;
+    prep_row([&](int i) { return xr[i]; }, k, xh + (size_t)t * k, inv + t);
 }
 
 using EncodeTiled = CUresult (*)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *, const cuuint64_t *,
@@ -731,10 +658,11 @@ EncodeTiled encode_fn() {
     return fn;
 }
 
-template <int DT>
-cudaError_t launch_dt(const CUtensorMap &map, const GemmArgs &a, dim3 grid, size_t smem, cudaStream_t s) {
+template <int DT, class Grp>
+cudaError_t launch_dt(const CUtensorMap &map, const GemmArgs &a, const Grp &q, dim3 grid, size_t smem,
+                      cudaStream_t s) {
     static std::atomic<unsigned long long> done{0};
-    auto kern = gemm_kernel<DT>;
+    auto kern = gemm_kernel<DT, Grp>;
     int dev = 0;
     cudaError_t e = cudaGetDevice(&dev);
     if (e != cudaSuccess) return e;
@@ -760,7 +688,33 @@ cudaError_t launch_dt(const CUtensorMap &map, const GemmArgs &a, dim3 grid, size
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    return cudaLaunchKernelEx(&cfg, kern, map, a);
+    return cudaLaunchKernelEx(&cfg, kern, map, a, q);
+}
+
+template <class Grp>
+cudaError_t launch_any(int dt, const CUtensorMap &map, const GemmArgs &a, const Grp &q, dim3 grid, size_t smem,
+                       cudaStream_t s) {
+    switch (dt) {
+    case GGUF_Q4_K: return launch_dt<GGUF_Q4_K>(map, a, q, grid, smem, s);
+    case GGUF_Q4_0: return launch_dt<GGUF_Q4_0>(map, a, q, grid, smem, s);
+    case GGUF_Q8_0: return launch_dt<GGUF_Q8_0>(map, a, q, grid, smem, s);
+    default: return cudaErrorInvalidValue;
+    }
+}
+
+// Tensor map of the fp16 activations [rows][k] (128-byte swizzle, boxes of
+// 64 columns x box_rows rows).
+cudaError_t act_map(CUtensorMap *map, const void *xh, int rows, int64_t k, int box_rows) {
+    EncodeTiled enc = encode_fn();
+    if (!enc) return cudaErrorNotSupported;
+    const cuuint64_t dims[2] = {(cuuint64_t)k, (cuuint64_t)rows};
+    const cuuint64_t strides[1] = {(cuuint64_t)k * 2};
+    const cuuint32_t box[2] = {(cuuint32_t)kBK, (cuuint32_t)box_rows};
+    const cuuint32_t estr[2] = {1, 1};
+    CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void *>(xh), dims, strides, box, estr,
+                     CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                     CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS ? cudaSuccess : cudaErrorInvalidValue;
 }
 
 }  // namespace
@@ -783,12 +737,11 @@ size_t gemm_workspace_bytes(const Geometry &g, int t_rows) {
 cudaError_t launch_gemm(int dt, const uint8_t *tiles, const Geometry &g, const float *x, size_t ldx, float *y,
                         size_t ldy, int t_rows, void *workspace, int *err, cudaStream_t s) {
     if (t_rows <= 0 || g.n_rows <= 0) return cudaSuccess;
-    EncodeTiled enc = encode_fn();
-    if (!enc) return cudaErrorNotSupported;
+    if (!encode_fn()) return cudaErrorNotSupported;
     __half *xh = static_cast<__half *>(workspace);
     const size_t xh_bytes = ((size_t)t_rows * g.n_cols * 2 + 255) / 256 * 256;
     float *inv = reinterpret_cast<float *>(static_cast<uint8_t *>(workspace) + xh_bytes);
-    prep_kernel<<<t_rows, 256, 0, s>>>(x, ldx, (int)g.n_cols, xh, inv);
+    prep_kernel<<<t_rows, kPrepThreads, 0, s>>>(x, ldx, (int)g.n_cols, xh, inv);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return e;
     int bn = gemm_bn(dt, t_rows);
@@ -809,14 +762,9 @@ cudaError_t launch_gemm(int dt, const uint8_t *tiles, const Geometry &g, const f
         while (bn > 64 && rbs * ((t_rows + bn - 1) / bn) * 10 < (long)sms * 6) bn /= 2;
     }
     CUtensorMap map;
-    const cuuint64_t dims[2] = {(cuuint64_t)g.n_cols, (cuuint64_t)t_rows};
-    const cuuint64_t strides[1] = {(cuuint64_t)g.n_cols * 2};
-    const cuuint32_t box[2] = {(cuuint32_t)kBK, (cuuint32_t)(bn < 256 ? bn : 256)};
-    const cuuint32_t estr[2] = {1, 1};
-    CUresult r = enc(&map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, xh, dims, strides, box, estr,
-                     CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                     CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-    if (r != CUDA_SUCCESS) return cudaErrorInvalidValue;
+    const int box_rows = bn < 256 ? bn : 256;
+    e = act_map(&map, xh, t_rows, g.n_cols, box_rows);
+    if (e != cudaSuccess) return e;
     GemmArgs a;
     a.w = tiles;
     a.y = y;
@@ -826,16 +774,57 @@ cudaError_t launch_gemm(int dt, const uint8_t *tiles, const Geometry &g, const f
     a.ldy = ldy;
     a.t_rows = t_rows;
     a.bn = bn;
+    a.box_rows = box_rows;
     const GemmSmem lay = gemm_smem(dt, bn);
     if (lay.pslots < 2) return cudaErrorInvalidConfiguration;
-    const size_t smem = lay.total;
     dim3 grid((g.n_tiles + 7) / 8, (t_rows + bn - 1) / bn);
-    switch (dt) {
-    case GGUF_Q4_K: return launch_dt<GGUF_Q4_K>(map, a, grid, smem, s);
-    case GGUF_Q4_0: return launch_dt<GGUF_Q4_0>(map, a, grid, smem, s);
-    case GGUF_Q8_0: return launch_dt<GGUF_Q8_0>(map, a, grid, smem, s);
-    default: return cudaErrorInvalidValue;
+    return launch_any(dt, map, a, NoGroup{}, grid, lay.total, s);
+}
+
+// Token tile of a grouped launch.
+static int gemm_grouped_bn(int rows, int n_sets, int max_rows) {
+    // twice the average rows per set, in whole 64-row boxes, 64 .. 256: sets
+    // up to that size are one token tile (each weight tile dequantised once)
+    const long avg2 = n_sets > 0 ? (2L * rows + n_sets - 1) / n_sets : rows;
+    long bn = (avg2 + 63) / 64 * 64;
+    if (bn > (long)(max_rows + 63) / 64 * 64) bn = (long)(max_rows + 63) / 64 * 64;
+    return (int)(bn < 64 ? 64 : (bn > 256 ? 256 : bn));
+}
+
+cudaError_t launch_gemm_grouped(int dt, const uint8_t *const *ws, float *const *ys, const int *set, int n,
+                                const Geometry &g, const void *xh, const float *inv, int rows, int rows_hint,
+                                const int32_t *off, int n_sets, int max_rows, size_t ldy, int *err, cudaStream_t s) {
+    if (n <= 0 || rows <= 0 || max_rows <= 0 || g.n_rows <= 0) return cudaSuccess;
+    if (n > kGemmMaxGroup || n_sets <= 0) return cudaErrorInvalidValue;
+    if (!encode_fn()) return cudaErrorNotSupported;
+    const int bn = gemm_grouped_bn(rows_hint, n_sets, max_rows);
+    constexpr int kBox = 64;
+    CUtensorMap map;
+    cudaError_t e = act_map(&map, xh, rows, g.n_cols, kBox);
+    if (e != cudaSuccess) return e;
+    GemmArgs a;
+    a.w = nullptr;
+    a.y = nullptr;
+    a.inv_scale = inv;
+    a.err = err;
+    a.g = g;
+    a.ldy = ldy;
+    a.t_rows = 0;
+    a.bn = bn;
+    a.box_rows = kBox;
+    GemmGroup q;
+    for (int z = 0; z < kGemmMaxGroup; z++) {
+        q.w[z] = z < n ? ws[z] : nullptr;
+        q.y[z] = z < n ? ys[z] : nullptr;
+        q.set[z] = z < n ? set[z] : 0;
+        if (z < n && (set[z] < 0 || set[z] >= n_sets)) return cudaErrorInvalidValue;
     }
+    q.off = off;
+    const GemmSmem lay = gemm_smem(dt, bn);
+    if (lay.pslots < 2) return cudaErrorInvalidConfiguration;
+    if ((max_rows + bn - 1) / bn > 65535) return cudaErrorInvalidValue;
+    dim3 grid((g.n_tiles + 7) / 8, (max_rows + bn - 1) / bn, n);
+    return launch_any(dt, map, a, q, grid, lay.total, s);
 }
 
 }  // namespace rce

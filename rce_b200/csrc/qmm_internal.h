@@ -101,6 +101,18 @@ size_t gemm_workspace_bytes(const Geometry &g, int t_rows);
 cudaError_t launch_gemm(int dt, const uint8_t *tiles, const Geometry &g, const float *x, size_t ldx, float *y,
                         size_t ldy, int t_rows, void *workspace, int *err, cudaStream_t s);
 
+// Expert-grouped prefill matmul: one launch for up to kGemmMaxGroup weights
+// of one shape.  Entry z multiplies ws[z] by the fp16 activation rows
+// [off[set[z]], off[set[z] + 1]) of xh ([rows][g.n_cols], scaled per row as
+// the MoE prep kernels write it, 1/scale in inv) into the same rows of ys[z]
+// (row stride ldy).  off (n_sets + 1 entries) is read on the device; no set
+// may hold more than max_rows rows; rows_hint (the expected rows over all
+// sets) sizes the token tile.
+constexpr int kGemmMaxGroup = 32;
+cudaError_t launch_gemm_grouped(int dt, const uint8_t *const *ws, float *const *ys, const int *set, int n,
+                                const Geometry &g, const void *xh, const float *inv, int rows, int rows_hint,
+                                const int32_t *off, int n_sets, int max_rows, size_t ldy, int *err, cudaStream_t s);
+
 // MoE pieces (qmm_moe.cu).  route: per token softmax / top_k / renormalise
 // of router logits [t_rows][ld] into idx, w [t_rows][top_k] (n_experts <=
 // 256).  plan: rows for the (token, slot) pairs whose expert lies in
@@ -114,6 +126,14 @@ cudaError_t launch_moe_plan(const int32_t *idx, int pairs, int top_k, int e_begi
 cudaError_t launch_moe_gather(const float *x, size_t ldx, const int32_t *token, int rows, int d_model, float *xg,
                               cudaStream_t s);
 cudaError_t launch_swiglu(const float *g, const float *u, float *h, size_t n, cudaStream_t s);
+// The GEMM inputs of the grouped path, for rows r < *n_rows (a device
+// count; max_rows bounds it): gather_prep xh[r] = fp16(x[token[r]] * s_r),
+// swiglu_prep xh[r] = fp16(silu(g[r]) * u[r] * s_r) (g, u rows of ld
+// floats); s_r a power of two with |v * s_r| < 2^14, inv[r] = 1 / s_r.
+cudaError_t launch_moe_gather_prep(const float *x, size_t ldx, const int32_t *token, const int32_t *n_rows,
+                                   int max_rows, int d_model, void *xh, float *inv, cudaStream_t s);
+cudaError_t launch_moe_swiglu_prep(const float *g, const float *u, size_t ld, const int32_t *n_rows, int max_rows,
+                                   int d_ff, void *xh, float *inv, cudaStream_t s);
 cudaError_t launch_moe_combine(const float *y, int d_model, const int32_t *pos, const float *w, int t_rows, int top_k,
                                float *out, size_t ldo, cudaStream_t s);
 

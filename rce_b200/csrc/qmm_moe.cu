@@ -12,6 +12,7 @@
 #include <cstdint>
 
 #include "qmm_internal.h"
+#include "qmm_prep.cuh"
 
 namespace rce {
 namespace {
@@ -126,6 +127,28 @@ __global__ void swiglu_kernel(const float *g, const float *u, float *h, size_t n
         h[i] = __fmul_rn(silu_ref(g[i]), u[i]);
 }
 
+// GEMM input of the grouped path, row r = blockIdx.x: x[token[r]] scaled and
+// rounded to fp16 (the gather and the dense prep in one pass).
+__global__ void __launch_bounds__(kPrepThreads) gather_prep_kernel(const float *x, size_t ldx, const int32_t *token,
+                                                                    const int32_t *n_rows, int d_model, __half *xh,
+                                                                    float *inv) {
+    const int r = blockIdx.x;
+    if (r >= *n_rows) return;
+    const float *src = x + (size_t)token[r] * ldx;
+    prep_row([&](int i) { return src[i]; }, d_model, xh + (size_t)r * d_model, inv + r);
+}
+
+// GEMM input of the down matmul, row r = blockIdx.x: h = silu(g) * u exactly
+// as swiglu_kernel computes it, scaled and rounded to fp16.
+__global__ void __launch_bounds__(kPrepThreads) swiglu_prep_kernel(const float *g, const float *u, size_t ld,
+                                                                    const int32_t *n_rows, int d_ff, __half *xh,
+                                                                    float *inv) {
+    const int r = blockIdx.x;
+    if (r >= *n_rows) return;
+    const float *gr = g + (size_t)r * ld, *ur = u + (size_t)r * ld;
+    prep_row([&](int i) { return __fmul_rn(silu_ref(gr[i]), ur[i]); }, d_ff, xh + (size_t)r * d_ff, inv + r);
+}
+
 // out[t] = sum over route slots j (in order, from 0) of w[t][j] * y[pos[t][j]],
 // slots whose expert is not local skipped (moe_combine, rce-op-moe/src/lib.rs:98-110).
 __global__ void combine_kernel(const float *y, int d_model, const int32_t *pos, const float *w, int top_k,
@@ -174,6 +197,21 @@ cudaError_t launch_swiglu(const float *g, const float *u, float *h, size_t n, cu
     size_t blocks = (n + 255) / 256;
     if (blocks > 4096) blocks = 4096;
     swiglu_kernel<<<(unsigned)blocks, 256, 0, s>>>(g, u, h, n);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_moe_gather_prep(const float *x, size_t ldx, const int32_t *token, const int32_t *n_rows,
+                                   int max_rows, int d_model, void *xh, float *inv, cudaStream_t s) {
+    if (max_rows <= 0) return cudaSuccess;
+    gather_prep_kernel<<<max_rows, kPrepThreads, 0, s>>>(x, ldx, token, n_rows, d_model, static_cast<__half *>(xh),
+                                                          inv);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_moe_swiglu_prep(const float *g, const float *u, size_t ld, const int32_t *n_rows, int max_rows,
+                                   int d_ff, void *xh, float *inv, cudaStream_t s) {
+    if (max_rows <= 0) return cudaSuccess;
+    swiglu_prep_kernel<<<max_rows, kPrepThreads, 0, s>>>(g, u, ld, n_rows, d_ff, static_cast<__half *>(xh), inv);
     return cudaGetLastError();
 }
 

@@ -1,0 +1,53 @@
+// qmm_prep.cuh -- the activation side of the tensor-core GEMM: one row of f32
+// values scaled by a power of two s (|v * s| < 2^14, so the scaling is exact
+// and no value overflows fp16) and rounded to fp16, with 1/s kept per row.
+// Shared by the dense prep kernel (qmm_gemm.cu) and the MoE gather and
+// SwiGLU preps (qmm_moe.cu), so every GEMM input is rounded the same way.
+#pragma once
+
+#include <cuda_fp16.h>
+
+namespace rce {
+
+constexpr int kPrepThreads = 256;
+
+// One kPrepThreads-thread block per row: val(i) yields element i (it is
+// called twice per element, for the row maximum and for the store).  A row
+// holding a NaN or an infinity gets s = 0 and 1/s = NaN, so its outputs are
+// NaN as the f32 arithmetic would make them.
+template <class Val>
+__device__ __forceinline__ void prep_row(Val val, int k, __half *o, float *inv) {
+    float mx = 0.f;
+    bool fin = true;
+    for (int i = threadIdx.x; i < k; i += kPrepThreads) {
+        const float v = val(i);
+        mx = fmaxf(mx, fabsf(v));
+        fin = fin && isfinite(v);
+    }
+    if (!fin) mx = INFINITY;
+    __shared__ float red[kPrepThreads / 32];
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = mx;
+    __syncthreads();
+    float v = 0.f;
+    for (int w = 0; w < kPrepThreads / 32; w++) v = fmaxf(v, red[w]);
+    float s = 1.f, is = 1.f;
+    if (!isfinite(v)) {
+        s = 0.f;
+        is = __int_as_float(0x7fc00000);
+    } else if (v > 0.f) {
+        int e;
+        frexpf(v, &e);
+        e = max(-100, min(100, e));
+        s = ldexpf(1.f, 14 - e);
+        is = ldexpf(1.f, e - 14);
+    }
+    // the GEMM may start its weight copies now; it reads these rows only
+    // after griddepcontrol.wait, i.e. after this grid has completed
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+    for (int i = threadIdx.x; i < k; i += kPrepThreads) o[i] = __float2half_rn(val(i) * s);
+    if (threadIdx.x == 0) *inv = is;
+}
+
+}  // namespace rce

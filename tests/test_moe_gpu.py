@@ -182,3 +182,71 @@ def test_bad_arguments_are_errors(ctx):
         R.moe_ffn_device(xd, ld, 1, g, d, u)          # up/down shapes swapped
     with pytest.raises(R.QmmError):
         R.moe_ffn_device(xd, ld, 1, g, u, d, expert_range=(1, 1))
+
+
+def _bars(got, want, model):
+    scale = np.abs(want).max()
+    tensor = np.abs(got.astype(np.float64) - want).max() / scale
+    vs_model = np.abs(got - model).max() / scale
+    return tensor, vs_model
+
+
+def test_ffn_grouped_many_experts_ragged(ctx):
+    # 20 experts (two grouped launches for gate/up: 16 experts per launch),
+    # top-4 of 40 tokens: per-expert row counts from 0 to ~20, most below the
+    # 16-token GEMM threshold, all through the grouped tensor-core path
+    assert ctx.prefill_min_tokens == 16
+    dt, n_e, k, d_model, d_ff, t = Q4_K, 20, 4, 256, 512, 40
+    got, want, (g, u, d, x, logits) = _ffn(ctx, dt, n_e, k, d_model, d_ff, t, 31)
+    gate, up, down, _, _ = _setup(dt, n_e, d_model, d_ff, t, 31)
+    model = _fp16_operand_model(dt, gate, up, down, x, logits, k, d_model, d_ff)
+    tensor, vs_model = _bars(got, want, model)
+    print(f"MoE grouped, 20 experts top-4: max-norm {tensor:.3e}, vs the fp16-operand model {vs_model:.3e}")
+    assert tensor <= 1e-3
+    assert vs_model <= 2.5e-4
+
+
+def test_ffn_grouped_expert_ranges_add_up(ctx):
+    import torch
+
+    # the grouped path per expert range: every (expert, token) output is the
+    # same whichever launch computes it, so the ranges add up bit for bit
+    full, _, (g, u, d, x, logits) = _ffn(ctx, Q8_0, 6, 2, 256, 512, 48, 5)
+    xd, ld = torch.from_numpy(x).cuda(), torch.from_numpy(logits).cuda()
+    parts = [R.moe_ffn_device(xd, ld, 2, g, u, d, expert_range=r).cpu().numpy() for r in [(0, 2), (2, 5), (5, 6)]]
+    total = parts[0] + parts[1] + parts[2]
+    print(f"grouped ranges: max |sum - full| = {np.abs(total - full).max():.3e}")
+    assert np.array_equal(total, full)
+
+
+def test_ffn_grouped_graph_replay(ctx):
+    import torch
+
+    # no host synchronisation inside the grouped call: it can be captured in
+    # a CUDA graph and replayed on new inputs
+    dt, n_e, d_model, d_ff, t = Q4_0, 4, 256, 512, 32
+    gate, up, down, x, logits = _setup(dt, n_e, d_model, d_ff, t, 17)
+    g, u, d = _device(ctx, dt, gate, up, down, d_model, d_ff)
+    xd, ld = torch.from_numpy(x).cuda(), torch.from_numpy(logits).cuda()
+    out = torch.empty((t, d_model), dtype=torch.float32, device="cuda")
+    s = torch.cuda.Stream()
+    with torch.cuda.stream(s):
+        R.moe_ffn_device(xd, ld, 2, g, u, d, out=out, stream=s)  # sizes the workspace
+    s.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=s):
+        R.moe_ffn_device(xd, ld, 2, g, u, d, out=out, stream=s)
+    rng = np.random.default_rng(18)
+    for _ in range(2):
+        x2 = synth.activations(t, d_model, rng)
+        l2 = rng.standard_normal((t, n_e)).astype(np.float32)
+        xd.copy_(torch.from_numpy(x2))
+        ld.copy_(torch.from_numpy(l2))
+        graph.replay()
+        torch.cuda.synchronize()
+        eager = R.moe_ffn_device(xd, ld, 2, g, u, d)
+        torch.cuda.synchronize()
+        assert np.array_equal(out.cpu().numpy(), eager.cpu().numpy())
+    want = O.moe_ffn(x2, l2, 2, np.stack(gate), np.stack(up), np.stack(down), dt, d_ff, nthreads=8)
+    assert np.abs(out.cpu().numpy() - want).max() / np.abs(want).max() <= 1e-3
+    assert ctx.device_error() == 0
