@@ -16,9 +16,11 @@ for every word of the step's last epochs) -- strong scaling: the model is
 fixed, value counts its bytes once.
 
 value  = weight bytes of the whole model x steps / device time (max over ranks)
-e2e    = the same through the host C-ABI call (rce_qmm_mm_1d with host buffers,
-         copies in and out on every call), timed by the wall clock around the
-         synchronous calls
+e2e    = the same through the public API with host buffers, copies in and out
+         on every call, timed by the wall clock around the synchronous calls:
+         the host C-ABI call rce_qmm_mm_batched on one GPU; with N GPUs each
+         rank's row-shard matmul with its fused gather (PeerGroup), its input
+         copied in from pinned memory and the whole gathered output copied back
 roofline = the dominant kernel (the 14336x4096 / 4096x14336 Q4_K GEMVs) timed
          launch by launch with CUDA events, algorithmic bytes / duration
 cpu_baseline = the C restatement of the reference's CPU path (oracle/) on one
@@ -458,7 +460,6 @@ def main():
     xs = {D_MODEL: torch.randn((m, D_MODEL), device=dev, generator=gen),
           D_FF: torch.randn((m, D_FF), device=dev, generator=gen)}
     ys = {name: torch.empty((m, n // world), device=dev) for name, n, _ in LAYER}
-    yfull = {name: torch.empty((world * m, n // world), device=dev) for name, n, _ in LAYER} if world > 1 else {}
     if world > 1:
         for name, n, _ in LAYER:
             pg.output(name, m, n)
@@ -636,23 +637,38 @@ def main():
     prefill = prefill_section(args, rank, world, dev, stream, ctx, pg)
     moe = moe_section(args, rank, world, dev, stream, ctx)
 
-    # ---- e2e through the host C-ABI ----------------------------------------------
+    # ---- e2e through the public API with host buffers -----------------------------
+    # N = 1: the C-ABI call rce_qmm_mm_batched (host in, host out; it stages
+    # through pinned memory and synchronises).  N > 1: per matmul the host
+    # activations are staged into pinned memory and copied in, the row shard's
+    # matmul runs with its fused NVLink gather (PeerGroup.mm + gather), and the
+    # whole gathered output is copied back to the host, synchronously.
     e2e = None
     hx = {k: v.cpu().numpy() for k, v in xs.items()}
     hy = {name: np.empty((m, n // world), np.float32) for name, n, _ in LAYER}
     h2d = d2h = 0
     for name, n, k in LAYER:
         h2d += 4 * m * k * args.layers
-        d2h += 4 * m * (n // world) * args.layers
+        d2h += 4 * m * (n // world if world == 1 else n) * args.layers
+    if world > 1:
+        px = {k: torch.empty((m, k), dtype=torch.float32, pin_memory=True) for k in xs}
+        dx = {k: torch.empty((m, k), dtype=torch.float32, device=dev) for k in xs}
+        py = {name: torch.empty((m, n), dtype=torch.float32, pin_memory=True) for name, n, _ in LAYER}
+        hyf = {name: np.empty((m, n), np.float32) for name, n, _ in LAYER}
 
     def e2e_step():
         for mats in layers:
             for name, ns, k, w in mats:
-                R.mm_batched(hx[k], m, w, hy[name].reshape(-1))
-                if world > 1:
-                    t = torch.from_numpy(hy[name]).to(dev)
-                    dist.all_gather_into_tensor(yfull[name], t)
-                    yfull[name].cpu()
+                if world == 1:
+                    R.mm_batched(hx[k], m, w, hy[name].reshape(-1))
+                    continue
+                with torch.cuda.stream(stream):
+                    px[k].numpy()[...] = hx[k]
+                    dx[k].copy_(px[k], non_blocking=True)
+                    pg.mm(dx[k], w, name, rank * ns, stream=stream)
+                    py[name].copy_(pg.gather(name, stream=stream), non_blocking=True)
+                stream.synchronize()
+                hyf[name][...] = py[name].numpy()
 
     e2e_step()
     if world > 1:
@@ -668,7 +684,9 @@ def main():
         e2e_s = float(t.item())
     e2e = {"value": round(total_bytes * args.e2e_steps / e2e_s / 1e9, 3), "unit": "GB/s",
            "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "steps": args.e2e_steps,
-           "timing": "wall clock around the synchronous host C-ABI calls (rce_qmm_mm_batched)"}
+           "timing": ("wall clock around the synchronous host C-ABI calls (rce_qmm_mm_batched)" if world == 1 else
+                      "wall clock around synchronous per-matmul calls: pinned host copy in, row-shard matmul with "
+                      "its fused NVLink gather (PeerGroup.mm + gather), full output copied back; max over ranks")}
 
     # ---- CPU baseline (rank 0, N = 1) ---------------------------------------------
     cpu = None
