@@ -25,9 +25,10 @@ GGUF_F16 = 1
 GGUF_Q4_0 = 2
 GGUF_Q8_0 = 8
 GGUF_Q4_K = 12
+GGUF_Q6_K = 14
 
-BLOCK = {GGUF_Q4_0: 32, GGUF_Q8_0: 32, GGUF_Q4_K: 256}
-BLOCK_BYTES = {GGUF_Q4_0: 18, GGUF_Q8_0: 34, GGUF_Q4_K: 144}
+BLOCK = {GGUF_Q4_0: 32, GGUF_Q8_0: 32, GGUF_Q4_K: 256, GGUF_Q6_K: 256}
+BLOCK_BYTES = {GGUF_Q4_0: 18, GGUF_Q8_0: 34, GGUF_Q4_K: 144, GGUF_Q6_K: 210}
 
 _HERE = os.path.dirname(os.path.abspath(__file__))
 _LIB_PATH = os.path.join(_HERE, "_build", "libqmm_oracle.so")
@@ -309,6 +310,31 @@ def unpack_q4_k(wbytes, n_rows, n_cols):
     return q, s, o
 
 
+def unpack_q6_k(wbytes, n_rows, n_cols):
+    """Q6_K bytes -> q [n][k] in -32..31 and s = d*sc [n][k/16] (f32, each
+    product exact), the operands of the spec's matmul_q6_k
+    (spec/RCE-SPEC.md, tensor.matmul_q6_k; kquant.rs:67-150), decoded with
+    independent numpy integer code: element 128 o + 32 q + l of a block takes
+    its low four bits from ql[64 o + 32 (q & 1) + l] (low nibble for q < 2)
+    and its high two from bits 2q of qh[32 o + l]."""
+    nsb = n_cols // 256
+    b = _u8(wbytes).reshape(n_rows, nsb, 210).astype(np.int32)
+    ql, qh = b[:, :, :128], b[:, :, 128:192]
+    sc = b[:, :, 192:208]
+    sc = np.where(sc >= 128, sc - 256, sc)
+    d = _f16(b[:, :, 208].astype(np.uint8), b[:, :, 209].astype(np.uint8))
+    q = np.zeros((n_rows, nsb, 256), dtype=np.int32)
+    for o in range(2):
+        for qq in range(4):
+            c0 = 64 * o + 32 * (qq & 1)
+            lo = ql[:, :, c0:c0 + 32]
+            lo = (lo & 15) if qq < 2 else (lo >> 4)
+            hi = (qh[:, :, 32 * o:32 * o + 32] >> (2 * qq)) & 3
+            q[:, :, 128 * o + 32 * qq:128 * o + 32 * qq + 32] = (lo | (hi << 4)) - 32
+    s = (d[:, :, None] * sc.astype(np.float32)).astype(np.float32).reshape(n_rows, nsb * 16)
+    return q.reshape(n_rows, n_cols), s
+
+
 def py_mm_1d(a, wbytes, dtype, n_rows, n_cols):
     """Pure-Python per-operation np.float32 restatement of mm_1d (tiny shapes)."""
     f = np.float32
@@ -351,6 +377,19 @@ def py_mm_1d(a, wbytes, dtype, n_rows, n_cols):
                 acc = f(acc + f(s[j, 2 * g + 1] * u2))
                 acc = f(acc - f(o[j, 2 * g + 1] * a2))
                 sumf = f(sumf + acc)
+            out[j] = sumf
+    elif dtype == GGUF_Q6_K:
+        # the spec's matmul_q6_k order: per half of a super-block, l = 0..31,
+        # positions l, l+32, l+64, l+96; y += (s * q) * x from +0.0
+        q, s = unpack_q6_k(wbytes, n_rows, n_cols)
+        for j in range(n_rows):
+            sumf = f(0)
+            for sb in range(n_cols // 256):
+                for o in range(2):
+                    for l in range(32):
+                        for qq in range(4):
+                            t = 256 * sb + 128 * o + 32 * qq + l
+                            sumf = f(sumf + f(f(s[j, t // 16] * f(q[j, t])) * a[t]))
             out[j] = sumf
     else:
         raise ValueError(dtype)

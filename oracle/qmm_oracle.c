@@ -108,6 +108,7 @@ size_t oracle_tensor_byte_size(int dtype, size_t n) {
     case ORACLE_GGUF_Q4_0: return (n + 31) / 32 * 18;
     case ORACLE_GGUF_Q8_0: return (n + 31) / 32 * 34;
     case ORACLE_GGUF_Q4_K: return (n + 255) / 256 * 144;
+    case ORACLE_GGUF_Q6_K: return (n + 255) / 256 * 210;
     default: return 0;
     }
 }
@@ -172,8 +173,43 @@ static void dequant_q4_k(const uint8_t *data, size_t nbytes, size_t n, float *ou
     }
 }
 
+/* The six-bit code of element 128 o + 32 q + l of a Q6_K block (ql, qh as
+ * in the block), minus 32: ql[64 o + 32 (q & 1) + l] supplies the low four
+ * bits (low nibble for q < 2, high nibble above), qh[32 o + l] bits 2q, 2q+1
+ * the high two. */
+static int q6k_code(const uint8_t *ql, const uint8_t *qh, int o, int q, int l) {
+    const uint8_t b = ql[64 * o + 32 * (q & 1) + l];
+    const int lo = q < 2 ? (b & 0x0F) : (b >> 4);
+    const int hi = (qh[32 * o + l] >> (2 * q)) & 0x03;
+    return (lo | (hi << 4)) - 32;
+}
+
+/* dequant_q6_k (dequant.rs:658-698): per half o and l = 0..31, the four
+ * elements l, l+32, l+64, l+96 of the half, value = (d * sc) * q with the
+ * scale of the element's 16 (is = l / 16, + 2 per quarter). */
+static void dequant_q6_k(const uint8_t *data, size_t nbytes, size_t n, float *out) {
+    size_t nb = (n + 255) / 256;
+    memset(out, 0, nb * 256 * sizeof(float));
+    for (size_t b = 0; b < nb; b++) {
+        size_t s = b * 210;
+        if (s + 210 > nbytes) break;
+        const uint8_t *ql = data + s, *qh = data + s + 128;
+        const int8_t *sc = (const int8_t *)(data + s + 192);
+        float d = rd_f16(data + s + 208);
+        for (int o = 0; o < 2; o++)
+            for (int l = 0; l < 32; l++) {
+                int is = l / 16;
+                for (int q = 0; q < 4; q++) {
+                    float t = d * (float)sc[8 * o + is + 2 * q];
+                    out[b * 256 + 128 * o + 32 * q + l] = t * (float)q6k_code(ql, qh, o, q, l);
+                }
+            }
+    }
+}
+
 int oracle_dequant(const uint8_t *bytes, size_t nbytes, int dtype, size_t n, float *out) {
     switch (dtype) {
+    case ORACLE_GGUF_Q6_K: dequant_q6_k(bytes, nbytes, n, out); return 0;
     case ORACLE_GGUF_Q4_0: dequant_q4_0(bytes, nbytes, n, out); return 0;
     case ORACLE_GGUF_Q8_0: dequant_q8_0(bytes, nbytes, n, out); return 0;
     case ORACLE_GGUF_Q4_K: dequant_q4_k(bytes, nbytes, n, out); return 0;
@@ -271,6 +307,32 @@ static float dot_row_q4_k(const float *a, const uint8_t *row, size_t k) {
     return sumf;
 }
 
+/* One row of mm_1d_q6_k (rce-op-qmm/src/lib.rs:1667-1705) == dot_row_q6_k
+ * (:426-450): per super-block, half o and l = 0..31, four terms in the
+ * order q1..q4, each ((d * sc) * q) * a added to the single running sum. */
+static float dot_row_q6_k(const float *a, const uint8_t *row, size_t k) {
+    float sumf = 0.0f;
+    for (size_t ib = 0; ib < k / 256; ib++) {
+        const uint8_t *s = row + ib * 210;
+        const uint8_t *ql = s, *qh = s + 128;
+        const int8_t *sc = (const int8_t *)(s + 192);
+        float d = rd_f16(s + 208);
+        for (int o = 0; o < 2; o++) {
+            const float *ab = a + ib * 256 + 128 * o;
+            for (int l = 0; l < 32; l++) {
+                int is = l / 16;
+                for (int q = 0; q < 4; q++) {
+                    float t = d * (float)sc[8 * o + is + 2 * q];
+                    t = t * (float)q6k_code(ql, qh, o, q, l);
+                    t = t * ab[32 * q + l];
+                    sumf = sumf + t;
+                }
+            }
+        }
+    }
+    return sumf;
+}
+
 typedef float (*dot_fn)(const float *, const uint8_t *, size_t);
 
 static int row_kernel(int dtype, dot_fn *fn, size_t *bb, size_t *blk) {
@@ -278,6 +340,7 @@ static int row_kernel(int dtype, dot_fn *fn, size_t *bb, size_t *blk) {
     case ORACLE_GGUF_Q4_0: *fn = dot_row_q4_0; *bb = 18; *blk = 32; return 0;
     case ORACLE_GGUF_Q8_0: *fn = dot_row_q8_0; *bb = 34; *blk = 32; return 0;
     case ORACLE_GGUF_Q4_K: *fn = dot_row_q4_k; *bb = 144; *blk = 256; return 0;
+    case ORACLE_GGUF_Q6_K: *fn = dot_row_q6_k; *bb = 210; *blk = 256; return 0;
     default: return -1;
     }
 }

@@ -139,6 +139,14 @@ int run_matmul(rce_qmm_ctx *ctx, const rce_qmm_weight *w, const float *d_x, size
         return ok();
     }
     size_t t0 = 0;
+    if (w->dtype == rce::GGUF_Q6_K) {  // its own decode GEMV, passes of kQ6MaxTokens tokens
+        for (; t0 < t_rows; t0 += (size_t)rce::kQ6MaxTokens) {
+            const size_t left = t_rows - t0;
+            const int m = (int)(left < (size_t)rce::kQ6MaxTokens ? left : (size_t)rce::kQ6MaxTokens);
+            CUDA_TRY(rce::launch_gemv_q6k(w->dev, g, d_x + t0 * lda, lda, d_y + t0 * ldo, ldo, m, ctx->sm_count, s));
+        }
+        return ok();
+    }
     while (t0 < t_rows) {
         const size_t left = t_rows - t0;
         const int m = (int)(left < (size_t)rce::kGemvMaxTokens ? left : (size_t)rce::kGemvMaxTokens);
@@ -181,7 +189,8 @@ int register_common(rce_qmm_ctx *ctx, const void *src, bool src_on_device, size_
     if (!ctx || !src || !out) return fail(RCE_QMM_ERR_INVALID, "weight_register: null argument");
     *out = nullptr;
     if (!rce::dtype_supported(dtype))
-        return fail(RCE_QMM_ERR_UNSUPPORTED, "weight_register: GGUF dtype %d is not supported (Q4_0=2, Q8_0=8, Q4_K=12)",
+        return fail(RCE_QMM_ERR_UNSUPPORTED,
+                    "weight_register: GGUF dtype %d is not supported (Q4_0=2, Q8_0=8, Q4_K=12, Q6_K=14)",
                     dtype);
     if (n_rows <= 0 || n_cols <= 0)
         return fail(RCE_QMM_ERR_INVALID, "weight_register: shape %lld x %lld", (long long)n_rows,
@@ -244,6 +253,7 @@ size_t rce_qmm_tensor_byte_size(int dt, uint64_t n) {
     case RCE_QMM_GGUF_Q4_0: return (size_t)((n + 31) / 32 * 18);
     case RCE_QMM_GGUF_Q8_0: return (size_t)((n + 31) / 32 * 34);
     case RCE_QMM_GGUF_Q4_K: return (size_t)((n + 255) / 256 * 144);
+    case RCE_QMM_GGUF_Q6_K: return (size_t)((n + 255) / 256 * 210);
     default: return 0;
     }
 }
@@ -448,8 +458,9 @@ int rce_qmm_mm_batched_device_multi(rce_qmm_ctx *ctx, const float *d_a, size_t l
                     (long long)ws[0]->g.n_cols);
     DeviceGuard dg(ctx->device);
     cudaStream_t s = (cudaStream_t)stream;
-    if (ctx->prefill_min_tokens > 0 && t_rows >= (size_t)ctx->prefill_min_tokens) {
-        // the tensor-core GEMM, one weight at a time
+    if ((ctx->prefill_min_tokens > 0 && t_rows >= (size_t)ctx->prefill_min_tokens) ||
+        ws[0]->dtype == rce::GGUF_Q6_K) {
+        // the tensor-core GEMM (or Q6_K's own GEMV), one weight at a time
         for (size_t i = 0; i < n_w; i++) {
             int rc = run_matmul(ctx, ws[i], d_a, lda, t_rows, d_outs[i], ldos[i], s);
             if (rc) return rc;
@@ -641,7 +652,8 @@ int rce_qmm_mm_batched_device_gather(rce_qmm_ctx *ctx, const float *d_a, size_t 
     ga.epoch_base = d_epoch_base;
     const Geometry &g = w->g;
     float *y_own = d_y + row_offset;
-    if (ctx->prefill_min_tokens > 0 && t_rows >= (size_t)ctx->prefill_min_tokens && t_rows <= (size_t)INT32_MAX) {
+    if ((ctx->prefill_min_tokens > 0 && t_rows >= (size_t)ctx->prefill_min_tokens && t_rows <= (size_t)INT32_MAX) ||
+        w->dtype == rce::GGUF_Q6_K) {
         rc = run_matmul(ctx, w, d_a, lda, t_rows, y_own, ldy, s);
         if (rc) return rc;
         CUDA_TRY(rce::launch_gather_push(ga, d_y, (int)t_rows, g.n_rows, ldy, s));
@@ -700,8 +712,10 @@ int rce_qmm_mm_batched_device_multi_gather(rce_qmm_ctx *ctx, const float *d_a, s
         ga[i].epoch = epoch;
         ga[i].epoch_base = d_epoch_base;
     }
-    if (ctx->prefill_min_tokens > 0 && t_rows >= (size_t)ctx->prefill_min_tokens && t_rows <= (size_t)INT32_MAX) {
-        // the tensor-core GEMM per weight, each output pushed to the peers after it
+    if ((ctx->prefill_min_tokens > 0 && t_rows >= (size_t)ctx->prefill_min_tokens && t_rows <= (size_t)INT32_MAX) ||
+        ws[0]->dtype == rce::GGUF_Q6_K) {
+        // the tensor-core GEMM (or Q6_K's GEMV) per weight, each output pushed
+        // to the peers after it
         for (size_t i = 0; i < n_w; i++) {
             int rc = run_matmul(ctx, ws[i], d_a, lda, t_rows, d_ys[i] + row_offsets[i], ldys[i], s);
             if (rc) return rc;

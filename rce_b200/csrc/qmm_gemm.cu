@@ -167,6 +167,11 @@ __device__ __forceinline__ unsigned long long f2fma(unsigned long long a, unsign
     asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(a), "l"(b), "l"(c));
     return r;
 }
+__device__ __forceinline__ unsigned long long f2mul(unsigned long long a, unsigned long long b) {
+    unsigned long long r;
+    asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+    return r;
+}
 // fp16x2 of the two f32 lanes (round to nearest even).
 __device__ __forceinline__ uint32_t f2_to_h2(unsigned long long v) {
     return pack_h2(__uint_as_float((uint32_t)v), __uint_as_float((uint32_t)(v >> 32)));
@@ -217,6 +222,20 @@ struct RowHalf {
                 s[j][1] = f2pack(d2, d2);
                 o[j][1] = f2pack(-m2, -m2);
             }
+        } else if (DT == GGUF_Q6_K) {
+            // k-block j, 16-value group k2 of this half: scale 4 j + 2 hf + k2,
+            // d * sc exact in f32 (11 x 8 bits)
+            const float d = h2f(*reinterpret_cast<const uint16_t *>(ch + kQ6D + 2 * r16));
+            const uint4 sv = *reinterpret_cast<const uint4 *>(ch + kQ6Sc + r16 * 16);
+            const uint32_t sw[4] = {sv.x, sv.y, sv.z, sv.w};
+#pragma unroll
+            for (int j = 0; j < 4; j++)
+#pragma unroll
+                for (int k2 = 0; k2 < 2; k2++) {
+                    const int i = 4 * j + 2 * hf + k2;  // hf is 0 or 1: the word is sw[j]
+                    const float ds = d * (float)(int8_t)(sw[i >> 2] >> (8 * (i & 3)));
+                    s[j][k2] = f2pack(ds, ds);
+                }
         }
     }
 
@@ -226,7 +245,33 @@ struct RowHalf {
         const int lane = 4 * r + J;
         uint32_t h[16];  // 32 fp16 values
         int cc[4];       // the four 16-byte A chunks they fill
-        if (DT == GGUF_Q4_K) {
+        if (DT == GGUF_Q6_K) {
+            // columns 32 hf .. 32 hf + 31 of the k-block: 16 lo-plane bytes
+            // (two codes each) and 8 hi-plane bytes (four each); value =
+            // (d * sc) * (code - 32), one rounding as in dequant_q6_k, then fp16
+            const uint4 lq = *reinterpret_cast<const uint4 *>(ch + r16 * 128 + 32 * J + 16 * hf);
+            const uint2 hq = *reinterpret_cast<const uint2 *>(ch + kQ6Hi + r16 * 64 + 16 * J + 8 * hf);
+            const uint32_t lw[4] = {lq.x, lq.y, lq.z, lq.w};
+            const unsigned long long bias = f2pack(-8388640.f, -8388640.f);  // 2^23 + 32
+#pragma unroll
+            for (int k = 0; k < 4; k++) {  // values 8k .. 8k + 7
+                const uint32_t hw = ((k < 2 ? hq.x : hq.y) >> (16 * (k & 1))) & 0xFFFFu;
+                uint32_t sp;
+                asm("prmt.b32 %0, %1, %2, 0x5140;" : "=r"(sp) : "r"(hw & 0x0F0Fu), "r"((hw >> 4) & 0x0F0Fu));
+                const uint32_t ua = (lw[k] & 0x0F0F0F0Fu) | ((sp << 4) & 0x30303030u);         // values 2b
+                const uint32_t ub = ((lw[k] >> 4) & 0x0F0F0F0Fu) | ((sp << 2) & 0x30303030u);  // values 2b + 1
+#pragma unroll
+                for (int p = 0; p < 4; p++) {
+                    uint32_t fa, fb;
+                    asm("prmt.b32 %0, %1, %2, %3;" : "=r"(fa) : "r"(ua), "r"(0x4B000000u), "r"(0x7540u | p));
+                    asm("prmt.b32 %0, %1, %2, %3;" : "=r"(fb) : "r"(ub), "r"(0x4B000000u), "r"(0x7540u | p));
+                    const unsigned long long q =
+                        f2add((unsigned long long)fa | ((unsigned long long)fb << 32), bias);
+                    h[4 * k + p] = f2_to_h2(f2mul(q, s[J][k >> 1]));
+                }
+                cc[k] = 4 * hf + k;
+            }
+        } else if (DT == GGUF_Q4_K) {
             const uint4 q = *reinterpret_cast<const uint4 *>(ch + ((2 * rh + hf) * 32 + lane) * 16);
             const uint32_t w[4] = {q.x, q.y, q.z, q.w};
             const unsigned long long bias = f2pack(-8388608.f, -8388608.f);
@@ -698,6 +743,7 @@ cudaError_t launch_any(int dt, const CUtensorMap &map, const GemmArgs &a, const 
     case GGUF_Q4_K: return launch_dt<GGUF_Q4_K>(map, a, q, grid, smem, s);
     case GGUF_Q4_0: return launch_dt<GGUF_Q4_0>(map, a, q, grid, smem, s);
     case GGUF_Q8_0: return launch_dt<GGUF_Q8_0>(map, a, q, grid, smem, s);
+    case GGUF_Q6_K: return launch_dt<GGUF_Q6_K>(map, a, q, grid, smem, s);
     default: return cudaErrorInvalidValue;
     }
 }
@@ -721,9 +767,9 @@ cudaError_t act_map(CUtensorMap *map, const void *xh, int rows, int64_t k, int b
 
 int gemm_bn(int dt, int t_rows) {
     // 512 tokens: two N = 256 accumulators fill tensor memory, so each weight
-    // tile is dequantised once per 512 tokens (Q8_0's larger chunks leave
-    // no room for the 2 x 64 KB activation stages)
-    if (t_rows >= 512 && dt != GGUF_Q8_0) return 512;
+    // tile is dequantised once per 512 tokens (the larger chunks of Q8_0 and
+    // Q6_K leave no room for the 2 x 64 KB activation stages)
+    if (t_rows >= 512 && dt != GGUF_Q8_0 && dt != GGUF_Q6_K) return 512;
     if (t_rows >= 256) return 256;
     int bn = (t_rows + 15) / 16 * 16;
     return bn < 16 ? 16 : bn;

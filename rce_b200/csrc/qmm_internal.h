@@ -20,6 +20,18 @@ cudaError_t launch_unpack(int dt, const uint8_t *tiles, uint8_t *gguf, const Geo
 cudaError_t launch_dequant(int dt, const uint8_t *tiles, float *out, size_t ldo, const Geometry &g,
                            int64_t row0, int64_t row1, cudaStream_t s);
 
+// Q6_K (qmm_q6k.cu): repack / unpack / dequant as above, and the decode GEMV
+// for m <= kQ6MaxTokens tokens.
+constexpr int kQ6MaxTokens = 2;
+cudaError_t launch_repack_q6k(const uint8_t *gguf, uint8_t *tiles, const Geometry &g, cudaStream_t s);
+cudaError_t launch_unpack_q6k(const uint8_t *tiles, uint8_t *gguf, const Geometry &g, int64_t row0, int64_t row1,
+                              cudaStream_t s);
+cudaError_t launch_dequant_q6k(const uint8_t *tiles, float *out, size_t ldo, const Geometry &g, int64_t row0,
+                               int64_t row1, cudaStream_t s);
+int q6k_gemv_warps(const Geometry &g, int sm_count);
+cudaError_t launch_gemv_q6k(const uint8_t *tiles, const Geometry &g, const float *x, size_t ldx, float *y,
+                            size_t ldy, int m, int sm_count, cudaStream_t s);
+
 // Fused all-gather of a row-sharded output over peer memory (see
 // qmm_gather.cuh): rank `rank` of `world` computes rows [row_off, row_off +
 // n) of the output, stores them in its own y, and stores each value with

@@ -252,6 +252,7 @@ cudaError_t launch_repack(int dt, const uint8_t *gguf, uint8_t *tiles, const Geo
     const int threads = 256;
     const unsigned blocks = (unsigned)((total + threads - 1) / threads);
     switch (dt) {
+    case GGUF_Q6_K: return launch_repack_q6k(gguf, tiles, g, s);
     case GGUF_Q4_K: repack_kernel<GGUF_Q4_K><<<blocks, threads, 0, s>>>(gguf, tiles, g); break;
     case GGUF_Q4_0: repack_kernel<GGUF_Q4_0><<<blocks, threads, 0, s>>>(gguf, tiles, g); break;
     case GGUF_Q8_0: repack_kernel<GGUF_Q8_0><<<blocks, threads, 0, s>>>(gguf, tiles, g); break;
@@ -267,6 +268,7 @@ cudaError_t launch_unpack(int dt, const uint8_t *tiles, uint8_t *gguf, const Geo
     const int threads = 128;
     const unsigned blocks = (unsigned)((n + threads - 1) / threads);
     switch (dt) {
+    case GGUF_Q6_K: return launch_unpack_q6k(tiles, gguf, g, row0, row1, s);
     case GGUF_Q4_K: unpack_kernel<GGUF_Q4_K><<<blocks, threads, 0, s>>>(tiles, gguf, g, row0, row1); break;
     case GGUF_Q4_0: unpack_kernel<GGUF_Q4_0><<<blocks, threads, 0, s>>>(tiles, gguf, g, row0, row1); break;
     case GGUF_Q8_0: unpack_kernel<GGUF_Q8_0><<<blocks, threads, 0, s>>>(tiles, gguf, g, row0, row1); break;
@@ -282,6 +284,7 @@ cudaError_t launch_dequant(int dt, const uint8_t *tiles, float *out, size_t ldo,
     const int threads = 128;
     const unsigned blocks = (unsigned)((n + threads - 1) / threads);
     switch (dt) {
+    case GGUF_Q6_K: return launch_dequant_q6k(tiles, out, ldo, g, row0, row1, s);
     case GGUF_Q4_K: dequant_kernel<GGUF_Q4_K><<<blocks, threads, 0, s>>>(tiles, out, ldo, g, row0, row1); break;
     case GGUF_Q4_0: dequant_kernel<GGUF_Q4_0><<<blocks, threads, 0, s>>>(tiles, out, ldo, g, row0, row1); break;
     case GGUF_Q8_0: dequant_kernel<GGUF_Q8_0><<<blocks, threads, 0, s>>>(tiles, out, ldo, g, row0, row1); break;

@@ -31,6 +31,15 @@
 //     quants [i 0..7][lane][16 B]: row r + 8 (i >> 2), bytes
 //       [16 (i & 1), +16) of block 2 g + ((i >> 1) & 1);
 //     scales [lane][4 x f16] as Q4_0.
+//   Q6_K (210 B per 256; chunk 3360 B; qmm_q6k.cu): the six-bit codes
+//     u = q + 32 of value v (0..255) of row r, split as in GGUF into four low
+//     and two high bits but re-ordered by value: lo plane [row][128 B], byte
+//     i = values 2i (low nibble) and 2i + 1 (high nibble); hi plane at 2048
+//     [row][64 B], byte i = values 4i .. 4i + 3 (bits 2e, 2e + 1); the 16
+//     int8 scales per row at 3072 [row][16 B] and d at 3328 [row][f16], as
+//     in GGUF.  Lane L of the GEMV reads values 8L .. 8L + 7 of a row: one
+//     32-bit word of the lo plane, one 16-bit word of the hi plane, scale
+//     L / 2.
 // Rows past n_rows and columns past n_cols are zero (zero scale and zero
 // quants), so padded elements contribute exactly 0.
 #pragma once
@@ -39,18 +48,26 @@
 
 namespace rce {
 
-enum : int { GGUF_F32 = 0, GGUF_F16 = 1, GGUF_Q4_0 = 2, GGUF_Q8_0 = 8, GGUF_Q4_K = 12 };
+enum : int { GGUF_F32 = 0, GGUF_F16 = 1, GGUF_Q4_0 = 2, GGUF_Q8_0 = 8, GGUF_Q4_K = 12, GGUF_Q6_K = 14 };
 
 constexpr int TILE_ROWS = 16;
 constexpr int CHUNK_K = 256;
 
-__host__ __device__ constexpr int chunk_bytes(int dt) { return dt == GGUF_Q8_0 ? 4352 : 2304; }
-__host__ __device__ constexpr int quant_bytes(int dt) { return dt == GGUF_Q8_0 ? 4096 : 2048; }
-__host__ __device__ constexpr int gguf_block(int dt) { return dt == GGUF_Q4_K ? 256 : 32; }
-__host__ __device__ constexpr int gguf_block_bytes(int dt) {
-    return dt == GGUF_Q4_K ? 144 : (dt == GGUF_Q8_0 ? 34 : 18);
+__host__ __device__ constexpr int chunk_bytes(int dt) {
+    return dt == GGUF_Q8_0 ? 4352 : (dt == GGUF_Q6_K ? 3360 : 2304);
 }
-inline bool dtype_supported(int dt) { return dt == GGUF_Q4_0 || dt == GGUF_Q8_0 || dt == GGUF_Q4_K; }
+__host__ __device__ constexpr int quant_bytes(int dt) {
+    return dt == GGUF_Q8_0 ? 4096 : (dt == GGUF_Q6_K ? 3072 : 2048);
+}
+__host__ __device__ constexpr int gguf_block(int dt) { return dt == GGUF_Q4_K || dt == GGUF_Q6_K ? 256 : 32; }
+__host__ __device__ constexpr int gguf_block_bytes(int dt) {
+    return dt == GGUF_Q4_K ? 144 : (dt == GGUF_Q8_0 ? 34 : (dt == GGUF_Q6_K ? 210 : 18));
+}
+inline bool dtype_supported(int dt) {
+    return dt == GGUF_Q4_0 || dt == GGUF_Q8_0 || dt == GGUF_Q4_K || dt == GGUF_Q6_K;
+}
+// Q6_K chunk planes (qmm_q6k.cu).
+constexpr int kQ6Hi = 2048, kQ6Sc = 3072, kQ6D = 3328;
 
 struct Geometry {
     int64_t n_rows = 0, n_cols = 0;

@@ -60,6 +60,17 @@ extern "C" int rce_qmm_mm_batched_device_noalloc(rce_qmm_ctx *ctx, const float *
     if (cd.status != cudaSuccess)
         return err(RCE_QMM_ERR_CUDA, "mm_batched_device_noalloc: set device: %s", cudaGetErrorString(cd.status));
     cudaStream_t s = static_cast<cudaStream_t>(stream);
+    if (w->dtype == rce::GGUF_Q6_K) {  // Q6_K's decode GEMV: no workspace either
+        for (size_t t0 = 0; t0 < t_rows; t0 += (size_t)rce::kQ6MaxTokens) {
+            const size_t left = t_rows - t0;
+            const int m = (int)(left < (size_t)rce::kQ6MaxTokens ? left : (size_t)rce::kQ6MaxTokens);
+            cudaError_t e = rce::launch_gemv_q6k(w->dev, g, d_a + t0 * lda, lda, d_out + t0 * ldo, ldo, m,
+                                                 ctx->sm_count, s);
+            if (e != cudaSuccess)
+                return err(RCE_QMM_ERR_CUDA, "mm_batched_device_noalloc: launch: %s", cudaGetErrorString(e));
+        }
+        return RCE_QMM_OK;
+    }
     for (size_t t0 = 0; t0 < t_rows;) {
         const size_t left = t_rows - t0;
         const int m = (int)(left < (size_t)rce::kGemvMaxTokens ? left : (size_t)rce::kGemvMaxTokens);

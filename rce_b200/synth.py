@@ -6,6 +6,8 @@ The value distributions follow the benchmark configurations of this path:
   Q4_K: fp16 d and dmin = |N(0,1)| * 0.01, the 12 packed scale bytes and the
         128 nibble bytes uniform (so every 6-bit scale/min and every nibble
         is uniform);
+  Q6_K: fp16 d = |N(0,1)| * 0.01, the 16 int8 scales uniform in [-128, 127],
+        the 192 code bytes uniform (every 6-bit code uniform in 0..63);
   activations: f32 N(0,1).
 Everything is generated from numpy's PCG64 with the given seed, so a (seed,
 shape) pair always produces the same bytes.  The fp16 fields are
@@ -17,7 +19,7 @@ import numpy as np
 
 from .gguf import GgufDtype
 
-DEFAULT_SCALE = {GgufDtype.Q8_0: 0.01, GgufDtype.Q4_0: 0.02, GgufDtype.Q4K: 0.01}
+DEFAULT_SCALE = {GgufDtype.Q8_0: 0.01, GgufDtype.Q4_0: 0.02, GgufDtype.Q4K: 0.01, GgufDtype.Q6K: 0.01}
 
 
 def _f16_bytes(v: np.ndarray) -> np.ndarray:
@@ -53,6 +55,15 @@ def q4_k(n_rows: int, n_cols: int, rng: np.random.Generator, scale: float = 0.01
     return blocks.reshape(-1)
 
 
+def q6_k(n_rows: int, n_cols: int, rng: np.random.Generator, scale: float = 0.01) -> np.ndarray:
+    nsb = n_cols // 256
+    blocks = np.empty((n_rows, nsb, 210), dtype=np.uint8)
+    blocks[:, :, :208] = rng.integers(0, 256, size=(n_rows, nsb, 208), dtype=np.uint8)
+    d = np.abs(rng.standard_normal((n_rows, nsb), dtype=np.float32)) * np.float32(scale)
+    blocks[:, :, 208:210] = _f16_bytes(d)
+    return blocks.reshape(-1)
+
+
 def weights(dtype, n_rows: int, n_cols: int, rng, scale=None) -> np.ndarray:
     dt = GgufDtype.parse(dtype)
     s = DEFAULT_SCALE[dt] if scale is None else scale
@@ -62,6 +73,8 @@ def weights(dtype, n_rows: int, n_cols: int, rng, scale=None) -> np.ndarray:
         return q4_0(n_rows, n_cols, rng, s)
     if dt == GgufDtype.Q4K:
         return q4_k(n_rows, n_cols, rng, s)
+    if dt == GgufDtype.Q6K:
+        return q6_k(n_rows, n_cols, rng, s)
     raise ValueError(f"no generator for {dt}")
 
 
@@ -90,6 +103,12 @@ def device_weights(dtype, n_rows: int, n_cols: int, gen, device, scale=None):
 
     dt = GgufDtype.parse(dtype)
     s = DEFAULT_SCALE[dt] if scale is None else scale
+    if dt == GgufDtype.Q6K:
+        nb = n_rows * n_cols // 256
+        raw = torch.randint(0, 256, (nb, 210), dtype=torch.uint8, device=device, generator=gen)
+        d = (torch.randn(nb, device=device, generator=gen).abs() * s).to(torch.float16)
+        raw[:, 208:210] = d.view(torch.uint8).view(nb, 2)
+        return raw.view(-1)
     if dt == GgufDtype.Q4K:
         nb, bb = n_rows * n_cols // 256, 144
     elif dt == GgufDtype.Q8_0:

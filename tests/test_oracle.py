@@ -259,3 +259,72 @@ def test_golden_seeded_cases(golden, case):
     rows = min(n, 256)
     y = np.stack([O.mm_1d_rows(x[t], w, dt, n, k, 0, rows) for t in range(m)])
     assert np.array_equal(y.view(np.uint32), golden[f"{name}__y"][:, :rows].view(np.uint32))
+
+
+# ---- Q6_K (rce-op-qmm/src/lib.rs:1667-1705, dequant.rs:658-698) --------------
+
+def _q6k_serial_fixture():
+    """mm_1d_serial_matches_parallel's Q6_K case (rce-op-qmm/src/lib.rs:
+    3629-3665): k = 512, n = 7, bytes (i * 37 + 11) & 0xFF, every block's d
+    patched to f16(0.05), a_i = sin(0.017 i - 0.3)."""
+    k, n = 512, 7
+    a = np.sin(np.arange(k, dtype=np.float32) * np.float32(0.017) - np.float32(0.3)).astype(np.float32)
+    wb = ((np.arange(n * (k // 256) * 210, dtype=np.int64) * 37 + 11) & 0xFF).astype(np.uint8)
+    blocks = wb.reshape(-1, 210)
+    blocks[:, 208:210] = np.array([0.05], dtype=np.float16).view(np.uint8)
+    return a, wb, n, k
+
+
+def test_q6k_byte_size():
+    assert O.tensor_byte_size(O.GGUF_Q6_K, 256) == 210
+    assert O.tensor_byte_size(O.GGUF_Q6_K, 4096 * 14336) == 4096 * 14336 // 256 * 210
+
+
+def test_q6k_python_restatement_bit_exact():
+    # the C restatement of dot_row_q6_k against the spec-order pure-Python
+    # one (tensor.matmul_q6_k: per half, l = 0..31, positions l, l+32, l+64,
+    # l+96; y += (s * q) * x), bit for bit, on the reference test's fixture
+    a, wb, n, k = _q6k_serial_fixture()
+    got = O.mm_1d(a, wb, O.GGUF_Q6_K, n, k)
+    want = O.py_mm_1d(a, wb, O.GGUF_Q6_K, n, k)
+    assert np.array_equal(got.view(np.uint32), want.view(np.uint32))
+    # serial (1 thread) == row-parallel (7 threads), as the reference asserts
+    par = O.mm_1d(a, wb, O.GGUF_Q6_K, n, k, nthreads=7)
+    assert np.array_equal(got.view(np.uint32), par.view(np.uint32))
+
+
+def test_q6k_dequant_equals_spec_values():
+    # dequant_q6_k's (d * sc) * q equals s * q of the independent unpacking
+    # (s = d * sc exact), bit for bit, and the matmul agrees with
+    # dequantise-then-dot to f32 rounding
+    rng = np.random.default_rng(14)
+    from rce_b200 import synth
+
+    n, k = 24, 1024
+    wb = synth.weights(O.GGUF_Q6_K, n, k, rng)
+    deq = O.dequant(wb, O.GGUF_Q6_K, n * k).reshape(n, k)
+    q, s = O.unpack_q6_k(wb, n, k)
+    assert np.array_equal(deq.view(np.uint32), (np.repeat(s, 16, axis=1) * q.astype(np.float32)).view(np.uint32))
+    x = synth.activations(1, k, rng)[0]
+    got = O.mm_1d(x, wb, O.GGUF_Q6_K, n, k)
+    want = deq.astype(np.float64) @ x.astype(np.float64)
+    assert np.abs(got - want).max() / np.abs(want).max() < 1e-5
+
+
+def test_q6k_code_layout_known_answers():
+    # one block by hand: value 128 o + 32 q + l takes ql[64 o + 32 (q & 1) + l]
+    # (low nibble for q < 2) and bits 2q of qh[32 o + l]; value = d * sc * (code - 32)
+    blk = np.zeros(210, np.uint8)
+    blk[208:210] = np.array([1.0], dtype=np.float16).view(np.uint8)
+    blk[192:208] = np.arange(1, 17, dtype=np.int8).view(np.uint8)  # scale j = j + 1
+    blk[5] = 0x3A          # ql[5]: low nibble 0xA -> value 5, high nibble 3 -> value 69
+    blk[128 + 5] = 0b10_01_11_00  # qh[5]: value 5 hi 0, value 37 hi 3, value 69 hi 1, value 101 hi 2
+    blk[64 + 32 + 7] = 0xF0  # ql[103]: high nibble 15 -> value 128 + 96 + 7 = 231
+    blk[128 + 32 + 7] = 0xC0  # qh[39]: value 231 hi 3
+    d = O.dequant(blk, O.GGUF_Q6_K, 256)
+    assert d[5] == 1 * (0xA - 32)            # scale 0 (values 0..15) = 1
+    assert d[37] == 3 * (((3 << 4) | 0) - 32)  # ql[37] = 0 low nibble, hi 3; scale 2 = 3
+    assert d[69] == 5 * (((1 << 4) | 3) - 32)  # scale 4 = 5
+    assert d[101] == 7 * (((2 << 4) | 0) - 32)  # scale 6 = 7
+    assert d[231] == 15 * (((3 << 4) | 15) - 32)  # scale 14 = 15
+    assert d[0] == 1 * (0 - 32)
