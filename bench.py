@@ -31,6 +31,9 @@ prefill  = BASELINE configs[2]: Q4_K 14336x4096 weight (row-sharded N ways),
          below); four distinct weights per pass (132 MB > L2) replayed from a
          CUDA graph, CUDA events; TFLOP/s = 2 M N K / time, against the
          measured bf16 dense peak
+formats_gemv = one GPU: the decode GEMV of every supported format (Q4_K, Q5_K,
+         Q6_K, Q8_0, Q4_0) at 14336x4096 and 4096x14336, 8 distinct weights
+         per shape in a CUDA graph, CUDA events
 The weights (3.9 GB) are far larger than L2 (126 MB), so no L2 flush is
 needed between steps.
 
@@ -295,6 +298,56 @@ def prefill_section(args, rank, world, dev, stream, ctx, pg=None):
 # ---- MoE FFN ------------------------------------------------------------
 
 MOE_E, MOE_K, MOE_T = 8, 2, 256
+
+
+def formats_section(args, dev, stream, ctx):
+    """Decode GEMV (one token) of every supported format at the stack's two
+    large shapes: 8 distinct weights per shape (more bytes than L2) launched
+    back to back in a CUDA graph, CUDA events; GB/s of algorithmic bytes."""
+    import torch
+
+    import rce_b200 as R
+    from rce_b200 import synth
+    from rce_b200.gguf import GgufDtype, tensor_byte_size
+
+    out = {}
+    for fmt in (GgufDtype.Q4K, GgufDtype.Q5K, GgufDtype.Q6K, GgufDtype.Q8_0, GgufDtype.Q4_0):
+        res = {}
+        for n, k in ((D_FF, D_MODEL), (D_MODEL, D_FF)):
+            ws = []
+            for i in range(8):
+                g = torch.Generator(device=dev)
+                g.manual_seed(5_000_000 + 31 * i + int(fmt))
+                raw = synth.device_weights(fmt, n, k, g, dev)
+                ws.append(R.QuantWeight.from_device_bytes(raw, fmt, n, k, ctx=ctx))
+                del raw
+            x = torch.randn((1, k), device=dev)
+            y = torch.empty((1, n), device=dev)
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.stream(stream):
+                for w in ws:
+                    R.mm_batched_device(x, w, y, stream=stream)
+            stream.synchronize()
+            with torch.cuda.graph(graph, stream=stream):
+                for w in ws:
+                    R.mm_batched_device(x, w, y, stream=stream)
+            with torch.cuda.stream(stream):
+                for _ in range(3):
+                    graph.replay()
+                e0 = torch.cuda.Event(enable_timing=True)
+                e1 = torch.cuda.Event(enable_timing=True)
+                reps = 20
+                e0.record(stream)
+                for _ in range(reps):
+                    graph.replay()
+                e1.record(stream)
+            e1.synchronize()
+            us = e0.elapsed_time(e1) * 1e3 / (reps * len(ws))
+            alg = tensor_byte_size(fmt, n * k) + 4 * k + 4 * n
+            res[f"{n}x{k}"] = {"us": round(us, 2), "gbs": round(alg / (us / 1e6) / 1e9, 1)}
+            del graph, ws
+        out[fmt.name] = res
+    return out
 
 
 def moe_section(args, rank, world, dev, stream, ctx):
@@ -636,6 +689,7 @@ def main():
         pg.end_step()  # absolute epochs for the eager legs below
     prefill = prefill_section(args, rank, world, dev, stream, ctx, pg)
     moe = moe_section(args, rank, world, dev, stream, ctx)
+    formats = formats_section(args, dev, stream, ctx) if world == 1 else None
 
     # ---- e2e through the public API with host buffers -----------------------------
     # N = 1: the C-ABI call rce_qmm_mm_batched (host in, host out; it stages
@@ -727,6 +781,7 @@ def main():
                              "peak_kind": f"{peak_kind} bf16 dense (burst)"},
             },
             "moe_ffn": moe,
+            "formats_gemv": formats,
             "e2e": e2e,
             "cpu_baseline": cpu,
             "clocks": clk,

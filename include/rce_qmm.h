@@ -1,7 +1,7 @@
 /*
  * rce_qmm.h -- C ABI of the B200 GGUF quantized-matmul library
  * (librce_qmm.so), the drop-in for the reference crate rce-op-qmm's operator
- * API for the Q8_0, Q4_0, Q4_K and Q6_K weight formats.
+ * API for the Q8_0, Q4_0, Q4_K, Q5_K and Q6_K weight formats.
  *
  * Reference interfaces replaced (paths relative to openIE-dev/rce,
  * compute/crates/):
@@ -58,6 +58,7 @@ extern "C" {
 #define RCE_QMM_GGUF_Q4_0 2
 #define RCE_QMM_GGUF_Q8_0 8
 #define RCE_QMM_GGUF_Q4_K 12
+#define RCE_QMM_GGUF_Q5_K 13
 #define RCE_QMM_GGUF_Q6_K 14
 
 typedef struct rce_qmm_ctx rce_qmm_ctx;
@@ -93,7 +94,7 @@ int rce_qmm_ctx_get_prefill_min_tokens(const rce_qmm_ctx *ctx, int *n);
  * the layout QuantWeight keeps, rce-op-qmm/src/lib.rs:15-19).  The bytes are
  * copied to the device once and repacked into the device tile layout (a byte
  * permutation: same byte count, recoverable bit for bit).  n_cols must be a
- * multiple of the block size (32; 256 for Q4_K and Q6_K) and nbytes must equal
+ * multiple of the block size (32; 256 for Q4_K, Q5_K and Q6_K) and nbytes must equal
  * rce_qmm_tensor_byte_size(dtype, n_rows * n_cols). */
 int rce_qmm_weight_register(rce_qmm_ctx *ctx, const void *gguf_bytes, size_t nbytes, int gguf_dtype,
                             int64_t n_rows, int64_t n_cols, rce_qmm_weight **out);

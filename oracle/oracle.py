@@ -25,10 +25,11 @@ GGUF_F16 = 1
 GGUF_Q4_0 = 2
 GGUF_Q8_0 = 8
 GGUF_Q4_K = 12
+GGUF_Q5_K = 13
 GGUF_Q6_K = 14
 
-BLOCK = {GGUF_Q4_0: 32, GGUF_Q8_0: 32, GGUF_Q4_K: 256, GGUF_Q6_K: 256}
-BLOCK_BYTES = {GGUF_Q4_0: 18, GGUF_Q8_0: 34, GGUF_Q4_K: 144, GGUF_Q6_K: 210}
+BLOCK = {GGUF_Q4_0: 32, GGUF_Q8_0: 32, GGUF_Q4_K: 256, GGUF_Q5_K: 256, GGUF_Q6_K: 256}
+BLOCK_BYTES = {GGUF_Q4_0: 18, GGUF_Q8_0: 34, GGUF_Q4_K: 144, GGUF_Q5_K: 176, GGUF_Q6_K: 210}
 
 _HERE = os.path.dirname(os.path.abspath(__file__))
 _LIB_PATH = os.path.join(_HERE, "_build", "libqmm_oracle.so")
@@ -310,6 +311,23 @@ def unpack_q4_k(wbytes, n_rows, n_cols):
     return q, s, o
 
 
+def unpack_q5_k(wbytes, n_rows, n_cols):
+    """Q5_K bytes -> q [n][k] in 0..31, s = d*sc and o = dmin*m [n][k/32]
+    (the operands of the spec's matmul_q5_k), decoded independently: Q4_K's
+    nibbles and scales (block bytes 0..15 and 48..175), the fifth bit of
+    value 64 g + 32 h + l from bit 2g + h of qh[l] (bytes 16..47)."""
+    nsb = n_cols // 256
+    b = _u8(wbytes).reshape(n_rows, nsb, 176)
+    as_q4k = np.concatenate([b[:, :, :16], b[:, :, 48:]], axis=2).reshape(-1)
+    q4, s, o = unpack_q4_k(as_q4k, n_rows, n_cols)
+    qh = b[:, :, 16:48].astype(np.int32)
+    hi = np.zeros((n_rows, nsb, 256), dtype=np.int32)
+    for g in range(4):
+        for h in range(2):
+            hi[:, :, 64 * g + 32 * h:64 * g + 32 * h + 32] = (qh >> (2 * g + h)) & 1
+    return q4 + 16 * hi.reshape(n_rows, n_cols), s, o
+
+
 def unpack_q6_k(wbytes, n_rows, n_cols):
     """Q6_K bytes -> q [n][k] in -32..31 and s = d*sc [n][k/16] (f32, each
     product exact), the operands of the spec's matmul_q6_k
@@ -361,8 +379,8 @@ def py_mm_1d(a, wbytes, dtype, n_rows, n_cols):
                     sub = f(sub + f(f(q[j, b * 32 + t + 16]) * a[b * 32 + t + 16]))
                 sumf = f(sumf + f(d[j, b] * sub))
             out[j] = sumf
-    elif dtype == GGUF_Q4_K:
-        q, s, o = unpack_q4_k(wbytes, n_rows, n_cols)
+    elif dtype in (GGUF_Q4_K, GGUF_Q5_K):
+        q, s, o = (unpack_q4_k if dtype == GGUF_Q4_K else unpack_q5_k)(wbytes, n_rows, n_cols)
         for j in range(n_rows):
             sumf = f(0)
             for g in range(n_cols // 64):

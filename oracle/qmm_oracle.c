@@ -108,6 +108,7 @@ size_t oracle_tensor_byte_size(int dtype, size_t n) {
     case ORACLE_GGUF_Q4_0: return (n + 31) / 32 * 18;
     case ORACLE_GGUF_Q8_0: return (n + 31) / 32 * 34;
     case ORACLE_GGUF_Q4_K: return (n + 255) / 256 * 144;
+    case ORACLE_GGUF_Q5_K: return (n + 255) / 256 * 176;
     case ORACLE_GGUF_Q6_K: return (n + 255) / 256 * 210;
     default: return 0;
     }
@@ -173,6 +174,36 @@ static void dequant_q4_k(const uint8_t *data, size_t nbytes, size_t n, float *ou
     }
 }
 
+/* dequant_q5_k (dequant.rs:606-656): Q4_K's groups of 64 with a fifth bit,
+ * bit 2j (low nibbles) or 2j + 1 (high) of qh[l], worth 16. */
+static void dequant_q5_k(const uint8_t *data, size_t nbytes, size_t n, float *out) {
+    size_t nb = (n + 255) / 256;
+    memset(out, 0, nb * 256 * sizeof(float));
+    for (size_t b = 0; b < nb; b++) {
+        size_t s = b * 176;
+        if (s + 176 > nbytes) break;
+        float d = rd_f16(data + s);
+        float dmin = rd_f16(data + s + 2);
+        const uint8_t *scales = data + s + 4, *qh = data + s + 16, *qs = data + s + 48;
+        for (int j = 0; j < 4; j++) {
+            uint8_t sc1, m1, sc2, m2;
+            oracle_q4k_get_scale_min(scales, j * 2, &sc1, &m1);
+            oracle_q4k_get_scale_min(scales, j * 2 + 1, &sc2, &m2);
+            float d1 = d * (float)sc1, min1 = dmin * (float)m1;
+            float d2 = d * (float)sc2, min2 = dmin * (float)m2;
+            for (int l = 0; l < 32; l++) {
+                uint8_t byte = qs[j * 32 + l];
+                unsigned h1 = (qh[l] & (1u << (2 * j))) ? 16u : 0u;
+                unsigned h2 = (qh[l] & (1u << (2 * j + 1))) ? 16u : 0u;
+                float t1 = d1 * (float)((byte & 0x0F) + h1);
+                out[b * 256 + j * 64 + l] = t1 - min1;
+                float t2 = d2 * (float)(((byte >> 4) & 0x0F) + h2);
+                out[b * 256 + j * 64 + 32 + l] = t2 - min2;
+            }
+        }
+    }
+}
+
 /* The six-bit code of element 128 o + 32 q + l of a Q6_K block (ql, qh as
  * in the block), minus 32: ql[64 o + 32 (q & 1) + l] supplies the low four
  * bits (low nibble for q < 2, high nibble above), qh[32 o + l] bits 2q, 2q+1
@@ -210,6 +241,7 @@ static void dequant_q6_k(const uint8_t *data, size_t nbytes, size_t n, float *ou
 int oracle_dequant(const uint8_t *bytes, size_t nbytes, int dtype, size_t n, float *out) {
     switch (dtype) {
     case ORACLE_GGUF_Q6_K: dequant_q6_k(bytes, nbytes, n, out); return 0;
+    case ORACLE_GGUF_Q5_K: dequant_q5_k(bytes, nbytes, n, out); return 0;
     case ORACLE_GGUF_Q4_0: dequant_q4_0(bytes, nbytes, n, out); return 0;
     case ORACLE_GGUF_Q8_0: dequant_q8_0(bytes, nbytes, n, out); return 0;
     case ORACLE_GGUF_Q4_K: dequant_q4_k(bytes, nbytes, n, out); return 0;
@@ -307,6 +339,51 @@ static float dot_row_q4_k(const float *a, const uint8_t *row, size_t k) {
     return sumf;
 }
 
+/* One row of mm_1d_q5_k (rce-op-qmm/src/lib.rs:783-832) == dot_row_q5_k
+ * (:387-422): dot_row_q4_k's order, the code (nibble | fifth bit << 4) from
+ * bit 2g / 2g + 1 of qh[l]. */
+static float dot_row_q5_k(const float *a, const uint8_t *row, size_t k) {
+    float sumf = 0.0f;
+    for (size_t ib = 0; ib < k / 256; ib++) {
+        const uint8_t *s = row + ib * 176;
+        float d = rd_f16(s);
+        float dmin = rd_f16(s + 2);
+        const uint8_t *scales = s + 4, *qh = s + 16, *qs = s + 48;
+        for (int g = 0; g < 4; g++) {
+            const float *ab = a + ib * 256 + g * 64;
+            uint8_t sc1, m1, sc2, m2;
+            oracle_q4k_get_scale_min(scales, g * 2, &sc1, &m1);
+            oracle_q4k_get_scale_min(scales, g * 2 + 1, &sc2, &m2);
+            float d1 = d * (float)sc1, min1 = dmin * (float)m1;
+            float d2 = d * (float)sc2, min2 = dmin * (float)m2;
+            float va_lo = 0.0f, a_lo = 0.0f, va_hi = 0.0f, a_hi = 0.0f;
+            for (int l = 0; l < 32; l++) {
+                uint8_t byte = qs[g * 32 + l];
+                unsigned h1 = ((qh[l] >> (2 * g)) & 1u) << 4;
+                unsigned h2 = ((qh[l] >> (2 * g + 1)) & 1u) << 4;
+                float v_lo = (float)((byte & 0x0F) | h1);
+                float v_hi = (float)(((byte >> 4) & 0x0F) | h2);
+                float al = ab[l];
+                float ah = ab[32 + l];
+                float p;
+                p = v_lo * al; va_lo = va_lo + p;
+                a_lo = a_lo + al;
+                p = v_hi * ah; va_hi = va_hi + p;
+                a_hi = a_hi + ah;
+            }
+            float t1 = d1 * va_lo;
+            float t2 = min1 * a_lo;
+            float t = t1 - t2;
+            float t3 = d2 * va_hi;
+            t = t + t3;
+            float t4 = min2 * a_hi;
+            t = t - t4;
+            sumf = sumf + t;
+        }
+    }
+    return sumf;
+}
+
 /* One row of mm_1d_q6_k (rce-op-qmm/src/lib.rs:1667-1705) == dot_row_q6_k
  * (:426-450): per super-block, half o and l = 0..31, four terms in the
  * order q1..q4, each ((d * sc) * q) * a added to the single running sum. */
@@ -341,6 +418,7 @@ static int row_kernel(int dtype, dot_fn *fn, size_t *bb, size_t *blk) {
     case ORACLE_GGUF_Q8_0: *fn = dot_row_q8_0; *bb = 34; *blk = 32; return 0;
     case ORACLE_GGUF_Q4_K: *fn = dot_row_q4_k; *bb = 144; *blk = 256; return 0;
     case ORACLE_GGUF_Q6_K: *fn = dot_row_q6_k; *bb = 210; *blk = 256; return 0;
+    case ORACLE_GGUF_Q5_K: *fn = dot_row_q5_k; *bb = 176; *blk = 256; return 0;
     default: return -1;
     }
 }

@@ -29,6 +29,7 @@ extern "C" {
 #define ORACLE_GGUF_Q4_0 2
 #define ORACLE_GGUF_Q8_0 8
 #define ORACLE_GGUF_Q4_K 12
+#define ORACLE_GGUF_Q5_K 13
 #define ORACLE_GGUF_Q6_K 14
 
 float oracle_f16_to_f32(uint16_t h);
@@ -37,7 +38,7 @@ uint16_t oracle_f32_to_f16_bits(float x);
 void oracle_q4k_get_scale_min(const uint8_t *scales, int j, uint8_t *sc, uint8_t *m);
 size_t oracle_tensor_byte_size(int dtype, size_t numel);
 
-/* dequantize_to_f32 for Q4_0 / Q8_0 / Q4_K / Q6_K.  Returns 0, or -1 for an
+/* dequantize_to_f32 for Q4_0 / Q8_0 / Q4_K / Q5_K / Q6_K.  Returns 0, or -1 for an
  * unsupported dtype (the reference returns None). out holds ceil(n/blk)*blk. */
 int oracle_dequant(const uint8_t *bytes, size_t nbytes, int dtype, size_t n, float *out);
 

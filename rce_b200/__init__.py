@@ -1,5 +1,5 @@
 """rce_b200 -- B200-native (sm_100a) GGUF block-quantized matmul for the
-Q8_0, Q4_0, Q4_K and Q6_K formats, a drop-in for the reference crate rce-op-qmm's
+Q8_0, Q4_0, Q4_K, Q5_K and Q6_K formats, a drop-in for the reference crate rce-op-qmm's
 operator API.  Compute runs in librce_qmm.so (include/rce_qmm.h); this
 package is the host-side mirror of the reference interface."""
 from .gguf import GgufDtype, GgufFile, GgufParseError, tensor_byte_size  # noqa: F401

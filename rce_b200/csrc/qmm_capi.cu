@@ -190,7 +190,7 @@ int register_common(rce_qmm_ctx *ctx, const void *src, bool src_on_device, size_
     *out = nullptr;
     if (!rce::dtype_supported(dtype))
         return fail(RCE_QMM_ERR_UNSUPPORTED,
-                    "weight_register: GGUF dtype %d is not supported (Q4_0=2, Q8_0=8, Q4_K=12, Q6_K=14)",
+                    "weight_register: GGUF dtype %d is not supported (Q4_0=2, Q8_0=8, Q4_K=12, Q5_K=13, Q6_K=14)",
                     dtype);
     if (n_rows <= 0 || n_cols <= 0)
         return fail(RCE_QMM_ERR_INVALID, "weight_register: shape %lld x %lld", (long long)n_rows,
@@ -253,6 +253,7 @@ size_t rce_qmm_tensor_byte_size(int dt, uint64_t n) {
     case RCE_QMM_GGUF_Q4_0: return (size_t)((n + 31) / 32 * 18);
     case RCE_QMM_GGUF_Q8_0: return (size_t)((n + 31) / 32 * 34);
     case RCE_QMM_GGUF_Q4_K: return (size_t)((n + 255) / 256 * 144);
+    case RCE_QMM_GGUF_Q5_K: return (size_t)((n + 255) / 256 * 176);
     case RCE_QMM_GGUF_Q6_K: return (size_t)((n + 255) / 256 * 210);
     default: return 0;
     }

@@ -206,7 +206,7 @@ struct RowHalf {
         r = r16 & 7;
         rh = r16 >> 3;
         ch = slot + tile * CB;
-        if (DT == GGUF_Q4_K) {
+        if (kquant45(DT)) {
             const uint4 hd = *reinterpret_cast<const uint4 *>(ch + 2048 + r16 * 16);
             const float d = h2f(hd.x), dmin = h2f(hd.x >> 16);
 #pragma unroll
@@ -271,6 +271,30 @@ struct RowHalf {
                 }
                 cc[k] = 4 * hf + k;
             }
+        } else if (DT == GGUF_Q5_K) {
+            // Q4_K's nibbles plus the fifth bit of value l = 16 hf + 8 qq + b
+            // at bit 8 (l & 3) + (l >> 2) of Y0 (low nibbles) / Y1 (high)
+            const uint4 q = *reinterpret_cast<const uint4 *>(ch + ((2 * rh + hf) * 32 + lane) * 16);
+            const uint2 y = *reinterpret_cast<const uint2 *>(ch + kQ5Hi + lane * 16 + 8 * rh);
+            const uint32_t y0 = y.x >> (4 * hf), y1 = y.y >> (4 * hf);
+            const uint32_t w[4] = {q.x, q.y, q.z, q.w};
+            const unsigned long long bias = f2pack(-8388608.f, -8388608.f);
+#pragma unroll
+            for (int qq = 0; qq < 2; qq++)
+#pragma unroll
+                for (int b = 0; b < 8; b += 2) {
+                    const uint32_t x = w[2 * qq + (b >> 2)] >> (8 * (b & 3));
+                    const int p0 = 8 * (b & 3) + 2 * qq + (b >> 2);  // value l; l + 1 sits 8 bits higher
+                    const uint32_t f0 = ((y0 >> p0) & 1u) << 4, f1 = ((y0 >> (p0 + 8)) & 1u) << 4;
+                    const uint32_t g0 = ((y1 >> p0) & 1u) << 4, g1 = ((y1 >> (p0 + 8)) & 1u) << 4;
+                    h[8 * qq + (b >> 1)] = dq_pair((x & 15u) | f0, ((x >> 8) & 15u) | f1, bias, s[J][0], o[J][0]);
+                    h[8 * qq + 4 + (b >> 1)] =
+                        dq_pair(((x >> 4) & 15u) | g0, ((x >> 12) & 15u) | g1, bias, s[J][1], o[J][1]);
+                }
+            cc[0] = 2 * hf;
+            cc[1] = 4 + 2 * hf;
+            cc[2] = 2 * hf + 1;
+            cc[3] = 5 + 2 * hf;
         } else if (DT == GGUF_Q4_K) {
             const uint4 q = *reinterpret_cast<const uint4 *>(ch + ((2 * rh + hf) * 32 + lane) * 16);
             const uint32_t w[4] = {q.x, q.y, q.z, q.w};
@@ -744,6 +768,7 @@ cudaError_t launch_any(int dt, const CUtensorMap &map, const GemmArgs &a, const 
     case GGUF_Q4_0: return launch_dt<GGUF_Q4_0>(map, a, q, grid, smem, s);
     case GGUF_Q8_0: return launch_dt<GGUF_Q8_0>(map, a, q, grid, smem, s);
     case GGUF_Q6_K: return launch_dt<GGUF_Q6_K>(map, a, q, grid, smem, s);
+    case GGUF_Q5_K: return launch_dt<GGUF_Q5_K>(map, a, q, grid, smem, s);
     default: return cudaErrorInvalidValue;
     }
 }

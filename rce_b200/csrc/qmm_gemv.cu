@@ -236,7 +236,8 @@ struct Fmt {
 template <int DT>
 struct ChunkRegs {
     uint4 q[Fmt<DT>::NQ];
-    uint4 h0, h1;  // Q4_K: headers of rows r and r+8; Q4_0/Q8_0: h0.xy = the lane's 4 scales
+    uint4 h0, h1;  // Q4_K/Q5_K: headers of rows r and r+8; Q4_0/Q8_0: h0.xy = the lane's 4 scales
+    uint4 y;       // Q5_K: fifth bits, words Y0, Y1 of row r, Y0, Y1 of row r + 8
 };
 
 // One chunk's lane data from its shared-memory ring slot (conflict-free:
@@ -250,7 +251,8 @@ template <int DT>
 __device__ __forceinline__ void load_chunk(ChunkRegs<DT> &c, const uint8_t *slot, int lane, int hw) {
 #pragma unroll
     for (int i = 0; i < Fmt<DT>::NQ; i++) c.q[i] = *reinterpret_cast<const uint4 *>(slot + (i * 32 + lane) * 16);
-    if (DT == GGUF_Q4_K) {
+    if (DT == GGUF_Q5_K) c.y = *reinterpret_cast<const uint4 *>(slot + kQ5Hi + lane * 16);
+    if (kquant45(DT)) {
         const uint8_t *h0 = slot + 2048 + (lane >> 2) * 16, *h1 = h0 + 8 * 16;
         c.h0 = make_uint4(*reinterpret_cast<const uint32_t *>(h0), *reinterpret_cast<const uint32_t *>(h0 + hw),
                           *reinterpret_cast<const uint32_t *>(h0 + hw + 4), 0u);
@@ -269,7 +271,21 @@ __device__ __forceinline__ void load_chunk(ChunkRegs<DT> &c, const uint8_t *slot
 template <int DT>
 __device__ __forceinline__ void make_a(const ChunkRegs<DT> &c, int s, uint32_t (&a)[4]) {
     const int h = s >> 2, ss = s & 3;
-    if (DT == GGUF_Q4_K) {
+    if (DT == GGUF_Q5_K) {
+        // the low (h = 0) or high (h = 1) nibbles as bytes, plus the fifth
+        // bit at bit 4: bit 8b + j of Y_h (j = 2 ss for a[0]/a[1], 2 ss + 1
+        // for a[2]/a[3]) moved to bit 8b + 4
+        const uint32_t r0 = comp(c.q[ss >> 1], (2 * ss) & 3), r1 = comp(c.q[ss >> 1], (2 * ss + 1) & 3);
+        const uint32_t e0 = comp(c.q[2 + (ss >> 1)], (2 * ss) & 3), e1 = comp(c.q[2 + (ss >> 1)], (2 * ss + 1) & 3);
+        const uint32_t yr = h ? c.y.y : c.y.x, ye = h ? c.y.w : c.y.z;
+        const int j0 = 2 * ss, j1 = 2 * ss + 1;
+        auto fifth = [](uint32_t y, int j) { return (j <= 4 ? y << (4 - j) : y >> (j - 4)) & 0x10101010u; };
+        const int sh = 4 * h;
+        a[0] = ((r0 >> sh) & 0x0F0F0F0Fu) | fifth(yr, j0);
+        a[2] = ((r1 >> sh) & 0x0F0F0F0Fu) | fifth(yr, j1);
+        a[1] = ((e0 >> sh) & 0x0F0F0F0Fu) | fifth(ye, j0);
+        a[3] = ((e1 >> sh) & 0x0F0F0F0Fu) | fifth(ye, j1);
+    } else if (DT == GGUF_Q4_K) {
         // group g's 32 qs bytes per row: words 2ss, 2ss+1; low nibbles are
         // sub-block 2g, high nibbles sub-block 2g+1
         const uint32_t r0 = comp(c.q[ss >> 1], (2 * ss) & 3), r1 = comp(c.q[ss >> 1], (2 * ss + 1) & 3);
@@ -380,9 +396,9 @@ __device__ __forceinline__ void chunk_epilogue(const ChunkRegs<DT> &c, const Chu
                                                const int *__restrict__ sint, int s_stride, const float (&isc)[NT],
                                                uint32_t sh, int lane) {
     const int g = lane & 3;
-    int sc[2][2], mn[2][2];  // Q4_K: [row r / r+8][sub-block h]
+    int sc[2][2], mn[2][2];  // Q4_K / Q5_K: [row r / r+8][sub-block h]
     float ds[2][2];          // Q4_0 / Q8_0: [sub-block h][row r / r+8]
-    if (DT == GGUF_Q4_K) {
+    if (kquant45(DT)) {
         q4k_fields(c.h0, sh, sc[0], mn[0]);
         q4k_fields(c.h1, sh, sc[1], mn[1]);
     } else {
@@ -392,10 +408,17 @@ __device__ __forceinline__ void chunk_epilogue(const ChunkRegs<DT> &c, const Chu
         ds[1][1] = h2f(c.h0.y >> 16);
     }
     int iq[NT][2][2], im[NT][2][2];  // Q4_K: [token][row][low / high digit-pair half]
+    // Q5_K: per token and row, the sum over both sub-blocks of sc * (hi * 2^16
+    // + lo) in 64 bits (a sub-block's sc * sum q X stays below 2^31, two of
+    // them need not: codes up to 31 instead of 15)
+    long long iq5[NT][2];
 #pragma unroll
     for (int t = 0; t < NT; t++)
 #pragma unroll
-        for (int w = 0; w < 2; w++) iq[t][w][0] = iq[t][w][1] = im[t][w][0] = im[t][w][1] = 0;
+        for (int w = 0; w < 2; w++) {
+            iq[t][w][0] = iq[t][w][1] = im[t][w][0] = im[t][w][1] = 0;
+            iq5[t][w] = 0;
+        }
 #pragma unroll
     for (int h = 0; h < 2; h++) {
 #pragma unroll
@@ -404,17 +427,22 @@ __device__ __forceinline__ void chunk_epilogue(const ChunkRegs<DT> &c, const Chu
             int lo0 = r.da[h][t][1] * 256 + r.da[h][t][0], hi0 = r.db[h][t][1] * 256 + r.db[h][t][0];  // row r
             int lo1 = r.da[h][t][3] * 256 + r.da[h][t][2], hi1 = r.db[h][t][3] * 256 + r.db[h][t][2];  // row r + 8
             const int2 sx = *reinterpret_cast<const int2 *>(sint + (t * s_stride + 2 * g + h) * 2);
-            if (DT == GGUF_Q4_K) {
-                if (h == 1) {  // 16 * code (make_a): exact multiples of 16
+            if (kquant45(DT)) {
+                if (DT == GGUF_Q4_K && h == 1) {  // 16 * code (make_a): exact multiples of 16
                     lo0 >>= 4;
                     hi0 >>= 4;
                     lo1 >>= 4;
                     hi1 >>= 4;
                 }
-                iq[t][0][0] += sc[0][h] * lo0;
-                iq[t][0][1] += sc[0][h] * hi0;
-                iq[t][1][0] += sc[1][h] * lo1;
-                iq[t][1][1] += sc[1][h] * hi1;
+                if (DT == GGUF_Q5_K) {
+                    iq5[t][0] += (long long)(sc[0][h] * lo0) + (long long)(sc[0][h] * hi0) * 65536;
+                    iq5[t][1] += (long long)(sc[1][h] * lo1) + (long long)(sc[1][h] * hi1) * 65536;
+                } else {
+                    iq[t][0][0] += sc[0][h] * lo0;
+                    iq[t][0][1] += sc[0][h] * hi0;
+                    iq[t][1][0] += sc[1][h] * lo1;
+                    iq[t][1][1] += sc[1][h] * hi1;
+                }
                 im[t][0][0] += mn[0][h] * sx.x;
                 im[t][0][1] += mn[0][h] * sx.y;
                 im[t][1][0] += mn[1][h] * sx.x;
@@ -434,12 +462,12 @@ __device__ __forceinline__ void chunk_epilogue(const ChunkRegs<DT> &c, const Chu
             }
         }
     }
-    if (DT == GGUF_Q4_K) {
+    if (kquant45(DT)) {
         const float d0 = h2f(c.h0.x), m0 = h2f(c.h0.x >> 16), d1 = h2f(c.h1.x), m1 = h2f(c.h1.x >> 16);
 #pragma unroll
         for (int t = 0; t < NT; t++) {
-            const double q0 = (double)((long long)iq[t][0][1] * 65536 + iq[t][0][0]);
-            const double q1 = (double)((long long)iq[t][1][1] * 65536 + iq[t][1][0]);
+            const double q0 = DT == GGUF_Q5_K ? (double)iq5[t][0] : (double)((long long)iq[t][0][1] * 65536 + iq[t][0][0]);
+            const double q1 = DT == GGUF_Q5_K ? (double)iq5[t][1] : (double)((long long)iq[t][1][1] * 65536 + iq[t][1][0]);
             const double s0 = (double)((long long)im[t][0][1] * 65536 + im[t][0][0]);
             const double s1 = (double)((long long)im[t][1][1] * 65536 + im[t][1][0]);
             acc[t][0] = fma((double)(d0 * isc[t]), q0, fma((double)(-m0 * isc[t]), s0, acc[t][0]));
@@ -1201,6 +1229,7 @@ cudaError_t launch_gemv_group(int dt, const GemvGroup &grp, const float *x, size
         cudaError_t e;
         switch (dt) {
         case GGUF_Q4_K: e = launch_nt<GGUF_Q4_K>(plan.nt, a, plan.smem, s); break;
+        case GGUF_Q5_K: e = launch_nt<GGUF_Q5_K>(plan.nt, a, plan.smem, s); break;
         case GGUF_Q4_0: e = launch_nt<GGUF_Q4_0>(plan.nt, a, plan.smem, s); break;
         case GGUF_Q8_0: e = launch_nt<GGUF_Q8_0>(plan.nt, a, plan.smem, s); break;
         default: return cudaErrorInvalidValue;

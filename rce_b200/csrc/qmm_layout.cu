@@ -47,10 +47,10 @@ __global__ void repack_kernel(const uint8_t *__restrict__ src, uint8_t *__restri
         int64_t row;
         int64_t blk;
         int off;
-        if (DT == GGUF_Q4_K) {
+        if (kquant45(DT)) {
             row = tile * 16 + r + 8 * (i >> 1);
             blk = c;
-            off = 16 + 32 * gq + 16 * (i & 1);
+            off = (DT == GGUF_Q5_K ? 48 : 16) + 32 * gq + 16 * (i & 1);
         } else if (DT == GGUF_Q4_0) {
             row = tile * 16 + r + 8 * (i >> 1);
             blk = (int64_t)c * 8 + 2 * gq + (i & 1);
@@ -65,12 +65,30 @@ __global__ void repack_kernel(const uint8_t *__restrict__ src, uint8_t *__restri
 #pragma unroll
             for (int b = 0; b < 16; b++) buf[b] = s[b];
         }
+    } else if (DT == GGUF_Q5_K && p >= QP + 16) {
+        // fifth bits of lane (r, gq): Y0, Y1 of row r, then of row r + 8
+        const int lane = p - QP - 16, r = lane >> 2, gq = lane & 3;
+#pragma unroll
+        for (int rr = 0; rr < 2; rr++) {
+            const int64_t row = tile * 16 + r + 8 * rr;
+            if (row >= g.n_rows || c >= blocks_per_row) continue;
+            const uint8_t *qh = src + row * g.gguf_row_bytes + (int64_t)c * 176 + 16;
+#pragma unroll
+            for (int h = 0; h < 2; h++) {
+                uint32_t y = 0;
+                for (int l = 0; l < 32; l++) y |= (uint32_t)((qh[l] >> (2 * gq + h)) & 1) << (8 * (l & 3) + (l >> 2));
+                buf[8 * rr + 4 * h] = (uint8_t)y;
+                buf[8 * rr + 4 * h + 1] = (uint8_t)(y >> 8);
+                buf[8 * rr + 4 * h + 2] = (uint8_t)(y >> 16);
+                buf[8 * rr + 4 * h + 3] = (uint8_t)(y >> 24);
+            }
+        }
     } else {
         const int q = p - QP;  // 0..15
-        if (DT == GGUF_Q4_K) {
+        if (kquant45(DT)) {
             const int64_t row = tile * 16 + q;
             if (row < g.n_rows && c < blocks_per_row) {
-                const uint8_t *h = src + row * g.gguf_row_bytes + (int64_t)c * 144;
+                const uint8_t *h = src + row * g.gguf_row_bytes + (int64_t)c * gguf_block_bytes(DT);
                 buf[0] = h[0];
                 buf[1] = h[1];
                 buf[2] = h[2];
@@ -124,8 +142,8 @@ __device__ __forceinline__ BlockLoc locate(const uint8_t *tiles, const Geometry 
     BlockLoc L;
     const int64_t tile = row / 16;
     L.r16 = (int)(row % 16);
-    const int64_t c = DT == GGUF_Q4_K ? blk : blk / 8;
-    const int bl = DT == GGUF_Q4_K ? 0 : (int)(blk % 8);
+    const int64_t c = kquant45(DT) ? blk : blk / 8;
+    const int bl = kquant45(DT) ? 0 : (int)(blk % 8);
     L.gq = bl / 2;
     L.hb = bl % 2;
     L.lane = 4 * (L.r16 % 8) + L.gq;
@@ -142,8 +160,9 @@ __global__ void unpack_kernel(const uint8_t *__restrict__ tiles, uint8_t *__rest
     if (idx >= (row1 - row0) * bpr) return;
     const int64_t row = row0 + idx / bpr, blk = idx % bpr;
     uint8_t *out = dst + (row - row0) * g.gguf_row_bytes + blk * gguf_block_bytes(DT);
-    if (DT == GGUF_Q4_K) {
+    if (kquant45(DT)) {
         BlockLoc L = locate<DT>(tiles, g, row, blk);
+        const int qs0 = DT == GGUF_Q5_K ? 48 : 16;
         const uint8_t *h = L.chunk + 2048 + L.r16 * 16;
         out[0] = h[0];
         out[1] = h[1];
@@ -169,8 +188,20 @@ __global__ void unpack_kernel(const uint8_t *__restrict__ tiles, uint8_t *__rest
             for (int hh = 0; hh < 2; hh++) {
                 const int i = 2 * rh + hh, lane = 4 * (L.r16 % 8) + gq;
                 const uint8_t *q = L.chunk + (i * 32 + lane) * 16;
-                for (int b = 0; b < 16; b++) out[16 + 32 * gq + 16 * hh + b] = q[b];
+                for (int b = 0; b < 16; b++) out[qs0 + 32 * gq + 16 * hh + b] = q[b];
             }
+        if (DT == GGUF_Q5_K) {  // qh[l] bit 2 gq + h from word Y_h of lane (r, gq)
+            for (int l = 0; l < 32; l++) out[16 + l] = 0;
+            for (int gq = 0; gq < 4; gq++) {
+                const uint8_t *yw = L.chunk + kQ5Hi + (4 * (L.r16 % 8) + gq) * 16 + 8 * rh;
+                for (int h = 0; h < 2; h++) {
+                    const uint32_t y = yw[4 * h] | (yw[4 * h + 1] << 8) | (yw[4 * h + 2] << 16) |
+                                       ((uint32_t)yw[4 * h + 3] << 24);
+                    for (int l = 0; l < 32; l++)
+                        out[16 + l] |= (uint8_t)(((y >> (8 * (l & 3) + (l >> 2))) & 1) << (2 * gq + h));
+                }
+            }
+        }
     } else {
         BlockLoc L = locate<DT>(tiles, g, row, blk);
         const int rh = L.r16 >= 8 ? 1 : 0;
@@ -204,7 +235,7 @@ __global__ void dequant_kernel(const uint8_t *__restrict__ tiles, float *__restr
     float *o = out + (size_t)(row - row0) * ldo + blk * gguf_block(DT);
     BlockLoc L = locate<DT>(tiles, g, row, blk);
     const int rh = L.r16 >= 8 ? 1 : 0;
-    if (DT == GGUF_Q4_K) {
+    if (kquant45(DT)) {
         const uint8_t *h = L.chunk + 2048 + L.r16 * 16;
         const float d = f16_bits_to_f32((uint16_t)(h[0] | (h[1] << 8)));
         const float dmin = f16_bits_to_f32((uint16_t)(h[2] | (h[3] << 8)));
@@ -214,13 +245,21 @@ __global__ void dequant_kernel(const uint8_t *__restrict__ tiles, float *__restr
             const float min1 = __fmul_rn(dmin, (float)((v >> 6) & 63));
             const float d2 = __fmul_rn(d, (float)((v >> 12) & 63));
             const float min2 = __fmul_rn(dmin, (float)((v >> 18) & 63));
+            const int lane = 4 * (L.r16 % 8) + gq;
+            uint32_t y0 = 0, y1 = 0;  // Q5_K fifth bits of sub-blocks 2 gq, 2 gq + 1
+            if (DT == GGUF_Q5_K) {
+                const uint8_t *yw = L.chunk + kQ5Hi + lane * 16 + 8 * rh;
+                y0 = yw[0] | (yw[1] << 8) | (yw[2] << 16) | ((uint32_t)yw[3] << 24);
+                y1 = yw[4] | (yw[5] << 8) | (yw[6] << 16) | ((uint32_t)yw[7] << 24);
+            }
             for (int hh = 0; hh < 2; hh++) {
-                const int lane = 4 * (L.r16 % 8) + gq;
                 const uint8_t *q = L.chunk + ((2 * rh + hh) * 32 + lane) * 16;
                 for (int b = 0; b < 16; b++) {
-                    const int l = 16 * hh + b;
-                    o[64 * gq + l] = __fsub_rn(__fmul_rn(d1, (float)(q[b] & 0x0F)), min1);
-                    o[64 * gq + 32 + l] = __fsub_rn(__fmul_rn(d2, (float)(q[b] >> 4)), min2);
+                    const int l = 16 * hh + b, bit = 8 * (l & 3) + (l >> 2);
+                    const uint32_t c0 = (q[b] & 0x0F) | (((y0 >> bit) & 1) << 4);
+                    const uint32_t c1 = (q[b] >> 4) | (((y1 >> bit) & 1) << 4);
+                    o[64 * gq + l] = __fsub_rn(__fmul_rn(d1, (float)c0), min1);
+                    o[64 * gq + 32 + l] = __fsub_rn(__fmul_rn(d2, (float)c1), min2);
                 }
             }
         }
@@ -254,6 +293,7 @@ cudaError_t launch_repack(int dt, const uint8_t *gguf, uint8_t *tiles, const Geo
     switch (dt) {
     case GGUF_Q6_K: return launch_repack_q6k(gguf, tiles, g, s);
     case GGUF_Q4_K: repack_kernel<GGUF_Q4_K><<<blocks, threads, 0, s>>>(gguf, tiles, g); break;
+    case GGUF_Q5_K: repack_kernel<GGUF_Q5_K><<<blocks, threads, 0, s>>>(gguf, tiles, g); break;
     case GGUF_Q4_0: repack_kernel<GGUF_Q4_0><<<blocks, threads, 0, s>>>(gguf, tiles, g); break;
     case GGUF_Q8_0: repack_kernel<GGUF_Q8_0><<<blocks, threads, 0, s>>>(gguf, tiles, g); break;
     default: return cudaErrorInvalidValue;
@@ -270,6 +310,7 @@ cudaError_t launch_unpack(int dt, const uint8_t *tiles, uint8_t *gguf, const Geo
     switch (dt) {
     case GGUF_Q6_K: return launch_unpack_q6k(tiles, gguf, g, row0, row1, s);
     case GGUF_Q4_K: unpack_kernel<GGUF_Q4_K><<<blocks, threads, 0, s>>>(tiles, gguf, g, row0, row1); break;
+    case GGUF_Q5_K: unpack_kernel<GGUF_Q5_K><<<blocks, threads, 0, s>>>(tiles, gguf, g, row0, row1); break;
     case GGUF_Q4_0: unpack_kernel<GGUF_Q4_0><<<blocks, threads, 0, s>>>(tiles, gguf, g, row0, row1); break;
     case GGUF_Q8_0: unpack_kernel<GGUF_Q8_0><<<blocks, threads, 0, s>>>(tiles, gguf, g, row0, row1); break;
     default: return cudaErrorInvalidValue;
@@ -286,6 +327,7 @@ cudaError_t launch_dequant(int dt, const uint8_t *tiles, float *out, size_t ldo,
     switch (dt) {
     case GGUF_Q6_K: return launch_dequant_q6k(tiles, out, ldo, g, row0, row1, s);
     case GGUF_Q4_K: dequant_kernel<GGUF_Q4_K><<<blocks, threads, 0, s>>>(tiles, out, ldo, g, row0, row1); break;
+    case GGUF_Q5_K: dequant_kernel<GGUF_Q5_K><<<blocks, threads, 0, s>>>(tiles, out, ldo, g, row0, row1); break;
     case GGUF_Q4_0: dequant_kernel<GGUF_Q4_0><<<blocks, threads, 0, s>>>(tiles, out, ldo, g, row0, row1); break;
     case GGUF_Q8_0: dequant_kernel<GGUF_Q8_0><<<blocks, threads, 0, s>>>(tiles, out, ldo, g, row0, row1); break;
     default: return cudaErrorInvalidValue;

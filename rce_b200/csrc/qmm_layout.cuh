@@ -31,6 +31,12 @@
 //     quants [i 0..7][lane][16 B]: row r + 8 (i >> 2), bytes
 //       [16 (i & 1), +16) of block 2 g + ((i >> 1) & 1);
 //     scales [lane][4 x f16] as Q4_0.
+//   Q5_K (176 B per 256; chunk 2816 B): Q4_K's quants and headers (the
+//     low four bits of every code), then the fifth bits [lane][16 B] at
+//     2304: for lane (r, g) the words Y0, Y1 of row r and Y0, Y1 of row
+//     r + 8, where bit 8b + j of Y_h is the fifth bit of value 64 g + 32 h +
+//     4 j + b (GGUF: bit 2g + h of qh[4 j + b]) -- so (Y_h >> j) &
+//     0x01010101 holds the bits of the four values a[] byte b carries.
 //   Q6_K (210 B per 256; chunk 3360 B; qmm_q6k.cu): the six-bit codes
 //     u = q + 32 of value v (0..255) of row r, split as in GGUF into four low
 //     and two high bits but re-ordered by value: lo plane [row][128 B], byte
@@ -48,24 +54,30 @@
 
 namespace rce {
 
-enum : int { GGUF_F32 = 0, GGUF_F16 = 1, GGUF_Q4_0 = 2, GGUF_Q8_0 = 8, GGUF_Q4_K = 12, GGUF_Q6_K = 14 };
+enum : int { GGUF_F32 = 0, GGUF_F16 = 1, GGUF_Q4_0 = 2, GGUF_Q8_0 = 8, GGUF_Q4_K = 12, GGUF_Q5_K = 13, GGUF_Q6_K = 14 };
 
 constexpr int TILE_ROWS = 16;
 constexpr int CHUNK_K = 256;
 
 __host__ __device__ constexpr int chunk_bytes(int dt) {
-    return dt == GGUF_Q8_0 ? 4352 : (dt == GGUF_Q6_K ? 3360 : 2304);
+    return dt == GGUF_Q8_0 ? 4352 : (dt == GGUF_Q6_K ? 3360 : (dt == GGUF_Q5_K ? 2816 : 2304));
 }
+// Q4_K and Q5_K share the super-block header and the nibble layout.
+__host__ __device__ constexpr bool kquant45(int dt) { return dt == GGUF_Q4_K || dt == GGUF_Q5_K; }
 __host__ __device__ constexpr int quant_bytes(int dt) {
     return dt == GGUF_Q8_0 ? 4096 : (dt == GGUF_Q6_K ? 3072 : 2048);
 }
-__host__ __device__ constexpr int gguf_block(int dt) { return dt == GGUF_Q4_K || dt == GGUF_Q6_K ? 256 : 32; }
+__host__ __device__ constexpr int gguf_block(int dt) {
+    return dt == GGUF_Q4_K || dt == GGUF_Q5_K || dt == GGUF_Q6_K ? 256 : 32;
+}
 __host__ __device__ constexpr int gguf_block_bytes(int dt) {
-    return dt == GGUF_Q4_K ? 144 : (dt == GGUF_Q8_0 ? 34 : (dt == GGUF_Q6_K ? 210 : 18));
+    return dt == GGUF_Q4_K ? 144 : (dt == GGUF_Q8_0 ? 34 : (dt == GGUF_Q6_K ? 210 : (dt == GGUF_Q5_K ? 176 : 18)));
 }
 inline bool dtype_supported(int dt) {
-    return dt == GGUF_Q4_0 || dt == GGUF_Q8_0 || dt == GGUF_Q4_K || dt == GGUF_Q6_K;
+    return dt == GGUF_Q4_0 || dt == GGUF_Q8_0 || dt == GGUF_Q4_K || dt == GGUF_Q5_K || dt == GGUF_Q6_K;
 }
+// Q5_K fifth-bit plane offset.
+constexpr int kQ5Hi = 2304;
 // Q6_K chunk planes (qmm_q6k.cu).
 constexpr int kQ6Hi = 2048, kQ6Sc = 3072, kQ6D = 3328;
 

@@ -38,7 +38,7 @@ class GgufDtype(IntEnum):
 Q4_K = GgufDtype.Q4K
 
 #: values per block and bytes per block (tensor_byte_size, dequant.rs:18-58:
-#: every format a GGUF file may hold beside the four this library computes
+#: every format a GGUF file may hold beside the five this library computes
 #: with, so that any tensor's byte range can be located)
 BLOCK = {GgufDtype.Q4_0: 32, GgufDtype.Q8_0: 32, GgufDtype.Q4K: 256, GgufDtype.F32: 1, GgufDtype.F16: 1,
          GgufDtype.BF16: 1, GgufDtype.Q4_1: 32, GgufDtype.Q5_0: 32, GgufDtype.Q5_1: 32, GgufDtype.Q8_1: 32,
@@ -47,7 +47,7 @@ BLOCK_BYTES = {GgufDtype.Q4_0: 18, GgufDtype.Q8_0: 34, GgufDtype.Q4K: 144, GgufD
                GgufDtype.BF16: 2, GgufDtype.Q4_1: 20, GgufDtype.Q5_0: 22, GgufDtype.Q5_1: 24, GgufDtype.Q8_1: 36,
                GgufDtype.Q2K: 84, GgufDtype.Q3K: 110, GgufDtype.Q5K: 176, GgufDtype.Q6K: 210}
 
-SUPPORTED = (GgufDtype.Q4_0, GgufDtype.Q8_0, GgufDtype.Q4K, GgufDtype.Q6K)
+SUPPORTED = (GgufDtype.Q4_0, GgufDtype.Q8_0, GgufDtype.Q4K, GgufDtype.Q5K, GgufDtype.Q6K)
 
 
 def tensor_byte_size(dtype, numel: int) -> int:

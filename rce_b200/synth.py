@@ -6,6 +6,7 @@ The value distributions follow the benchmark configurations of this path:
   Q4_K: fp16 d and dmin = |N(0,1)| * 0.01, the 12 packed scale bytes and the
         128 nibble bytes uniform (so every 6-bit scale/min and every nibble
         is uniform);
+  Q5_K: as Q4_K, with the 32 fifth-bit bytes uniform;
   Q6_K: fp16 d = |N(0,1)| * 0.01, the 16 int8 scales uniform in [-128, 127],
         the 192 code bytes uniform (every 6-bit code uniform in 0..63);
   activations: f32 N(0,1).
@@ -19,7 +20,8 @@ import numpy as np
 
 from .gguf import GgufDtype
 
-DEFAULT_SCALE = {GgufDtype.Q8_0: 0.01, GgufDtype.Q4_0: 0.02, GgufDtype.Q4K: 0.01, GgufDtype.Q6K: 0.01}
+DEFAULT_SCALE = {GgufDtype.Q8_0: 0.01, GgufDtype.Q4_0: 0.02, GgufDtype.Q4K: 0.01, GgufDtype.Q5K: 0.01,
+                 GgufDtype.Q6K: 0.01}
 
 
 def _f16_bytes(v: np.ndarray) -> np.ndarray:
@@ -55,6 +57,17 @@ def q4_k(n_rows: int, n_cols: int, rng: np.random.Generator, scale: float = 0.01
     return blocks.reshape(-1)
 
 
+def q5_k(n_rows: int, n_cols: int, rng: np.random.Generator, scale: float = 0.01) -> np.ndarray:
+    nsb = n_cols // 256
+    blocks = np.empty((n_rows, nsb, 176), dtype=np.uint8)
+    d = np.abs(rng.standard_normal((n_rows, nsb), dtype=np.float32)) * np.float32(scale)
+    dmin = np.abs(rng.standard_normal((n_rows, nsb), dtype=np.float32)) * np.float32(scale)
+    blocks[:, :, 0:2] = _f16_bytes(d)
+    blocks[:, :, 2:4] = _f16_bytes(dmin)
+    blocks[:, :, 4:] = rng.integers(0, 256, size=(n_rows, nsb, 172), dtype=np.uint8)
+    return blocks.reshape(-1)
+
+
 def q6_k(n_rows: int, n_cols: int, rng: np.random.Generator, scale: float = 0.01) -> np.ndarray:
     nsb = n_cols // 256
     blocks = np.empty((n_rows, nsb, 210), dtype=np.uint8)
@@ -73,6 +86,8 @@ def weights(dtype, n_rows: int, n_cols: int, rng, scale=None) -> np.ndarray:
         return q4_0(n_rows, n_cols, rng, s)
     if dt == GgufDtype.Q4K:
         return q4_k(n_rows, n_cols, rng, s)
+    if dt == GgufDtype.Q5K:
+        return q5_k(n_rows, n_cols, rng, s)
     if dt == GgufDtype.Q6K:
         return q6_k(n_rows, n_cols, rng, s)
     raise ValueError(f"no generator for {dt}")
@@ -109,8 +124,8 @@ def device_weights(dtype, n_rows: int, n_cols: int, gen, device, scale=None):
         d = (torch.randn(nb, device=device, generator=gen).abs() * s).to(torch.float16)
         raw[:, 208:210] = d.view(torch.uint8).view(nb, 2)
         return raw.view(-1)
-    if dt == GgufDtype.Q4K:
-        nb, bb = n_rows * n_cols // 256, 144
+    if dt in (GgufDtype.Q4K, GgufDtype.Q5K):
+        nb, bb = n_rows * n_cols // 256, (144 if dt == GgufDtype.Q4K else 176)
     elif dt == GgufDtype.Q8_0:
         nb, bb = n_rows * n_cols // 32, 34
     else:
@@ -121,7 +136,7 @@ def device_weights(dtype, n_rows: int, n_cols: int, gen, device, scale=None):
         raw[:, 2:] = q.view(torch.uint8)
     d = (torch.randn(nb, device=device, generator=gen).abs() * s).to(torch.float16)
     raw[:, 0:2] = d.view(torch.uint8).view(nb, 2)
-    if dt == GgufDtype.Q4K:
+    if dt in (GgufDtype.Q4K, GgufDtype.Q5K):
         dmin = (torch.randn(nb, device=device, generator=gen).abs() * s).to(torch.float16)
         raw[:, 2:4] = dmin.view(torch.uint8).view(nb, 2)
     return raw.view(-1)

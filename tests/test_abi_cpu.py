@@ -38,7 +38,7 @@ def test_library_exports_every_declared_symbol():
 def test_abi_version_and_pure_functions():
     L = _lib.lib()
     assert L.rce_qmm_abi_version() == 1
-    for dt in (O.GGUF_Q4_0, O.GGUF_Q8_0, O.GGUF_Q4_K, O.GGUF_Q6_K):
+    for dt in (O.GGUF_Q4_0, O.GGUF_Q8_0, O.GGUF_Q4_K, O.GGUF_Q5_K, O.GGUF_Q6_K):
         for n in (1, 31, 32, 33, 255, 256, 257, 4096 * 4096):
             assert L.rce_qmm_tensor_byte_size(dt, n) == O.tensor_byte_size(dt, n) == gguf.tensor_byte_size(dt, n)
     assert L.rce_qmm_tensor_byte_size(6, 32) == 0

@@ -328,3 +328,39 @@ def test_q6k_code_layout_known_answers():
     assert d[101] == 7 * (((2 << 4) | 0) - 32)  # scale 6 = 7
     assert d[231] == 15 * (((3 << 4) | 15) - 32)  # scale 14 = 15
     assert d[0] == 1 * (0 - 32)
+
+
+# ---- Q5_K (rce-op-qmm/src/lib.rs:783-832, dequant.rs:606-656) ----------------
+
+def test_q5k_restatements_bit_exact():
+    # mm_1d_serial_matches_parallel's Q5_K case (lib.rs:3629-3665: k = 512,
+    # n = 7, bytes (i * 37 + 11) & 0xFF, d and dmin patched to f16(0.05)):
+    # the C restatement against the spec-order Python one (tensor.matmul_q5_k
+    # = matmul_q4_k's order with codes 0..31), and serial == row-parallel
+    k, n = 512, 7
+    a = np.sin(np.arange(k, dtype=np.float32) * np.float32(0.017) - np.float32(0.3)).astype(np.float32)
+    wb = ((np.arange(n * (k // 256) * 176, dtype=np.int64) * 37 + 11) & 0xFF).astype(np.uint8)
+    blocks = wb.reshape(-1, 176)
+    sc = np.array([0.05], dtype=np.float16).view(np.uint8)
+    blocks[:, 0:2] = sc
+    blocks[:, 2:4] = sc
+    got = O.mm_1d(a, wb, O.GGUF_Q5_K, n, k)
+    assert np.array_equal(got.view(np.uint32), O.py_mm_1d(a, wb, O.GGUF_Q5_K, n, k).view(np.uint32))
+    assert np.array_equal(got.view(np.uint32), O.mm_1d(a, wb, O.GGUF_Q5_K, n, k, nthreads=7).view(np.uint32))
+
+
+def test_q5k_dequant_equals_spec_values():
+    from rce_b200 import synth
+
+    rng = np.random.default_rng(13)
+    n, k = 24, 1024
+    wb = synth.weights(O.GGUF_Q5_K, n, k, rng)
+    deq = O.dequant(wb, O.GGUF_Q5_K, n * k).reshape(n, k)
+    q, s, o = O.unpack_q5_k(wb, n, k)
+    spec = (np.repeat(s, 32, axis=1) * q.astype(np.float32)).astype(np.float32) - np.repeat(o, 32, axis=1)
+    assert np.array_equal(deq.view(np.uint32), spec.astype(np.float32).view(np.uint32))
+    assert q.min() >= 0 and q.max() == 31
+    x = synth.activations(1, k, rng)[0]
+    got = O.mm_1d(x, wb, O.GGUF_Q5_K, n, k)
+    want = deq.astype(np.float64) @ x.astype(np.float64)
+    assert np.abs(got - want).max() / np.abs(want).max() < 1e-5

@@ -38,7 +38,7 @@ def _noalloc(L, ctx, x, w, out, stream):
 # the GEMV's 4-token pass, one above the GEMM threshold
 @pytest.mark.parametrize("dt,n,k,m", [(O.GGUF_Q4_K, 1024, 4096, 1), (O.GGUF_Q4_K, 1024, 4096, 5),
                                       (O.GGUF_Q8_0, 700, 4096, 3), (O.GGUF_Q4_0, 512, 11008, 17),
-                                      (O.GGUF_Q6_K, 1024, 4096, 3)])
+                                      (O.GGUF_Q6_K, 1024, 4096, 3), (O.GGUF_Q5_K, 1024, 4096, 5)])
 def test_noalloc_matches_regular_entry_point(dt, n, k, m):
     import torch
 
