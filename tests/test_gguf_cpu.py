@@ -45,7 +45,7 @@ def test_tensors_and_alignment(align):
     q4k = synth.weights(G.GgufDtype.Q4K, 48, 512, rng)
     q8 = synth.weights(G.GgufDtype.Q8_0, 3, 64, rng)
     q40 = synth.weights(G.GgufDtype.Q4_0, 5, 96, rng)
-    q6k = rng.integers(0, 256, G.tensor_byte_size(G.GgufDtype.Q6K, 256 * 4), dtype=np.uint8)  # a format not computed here
+    q6k = rng.integers(0, 256, G.tensor_byte_size(G.GgufDtype.Q6K, 256 * 4), dtype=np.uint8)
     tensors = [("blk.0.ffn_up.weight", [512, 48], 12, q4k), ("tok_embd", [64, 3], 8, q8),
                ("blk.0.attn_v.weight", [96, 5], 2, q40), ("output.weight", [256, 4], 14, q6k)]
     b = G.build_gguf([("general.architecture", G.T_STRING, "llama")], tensors, alignment=align)

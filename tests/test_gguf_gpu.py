@@ -16,11 +16,13 @@ pytestmark = pytest.mark.gpu
 
 def test_from_gguf_matmuls_match_oracle(ctx, tmp_path):
     rng = np.random.default_rng(12)
+    # a Q4_K_M-style mix: Q4_K, Q6_K and Q5_K tensors beside Q8_0 / Q4_0
     shapes = {"blk.0.attn_q.weight": (O.GGUF_Q4_K, 256, 1024), "blk.0.attn_k.weight": (O.GGUF_Q8_0, 96, 1024),
-              "blk.0.ffn_down.weight": (O.GGUF_Q4_0, 160, 512)}
+              "blk.0.ffn_down.weight": (O.GGUF_Q4_0, 160, 512), "blk.0.attn_v.weight": (O.GGUF_Q6_K, 96, 1024),
+              "blk.0.ffn_up.weight": (O.GGUF_Q5_K, 160, 512)}
     data = {name: synth.weights(dt, n, k, rng) for name, (dt, n, k) in shapes.items()}
     tensors = [(name, [k, n], dt, data[name]) for name, (dt, n, k) in shapes.items()]
-    tensors.append(("output.weight", [256, 8], 14, rng.integers(0, 256, 8 * 210, dtype=np.uint8)))  # Q6_K
+    tensors.append(("output.weight", [256, 8], 11, rng.integers(0, 256, 8 * 110, dtype=np.uint8)))  # Q3_K
     p = tmp_path / "model.gguf"
     p.write_bytes(G.build_gguf([("general.architecture", G.T_STRING, "llama")], tensors))
     f = G.GgufFile.open(p)
