@@ -829,8 +829,10 @@ cudaError_t launch_gemm(int dt, const uint8_t *tiles, const Geometry &g, const f
                 sms_cache[dev].store(sms);
             }
         }
+        // (bn stays a multiple of 16: the MMA's N step at M = 128, and whole
+        // 1024-byte swizzle atoms per activation stage)
         const long rbs = (g.n_tiles + 7) / 8;
-        while (bn > 64 && rbs * ((t_rows + bn - 1) / bn) * 10 < (long)sms * 6) bn /= 2;
+        while (bn > 64 && rbs * ((t_rows + bn - 1) / bn) * 10 < (long)sms * 6) bn = (bn / 2 + 15) / 16 * 16;
     }
     CUtensorMap map;
     const int box_rows = bn < 256 ? bn : 256;

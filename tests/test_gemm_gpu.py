@@ -70,6 +70,24 @@ def test_gemm_against_oracle(ctx, dt, n, k, m):
     check(got, want, f"dtype {dt} {n}x{k} m={m}")
 
 
+@pytest.mark.parametrize("dt,n,k,m", [(Q4_K, 1024, 4096, 130), (Q4_K, 1024, 4096, 70), (Q4_0, 1024, 4096, 200),
+                                      (Q8_0, 512, 4096, 150)])
+def test_gemm_narrowed_token_tile_writes_every_output(ctx, dt, n, k, m):
+    # few row blocks: the token tile is narrowed to spread CTAs over the SMs,
+    # and must stay a whole MMA width (a multiple of 16); every output is
+    # written (the buffer starts as NaN)
+    import torch
+
+    w, _, _, _, x = refcases.seeded_case(dt, n, k, m, 2000 + m)
+    qw = R.QuantWeight.from_owned_bytes(w, dt, n, k, ctx=ctx)
+    out = torch.full((m, n), float("nan"), device="cuda:0")
+    R.mm_batched_device(torch.from_numpy(x).cuda(), qw, out=out)
+    torch.cuda.synchronize()
+    assert ctx.device_error() == 0
+    want = O.mm_batched(x, m, w, dt, n, k, nthreads=8)
+    check(out.cpu().numpy(), want, f"narrowed tile dtype {dt} {n}x{k} m={m}")
+
+
 def test_small_m_repeatable_between_large_calls(ctx):
     # a small batch gives the same bits on every call, also when a large
     # batch on the same stream reuses the per-stream workspace in between
