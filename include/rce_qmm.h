@@ -150,13 +150,23 @@ int rce_qmm_mm_batched_device_multi(rce_qmm_ctx *ctx, const float *d_a, size_t l
                                     const size_t *ldos, void *stream);
 
 /* As rce_qmm_mm_batched_device, for callers that cannot allocate device
- * memory (a custom allocator owning the device, a serving loop that forbids
- * cudaMalloc after start-up).  No counterpart in the reference: its CPU path
- * never allocates device memory.  Every batch runs through the decode GEMV
- * (passes of up to 4 tokens), which needs no device workspace: this call
- * performs no cudaMalloc/cudaFree and may be captured in a CUDA graph.  A
- * weight too large for the GEMV's shared-memory plan is rejected with
- * RCE_QMM_ERR_UNSUPPORTED. */
+ * memory: an engine whose own allocator has reserved the whole device, or a
+ * serving loop that forbids cudaMalloc after start-up.  No counterpart in the
+ * reference: its CPU path never allocates device memory.  The regular entry
+ * point allocates the tensor-core GEMM's workspace (fp16 activations and
+ * per-token scales) on first use; this one keeps it in one fixed 16 MiB
+ * device array per GPU, held from library load to process exit, and calls no
+ * cudaMalloc, cudaFree or allocating library routine.  Outputs equal
+ * rce_qmm_mm_batched_device's bit for bit under the same context settings.
+ * Limits: a GEMM batch (prefill_min_tokens tokens or more) needing more than
+ * 16 MiB of workspace -- t_rows * n_cols * 2 bytes rounded up to 256, plus
+ * 4 bytes per token; 2047 tokens at n_cols 4096 -- is rejected with
+ * RCE_QMM_ERR_INVALID.  Every call on a GPU shares the array, whatever its
+ * context or stream, so calls that overlap on the GPU race: order them.  The
+ * array keeps the last call's contents; nothing in it needs to start at zero.
+ * The first call on each GPU looks up the array's device address, so make it
+ * before any stream capture.  A weight too large for the decode GEMV's
+ * shared-memory plan is rejected with RCE_QMM_ERR_UNSUPPORTED. */
 int rce_qmm_mm_batched_device_noalloc(rce_qmm_ctx *ctx, const float *d_a, size_t lda, size_t t_rows,
                                       const rce_qmm_weight *w, float *d_out, size_t ldo, void *stream);
 

@@ -1,25 +1,56 @@
-// qmm_noalloc.cu -- rce_qmm_mm_batched_device_noalloc, the decode matmul for
-// callers that cannot allocate device memory: a custom allocator that owns
-// all of the device's memory, a serving loop that forbids cudaMalloc after
-// start-up, or a host that only hands us pointers it already owns.
+// qmm_noalloc.cu -- rce_qmm_mm_batched_device_noalloc, rce_qmm_mm_batched_device
+// for callers that cannot allocate device memory: an engine whose own
+// allocator has already reserved the whole device, a serving loop that
+// forbids cudaMalloc after start-up (an allocation there can stall every
+// stream or fail under memory pressure), or a host that only hands us
+// pointers it already owns.
 //
-// Every batch goes through the decode GEMV, in passes of at most
-// kGemvMaxTokens tokens.  The GEMV keeps its partial sums in the shared
-// memory of its CTA clusters and needs no device workspace, so this entry
-// point calls no cudaMalloc, cudaFree or allocating library routine (the
-// regular entry point sends batches of prefill_min_tokens or more through the
-// tensor-core GEMM, whose activation workspace it allocates per stream on
-// first use).
+// The regular entry point runs batches of prefill_min_tokens or more through
+// the tensor-core GEMM, whose workspace (the activations rounded to fp16 and
+// one inverse scale per token) it allocates per stream on first use.  Here
+// that workspace is a file-scope __device__ array of kNoallocScratchBytes
+// (16 MiB) instead, which every GPU that loads the library holds until the
+// process exits.  Smaller batches run the decode GEMV exactly as the regular
+// entry point does; it keeps its partial sums in shared memory and needs no
+// workspace.  Outputs are bit-identical to rce_qmm_mm_batched_device's for
+// the same context settings.
+//
+// Rules that follow from the one shared array:
+//  - a batch whose workspace exceeds kNoallocScratchBytes (t_rows * n_cols * 2
+//    bytes, rounded up to 256, plus 4 bytes per token) is rejected with
+//    RCE_QMM_ERR_INVALID;
+//  - every call on a device uses the same array, whatever its context or
+//    stream, so calls whose GEMM launches overlap on the GPU race and return
+//    garbage: order them on one stream or with events;
+//  - the array keeps the previous call's contents; the GEMM's prep kernel
+//    writes every workspace byte it later reads (rows beyond t_rows come from
+//    the tensor map's zero fill), so nothing has to be cleared;
+//  - the first call on a device looks the array's device address up
+//    (cudaGetSymbolAddress, which may load the module), so make that first
+//    call before any stream capture.
 #include <cuda_runtime.h>
 
 #include <cstdarg>
+#include <cstdint>
 #include <cstdio>
+#include <mutex>
 
 #include "../../include/rce_qmm.h"
 #include "qmm_handles.h"
 #include "qmm_internal.h"
 
+static constexpr size_t kNoallocScratchBytes = size_t(16) << 20;
+
+// The GEMM workspace of this entry point.  In host code this name is a
+// host-side stand-in, not a device address: kernels get the address from
+// scratch_address().
+static __device__ __align__(256) uint8_t g_noalloc_scratch[kNoallocScratchBytes];
+
 namespace {
+
+constexpr int kMaxDevices = 64;
+std::mutex g_scratch_mu;
+void *g_scratch_dev[kMaxDevices];  // device address of g_noalloc_scratch per device, once looked up
 
 int err(int code, const char *fmt, ...) {
     char buf[512];
@@ -44,6 +75,30 @@ struct CurrentDevice {
     }
 };
 
+// Device address of g_noalloc_scratch on `dev` (which must be current):
+// looked up on the first call per device, cached after.
+cudaError_t scratch_address(int dev, void **out) {
+    if (dev < 0 || dev >= kMaxDevices) return cudaErrorInvalidDevice;
+    std::lock_guard<std::mutex> lk(g_scratch_mu);
+    if (!g_scratch_dev[dev]) {
+        void *p = nullptr;
+        cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+        if (e != cudaSuccess) return e;
+        if (!p) return cudaErrorInvalidSymbol;
+        g_scratch_dev[dev] = p;
+    }
+    *out = g_scratch_dev[dev];
+    return cudaSuccess;
+}
+
+// Most tokens whose GEMM workspace fits the array at this weight's n_cols.
+size_t max_gemm_tokens(const rce::Geometry &g) {
+    size_t t = kNoallocScratchBytes / ((size_t)g.n_cols * 2 + 4);
+    while (t > 0 && rce::gemm_workspace_bytes(g, (int)t) > kNoallocScratchBytes) t--;
+    while (rce::gemm_workspace_bytes(g, (int)(t + 1)) <= kNoallocScratchBytes) t++;
+    return t;
+}
+
 }  // namespace
 
 extern "C" int rce_qmm_mm_batched_device_noalloc(rce_qmm_ctx *ctx, const float *d_a, size_t lda, size_t t_rows,
@@ -60,7 +115,25 @@ extern "C" int rce_qmm_mm_batched_device_noalloc(rce_qmm_ctx *ctx, const float *
     if (cd.status != cudaSuccess)
         return err(RCE_QMM_ERR_CUDA, "mm_batched_device_noalloc: set device: %s", cudaGetErrorString(cd.status));
     cudaStream_t s = static_cast<cudaStream_t>(stream);
-    if (w->dtype == rce::GGUF_Q6_K) {  // Q6_K's decode GEMV: no workspace either
+
+    // the regular entry point's routing (run_matmul), GEMM workspace aside
+    if (ctx->prefill_min_tokens > 0 && t_rows >= (size_t)ctx->prefill_min_tokens && t_rows <= (size_t)INT32_MAX) {
+        const size_t need = rce::gemm_workspace_bytes(g, (int)t_rows);
+        if (need > kNoallocScratchBytes)
+            return err(RCE_QMM_ERR_INVALID,
+                       "mm_batched_device_noalloc: %zu tokens x k %lld need %zu bytes of GEMM workspace, above this "
+                       "entry point's fixed %zu (at most %zu tokens at this k)",
+                       t_rows, (long long)g.n_cols, need, kNoallocScratchBytes, max_gemm_tokens(g));
+        void *ws = nullptr;
+        cudaError_t e = scratch_address(ctx->device, &ws);
+        if (e != cudaSuccess)
+            return err(RCE_QMM_ERR_CUDA, "mm_batched_device_noalloc: scratch address: %s", cudaGetErrorString(e));
+        e = rce::launch_gemm(w->dtype, w->dev, g, d_a, lda, d_out, ldo, (int)t_rows, ws, ctx->err_dev, s);
+        if (e != cudaSuccess)
+            return err(RCE_QMM_ERR_CUDA, "mm_batched_device_noalloc: launch: %s", cudaGetErrorString(e));
+        return RCE_QMM_OK;
+    }
+    if (w->dtype == rce::GGUF_Q6_K) {  // Q6_K's decode GEMV, passes of kQ6MaxTokens tokens
         for (size_t t0 = 0; t0 < t_rows; t0 += (size_t)rce::kQ6MaxTokens) {
             const size_t left = t_rows - t0;
             const int m = (int)(left < (size_t)rce::kQ6MaxTokens ? left : (size_t)rce::kQ6MaxTokens);
