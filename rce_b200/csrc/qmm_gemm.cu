@@ -482,7 +482,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     constexpr int CB = chunk_bytes(DT);
     constexpr bool kGrouped = std::is_same<Grp, GemmGroup>::value;
     extern __shared__ uint8_t smem_raw[];
-    uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    // 1024-byte aligned by pointer arithmetic on the shared array itself (an
+    // integer round trip would turn every access into a generic one)
+    uint8_t *smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
     const int bn = p.bn;
     const GemmSmem L = gemm_smem(DT, bn);
     const int NA = L.a_stages, NB = L.b_stages, NP = L.pslots;
