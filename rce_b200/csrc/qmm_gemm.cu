@@ -187,6 +187,24 @@ __device__ __forceinline__ uint32_t dq_pair(uint32_t c0, uint32_t c1, unsigned l
     return f2_to_h2(f2fma(f2add(f, bias), sc, off));
 }
 
+// Byte b (0..3) of v under the 2^23 exponent byte: 0x4B0000vv, i.e. the f32
+// 2^23 + v for the byte's value v (one byte permute, no shift or mask).
+template <int B>
+__device__ __forceinline__ uint32_t byte_f32(uint32_t v) {
+    uint32_t r;
+    asm("prmt.b32 %0, %1, %2, %3;" : "=r"(r) : "r"(v), "r"(0x4B000000u), "r"(0x7540u | B));
+    return r;
+}
+// (2^23 + c0, 2^23 + c1) -> fp16x2 of (c - 2^23 - bias) * scale + offset, one
+// rounding to fp16 of a value exact in f32.
+__device__ __forceinline__ uint32_t dq_f32pair(uint32_t f0, uint32_t f1, unsigned long long bias,
+                                               unsigned long long sc, unsigned long long off) {
+    return f2_to_h2(f2fma(f2add((unsigned long long)f0 | ((unsigned long long)f1 << 32), bias), sc, off));
+}
+// An integer 0 .. 2^23 - 1 as f32, exactly, by the exponent bias (an add
+// instead of an integer-to-float conversion).
+__device__ __forceinline__ float u23_f32(uint32_t v) { return __uint_as_float(0x4B000000u | v) - 8388608.f; }
+
 // A thread's half of weight row `row` (32 of the 64 values of each k-block),
 // the rows' scales decoded once per chunk.  Values are exact in f32 (as the
 // reference's dequantize_to_f32 computes them) and rounded once to fp16; per
@@ -215,8 +233,8 @@ struct RowHalf {
                 const uint32_t hi = j < 2 ? hd.z : (j == 2 ? hd.w : 0u);
                 const uint32_t sh = j == 0 ? 0u : (j == 1 ? 24u : (j == 2 ? 16u : 8u));
                 const uint32_t f = __funnelshift_r(lo, hi, sh) & 0xFFFFFFu;
-                const float d1 = d * (float)(f & 63u), m1 = dmin * (float)((f >> 6) & 63u);
-                const float d2 = d * (float)((f >> 12) & 63u), m2 = dmin * (float)((f >> 18) & 63u);
+                const float d1 = d * u23_f32(f & 63u), m1 = dmin * u23_f32((f >> 6) & 63u);
+                const float d2 = d * u23_f32((f >> 12) & 63u), m2 = dmin * u23_f32((f >> 18) & 63u);
                 s[j][0] = f2pack(d1, d1);
                 o[j][0] = f2pack(-m1, -m1);
                 s[j][1] = f2pack(d2, d2);
@@ -296,16 +314,20 @@ struct RowHalf {
             cc[2] = 2 * hf + 1;
             cc[3] = 5 + 2 * hf;
         } else if (DT == GGUF_Q4_K) {
+            // per word the low and the high nibble planes by two masks, then
+            // one byte permute per value
             const uint4 q = *reinterpret_cast<const uint4 *>(ch + ((2 * rh + hf) * 32 + lane) * 16);
             const uint32_t w[4] = {q.x, q.y, q.z, q.w};
             const unsigned long long bias = f2pack(-8388608.f, -8388608.f);
 #pragma unroll
             for (int qq = 0; qq < 2; qq++)  // quarter 2 hf + qq: bytes 8 qq .. 8 qq + 7
 #pragma unroll
-                for (int b = 0; b < 8; b += 2) {
-                    const uint32_t x = w[2 * qq + (b >> 2)] >> (8 * (b & 3));
-                    h[8 * qq + (b >> 1)] = dq_pair(x & 15u, (x >> 8) & 15u, bias, s[J][0], o[J][0]);
-                    h[8 * qq + 4 + (b >> 1)] = dq_pair((x >> 4) & 15u, (x >> 12) & 15u, bias, s[J][1], o[J][1]);
+                for (int wi = 0; wi < 2; wi++) {
+                    const uint32_t lo = w[2 * qq + wi] & 0x0F0F0F0Fu, hi = (w[2 * qq + wi] >> 4) & 0x0F0F0F0Fu;
+                    h[8 * qq + 2 * wi] = dq_f32pair(byte_f32<0>(lo), byte_f32<1>(lo), bias, s[J][0], o[J][0]);
+                    h[8 * qq + 2 * wi + 1] = dq_f32pair(byte_f32<2>(lo), byte_f32<3>(lo), bias, s[J][0], o[J][0]);
+                    h[8 * qq + 4 + 2 * wi] = dq_f32pair(byte_f32<0>(hi), byte_f32<1>(hi), bias, s[J][1], o[J][1]);
+                    h[8 * qq + 5 + 2 * wi] = dq_f32pair(byte_f32<2>(hi), byte_f32<3>(hi), bias, s[J][1], o[J][1]);
                 }
             cc[0] = 2 * hf;
             cc[1] = 4 + 2 * hf;
@@ -325,10 +347,12 @@ struct RowHalf {
                         *reinterpret_cast<const uint2 *>(ch + ((2 * rh + hf) * 32 + lane) * 16 + 8 * (qr & 1));
                     const uint32_t w[2] = {q.x, q.y};
 #pragma unroll
-                    for (int b = 0; b < 8; b += 2) {
-                        const uint32_t x = w[b >> 2] >> (8 * (b & 3));
-                        h[8 * qq + (b >> 1)] = dq_pair(x & 15u, (x >> 8) & 15u, bias, sd, zero);
-                        h[8 * qq + 4 + (b >> 1)] = dq_pair((x >> 4) & 15u, (x >> 12) & 15u, bias, sd, zero);
+                    for (int wi = 0; wi < 2; wi++) {
+                        const uint32_t lo = w[wi] & 0x0F0F0F0Fu, hi = (w[wi] >> 4) & 0x0F0F0F0Fu;
+                        h[8 * qq + 2 * wi] = dq_f32pair(byte_f32<0>(lo), byte_f32<1>(lo), bias, sd, zero);
+                        h[8 * qq + 2 * wi + 1] = dq_f32pair(byte_f32<2>(lo), byte_f32<3>(lo), bias, sd, zero);
+                        h[8 * qq + 4 + 2 * wi] = dq_f32pair(byte_f32<0>(hi), byte_f32<1>(hi), bias, sd, zero);
+                        h[8 * qq + 5 + 2 * wi] = dq_f32pair(byte_f32<2>(hi), byte_f32<3>(hi), bias, sd, zero);
                     }
                     cc[2 * qq] = 4 * hf + (qr & 1);
                     cc[2 * qq + 1] = cc[2 * qq] + 2;
@@ -338,9 +362,9 @@ struct RowHalf {
                     const uint32_t w[4] = {q.x ^ 0x80808080u, q.y ^ 0x80808080u, q.z ^ 0x80808080u,
                                            q.w ^ 0x80808080u};
 #pragma unroll
-                    for (int b = 0; b < 16; b += 2) {
-                        const uint32_t x = w[b >> 2] >> (8 * (b & 3));  // byte ^ 0x80 = q + 128
-                        h[8 * qq + (b >> 1)] = dq_pair(x & 255u, (x >> 8) & 255u, bias, sd, zero);
+                    for (int wi = 0; wi < 4; wi++) {  // byte ^ 0x80 = q + 128
+                        h[8 * qq + 2 * wi] = dq_f32pair(byte_f32<0>(w[wi]), byte_f32<1>(w[wi]), bias, sd, zero);
+                        h[8 * qq + 2 * wi + 1] = dq_f32pair(byte_f32<2>(w[wi]), byte_f32<3>(w[wi]), bias, sd, zero);
                     }
                     cc[2 * qq] = 2 * qr;
                     cc[2 * qq + 1] = 2 * qr + 1;
