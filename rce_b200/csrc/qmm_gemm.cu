@@ -177,16 +177,6 @@ __device__ __forceinline__ uint32_t f2_to_h2(unsigned long long v) {
     return pack_h2(__uint_as_float((uint32_t)v), __uint_as_float((uint32_t)(v >> 32)));
 }
 
-// Two codes -> their values as f32 pair: exact integer c via the exponent
-// bias (0x4B000000 | c is 2^23 + c), minus `bias`, then value = c' * scale -
-// offset in one fused rounding (the product is exact, as in the reference's
-// d1 * q - min1, which rounds once at the subtraction).
-__device__ __forceinline__ uint32_t dq_pair(uint32_t c0, uint32_t c1, unsigned long long bias, unsigned long long sc,
-                                            unsigned long long off) {
-    const unsigned long long f = f2pack(__uint_as_float(0x4B000000u | c0), __uint_as_float(0x4B000000u | c1));
-    return f2_to_h2(f2fma(f2add(f, bias), sc, off));
-}
-
 // Byte b (0..3) of v under the 2^23 exponent byte: 0x4B0000vv, i.e. the f32
 // 2^23 + v for the byte's value v (one byte permute, no shift or mask).
 template <int B>
@@ -195,8 +185,10 @@ __device__ __forceinline__ uint32_t byte_f32(uint32_t v) {
     asm("prmt.b32 %0, %1, %2, %3;" : "=r"(r) : "r"(v), "r"(0x4B000000u), "r"(0x7540u | B));
     return r;
 }
-// (2^23 + c0, 2^23 + c1) -> fp16x2 of (c - 2^23 - bias) * scale + offset, one
-// rounding to fp16 of a value exact in f32.
+// (2^23 + c0, 2^23 + c1) -> fp16x2 of the values (c - bias) * scale + offset:
+// the exact integer c - bias by one subtraction, then the value in one fused
+// rounding (the product is exact, as in the reference's d1 * q - min1, which
+// rounds once at the subtraction), then one rounding to fp16.
 __device__ __forceinline__ uint32_t dq_f32pair(uint32_t f0, uint32_t f1, unsigned long long bias,
                                                unsigned long long sc, unsigned long long off) {
     return f2_to_h2(f2fma(f2add((unsigned long long)f0 | ((unsigned long long)f1 << 32), bias), sc, off));
@@ -300,14 +292,17 @@ struct RowHalf {
 #pragma unroll
             for (int qq = 0; qq < 2; qq++)
 #pragma unroll
-                for (int b = 0; b < 8; b += 2) {
-                    const uint32_t x = w[2 * qq + (b >> 2)] >> (8 * (b & 3));
-                    const int p0 = 8 * (b & 3) + 2 * qq + (b >> 2);  // value l; l + 1 sits 8 bits higher
-                    const uint32_t f0 = ((y0 >> p0) & 1u) << 4, f1 = ((y0 >> (p0 + 8)) & 1u) << 4;
-                    const uint32_t g0 = ((y1 >> p0) & 1u) << 4, g1 = ((y1 >> (p0 + 8)) & 1u) << 4;
-                    h[8 * qq + (b >> 1)] = dq_pair((x & 15u) | f0, ((x >> 8) & 15u) | f1, bias, s[J][0], o[J][0]);
-                    h[8 * qq + 4 + (b >> 1)] =
-                        dq_pair(((x >> 4) & 15u) | g0, ((x >> 12) & 15u) | g1, bias, s[J][1], o[J][1]);
+                for (int wi = 0; wi < 2; wi++) {
+                    // byte c of word 2 qq + wi: its fifth bits are bits 8 c + 2 qq + wi
+                    // of Y0 / Y1, i.e. one shift and one mask put all four at bit 4
+                    const int sh = 2 * qq + wi;
+                    const uint32_t wd = w[2 * qq + wi];
+                    const uint32_t lo = (wd & 0x0F0F0F0Fu) | (((y0 >> sh) & 0x01010101u) << 4);
+                    const uint32_t hi = ((wd >> 4) & 0x0F0F0F0Fu) | (((y1 >> sh) & 0x01010101u) << 4);
+                    h[8 * qq + 2 * wi] = dq_f32pair(byte_f32<0>(lo), byte_f32<1>(lo), bias, s[J][0], o[J][0]);
+                    h[8 * qq + 2 * wi + 1] = dq_f32pair(byte_f32<2>(lo), byte_f32<3>(lo), bias, s[J][0], o[J][0]);
+                    h[8 * qq + 4 + 2 * wi] = dq_f32pair(byte_f32<0>(hi), byte_f32<1>(hi), bias, s[J][1], o[J][1]);
+                    h[8 * qq + 5 + 2 * wi] = dq_f32pair(byte_f32<2>(hi), byte_f32<3>(hi), bias, s[J][1], o[J][1]);
                 }
             cc[0] = 2 * hf;
             cc[1] = 4 + 2 * hf;
