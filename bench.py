@@ -457,6 +457,9 @@ def main():
     ap.add_argument("--profile", action="store_true", help="short run for ncu: warm-up + steps only")
     ap.add_argument("--profile-prefill", type=int, default=0, metavar="M",
                     help="for ncu: only the configs[2] prefill matmul at M tokens, warm-up + steps launches")
+    ap.add_argument("--profile-gemv", default="", metavar="FORMAT",
+                    help="for ncu: only the one-token decode GEMV of a 14336x4096 weight in FORMAT "
+                         "(Q4K, Q5K, Q6K, Q8_0, Q4_0), warm-up + steps launches")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
 
@@ -483,6 +486,23 @@ def main():
 
     dev = torch.device("cuda", local)
     torch.cuda.set_device(dev)
+    if args.profile_gemv:
+        from rce_b200 import synth
+        from rce_b200.gguf import GgufDtype
+
+        fmt = GgufDtype[args.profile_gemv]
+        ctx = R.default_context(dev.index)
+        g = torch.Generator(device=dev)
+        g.manual_seed(5)
+        raw = synth.device_weights(fmt, D_FF, D_MODEL, g, dev)
+        w = R.QuantWeight.from_device_bytes(raw, fmt, D_FF, D_MODEL, ctx=ctx)
+        x = torch.randn((1, D_MODEL), device=dev, generator=g)
+        y = torch.empty((1, D_FF), device=dev)
+        for _ in range(args.warmup + args.steps):
+            R.mm_batched_device(x, w, y)
+        torch.cuda.synchronize(dev)
+        print(json.dumps({"profile_gemv": args.profile_gemv, "launches": args.warmup + args.steps}))
+        return
     if args.profile_prefill:
         from rce_b200 import synth
 

@@ -143,7 +143,8 @@ int run_matmul(rce_qmm_ctx *ctx, const rce_qmm_weight *w, const float *d_x, size
         for (; t0 < t_rows; t0 += (size_t)rce::kQ6MaxTokens) {
             const size_t left = t_rows - t0;
             const int m = (int)(left < (size_t)rce::kQ6MaxTokens ? left : (size_t)rce::kQ6MaxTokens);
-            CUDA_TRY(rce::launch_gemv_q6k(w->dev, g, d_x + t0 * lda, lda, d_y + t0 * ldo, ldo, m, ctx->sm_count, s));
+            CUDA_TRY(rce::launch_gemv_q6k(w->dev, g, d_x + t0 * lda, lda, d_y + t0 * ldo, ldo, m, ctx->sm_count,
+                                          ctx->err_dev, s));
         }
         return ok();
     }

@@ -30,7 +30,7 @@ cudaError_t launch_dequant_q6k(const uint8_t *tiles, float *out, size_t ldo, con
                                int64_t row1, cudaStream_t s);
 int q6k_gemv_warps(const Geometry &g, int sm_count);
 cudaError_t launch_gemv_q6k(const uint8_t *tiles, const Geometry &g, const float *x, size_t ldx, float *y,
-                            size_t ldy, int m, int sm_count, cudaStream_t s);
+                            size_t ldy, int m, int sm_count, int *err, cudaStream_t s);
 
 // Fused all-gather of a row-sharded output over peer memory (see
 // qmm_gather.cuh): rank `rank` of `world` computes rows [row_off, row_off +

@@ -138,7 +138,7 @@ extern "C" int rce_qmm_mm_batched_device_noalloc(rce_qmm_ctx *ctx, const float *
             const size_t left = t_rows - t0;
             const int m = (int)(left < (size_t)rce::kQ6MaxTokens ? left : (size_t)rce::kQ6MaxTokens);
             cudaError_t e = rce::launch_gemv_q6k(w->dev, g, d_a + t0 * lda, lda, d_out + t0 * ldo, ldo, m,
-                                                 ctx->sm_count, s);
+                                                 ctx->sm_count, ctx->err_dev, s);
             if (e != cudaSuccess)
                 return err(RCE_QMM_ERR_CUDA, "mm_batched_device_noalloc: launch: %s", cudaGetErrorString(e));
         }

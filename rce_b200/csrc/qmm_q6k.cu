@@ -20,6 +20,7 @@
 // shuffles per token) and the W warps' sums are added in warp order.  Every
 // output is therefore a sum in a fixed order, the same for every batch.
 #include <cuda_fp16.h>
+#include <atomic>
 #include <cuda_runtime.h>
 
 #include "qmm_internal.h"
@@ -157,7 +158,50 @@ struct Q6Args {
     size_t ldx, ldy;
     Geometry g;
     int x_vec4;  // x rows 16-byte aligned: float4 loads
+    int stages;  // chunk slots per warp in shared memory
+    int *err;    // kernel error word (a bounded wait expired)
 };
+
+constexpr unsigned long long kQ6WaitNs = 1000000000ull;
+
+__device__ __forceinline__ uint32_t q6_smem_u32(const void *p) {
+    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+__device__ __forceinline__ unsigned long long q6_gtimer() {
+    unsigned long long t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+__device__ __forceinline__ bool q6_mbar_try(uint32_t bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\tselp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(bar), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+// Bounded wait; false if the phase did not complete within kQ6WaitNs.
+__device__ __forceinline__ bool q6_mbar_wait(uint32_t bar, uint32_t parity) {
+    if (q6_mbar_try(bar, parity)) return true;
+    const unsigned long long t0 = q6_gtimer();
+    while (!q6_mbar_try(bar, parity))
+        if (q6_gtimer() - t0 > kQ6WaitNs) return false;
+    return true;
+}
+// One chunk from global memory into a shared-memory slot, completing on bar.
+__device__ __forceinline__ void q6_bulk_load(uint32_t dst, const void *src, uint32_t bytes, uint32_t bar) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
+    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst),
+                 "l"(src), "r"(bytes), "r"(bar)
+                 : "memory");
+}
+
+// Shared memory of a launch: stages chunk slots per warp, then one mbarrier
+// per slot.
+__host__ __device__ inline size_t q6_smem_bytes(int warps, int stages) {
+    return (size_t)warps * stages * (chunk_bytes(GGUF_Q6_K) + 8);
+}
 
 // Sum over the lane's eight values of one row: (u - 32) * x, in f32x2 pairs
 // (values 2p, 2p + 1), the two lanes of the pair chain added at the end.
@@ -196,10 +240,32 @@ __global__ void __launch_bounds__(kQ6MaxWarps * 32) gemv_q6k_kernel(const Q6Args
     for (int r = 0; r < 16; r++)
 #pragma unroll
         for (int t = 0; t < NT; t++) acc[r][t] = 0.f;
+    // this warp's chunks c = warp, warp + nw, ... stream through its ring of
+    // S slots by TMA bulk copies (the weights do not depend on the previous
+    // kernel, so the first S are requested before waiting for it)
+    extern __shared__ __align__(128) uint8_t q6smem[];
+    const int S = a.stages;
+    uint8_t *ring = q6smem + (size_t)warp * S * CB;
+    const uint32_t bar0 = q6_smem_u32(q6smem + (size_t)nw * S * CB) + 8u * (uint32_t)(warp * S);
+    const int nmine = warp < nc ? (nc - warp + nw - 1) / nw : 0;
+    if (lane == 0) {
+        for (int i = 0; i < S; i++)
+            asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar0 + 8u * i), "r"(1));
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+        for (int i = 0; i < S && i < nmine; i++)
+            q6_bulk_load(q6_smem_u32(ring + (size_t)i * CB), tbase + (size_t)(warp + i * nw) * CB, CB, bar0 + 8u * i);
+    }
+    __syncwarp();
     // the activations may be the previous kernel's output
     asm volatile("griddepcontrol.wait;" ::: "memory");
-    for (int c = warp; c < nc; c += nw) {
-        const uint8_t *ch = tbase + (size_t)c * CB;
+    int failed_at = nmine;
+    for (int j = 0; j < nmine; j++) {
+        const int c = warp + j * nw, slot = j % S;
+        if (!q6_mbar_wait(bar0 + 8u * slot, (uint32_t)((j / S) & 1))) {
+            failed_at = j;
+            break;
+        }
+        const uint8_t *ch = ring + (size_t)slot * CB;
         unsigned long long xp[NT][4];
 #pragma unroll
         for (int t = 0; t < NT; t++) {
@@ -238,6 +304,23 @@ __global__ void __launch_bounds__(kQ6MaxWarps * 32) gemv_q6k_kernel(const Q6Args
                 for (int t = 0; t < NT; t++) acc[r][t] = fmaf(ds, dot[t], acc[r][t]);
             }
         }
+        // the slot's reads are done: refill it with chunk j + S
+        __syncwarp();
+        if (lane == 0 && j + S < nmine) {
+            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+            q6_bulk_load(q6_smem_u32(ring + (size_t)slot * CB), tbase + (size_t)(c + S * nw) * CB, CB,
+                         bar0 + 8u * slot);
+        }
+    }
+    if (failed_at < nmine) {
+        // report, then let this warp's copies in flight (numbers failed_at ..
+        // min(failed_at + S, nmine) - 1) land before the CTA exits
+        if (lane == 0) {
+            *reinterpret_cast<volatile int *>(a.err) = kKernelErrWaitTimeout;
+            for (int j = failed_at; j < nmine && j < failed_at + S; j++)
+                q6_mbar_wait(bar0 + 8u * (j % S), (uint32_t)((j / S) & 1));
+        }
+        __syncwarp();
     }
     // warp reduction by halving exchanges: after step k (offsets 16, 8, 4,
     // 2) a lane keeps 16 >> (k + 1) rows -- those whose index has the lane's
@@ -328,10 +411,34 @@ int q6k_gemv_warps(const Geometry &g, int sm_count) {
 }
 
 cudaError_t launch_gemv_q6k(const uint8_t *tiles, const Geometry &g, const float *x, size_t ldx, float *y,
-                            size_t ldy, int m, int sm_count, cudaStream_t s) {
+                            size_t ldy, int m, int sm_count, int *err, cudaStream_t s) {
     if (m <= 0 || g.n_tiles == 0) return cudaSuccess;
     if (m > kQ6MaxTokens) return cudaErrorInvalidValue;
+    const int warps = q6k_gemv_warps(g, sm_count);
+    // slots per warp: up to four, within ~110 KB per CTA (two CTAs per SM)
+    const int per_warp = (int)((g.n_chunks + warps - 1) / warps);
+    int stages = (int)((110 * 1024) / ((size_t)warps * (chunk_bytes(GGUF_Q6_K) + 8)));
+    if (stages > 4) stages = 4;
+    if (stages > per_warp) stages = per_warp;
+    if (stages < 1) stages = 1;
+    const size_t smem = q6_smem_bytes(warps, stages);
+    {
+        static std::atomic<unsigned long long> done{0};
+        int dev = 0;
+        cudaError_t e = cudaGetDevice(&dev);
+        if (e != cudaSuccess) return e;
+        const unsigned long long bit = dev < 64 ? (1ull << dev) : 0ull;
+        if (!bit || !(done.load() & bit)) {
+            e = cudaFuncSetAttribute(gemv_q6k_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+            if (e == cudaSuccess)
+                e = cudaFuncSetAttribute(gemv_q6k_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+            if (e != cudaSuccess) return e;
+            if (bit) done.fetch_or(bit);
+        }
+    }
     Q6Args a;
+    a.stages = stages;
+    a.err = err;
     a.x_vec4 = !(reinterpret_cast<uintptr_t>(x) & 15) && (m == 1 || !(ldx & 3));
     a.w = tiles;
     a.x = x;
@@ -341,7 +448,8 @@ cudaError_t launch_gemv_q6k(const uint8_t *tiles, const Geometry &g, const float
     a.g = g;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3((unsigned)g.n_tiles, 1, 1);
-    cfg.blockDim = dim3((unsigned)(32 * q6k_gemv_warps(g, sm_count)), 1, 1);
+    cfg.blockDim = dim3((unsigned)(32 * warps), 1, 1);
+    cfg.dynamicSmemBytes = smem;
     cfg.stream = s;
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
