@@ -9,7 +9,9 @@ rce_qmm_mm_batched_device_multi_gather_bulk + rce_qmm_peer_unpack_bulk), and
 a second round through the same buffers (new epochs), likewise; and two
 shards sharing x gathered from one grouped
 launch (rce_qmm_mm_batched_device_multi_gather) against each rank's grouped
-device call, at 1, 3 and 20 tokens.  Skipped with fewer than two GPUs."""
+device call, at 1, 3 and 20 tokens.  Skipped with fewer than two GPUs.
+On one GPU: an unpack whose words never arrive ends its bounded wait with
+the timeout in the context's error word, and the context stays usable."""
 import os
 import socket
 
@@ -131,3 +133,43 @@ def test_fused_gather_two_gpus():
         assert res[r]["gemm"] == (True, True), res
         assert res[r]["group"] == (True,) * 6, res
         assert res[r]["device_error"] == 0
+
+
+def test_unpack_wait_expires_and_is_reported(ctx):
+    # Failure detection without a GPU fault: a receive buffer that no peer
+    # ever writes (one GPU, nothing else running).  The unpack kernel's
+    # bounded wait runs out after about a second, records the timeout in the
+    # context's error word and returns; the context stays usable.
+    import ctypes
+    import time
+
+    import torch
+
+    import oracle as O
+    import rce_b200 as R
+    import refcases
+    from rce_b200 import _lib
+
+    L = _lib.lib()
+    t_rows, n, own0, own1 = 2, 64, 0, 32
+    ll = torch.zeros((t_rows, n), dtype=torch.int64, device="cuda:0")  # every word at epoch 0
+    y = torch.zeros((t_rows, n), device="cuda:0")
+    stream = torch.cuda.current_stream()
+    assert ctx.device_error() == 0
+    t0 = time.time()
+    rc = L.rce_qmm_peer_unpack(ctx.handle, ctypes.c_void_p(ll.data_ptr()), ctypes.c_void_p(y.data_ptr()), n, t_rows,
+                               n, own0, own1, 7, None, ctypes.c_void_p(stream.cuda_stream))
+    assert rc == 0, L.rce_qmm_last_error()
+    torch.cuda.synchronize()
+    waited = time.time() - t0
+    assert ctx.device_error() == 1  # kKernelErrWaitTimeout, cleared by the read
+    assert 0.5 < waited < 30, waited
+    assert torch.count_nonzero(y) == 0  # nothing copied for the words that never arrived
+    # the context and the device still work
+    n2, k2 = 256, 1024
+    w, _, _, _, x = refcases.seeded_case(O.GGUF_Q4_K, n2, k2, 1, 3)
+    qw = R.QuantWeight.from_owned_bytes(w, O.GGUF_Q4_K, n2, k2, ctx=ctx)
+    got = R.mm_batched(x, 1, qw)
+    want = O.mm_batched(x, 1, w, O.GGUF_Q4_K, n2, k2)
+    assert float(np.abs(got - want).max() / np.abs(want).max()) <= 1e-3
+    assert ctx.device_error() == 0
