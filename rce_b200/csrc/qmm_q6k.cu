@@ -14,8 +14,9 @@
 // GEMV: one CTA per 16-row tile, W warps splitting the tile's chunks
 // (chunk c to warp c % W); lane L takes values 8L .. 8L + 7 of every row of a
 // chunk, so its activations are loaded once and used for all 16 rows.  Per
-// row and chunk the eight products are summed in f32 (codes and activations
-// exact, two f32x2 chains), scaled by d * sc once, and added to the lane's
+// row and chunk the eight products q' x, q' = 0.5 + u / 256 exact, are summed
+// in f32 (two f32x2 chains), turned into sum (u - 32) x with the chunk's
+// activation sum, scaled by d * sc once, and added to the lane's
 // row sum; a warp then reduces its lanes' sums (halving exchanges: 16
 // shuffles per token) and the W warps' sums are added in warp order.  Every
 // output is therefore a sum in a fixed order, the same for every batch.
@@ -203,8 +204,10 @@ __host__ __device__ inline size_t q6_smem_bytes(int warps, int stages) {
     return (size_t)warps * stages * (chunk_bytes(GGUF_Q6_K) + 8);
 }
 
-// Sum over the lane's eight values of one row: (u - 32) * x, in f32x2 pairs
+// Sum over the lane's eight values of one row of q' * x, q' = 0.5 + u / 256
+// (exact: the code byte under the exponent byte of 0.5), in f32x2 pairs
 // (values 2p, 2p + 1), the two lanes of the pair chain added at the end.
+// The caller recovers sum (u - 32) * x = 256 * sum q' x - 160 * sum x.
 // lo: the row's lo-plane word (value e in bits 4e .. 4e + 3), hi: its
 // hi-plane half word (value e in bits 2e, 2e + 1).
 template <int NT>
@@ -214,13 +217,11 @@ __device__ __forceinline__ void row_dot(uint32_t lo, uint32_t hi, const unsigned
     const uint32_t s = prmt(hi & 0x0F0Fu, (hi >> 4) & 0x0F0Fu, 0x5140u);  // byte b = hi bits of values 2b, 2b+1
     const uint32_t ua = (lo & 0x0F0F0F0Fu) | ((s << 4) & 0x30303030u);
     const uint32_t ub = ((lo >> 4) & 0x0F0F0F0Fu) | ((s << 2) & 0x30303030u);
-    // 2^23 + u as f32 (exponent byte 0x4B over the code byte), minus 2^23 + 32
-    const unsigned long long bias = f2pack(-8388640.f, -8388640.f);
     unsigned long long acc[NT];
 #pragma unroll
     for (int p = 0; p < 4; p++) {
-        const uint32_t sel = 0x7540u | (uint32_t)p;
-        const unsigned long long q = f2add(u2pack(prmt(ua, 0x4B000000u, sel), prmt(ub, 0x4B000000u, sel)), bias);
+        const uint32_t sel = 0x7054u | ((uint32_t)p << 8);  // bytes: 0, 0, code byte p, 0x3F
+        const unsigned long long q = u2pack(prmt(ua, 0x3F000000u, sel), prmt(ub, 0x3F000000u, sel));
 #pragma unroll
         for (int t = 0; t < NT; t++) acc[t] = p == 0 ? f2mul(q, xp[t][0]) : f2fma(q, xp[t][p], acc[t]);
     }
@@ -281,6 +282,13 @@ __global__ void __launch_bounds__(kQ6MaxWarps * 32) gemv_q6k_kernel(const Q6Args
                 for (int p = 0; p < 4; p++) xp[t][p] = f2pack(xr[2 * p], xr[2 * p + 1]);
             }
         }
+        // -160 * (the lane's eight activations), once per chunk for all rows
+        float m160[NT];
+#pragma unroll
+        for (int t = 0; t < NT; t++) {
+            const unsigned long long s2 = f2add(f2add(xp[t][0], xp[t][1]), f2add(xp[t][2], xp[t][3]));
+            m160[t] = -160.f * (f2lo(s2) + f2hi(s2));
+        }
         const uint4 d0 = *reinterpret_cast<const uint4 *>(ch + kQ6D), d1 = *reinterpret_cast<const uint4 *>(ch + kQ6D + 16);
         const uint32_t dw[8] = {d0.x, d0.y, d0.z, d0.w, d1.x, d1.y, d1.z, d1.w};
 #pragma unroll
@@ -301,7 +309,7 @@ __global__ void __launch_bounds__(kQ6MaxWarps * 32) gemv_q6k_kernel(const Q6Args
                 row_dot<NT>(lo[i], hi[i], xp, dot);
                 const float ds = f16_to_f32(dw[r >> 1] >> (16 * (r & 1))) * (float)sc[i];
 #pragma unroll
-                for (int t = 0; t < NT; t++) acc[r][t] = fmaf(ds, dot[t], acc[r][t]);
+                for (int t = 0; t < NT; t++) acc[r][t] = fmaf(ds, fmaf(256.f, dot[t], m160[t]), acc[r][t]);
             }
         }
         // the slot's reads are done: refill it with chunk j + S
