@@ -12,7 +12,8 @@
 // 16-bit word.
 //
 // GEMV: one CTA per 16-row tile, W warps splitting the tile's chunks
-// (chunk c to warp c % W); lane L takes values 8L .. 8L + 7 of every row of a
+// (chunk c to warp c % W), each warp streaming its chunks through a private
+// shared-memory ring filled by TMA bulk copies; lane L takes values 8L .. 8L + 7 of every row of a
 // chunk, so its activations are loaded once and used for all 16 rows.  Per
 // row and chunk the eight products q' x, q' = 0.5 + u / 256 exact, are summed
 // in f32 (two f32x2 chains), turned into sum (u - 32) x with the chunk's
@@ -21,8 +22,9 @@
 // shuffles per token) and the W warps' sums are added in warp order.  Every
 // output is therefore a sum in a fixed order, the same for every batch.
 #include <cuda_fp16.h>
-#include <atomic>
 #include <cuda_runtime.h>
+
+#include <atomic>
 
 #include "qmm_internal.h"
 
