@@ -159,13 +159,16 @@ int rce_qmm_mm_batched_device_multi(rce_qmm_ctx *ctx, const float *d_a, size_t l
  * cudaMalloc, cudaFree or allocating library routine.  Outputs equal
  * rce_qmm_mm_batched_device's bit for bit under the same context settings.
  * Limits: a GEMM batch (prefill_min_tokens tokens or more) needing more than
- * 16 MiB of workspace -- t_rows * n_cols * 2 bytes rounded up to 256, plus
- * 4 bytes per token; 2047 tokens at n_cols 4096 -- is rejected with
- * RCE_QMM_ERR_INVALID.  Every call on a GPU shares the array, whatever its
+ * 16 MiB of workspace -- t_rows * n_cols * 2 bytes (twice that for batches of
+ * up to 128 tokens, whose activations the GEMM carries as two fp16 terms)
+ * rounded up to 256, plus 4 bytes per token; 2047 tokens at n_cols 4096 -- is
+ * rejected with RCE_QMM_ERR_INVALID.  Every call on a GPU shares the array, whatever its
  * context or stream, so calls that overlap on the GPU race: order them.  The
  * array keeps the last call's contents; nothing in it needs to start at zero.
  * The first call on each GPU looks up the array's device address, so make it
- * before any stream capture.  A weight too large for the decode GEMV's
+ * before any stream capture; the address is kept for the life of the
+ * process, so, like every handle of this library, the entry point must not
+ * be used after cudaDeviceReset.  A weight too large for the decode GEMV's
  * shared-memory plan is rejected with RCE_QMM_ERR_UNSUPPORTED. */
 int rce_qmm_mm_batched_device_noalloc(rce_qmm_ctx *ctx, const float *d_a, size_t lda, size_t t_rows,
                                       const rce_qmm_weight *w, float *d_out, size_t ldo, void *stream);

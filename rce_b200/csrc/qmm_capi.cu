@@ -908,8 +908,10 @@ int rce_qmm_moe_ffn_device(rce_qmm_ctx *ctx, const float *d_x, size_t ldx, size_
     o += al(P * (size_t)d_ff * 4);
     const size_t o_y = o;
     o += al(P * (size_t)d_model * 4);
-    const size_t o_xh2 = o;  // grouped path: fp16 SwiGLU outputs and both inputs' row scales
-    o += al(P * (size_t)d_ff * 2);
+    // grouped path: the gate/up input's two fp16 terms reuse xg's bytes; the
+    // SwiGLU outputs' two fp16 terms; both inputs' row scales
+    const size_t o_xh2 = o;
+    o += al(2 * P * (size_t)d_ff * 2);
     const size_t o_inv = o;
     o += al(P * 4);
     const size_t o_inv2 = o;

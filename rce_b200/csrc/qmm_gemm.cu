@@ -10,7 +10,16 @@
 // scaled per token by a power of two (exact) so that |x * s| < 2^14 and
 // rounded to fp16; products accumulate in f32 in tensor memory.  fp16 (11
 // significant bits) instead of bf16 (8) keeps the output within the 1e-3
-// normwise bar for Q4_K, at the same tensor-core rate.
+// bar for Q4_K, at the same tensor-core rate.  Token tiles of up to
+// kTwoTermMaxTile tokens (dense batches of up to kGemmTwoTermMaxTokens
+// tokens, and every expert-grouped launch) carry each activation as two fp16
+// terms, high + low (about 22 significant bits): the low rows sit after the
+// high rows in the activation stage, one MMA of N = high + low rows covers
+// both, and the epilogue adds the two accumulator halves.  At those widths
+// the MMA instruction count is the same as for the high rows alone, and the
+// only rounding left is the weights' (the activations' rounding is what
+// gives the one-term path its error tail on outputs that partly cancel,
+// e.g. an MoE token's weighted sum of two experts).
 //
 // Structure (one CTA = 128 weight rows x BN tokens, all of K; BN up to 512,
 // i.e. two N = 256 accumulators filling tensor memory, so that a weight
@@ -151,6 +160,7 @@ struct GemmArgs {
     int t_rows;
     int bn;
     int box_rows;  // rows of one activation TMA box
+    int lo_row;    // two-term activations: row of the tensor map where the low terms start (0: one term)
 };
 
 // Packed f32x2 arithmetic (two lanes of f32 per instruction).
@@ -382,15 +392,19 @@ struct GemmSmem {
 
 constexpr int kMaxA = 8, kMaxB = 4, kMaxP = 4;  // ring depth limits (barrier slots)
 
-__host__ __device__ inline GemmSmem gemm_smem(int dt, int bn) {
+// Token tiles up to this width carry two-term activations (N = 2 bn <= 256).
+constexpr int kTwoTermMaxTile = 128;
+
+__host__ __device__ inline GemmSmem gemm_smem(int dt, int bn, int terms) {
     // Rings as deep as 227 KB allow: the dequantiser <-> MMA hand-off takes
     // a few thousand cycles, so the A ring should span several k-blocks;
     // the activation ring shrinks as its stages grow with bn.
     constexpr size_t kLimit = 227 * 1024;  // dynamic shared memory per CTA (opt-in)
     GemmSmem L;
-    L.b_stages = bn > 256 ? 2 : (bn > 128 ? 3 : kMaxB);
+    const int brows = terms * bn;  // activation rows per stage
+    L.b_stages = brows > 256 ? 2 : (brows > 128 ? 3 : kMaxB);
     const size_t a_stage = (size_t)kBM * kBK * 2;
-    const size_t b_bytes = (size_t)L.b_stages * bn * kBK * 2;
+    const size_t b_bytes = (size_t)L.b_stages * brows * kBK * 2;
     const size_t slot = (size_t)8 * chunk_bytes(dt);
     const size_t misc = 64 * 8 + 16 + 1024;
     L.pslots = 2;
@@ -505,7 +519,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     // integer round trip would turn every access into a generic one)
     uint8_t *smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
     const int bn = p.bn;
-    const GemmSmem L = gemm_smem(DT, bn);
+    const int terms = p.lo_row ? 2 : 1;
+    const GemmSmem L = gemm_smem(DT, bn, terms);
     const int NA = L.a_stages, NB = L.b_stages, NP = L.pslots;
     uint8_t *a_st = smem + L.a;
     uint8_t *b_st = smem + L.b;
@@ -543,10 +558,14 @@ __global__ void __launch_bounds__(kThreads, 1)
     // activation rows loaded per k-block (whole boxes) and MMA width
     const int b_rows = kGrouped ? (live + p.box_rows - 1) / p.box_rows * p.box_rows : bn;
     const int ncol = kGrouped ? (live + 15) / 16 * 16 : bn;
+    // two terms: the low rows follow the b_rows high rows of a stage, so
+    // the MMA's N covers b_rows + ncol rows and accumulator column c's low
+    // part sits at column b_rows + c
+    const int nmma = terms == 2 ? b_rows + ncol : ncol;
     const int nchunks = p.g.n_chunks;
     const int nkb = nchunks * 4;
     const int MW = mma_warps(bn);
-    const uint32_t acc_cols = tmem_cols(bn), ncols = acc_cols * (uint32_t)MW;
+    const uint32_t acc_cols = tmem_cols(terms * bn), ncols = acc_cols * (uint32_t)MW;
 
     if (tid == 0) {
         for (int s = 0; s < NP; s++) {
@@ -610,10 +629,14 @@ __global__ void __launch_bounds__(kThreads, 1)
                     ok = false;
                     break;
                 }
-                mbar_expect_tx(BF(st), (uint32_t)(b_rows * kBK * 2));
-                uint8_t *dst = b_st + (size_t)st * bn * kBK * 2;
-                for (int r0 = 0; r0 < b_rows; r0 += p.box_rows)  // a tensor-map box is at most 256 rows
+                mbar_expect_tx(BF(st), (uint32_t)(terms * b_rows * kBK * 2));
+                uint8_t *dst = b_st + (size_t)st * terms * bn * kBK * 2;
+                for (int r0 = 0; r0 < b_rows; r0 += p.box_rows) {  // a tensor-map box is at most 256 rows
                     tma_2d(smem_u32(dst + (size_t)r0 * kBK * 2), &xmap, kb * kBK, t_begin + tok0 + r0, BF(st));
+                    if (terms == 2)
+                        tma_2d(smem_u32(dst + (size_t)(b_rows + r0) * kBK * 2), &xmap, kb * kBK,
+                               p.lo_row + t_begin + tok0 + r0, BF(st));
+                }
                 if (++st == NB) {
                     st = 0;
                     ph ^= 1;
@@ -640,12 +663,12 @@ __global__ void __launch_bounds__(kThreads, 1)
         // One lane issues; descriptors advance by 32 bytes (2 in the >> 4
         // address field) per K = 16 step and by a whole stage per stage.
         const int w = warp - kMmaWarp;
-        const int nsub = ncol > 256 ? ncol / 256 : 1, nw = ncol > 256 ? 256 : ncol;
+        const int nsub = nmma > 256 ? nmma / 256 : 1, nw = nmma > 256 ? 256 : nmma;
         const uint32_t idesc = idesc_f16(nw);
         const uint32_t acc = tmem + (uint32_t)w * acc_cols;
         if (lane == 0) {
             const uint64_t da0 = sw128_desc(smem_u32(a_st)), db0 = sw128_desc(smem_u32(b_st));
-            const uint64_t a_step = (uint64_t)(kBM * kBK * 2) >> 4, b_step = (uint64_t)(bn * kBK * 2) >> 4;
+            const uint64_t a_step = (uint64_t)(kBM * kBK * 2) >> 4, b_step = (uint64_t)(terms * bn * kBK * 2) >> 4;
             const uint64_t h_step = (uint64_t)(256 * kBK * 2) >> 4;
             int sa = w, sb = w;  // stages of k-block kb = w (MW <= NA, NB)
             uint32_t aph = 0, bph = 0;
@@ -693,14 +716,18 @@ __global__ void __launch_bounds__(kThreads, 1)
             for (int c0 = c_begin; c0 < c_end; c0 += 8) {
                 float v[8];
                 for (int w = 0; w < MW; w++) {  // the issuers' accumulators, added in order
-                    uint32_t r[8];
-                    asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
-                                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
-                                   "=r"(r[7])
-                                 : "r"(tmem + ((uint32_t)lane_base << 16) + (uint32_t)w * acc_cols + (uint32_t)c0));
-                    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+                    for (int h = 0; h < terms; h++) {  // high part, then low part
+                        uint32_t r[8];
+                        const uint32_t col = (uint32_t)w * acc_cols + (uint32_t)(c0 + h * b_rows);
+                        asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
+                                     : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]),
+                                       "=r"(r[6]), "=r"(r[7])
+                                     : "r"(tmem + ((uint32_t)lane_base << 16) + col));
+                        asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 #pragma unroll
-                    for (int i = 0; i < 8; i++) v[i] = w ? v[i] + __uint_as_float(r[i]) : __uint_as_float(r[i]);
+                        for (int i = 0; i < 8; i++)
+                            v[i] = (w || h) ? v[i] + __uint_as_float(r[i]) : __uint_as_float(r[i]);
+                    }
                 }
                 if (row < p.g.n_rows) {
 #pragma unroll
@@ -723,12 +750,13 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
 }
 
-// X f32 [t][ldx] -> Xh fp16 [t][k] with x * 2^e, |x * 2^e| < 2^14, and 1/2^e.
+// X f32 [t][ldx] -> Xh fp16 [t][k] with x * 2^e, |x * 2^e| < 2^14, and 1/2^e;
+// with xl, also the low terms [t][k].
 __global__ void __launch_bounds__(kPrepThreads) prep_kernel(const float *x, size_t ldx, int k, __half *xh,
-                                                             float *inv) {
+                                                             float *inv, __half *xl) {
     const int t = blockIdx.x;
     const float *xr = x + (size_t)t * ldx;
-    prep_row([&](int i) { return xr[i]; }, k, xh + (size_t)t * k, inv + t);
+    prep_row([&](int i) { return xr[i]; }, k, xh + (size_t)t * k, inv + t, xl ? xl + (size_t)t * k : nullptr);
 }
 
 using EncodeTiled = CUresult (*)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *, const cuuint64_t *,
@@ -821,8 +849,10 @@ int gemm_bn(int dt, int t_rows) {
     return bn < 16 ? 16 : bn;
 }
 
+int gemm_terms(int t_rows) { return t_rows <= kGemmTwoTermMaxTokens ? 2 : 1; }
+
 size_t gemm_workspace_bytes(const Geometry &g, int t_rows) {
-    const size_t xh = (size_t)t_rows * g.n_cols * 2;
+    const size_t xh = (size_t)gemm_terms(t_rows) * t_rows * g.n_cols * 2;
     return (xh + 255) / 256 * 256 + (size_t)t_rows * 4;
 }
 
@@ -830,10 +860,14 @@ cudaError_t launch_gemm(int dt, const uint8_t *tiles, const Geometry &g, const f
                         size_t ldy, int t_rows, void *workspace, int *err, cudaStream_t s) {
     if (t_rows <= 0 || g.n_rows <= 0) return cudaSuccess;
     if (!encode_fn()) return cudaErrorNotSupported;
+    // [terms][t_rows][n_cols] fp16 activations (high terms, then low), then
+    // the per-token inverse scales
+    const int terms = gemm_terms(t_rows);
     __half *xh = static_cast<__half *>(workspace);
-    const size_t xh_bytes = ((size_t)t_rows * g.n_cols * 2 + 255) / 256 * 256;
+    const size_t xh_bytes = ((size_t)terms * t_rows * g.n_cols * 2 + 255) / 256 * 256;
     float *inv = reinterpret_cast<float *>(static_cast<uint8_t *>(workspace) + xh_bytes);
-    prep_kernel<<<t_rows, kPrepThreads, 0, s>>>(x, ldx, (int)g.n_cols, xh, inv);
+    prep_kernel<<<t_rows, kPrepThreads, 0, s>>>(x, ldx, (int)g.n_cols, xh, inv,
+                                                terms == 2 ? xh + (size_t)t_rows * g.n_cols : nullptr);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return e;
     int bn = gemm_bn(dt, t_rows);
@@ -857,9 +891,10 @@ cudaError_t launch_gemm(int dt, const uint8_t *tiles, const Geometry &g, const f
     }
     CUtensorMap map;
     const int box_rows = bn < 256 ? bn : 256;
-    e = act_map(&map, xh, t_rows, g.n_cols, box_rows);
+    e = act_map(&map, xh, terms * t_rows, g.n_cols, box_rows);
     if (e != cudaSuccess) return e;
     GemmArgs a;
+    a.lo_row = terms == 2 ? t_rows : 0;
     a.w = tiles;
     a.y = y;
     a.inv_scale = inv;
@@ -869,7 +904,7 @@ cudaError_t launch_gemm(int dt, const uint8_t *tiles, const Geometry &g, const f
     a.t_rows = t_rows;
     a.bn = bn;
     a.box_rows = box_rows;
-    const GemmSmem lay = gemm_smem(dt, bn);
+    const GemmSmem lay = gemm_smem(dt, bn, terms);
     if (lay.pslots < 2) return cudaErrorInvalidConfiguration;
     dim3 grid((g.n_tiles + 7) / 8, (t_rows + bn - 1) / bn);
     return launch_any(dt, map, a, NoGroup{}, grid, lay.total, s);
@@ -877,12 +912,13 @@ cudaError_t launch_gemm(int dt, const uint8_t *tiles, const Geometry &g, const f
 
 // Token tile of a grouped launch.
 static int gemm_grouped_bn(int rows, int n_sets, int max_rows) {
-    // twice the average rows per set, in whole 64-row boxes, 64 .. 256: sets
-    // up to that size are one token tile (each weight tile dequantised once)
+    // twice the average rows per set, in whole 64-row boxes, 64 ..
+    // kTwoTermMaxTile (two-term activations): sets up to that size are one
+    // token tile (each weight tile dequantised once)
     const long avg2 = n_sets > 0 ? (2L * rows + n_sets - 1) / n_sets : rows;
     long bn = (avg2 + 63) / 64 * 64;
     if (bn > (long)(max_rows + 63) / 64 * 64) bn = (long)(max_rows + 63) / 64 * 64;
-    return (int)(bn < 64 ? 64 : (bn > 256 ? 256 : bn));
+    return (int)(bn < 64 ? 64 : (bn > kTwoTermMaxTile ? kTwoTermMaxTile : bn));
 }
 
 cudaError_t launch_gemm_grouped(int dt, const uint8_t *const *ws, float *const *ys, const int *set, int n,
@@ -894,9 +930,10 @@ cudaError_t launch_gemm_grouped(int dt, const uint8_t *const *ws, float *const *
     const int bn = gemm_grouped_bn(rows_hint, n_sets, max_rows);
     constexpr int kBox = 64;
     CUtensorMap map;
-    cudaError_t e = act_map(&map, xh, rows, g.n_cols, kBox);
+    cudaError_t e = act_map(&map, xh, 2 * rows, g.n_cols, kBox);  // high rows, then low rows
     if (e != cudaSuccess) return e;
     GemmArgs a;
+    a.lo_row = rows;
     a.w = nullptr;
     a.y = nullptr;
     a.inv_scale = inv;
@@ -914,7 +951,7 @@ cudaError_t launch_gemm_grouped(int dt, const uint8_t *const *ws, float *const *
         if (z < n && (set[z] < 0 || set[z] >= n_sets)) return cudaErrorInvalidValue;
     }
     q.off = off;
-    const GemmSmem lay = gemm_smem(dt, bn);
+    const GemmSmem lay = gemm_smem(dt, bn, 2);
     if (lay.pslots < 2) return cudaErrorInvalidConfiguration;
     if ((max_rows + bn - 1) / bn > 65535) return cudaErrorInvalidValue;
     dim3 grid((g.n_tiles + 7) / 8, (max_rows + bn - 1) / bn, n);

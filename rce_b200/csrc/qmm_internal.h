@@ -109,15 +109,19 @@ cudaError_t launch_gather_unpack_bulk(const float *buf, size_t flag_off, float *
 // Prefill matmul on tcgen05 (fp16 operands, f32 accumulation in tensor
 // memory) for t_rows tokens at once.  `workspace` holds
 // gemm_workspace_bytes() bytes (the fp16 activations and per-token scales).
+// Batches of up to kGemmTwoTermMaxTokens tokens carry each activation as two
+// fp16 terms (gemm_terms() == 2: high + low, about 22 significant bits).
+constexpr int kGemmTwoTermMaxTokens = 128;
+int gemm_terms(int t_rows);
 size_t gemm_workspace_bytes(const Geometry &g, int t_rows);
 cudaError_t launch_gemm(int dt, const uint8_t *tiles, const Geometry &g, const float *x, size_t ldx, float *y,
                         size_t ldy, int t_rows, void *workspace, int *err, cudaStream_t s);
 
 // Expert-grouped prefill matmul: one launch for up to kGemmMaxGroup weights
-// of one shape.  Entry z multiplies ws[z] by the fp16 activation rows
-// [off[set[z]], off[set[z] + 1]) of xh ([rows][g.n_cols], scaled per row as
-// the MoE prep kernels write it, 1/scale in inv) into the same rows of ys[z]
-// (row stride ldy).  off (n_sets + 1 entries) is read on the device; no set
+// of one shape.  Entry z multiplies ws[z] by the two-term fp16 activation
+// rows [off[set[z]], off[set[z] + 1]) of xh ([2][rows][g.n_cols]: high terms,
+// then low terms, scaled per row as the MoE prep kernels write them, 1/scale
+// in inv) into the same rows of ys[z] (row stride ldy).  off (n_sets + 1 entries) is read on the device; no set
 // may hold more than max_rows rows; rows_hint (the expected rows over all
 // sets) sizes the token tile.
 constexpr int kGemmMaxGroup = 32;
@@ -139,9 +143,10 @@ cudaError_t launch_moe_gather(const float *x, size_t ldx, const int32_t *token, 
                               cudaStream_t s);
 cudaError_t launch_swiglu(const float *g, const float *u, float *h, size_t n, cudaStream_t s);
 // The GEMM inputs of the grouped path, for rows r < *n_rows (a device
-// count; max_rows bounds it): gather_prep xh[r] = fp16(x[token[r]] * s_r),
-// swiglu_prep xh[r] = fp16(silu(g[r]) * u[r] * s_r) (g, u rows of ld
-// floats); s_r a power of two with |v * s_r| < 2^14, inv[r] = 1 / s_r.
+// count; max_rows bounds it): gather_prep v = x[token[r]], swiglu_prep
+// v = silu(g[r]) * u[r] (g, u rows of ld floats), each as two fp16 terms
+// xh[r] = fp16(v * s_r) and xh[max_rows + r] = fp16(v * s_r - xh[r]); s_r a
+// power of two with |v * s_r| < 2^14, inv[r] = 1 / s_r.
 cudaError_t launch_moe_gather_prep(const float *x, size_t ldx, const int32_t *token, const int32_t *n_rows,
                                    int max_rows, int d_model, void *xh, float *inv, cudaStream_t s);
 cudaError_t launch_moe_swiglu_prep(const float *g, const float *u, size_t ld, const int32_t *n_rows, int max_rows,

@@ -128,25 +128,27 @@ __global__ void swiglu_kernel(const float *g, const float *u, float *h, size_t n
 }
 
 // GEMM input of the grouped path, row r = blockIdx.x: x[token[r]] scaled and
-// rounded to fp16 (the gather and the dense prep in one pass).
+// rounded to two fp16 terms (high in xh, low in xl; the gather and the dense
+// prep in one pass).
 __global__ void __launch_bounds__(kPrepThreads) gather_prep_kernel(const float *x, size_t ldx, const int32_t *token,
                                                                     const int32_t *n_rows, int d_model, __half *xh,
-                                                                    float *inv) {
+                                                                    float *inv, __half *xl) {
     const int r = blockIdx.x;
     if (r >= *n_rows) return;
     const float *src = x + (size_t)token[r] * ldx;
-    prep_row([&](int i) { return src[i]; }, d_model, xh + (size_t)r * d_model, inv + r);
+    prep_row([&](int i) { return src[i]; }, d_model, xh + (size_t)r * d_model, inv + r, xl + (size_t)r * d_model);
 }
 
 // GEMM input of the down matmul, row r = blockIdx.x: h = silu(g) * u exactly
-// as swiglu_kernel computes it, scaled and rounded to fp16.
+// as swiglu_kernel computes it, scaled and rounded to two fp16 terms.
 __global__ void __launch_bounds__(kPrepThreads) swiglu_prep_kernel(const float *g, const float *u, size_t ld,
                                                                     const int32_t *n_rows, int d_ff, __half *xh,
-                                                                    float *inv) {
+                                                                    float *inv, __half *xl) {
     const int r = blockIdx.x;
     if (r >= *n_rows) return;
     const float *gr = g + (size_t)r * ld, *ur = u + (size_t)r * ld;
-    prep_row([&](int i) { return __fmul_rn(silu_ref(gr[i]), ur[i]); }, d_ff, xh + (size_t)r * d_ff, inv + r);
+    prep_row([&](int i) { return __fmul_rn(silu_ref(gr[i]), ur[i]); }, d_ff, xh + (size_t)r * d_ff, inv + r,
+             xl + (size_t)r * d_ff);
 }
 
 // out[t] = sum over route slots j (in order, from 0) of w[t][j] * y[pos[t][j]],
@@ -203,15 +205,18 @@ cudaError_t launch_swiglu(const float *g, const float *u, float *h, size_t n, cu
 cudaError_t launch_moe_gather_prep(const float *x, size_t ldx, const int32_t *token, const int32_t *n_rows,
                                    int max_rows, int d_model, void *xh, float *inv, cudaStream_t s) {
     if (max_rows <= 0) return cudaSuccess;
-    gather_prep_kernel<<<max_rows, kPrepThreads, 0, s>>>(x, ldx, token, n_rows, d_model, static_cast<__half *>(xh),
-                                                          inv);
+    __half *hi = static_cast<__half *>(xh);
+    gather_prep_kernel<<<max_rows, kPrepThreads, 0, s>>>(x, ldx, token, n_rows, d_model, hi, inv,
+                                                          hi + (size_t)max_rows * d_model);
     return cudaGetLastError();
 }
 
 cudaError_t launch_moe_swiglu_prep(const float *g, const float *u, size_t ld, const int32_t *n_rows, int max_rows,
                                    int d_ff, void *xh, float *inv, cudaStream_t s) {
     if (max_rows <= 0) return cudaSuccess;
-    swiglu_prep_kernel<<<max_rows, kPrepThreads, 0, s>>>(g, u, ld, n_rows, d_ff, static_cast<__half *>(xh), inv);
+    __half *hi = static_cast<__half *>(xh);
+    swiglu_prep_kernel<<<max_rows, kPrepThreads, 0, s>>>(g, u, ld, n_rows, d_ff, hi, inv,
+                                                          hi + (size_t)max_rows * d_ff);
     return cudaGetLastError();
 }
 

@@ -17,7 +17,8 @@
 //
 // Rules that follow from the one shared array:
 //  - a batch whose workspace exceeds kNoallocScratchBytes (t_rows * n_cols * 2
-//    bytes, rounded up to 256, plus 4 bytes per token) is rejected with
+//    bytes, twice that for the GEMM's two-term activations at up to 128
+//    tokens, rounded up to 256, plus 4 bytes per token) is rejected with
 //    RCE_QMM_ERR_INVALID;
 //  - every call on a device uses the same array, whatever its context or
 //    stream, so calls whose GEMM launches overlap on the GPU race and return
@@ -27,7 +28,10 @@
 //    the tensor map's zero fill), so nothing has to be cleared;
 //  - the first call on a device looks the array's device address up
 //    (cudaGetSymbolAddress, which may load the module), so make that first
-//    call before any stream capture.
+//    call before any stream capture;
+//  - the address is cached for the life of the process: after a
+//    cudaDeviceReset (which also frees every weight this library holds) the
+//    entry point must not be used.
 #include <cuda_runtime.h>
 
 #include <cstdarg>

@@ -1,8 +1,11 @@
 // qmm_prep.cuh -- the activation side of the tensor-core GEMM: one row of f32
 // values scaled by a power of two s (|v * s| < 2^14, so the scaling is exact
-// and no value overflows fp16) and rounded to fp16, with 1/s kept per row.
-// Shared by the dense prep kernel (qmm_gemm.cu) and the MoE gather and
-// SwiGLU preps (qmm_moe.cu), so every GEMM input is rounded the same way.
+// and no value overflows fp16) and rounded to fp16 (the high term), with 1/s
+// kept per row; optionally also the low term, the fp16 rounding of the
+// remainder v * s - high (exact in f32), so that high + low carries about 22
+// significant bits of v.  Shared by the dense prep kernel (qmm_gemm.cu) and
+// the MoE gather and SwiGLU preps (qmm_moe.cu), so every GEMM input is
+// rounded the same way.
 #pragma once
 
 #include <cuda_fp16.h>
@@ -12,11 +15,12 @@ namespace rce {
 constexpr int kPrepThreads = 256;
 
 // One kPrepThreads-thread block per row: val(i) yields element i (it is
-// called twice per element, for the row maximum and for the store).  A row
+// called twice per element, for the row maximum and for the store); o_lo
+// (optional) receives the low terms.  A row
 // holding a NaN or an infinity gets s = 0 and 1/s = NaN, so its outputs are
 // NaN as the f32 arithmetic would make them.
 template <class Val>
-__device__ __forceinline__ void prep_row(Val val, int k, __half *o, float *inv) {
+__device__ __forceinline__ void prep_row(Val val, int k, __half *o, float *inv, __half *o_lo = nullptr) {
     float mx = 0.f;
     bool fin = true;
     for (int i = threadIdx.x; i < k; i += kPrepThreads) {
@@ -46,7 +50,16 @@ __device__ __forceinline__ void prep_row(Val val, int k, __half *o, float *inv) 
     // the GEMM may start its weight copies now; it reads these rows only
     // after griddepcontrol.wait, i.e. after this grid has completed
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
-    for (int i = threadIdx.x; i < k; i += kPrepThreads) o[i] = __float2half_rn(val(i) * s);
+    if (o_lo) {
+        for (int i = threadIdx.x; i < k; i += kPrepThreads) {
+            const float v = val(i) * s;
+            const __half hi = __float2half_rn(v);
+            o[i] = hi;
+            o_lo[i] = __float2half_rn(v - __half2float(hi));
+        }
+    } else {
+        for (int i = threadIdx.x; i < k; i += kPrepThreads) o[i] = __float2half_rn(val(i) * s);
+    }
     if (threadIdx.x == 0) *inv = is;
 }
 

@@ -3,15 +3,18 @@ tensor memory) that mm_batched uses for batches of at least
 ctx.prefill_min_tokens tokens.
 
 Bar (the path's 1e-3 max-relative-error contract for final float outputs,
-with fp16 operands and f32 accumulation): over the whole [t_rows, n] output,
+with fp16 weights and f32 accumulation): over the whole [t_rows, n] output,
 max |got - want| / max |want| <= 1e-3, and for every token row the relative
-L2 error ||got - want|| / ||want|| <= 1e-3; checked against the oracle (the
-reference's f32 CPU path) and against a torch fp64 matmul of the bit-exact
-dequantised weights.  One fp16 rounding of each operand gives about 3e-4 rms
-relative error; the per-row max-norm ratio, printed for information, has a
-statistical tail that reaches about 1.1e-3 on narrow outputs (a few hundred
-columns, a thousand rows).  Callers that need the reference's results to
-f32 rounding use prefill_min_tokens = 0 (the integer-exact GEMV path).
+L2 error ||got - want|| / ||want|| <= 1e-3; batches of up to 128 tokens
+(two-term fp16 activations, so only the weights are rounded) also hold the
+per-row max-norm bar max_i |got - want| / max_i |want| <= 1e-3.  Checked
+against the oracle (the reference's f32 CPU path) and against a torch fp64
+matmul of the bit-exact dequantised weights.  Larger batches round the
+activations to fp16 as well (one term): about 3e-4 rms relative error, and
+the per-row max-norm ratio, printed for information, has a statistical tail
+that reaches about 1.1e-3 on narrow outputs (a few hundred columns, a
+thousand rows).  Callers that need the reference's results to f32 rounding
+use prefill_min_tokens = 0 (the integer-exact GEMV path).
 """
 import numpy as np
 import pytest
@@ -42,6 +45,8 @@ def check(got, want, label):
     tensor, l2, row_inf = gemm_errors(got, want)
     print(f"{label}: max-norm rel err {tensor:.3e}, per-row L2 rel err {l2:.3e}, per-row max-norm {row_inf:.3e}")
     assert tensor <= 1e-3 and l2 <= 1e-3
+    if np.asarray(got).shape[0] <= 128:  # two-term activations
+        assert row_inf <= 1e-3
 
 
 def test_prefill_threshold_option(ctx):

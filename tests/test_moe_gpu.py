@@ -9,11 +9,10 @@ Bars:
   in the last bit);
 - exact path (prefill_min_tokens = 0, every expert's rows through the
   decode GEMV): per token max|got - want| / max|want| <= 1e-5;
-- default path (experts with >= 16 rows through the fp16 tensor-core GEMM):
-  max-norm error over the whole output <= 1e-3, and within 2.5e-4 of a model
-  of fp16 operands with exact accumulation (per-token relative L2 errors are
-  printed: tokens whose two experts' outputs cancel have a tail of a few
-  1e-3, which that model reproduces);
+- default path (the grouped tensor-core GEMM: weights rounded to fp16,
+  activations carried as two fp16 terms): max-norm error over the whole
+  output <= 1e-3, and within 2.5e-4 of a model of those operands with exact
+  accumulation (per-token relative L2 errors are printed);
 - experts split into ranges: the ranges' outputs add up to the full output
   bit for bit (top-2).
 """
@@ -90,8 +89,9 @@ def test_ffn_exact_path_matches_oracle(ctx, dt):
 
 def _fp16_operand_model(dt, gate, up, down, x, logits, top_k, d_model, d_ff):
     """The FFN as the tensor-core path computes it: each matmul's activation
-    row scaled by a power of two and rounded to fp16, the dequantised weights
-    rounded to fp16, products accumulated exactly (f64), SwiGLU in f32."""
+    row scaled by a power of two and split into two fp16 terms (the rounding
+    and the rounding of the remainder), the dequantised weights rounded to
+    fp16, products accumulated exactly (f64), SwiGLU in f32."""
     Wg = [O.dequant(b, dt, d_ff * d_model).reshape(d_ff, d_model) for b in gate]
     Wu = [O.dequant(b, dt, d_ff * d_model).reshape(d_ff, d_model) for b in up]
     Wd = [O.dequant(b, dt, d_model * d_ff).reshape(d_model, d_ff) for b in down]
@@ -101,7 +101,10 @@ def _fp16_operand_model(dt, gate, up, down, x, logits, top_k, d_model, d_ff):
         a = np.asarray(a, np.float32)
         e = np.frexp(np.abs(a).max(axis=-1, keepdims=True))[1]
         s = np.ldexp(np.float32(1.0), 14 - e).astype(np.float32)
-        return (a * s).astype(np.float16).astype(np.float64) / s
+        v = a * s
+        hi = v.astype(np.float16)
+        lo = (v - hi.astype(np.float32)).astype(np.float16)
+        return (hi.astype(np.float64) + lo.astype(np.float64)) / s
 
     Wg, Wu, Wd = [h16(w) for w in Wg], [h16(w) for w in Wu], [h16(w) for w in Wd]
     out = np.zeros((x.shape[0], d_model))
@@ -133,10 +136,9 @@ def test_ffn_gemm_path_matches_oracle(ctx, dt):
     print(f"MoE GEMM path dtype {dt}: max-norm {tensor:.3e}; per-token L2 median {np.median(l2):.3e}, "
           f"max {l2.max():.3e}; vs the fp16-operand model {vs_model:.3e}")
     assert tensor <= 1e-3
-    # the tensor-core path is "fp16 operands, exact accumulation" up to f32
-    # accumulation and the last bit of exp inside silu, which can flip the
-    # fp16 rounding of an intermediate (the per-token L2 tail above is that
-    # operand rounding on tokens whose expert outputs cancel)
+    # the tensor-core path is "fp16 weights, two-term activations, exact
+    # accumulation" up to f32 accumulation and the last bit of exp inside
+    # silu, which can flip the rounding of an intermediate
     assert vs_model <= 2.5e-4
 
 

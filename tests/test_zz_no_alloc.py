@@ -131,3 +131,74 @@ def _check_limit(L, R, ctx, w, n, k, stream):
             msg = L.rce_qmm_last_error()
             msg = msg.decode() if isinstance(msg, bytes) else str(msg)
             assert "workspace" in msg and "2047 tokens" in msg, msg
+
+
+def _new_stream():
+    """A CUDA stream created here, so that no earlier call of this library has
+    used its handle (torch.cuda.Stream() recycles a fixed pool)."""
+    import torch
+    from cuda.bindings import runtime as cudart
+
+    err, s = cudart.cudaStreamCreate()
+    assert err == cudart.cudaError_t.cudaSuccess
+    return torch.cuda.ExternalStream(int(s))
+
+
+def test_noalloc_allocates_nothing():
+    # The property the entry point exists for.  On a stream it has never seen,
+    # the regular entry point allocates its GEMM workspace (cudaMalloc); this
+    # one must leave the device's free memory as it was.  A first call warms
+    # up (it loads the module holding the fixed array and looks the array's
+    # address up); the measured call runs on a new stream.
+    import torch
+
+    import rce_b200 as R
+    from rce_b200 import _lib
+
+    L = _lib.lib()
+    ctx = R.default_context(0)
+    n, k, m = 1024, 4096, 130
+    wb, _, _, _, x = refcases.seeded_case(O.GGUF_Q4_K, n, k, m, 61)
+    w = R.QuantWeight.from_owned_bytes(wb, O.GGUF_Q4_K, n, k, ctx=ctx)
+    assert m >= ctx.prefill_min_tokens  # the GEMM route, the one with a workspace
+    xd = torch.from_numpy(x).cuda()
+    out = torch.zeros((m, n), device="cuda:0")
+    want = torch.zeros((m, n), device="cuda:0")
+    assert _noalloc(L, ctx, xd, w, out, torch.cuda.current_stream()) == 0, L.rce_qmm_last_error()
+    torch.cuda.synchronize()
+    fresh = _new_stream()
+    free0 = torch.cuda.mem_get_info()[0]
+    assert _noalloc(L, ctx, xd, w, out, fresh) == 0, L.rce_qmm_last_error()
+    fresh.synchronize()
+    free1 = torch.cuda.mem_get_info()[0]
+    assert free1 == free0, f"device free memory changed by {free0 - free1} bytes"
+    # the check can see an allocation: the regular entry point on another new
+    # stream allocates that stream's workspace
+    other = _new_stream()
+    R.mm_batched_device(xd, w, out=want, stream=other)
+    other.synchronize()
+    assert torch.cuda.mem_get_info()[0] < free1
+    assert torch.equal(out, want)
+
+
+def test_noalloc_gemm_against_oracle():
+    # the GEMM route at 512 tokens checked directly against the oracle (the
+    # reference's f32 CPU path), with the per-row bar of the GEMM tests
+    import torch
+
+    import rce_b200 as R
+    from rce_b200 import _lib
+
+    L = _lib.lib()
+    ctx = R.default_context(0)
+    dt, n, k, m = O.GGUF_Q4_K, 4096, 4096, 512
+    wb, _, _, _, x = refcases.seeded_case(dt, n, k, m, 512)
+    w = R.QuantWeight.from_owned_bytes(wb, dt, n, k, ctx=ctx)
+    xd = torch.from_numpy(x).cuda()
+    out = torch.full((m, n), float("nan"), device="cuda:0")
+    assert _noalloc(L, ctx, xd, w, out, torch.cuda.current_stream()) == 0, L.rce_qmm_last_error()
+    torch.cuda.synchronize()
+    got = out.cpu().numpy().astype(np.float64)
+    want = O.mm_batched(x, m, wb, dt, n, k, nthreads=8).astype(np.float64)
+    err = np.abs(got - want).max(axis=1) / np.abs(want).max(axis=1)
+    assert np.all(np.isfinite(got)) and err.max() <= 1e-3, f"per-row error {err.max():.3e}"
