@@ -160,7 +160,7 @@ int rce_qmm_mm_batched_device_multi(rce_qmm_ctx *ctx, const float *d_a, size_t l
  * rce_qmm_mm_batched_device's bit for bit under the same context settings.
  * Limits: a GEMM batch (prefill_min_tokens tokens or more) needing more than
  * 16 MiB of workspace -- t_rows * n_cols * 2 bytes (twice that for batches of
- * up to 128 tokens, whose activations the GEMM carries as two fp16 terms)
+ * up to 64 tokens, whose activations the GEMM carries as two fp16 terms)
  * rounded up to 256, plus 4 bytes per token; 2047 tokens at n_cols 4096 -- is
  * rejected with RCE_QMM_ERR_INVALID.  Every call on a GPU shares the array, whatever its
  * context or stream, so calls that overlap on the GPU race: order them.  The

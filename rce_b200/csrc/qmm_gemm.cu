@@ -15,9 +15,9 @@
 // tokens, and every expert-grouped launch) carry each activation as two fp16
 // terms, high + low (about 22 significant bits): the low rows sit after the
 // high rows in the activation stage, one MMA of N = high + low rows covers
-// both, and the epilogue adds the two accumulator halves.  At those widths
-// the MMA instruction count is the same as for the high rows alone, and the
-// only rounding left is the weights' (the activations' rounding is what
+// both, and the epilogue adds the two accumulator halves.  Up to 64 tokens
+// (N <= 128) an MMA instruction costs the same as for the high rows alone,
+// and the only rounding left is the weights' (the activations' rounding is what
 // gives the one-term path its error tail on outputs that partly cancel,
 // e.g. an MoE token's weighted sum of two experts).
 //
@@ -58,7 +58,7 @@ constexpr int kBK = 64;                // k-block (one 128-byte swizzle row of f
 constexpr int kBM = 128;               // weight rows per CTA (UMMA M)
 constexpr int kDqWarps = 16;           // dequantiser warps (four threads per weight row)
 constexpr int kWeightWarp = 0;         // TMA bulk copies of the packed weight chunks
-constexpr int kMaxMmaWarps = 1;       // tcgen05.mma issuers (K split between them; see mma_warps)
+constexpr int kMaxMmaWarps = 2;       // tcgen05.mma issuers (K split between them; see mma_warps)
 constexpr int kMmaWarp = kDqWarps + 1;  // the first; also tcgen05.alloc / dealloc
 constexpr int kActWarp = kDqWarps + 1 + kMaxMmaWarps;  // TMA tensor loads of the activation k-blocks
 constexpr int kThreads = 32 * (kActWarp + 1);
@@ -172,11 +172,6 @@ __device__ __forceinline__ unsigned long long f2add(unsigned long long a, unsign
     asm("add.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
     return r;
 }
-__device__ __forceinline__ unsigned long long f2fma(unsigned long long a, unsigned long long b, unsigned long long c) {
-    unsigned long long r;
-    asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(a), "l"(b), "l"(c));
-    return r;
-}
 __device__ __forceinline__ unsigned long long f2mul(unsigned long long a, unsigned long long b) {
     unsigned long long r;
     asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
@@ -187,36 +182,79 @@ __device__ __forceinline__ uint32_t f2_to_h2(unsigned long long v) {
     return pack_h2(__uint_as_float((uint32_t)v), __uint_as_float((uint32_t)(v >> 32)));
 }
 
-// Byte b (0..3) of v under the 2^23 exponent byte: 0x4B0000vv, i.e. the f32
-// 2^23 + v for the byte's value v (one byte permute, no shift or mask).
-template <int B>
-__device__ __forceinline__ uint32_t byte_f32(uint32_t v) {
+// Packed fp16x2 arithmetic, round to nearest even, subnormals kept.
+__device__ __forceinline__ uint32_t h2fma(uint32_t a, uint32_t b, uint32_t c) {
     uint32_t r;
-    asm("prmt.b32 %0, %1, %2, %3;" : "=r"(r) : "r"(v), "r"(0x4B000000u), "r"(0x7540u | B));
+    asm("fma.rn.f16x2 %0, %1, %2, %3;" : "=r"(r) : "r"(a), "r"(b), "r"(c));
     return r;
 }
-// (2^23 + c0, 2^23 + c1) -> fp16x2 of the values (c - bias) * scale + offset:
-// the exact integer c - bias by one subtraction, then the value in one fused
-// rounding (the product is exact, as in the reference's d1 * q - min1, which
-// rounds once at the subtraction), then one rounding to fp16.
-__device__ __forceinline__ uint32_t dq_f32pair(uint32_t f0, uint32_t f1, unsigned long long bias,
-                                               unsigned long long sc, unsigned long long off) {
-    return f2_to_h2(f2fma(f2add((unsigned long long)f0 | ((unsigned long long)f1 << 32), bias), sc, off));
+__device__ __forceinline__ uint32_t h2sub(uint32_t a, uint32_t b) {
+    uint32_t r;
+    asm("sub.rn.f16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
+    return r;
 }
-// An integer 0 .. 2^23 - 1 as f32, exactly, by the exponent bias (an add
-// instead of an integer-to-float conversion).
-__device__ __forceinline__ float u23_f32(uint32_t v) { return __uint_as_float(0x4B000000u | v) - 8388608.f; }
+__device__ __forceinline__ uint32_t h2mul(uint32_t a, uint32_t b) {
+    uint32_t r;
+    asm("mul.rn.f16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
+    return r;
+}
+// Shared-space loads and stores by 32-bit shared address (the dequantiser's
+// pointers pass through a struct; generic accesses would go the long way).
+__device__ __forceinline__ uint4 lds128(uint32_t a) {
+    uint4 v;
+    asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "r"(a));
+    return v;
+}
+__device__ __forceinline__ uint2 lds64(uint32_t a) {
+    uint2 v;
+    asm volatile("ld.shared.v2.u32 {%0,%1}, [%2];" : "=r"(v.x), "=r"(v.y) : "r"(a));
+    return v;
+}
+__device__ __forceinline__ uint32_t lds16(uint32_t a) {
+    unsigned short v;
+    asm volatile("ld.shared.u16 %0, [%1];" : "=h"(v) : "r"(a));
+    return v;
+}
+__device__ __forceinline__ void sts128(uint32_t a, uint32_t x, uint32_t y, uint32_t z, uint32_t w) {
+    asm volatile("st.shared.v4.u32 [%0], {%1,%2,%3,%4};" ::"r"(a), "r"(x), "r"(y), "r"(z), "r"(w) : "memory");
+}
+__device__ __forceinline__ uint32_t h2dup(uint32_t bits16) { return (bits16 & 0xFFFFu) | (bits16 << 16); }
+// Bytes P and P + 1 (P = 0 or 2) of v under the fp16 exponent of 1024: the
+// fp16 pair (1024 + b_P, 1024 + b_{P+1}), exact for bytes up to 1023, in one
+// byte permute.
+template <int P>
+__device__ __forceinline__ uint32_t byte_h2(uint32_t v) {
+    uint32_t r;
+    asm("prmt.b32 %0, %1, %2, %3;" : "=r"(r) : "r"(v), "r"(0x64646464u), "r"(P == 0 ? 0x4140u : 0x4342u));
+    return r;
+}
+// The fp16 pair of a small integer 0 .. 1023 in both halves (exact).
+__device__ __forceinline__ uint32_t small_h2(uint32_t v) { return h2sub(h2dup(0x6400u | v), 0x64006400u); }
 
 // A thread's half of weight row `row` (32 of the 64 values of each k-block),
 // the rows' scales decoded once per chunk.  Values are exact in f32 (as the
 // reference's dequantize_to_f32 computes them) and rounded once to fp16; per
 // k-block one 16-byte load of the codes and, for Q4_K, no header work.
+//
+// Q4_K / Q5_K / Q4_0 / Q8_0 values are built in fp16 arithmetic: one byte
+// permute gives the pair (1024 + code); for the K-quants an exact fp16 FMA
+// gives sc * code (at most 63 * 31 = 1953, so exact in fp16: the product is
+// exact inside the FMA and so is the result) and a second FMA gives
+// d * (sc * code) - fp16(dmin * m), rounded once to fp16; for Q4_0 / Q8_0 an
+// exact subtraction gives code - offset and one multiply d * (code - offset),
+// rounded once (the same fp16 value as rounding the exact f32 product).
+// Against rounding the exact f32 value d * sc * code - dmin * m once, the
+// K-quants add only the rounding of dmin * m to fp16.  Q6_K keeps the f32
+// path ((d * sc) * (code - 32), rounded as the reference rounds it).
 template <int DT>
 struct RowHalf {
-    const uint8_t *ch;  // this row's 16-row tile in the packed chunk
+    uint32_t ch;  // shared address of this row's 16-row tile in the packed chunk
     int row, hf, r16, r, rh;
-    unsigned long long s[4][2], o[4][2];  // Q4_K: [k-block j][sub-block 2j, 2j+1] scale and -offset pairs
+    unsigned long long s[4][2];                   // Q6_K: [k-block j][16-value group] scale pairs (f32x2)
+    uint32_t hs[4][2], hc[4][2], hm[4][2], hd;     // K-quants: fp16 pairs sc, -1024 sc, -(dmin * m); d
 
+    // k-blocks G and G + 2 of the chunk (the ones dequantiser group G fills)
+    template <int G>
     __device__ __forceinline__ void begin(const uint8_t *slot, int row_, int hf_) {
         constexpr int CB = chunk_bytes(DT);
         row = row_;
@@ -225,31 +263,33 @@ struct RowHalf {
         r16 = row & 15;
         r = r16 & 7;
         rh = r16 >> 3;
-        ch = slot + tile * CB;
+        ch = smem_u32(slot) + (uint32_t)(tile * CB);
         if (kquant45(DT)) {
-            const uint4 hd = *reinterpret_cast<const uint4 *>(ch + 2048 + r16 * 16);
-            const float d = h2f(hd.x), dmin = h2f(hd.x >> 16);
+            const uint4 h4 = lds128(ch + 2048 + r16 * 16);
+            hd = h2dup(h4.x);                                // d
+            const uint32_t ndmin = h2dup(h4.x >> 16) ^ 0x80008000u;  // -dmin
 #pragma unroll
-            for (int j = 0; j < 4; j++) {
-                const uint32_t lo = j < 2 ? hd.y : (j == 2 ? hd.z : hd.w);
-                const uint32_t hi = j < 2 ? hd.z : (j == 2 ? hd.w : 0u);
+            for (int j = G; j < 4; j += 2) {
+                const uint32_t lo = j < 2 ? h4.y : (j == 2 ? h4.z : h4.w);
+                const uint32_t hi = j < 2 ? h4.z : (j == 2 ? h4.w : 0u);
                 const uint32_t sh = j == 0 ? 0u : (j == 1 ? 24u : (j == 2 ? 16u : 8u));
                 const uint32_t f = __funnelshift_r(lo, hi, sh) & 0xFFFFFFu;
-                const float d1 = d * u23_f32(f & 63u), m1 = dmin * u23_f32((f >> 6) & 63u);
-                const float d2 = d * u23_f32((f >> 12) & 63u), m2 = dmin * u23_f32((f >> 18) & 63u);
-                s[j][0] = f2pack(d1, d1);
-                o[j][0] = f2pack(-m1, -m1);
-                s[j][1] = f2pack(d2, d2);
-                o[j][1] = f2pack(-m2, -m2);
+#pragma unroll
+                for (int h = 0; h < 2; h++) {
+                    const uint32_t sc = small_h2((f >> (12 * h)) & 63u), m = small_h2((f >> (12 * h + 6)) & 63u);
+                    hs[j][h] = sc;
+                    hc[j][h] = h2mul(sc, 0xE400E400u);  // -1024 * sc, exact
+                    hm[j][h] = h2mul(ndmin, m);          // -(dmin * m), rounded once to fp16
+                }
             }
         } else if (DT == GGUF_Q6_K) {
             // k-block j, 16-value group k2 of this half: scale 4 j + 2 hf + k2,
             // d * sc exact in f32 (11 x 8 bits)
-            const float d = h2f(*reinterpret_cast<const uint16_t *>(ch + kQ6D + 2 * r16));
-            const uint4 sv = *reinterpret_cast<const uint4 *>(ch + kQ6Sc + r16 * 16);
+            const float d = h2f(lds16(ch + kQ6D + 2 * r16));
+            const uint4 sv = lds128(ch + kQ6Sc + r16 * 16);
             const uint32_t sw[4] = {sv.x, sv.y, sv.z, sv.w};
 #pragma unroll
-            for (int j = 0; j < 4; j++)
+            for (int j = G; j < 4; j += 2)
 #pragma unroll
                 for (int k2 = 0; k2 < 2; k2++) {
                     const int i = 4 * j + 2 * hf + k2;  // hf is 0 or 1: the word is sw[j]
@@ -259,18 +299,24 @@ struct RowHalf {
         }
     }
 
-    // k-block J of the chunk into row `row` of A (K-major, 128-byte swizzle)
+    // K-quant value pair from the fp16 pair (1024 + code): sc * code exactly,
+    // then d * (sc * code) - dmin * m with one rounding (sub-block h of
+    // k-block j)
+    __device__ __forceinline__ uint32_t kq_pair(uint32_t c1024, int j, int h) const {
+        return h2fma(h2fma(c1024, hs[j][h], hc[j][h]), hd, hm[j][h]);
+    }
+
+    // k-block J of the chunk: this thread's 32 fp16 values (h) and the four
+    // 16-byte chunks of its A-tile row they fill (cc)
     template <int J>
-    __device__ __forceinline__ void kblock(uint8_t *a_tile) const {
+    __device__ __forceinline__ void compute(uint32_t (&h)[16], int (&cc)[4]) const {
         const int lane = 4 * r + J;
-        uint32_t h[16];  // 32 fp16 values
-        int cc[4];       // the four 16-byte A chunks they fill
         if (DT == GGUF_Q6_K) {
             // columns 32 hf .. 32 hf + 31 of the k-block: 16 lo-plane bytes
             // (two codes each) and 8 hi-plane bytes (four each); value =
             // (d * sc) * (code - 32), one rounding as in dequant_q6_k, then fp16
-            const uint4 lq = *reinterpret_cast<const uint4 *>(ch + r16 * 128 + 32 * J + 16 * hf);
-            const uint2 hq = *reinterpret_cast<const uint2 *>(ch + kQ6Hi + r16 * 64 + 16 * J + 8 * hf);
+            const uint4 lq = lds128(ch + r16 * 128 + 32 * J + 16 * hf);
+            const uint2 hq = lds64(ch + kQ6Hi + r16 * 64 + 16 * J + 8 * hf);
             const uint32_t lw[4] = {lq.x, lq.y, lq.z, lq.w};
             const unsigned long long bias = f2pack(-8388640.f, -8388640.f);  // 2^23 + 32
 #pragma unroll
@@ -294,11 +340,10 @@ struct RowHalf {
         } else if (DT == GGUF_Q5_K) {
             // Q4_K's nibbles plus the fifth bit of value l = 16 hf + 8 qq + b
             // at bit 8 (l & 3) + (l >> 2) of Y0 (low nibbles) / Y1 (high)
-            const uint4 q = *reinterpret_cast<const uint4 *>(ch + ((2 * rh + hf) * 32 + lane) * 16);
-            const uint2 y = *reinterpret_cast<const uint2 *>(ch + kQ5Hi + lane * 16 + 8 * rh);
+            const uint4 q = lds128(ch + ((2 * rh + hf) * 32 + lane) * 16);
+            const uint2 y = lds64(ch + kQ5Hi + lane * 16 + 8 * rh);
             const uint32_t y0 = y.x >> (4 * hf), y1 = y.y >> (4 * hf);
             const uint32_t w[4] = {q.x, q.y, q.z, q.w};
-            const unsigned long long bias = f2pack(-8388608.f, -8388608.f);
 #pragma unroll
             for (int qq = 0; qq < 2; qq++)
 #pragma unroll
@@ -309,10 +354,10 @@ struct RowHalf {
                     const uint32_t wd = w[2 * qq + wi];
                     const uint32_t lo = (wd & 0x0F0F0F0Fu) | (((y0 >> sh) & 0x01010101u) << 4);
                     const uint32_t hi = ((wd >> 4) & 0x0F0F0F0Fu) | (((y1 >> sh) & 0x01010101u) << 4);
-                    h[8 * qq + 2 * wi] = dq_f32pair(byte_f32<0>(lo), byte_f32<1>(lo), bias, s[J][0], o[J][0]);
-                    h[8 * qq + 2 * wi + 1] = dq_f32pair(byte_f32<2>(lo), byte_f32<3>(lo), bias, s[J][0], o[J][0]);
-                    h[8 * qq + 4 + 2 * wi] = dq_f32pair(byte_f32<0>(hi), byte_f32<1>(hi), bias, s[J][1], o[J][1]);
-                    h[8 * qq + 5 + 2 * wi] = dq_f32pair(byte_f32<2>(hi), byte_f32<3>(hi), bias, s[J][1], o[J][1]);
+                    h[8 * qq + 2 * wi] = kq_pair(byte_h2<0>(lo), J, 0);
+                    h[8 * qq + 2 * wi + 1] = kq_pair(byte_h2<2>(lo), J, 0);
+                    h[8 * qq + 4 + 2 * wi] = kq_pair(byte_h2<0>(hi), J, 1);
+                    h[8 * qq + 5 + 2 * wi] = kq_pair(byte_h2<2>(hi), J, 1);
                 }
             cc[0] = 2 * hf;
             cc[1] = 4 + 2 * hf;
@@ -321,18 +366,17 @@ struct RowHalf {
         } else if (DT == GGUF_Q4_K) {
             // per word the low and the high nibble planes by two masks, then
             // one byte permute per value
-            const uint4 q = *reinterpret_cast<const uint4 *>(ch + ((2 * rh + hf) * 32 + lane) * 16);
+            const uint4 q = lds128(ch + ((2 * rh + hf) * 32 + lane) * 16);
             const uint32_t w[4] = {q.x, q.y, q.z, q.w};
-            const unsigned long long bias = f2pack(-8388608.f, -8388608.f);
 #pragma unroll
             for (int qq = 0; qq < 2; qq++)  // quarter 2 hf + qq: bytes 8 qq .. 8 qq + 7
 #pragma unroll
                 for (int wi = 0; wi < 2; wi++) {
                     const uint32_t lo = w[2 * qq + wi] & 0x0F0F0F0Fu, hi = (w[2 * qq + wi] >> 4) & 0x0F0F0F0Fu;
-                    h[8 * qq + 2 * wi] = dq_f32pair(byte_f32<0>(lo), byte_f32<1>(lo), bias, s[J][0], o[J][0]);
-                    h[8 * qq + 2 * wi + 1] = dq_f32pair(byte_f32<2>(lo), byte_f32<3>(lo), bias, s[J][0], o[J][0]);
-                    h[8 * qq + 4 + 2 * wi] = dq_f32pair(byte_f32<0>(hi), byte_f32<1>(hi), bias, s[J][1], o[J][1]);
-                    h[8 * qq + 5 + 2 * wi] = dq_f32pair(byte_f32<2>(hi), byte_f32<3>(hi), bias, s[J][1], o[J][1]);
+                    h[8 * qq + 2 * wi] = kq_pair(byte_h2<0>(lo), J, 0);
+                    h[8 * qq + 2 * wi + 1] = kq_pair(byte_h2<2>(lo), J, 0);
+                    h[8 * qq + 4 + 2 * wi] = kq_pair(byte_h2<0>(hi), J, 1);
+                    h[8 * qq + 5 + 2 * wi] = kq_pair(byte_h2<2>(hi), J, 1);
                 }
             cc[0] = 2 * hf;
             cc[1] = 4 + 2 * hf;
@@ -342,45 +386,46 @@ struct RowHalf {
 #pragma unroll
             for (int qq = 0; qq < 2; qq++) {
                 const int qr = 2 * hf + qq;
-                const uint2 sc = *reinterpret_cast<const uint2 *>(ch + quant_bytes(DT) + lane * 8);
+                const uint2 sc = lds64(ch + quant_bytes(DT) + lane * 8);
                 const uint32_t sw = rh ? sc.y : sc.x;
-                const float dd = h2f(sw >> (16 * hf));
-                const unsigned long long zero = f2pack(0.f, 0.f), sd = f2pack(dd, dd);
+                const uint32_t d2 = h2dup(sw >> (16 * hf));  // the block's fp16 d in both halves
                 if (DT == GGUF_Q4_0) {
-                    const unsigned long long bias = f2pack(-8388616.f, -8388616.f);  // 2^23 + 8
-                    const uint2 q =
-                        *reinterpret_cast<const uint2 *>(ch + ((2 * rh + hf) * 32 + lane) * 16 + 8 * (qr & 1));
+                    constexpr uint32_t kOff = 0x64086408u;  // (1032, 1032): 1024 + the offset 8
+                    const uint2 q = lds64(ch + ((2 * rh + hf) * 32 + lane) * 16 + 8 * (qr & 1));
                     const uint32_t w[2] = {q.x, q.y};
 #pragma unroll
                     for (int wi = 0; wi < 2; wi++) {
                         const uint32_t lo = w[wi] & 0x0F0F0F0Fu, hi = (w[wi] >> 4) & 0x0F0F0F0Fu;
-                        h[8 * qq + 2 * wi] = dq_f32pair(byte_f32<0>(lo), byte_f32<1>(lo), bias, sd, zero);
-                        h[8 * qq + 2 * wi + 1] = dq_f32pair(byte_f32<2>(lo), byte_f32<3>(lo), bias, sd, zero);
-                        h[8 * qq + 4 + 2 * wi] = dq_f32pair(byte_f32<0>(hi), byte_f32<1>(hi), bias, sd, zero);
-                        h[8 * qq + 5 + 2 * wi] = dq_f32pair(byte_f32<2>(hi), byte_f32<3>(hi), bias, sd, zero);
+                        h[8 * qq + 2 * wi] = h2mul(h2sub(byte_h2<0>(lo), kOff), d2);
+                        h[8 * qq + 2 * wi + 1] = h2mul(h2sub(byte_h2<2>(lo), kOff), d2);
+                        h[8 * qq + 4 + 2 * wi] = h2mul(h2sub(byte_h2<0>(hi), kOff), d2);
+                        h[8 * qq + 5 + 2 * wi] = h2mul(h2sub(byte_h2<2>(hi), kOff), d2);
                     }
                     cc[2 * qq] = 4 * hf + (qr & 1);
                     cc[2 * qq + 1] = cc[2 * qq] + 2;
                 } else {
-                    const unsigned long long bias = f2pack(-8388736.f, -8388736.f);  // 2^23 + 128
-                    const uint4 q = *reinterpret_cast<const uint4 *>(ch + ((4 * rh + qr) * 32 + lane) * 16);
+                    constexpr uint32_t kOff = 0x64806480u;  // (1152, 1152): 1024 + 128
+                    const uint4 q = lds128(ch + ((4 * rh + qr) * 32 + lane) * 16);
                     const uint32_t w[4] = {q.x ^ 0x80808080u, q.y ^ 0x80808080u, q.z ^ 0x80808080u,
                                            q.w ^ 0x80808080u};
 #pragma unroll
                     for (int wi = 0; wi < 4; wi++) {  // byte ^ 0x80 = q + 128
-                        h[8 * qq + 2 * wi] = dq_f32pair(byte_f32<0>(w[wi]), byte_f32<1>(w[wi]), bias, sd, zero);
-                        h[8 * qq + 2 * wi + 1] = dq_f32pair(byte_f32<2>(w[wi]), byte_f32<3>(w[wi]), bias, sd, zero);
+                        h[8 * qq + 2 * wi] = h2mul(h2sub(byte_h2<0>(w[wi]), kOff), d2);
+                        h[8 * qq + 2 * wi + 1] = h2mul(h2sub(byte_h2<2>(w[wi]), kOff), d2);
                     }
                     cc[2 * qq] = 2 * qr;
                     cc[2 * qq + 1] = 2 * qr + 1;
                 }
             }
         }
-        uint8_t *dst = a_tile + (row >> 3) * 1024 + (row & 7) * 128;
+    }
+    // the values into row `row` of the A tile at shared address a (K-major,
+    // 128-byte swizzle)
+    __device__ __forceinline__ void store(uint32_t a, const uint32_t (&h)[16], const int (&cc)[4]) const {
+        const uint32_t dst = a + (uint32_t)((row >> 3) * 1024 + (row & 7) * 128);
 #pragma unroll
         for (int i = 0; i < 4; i++)
-            *reinterpret_cast<uint4 *>(dst + ((cc[i] ^ (row & 7)) * 16)) =
-                make_uint4(h[4 * i], h[4 * i + 1], h[4 * i + 2], h[4 * i + 3]);
+            sts128(dst + (uint32_t)((cc[i] ^ (row & 7)) * 16), h[4 * i], h[4 * i + 1], h[4 * i + 2], h[4 * i + 3]);
     }
 };
 
@@ -390,7 +435,7 @@ struct GemmSmem {
     int a_stages, b_stages, pslots;
 };
 
-constexpr int kMaxA = 8, kMaxB = 4, kMaxP = 4;  // ring depth limits (barrier slots)
+constexpr int kMaxA = 8, kMaxB = 8, kMaxP = 4;  // ring depth limits (barrier slots)
 
 // Token tiles up to this width carry two-term activations (N = 2 bn <= 256).
 constexpr int kTwoTermMaxTile = 128;
@@ -402,7 +447,11 @@ __host__ __device__ inline GemmSmem gemm_smem(int dt, int bn, int terms) {
     constexpr size_t kLimit = 227 * 1024;  // dynamic shared memory per CTA (opt-in)
     GemmSmem L;
     const int brows = terms * bn;  // activation rows per stage
-    L.b_stages = brows > 256 ? 2 : (brows > 128 ? 3 : kMaxB);
+    // at least 2-4 stages, and up to kMaxB of them within 32 KB: at small
+    // token tiles a stage is consumed faster than an L2 round trip
+    L.b_stages = brows > 256 ? 2 : (brows > 128 ? 3 : 4);
+    const int by_bytes = (int)((32 * 1024) / (brows * kBK * 2));
+    if (by_bytes > L.b_stages) L.b_stages = by_bytes < kMaxB ? by_bytes : kMaxB;
     const size_t a_stage = (size_t)kBM * kBK * 2;
     const size_t b_bytes = (size_t)L.b_stages * brows * kBK * 2;
     const size_t slot = (size_t)8 * chunk_bytes(dt);
@@ -416,6 +465,12 @@ __host__ __device__ inline GemmSmem gemm_smem(int dt, int bn, int terms) {
         L.pslots++;
         avail -= slot;
     }
+    // an even number of A stages: k-block kb uses stage kb % NA, so with NA
+    // even each stage only ever holds k-blocks of one dequantiser group, which
+    // waits for the stage's previous use before refilling it (a stage shared
+    // by the two groups could be refilled two phases ahead of its consumer,
+    // which a parity wait cannot tell from one phase behind)
+    na &= ~1;
     L.a_stages = na < 2 ? 2 : na;
     size_t o = 0;
     L.a = o;  // 1024-aligned stages
@@ -438,17 +493,93 @@ __host__ __device__ inline uint32_t tmem_cols(int bn) {
 }
 
 // MMA issuer warps for token-tile width bn: k-blocks are dealt round-robin
-// to this many warps, each with its own accumulator (bn columns of tensor
-// memory each, 512 in all), and the epilogue adds them.  One issuer keeps
-// up with the rest of the pipeline at every bn measured (a second to fourth
-// issuer changed nothing at 16-128 tokens), so the split is kept at one.
-__host__ __device__ inline int mma_warps(int bn) { return (void)bn, 1; }
+// to this many warps, each with its own accumulator (terms * bn columns of
+// tensor memory each, 512 in all), and the epilogue adds them.  A thread
+// issues a tcgen05.mma about every 60-95 cycles whatever N, while the tensor
+// pipe takes one M = 128, K = 16 instruction every ~40 cycles at N <= 32
+// (~48 at N = 64) when two threads issue (no faster with four): at small
+// token tiles one issuer would bound the k-block rate.
+__host__ __device__ inline int mma_warps(int bn, int terms) {
+    const int by_tmem = 512 / (int)tmem_cols(terms * bn);
+    return by_tmem < kMaxMmaWarps ? by_tmem : kMaxMmaWarps;
+}
 
 // One dequantiser group's loop (group G takes k-blocks j = G and G + 2 of
-// every chunk); returns false if a bounded wait expired.
+// every chunk): per chunk both k-blocks' values are computed before their A
+// stages are awaited, then stored with one proxy fence and arrival; needs at
+// least 4 A stages (the two k-blocks in distinct stages).  Returns false if a
+// bounded wait expired.
 template <int DT, int G>
-__device__ __forceinline__ bool dequant_group(const GemmArgs &p, uint8_t *pk, uint8_t *a_st, uint32_t bar0, int row,
-                                              int hf, int ntiles, int nchunks, int NP, int NA, int lane) {
+__device__ __forceinline__ bool dequant_group_pairs(const GemmArgs &p, uint8_t *pk, uint8_t *a_st, uint32_t bar0,
+                                                    int row, int hf, int ntiles, int nchunks, int NP, int NA,
+                                                    int lane) {
+    constexpr int CB = chunk_bytes(DT);
+    auto PF = [&](int s) { return bar0 + 8 * (0 + s); };
+    auto PE = [&](int s) { return bar0 + 8 * (kMaxP + s); };
+    auto AF = [&](int s) { return bar0 + 8 * (2 * kMaxP + s); };
+    auto AE = [&](int s) { return bar0 + 8 * (2 * kMaxP + kMaxA + s); };
+    int s = 0, st = G;  // packed slot and A stage (of k-block 4 c + G), with their phases
+    uint32_t sph = 0, aph = 0;
+    const bool live = row < ntiles * 16;
+    const uint32_t a0 = smem_u32(a_st);
+    for (int c = 0; c < nchunks; c++) {
+        if (!mbar_wait(PF(s), sph)) return false;
+        uint32_t h0[16], h1[16];
+        int c0[4], c1[4];
+        RowHalf<DT> rw;
+        if (live) {
+            rw.template begin<G>(pk + (size_t)s * 8 * CB, row, hf);
+            rw.template compute<G>(h0, c0);
+            rw.template compute<G + 2>(h1, c1);
+        }
+        // the stage of k-block 4 c + G + 2, two stages on
+        int st1 = st + 2;
+        uint32_t aph1 = aph;
+        if (st1 >= NA) {
+            st1 -= NA;
+            aph1 ^= 1;
+        }
+        const int kb = 4 * c + G;
+        if (kb >= NA && !mbar_wait(AE(st), aph ^ 1)) return false;
+        if (kb + 2 >= NA && !mbar_wait(AE(st1), aph1 ^ 1)) return false;
+        const uint32_t t0 = a0 + (uint32_t)(st * kBM * kBK * 2), t1 = a0 + (uint32_t)(st1 * kBM * kBK * 2);
+        if (live) {
+            rw.store(t0, h0, c0);
+            rw.store(t1, h1, c1);
+        } else {  // rows past the weight: zeros
+            const uint32_t o = (uint32_t)((row >> 3) * 1024 + (row & 7) * 128 + 64 * hf);
+#pragma unroll
+            for (int q = 0; q < 4; q++) {
+                sts128(t0 + o + 16 * q, 0u, 0u, 0u, 0u);
+                sts128(t1 + o + 16 * q, 0u, 0u, 0u, 0u);
+            }
+        }
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // generic writes -> tensor-core reads
+        __syncwarp();
+        if (lane == 0) {  // one arrival per warp and stage; this group is done with the chunk
+            mbar_arrive(AF(st));
+            mbar_arrive(AF(st1));
+            mbar_arrive(PE(s));
+        }
+        st = st1 + 2;
+        aph = aph1;
+        if (st >= NA) {
+            st -= NA;
+            aph ^= 1;
+        }
+        if (++s == NP) {
+            s = 0;
+            sph ^= 1;
+        }
+    }
+    return true;
+}
+
+// The same, one k-block at a time (2 A stages: one per group).
+template <int DT, int G>
+__device__ __forceinline__ bool dequant_group_single(const GemmArgs &p, uint8_t *pk, uint8_t *a_st, uint32_t bar0,
+                                                     int row, int hf, int ntiles, int nchunks, int NP, int NA,
+                                                     int lane) {
     constexpr int CB = chunk_bytes(DT);
     auto PF = [&](int s) { return bar0 + 8 * (0 + s); };
     auto PE = [&](int s) { return bar0 + 8 * (kMaxP + s); };
@@ -457,24 +588,30 @@ __device__ __forceinline__ bool dequant_group(const GemmArgs &p, uint8_t *pk, ui
     int s = 0, st = G;  // packed slot and A stage, with their phases
     uint32_t sph = 0, aph = 0;
     const bool live = row < ntiles * 16;
+    const uint32_t a0 = smem_u32(a_st);
     for (int c = 0; c < nchunks; c++) {
         if (!mbar_wait(PF(s), sph)) return false;
         RowHalf<DT> rw;
-        if (live) rw.begin(pk + (size_t)s * 8 * CB, row, hf);
+        if (live) rw.template begin<G>(pk + (size_t)s * 8 * CB, row, hf);
 #pragma unroll
         for (int jj = 0; jj < 2; jj++) {
-            const int kb = 4 * c + G + 2 * jj;
-            if (kb >= NA && !mbar_wait(AE(st), aph ^ 1)) return false;
-            uint8_t *a_tile = a_st + (size_t)st * kBM * kBK * 2;
+            uint32_t h[16];
+            int cc[4];
             if (live) {
                 if (jj == 0)
-                    rw.template kblock<G>(a_tile);
+                    rw.template compute<G>(h, cc);
                 else
-                    rw.template kblock<G + 2>(a_tile);
+                    rw.template compute<G + 2>(h, cc);
+            }
+            const int kb = 4 * c + G + 2 * jj;
+            if (kb >= NA && !mbar_wait(AE(st), aph ^ 1)) return false;
+            const uint32_t t = a0 + (uint32_t)(st * kBM * kBK * 2);
+            if (live) {
+                rw.store(t, h, cc);
             } else {  // rows past the weight: zeros
-                uint8_t *dst = a_tile + (row >> 3) * 1024 + (row & 7) * 128 + 64 * hf;
+                const uint32_t o = (uint32_t)((row >> 3) * 1024 + (row & 7) * 128 + 64 * hf);
 #pragma unroll
-                for (int q = 0; q < 4; q++) *reinterpret_cast<uint4 *>(dst + 16 * q) = make_uint4(0, 0, 0, 0);
+                for (int q = 0; q < 4; q++) sts128(t + o + 16 * q, 0u, 0u, 0u, 0u);
             }
             asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // generic writes -> tensor-core reads
             __syncwarp();
@@ -494,6 +631,13 @@ __device__ __forceinline__ bool dequant_group(const GemmArgs &p, uint8_t *pk, ui
         }
     }
     return true;
+}
+
+template <int DT, int G>
+__device__ __forceinline__ bool dequant_group(const GemmArgs &p, uint8_t *pk, uint8_t *a_st, uint32_t bar0, int row,
+                                              int hf, int ntiles, int nchunks, int NP, int NA, int lane) {
+    return NA >= 4 ? dequant_group_pairs<DT, G>(p, pk, a_st, bar0, row, hf, ntiles, nchunks, NP, NA, lane)
+                   : dequant_group_single<DT, G>(p, pk, a_st, bar0, row, hf, ntiles, nchunks, NP, NA, lane);
 }
 
 // Expert-grouped launch: blockIdx.z selects entry z, which multiplies
@@ -564,7 +708,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int nmma = terms == 2 ? b_rows + ncol : ncol;
     const int nchunks = p.g.n_chunks;
     const int nkb = nchunks * 4;
-    const int MW = mma_warps(bn);
+    const int MW = min(mma_warps(bn, terms), min(NA, NB));  // an issuer per stage at most
     const uint32_t acc_cols = tmem_cols(terms * bn), ncols = acc_cols * (uint32_t)MW;
 
     if (tid == 0) {

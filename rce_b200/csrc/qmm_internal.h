@@ -111,7 +111,7 @@ cudaError_t launch_gather_unpack_bulk(const float *buf, size_t flag_off, float *
 // gemm_workspace_bytes() bytes (the fp16 activations and per-token scales).
 // Batches of up to kGemmTwoTermMaxTokens tokens carry each activation as two
 // fp16 terms (gemm_terms() == 2: high + low, about 22 significant bits).
-constexpr int kGemmTwoTermMaxTokens = 128;
+constexpr int kGemmTwoTermMaxTokens = 64;
 int gemm_terms(int t_rows);
 size_t gemm_workspace_bytes(const Geometry &g, int t_rows);
 cudaError_t launch_gemm(int dt, const uint8_t *tiles, const Geometry &g, const float *x, size_t ldx, float *y,

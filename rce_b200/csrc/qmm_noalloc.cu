@@ -17,7 +17,7 @@
 //
 // Rules that follow from the one shared array:
 //  - a batch whose workspace exceeds kNoallocScratchBytes (t_rows * n_cols * 2
-//    bytes, twice that for the GEMM's two-term activations at up to 128
+//    bytes, twice that for the GEMM's two-term activations at up to 64
 //    tokens, rounded up to 256, plus 4 bytes per token) is rejected with
 //    RCE_QMM_ERR_INVALID;
 //  - every call on a device uses the same array, whatever its context or

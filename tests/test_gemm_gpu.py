@@ -5,7 +5,7 @@ ctx.prefill_min_tokens tokens.
 Bar (the path's 1e-3 max-relative-error contract for final float outputs,
 with fp16 weights and f32 accumulation): over the whole [t_rows, n] output,
 max |got - want| / max |want| <= 1e-3, and for every token row the relative
-L2 error ||got - want|| / ||want|| <= 1e-3; batches of up to 128 tokens
+L2 error ||got - want|| / ||want|| <= 1e-3; batches of up to 64 tokens
 (two-term fp16 activations, so only the weights are rounded) also hold the
 per-row max-norm bar max_i |got - want| / max_i |want| <= 1e-3.  Checked
 against the oracle (the reference's f32 CPU path) and against a torch fp64
@@ -45,7 +45,7 @@ def check(got, want, label):
     tensor, l2, row_inf = gemm_errors(got, want)
     print(f"{label}: max-norm rel err {tensor:.3e}, per-row L2 rel err {l2:.3e}, per-row max-norm {row_inf:.3e}")
     assert tensor <= 1e-3 and l2 <= 1e-3
-    if np.asarray(got).shape[0] <= 128:  # two-term activations
+    if np.asarray(got).shape[0] <= 64:  # two-term activations
         assert row_inf <= 1e-3
 
 

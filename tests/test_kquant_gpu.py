@@ -14,8 +14,8 @@ Bars:
   exact sum (the reference's own f32 sums do not hold it everywhere at the
   largest shapes); a batch gives, row for row, the bits of one-token calls;
 - tensor-core GEMM (16 tokens and more): the same normwise bar over the whole
-  output, and within 2.5e-4 of a model of fp16 operands with exact
-  accumulation.
+  output, and within 2.5e-4 of a model of its operands with exact
+  accumulation (gemm_operand_model).
 The allocation-free entry point's Q6_K case is in test_zz_no_alloc.py.
 """
 import numpy as np
@@ -76,6 +76,30 @@ def test_decode_gemv_against_oracle(ctx, dt, n, k, m):
     assert ctx.device_error() == 0
 
 
+def gemm_operand_model(dt, w, x, n, k):
+    """The GEMM's operands with exact accumulation: x scaled by a power of two
+    per token and rounded to fp16 (plus the fp16 rounding of the remainder for
+    batches of up to 64 tokens); Q5_K weights d * (sc * q) - fp16(dmin * m)
+    rounded once to fp16, Q6_K weights their exact f32 dequantised values
+    rounded to fp16."""
+    m = x.shape[0]
+    if dt == Q5_K:
+        q, sv, ov = O.unpack_q5_k(w, n, k)
+        sv = np.repeat(sv.astype(np.float64), 32, axis=1)
+        ov = np.repeat(ov.astype(np.float16).astype(np.float64), 32, axis=1)
+        wm = (sv * q - ov).astype(np.float16).astype(np.float64)
+    else:
+        wm = O.dequant(w, dt, n * k).reshape(n, k).astype(np.float16).astype(np.float64)
+    e = np.frexp(np.abs(x).max(axis=1, keepdims=True))[1]
+    s = np.ldexp(np.float32(1.0), 14 - e).astype(np.float32)
+    v = x * s
+    hi = v.astype(np.float16)
+    xm = hi.astype(np.float64)
+    if m <= 64:
+        xm = xm + (v - hi.astype(np.float32)).astype(np.float16).astype(np.float64)
+    return (xm / s) @ wm.T
+
+
 @pytest.mark.parametrize("dt", KQ)
 @pytest.mark.parametrize("n,k,m", [(1024, 4096, 16), (2048, 4096, 128), (1024, 14336, 64), (512, 2048, 300),
                                    (256, 1024, 520)])
@@ -89,13 +113,7 @@ def test_prefill_gemm_against_oracle(ctx, dt, n, k, m):
     want = O.mm_batched(x, m, w, dt, n, k, nthreads=8).reshape(m, n).astype(np.float64)
     scale = np.abs(want).max()
     tensor = np.abs(got - want).max() / scale
-    # fp16 operands (weights rounded once from their exact f32 values, x scaled
-    # by a power of two per token), exact accumulation
-    deq = O.dequant(w, dt, n * k).reshape(n, k).astype(np.float16).astype(np.float64)
-    e = np.frexp(np.abs(x).max(axis=1, keepdims=True))[1]
-    s = np.ldexp(np.float32(1.0), 14 - e).astype(np.float32)
-    xh = (x * s).astype(np.float16).astype(np.float64) / s
-    model = xh @ deq.T
+    model = gemm_operand_model(dt, w, x, n, k)
     vs_model = np.abs(got - model).max() / scale
     print(f"dtype {dt} GEMM {n}x{k} m={m}: max-norm {tensor:.2e}, vs the fp16-operand model {vs_model:.2e}")
     assert tensor <= 1e-3

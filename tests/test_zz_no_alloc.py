@@ -164,11 +164,15 @@ def test_noalloc_allocates_nothing():
     xd = torch.from_numpy(x).cuda()
     out = torch.zeros((m, n), device="cuda:0")
     want = torch.zeros((m, n), device="cuda:0")
+    # a batch whose regular workspace (8 MiB) shows in the free memory
+    xc = torch.randn(1024, k, device="cuda:0")
+    outc = torch.zeros((1024, n), device="cuda:0")
     assert _noalloc(L, ctx, xd, w, out, torch.cuda.current_stream()) == 0, L.rce_qmm_last_error()
     torch.cuda.synchronize()
     fresh = _new_stream()
     free0 = torch.cuda.mem_get_info()[0]
     assert _noalloc(L, ctx, xd, w, out, fresh) == 0, L.rce_qmm_last_error()
+    assert _noalloc(L, ctx, xc, w, outc, fresh) == 0, L.rce_qmm_last_error()
     fresh.synchronize()
     free1 = torch.cuda.mem_get_info()[0]
     assert free1 == free0, f"device free memory changed by {free0 - free1} bytes"
@@ -176,6 +180,7 @@ def test_noalloc_allocates_nothing():
     # stream allocates that stream's workspace
     other = _new_stream()
     R.mm_batched_device(xd, w, out=want, stream=other)
+    R.mm_batched_device(xc, w, out=outc, stream=other)
     other.synchronize()
     assert torch.cuda.mem_get_info()[0] < free1
     assert torch.equal(out, want)
