@@ -264,10 +264,13 @@ def prefill_section(args, rank, world, dev, stream, ctx, pg=None):
         stream.synchronize()
         if world > 1:
             dist.barrier()
+        # two passes per graph: a bulk-gathered output alternates between two
+        # receive buffers per call, so every replay must make an even number
         graph = torch.cuda.CUDAGraph()
         with torch.cuda.graph(graph, stream=stream):
             one()
-        reps = 20
+            one()
+        reps = 10
         with torch.cuda.stream(stream):
             for _ in range(3):
                 graph.replay()
@@ -281,7 +284,7 @@ def prefill_section(args, rank, world, dev, stream, ctx, pg=None):
                 graph.replay()
             e1.record(stream)
         e1.synchronize()
-        ms = e0.elapsed_time(e1) / (reps * len(ws))
+        ms = e0.elapsed_time(e1) / (reps * 2 * len(ws))
         if world > 1:
             t = torch.tensor([ms], device=dev)
             dist.all_reduce(t, op=dist.ReduceOp.MAX)

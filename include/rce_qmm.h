@@ -52,7 +52,8 @@ extern "C" {
 #define RCE_QMM_ERR_UNSUPPORTED 2 /* dtype or shape outside this library */
 #define RCE_QMM_ERR_CUDA 3        /* a CUDA runtime call failed */
 #define RCE_QMM_ERR_NOMEM 4       /* device or host allocation failed */
-#define RCE_QMM_ERR_TIMEOUT 5     /* a bounded wait inside a kernel expired */
+#define RCE_QMM_ERR_TIMEOUT 5     /* a bounded wait inside a kernel expired, or a gathered
+                                   * output's buffer was overwritten by a later call */
 
 /* GGUF dtype tags (rce-ingest-gguf/src/parser.rs:308-338). */
 #define RCE_QMM_GGUF_Q4_0 2
@@ -246,8 +247,13 @@ int rce_qmm_mm_batched_device_multi_gather_bulk(rce_qmm_ctx *ctx, const float *d
                                                 float *const *d_bulks, const size_t *flag_offsets, unsigned epoch,
                                                 const unsigned *d_epoch_base, void *stream);
 /* Wait (bounded) until every other rank's flag in this rank's bulk buffer
- * carries the epoch (or a later one), then copy their rows (columns [0, n)
- * except [own0, own1)) of the [t_rows][ldy] values into d_y. */
+ * carries the epoch, then copy their rows (columns [0, n) except
+ * [own0, own1)) of the [t_rows][ldy] values into d_y.  The values carry no
+ * epoch, so a peer must not write the next call's rows into a bulk buffer
+ * that is still being unpacked: alternate two bulk buffers per output (a
+ * peer may then run one call ahead, not two).  A flag that already carries
+ * a later epoch is reported in the device error word (code 2) and nothing
+ * is copied. */
 int rce_qmm_peer_unpack_bulk(rce_qmm_ctx *ctx, const float *d_bulk, size_t flag_offset, float *d_y, size_t ldy,
                              size_t t_rows, int64_t n, int64_t own0, int64_t own1, int world, int rank, unsigned epoch,
                              const unsigned *d_epoch_base, void *stream);
@@ -278,6 +284,17 @@ int rce_qmm_peer_epoch_advance(rce_qmm_ctx *ctx, unsigned *d_epoch_base, unsigne
 int rce_qmm_moe_route_device(rce_qmm_ctx *ctx, const float *d_logits, size_t ld_logits, size_t t_rows,
                              int n_experts, int top_k, int normalize, int32_t *d_idx, float *d_w, void *stream);
 
+/* moe_router (rce-op-moe/src/lib.rs:35-73) with the router's quantized gate
+ * weight router_w [n_experts x d_model] (n_experts <= 256): per token the
+ * logits router_w . x, computed as mm_batched computes them (the decode
+ * path, per token as mm_1d, below the context's prefill_min_tokens; set it
+ * to 0 for that path at every batch size), into d_logits [t_rows][ld_logits],
+ * then softmax / top_k / renormalise as rce_qmm_moe_route_device.
+ * Asynchronous on `stream`. */
+int rce_qmm_moe_router_device(rce_qmm_ctx *ctx, const float *d_x, size_t ldx, size_t t_rows,
+                              const rce_qmm_weight *router_w, int top_k, int normalize, float *d_logits,
+                              size_t ld_logits, int32_t *d_idx, float *d_w, void *stream);
+
 /* The expert-grouped SwiGLU FFN of moe_ffn_forward
  * (rce-qwen36-moe/src/lib.rs:666-705) with moe_router / moe_combine
  * (rce-op-moe/src/lib.rs:35-110): route every token as
@@ -299,6 +316,18 @@ int rce_qmm_moe_ffn_device(rce_qmm_ctx *ctx, const float *d_x, size_t ldx, size_
                            int expert_begin, int expert_end, const rce_qmm_weight *const *gate,
                            const rce_qmm_weight *const *up, const rce_qmm_weight *const *down, float *d_out,
                            size_t ldo, int32_t *d_idx, float *d_w, void *stream);
+
+/* Host-buffer rce_qmm_moe_ffn_device, synchronous (the MoE FFN call of the
+ * reference's runtimes, rce-qwen36-moe/src/lib.rs:666-705, routed by
+ * moe_router, rce-op-moe/src/lib.rs:35-73): x [t_rows][d_model] and out
+ * [t_rows][d_model] host f32.  The routes come from router_logits
+ * ([t_rows][n_experts] host f32) or, when it is NULL, from the gate weight
+ * router_w as rce_qmm_moe_router_device computes them.  idx_out / w_out
+ * (optional, host, [t_rows][top_k]) receive the routes. */
+int rce_qmm_moe_ffn(rce_qmm_ctx *ctx, const float *x, size_t t_rows, const float *router_logits,
+                    const rce_qmm_weight *router_w, int n_experts, int top_k, int expert_begin, int expert_end,
+                    const rce_qmm_weight *const *gate, const rce_qmm_weight *const *up,
+                    const rce_qmm_weight *const *down, float *out, int32_t *idx_out, float *w_out);
 
 #ifdef __cplusplus
 }

@@ -74,6 +74,8 @@ SIGNATURES = {
     "rce_qmm_moe_route_device": (_int, [_vp, _vp, _sz, _sz, _int, _int, _int, _vp, _vp, _vp]),
     "rce_qmm_moe_ffn_device": (_int, [_vp, _vp, _sz, _sz, _vp, _sz, _int, _int, _int, _int, _vp, _vp, _vp, _vp,
                                        _sz, _vp, _vp, _vp]),
+    "rce_qmm_moe_router_device": (_int, [_vp, _vp, _sz, _sz, _vp, _int, _int, _vp, _sz, _vp, _vp, _vp]),
+    "rce_qmm_moe_ffn": (_int, [_vp, _vp, _sz, _vp, _vp, _int, _int, _int, _int, _vp, _vp, _vp, _vp, _vp, _vp]),
     "rce_qmm_synchronize": (_int, [_vp]),
 }
 

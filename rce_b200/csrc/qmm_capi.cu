@@ -99,6 +99,9 @@ int take_kernel_error(rce_qmm_ctx *ctx) {
     const int code = *reinterpret_cast<volatile int *>(ctx->err_host);
     if (code == 0) return ok();
     *reinterpret_cast<volatile int *>(ctx->err_host) = 0;
+    if (code == rce::kKernelErrOverrun)
+        return fail(RCE_QMM_ERR_TIMEOUT, "a gathered output's bulk buffer held a later call's rows when it was "
+                                         "unpacked (a peer ran more than one call ahead); its results are invalid");
     return fail(RCE_QMM_ERR_TIMEOUT, "a kernel's bounded wait expired (device error code %d); its results are invalid",
                 code);
 }
@@ -846,6 +849,30 @@ int rce_qmm_moe_route_device(rce_qmm_ctx *ctx, const float *d_logits, size_t ld_
     return ok();
 }
 
+int rce_qmm_moe_router_device(rce_qmm_ctx *ctx, const float *d_x, size_t ldx, size_t t_rows,
+                              const rce_qmm_weight *router_w, int top_k, int normalize, float *d_logits,
+                              size_t ld_logits, int32_t *d_idx, float *d_w, void *stream) {
+    if (!ctx) return fail(RCE_QMM_ERR_INVALID, "moe_router_device: null ctx");
+    int rc = check_weight(router_w);
+    if (rc) return rc;
+    if (router_w->ctx != ctx) return fail(RCE_QMM_ERR_INVALID, "moe_router_device: weight of another context");
+    const int64_t n_experts = router_w->g.n_rows;
+    if (n_experts < 1 || n_experts > 256 || top_k < 1 || top_k > n_experts)
+        return fail(RCE_QMM_ERR_INVALID, "moe_router_device: n_experts %lld (1..256), top_k %d (1..n_experts)",
+                    (long long)n_experts, top_k);
+    if (t_rows == 0) return ok();
+    if (!d_x || !d_logits || !d_idx || !d_w || ldx < (size_t)router_w->g.n_cols || ld_logits < (size_t)n_experts ||
+        t_rows > (size_t)INT32_MAX)
+        return fail(RCE_QMM_ERR_INVALID, "moe_router_device: null buffer, ldx < d_model, ld_logits < n_experts or "
+                                         "too many rows");
+    DeviceGuard dg(ctx->device);
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    rc = run_matmul(ctx, router_w, d_x, ldx, t_rows, d_logits, ld_logits, s);
+    if (rc) return rc;
+    CUDA_TRY(rce::launch_moe_route(d_logits, ld_logits, (int)t_rows, (int)n_experts, top_k, normalize, d_idx, d_w, s));
+    return ok();
+}
+
 int rce_qmm_moe_ffn_device(rce_qmm_ctx *ctx, const float *d_x, size_t ldx, size_t t_rows,
                            const float *d_logits, size_t ld_logits, int n_experts, int top_k,
                            int expert_begin, int expert_end, const rce_qmm_weight *const *gate,
@@ -999,6 +1026,57 @@ int rce_qmm_moe_ffn_device(rce_qmm_ctx *ctx, const float *d_x, size_t ldx, size_
         }
     }
     CUDA_TRY(rce::launch_moe_combine(yb, (int)d_model, pos, wt, (int)t_rows, top_k, d_out, ldo, s));
+    return ok();
+}
+
+int rce_qmm_moe_ffn(rce_qmm_ctx *ctx, const float *x, size_t t_rows, const float *router_logits,
+                    const rce_qmm_weight *router_w, int n_experts, int top_k, int expert_begin, int expert_end,
+                    const rce_qmm_weight *const *gate, const rce_qmm_weight *const *up,
+                    const rce_qmm_weight *const *down, float *out, int32_t *idx_out, float *w_out) {
+    if (!ctx) return fail(RCE_QMM_ERR_INVALID, "moe_ffn: null ctx");
+    if (!gate || !up || !down || expert_begin < 0 || expert_begin >= n_experts)
+        return fail(RCE_QMM_ERR_INVALID, "moe_ffn: null weight array or bad expert range");
+    int rc = check_weight(gate[expert_begin]);
+    if (rc) return rc;
+    if (t_rows == 0) return ok();
+    if (!x || !out) return fail(RCE_QMM_ERR_INVALID, "moe_ffn: null buffer");
+    if (!router_logits) {
+        if ((rc = check_weight(router_w))) return rc;
+        if (router_w->g.n_rows != n_experts || router_w->g.n_cols != gate[expert_begin]->g.n_cols)
+            return fail(RCE_QMM_ERR_INVALID, "moe_ffn: router weight is [%lld x %lld], [n_experts x d_model] needed",
+                        (long long)router_w->g.n_rows, (long long)router_w->g.n_cols);
+    }
+    if (top_k < 1 || top_k > n_experts || n_experts > 256)
+        return fail(RCE_QMM_ERR_INVALID, "moe_ffn: n_experts %d (1..256), top_k %d (1..n_experts)", n_experts, top_k);
+    const size_t d_model = (size_t)gate[expert_begin]->g.n_cols;
+    DeviceGuard dg(ctx->device);
+    RceThreadState *ts = nullptr;
+    if ((rc = thread_state(ctx, &ts))) return rc;
+    // device staging: x and logits in d_in; out, weights and indices in d_out
+    const size_t xf = t_rows * d_model, lf = t_rows * (size_t)n_experts, rf = t_rows * (size_t)top_k;
+    const size_t in_f = xf + lf, out_f = xf + 2 * rf;
+    if ((rc = grow_device(&ts->d_in, &ts->d_in_cap, in_f))) return rc;
+    if ((rc = grow_device(&ts->d_out, &ts->d_out_cap, out_f))) return rc;
+    if ((rc = grow_pinned(ts, (in_f > out_f ? in_f : out_f) * sizeof(float)))) return rc;
+    float *d_x = ts->d_in, *d_lg = ts->d_in + xf, *d_y = ts->d_out, *d_w = ts->d_out + xf;
+    int32_t *d_idx = reinterpret_cast<int32_t *>(ts->d_out + xf + rf);
+    float *h = static_cast<float *>(ts->h_pin);
+    std::memcpy(h, x, xf * sizeof(float));
+    if (router_logits) std::memcpy(h + xf, router_logits, lf * sizeof(float));
+    CUDA_TRY(cudaMemcpyAsync(d_x, h, (router_logits ? in_f : xf) * sizeof(float), cudaMemcpyHostToDevice, ts->stream));
+    if (!router_logits) {
+        rc = run_matmul(ctx, router_w, d_x, d_model, t_rows, d_lg, (size_t)n_experts, ts->stream);
+        if (rc) return rc;
+    }
+    rc = rce_qmm_moe_ffn_device(ctx, d_x, d_model, t_rows, d_lg, (size_t)n_experts, n_experts, top_k, expert_begin,
+                                expert_end, gate, up, down, d_y, d_model, d_idx, d_w, ts->stream);
+    if (rc) return rc;
+    CUDA_TRY(cudaMemcpyAsync(h, d_y, out_f * sizeof(float), cudaMemcpyDeviceToHost, ts->stream));
+    CUDA_TRY(cudaStreamSynchronize(ts->stream));
+    if ((rc = take_kernel_error(ctx))) return rc;
+    std::memcpy(out, h, xf * sizeof(float));
+    if (w_out) std::memcpy(w_out, h + xf, rf * sizeof(float));
+    if (idx_out) std::memcpy(idx_out, h + xf + rf, rf * sizeof(int32_t));
     return ok();
 }
 

@@ -95,8 +95,11 @@ __global__ void push_flags_kernel(BulkPeers bp, size_t flag_off, int world, int 
     }
 }
 
-// Wait (bounded) until every other rank's flag carries this epoch or a later
-// one, then copy their rows out of the local bulk buffer.
+// Wait (bounded) until every other rank's flag carries this epoch, then copy
+// their rows out of the local bulk buffer.  A flag that already carries a
+// later epoch means a later call has overwritten the rows: that is reported
+// in the error word (kKernelErrOverrun) and nothing is copied, never a mix
+// of two calls' rows.
 __global__ void unpack_bulk_kernel(const float *buf, size_t flag_off, float *y, int t_rows, int64_t n, size_t ldy,
                                    int64_t own0, int64_t own1, int world, int rank, unsigned epoch_rel,
                                    const unsigned *epoch_base, int *err) {
@@ -120,6 +123,10 @@ __global__ void unpack_bulk_kernel(const float *buf, size_t flag_off, float *y, 
                 break;
             }
             asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(f) : "memory");
+        }
+        if (!failed && v != e) {
+            failed = 1;
+            *reinterpret_cast<volatile int *>(err) = kKernelErrOverrun;
         }
     }
     __syncthreads();

@@ -156,5 +156,8 @@ cudaError_t launch_moe_combine(const float *y, int d_model, const int32_t *pos, 
 
 // Kernel error codes written to the context's error word.
 constexpr int kKernelErrWaitTimeout = 1;
+// A bulk receive buffer already held a later call's rows when its unpack
+// looked (a peer ran more than one call ahead into the same buffer).
+constexpr int kKernelErrOverrun = 2;
 
 }  // namespace rce

@@ -44,10 +44,12 @@ class _Output:
 
     def __init__(self, y, ll, t_rows, n_rows, bulk=None, flag_off=0):
         self.y, self.ll, self.t_rows, self.n_rows = y, ll, t_rows, n_rows
-        self.bulk, self.flag_off = bulk, flag_off
+        self.bulk, self.flag_off = bulk, flag_off  # bulk: two buffer sets, alternated per bulk call
         self.own0 = self.own1 = 0
         self.epoch = None
         self.bulk_mode = False
+        self.bulk_calls = 0  # bulk calls made into this output
+        self.bulk_sel = 0    # the buffer set of the latest one
 
 
 class PeerGroup:
@@ -57,12 +59,29 @@ class PeerGroup:
     (decode-sized calls), and for outputs of BULK_MIN_TOKENS or more tokens
     a bulk buffer of plain values plus one release flag per peer (prefill
     calls; half the NVLink bytes).  `exchange` is a callable (obj -> list of
-    every rank's obj, in rank order), e.g. torch_exchange()."""
+    every rank's obj, in rank order), e.g. torch_exchange().
 
-    def __init__(self, ctx: Context, world: int, rank: int, exchange):
+    Run-ahead: bulk values carry no epoch, so consecutive bulk calls into an
+    output alternate between two bulk buffers: a rank may start the next
+    call into an output while its peers still unpack the previous one, but
+    not the one after (every rank gathers an output before its second next
+    call into it, as the step pattern mm... then gather... does).  A buffer
+    overwritten by a later call before its unpack is reported as an error,
+    never mixed.  Word-mode outputs carry the epoch in every word and a
+    gather accepts a later call's words, which replace the earlier ones: a
+    rank must not start the next call into a word-mode output before every
+    peer has gathered the previous one whenever the values differ (a
+    barrier between steps, or each output's gather before its next call).
+    In a CUDA graph, capture an even number of bulk calls per output, so
+    that every replay alternates the same way."""
+
+    def __init__(self, ctx: Context, world: int, rank: int, exchange, transport=None):
         if not 2 <= world <= 8:
             raise ValueError("world must be 2..8")
         self.ctx, self.world, self.rank, self._exchange = ctx, world, rank, exchange
+        # the library entry points, device tensors and stream handles this
+        # group uses (librce_qmm.so and CUDA unless a test supplies another)
+        self._t = transport if transport is not None else _LibTransport()
         self.epoch = 0
         self._own: List[int] = []          # own allocations (device pointers)
         self._opened: List[int] = []       # peers' allocations mapped here
@@ -72,11 +91,12 @@ class PeerGroup:
         # every replay
         self._base = None
         self._rel = None
+        self._step_calls = 0
 
     def _shared(self, nbytes: int) -> List[int]:
         ptr = ctypes.c_void_p()
         handle = ctypes.create_string_buffer(64)
-        check(lib().rce_qmm_peer_alloc(self.ctx.handle, nbytes, ctypes.byref(ptr), handle))
+        check(self._t.rce_qmm_peer_alloc(self.ctx.handle, nbytes, ctypes.byref(ptr), handle))
         self._own.append(ptr.value)
         handles = self._exchange(handle.raw)
         ptrs = []
@@ -85,7 +105,7 @@ class PeerGroup:
                 ptrs.append(ptr.value)
                 continue
             p = ctypes.c_void_p()
-            check(lib().rce_qmm_peer_open(self.ctx.handle, ctypes.create_string_buffer(h, 64), ctypes.byref(p)))
+            check(self._t.rce_qmm_peer_open(self.ctx.handle, ctypes.create_string_buffer(h, 64), ctypes.byref(p)))
             self._opened.append(p.value)
             ptrs.append(p.value)
         return ptrs
@@ -100,8 +120,8 @@ class PeerGroup:
             bulk, flag_off = None, 0
             if t_rows >= BULK_MIN_TOKENS:
                 flag_off = (4 * t_rows * n_rows + 63) // 64 * 64
-                bulk = (ctypes.c_void_p * self.world)(*self._shared(flag_off + 64))
-            y = torch.zeros((t_rows, n_rows), dtype=torch.float32, device=f"cuda:{self.ctx.device}")
+                bulk = [(ctypes.c_void_p * self.world)(*self._shared(flag_off + 64)) for _ in range(2)]
+            y = self._t.zeros((t_rows, n_rows), torch.float32, self.ctx.device)
             self.outputs[name] = _Output(y, (ctypes.c_void_p * self.world)(*ll), t_rows, n_rows, bulk, flag_off)
         return self.outputs[name].y
 
@@ -152,20 +172,25 @@ class PeerGroup:
         ys = (ctypes.c_void_p * n)(*[o.y.data_ptr() for o in outs])
         lds = (ctypes.c_size_t * n)(*[o.n_rows for o in outs])
         bulk = self._bulk_call(x, outs)
-        s = _stream_handle(stream, x.device)
+        s = self._t.stream(stream, x.device)
         if bulk:
-            bufs = (ctypes.c_void_p * (n * self.world))(*[o.bulk[r] for o in outs for r in range(self.world)])
+            sel = [o.bulk_calls % 2 for o in outs]
+            bufs = (ctypes.c_void_p * (n * self.world))(*[o.bulk[s_][r] for o, s_ in zip(outs, sel)
+                                                          for r in range(self.world)])
             flags = (ctypes.c_size_t * n)(*[o.flag_off for o in outs])
-            check(lib().rce_qmm_mm_batched_device_multi_gather_bulk(
+            check(self._t.rce_qmm_mm_batched_device_multi_gather_bulk(
                 self.ctx.handle, ctypes.c_void_p(x.data_ptr()), x.stride(0), x.shape[0], hs, n, self.world,
                 self.rank, offs, ys, lds, bufs, flags, epoch, base, s))
         else:
             lls = (ctypes.c_void_p * (n * self.world))(*[o.ll[r] for o in outs for r in range(self.world)])
-            check(lib().rce_qmm_mm_batched_device_multi_gather(
+            check(self._t.rce_qmm_mm_batched_device_multi_gather(
                 self.ctx.handle, ctypes.c_void_p(x.data_ptr()), x.stride(0), x.shape[0], hs, n, self.world,
                 self.rank, offs, ys, lds, lls, epoch, base, s))
-        for o, w, r0 in zip(outs, weights, row_offsets):
+        for i, (o, w, r0) in enumerate(zip(outs, weights, row_offsets)):
             o.own0, o.own1, o.epoch, o.bulk_mode = r0, r0 + w.n_rows, epoch, bulk
+            if bulk:
+                o.bulk_sel = sel[i]
+                o.bulk_calls += 1
         return epoch
 
     def gather(self, name: str, epoch: Optional[int] = None, t_rows: Optional[int] = None, stream=None):
@@ -176,13 +201,14 @@ class PeerGroup:
         epoch = o.epoch if epoch is None else epoch
         base = ctypes.c_void_p(self._base.data_ptr()) if self._rel is not None else None
         rows = o.t_rows if t_rows is None else t_rows
-        s = _stream_handle(stream, o.y.device)
+        s = self._t.stream(stream, o.y.device)
         if o.bulk_mode:
-            check(lib().rce_qmm_peer_unpack_bulk(self.ctx.handle, ctypes.c_void_p(o.bulk[self.rank]), o.flag_off,
+            check(self._t.rce_qmm_peer_unpack_bulk(self.ctx.handle, ctypes.c_void_p(o.bulk[o.bulk_sel][self.rank]),
+                                                 o.flag_off,
                                                  ctypes.c_void_p(o.y.data_ptr()), o.n_rows, rows, o.n_rows,
                                                  int(o.own0), int(o.own1), self.world, self.rank, int(epoch), base, s))
         else:
-            check(lib().rce_qmm_peer_unpack(self.ctx.handle, ctypes.c_void_p(o.ll[self.rank]),
+            check(self._t.rce_qmm_peer_unpack(self.ctx.handle, ctypes.c_void_p(o.ll[self.rank]),
                                             ctypes.c_void_p(o.y.data_ptr()), o.n_rows, rows, o.n_rows, int(o.own0),
                                             int(o.own1), int(epoch), base, s))
         return o.y
@@ -191,25 +217,53 @@ class PeerGroup:
         """Start a step of at most `calls` mm calls whose epochs are relative
         to a device counter advanced here by `calls` -- capture begin_step,
         the calls and the gathers in one CUDA graph and every replay uses
-        new epochs.  Every rank must use the same `calls` and call sequence."""
+        new epochs.  Every rank must use the same `calls` and call sequence.
+        The counter starts at (and, coming from absolute epochs, is raised
+        to) the last absolute epoch, so epochs only grow across both modes:
+        make the first begin_step after absolute calls outside a capture."""
         import torch
 
         if self._base is None:
-            self._base = torch.zeros(1, dtype=torch.int32, device=f"cuda:{self.ctx.device}")
+            self._base = self._t.zeros((1,), torch.int32, self.ctx.device)
+            self._base.fill_(self.epoch)
+        elif self._rel is None and self.epoch > 0:
+            self._base.clamp_(min=self.epoch)
         self._rel = 0
-        check(lib().rce_qmm_peer_epoch_advance(self.ctx.handle, ctypes.c_void_p(self._base.data_ptr()), int(calls),
-                                               _stream_handle(stream, self._base.device)))
+        self._step_calls = int(calls)
+        check(self._t.rce_qmm_peer_epoch_advance(self.ctx.handle, ctypes.c_void_p(self._base.data_ptr()), int(calls),
+                                               self._t.stream(stream, self._base.device)))
 
     def end_step(self) -> None:
-        """Leave step mode: later calls use absolute epochs again."""
+        """Leave step mode: later calls use absolute epochs again, above
+        every epoch the steps used (the counter is read back: this
+        synchronises with the device, so call it outside a capture)."""
+        if self._rel is not None and self._base is not None:
+            self.epoch = max(self.epoch, int(self._base.cpu()[0]) + self._step_calls) & 0xFFFFFFFF
         self._rel = None
 
     def close(self) -> None:
         for p in self._opened:
-            lib().rce_qmm_peer_close(self.ctx.handle, ctypes.c_void_p(p))
+            self._t.rce_qmm_peer_close(self.ctx.handle, ctypes.c_void_p(p))
         for p in self._own:
-            lib().rce_qmm_peer_free(self.ctx.handle, ctypes.c_void_p(p))
+            self._t.rce_qmm_peer_free(self.ctx.handle, ctypes.c_void_p(p))
         self._opened, self._own, self.outputs = [], [], {}
+
+
+class _LibTransport:
+    """librce_qmm.so's entry points, CUDA tensors and stream handles."""
+
+    def __getattr__(self, name):
+        return getattr(lib(), name)
+
+    @staticmethod
+    def zeros(shape, dtype, device: int):
+        import torch
+
+        return torch.zeros(shape, dtype=dtype, device=f"cuda:{device}")
+
+    @staticmethod
+    def stream(stream, device):
+        return _stream_handle(stream, device)
 
 
 def _wrap_device(ptr: int, shape, device: int):

@@ -252,3 +252,101 @@ def test_ffn_grouped_graph_replay(ctx):
     want = O.moe_ffn(x2, l2, 2, np.stack(gate), np.stack(up), np.stack(down), dt, d_ff, nthreads=8)
     assert np.abs(out.cpu().numpy() - want).max() / np.abs(want).max() <= 1e-3
     assert ctx.device_error() == 0
+
+
+# ---- moe_router with the gate weight (rce-op-moe/src/lib.rs:35-73, tests :140-204)
+
+@pytest.mark.parametrize("n_e,top_k,norm,kind,c1", [(8, 2, True, "sin", 0.013), (16, 1, True, "cos", 0.017),
+                                                    (32, 2, False, "sin", 0.013)])
+def test_router_from_gate_weight_reference_fixtures(ctx, n_e, top_k, norm, kind, c1):
+    import refcases
+
+    gate = refcases.router_gate_q8_0(n_e, 64)
+    x = O.test_activations(kind, c1, 0.0, 64)
+    gw = R.QuantWeight.from_owned_bytes(gate, Q8_0, n_e, 64, ctx=ctx)
+    dec = R.moe_router(x, gw, top_k, norm)
+    ri, rw = O.moe_router(x, gate, Q8_0, n_e, top_k, norm)
+    assert dec.expert_indices == list(ri)
+    np.testing.assert_allclose(dec.expert_weights, rw, rtol=1e-5)
+    w = np.array(dec.expert_weights)
+    assert np.all((w >= 0) & (w <= 1)) and list(w) == sorted(w, reverse=True)
+    assert len(set(dec.expert_indices)) == top_k
+    if norm:
+        assert abs(w.sum() - 1.0) < 1e-5
+    else:
+        assert 0.0 < w.sum() < 1.0
+
+
+def _safe_margin(logits, top_k, rel=1e-3):
+    """Tokens whose k-th and (k+1)-th largest logits differ by more than rel
+    of the logits' spread (a route that rounding cannot flip)."""
+    s = np.sort(logits, axis=1)[:, ::-1]
+    spread = np.maximum(s[:, 0] - s[:, -1], 1e-30)
+    return (s[:, top_k - 1] - s[:, top_k]) > rel * spread
+
+
+def test_router_from_gate_weight_batches(ctx):
+    import torch
+
+    rng = np.random.default_rng(55)
+    n_e, d, t, top_k = 8, 4096, 200, 2
+    gate = synth.weights(Q4_K, n_e, d, rng)
+    x = synth.activations(t, d, rng)
+    gw = R.QuantWeight.from_owned_bytes(gate, Q4_K, n_e, d, ctx=ctx)
+    want_logits = O.mm_batched(x, t, gate, Q4_K, n_e, d, nthreads=8)
+    want = [O.moe_router(x[i], gate, Q4_K, n_e, top_k, True) for i in range(t)]
+    saved = ctx.prefill_min_tokens
+    try:
+        for pmt in (0, saved):  # the exact decode path for every batch; then the default routing
+            ctx.prefill_min_tokens = pmt
+            idx, w, logits = R.moe_router_device(torch.from_numpy(x).cuda(), gw, top_k)
+            idx, w, logits = idx.cpu().numpy(), w.cpu().numpy(), logits.cpu().numpy()
+            if pmt == 0:  # per token, the exact path's bar
+                err = np.abs(logits - want_logits).max(axis=1) / np.abs(want_logits).max(axis=1)
+                assert err.max() <= 1e-5
+            else:  # 200 tokens through the one-term fp16 GEMM: its bar over the whole output
+                err = np.abs(logits - want_logits).max() / np.abs(want_logits).max()
+                assert err <= 1e-3
+            ok = np.ones(t, bool) if pmt == 0 else _safe_margin(want_logits, top_k)
+            # a routing weight moves by at most w (1 - w) times the change of
+            # the difference of two logits, i.e. by at most half of the
+            # token's largest logit error
+            lerr = np.abs(logits.astype(np.float64) - want_logits).max(axis=1)
+            for i in np.nonzero(ok)[0]:
+                assert list(idx[i]) == list(want[i][0]), f"token {i}"
+                np.testing.assert_allclose(w[i], want[i][1], rtol=1e-5, atol=0.5 * lerr[i] + 1e-7)
+            print(f"router prefill_min_tokens={pmt}: logits {err.max():.2e}, {ok.sum()} of {t} routes compared")
+    finally:
+        ctx.prefill_min_tokens = saved
+
+
+def test_host_moe_ffn(ctx):
+    import torch
+
+    dt, n_e, top_k, d_model, d_ff, t = Q4_K, 4, 2, 256, 512, 37
+    gate, up, down, x, logits = _setup(dt, n_e, d_model, d_ff, t, 71)
+    g, u, d = _device(ctx, dt, gate, up, down, d_model, d_ff)
+    # routed by given logits: the same results as the device entry point
+    out, idx, w = R.moe_ffn(x, top_k, g, u, d, router_logits=logits, return_routes=True)
+    dev, didx, dw = R.moe_ffn_device(torch.from_numpy(x).cuda(), torch.from_numpy(logits).cuda(), top_k, g, u, d,
+                                     return_routes=True)
+    assert np.array_equal(out, dev.cpu().numpy())
+    assert np.array_equal(idx, didx.cpu().numpy()) and np.array_equal(w, dw.cpu().numpy())
+    # routed by a gate weight, exact path: against the oracle's moe_router +
+    # moe_ffn composition
+    rw = synth.weights(Q8_0, n_e, d_model, np.random.default_rng(72))
+    rq = R.QuantWeight.from_owned_bytes(rw, Q8_0, n_e, d_model, ctx=ctx)
+    saved = ctx.prefill_min_tokens
+    ctx.prefill_min_tokens = 0
+    try:
+        got, gidx, _ = R.moe_ffn(x, top_k, g, u, d, router_w=rq, return_routes=True)
+    finally:
+        ctx.prefill_min_tokens = saved
+    want_logits = O.mm_batched(x, t, rw, Q8_0, n_e, d_model)
+    want = O.moe_ffn(x, want_logits, top_k, np.stack(gate), np.stack(up), np.stack(down), dt, d_ff, nthreads=8)
+    for i in range(t):
+        assert list(gidx[i]) == list(O.moe_router(x[i], rw, Q8_0, n_e, top_k, True)[0])
+    err = np.abs(got - want).max(axis=1) / np.abs(want).max(axis=1)
+    assert err.max() <= 1e-5
+    with pytest.raises(ValueError):
+        R.moe_ffn(x, top_k, g, u, d)  # neither logits nor a gate weight
