@@ -162,8 +162,10 @@ int rce_qmm_mm_batched_device_multi(rce_qmm_ctx *ctx, const float *d_a, size_t l
  * Limits: a GEMM batch (prefill_min_tokens tokens or more) needing more than
  * 16 MiB of workspace -- t_rows * n_cols * 2 bytes (twice that for batches of
  * up to 64 tokens, whose activations the GEMM carries as two fp16 terms)
- * rounded up to 256, plus 4 bytes per token; 2047 tokens at n_cols 4096 -- is
- * rejected with RCE_QMM_ERR_INVALID.  Every call on a GPU shares the array, whatever its
+ * rounded up to 256, plus 4 bytes per token rounded up to 256; 2047 tokens at
+ * n_cols 4096 -- is rejected with RCE_QMM_ERR_INVALID.  (Weights of few rows,
+ * such as row shards, may also keep split-K partial sums there, on both
+ * entry points alike, only when they fit the 16 MiB.)  Every call on a GPU shares the array, whatever its
  * context or stream, so calls that overlap on the GPU race: order them.  The
  * array keeps the last call's contents; nothing in it needs to start at zero.
  * The first call on each GPU looks up the array's device address, so make it

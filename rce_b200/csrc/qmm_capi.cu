@@ -136,7 +136,7 @@ int run_matmul(rce_qmm_ctx *ctx, const rce_qmm_weight *w, const float *d_x, size
     const Geometry &g = w->g;
     if (ctx->prefill_min_tokens > 0 && t_rows >= (size_t)ctx->prefill_min_tokens && t_rows <= (size_t)INT32_MAX) {
         void *ws = nullptr;
-        int rc = stream_gemm_ws(ctx, s, rce::gemm_workspace_bytes(g, (int)t_rows), &ws);
+        int rc = stream_gemm_ws(ctx, s, rce::gemm_workspace_bytes(w->dtype, g, (int)t_rows), &ws);
         if (rc) return rc;
         CUDA_TRY(rce::launch_gemm(w->dtype, w->dev, g, d_x, lda, d_y, ldo, (int)t_rows, ws, ctx->err_dev, s));
         return ok();

@@ -161,6 +161,8 @@ struct GemmArgs {
     int bn;
     int box_rows;  // rows of one activation TMA box
     int lo_row;    // two-term activations: row of the tensor map where the low terms start (0: one term)
+    int splits;    // split-K: CTA z of the dense launch covers chunks [z C / splits, (z + 1) C / splits)
+    float *part;   // split-K partial outputs [splits][t_rows][n_rows] (splits > 1)
 };
 
 // Packed f32x2 arithmetic (two lanes of f32 per instruction).
@@ -706,7 +708,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     // the MMA's N covers b_rows + ncol rows and accumulator column c's low
     // part sits at column b_rows + c
     const int nmma = terms == 2 ? b_rows + ncol : ncol;
-    const int nchunks = p.g.n_chunks;
+    // split-K (dense launches): this CTA's chunks [ch0, ch0 + nchunks) of K
+    const int sz = kGrouped ? 0 : (int)blockIdx.z;
+    const int ch0 = kGrouped ? 0 : sz * p.g.n_chunks / p.splits;
+    const int nchunks = (kGrouped ? p.g.n_chunks : (sz + 1) * p.g.n_chunks / p.splits) - ch0;
     const int nkb = nchunks * 4;
     const int MW = min(mma_warps(bn, terms), min(NA, NB));  // an issuer per stage at most
     const uint32_t acc_cols = tmem_cols(terms * bn), ncols = acc_cols * (uint32_t)MW;
@@ -752,8 +757,8 @@ __global__ void __launch_bounds__(kThreads, 1)
                 }
                 mbar_expect_tx(PF(s), (uint32_t)(ntiles * CB));
                 for (int t = 0; t < ntiles; t++)
-                    bulk_g2s(smem_u32(pk + (size_t)(s * 8 + t) * CB), wt + ((size_t)(tile0 + t) * nchunks + c) * CB,
-                             CB, PF(s));
+                    bulk_g2s(smem_u32(pk + (size_t)(s * 8 + t) * CB),
+                             wt + ((size_t)(tile0 + t) * p.g.n_chunks + ch0 + c) * CB, CB, PF(s));
                 if (++s == NP) {
                     s = 0;
                     ph ^= 1;
@@ -776,9 +781,10 @@ __global__ void __launch_bounds__(kThreads, 1)
                 mbar_expect_tx(BF(st), (uint32_t)(terms * b_rows * kBK * 2));
                 uint8_t *dst = b_st + (size_t)st * terms * bn * kBK * 2;
                 for (int r0 = 0; r0 < b_rows; r0 += p.box_rows) {  // a tensor-map box is at most 256 rows
-                    tma_2d(smem_u32(dst + (size_t)r0 * kBK * 2), &xmap, kb * kBK, t_begin + tok0 + r0, BF(st));
+                    const int kx = (4 * ch0 + kb) * kBK;
+                    tma_2d(smem_u32(dst + (size_t)r0 * kBK * 2), &xmap, kx, t_begin + tok0 + r0, BF(st));
                     if (terms == 2)
-                        tma_2d(smem_u32(dst + (size_t)(b_rows + r0) * kBK * 2), &xmap, kb * kBK,
+                        tma_2d(smem_u32(dst + (size_t)(b_rows + r0) * kBK * 2), &xmap, kx,
                                p.lo_row + t_begin + tok0 + r0, BF(st));
                 }
                 if (++st == NB) {
@@ -874,10 +880,13 @@ __global__ void __launch_bounds__(kThreads, 1)
                     }
                 }
                 if (row < p.g.n_rows) {
+                    // split-K: this CTA's partial sums, added in order by reduce_splits
+                    float *dst = p.splits > 1 ? p.part + (size_t)sz * p.t_rows * p.g.n_rows : yo;
+                    const size_t ld = p.splits > 1 ? (size_t)p.g.n_rows : p.ldy;
 #pragma unroll
                     for (int i = 0; i < 8; i++) {
                         const int t = t_begin + tok0 + c0 + i;
-                        if (c0 + i < live) yo[(size_t)t * p.ldy + row] = v[i] * p.inv_scale[t];
+                        if (c0 + i < live) dst[(size_t)t * ld + row] = v[i] * p.inv_scale[t];
                     }
                 }
             }
@@ -901,6 +910,16 @@ __global__ void __launch_bounds__(kPrepThreads) prep_kernel(const float *x, size
     const int t = blockIdx.x;
     const float *xr = x + (size_t)t * ldx;
     prep_row([&](int i) { return xr[i]; }, k, xh + (size_t)t * k, inv + t, xl ? xl + (size_t)t * k : nullptr);
+}
+
+// y[t][r] = sum over z, in order, of part[z][t][r] (split-K partials).
+__global__ void reduce_splits_kernel(const float *part, int splits, int t_rows, int64_t n, float *y, size_t ldy) {
+    const size_t total = (size_t)t_rows * (size_t)n;
+    for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (size_t)gridDim.x * blockDim.x) {
+        float v = part[i];
+        for (int z = 1; z < splits; z++) v += part[(size_t)z * total + i];
+        y[(i / (size_t)n) * ldy + i % (size_t)n] = v;
+    }
 }
 
 using EncodeTiled = CUresult (*)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *, const cuuint64_t *,
@@ -995,50 +1014,95 @@ int gemm_bn(int dt, int t_rows) {
 
 int gemm_terms(int t_rows) { return t_rows <= kGemmTwoTermMaxTokens ? 2 : 1; }
 
-size_t gemm_workspace_bytes(const Geometry &g, int t_rows) {
-    const size_t xh = (size_t)gemm_terms(t_rows) * t_rows * g.n_cols * 2;
-    return (xh + 255) / 256 * 256 + (size_t)t_rows * 4;
+namespace {
+
+int device_sms() {
+    static std::atomic<int> sms_cache[64];
+    int dev = 0, sms = 148;
+    if (cudaGetDevice(&dev) == cudaSuccess && dev >= 0 && dev < 64) {
+        sms = sms_cache[dev].load();
+        if (sms <= 0) {
+            if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) sms = 148;
+            sms_cache[dev].store(sms);
+        }
+    }
+    return sms;
 }
+
+size_t align256(size_t v) { return (v + 255) / 256 * 256; }
+
+// The dense launch's plan: token tile, K splits and workspace bytes.  When
+// the row blocks and token tiles alone would leave most SMs idle (weights
+// of few rows: row shards), the CTAs split K -- each a contiguous range of
+// chunks, partial outputs summed in order by reduce_splits -- into as many
+// splits as the SMs take and the workspace (fp16 activations, inverse
+// scales, partials) fits kGemmSplitWorkspace, after narrowing the token tile
+// to 128 (more CTAs, each weight tile dequantised once per bn tokens); with
+// no room for partials the tile narrows on to 64.  The plan
+// depends on the shape, t_rows and the SM count only.
+struct GemmPlan {
+    int bn = 16, splits = 1, terms = 1;
+    size_t xh_bytes = 0, inv_bytes = 0, part_bytes = 0;
+    size_t total() const { return xh_bytes + inv_bytes + part_bytes; }
+};
+
+GemmPlan plan_dense(int dt, const Geometry &g, int t_rows) {
+    GemmPlan pl;
+    pl.terms = gemm_terms(t_rows);
+    pl.bn = gemm_bn(dt, t_rows);
+    pl.xh_bytes = align256((size_t)pl.terms * t_rows * g.n_cols * 2);
+    pl.inv_bytes = align256((size_t)t_rows * 4);
+    const long sms = device_sms();
+    const long rbs = (g.n_tiles + 7) / 8;
+    auto ctas = [&](int bn) { return rbs * ((t_rows + bn - 1) / bn); };
+    auto idle = [&](int bn) { return ctas(bn) * 10 < sms * 6; };
+    if (!idle(pl.bn)) return pl;
+    // token tiles down to 128 first (a 512-token tile's two N = 256
+    // accumulators leave one MMA issuer), then K splits
+    while (pl.bn > 128 && idle(pl.bn)) pl.bn = (pl.bn / 2 + 15) / 16 * 16;
+    if (!idle(pl.bn)) return pl;
+    long sp = sms / ctas(pl.bn);
+    if (sp > g.n_chunks) sp = g.n_chunks;
+    const size_t part1 = (size_t)t_rows * (size_t)g.n_rows * 4;
+    while (sp >= 2 && pl.xh_bytes + pl.inv_bytes + align256((size_t)sp * part1) > kGemmSplitWorkspace) sp--;
+    if (sp >= 2) {
+        pl.splits = (int)sp;
+        pl.part_bytes = align256((size_t)sp * part1);
+        return pl;
+    }
+    // (bn stays a multiple of 16: the MMA's N step at M = 128, and whole
+    // 1024-byte swizzle atoms per activation stage)
+    while (pl.bn > 64 && idle(pl.bn)) pl.bn = (pl.bn / 2 + 15) / 16 * 16;
+    return pl;
+}
+
+}  // namespace
+
+size_t gemm_workspace_bytes(int dt, const Geometry &g, int t_rows) { return plan_dense(dt, g, t_rows).total(); }
 
 cudaError_t launch_gemm(int dt, const uint8_t *tiles, const Geometry &g, const float *x, size_t ldx, float *y,
                         size_t ldy, int t_rows, void *workspace, int *err, cudaStream_t s) {
     if (t_rows <= 0 || g.n_rows <= 0) return cudaSuccess;
     if (!encode_fn()) return cudaErrorNotSupported;
-    // [terms][t_rows][n_cols] fp16 activations (high terms, then low), then
-    // the per-token inverse scales
-    const int terms = gemm_terms(t_rows);
+    const GemmPlan pl = plan_dense(dt, g, t_rows);
+    // workspace: [terms][t_rows][n_cols] fp16 activations (high terms, then
+    // low), the per-token inverse scales, the split-K partials
+    const int terms = pl.terms, bn = pl.bn;
     __half *xh = static_cast<__half *>(workspace);
-    const size_t xh_bytes = ((size_t)terms * t_rows * g.n_cols * 2 + 255) / 256 * 256;
-    float *inv = reinterpret_cast<float *>(static_cast<uint8_t *>(workspace) + xh_bytes);
+    float *inv = reinterpret_cast<float *>(static_cast<uint8_t *>(workspace) + pl.xh_bytes);
+    float *part = reinterpret_cast<float *>(static_cast<uint8_t *>(workspace) + pl.xh_bytes + pl.inv_bytes);
     prep_kernel<<<t_rows, kPrepThreads, 0, s>>>(x, ldx, (int)g.n_cols, xh, inv,
                                                 terms == 2 ? xh + (size_t)t_rows * g.n_cols : nullptr);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return e;
-    int bn = gemm_bn(dt, t_rows);
-    {
-        // a narrower token tile when the row blocks alone leave most SMs idle
-        // (row shards on several GPUs): more CTAs, each weight tile
-        // dequantised once per bn tokens instead of once per 512
-        static std::atomic<int> sms_cache[64];
-        int dev = 0, sms = 148;
-        if (cudaGetDevice(&dev) == cudaSuccess && dev >= 0 && dev < 64) {
-            sms = sms_cache[dev].load();
-            if (sms <= 0) {
-                if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) sms = 148;
-                sms_cache[dev].store(sms);
-            }
-        }
-        // (bn stays a multiple of 16: the MMA's N step at M = 128, and whole
-        // 1024-byte swizzle atoms per activation stage)
-        const long rbs = (g.n_tiles + 7) / 8;
-        while (bn > 64 && rbs * ((t_rows + bn - 1) / bn) * 10 < (long)sms * 6) bn = (bn / 2 + 15) / 16 * 16;
-    }
     CUtensorMap map;
     const int box_rows = bn < 256 ? bn : 256;
     e = act_map(&map, xh, terms * t_rows, g.n_cols, box_rows);
     if (e != cudaSuccess) return e;
     GemmArgs a;
     a.lo_row = terms == 2 ? t_rows : 0;
+    a.splits = pl.splits;
+    a.part = part;
     a.w = tiles;
     a.y = y;
     a.inv_scale = inv;
@@ -1050,8 +1114,14 @@ cudaError_t launch_gemm(int dt, const uint8_t *tiles, const Geometry &g, const f
     a.box_rows = box_rows;
     const GemmSmem lay = gemm_smem(dt, bn, terms);
     if (lay.pslots < 2) return cudaErrorInvalidConfiguration;
-    dim3 grid((g.n_tiles + 7) / 8, (t_rows + bn - 1) / bn);
-    return launch_any(dt, map, a, NoGroup{}, grid, lay.total, s);
+    dim3 grid((g.n_tiles + 7) / 8, (t_rows + bn - 1) / bn, pl.splits);
+    e = launch_any(dt, map, a, NoGroup{}, grid, lay.total, s);
+    if (e != cudaSuccess || pl.splits == 1) return e;
+    const size_t total = (size_t)t_rows * (size_t)g.n_rows;
+    unsigned blocks = (unsigned)((total + 255) / 256);
+    if (blocks > 1184) blocks = 1184;
+    reduce_splits_kernel<<<blocks, 256, 0, s>>>(part, pl.splits, t_rows, g.n_rows, y, ldy);
+    return cudaGetLastError();
 }
 
 // Token tile of a grouped launch.
@@ -1078,6 +1148,8 @@ cudaError_t launch_gemm_grouped(int dt, const uint8_t *const *ws, float *const *
     if (e != cudaSuccess) return e;
     GemmArgs a;
     a.lo_row = rows;
+    a.splits = 1;
+    a.part = nullptr;
     a.w = nullptr;
     a.y = nullptr;
     a.inv_scale = inv;

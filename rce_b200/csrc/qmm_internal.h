@@ -113,7 +113,12 @@ cudaError_t launch_gather_unpack_bulk(const float *buf, size_t flag_off, float *
 // fp16 terms (gemm_terms() == 2: high + low, about 22 significant bits).
 constexpr int kGemmTwoTermMaxTokens = 64;
 int gemm_terms(int t_rows);
-size_t gemm_workspace_bytes(const Geometry &g, int t_rows);
+// Weights of few row blocks (row shards) split K over CTAs when their
+// workspace -- activations, inverse scales and partial outputs -- stays
+// within this many bytes (the allocation-free entry point's fixed array, so
+// both entry points run a batch the same way).
+constexpr size_t kGemmSplitWorkspace = size_t(16) << 20;
+size_t gemm_workspace_bytes(int dt, const Geometry &g, int t_rows);
 cudaError_t launch_gemm(int dt, const uint8_t *tiles, const Geometry &g, const float *x, size_t ldx, float *y,
                         size_t ldy, int t_rows, void *workspace, int *err, cudaStream_t s);
 

@@ -18,8 +18,10 @@
 // Rules that follow from the one shared array:
 //  - a batch whose workspace exceeds kNoallocScratchBytes (t_rows * n_cols * 2
 //    bytes, twice that for the GEMM's two-term activations at up to 64
-//    tokens, rounded up to 256, plus 4 bytes per token) is rejected with
-//    RCE_QMM_ERR_INVALID;
+//    tokens, rounded up to 256, plus 4 bytes per token rounded up to 256) is
+//    rejected with RCE_QMM_ERR_INVALID; the GEMM splits K over its CTAs
+//    (weights of few rows) only when the partial sums fit the same bytes, so
+//    this entry point and the regular one run every batch the same way;
 //  - every call on a device uses the same array, whatever its context or
 //    stream, so calls whose GEMM launches overlap on the GPU race and return
 //    garbage: order them on one stream or with events;
@@ -96,10 +98,10 @@ cudaError_t scratch_address(int dev, void **out) {
 }
 
 // Most tokens whose GEMM workspace fits the array at this weight's n_cols.
-size_t max_gemm_tokens(const rce::Geometry &g) {
+size_t max_gemm_tokens(int dt, const rce::Geometry &g) {
     size_t t = kNoallocScratchBytes / ((size_t)g.n_cols * 2 + 4);
-    while (t > 0 && rce::gemm_workspace_bytes(g, (int)t) > kNoallocScratchBytes) t--;
-    while (rce::gemm_workspace_bytes(g, (int)(t + 1)) <= kNoallocScratchBytes) t++;
+    while (t > 0 && rce::gemm_workspace_bytes(dt, g, (int)t) > kNoallocScratchBytes) t--;
+    while (rce::gemm_workspace_bytes(dt, g, (int)(t + 1)) <= kNoallocScratchBytes) t++;
     return t;
 }
 
@@ -122,12 +124,12 @@ extern "C" int rce_qmm_mm_batched_device_noalloc(rce_qmm_ctx *ctx, const float *
 
     // the regular entry point's routing (run_matmul), GEMM workspace aside
     if (ctx->prefill_min_tokens > 0 && t_rows >= (size_t)ctx->prefill_min_tokens && t_rows <= (size_t)INT32_MAX) {
-        const size_t need = rce::gemm_workspace_bytes(g, (int)t_rows);
+        const size_t need = rce::gemm_workspace_bytes(w->dtype, g, (int)t_rows);
         if (need > kNoallocScratchBytes)
             return err(RCE_QMM_ERR_INVALID,
                        "mm_batched_device_noalloc: %zu tokens x k %lld need %zu bytes of GEMM workspace, above this "
                        "entry point's fixed %zu (at most %zu tokens at this k)",
-                       t_rows, (long long)g.n_cols, need, kNoallocScratchBytes, max_gemm_tokens(g));
+                       t_rows, (long long)g.n_cols, need, kNoallocScratchBytes, max_gemm_tokens(w->dtype, g));
         void *ws = nullptr;
         cudaError_t e = scratch_address(ctx->device, &ws);
         if (e != cudaSuccess)
