@@ -788,6 +788,24 @@ int rce_qmm_mm_batched_device_multi_gather_bulk(rce_qmm_ctx *ctx, const float *d
     DeviceGuard dg(ctx->device);
     cudaStream_t s = static_cast<cudaStream_t>(stream);
     for (size_t i = 0; i < n_w; i++) {
+        const bool gemm = ctx->prefill_min_tokens > 0 && t_rows >= (size_t)ctx->prefill_min_tokens;
+        if (gemm) {
+            // the GEMM (or its split-K reduce) stores every value into the
+            // peers' bulk buffers itself; then the flags
+            rce::BulkPush push;
+            push.world = world;
+            push.rank = rank;
+            for (int r = 0; r < world; r++)
+                push.peer[r] = r == rank ? nullptr : d_bulks[i * world + r] + row_offsets[i];
+            void *wsp = nullptr;
+            int rc = stream_gemm_ws(ctx, s, rce::gemm_workspace_bytes(ws[i]->dtype, ws[i]->g, (int)t_rows), &wsp);
+            if (rc) return rc;
+            CUDA_TRY(rce::launch_gemm(ws[i]->dtype, ws[i]->dev, ws[i]->g, d_a, lda, d_ys[i] + row_offsets[i], ldys[i],
+                                      (int)t_rows, wsp, ctx->err_dev, s, &push));
+            CUDA_TRY(rce::launch_gather_flags_bulk(world, rank, d_bulks + i * world, flag_offsets[i], epoch,
+                                                   d_epoch_base, s));
+            continue;
+        }
         int rc = run_matmul(ctx, ws[i], d_a, lda, t_rows, d_ys[i] + row_offsets[i], ldys[i], s);
         if (rc) return rc;
         CUDA_TRY(rce::launch_gather_push_bulk(world, rank, d_bulks + i * world, flag_offsets[i], d_ys[i], (int)t_rows,

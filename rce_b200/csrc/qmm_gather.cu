@@ -185,6 +185,15 @@ cudaError_t launch_gather_push_bulk(int world, int rank, float *const *peer_bufs
     return cudaGetLastError();
 }
 
+cudaError_t launch_gather_flags_bulk(int world, int rank, float *const *peer_bufs, size_t flag_off, unsigned epoch,
+                                     const unsigned *epoch_base, cudaStream_t s) {
+    if (world < 2 || world > kMaxPeers) return cudaErrorInvalidValue;
+    BulkPeers bp = {};
+    for (int r = 0; r < world; r++) bp.buf[r] = peer_bufs[r];
+    push_flags_kernel<<<1, 32, 0, s>>>(bp, flag_off, world, rank, epoch, epoch_base);
+    return cudaGetLastError();
+}
+
 cudaError_t launch_gather_unpack_bulk(const float *buf, size_t flag_off, float *y, int t_rows, int64_t n, size_t ldy,
                                       int64_t own0, int64_t own1, int world, int rank, unsigned epoch,
                                       const unsigned *epoch_base, int *err, cudaStream_t s) {

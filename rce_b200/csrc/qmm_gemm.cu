@@ -163,6 +163,7 @@ struct GemmArgs {
     int lo_row;    // two-term activations: row of the tensor map where the low terms start (0: one term)
     int splits;    // split-K: CTA z of the dense launch covers chunks [z C / splits, (z + 1) C / splits)
     float *part;   // split-K partial outputs [splits][t_rows][n_rows] (splits > 1)
+    BulkPush push; // fused bulk all-gather (push.world > 1; dense launches without splits)
 };
 
 // Packed f32x2 arithmetic (two lanes of f32 per instruction).
@@ -886,7 +887,15 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
                     for (int i = 0; i < 8; i++) {
                         const int t = t_begin + tok0 + c0 + i;
-                        if (c0 + i < live) dst[(size_t)t * ld + row] = v[i] * p.inv_scale[t];
+                        if (c0 + i < live) {
+                            const float o = v[i] * p.inv_scale[t];
+                            dst[(size_t)t * ld + row] = o;
+                            // the fused all-gather: the same value into every
+                            // peer's bulk buffer, over NVLink
+                            if (p.push.world > 1)
+                                for (int q = 0; q < p.push.world; q++)
+                                    if (q != p.push.rank) p.push.peer[q][(size_t)t * p.ldy + row] = o;
+                        }
                     }
                 }
             }
@@ -912,13 +921,19 @@ __global__ void __launch_bounds__(kPrepThreads) prep_kernel(const float *x, size
     prep_row([&](int i) { return xr[i]; }, k, xh + (size_t)t * k, inv + t, xl ? xl + (size_t)t * k : nullptr);
 }
 
-// y[t][r] = sum over z, in order, of part[z][t][r] (split-K partials).
-__global__ void reduce_splits_kernel(const float *part, int splits, int t_rows, int64_t n, float *y, size_t ldy) {
+// y[t][r] = sum over z, in order, of part[z][t][r] (split-K partials); with
+// a fused bulk all-gather also into every peer's bulk buffer.
+__global__ void reduce_splits_kernel(const float *part, int splits, int t_rows, int64_t n, float *y, size_t ldy,
+                                     BulkPush push) {
     const size_t total = (size_t)t_rows * (size_t)n;
     for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (size_t)gridDim.x * blockDim.x) {
         float v = part[i];
         for (int z = 1; z < splits; z++) v += part[(size_t)z * total + i];
-        y[(i / (size_t)n) * ldy + i % (size_t)n] = v;
+        const size_t o = (i / (size_t)n) * ldy + i % (size_t)n;
+        y[o] = v;
+        if (push.world > 1)
+            for (int q = 0; q < push.world; q++)
+                if (q != push.rank) push.peer[q][o] = v;
     }
 }
 
@@ -1081,8 +1096,9 @@ GemmPlan plan_dense(int dt, const Geometry &g, int t_rows) {
 size_t gemm_workspace_bytes(int dt, const Geometry &g, int t_rows) { return plan_dense(dt, g, t_rows).total(); }
 
 cudaError_t launch_gemm(int dt, const uint8_t *tiles, const Geometry &g, const float *x, size_t ldx, float *y,
-                        size_t ldy, int t_rows, void *workspace, int *err, cudaStream_t s) {
+                        size_t ldy, int t_rows, void *workspace, int *err, cudaStream_t s, const BulkPush *push) {
     if (t_rows <= 0 || g.n_rows <= 0) return cudaSuccess;
+    if (push && (push->world > kMaxPeers || push->rank < 0 || push->rank >= push->world)) return cudaErrorInvalidValue;
     if (!encode_fn()) return cudaErrorNotSupported;
     const GemmPlan pl = plan_dense(dt, g, t_rows);
     // workspace: [terms][t_rows][n_cols] fp16 activations (high terms, then
@@ -1103,6 +1119,7 @@ cudaError_t launch_gemm(int dt, const uint8_t *tiles, const Geometry &g, const f
     a.lo_row = terms == 2 ? t_rows : 0;
     a.splits = pl.splits;
     a.part = part;
+    if (push && push->world > 1 && pl.splits == 1) a.push = *push;
     a.w = tiles;
     a.y = y;
     a.inv_scale = inv;
@@ -1120,7 +1137,8 @@ cudaError_t launch_gemm(int dt, const uint8_t *tiles, const Geometry &g, const f
     const size_t total = (size_t)t_rows * (size_t)g.n_rows;
     unsigned blocks = (unsigned)((total + 255) / 256);
     if (blocks > 1184) blocks = 1184;
-    reduce_splits_kernel<<<blocks, 256, 0, s>>>(part, pl.splits, t_rows, g.n_rows, y, ldy);
+    reduce_splits_kernel<<<blocks, 256, 0, s>>>(part, pl.splits, t_rows, g.n_rows, y, ldy,
+                                                push && push->world > 1 ? *push : BulkPush{});
     return cudaGetLastError();
 }
 

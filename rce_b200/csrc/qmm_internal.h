@@ -102,6 +102,11 @@ cudaError_t launch_epoch_advance(unsigned *epoch_base, unsigned delta, cudaStrea
 cudaError_t launch_gather_push_bulk(int world, int rank, float *const *peer_bufs, size_t flag_off, const float *y,
                                     int t_rows, int64_t row_off, int64_t n_own, size_t ldy, unsigned epoch,
                                     const unsigned *epoch_base, cudaStream_t s);
+// Only the flags of a bulk push whose values are already in the peers'
+// buffers (stored by the GEMM itself, BulkPush): one system-scope release of
+// the epoch into slot `rank` of each peer's flags.
+cudaError_t launch_gather_flags_bulk(int world, int rank, float *const *peer_bufs, size_t flag_off, unsigned epoch,
+                                     const unsigned *epoch_base, cudaStream_t s);
 cudaError_t launch_gather_unpack_bulk(const float *buf, size_t flag_off, float *y, int t_rows, int64_t n, size_t ldy,
                                       int64_t own0, int64_t own1, int world, int rank, unsigned epoch,
                                       const unsigned *epoch_base, int *err, cudaStream_t s);
@@ -119,8 +124,18 @@ int gemm_terms(int t_rows);
 // both entry points run a batch the same way).
 constexpr size_t kGemmSplitWorkspace = size_t(16) << 20;
 size_t gemm_workspace_bytes(int dt, const Geometry &g, int t_rows);
+// Bulk all-gather fused into the GEMM: every output value the GEMM writes at
+// y[t * ldy + r] is also stored at peer[p][t * ldy + r] for each peer p (the
+// peers' bulk buffers, offset by this rank's row offset; entries of this
+// rank and of ranks beyond world are ignored).  Release the flags with
+// launch_gather_flags_bulk after the GEMM.
+struct BulkPush {
+    int world = 0, rank = 0;
+    float *peer[kMaxPeers] = {};
+};
 cudaError_t launch_gemm(int dt, const uint8_t *tiles, const Geometry &g, const float *x, size_t ldx, float *y,
-                        size_t ldy, int t_rows, void *workspace, int *err, cudaStream_t s);
+                        size_t ldy, int t_rows, void *workspace, int *err, cudaStream_t s,
+                        const BulkPush *push = nullptr);
 
 // Expert-grouped prefill matmul: one launch for up to kGemmMaxGroup weights
 // of one shape.  Entry z multiplies ws[z] by the two-term fp16 activation
