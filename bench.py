@@ -34,6 +34,14 @@ prefill  = BASELINE configs[2]: Q4_K 14336x4096 weight (row-sharded N ways),
 formats_gemv = one GPU: the decode GEMV of every supported format (Q4_K, Q5_K,
          Q6_K, Q8_0, Q4_0) at 14336x4096 and 4096x14336, 8 distinct weights
          per shape in a CUDA graph, CUDA events
+stack_batch16 = one GPU: the same stack at batch 16 (configs[3]'s second batch
+         size), every matmul through mm_batched's routing (the tcgen05 GEMM),
+         replayed from a CUDA graph; GB/s of weights and tokens/s
+baseline_configs_gemv = one GPU: configs[0] (Q8_0 4096x4096, seed 0) and
+         configs[1] (Q4_0 11008x4096 / 4096x11008, seed 1) at their own shapes
+prefill.e2e_m512 = configs[2] at M = 512 through the host C-ABI
+         (rce_qmm_mm_batched), wall clock
+cpu_baseline.one_thread = the same CPU sample on one host thread
 The weights (3.9 GB) are far larger than L2 (126 MB), so no L2 flush is
 needed between steps.
 
@@ -295,6 +303,23 @@ def prefill_section(args, rank, world, dev, stream, ctx, pg=None):
         del graph
     if pg is not None:
         pg.end_step()
+    if world == 1:
+        # end to end through the host C-ABI (rce_qmm_mm_batched: host
+        # activations in, host outputs out, synchronous), M = 512
+        m = 512
+        g = torch.Generator(device=dev)
+        g.manual_seed(2)
+        xh = torch.randn((m, PREFILL_K), device=dev, generator=g).cpu().numpy()
+        yh = np.empty(m * ns, np.float32)
+        R.mm_batched(xh, m, ws[0], yh)
+        calls = 10
+        t0 = time.perf_counter()
+        for i in range(calls):
+            R.mm_batched(xh, m, ws[i % len(ws)], yh)
+        dt = (time.perf_counter() - t0) / calls
+        out["e2e_m512"] = {"us": round(dt * 1e6, 1), "tflops": round(2.0 * m * ns * PREFILL_K / dt / 1e12, 1),
+                           "h2d_bytes": m * PREFILL_K * 4, "d2h_bytes": m * ns * 4,
+                           "timing": "wall clock around synchronous rce_qmm_mm_batched calls (host buffers)"}
     return out
 
 
@@ -350,6 +375,60 @@ def formats_section(args, dev, stream, ctx):
             res[f"{n}x{k}"] = {"us": round(us, 2), "gbs": round(alg / (us / 1e6) / 1e9, 1)}
             del graph, ws
         out[fmt.name] = res
+    return out
+
+
+def baseline_configs_section(args, dev, stream, ctx, hbm):
+    """configs[0] (Q8_0 4096x4096, seed 0) and configs[1] (Q4_0 11008x4096 and
+    4096x11008, seed 1) at their own shapes: the one-token decode GEMV, 8
+    distinct weights per shape (more bytes than L2) back to back in a CUDA
+    graph, CUDA events; GB/s of algorithmic bytes and the fraction of HBM."""
+    import torch
+
+    import rce_b200 as R
+    from rce_b200 import synth
+    from rce_b200.gguf import GgufDtype, tensor_byte_size
+
+    out = {}
+    for name, fmt, n, k, seed in (("configs[0] Q8_0 4096x4096", GgufDtype.Q8_0, 4096, 4096, 0),
+                                  ("configs[1] Q4_0 11008x4096", GgufDtype.Q4_0, 11008, 4096, 1),
+                                  ("configs[1] Q4_0 4096x11008", GgufDtype.Q4_0, 4096, 11008, 1)):
+        ws = []
+        for i in range(8):
+            g = torch.Generator(device=dev)
+            g.manual_seed(seed * 1_000_003 + i)
+            raw = synth.device_weights(fmt, n, k, g, dev)
+            ws.append(R.QuantWeight.from_device_bytes(raw, fmt, n, k, ctx=ctx))
+            del raw
+        g = torch.Generator(device=dev)
+        g.manual_seed(seed)
+        x = torch.randn((1, k), device=dev, generator=g)
+        y = torch.empty((1, n), device=dev)
+        with torch.cuda.stream(stream):
+            for w in ws:
+                R.mm_batched_device(x, w, y, stream=stream)
+        stream.synchronize()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=stream):
+            for w in ws:
+                R.mm_batched_device(x, w, y, stream=stream)
+        with torch.cuda.stream(stream):
+            for _ in range(3):
+                graph.replay()
+            e0 = torch.cuda.Event(enable_timing=True)
+            e1 = torch.cuda.Event(enable_timing=True)
+            reps = 20
+            e0.record(stream)
+            for _ in range(reps):
+                graph.replay()
+            e1.record(stream)
+        e1.synchronize()
+        us = e0.elapsed_time(e1) * 1e3 / (reps * len(ws))
+        alg = tensor_byte_size(fmt, n * k) + 4 * k + 4 * n
+        gbs = alg / (us / 1e6) / 1e9
+        out[name] = {"us": round(us, 2), "gbs": round(gbs, 1), "frac_of_hbm": round(gbs / hbm, 4),
+                     "alg_bytes": alg}
+        del graph, ws
     return out
 
 
@@ -453,7 +532,7 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--batch", type=int, default=1)
     ap.add_argument("--layers", type=int, default=32)
-    ap.add_argument("--e2e-steps", type=int, default=3)
+    ap.add_argument("--e2e-steps", type=int, default=20)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-group", action="store_true",
                     help="one launch per matrix (no grouped q/k/v and gate/up launches)")
@@ -710,9 +789,55 @@ def main():
 
     if pg is not None:
         pg.end_step()  # absolute epochs for the eager legs below
+    # ---- the batch-16 decode stack (configs[3] at batch 16), one GPU: the
+    # same 32 layers, each matmul through mm_batched's routing (the tensor-core
+    # GEMM from 16 tokens), grouped as the step above ---------------------------
+    stack16 = None
+    if world == 1 and m == 1:
+        x16 = {D_MODEL: torch.randn((16, D_MODEL), device=dev, generator=gen),
+               D_FF: torch.randn((16, D_FF), device=dev, generator=gen)}
+        y16 = {name: torch.empty((16, n), device=dev) for name, n, _ in LAYER}
+
+        def step16():
+            for mats in layers:
+                by = {name: (ns, k, w) for name, ns, k, w in mats}
+                for grp in GROUPS:
+                    k = by[grp[0]][1]
+                    if len(grp) == 1:
+                        R.mm_batched_device(x16[k], by[grp[0]][2], y16[grp[0]], stream=stream)
+                    else:
+                        R.mm_multi_device(x16[k], [by[nm][2] for nm in grp], [y16[nm] for nm in grp],
+                                          stream=stream)
+
+        with torch.cuda.stream(stream):
+            for _ in range(2):
+                step16()
+        stream.synchronize()
+        g16 = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g16, stream=stream):
+            step16()
+        with torch.cuda.stream(stream):
+            for _ in range(3):
+                g16.replay()
+            e0 = torch.cuda.Event(enable_timing=True)
+            e1 = torch.cuda.Event(enable_timing=True)
+            reps = 20
+            e0.record(stream)
+            for _ in range(reps):
+                g16.replay()
+            e1.record(stream)
+        e1.synchronize()
+        ms16 = e0.elapsed_time(e1) / reps
+        v16 = layer_bytes() * args.layers / (ms16 / 1e3) / 1e9
+        stack16 = {"batch": 16, "ms_per_step": round(ms16, 4), "value": round(v16, 1), "unit": "GB/s",
+                   "frac_of_hbm": round(v16 / load_peaks()[0], 4),
+                   "tokens_per_s": round(16 / (ms16 / 1e3), 1),
+                   "path": "tcgen05 GEMM per matmul (two-term activations), grouped q+k+v and gate+up"}
+        del g16
     prefill = prefill_section(args, rank, world, dev, stream, ctx, pg)
     moe = moe_section(args, rank, world, dev, stream, ctx)
     formats = formats_section(args, dev, stream, ctx) if world == 1 else None
+    base_cfgs = baseline_configs_section(args, dev, stream, ctx, load_peaks()[0]) if world == 1 else None
 
     # ---- e2e through the public API with host buffers -----------------------------
     # N = 1: the C-ABI call rce_qmm_mm_batched (host in, host out; it stages
@@ -771,8 +896,11 @@ def main():
         threads = os.cpu_count() or 1
         mats_h, xs_h = cpu_layer_sample()
         times = time_cpu_layer(mats_h, xs_h, threads, budget_s=10.0)
+        t1 = time_cpu_layer(mats_h, xs_h, 1, reps=2)
         cpu = {"value": round(layer_bytes() * len(times) / sum(times) / 1e9, 3), "unit": "GB/s", "cores": threads,
                "kind": "port",
+               "one_thread": {"value": round(layer_bytes() * len(t1) / sum(t1) / 1e9, 3), "unit": "GB/s", "cores": 1,
+                              "sample": "2 passes over the same layer, one host thread"},
                "sample": f"{len(times)} passes over one layer of the stack (7 Q4_K matmuls, 122,683,392 weight bytes), "
                          "batch 1, oracle/qmm_oracle.c (bit-exact restatement of rce-op-qmm mm_1d_q4_k), rows split "
                          "over all host threads as rayon does"}
@@ -790,11 +918,15 @@ def main():
                          "timing": "32 launches of this matrix back to back in a CUDA graph, CUDA events",
                          "achieved": round(kern[dom]["gbs"], 1), "peak": hbm, "unit": "GB/s",
                          "frac": round(kern[dom]["gbs"] / hbm, 4), "peak_kind": peak_kind,
-                         "traffic": traffic, "alg_bytes_per_launch": kern[dom]["alg_bytes"],
+                         "traffic": traffic,
+                         "traffic_source": "dram__bytes_read.sum + dram__bytes_write.sum of this kernel from an ncu "
+                                           "capture of the same launch (profiles/gemv_q4k_traffic.json), not this run",
+                         "alg_bytes_per_launch": kern[dom]["alg_bytes"],
                          "avg_launch_us": round(kern[dom]["avg_us"], 2)},
             "kernels": {nm: {"avg_us": round(v["avg_us"], 2), "gbs": round(v["gbs"], 1)} for nm, v in kern.items()},
             "grouped_launches": groups,
             "stack_frac_of_hbm": round(value / world / hbm, 4),
+            "stack_batch16": stack16,
             "prefill_gemm": {
                 "workload": f"configs[2]: Q4_K {PREFILL_N}x{PREFILL_K} weight, M f32 activations, fp16 operands, "
                             "f32 accumulation in tensor memory",
@@ -805,6 +937,7 @@ def main():
             },
             "moe_ffn": moe,
             "formats_gemv": formats,
+            "baseline_configs_gemv": base_cfgs,
             "e2e": e2e,
             "cpu_baseline": cpu,
             "clocks": clk,

@@ -2,8 +2,9 @@
 
 Mirrors ``GgufDtype`` (rce-ingest-gguf/src/parser.rs:228, tags :308-338),
 ``tensor_byte_size`` (rce-ingest-gguf/src/dequant.rs:18-58) and the block
-geometry of ``quant_info`` (rce-ingest-gguf/src/quant.rs:22-217) for the three
-formats this library implements.
+geometry of ``quant_info`` (rce-ingest-gguf/src/quant.rs:22-217) for the five
+formats this library implements (Q8_0, Q4_0, Q4_K, Q5_K, Q6_K), and the GGUF
+file reader (``GgufFile``, after ``GgufFile::parse``, parser.rs:446).
 """
 from __future__ import annotations
 
