@@ -110,6 +110,26 @@ __device__ __forceinline__ void tma_2d(uint32_t dst, const CUtensorMap *map, int
         : "memory");
 }
 
+// One chunk (256 columns) of 8 consecutive 16-row tiles of a T16 weight:
+// the 4-d tensor map of weight_map, coordinates (0, 0, chunk, first tile).
+__device__ __forceinline__ void tma_4d(uint32_t dst, const CUtensorMap *map, int c, int t, uint32_t bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.4d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4, "
+        "%5}], [%6];" ::"r"(dst),
+        "l"(map), "r"(0), "r"(0), "r"(c), "r"(t), "r"(bar)
+        : "memory");
+}
+
+// kps k-blocks of the activations, all terms, bn rows from `row`: the 4-d
+// tensor map of act_map4, coordinates (0, row, 0, first k-block).
+__device__ __forceinline__ void tma_act4(uint32_t dst, const CUtensorMap *map, int row, int kb, uint32_t bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.4d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4, "
+        "%5}], [%6];" ::"r"(dst),
+        "l"(map), "r"(0), "r"(row), "r"(0), "r"(kb), "r"(bar)
+        : "memory");
+}
+
 // UMMA shared-memory descriptor: K-major, 128-byte swizzle, 8-row groups
 // 1024 bytes apart (SBO), version 1.
 __device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr) {
@@ -127,16 +147,46 @@ __device__ __forceinline__ uint32_t idesc_f16(int n) {
     return (1u << 4) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(kBM >> 4) << 24);
 }
 
+// The MMA issuers run as whole warps with warp-uniform operands (kept in
+// uniform registers) and one elected lane issues: a single thread issuing
+// from divergent code spends 60-95 cycles per instruction, an elected lane
+// of a converged warp reaches the tensor pipe's own rate (~40 cycles per
+// M = 128, N <= 32, K = 16 instruction).  The same lane is elected every
+// time (the lowest), so its commits track its MMAs.
 __device__ __forceinline__ void umma_f16(uint32_t tmem_d, uint64_t da, uint64_t db, uint32_t idesc, uint32_t acc) {
     asm volatile(
-        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
-        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
+        "{\n\t.reg .pred p, e;\n\tsetp.ne.b32 p, %4, 0;\n\telect.sync _|e, 0xffffffff;\n\t"
+        "@e tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
         "l"(da), "l"(db), "r"(idesc), "r"(acc)
         : "memory");
 }
 __device__ __forceinline__ void umma_commit(uint32_t bar) {
-    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar)
-                 : "memory");
+    asm volatile(
+        "{\n\t.reg .pred e;\n\telect.sync _|e, 0xffffffff;\n\t"
+        "@e tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];\n\t}" ::"r"(bar)
+        : "memory");
+}
+// The same with A in tensor memory (128 lanes = rows, K packed two fp16
+// per 32-bit column).
+__device__ __forceinline__ void umma_f16_ta(uint32_t tmem_d, uint32_t tmem_a, uint64_t db, uint32_t idesc,
+                                            uint32_t acc) {
+    asm volatile(
+        "{\n\t.reg .pred p, e;\n\tsetp.ne.b32 p, %4, 0;\n\telect.sync _|e, 0xffffffff;\n\t"
+        "@e tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(tmem_d),
+        "r"(tmem_a), "l"(db), "r"(idesc), "r"(acc)
+        : "memory");
+}
+// 32 consecutive 32-bit columns of this thread's tensor-memory lane (the
+// warp's 32 lanes at once).
+__device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&v)[32]) {
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,"
+        "%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};" ::"r"(taddr),
+        "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]), "r"(v[8]), "r"(v[9]),
+        "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15]), "r"(v[16]), "r"(v[17]), "r"(v[18]),
+        "r"(v[19]), "r"(v[20]), "r"(v[21]), "r"(v[22]), "r"(v[23]), "r"(v[24]), "r"(v[25]), "r"(v[26]), "r"(v[27]),
+        "r"(v[28]), "r"(v[29]), "r"(v[30]), "r"(v[31])
+        : "memory");
 }
 __device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
 __device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
@@ -164,6 +214,8 @@ struct GemmArgs {
     int splits;    // split-K: CTA z of the dense launch covers chunks [z C / splits, (z + 1) C / splits)
     float *part;   // split-K partial outputs [splits][t_rows][n_rows] (splits > 1)
     BulkPush push; // fused bulk all-gather (push.world > 1; dense launches without splits)
+    int kps_log;   // log2 of the k-blocks per activation stage: 0 (2-d map, a box per k-block and term) or
+                   // 1, 2 (4-d map over [k-block][term][row][64], one copy per stage; dense launches)
 };
 
 // Packed f32x2 arithmetic (two lanes of f32 per instruction).
@@ -271,34 +323,65 @@ struct RowHalf {
             const uint4 h4 = lds128(ch + 2048 + r16 * 16);
             hd = h2dup(h4.x);                                // d
             const uint32_t ndmin = h2dup(h4.x >> 16) ^ 0x80008000u;  // -dmin
-#pragma unroll
-            for (int j = G; j < 4; j += 2) {
-                const uint32_t lo = j < 2 ? h4.y : (j == 2 ? h4.z : h4.w);
-                const uint32_t hi = j < 2 ? h4.z : (j == 2 ? h4.w : 0u);
-                const uint32_t sh = j == 0 ? 0u : (j == 1 ? 24u : (j == 2 ? 16u : 8u));
-                const uint32_t f = __funnelshift_r(lo, hi, sh) & 0xFFFFFFu;
-#pragma unroll
-                for (int h = 0; h < 2; h++) {
-                    const uint32_t sc = small_h2((f >> (12 * h)) & 63u), m = small_h2((f >> (12 * h + 6)) & 63u);
-                    hs[j][h] = sc;
-                    hc[j][h] = h2mul(sc, 0xE400E400u);  // -1024 * sc, exact
-                    hm[j][h] = h2mul(ndmin, m);          // -(dmin * m), rounded once to fp16
-                }
-            }
+            kq_scales<G>(h4, ndmin);
+            kq_scales<G + 2>(h4, ndmin);
         } else if (DT == GGUF_Q6_K) {
-            // k-block j, 16-value group k2 of this half: scale 4 j + 2 hf + k2,
-            // d * sc exact in f32 (11 x 8 bits)
             const float d = h2f(lds16(ch + kQ6D + 2 * r16));
             const uint4 sv = lds128(ch + kQ6Sc + r16 * 16);
-            const uint32_t sw[4] = {sv.x, sv.y, sv.z, sv.w};
+            q6_scales<G>(d, sv);
+            q6_scales<G + 2>(d, sv);
+        }
+    }
+
+    // The same for k-block J alone (a thread that fills one k-block of the
+    // chunk, both halves: for K-quants the scales do not depend on hf, so a
+    // copy of this object with hf = 1 serves the other half; Q6_K's do).
+    template <int J>
+    __device__ __forceinline__ void begin1(const uint8_t *slot, int row_, int hf_) {
+        constexpr int CB = chunk_bytes(DT);
+        row = row_;
+        hf = hf_;
+        const int tile = row >> 4;
+        r16 = row & 15;
+        r = r16 & 7;
+        rh = r16 >> 3;
+        ch = smem_u32(slot) + (uint32_t)(tile * CB);
+        if (kquant45(DT)) {
+            const uint4 h4 = lds128(ch + 2048 + r16 * 16);
+            hd = h2dup(h4.x);
+            kq_scales<J>(h4, h2dup(h4.x >> 16) ^ 0x80008000u);
+        } else if (DT == GGUF_Q6_K) {
+            q6_scales<J>(h2f(lds16(ch + kQ6D + 2 * r16)), lds128(ch + kQ6Sc + r16 * 16));
+        }
+    }
+
+    // K-quant scales of k-block j (sub-blocks 2 j, 2 j + 1) from the 16-byte
+    // row header (d, dmin, then the 12 permuted scale bytes: 24 bits per
+    // k-block, sc and m of 6 bits per sub-block)
+    template <int j>
+    __device__ __forceinline__ void kq_scales(const uint4 &h4, uint32_t ndmin) {
+        const uint32_t lo = j < 2 ? h4.y : (j == 2 ? h4.z : h4.w);
+        const uint32_t hi = j < 2 ? h4.z : (j == 2 ? h4.w : 0u);
+        const uint32_t sh = j == 0 ? 0u : (j == 1 ? 24u : (j == 2 ? 16u : 8u));
+        const uint32_t f = __funnelshift_r(lo, hi, sh) & 0xFFFFFFu;
 #pragma unroll
-            for (int j = G; j < 4; j += 2)
+        for (int h = 0; h < 2; h++) {
+            const uint32_t sc = small_h2((f >> (12 * h)) & 63u), m = small_h2((f >> (12 * h + 6)) & 63u);
+            hs[j][h] = sc;
+            hc[j][h] = h2mul(sc, 0xE400E400u);  // -1024 * sc, exact
+            hm[j][h] = h2mul(ndmin, m);          // -(dmin * m), rounded once to fp16
+        }
+    }
+    // Q6_K, k-block j, 16-value group k2 of this half: scale 4 j + 2 hf + k2,
+    // d * sc exact in f32 (11 x 8 bits)
+    template <int j>
+    __device__ __forceinline__ void q6_scales(float d, const uint4 &sv) {
+        const uint32_t sw[4] = {sv.x, sv.y, sv.z, sv.w};
 #pragma unroll
-                for (int k2 = 0; k2 < 2; k2++) {
-                    const int i = 4 * j + 2 * hf + k2;  // hf is 0 or 1: the word is sw[j]
-                    const float ds = d * (float)(int8_t)(sw[i >> 2] >> (8 * (i & 3)));
-                    s[j][k2] = f2pack(ds, ds);
-                }
+        for (int k2 = 0; k2 < 2; k2++) {
+            const int i = 4 * j + 2 * hf + k2;  // hf is 0 or 1: the word is sw[j]
+            const float ds = d * (float)(int8_t)(sw[i >> 2] >> (8 * (i & 3)));
+            s[j][k2] = f2pack(ds, ds);
         }
     }
 
@@ -438,31 +521,77 @@ struct GemmSmem {
     int a_stages, b_stages, pslots;
 };
 
-constexpr int kMaxA = 8, kMaxB = 8, kMaxP = 4;  // ring depth limits (barrier slots)
+constexpr int kMaxA = 12, kMaxB = 16, kMaxP = 4;  // ring depth limits (barrier slots)
+constexpr int kBars = 2 * kMaxP + 2 * kMaxA + 2 * kMaxB + 1;  // mbarriers of the CTA
+constexpr int kMaxASmem = 8;  // A stages in shared memory at most
+constexpr uint32_t kTmemCols = 512;  // tensor memory of the CTA (all of the SM's)
+constexpr uint32_t kTmemStage = kBK / 2;  // columns of one A k-block in tensor memory
+
+// Activation stages of several k-blocks: one tensor copy (and one mbarrier
+// phase) per stage instead of one box per k-block and term.  A copy costs
+// the TMA unit a few hundred cycles whatever its size, so per-k-block boxes
+// of a small token tile cannot keep up with the MMAs.
+constexpr size_t kActStageBudget = 128 * 1024;
+
+// log2 of the k-blocks per activation stage of a dense launch: with A in
+// tensor memory, 4 or 2 if two such stages fit kActStageBudget, else 1.
+__host__ __device__ inline int act_kps_log(int bn, int terms, bool tmem_a) {
+    if (!tmem_a) return 0;
+    const size_t kb_bytes = (size_t)terms * bn * kBK * 2;
+    if (2 * 4 * kb_bytes <= kActStageBudget) return 2;
+    if (2 * 2 * kb_bytes <= kActStageBudget) return 1;
+    return 0;
+}
 
 // Token tiles up to this width carry two-term activations (N = 2 bn <= 256).
 constexpr int kTwoTermMaxTile = 128;
 
-__host__ __device__ inline GemmSmem gemm_smem(int dt, int bn, int terms) {
+__host__ __device__ inline GemmSmem gemm_smem(int dt, int bn, int terms, bool tmem_a, int kps_log) {
     // Rings as deep as 227 KB allow: the dequantiser <-> MMA hand-off takes
     // a few thousand cycles, so the A ring should span several k-blocks;
     // the activation ring shrinks as its stages grow with bn.
     constexpr size_t kLimit = 227 * 1024;  // dynamic shared memory per CTA (opt-in)
     GemmSmem L;
     const int brows = terms * bn;  // activation rows per stage
-    // at least 2-4 stages, and up to kMaxB of them within 32 KB: at small
+    // at least 2-4 stages, and up to 8 of them within 32 KB (A tile in
+    // shared memory) or kMaxB within 64 KB (A in tensor memory): at small
     // token tiles a stage is consumed faster than an L2 round trip
     L.b_stages = brows > 256 ? 2 : (brows > 128 ? 3 : 4);
-    const int by_bytes = (int)((32 * 1024) / (brows * kBK * 2));
-    if (by_bytes > L.b_stages) L.b_stages = by_bytes < kMaxB ? by_bytes : kMaxB;
+    const int by_bytes = (int)(((tmem_a ? 64 : 32) * 1024) / (brows * kBK * 2));
+    const int max_b = tmem_a ? kMaxB : 8;
+    if (by_bytes > L.b_stages) L.b_stages = by_bytes < max_b ? by_bytes : max_b;
+    const int kps = 1 << kps_log;
+    if (kps > 1) {  // stages of kps k-blocks: as many as kActStageBudget holds (at least 2)
+        const int n = (int)(kActStageBudget / ((size_t)kps * brows * kBK * 2));
+        L.b_stages = n < 2 ? 2 : (n > kMaxB ? kMaxB : n);
+    }
     const size_t a_stage = (size_t)kBM * kBK * 2;
-    const size_t b_bytes = (size_t)L.b_stages * brows * kBK * 2;
+    const size_t b_bytes = (size_t)L.b_stages * kps * brows * kBK * 2;
     const size_t slot = (size_t)8 * chunk_bytes(dt);
-    const size_t misc = 64 * 8 + 16 + 1024;
+    const size_t misc = kBars * 8 + 16 + 1024;
     L.pslots = 2;
     size_t avail = kLimit > b_bytes + misc + 2 * slot ? kLimit - b_bytes - misc - 2 * slot : 0;
+    if (tmem_a) {  // the A stages live in tensor memory: all the rest buys weight slots
+        while (L.pslots < kMaxP && slot <= avail) {
+            L.pslots++;
+            avail -= slot;
+        }
+        L.a_stages = 0;
+        L.a = 0;
+        L.b = 0;
+        size_t o = b_bytes;
+        L.packed = o;
+        o += (size_t)L.pslots * slot;
+        o = (o + 15) / 16 * 16;
+        L.bars = o;
+        o += kBars * 8;
+        L.tmem_slot = o;
+        o += 16;
+        L.total = o + 1024;
+        return L;
+    }
     int na = (int)(avail / a_stage);
-    if (na > kMaxA) na = kMaxA;
+    if (na > kMaxASmem) na = kMaxASmem;
     // leftover room buys a third and fourth weight slot
     while (L.pslots < kMaxP && na >= 3 && (size_t)na * a_stage + slot <= avail) {
         L.pslots++;
@@ -484,7 +613,7 @@ __host__ __device__ inline GemmSmem gemm_smem(int dt, int bn, int terms) {
     o += (size_t)L.pslots * slot;
     o = (o + 15) / 16 * 16;
     L.bars = o;
-    o += 64 * 8;
+    o += kBars * 8;
     L.tmem_slot = o;
     o += 16;
     L.total = o + 1024;  // slack to align the base to 1024
@@ -636,6 +765,73 @@ __device__ __forceinline__ bool dequant_group_single(const GemmArgs &p, uint8_t 
     return true;
 }
 
+// A in tensor memory: dequantiser warp w (1 .. 16) fills k-block
+// J = (w - 1) / 4 of every chunk for the 32 rows of its lane quadrant
+// (w % 4, the tensor-memory lanes a warp may write), one weight row per
+// thread, all 64 values; stages of kTmemStage columns from ta0, chunk c's
+// k-block J in stage 4 (c % NC) + J.  No shared-memory A tile, swizzle or
+// proxy fence: the values go from registers to tensor memory
+// (tcgen05.st), and the MMA reads A from there.
+template <int DT, int J>
+__device__ __forceinline__ bool dequant_tmem(uint8_t *pk, uint32_t bar0, uint32_t ta0, int row, int ntiles,
+                                             int nchunks, int NP, int NC, int lane) {
+    constexpr int CB = chunk_bytes(DT);
+    auto PF = [&](int s) { return bar0 + 8 * (0 + s); };
+    auto PE = [&](int s) { return bar0 + 8 * (kMaxP + s); };
+    auto AF = [&](int s) { return bar0 + 8 * (2 * kMaxP + s); };
+    auto AE = [&](int s) { return bar0 + 8 * (2 * kMaxP + kMaxA + s); };
+    int s = 0, sc = 0;  // packed slot, stage chunk (chunk c % NC), with their phases
+    uint32_t sph = 0, aph = 0;
+    const bool live = row < ntiles * 16;
+    for (int c = 0; c < nchunks; c++) {
+        if (!mbar_wait(PF(s), sph)) return false;
+        uint32_t v[32];  // column i of the k-block: values 2 i, 2 i + 1
+        if (live) {
+            const uint8_t *slot = pk + (size_t)s * 8 * CB;
+            RowHalf<DT> r0;
+            r0.template begin1<J>(slot, row, 0);
+            RowHalf<DT> r1 = r0;
+            r1.hf = 1;
+            if (DT == GGUF_Q6_K) r1.template begin1<J>(slot, row, 1);
+            uint32_t h[16];
+            int cc[4];
+            r0.template compute<J>(h, cc);
+#pragma unroll
+            for (int i = 0; i < 4; i++)
+#pragma unroll
+                for (int u = 0; u < 4; u++) v[4 * cc[i] + u] = h[4 * i + u];
+            r1.template compute<J>(h, cc);
+#pragma unroll
+            for (int i = 0; i < 4; i++)
+#pragma unroll
+                for (int u = 0; u < 4; u++) v[4 * cc[i] + u] = h[4 * i + u];
+        } else {  // rows past the weight (their outputs are not stored)
+#pragma unroll
+            for (int i = 0; i < 32; i++) v[i] = 0u;
+        }
+        const int st = 4 * sc + J;
+        if (c >= NC && !mbar_wait(AE(st), aph ^ 1)) return false;  // the MMAs of chunk c - NC are done
+        tc_fence_after();
+        tmem_st32(ta0 + (uint32_t)st * kTmemStage, v);
+        asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) {
+            mbar_arrive(AF(st));
+            mbar_arrive(PE(s));
+        }
+        if (++sc == NC) {
+            sc = 0;
+            aph ^= 1;
+        }
+        if (++s == NP) {
+            s = 0;
+            sph ^= 1;
+        }
+    }
+    return true;
+}
+
 template <int DT, int G>
 __device__ __forceinline__ bool dequant_group(const GemmArgs &p, uint8_t *pk, uint8_t *a_st, uint32_t bar0, int row,
                                               int hf, int ntiles, int nchunks, int NP, int NA, int lane) {
@@ -656,9 +852,10 @@ struct GemmGroup {
 };
 struct NoGroup {};
 
-template <int DT, class Grp>
+template <int DT, class Grp, bool TA>
 __global__ void __launch_bounds__(kThreads, 1)
-    gemm_kernel(const __grid_constant__ CUtensorMap xmap, const GemmArgs p, const __grid_constant__ Grp q) {
+    gemm_kernel(const __grid_constant__ CUtensorMap xmap, const __grid_constant__ CUtensorMap wmap, const GemmArgs p,
+                const __grid_constant__ Grp q) {
     constexpr int CB = chunk_bytes(DT);
     constexpr bool kGrouped = std::is_same<Grp, GemmGroup>::value;
     extern __shared__ uint8_t smem_raw[];
@@ -667,8 +864,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint8_t *smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
     const int bn = p.bn;
     const int terms = p.lo_row ? 2 : 1;
-    const GemmSmem L = gemm_smem(DT, bn, terms);
-    const int NA = L.a_stages, NB = L.b_stages, NP = L.pslots;
+    const int KL = p.kps_log, KPS = 1 << KL;  // k-blocks per activation stage
+    const GemmSmem L = gemm_smem(DT, bn, terms, TA, KL);
+    const int NB = L.b_stages, NP = L.pslots;
     uint8_t *a_st = smem + L.a;
     uint8_t *b_st = smem + L.b;
     uint8_t *pk = smem + L.packed;
@@ -714,8 +912,16 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int ch0 = kGrouped ? 0 : sz * p.g.n_chunks / p.splits;
     const int nchunks = (kGrouped ? p.g.n_chunks : (sz + 1) * p.g.n_chunks / p.splits) - ch0;
     const int nkb = nchunks * 4;
-    const int MW = min(mma_warps(bn, terms), min(NA, NB));  // an issuer per stage at most
-    const uint32_t acc_cols = tmem_cols(terms * bn), ncols = acc_cols * (uint32_t)MW;
+    // MMA issuers (an issuer per stage at most), their accumulators from
+    // column 0; with A in tensor memory (TA) the stages follow them, at
+    // least 256 columns, in whole chunks (4 k-blocks)
+    const uint32_t acc_cols = tmem_cols(terms * bn);
+    int MW = min(mma_warps(bn, terms), NB);
+    if (TA) MW = min(MW, (int)(256u / acc_cols));
+    else MW = min(MW, L.a_stages);
+    const uint32_t a_col = TA ? acc_cols * (uint32_t)MW : 0u;
+    const int NA = TA ? min((int)((kTmemCols - a_col) / kTmemStage) & ~3, kMaxA) : L.a_stages;
+    const uint32_t ncols = TA ? kTmemCols : acc_cols * (uint32_t)MW;
 
     if (tid == 0) {
         for (int s = 0; s < NP; s++) {
@@ -723,12 +929,12 @@ __global__ void __launch_bounds__(kThreads, 1)
             mbar_init(PE(s), kDqWarps);
         }
         for (int s = 0; s < NA; s++) {
-            mbar_init(AF(s), kDqWarps / 2);  // one group fills a stage
+            mbar_init(AF(s), TA ? 4 : kDqWarps / 2);  // four quadrant warps / one group fill a stage
             mbar_init(AE(s), 1);
         }
         for (int s = 0; s < NB; s++) {
             mbar_init(BF(s), 1);
-            mbar_init(BE(s), 1);
+            mbar_init(BE(s), min(MW, KPS));  // each issuer with k-blocks in the stage commits once
         }
         mbar_init(ACC, MW);  // each MMA warp's final commit
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
@@ -756,10 +962,15 @@ __global__ void __launch_bounds__(kThreads, 1)
                     ok = false;
                     break;
                 }
-                mbar_expect_tx(PF(s), (uint32_t)(ntiles * CB));
-                for (int t = 0; t < ntiles; t++)
-                    bulk_g2s(smem_u32(pk + (size_t)(s * 8 + t) * CB),
-                             wt + ((size_t)(tile0 + t) * p.g.n_chunks + ch0 + c) * CB, CB, PF(s));
+                if (kGrouped) {  // one bulk copy per tile (each entry its own weight)
+                    mbar_expect_tx(PF(s), (uint32_t)(ntiles * CB));
+                    for (int t = 0; t < ntiles; t++)
+                        bulk_g2s(smem_u32(pk + (size_t)(s * 8 + t) * CB),
+                                 wt + ((size_t)(tile0 + t) * p.g.n_chunks + ch0 + c) * CB, CB, PF(s));
+                } else {  // the 8 tiles' chunk in one tensor copy (tiles past the weight read as zeros)
+                    mbar_expect_tx(PF(s), (uint32_t)(8 * CB));
+                    tma_4d(smem_u32(pk + (size_t)s * 8 * CB), &wmap, ch0 + c, tile0, PF(s));
+                }
                 if (++s == NP) {
                     s = 0;
                     ph ^= 1;
@@ -771,7 +982,27 @@ __global__ void __launch_bounds__(kThreads, 1)
     } else if (warp == kActWarp) {
         // activation k-blocks: the prep kernel just before this one writes Xh
         asm volatile("griddepcontrol.wait;" ::: "memory");
-        if (lane == 0) {
+        if (lane == 0 && KPS > 1) {
+            // one copy per stage: kps k-blocks x terms x bn rows
+            const uint32_t sbytes = (uint32_t)(terms * bn * kBK * 2) << KL;
+            const int nst = nkb >> KL;
+            int cs = 0, st = 0;
+            uint32_t ph = 0;
+            for (; cs < nst; cs++) {
+                if (cs >= NB && !mbar_wait(BE(st), ph ^ 1)) {
+                    ok = false;
+                    break;
+                }
+                mbar_expect_tx(BF(st), sbytes);
+                tma_act4(smem_u32(b_st + (size_t)st * sbytes), &xmap, tok0, 4 * ch0 + (cs << KL), BF(st));
+                if (++st == NB) {
+                    st = 0;
+                    ph ^= 1;
+                }
+            }
+            if (!ok)
+                for (int u = max(0, cs - NB); u < cs; u++) mbar_wait(BF(u % NB), (u / NB) & 1);
+        } else if (lane == 0) {
             int kb = 0, st = 0;
             uint32_t ph = 0;
             for (; kb < nkb; kb++) {
@@ -796,6 +1027,17 @@ __global__ void __launch_bounds__(kThreads, 1)
             if (!ok)
                 for (int u = max(0, kb - NB); u < kb; u++) mbar_wait(BF(u % NB), (u / NB) & 1);
         }
+    } else if (TA && warp >= 1 && warp <= kDqWarps) {
+        const int qd = warp & 3, j = (warp - 1) >> 2;
+        const int row = 32 * qd + lane;
+        const uint32_t ta0 = tmem + ((uint32_t)(32 * qd) << 16) + a_col;
+        const int NC = NA / 4;
+        switch (j) {
+        case 0: ok = dequant_tmem<DT, 0>(pk, bar0, ta0, row, ntiles, nchunks, NP, NC, lane); break;
+        case 1: ok = dequant_tmem<DT, 1>(pk, bar0, ta0, row, ntiles, nchunks, NP, NC, lane); break;
+        case 2: ok = dequant_tmem<DT, 2>(pk, bar0, ta0, row, ntiles, nchunks, NP, NC, lane); break;
+        default: ok = dequant_tmem<DT, 3>(pk, bar0, ta0, row, ntiles, nchunks, NP, NC, lane); break;
+        }
     } else if (warp >= 1 && warp <= kDqWarps) {
         // dequantisers: two groups of eight warps take alternate k-blocks
         // (each warp has two k-blocks' time for its chain of waits, loads,
@@ -811,42 +1053,55 @@ __global__ void __launch_bounds__(kThreads, 1)
         // MMA issuer w takes k-blocks w, w + MW, ... into its own accumulator
         // (columns w * acc_cols ..); per k-block, bn / 256 (at least one)
         // sub-accumulators of up to 256 columns, 4 instructions of K = 16.
-        // One lane issues; descriptors advance by 32 bytes (2 in the >> 4
-        // address field) per K = 16 step and by a whole stage per stage.
+        // The whole warp runs the loop, one elected lane issues; descriptors
+        // advance by 32 bytes (2 in the >> 4 address field) per K = 16 step
+        // and by a whole stage per stage.
         const int w = warp - kMmaWarp;
         const int nsub = nmma > 256 ? nmma / 256 : 1, nw = nmma > 256 ? 256 : nmma;
         const uint32_t idesc = idesc_f16(nw);
         const uint32_t acc = tmem + (uint32_t)w * acc_cols;
-        if (lane == 0) {
+        {
             const uint64_t da0 = sw128_desc(smem_u32(a_st)), db0 = sw128_desc(smem_u32(b_st));
             const uint64_t a_step = (uint64_t)(kBM * kBK * 2) >> 4, b_step = (uint64_t)(terms * bn * kBK * 2) >> 4;
             const uint64_t h_step = (uint64_t)(256 * kBK * 2) >> 4;
-            int sa = w, sb = w;  // stages of k-block kb = w (MW <= NA, NB)
+            // A stage of k-block kb = w; activation stage sb of stage index bi (k-blocks bi * KPS ..)
+            int sa = w, sb = 0, bi = 0;
             uint32_t aph = 0, bph = 0;
+            const uint64_t bs_step = b_step << KL;
             for (int kb = w; kb < nkb; kb += MW) {
-                if (!mbar_wait(AF(sa), aph) || !mbar_wait(BF(sb), bph)) {
+                for (; bi < (kb >> KL); bi++)
+                    if (++sb == NB) {
+                        sb = 0;
+                        bph ^= 1;
+                    }
+                const bool got = mbar_wait(AF(sa), aph) && mbar_wait(BF(sb), bph);
+                if (!__all_sync(0xffffffffu, got)) {  // (the lanes leave together)
                     ok = false;
                     break;
                 }
                 tc_fence_after();
-                const uint64_t da = da0 + (uint64_t)sa * a_step, db = db0 + (uint64_t)sb * b_step;
-                for (int h = 0; h < nsub; h++) {
+                const uint64_t da = da0 + (uint64_t)sa * a_step,
+                               db = db0 + (uint64_t)sb * bs_step + (uint64_t)(kb & (KPS - 1)) * b_step;
+                if (TA) {
+                    const uint32_t ta = tmem + a_col + (uint32_t)sa * kTmemStage;
 #pragma unroll
-                    for (int k = 0; k < kBK / 16; k++)  // 16 fp16 = 32 bytes per instruction
-                        umma_f16(acc + (uint32_t)(h * 256), da + 2 * k, db + (uint64_t)h * h_step + 2 * k, idesc,
-                                 (kb != w || k) ? 1u : 0u);
+                    for (int k = 0; k < kBK / 16; k++)  // 16 fp16 = 8 columns of A, 32 bytes of B
+                        umma_f16_ta(acc, ta + 8 * k, db + 2 * k, idesc, (kb != w || k) ? 1u : 0u);
+                } else {
+                    for (int h = 0; h < nsub; h++) {
+#pragma unroll
+                        for (int k = 0; k < kBK / 16; k++)  // 16 fp16 = 32 bytes per instruction
+                            umma_f16(acc + (uint32_t)(h * 256), da + 2 * k, db + (uint64_t)h * h_step + 2 * k,
+                                     idesc, (kb != w || k) ? 1u : 0u);
+                    }
                 }
                 umma_commit(AE(sa));
-                umma_commit(BE(sb));
+                // this issuer's last k-block of the stage: it may refill once these MMAs are done
+                if (((kb + MW) >> KL) != (kb >> KL) || kb + MW >= nkb) umma_commit(BE(sb));
                 sa += MW;
                 if (sa >= NA) {
                     sa -= NA;
                     aph ^= 1;
-                }
-                sb += MW;
-                if (sb >= NB) {
-                    sb -= NB;
-                    bph ^= 1;
                 }
             }
             umma_commit(ACC);  // arrives once this warp's MMAs above have completed
@@ -954,11 +1209,11 @@ EncodeTiled encode_fn() {
     return fn;
 }
 
-template <int DT, class Grp>
-cudaError_t launch_dt(const CUtensorMap &map, const GemmArgs &a, const Grp &q, dim3 grid, size_t smem,
-                      cudaStream_t s) {
+template <int DT, class Grp, bool TA>
+cudaError_t launch_dt(const CUtensorMap &map, const CUtensorMap &wmap, const GemmArgs &a, const Grp &q, dim3 grid,
+                      size_t smem, cudaStream_t s) {
     static std::atomic<unsigned long long> done{0};
-    auto kern = gemm_kernel<DT, Grp>;
+    auto kern = gemm_kernel<DT, Grp, TA>;
     int dev = 0;
     cudaError_t e = cudaGetDevice(&dev);
     if (e != cudaSuccess) return e;
@@ -984,20 +1239,35 @@ cudaError_t launch_dt(const CUtensorMap &map, const GemmArgs &a, const Grp &q, d
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    return cudaLaunchKernelEx(&cfg, kern, map, a, q);
+    return cudaLaunchKernelEx(&cfg, kern, map, wmap, a, q);
 }
 
-template <class Grp>
-cudaError_t launch_any(int dt, const CUtensorMap &map, const GemmArgs &a, const Grp &q, dim3 grid, size_t smem,
-                       cudaStream_t s) {
+template <class Grp, bool TA>
+cudaError_t launch_ta(int dt, const CUtensorMap &map, const CUtensorMap &wmap, const GemmArgs &a, const Grp &q,
+                      dim3 grid, size_t smem, cudaStream_t s) {
     switch (dt) {
-    case GGUF_Q4_K: return launch_dt<GGUF_Q4_K>(map, a, q, grid, smem, s);
-    case GGUF_Q4_0: return launch_dt<GGUF_Q4_0>(map, a, q, grid, smem, s);
-    case GGUF_Q8_0: return launch_dt<GGUF_Q8_0>(map, a, q, grid, smem, s);
-    case GGUF_Q6_K: return launch_dt<GGUF_Q6_K>(map, a, q, grid, smem, s);
-    case GGUF_Q5_K: return launch_dt<GGUF_Q5_K>(map, a, q, grid, smem, s);
+    case GGUF_Q4_K: return launch_dt<GGUF_Q4_K, Grp, TA>(map, wmap, a, q, grid, smem, s);
+    case GGUF_Q4_0: return launch_dt<GGUF_Q4_0, Grp, TA>(map, wmap, a, q, grid, smem, s);
+    case GGUF_Q8_0: return launch_dt<GGUF_Q8_0, Grp, TA>(map, wmap, a, q, grid, smem, s);
+    case GGUF_Q6_K: return launch_dt<GGUF_Q6_K, Grp, TA>(map, wmap, a, q, grid, smem, s);
+    case GGUF_Q5_K: return launch_dt<GGUF_Q5_K, Grp, TA>(map, wmap, a, q, grid, smem, s);
     default: return cudaErrorInvalidValue;
     }
+}
+
+// A in tensor memory when the accumulators leave it room: 256 columns of
+// accumulator at most (token tiles up to 256 one-term / 128 two-term
+// columns); the 512-token tile keeps the shared-memory A tile.
+inline bool tmem_a(int bn, int terms) { return tmem_cols(terms * bn) <= 256; }
+
+template <class Grp>
+cudaError_t launch_any(int dt, const CUtensorMap &map, const CUtensorMap &wmap, const GemmArgs &a, const Grp &q,
+                       dim3 grid, int terms, cudaStream_t s) {
+    const bool ta = tmem_a(a.bn, terms);
+    const GemmSmem lay = gemm_smem(dt, a.bn, terms, ta, a.kps_log);
+    if (lay.pslots < 2) return cudaErrorInvalidConfiguration;
+    return ta ? launch_ta<Grp, true>(dt, map, wmap, a, q, grid, lay.total, s)
+              : launch_ta<Grp, false>(dt, map, wmap, a, q, grid, lay.total, s);
 }
 
 // Tensor map of the fp16 activations [rows][k] (128-byte swizzle, boxes of
@@ -1010,6 +1280,44 @@ cudaError_t act_map(CUtensorMap *map, const void *xh, int rows, int64_t k, int b
     const cuuint32_t box[2] = {(cuuint32_t)kBK, (cuuint32_t)box_rows};
     const cuuint32_t estr[2] = {1, 1};
     CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void *>(xh), dims, strides, box, estr,
+                     CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                     CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS ? cudaSuccess : cudaErrorInvalidValue;
+}
+
+// Tensor map of a T16 weight as 4-d uint8: (piece bytes, pieces of a chunk,
+// chunks, tiles), so that one copy with box (piece, pieces, 1, 8) brings one
+// chunk of 8 consecutive tiles, tile by tile, as the shared-memory slot holds
+// them.  A piece is the largest multiple of 16 bytes up to 256 dividing the
+// chunk (256 for Q4_K / Q4_0 / Q8_0 / Q5_K, 240 for Q6_K's 3360).
+cudaError_t weight_map(CUtensorMap *map, const uint8_t *tiles, const Geometry &g, int dt) {
+    EncodeTiled enc = encode_fn();
+    if (!enc) return cudaErrorNotSupported;
+    const int cb = chunk_bytes(dt);
+    int ip = 256;
+    while (ip > 16 && cb % ip) ip -= 16;
+    const cuuint64_t dims[4] = {(cuuint64_t)ip, (cuuint64_t)(cb / ip), (cuuint64_t)g.n_chunks, (cuuint64_t)g.n_tiles};
+    const cuuint64_t strides[3] = {(cuuint64_t)ip, (cuuint64_t)cb, (cuuint64_t)g.n_chunks * (cuuint64_t)cb};
+    const cuuint32_t box[4] = {(cuuint32_t)ip, (cuuint32_t)(cb / ip), 1, 8};
+    const cuuint32_t estr[4] = {1, 1, 1, 1};
+    CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 4, const_cast<uint8_t *>(tiles), dims, strides, box, estr,
+                     CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                     CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS ? cudaSuccess : cudaErrorInvalidValue;
+}
+
+// Tensor map of the fp16 activations [terms][rows][k] as 4-d (64 columns,
+// rows, terms, k-blocks), 128-byte swizzle, box (64, bn, terms, kps): one
+// copy fills an activation stage laid out [k-block][term][row][64], each
+// k-block's rows of both terms one 1024-byte-aligned swizzled tile.
+cudaError_t act_map4(CUtensorMap *map, const void *xh, int rows, int64_t k, int terms, int bn, int kps) {
+    EncodeTiled enc = encode_fn();
+    if (!enc) return cudaErrorNotSupported;
+    const cuuint64_t dims[4] = {(cuuint64_t)kBK, (cuuint64_t)rows, (cuuint64_t)terms, (cuuint64_t)(k / kBK)};
+    const cuuint64_t strides[3] = {(cuuint64_t)k * 2, (cuuint64_t)k * 2 * (cuuint64_t)rows, (cuuint64_t)kBK * 2};
+    const cuuint32_t box[4] = {(cuuint32_t)kBK, (cuuint32_t)bn, (cuuint32_t)terms, (cuuint32_t)kps};
+    const cuuint32_t estr[4] = {1, 1, 1, 1};
+    CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 4, const_cast<void *>(xh), dims, strides, box, estr,
                      CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                      CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     return r == CUDA_SUCCESS ? cudaSuccess : cudaErrorInvalidValue;
@@ -1113,9 +1421,14 @@ cudaError_t launch_gemm(int dt, const uint8_t *tiles, const Geometry &g, const f
     if (e != cudaSuccess) return e;
     CUtensorMap map;
     const int box_rows = bn < 256 ? bn : 256;
-    e = act_map(&map, xh, terms * t_rows, g.n_cols, box_rows);
-    if (e != cudaSuccess) return e;
+    int kl = act_kps_log(bn, terms, tmem_a(bn, terms));
+    if (kl > 0 && act_map4(&map, xh, t_rows, g.n_cols, terms, bn, 1 << kl) != cudaSuccess) kl = 0;
+    if (kl == 0) {
+        e = act_map(&map, xh, terms * t_rows, g.n_cols, box_rows);
+        if (e != cudaSuccess) return e;
+    }
     GemmArgs a;
+    a.kps_log = kl;
     a.lo_row = terms == 2 ? t_rows : 0;
     a.splits = pl.splits;
     a.part = part;
@@ -1129,10 +1442,11 @@ cudaError_t launch_gemm(int dt, const uint8_t *tiles, const Geometry &g, const f
     a.t_rows = t_rows;
     a.bn = bn;
     a.box_rows = box_rows;
-    const GemmSmem lay = gemm_smem(dt, bn, terms);
-    if (lay.pslots < 2) return cudaErrorInvalidConfiguration;
+    CUtensorMap wmap;
+    e = weight_map(&wmap, tiles, g, dt);
+    if (e != cudaSuccess) return e;
     dim3 grid((g.n_tiles + 7) / 8, (t_rows + bn - 1) / bn, pl.splits);
-    e = launch_any(dt, map, a, NoGroup{}, grid, lay.total, s);
+    e = launch_any(dt, map, wmap, a, NoGroup{}, grid, terms, s);
     if (e != cudaSuccess || pl.splits == 1) return e;
     const size_t total = (size_t)t_rows * (size_t)g.n_rows;
     unsigned blocks = (unsigned)((total + 255) / 256);
@@ -1177,6 +1491,7 @@ cudaError_t launch_gemm_grouped(int dt, const uint8_t *const *ws, float *const *
     a.t_rows = 0;
     a.bn = bn;
     a.box_rows = kBox;
+    a.kps_log = 0;
     GemmGroup q;
     for (int z = 0; z < kGemmMaxGroup; z++) {
         q.w[z] = z < n ? ws[z] : nullptr;
@@ -1185,11 +1500,9 @@ cudaError_t launch_gemm_grouped(int dt, const uint8_t *const *ws, float *const *
         if (z < n && (set[z] < 0 || set[z] >= n_sets)) return cudaErrorInvalidValue;
     }
     q.off = off;
-    const GemmSmem lay = gemm_smem(dt, bn, 2);
-    if (lay.pslots < 2) return cudaErrorInvalidConfiguration;
     if ((max_rows + bn - 1) / bn > 65535) return cudaErrorInvalidValue;
     dim3 grid((g.n_tiles + 7) / 8, (max_rows + bn - 1) / bn, n);
-    return launch_any(dt, map, a, q, grid, lay.total, s);
+    return launch_any(dt, map, map, a, q, grid, 2, s);  // (grouped weights: bulk copies, no weight map)
 }
 
 }  // namespace rce
