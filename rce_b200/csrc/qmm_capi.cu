@@ -945,6 +945,8 @@ int rce_qmm_moe_ffn_device(rce_qmm_ctx *ctx, const float *d_x, size_t ldx, size_
     o += al(P * 4);
     const size_t o_off = o;
     o += al((size_t)(n_local + 1) * 4);
+    const size_t o_rw = o;  // route weight of each grouped row (the fused combine's factor)
+    o += al(P * 4);
     const size_t o_xg = o;
     o += al(P * (size_t)d_model * 4);
     const size_t o_g = o;
@@ -975,9 +977,11 @@ int rce_qmm_moe_ffn_device(rce_qmm_ctx *ctx, const float *d_x, size_t ldx, size_
     float *gb = reinterpret_cast<float *>(ws + o_g);
     float *ub = reinterpret_cast<float *>(ws + o_u);
     float *yb = reinterpret_cast<float *>(ws + o_y);
+    float *rw = reinterpret_cast<float *>(ws + o_rw);
 
-    CUDA_TRY(rce::launch_moe_route(d_logits, ld_logits, (int)t_rows, n_experts, top_k, 1, idx, wt, s));
-    CUDA_TRY(rce::launch_moe_plan(idx, (int)P, top_k, expert_begin, expert_end, off, pos, tok, s));
+    // routing and the grouping by expert: one single-CTA launch
+    CUDA_TRY(rce::launch_moe_route_plan(d_logits, ld_logits, (int)t_rows, n_experts, top_k, 1, idx, wt, expert_begin,
+                                        expert_end, off, pos, tok, rw, s));
     // Prefill-sized batches: every local expert's gate and up in one grouped
     // tensor-core launch, the down matmuls in another, the row counts read
     // on the device (no host synchronisation; the call can be captured in a
@@ -989,34 +993,52 @@ int rce_qmm_moe_ffn_device(rce_qmm_ctx *ctx, const float *d_x, size_t ldx, size_
         grouped = gate[e]->dtype == g0->dtype && up[e]->dtype == g0->dtype &&
                   down[e]->dtype == down[expert_begin]->dtype;
     if (grouped) {
+        // Launches: route+plan, gather_prep (also clears the output), the
+        // gate/up matmuls of every local expert with h = silu(g) * u from
+        // their epilogue, h_prep, the down matmuls adding w * y into the
+        // output from their epilogue (at most two route slots per token: a
+        // sum of two is the same in either order, so the atomic adds give
+        // the combine's bits; more slots keep the ordered combine kernel).
         constexpr int kG = rce::kGemmMaxGroup;
         const int32_t *n_rows = off + n_local;
         const int max_rows = (int)t_rows;  // a token picks an expert at most once
         const int rows_hint = (int)(P * (size_t)n_local / (size_t)n_experts);
+        const bool fuse_combine = top_k <= 2;
         void *xh = ws + o_xg, *xh2 = ws + o_xh2;
         float *inv = reinterpret_cast<float *>(ws + o_inv), *inv2 = reinterpret_cast<float *>(ws + o_inv2);
-        const uint8_t *wz[kG];
+        const uint8_t *wz[kG], *w2z[kG];
         float *yz[kG];
         int sz[kG];
-        CUDA_TRY(rce::launch_moe_gather_prep(d_x, ldx, tok, n_rows, (int)P, (int)d_model, xh, inv, s));
-        for (int i0 = 0; i0 < n_local; i0 += kG / 2) {  // entries 2i, 2i + 1: gate and up of local expert i
+        CUDA_TRY(rce::launch_moe_gather_prep(d_x, ldx, tok, n_rows, (int)P, (int)d_model, xh, inv,
+                                             fuse_combine ? d_out : nullptr, ldo, (int)t_rows, s));
+        for (int i0 = 0; i0 < n_local; i0 += kG) {  // entry i: gate and up of local expert i, h into gb
             int n = 0;
-            for (int i = i0; i < n_local && i < i0 + kG / 2; i++) {
-                wz[n] = gate[expert_begin + i]->dev, yz[n] = gb, sz[n++] = i;
-                wz[n] = up[expert_begin + i]->dev, yz[n] = ub, sz[n++] = i;
-            }
+            for (int i = i0; i < n_local && i < i0 + kG; i++)
+                wz[n] = gate[expert_begin + i]->dev, w2z[n] = up[expert_begin + i]->dev, yz[n] = gb, sz[n++] = i;
+            rce::GroupEpi ge;
+            ge.mode = rce::kGroupSwiGLU;
+            ge.ws2 = w2z;
             CUDA_TRY(rce::launch_gemm_grouped(g0->dtype, wz, yz, sz, n, g0->g, xh, inv, (int)P, rows_hint, off,
-                                              n_local, max_rows, (size_t)d_ff, ctx->err_dev, s));
+                                              n_local, max_rows, (size_t)d_ff, ctx->err_dev, s, ge));
         }
-        CUDA_TRY(rce::launch_moe_swiglu_prep(gb, ub, (size_t)d_ff, n_rows, (int)P, (int)d_ff, xh2, inv2, s));
+        CUDA_TRY(rce::launch_moe_h_prep(gb, (size_t)d_ff, n_rows, (int)P, (int)d_ff, xh2, inv2, s));
         const rce_qmm_weight *d0 = down[expert_begin];
+        rce::GroupEpi de;
+        if (fuse_combine) {
+            de.mode = rce::kGroupCombine;
+            de.row_token = tok;
+            de.row_w = rw;
+            de.out = d_out;
+            de.ldo = ldo;
+        }
         for (int i0 = 0; i0 < n_local; i0 += kG) {
             int n = 0;
             for (int i = i0; i < n_local && i < i0 + kG; i++) wz[n] = down[expert_begin + i]->dev, yz[n] = yb, sz[n++] = i;
             CUDA_TRY(rce::launch_gemm_grouped(d0->dtype, wz, yz, sz, n, d0->g, xh2, inv2, (int)P, rows_hint, off,
-                                              n_local, max_rows, (size_t)d_model, ctx->err_dev, s));
+                                              n_local, max_rows, (size_t)d_model, ctx->err_dev, s, de));
         }
-        CUDA_TRY(rce::launch_moe_combine(yb, (int)d_model, pos, wt, (int)t_rows, top_k, d_out, ldo, s));
+        if (!fuse_combine)
+            CUDA_TRY(rce::launch_moe_combine(yb, (int)d_model, pos, wt, (int)t_rows, top_k, d_out, ldo, s));
         return ok();
     }
     // the per-expert row counts size the matmuls below

@@ -846,9 +846,15 @@ __device__ __forceinline__ bool dequant_group(const GemmArgs &p, uint8_t *pk, ui
 // lies past their entry's rows exit at once.
 struct GemmGroup {
     const uint8_t *w[kGemmMaxGroup];
+    const uint8_t *w2[kGemmMaxGroup];  // kGroupSwiGLU: the up weights (w: the gate weights)
     float *y[kGemmMaxGroup];
     int set[kGemmMaxGroup];
     const int32_t *off;
+    int epi;                   // GroupEpilogue
+    const int32_t *row_token;  // kGroupCombine: the token of each activation row
+    const float *row_w;        //   and its route weight
+    float *out;                //   out[token][row] += w * value
+    size_t ldo;
 };
 struct NoGroup {};
 
@@ -884,15 +890,23 @@ __global__ void __launch_bounds__(kThreads, 1)
     const uint32_t ACC = bar0 + 8 * (2 * kMaxP + 2 * kMaxA + 2 * kMaxB);
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    // SwiGLU epilogue (grouped): the CTA's tiles are gate / up tile pairs,
+    // gate and up tile hb + t / 2 at tile t = even / odd, so that a lane
+    // quadrant holds 16 gate rows (lanes 0-15) and the same 16 up rows
+    int gepi = kGroupStore;
+    if constexpr (kGrouped) gepi = q.epi;
+    const bool swiglu = gepi == kGroupSwiGLU;
+    const int hb = blockIdx.x * 4;     // SwiGLU: first gate / up tile of this CTA
     const int tile0 = blockIdx.x * 8;  // first 16-row tile of this CTA
-    const int ntiles = min(8, p.g.n_tiles - tile0);
+    const int ntiles = swiglu ? 2 * min(4, p.g.n_tiles - hb) : min(8, p.g.n_tiles - tile0);
     // this CTA's weight, output and activation rows t_begin + tok0 ..
-    const uint8_t *wt = p.w;
+    const uint8_t *wt = p.w, *wt2 = nullptr;
     float *yo = p.y;
     int t_begin = 0, t_count = p.t_rows;
     if constexpr (kGrouped) {
         const int z = blockIdx.z;
         wt = q.w[z];
+        wt2 = q.w2[z];
         yo = q.y[z];
         t_begin = q.off[q.set[z]];
         t_count = q.off[q.set[z] + 1] - t_begin;
@@ -964,9 +978,12 @@ __global__ void __launch_bounds__(kThreads, 1)
                 }
                 if (kGrouped) {  // one bulk copy per tile (each entry its own weight)
                     mbar_expect_tx(PF(s), (uint32_t)(ntiles * CB));
-                    for (int t = 0; t < ntiles; t++)
+                    for (int t = 0; t < ntiles; t++) {
+                        const uint8_t *src = swiglu ? (t & 1 ? wt2 : wt) : wt;
+                        const int tile = swiglu ? hb + (t >> 1) : tile0 + t;
                         bulk_g2s(smem_u32(pk + (size_t)(s * 8 + t) * CB),
-                                 wt + ((size_t)(tile0 + t) * p.g.n_chunks + ch0 + c) * CB, CB, PF(s));
+                                 src + ((size_t)tile * p.g.n_chunks + ch0 + c) * CB, CB, PF(s));
+                    }
                 } else {  // the 8 tiles' chunk in one tensor copy (tiles past the weight read as zeros)
                     mbar_expect_tx(PF(s), (uint32_t)(8 * CB));
                     tma_4d(smem_u32(pk + (size_t)s * 8 * CB), &wmap, ch0 + c, tile0, PF(s));
@@ -1113,6 +1130,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     // + 31 (the only lanes a warp may read) and one of four column groups
     if (warp >= 1 && warp <= kDqWarps) {
         if (ok && !mbar_wait(ACC, 0)) ok = false;
+        if constexpr (kGrouped) ok = __all_sync(0xffffffffu, ok);  // (the SwiGLU epilogue exchanges values between lanes)
         tc_fence_after();
         const int lane_base = 32 * (warp & 3);
         const int cpg = (ncol / 8 + 3) / 4 * 8;  // columns per group, a multiple of 8
@@ -1135,7 +1153,42 @@ __global__ void __launch_bounds__(kThreads, 1)
                             v[i] = (w || h) ? v[i] + __uint_as_float(r[i]) : __uint_as_float(r[i]);
                     }
                 }
-                if (row < p.g.n_rows) {
+                if (swiglu) {
+                    // h = silu(g) * u for h row hrow: lanes l and l + 16 hold its gate
+                    // and up values; after one exchange each of the two computes h
+                    // for half of the 8 tokens (lane l tokens 0-3, lane l + 16 tokens 4-7)
+                    const int hrow = hb * 16 + 16 * (warp & 3) + (lane & 15);
+                    const bool up_lane = lane & 16;
+                    float g4[4], u4[4];
+#pragma unroll
+                    for (int i = 0; i < 8; i++) {
+                        const int t = t_begin + tok0 + c0 + i;
+                        const float o = c0 + i < live ? v[i] * p.inv_scale[t] : 0.f;
+                        const float other = __shfl_xor_sync(0xffffffffu, o, 16);
+                        if ((i < 4) == !up_lane) {
+                            g4[i & 3] = up_lane ? other : o;
+                            u4[i & 3] = up_lane ? o : other;
+                        }
+                    }
+                    if (hrow < p.g.n_rows)
+#pragma unroll
+                        for (int i4 = 0; i4 < 4; i4++) {
+                            const int i = (up_lane ? 4 : 0) + i4;
+                            if (c0 + i < live)
+                                yo[(size_t)(t_begin + tok0 + c0 + i) * p.ldy + hrow] = __fmul_rn(silu_fast(g4[i4]), u4[i4]);
+                        }
+                } else if (gepi == kGroupCombine) {
+                    if constexpr (kGrouped) {
+                        if (row < p.g.n_rows)
+#pragma unroll
+                            for (int i = 0; i < 8; i++) {
+                                const int t = t_begin + tok0 + c0 + i;
+                                if (c0 + i < live)
+                                    atomicAdd(q.out + (size_t)q.row_token[t] * q.ldo + row,
+                                              __fmul_rn(q.row_w[t], v[i] * p.inv_scale[t]));
+                            }
+                    }
+                } else if (row < p.g.n_rows) {
                     // split-K: this CTA's partial sums, added in order by reduce_splits
                     float *dst = p.splits > 1 ? p.part + (size_t)sz * p.t_rows * p.g.n_rows : yo;
                     const size_t ld = p.splits > 1 ? (size_t)p.g.n_rows : p.ldy;
@@ -1469,7 +1522,8 @@ static int gemm_grouped_bn(int rows, int n_sets, int max_rows) {
 
 cudaError_t launch_gemm_grouped(int dt, const uint8_t *const *ws, float *const *ys, const int *set, int n,
                                 const Geometry &g, const void *xh, const float *inv, int rows, int rows_hint,
-                                const int32_t *off, int n_sets, int max_rows, size_t ldy, int *err, cudaStream_t s) {
+                                const int32_t *off, int n_sets, int max_rows, size_t ldy, int *err, cudaStream_t s,
+                                const GroupEpi &epi) {
     if (n <= 0 || rows <= 0 || max_rows <= 0 || g.n_rows <= 0) return cudaSuccess;
     if (n > kGemmMaxGroup || n_sets <= 0) return cudaErrorInvalidValue;
     if (!encode_fn()) return cudaErrorNotSupported;
@@ -1492,16 +1546,25 @@ cudaError_t launch_gemm_grouped(int dt, const uint8_t *const *ws, float *const *
     a.bn = bn;
     a.box_rows = kBox;
     a.kps_log = 0;
+    if (epi.mode == kGroupSwiGLU && !epi.ws2) return cudaErrorInvalidValue;
+    if (epi.mode == kGroupCombine && (!epi.row_token || !epi.row_w || !epi.out)) return cudaErrorInvalidValue;
     GemmGroup q;
     for (int z = 0; z < kGemmMaxGroup; z++) {
         q.w[z] = z < n ? ws[z] : nullptr;
+        q.w2[z] = z < n && epi.mode == kGroupSwiGLU ? epi.ws2[z] : nullptr;
         q.y[z] = z < n ? ys[z] : nullptr;
         q.set[z] = z < n ? set[z] : 0;
         if (z < n && (set[z] < 0 || set[z] >= n_sets)) return cudaErrorInvalidValue;
     }
     q.off = off;
+    q.epi = epi.mode;
+    q.row_token = epi.row_token;
+    q.row_w = epi.row_w;
+    q.out = epi.out;
+    q.ldo = epi.ldo;
     if ((max_rows + bn - 1) / bn > 65535) return cudaErrorInvalidValue;
-    dim3 grid((g.n_tiles + 7) / 8, (max_rows + bn - 1) / bn, n);
+    // SwiGLU: 4 gate and 4 up tiles per CTA
+    dim3 grid(epi.mode == kGroupSwiGLU ? (g.n_tiles + 3) / 4 : (g.n_tiles + 7) / 8, (max_rows + bn - 1) / bn, n);
     return launch_any(dt, map, map, a, q, grid, 2, s);  // (grouped weights: bulk copies, no weight map)
 }
 

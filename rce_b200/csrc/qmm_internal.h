@@ -145,9 +145,26 @@ cudaError_t launch_gemm(int dt, const uint8_t *tiles, const Geometry &g, const f
 // may hold more than max_rows rows; rows_hint (the expected rows over all
 // sets) sizes the token tile.
 constexpr int kGemmMaxGroup = 32;
+// The grouped launch's epilogue (GroupEpilogue): kGroupStore stores each
+// output row; kGroupSwiGLU takes entry z's gate weight from ws and its up
+// weight from ws2 (same shape), 64 rows of each per CTA, and stores
+// h = silu(gate) * up (the f32 arithmetic of the separate SwiGLU); kGroupCombine
+// adds row_w[r] * y into out[row_token[r]] atomically instead of storing y
+// (out cleared beforehand; exact and order-free for at most two route slots
+// per token, as a + b = b + a and 0 + a = a).
+enum GroupEpilogue { kGroupStore = 0, kGroupSwiGLU = 1, kGroupCombine = 2 };
+struct GroupEpi {
+    int mode = kGroupStore;
+    const uint8_t *const *ws2 = nullptr;  // kGroupSwiGLU: up weights, entry by entry
+    const int32_t *row_token = nullptr;   // kGroupCombine
+    const float *row_w = nullptr;
+    float *out = nullptr;
+    size_t ldo = 0;
+};
 cudaError_t launch_gemm_grouped(int dt, const uint8_t *const *ws, float *const *ys, const int *set, int n,
                                 const Geometry &g, const void *xh, const float *inv, int rows, int rows_hint,
-                                const int32_t *off, int n_sets, int max_rows, size_t ldy, int *err, cudaStream_t s);
+                                const int32_t *off, int n_sets, int max_rows, size_t ldy, int *err, cudaStream_t s,
+                                const GroupEpi &epi = GroupEpi());
 
 // MoE pieces (qmm_moe.cu).  route: per token softmax / top_k / renormalise
 // of router logits [t_rows][ld] into idx, w [t_rows][top_k] (n_experts <=
@@ -157,20 +174,27 @@ cudaError_t launch_gemm_grouped(int dt, const uint8_t *const *ws, float *const *
 // swiglu: h = silu(g) * u.  combine: out[t] = sum_j w[t][j] y[pos[t][j]].
 cudaError_t launch_moe_route(const float *logits, size_t ld, int t_rows, int n_experts, int top_k, int normalize,
                              int32_t *idx, float *w, cudaStream_t s);
-cudaError_t launch_moe_plan(const int32_t *idx, int pairs, int top_k, int e_begin, int e_end, int32_t *offsets,
-                            int32_t *pos, int32_t *token, cudaStream_t s);
+cudaError_t launch_moe_plan(const int32_t *idx, const float *w, int pairs, int top_k, int e_begin, int e_end,
+                            int32_t *offsets, int32_t *pos, int32_t *token, float *row_w, cudaStream_t s);
+// route then plan in one single-CTA launch (also row_w[row] = w[pair] when
+// row_w is given)
+cudaError_t launch_moe_route_plan(const float *logits, size_t ld, int t_rows, int n_experts, int top_k, int normalize,
+                                  int32_t *idx, float *w, int e_begin, int e_end, int32_t *offsets, int32_t *pos,
+                                  int32_t *token, float *row_w, cudaStream_t s);
 cudaError_t launch_moe_gather(const float *x, size_t ldx, const int32_t *token, int rows, int d_model, float *xg,
                               cudaStream_t s);
 cudaError_t launch_swiglu(const float *g, const float *u, float *h, size_t n, cudaStream_t s);
 // The GEMM inputs of the grouped path, for rows r < *n_rows (a device
-// count; max_rows bounds it): gather_prep v = x[token[r]], swiglu_prep
-// v = silu(g[r]) * u[r] (g, u rows of ld floats), each as two fp16 terms
-// xh[r] = fp16(v * s_r) and xh[max_rows + r] = fp16(v * s_r - xh[r]); s_r a
-// power of two with |v * s_r| < 2^14, inv[r] = 1 / s_r.
+// count; max_rows bounds it): gather_prep v = x[token[r]], h_prep v = h[r]
+// (rows of ld floats), each as two fp16 terms xh[r] = fp16(v * s_r) and
+// xh[max_rows + r] = fp16(v * s_r - xh[r]); s_r a power of two with
+// |v * s_r| < 2^14, inv[r] = 1 / s_r.  gather_prep also clears rows
+// [0, zero_rows) of zero (d_model floats each) when zero is given.
 cudaError_t launch_moe_gather_prep(const float *x, size_t ldx, const int32_t *token, const int32_t *n_rows,
-                                   int max_rows, int d_model, void *xh, float *inv, cudaStream_t s);
-cudaError_t launch_moe_swiglu_prep(const float *g, const float *u, size_t ld, const int32_t *n_rows, int max_rows,
-                                   int d_ff, void *xh, float *inv, cudaStream_t s);
+                                   int max_rows, int d_model, void *xh, float *inv, float *zero, size_t ldz,
+                                   int zero_rows, cudaStream_t s);
+cudaError_t launch_moe_h_prep(const float *h, size_t ld, const int32_t *n_rows, int max_rows, int d_ff, void *xh,
+                              float *inv, cudaStream_t s);
 cudaError_t launch_moe_combine(const float *y, int d_model, const int32_t *pos, const float *w, int t_rows, int top_k,
                                float *out, size_t ldo, cudaStream_t s);
 

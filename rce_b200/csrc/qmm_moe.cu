@@ -24,10 +24,8 @@ namespace {
 // one IEEE division per probability, the selected weights summed in rank
 // order.  exp is the device expf (the reference uses the platform libm; the
 // two may differ in the last bit).
-__global__ void route_kernel(const float *logits, size_t ld, int t_rows, int n_experts, int top_k, int normalize,
-                             int32_t *idx, float *w) {
-    const int t = blockIdx.x * blockDim.x + threadIdx.x;
-    if (t >= t_rows) return;
+__device__ __forceinline__ void route_token(const float *logits, size_t ld, int t, int n_experts, int top_k,
+                                            int normalize, int32_t *idx, float *w) {
     const float *l = logits + (size_t)t * ld;
     float mx = -INFINITY;
     for (int e = 0; e < n_experts; e++) mx = fmaxf(mx, l[e]);
@@ -61,13 +59,21 @@ __global__ void route_kernel(const float *logits, size_t ld, int t_rows, int n_e
     }
 }
 
+__global__ void route_kernel(const float *logits, size_t ld, int t_rows, int n_experts, int top_k, int normalize,
+                             int32_t *idx, float *w) {
+    const int t = blockIdx.x * blockDim.x + threadIdx.x;
+    if (t < t_rows) route_token(logits, ld, t, n_experts, top_k, normalize, idx, w);
+}
+
 // One CTA: rows for the (token, slot) pairs routed to experts [e_begin,
 // e_end), grouped by expert.  offsets[i] = first row of local expert i
 // (offsets[n_local] = rows in all); pos[pair] = its row or -1; token[row] =
 // the pair's token.  The order of rows inside an expert is not defined (it
 // does not change any result: every row of a matmul is computed on its own).
-__global__ void __launch_bounds__(1024) plan_kernel(const int32_t *idx, int pairs, int top_k, int e_begin,
-                                                    int e_end, int32_t *offsets, int32_t *pos, int32_t *token) {
+// With w, also row_w[row] = the pair's route weight (the fused combine's
+// factor).
+__device__ __forceinline__ void plan_cta(const int32_t *idx, const float *w, int pairs, int top_k, int e_begin,
+                                         int e_end, int32_t *offsets, int32_t *pos, int32_t *token, float *row_w) {
     extern __shared__ int32_t cnt[];  // [n_local + 1]
     const int n_local = e_end - e_begin;
     for (int i = threadIdx.x; i <= n_local; i += blockDim.x) cnt[i] = 0;
@@ -94,8 +100,27 @@ __global__ void __launch_bounds__(1024) plan_kernel(const int32_t *idx, int pair
             const int row = cnt[e - e_begin] + pos[p];
             pos[p] = row;
             token[row] = p / top_k;
+            if (row_w) row_w[row] = w[p];
         }
     }
+}
+
+__global__ void __launch_bounds__(1024) plan_kernel(const int32_t *idx, const float *w, int pairs, int top_k,
+                                                    int e_begin, int e_end, int32_t *offsets, int32_t *pos,
+                                                    int32_t *token, float *row_w) {
+    plan_cta(idx, w, pairs, top_k, e_begin, e_end, offsets, pos, token, row_w);
+}
+
+// route_kernel then plan_kernel in one CTA: every token routed (a thread per
+// token, in turn), then the grouping; one launch instead of two.
+__global__ void __launch_bounds__(1024) route_plan_kernel(const float *logits, size_t ld, int t_rows, int n_experts,
+                                                          int top_k, int normalize, int32_t *idx, float *w,
+                                                          int e_begin, int e_end, int32_t *offsets, int32_t *pos,
+                                                          int32_t *token, float *row_w) {
+    for (int t = threadIdx.x; t < t_rows; t += blockDim.x)
+        route_token(logits, ld, t, n_experts, top_k, normalize, idx, w);
+    __syncthreads();  // (the routes are this CTA's own global writes)
+    plan_cta(idx, w, t_rows * top_k, top_k, e_begin, e_end, offsets, pos, token, row_w);
 }
 
 // xg[row] = x[token[row]], d_model floats per row.
@@ -107,20 +132,6 @@ __global__ void gather_kernel(const float *x, size_t ldx, const int32_t *token, 
     for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < d_model; i += gridDim.x * blockDim.x) dst[i] = src[i];
 }
 
-// silu as moe_ffn_forward's expert computes it (rce-qwen36-moe/src/lib.rs:649-656):
-// x / (1 + exp(-x)) for x >= 0, x e^x / (1 + e^x) below, each operation
-// rounded on its own.
-__device__ __forceinline__ float silu_ref(float x) {
-    if (x >= 0.f) {
-        const float den = __fadd_rn(1.f, expf(-x));
-        return __fdiv_rn(x, den);
-    }
-    const float e = expf(x);
-    const float num = __fmul_rn(x, e);
-    const float den = __fadd_rn(1.f, e);
-    return __fdiv_rn(num, den);
-}
-
 // h = silu(g) * u, element by element (h may be g).
 __global__ void swiglu_kernel(const float *g, const float *u, float *h, size_t n) {
     for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x)
@@ -129,26 +140,29 @@ __global__ void swiglu_kernel(const float *g, const float *u, float *h, size_t n
 
 // GEMM input of the grouped path, row r = blockIdx.x: x[token[r]] scaled and
 // rounded to two fp16 terms (high in xh, low in xl; the gather and the dense
-// prep in one pass).
+// prep in one pass).  With zero, block r < zero_rows also clears row r of
+// zero (the output the fused combine adds into).
 __global__ void __launch_bounds__(kPrepThreads) gather_prep_kernel(const float *x, size_t ldx, const int32_t *token,
                                                                     const int32_t *n_rows, int d_model, __half *xh,
-                                                                    float *inv, __half *xl) {
+                                                                    float *inv, __half *xl, float *zero, size_t ldz,
+                                                                    int zero_rows) {
     const int r = blockIdx.x;
+    if (zero && r < zero_rows)
+        for (int i = threadIdx.x; i < d_model; i += kPrepThreads) zero[(size_t)r * ldz + i] = 0.f;
     if (r >= *n_rows) return;
     const float *src = x + (size_t)token[r] * ldx;
     prep_row([&](int i) { return src[i]; }, d_model, xh + (size_t)r * d_model, inv + r, xl + (size_t)r * d_model);
 }
 
-// GEMM input of the down matmul, row r = blockIdx.x: h = silu(g) * u exactly
-// as swiglu_kernel computes it, scaled and rounded to two fp16 terms.
-__global__ void __launch_bounds__(kPrepThreads) swiglu_prep_kernel(const float *g, const float *u, size_t ld,
-                                                                    const int32_t *n_rows, int d_ff, __half *xh,
-                                                                    float *inv, __half *xl) {
+// GEMM input of the down matmul when the gate/up launch wrote h itself (its
+// SwiGLU epilogue): row r = blockIdx.x of h, scaled and rounded to two fp16
+// terms.
+__global__ void __launch_bounds__(kPrepThreads) h_prep_kernel(const float *h, size_t ld, const int32_t *n_rows,
+                                                               int d_ff, __half *xh, float *inv, __half *xl) {
     const int r = blockIdx.x;
     if (r >= *n_rows) return;
-    const float *gr = g + (size_t)r * ld, *ur = u + (size_t)r * ld;
-    prep_row([&](int i) { return __fmul_rn(silu_ref(gr[i]), ur[i]); }, d_ff, xh + (size_t)r * d_ff, inv + r,
-             xl + (size_t)r * d_ff);
+    const float *hr = h + (size_t)r * ld;
+    prep_row([&](int i) { return hr[i]; }, d_ff, xh + (size_t)r * d_ff, inv + r, xl + (size_t)r * d_ff);
 }
 
 // out[t] = sum over route slots j (in order, from 0) of w[t][j] * y[pos[t][j]],
@@ -176,13 +190,26 @@ cudaError_t launch_moe_route(const float *logits, size_t ld, int t_rows, int n_e
     return cudaGetLastError();
 }
 
-cudaError_t launch_moe_plan(const int32_t *idx, int pairs, int top_k, int e_begin, int e_end, int32_t *offsets,
-                            int32_t *pos, int32_t *token, cudaStream_t s) {
+cudaError_t launch_moe_plan(const int32_t *idx, const float *w, int pairs, int top_k, int e_begin, int e_end,
+                            int32_t *offsets, int32_t *pos, int32_t *token, float *row_w, cudaStream_t s) {
     const int n_local = e_end - e_begin;
     if (pairs <= 0 || n_local < 1) return cudaErrorInvalidValue;
     const size_t smem = (size_t)(n_local + 1) * sizeof(int32_t);
     if (smem > 48 * 1024) return cudaErrorInvalidValue;
-    plan_kernel<<<1, 1024, smem, s>>>(idx, pairs, top_k, e_begin, e_end, offsets, pos, token);
+    plan_kernel<<<1, 1024, smem, s>>>(idx, w, pairs, top_k, e_begin, e_end, offsets, pos, token, row_w);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_moe_route_plan(const float *logits, size_t ld, int t_rows, int n_experts, int top_k, int normalize,
+                                  int32_t *idx, float *w, int e_begin, int e_end, int32_t *offsets, int32_t *pos,
+                                  int32_t *token, float *row_w, cudaStream_t s) {
+    const int n_local = e_end - e_begin;
+    if (t_rows <= 0 || n_local < 1) return cudaErrorInvalidValue;
+    if (n_experts < 1 || n_experts > 256 || top_k < 1 || top_k > n_experts) return cudaErrorInvalidValue;
+    const size_t smem = (size_t)(n_local + 1) * sizeof(int32_t);
+    if (smem > 48 * 1024) return cudaErrorInvalidValue;
+    route_plan_kernel<<<1, 1024, smem, s>>>(logits, ld, t_rows, n_experts, top_k, normalize, idx, w, e_begin, e_end,
+                                            offsets, pos, token, row_w);
     return cudaGetLastError();
 }
 
@@ -203,20 +230,21 @@ cudaError_t launch_swiglu(const float *g, const float *u, float *h, size_t n, cu
 }
 
 cudaError_t launch_moe_gather_prep(const float *x, size_t ldx, const int32_t *token, const int32_t *n_rows,
-                                   int max_rows, int d_model, void *xh, float *inv, cudaStream_t s) {
+                                   int max_rows, int d_model, void *xh, float *inv, float *zero, size_t ldz,
+                                   int zero_rows, cudaStream_t s) {
     if (max_rows <= 0) return cudaSuccess;
+    if (zero && zero_rows > max_rows) return cudaErrorInvalidValue;
     __half *hi = static_cast<__half *>(xh);
     gather_prep_kernel<<<max_rows, kPrepThreads, 0, s>>>(x, ldx, token, n_rows, d_model, hi, inv,
-                                                          hi + (size_t)max_rows * d_model);
+                                                          hi + (size_t)max_rows * d_model, zero, ldz, zero_rows);
     return cudaGetLastError();
 }
 
-cudaError_t launch_moe_swiglu_prep(const float *g, const float *u, size_t ld, const int32_t *n_rows, int max_rows,
-                                   int d_ff, void *xh, float *inv, cudaStream_t s) {
+cudaError_t launch_moe_h_prep(const float *h, size_t ld, const int32_t *n_rows, int max_rows, int d_ff, void *xh,
+                              float *inv, cudaStream_t s) {
     if (max_rows <= 0) return cudaSuccess;
     __half *hi = static_cast<__half *>(xh);
-    swiglu_prep_kernel<<<max_rows, kPrepThreads, 0, s>>>(g, u, ld, n_rows, d_ff, hi, inv,
-                                                          hi + (size_t)max_rows * d_ff);
+    h_prep_kernel<<<max_rows, kPrepThreads, 0, s>>>(h, ld, n_rows, d_ff, hi, inv, hi + (size_t)max_rows * d_ff);
     return cudaGetLastError();
 }
 
