@@ -308,16 +308,34 @@ int rce_qmm_moe_router_device(rce_qmm_ctx *ctx, const float *d_x, size_t ldx, si
  * FFN (for top_k <= 2 bit for bit: adding zeros and swapping two terms
  * round alike).  gate/up/down hold n_experts weight handles each (entries
  * outside the local range may be NULL); gate/up are [d_ff x d_model], down
- * [d_model x d_ff].  Each expert's rows run through mm_batched's dispatch
- * (the decode GEMV below prefill_min_tokens rows, the tensor-core GEMM
- * above).  Device buffers; the call synchronises `stream` once (to size
- * the per-expert matmuls) and grows a per-stream workspace on first use.
- * d_idx / d_w (optional, [t_rows][top_k]) receive the routes. */
+ * [d_model x d_ff].  From prefill_min_tokens tokens (and experts of one
+ * format) the experts run as expert-grouped tensor-core launches with the
+ * row counts read on the device (no host synchronisation: the call can be
+ * captured in a CUDA graph); below, each expert's rows run through
+ * mm_batched's dispatch, sized by row counts the call copies to the host
+ * (one synchronisation of `stream`).  Device buffers; a per-stream
+ * workspace grows on first use.  d_idx / d_w (optional, [t_rows][top_k])
+ * receive the routes. */
 int rce_qmm_moe_ffn_device(rce_qmm_ctx *ctx, const float *d_x, size_t ldx, size_t t_rows,
                            const float *d_logits, size_t ld_logits, int n_experts, int top_k,
                            int expert_begin, int expert_end, const rce_qmm_weight *const *gate,
                            const rce_qmm_weight *const *up, const rce_qmm_weight *const *down, float *d_out,
                            size_t ldo, int32_t *d_idx, float *d_w, void *stream);
+
+/* The always-on shared expert of moe_ffn_forward
+ * (rce-qwen36-moe/src/lib.rs:684-705), added into out:
+ * sh = W_down (silu(W_gate x) * (W_up x)) with the shared weights, then
+ * out[t] += sigmoid(gate_inp . x[t]) * sh[t], the dot product summed left
+ * to right in f32.  Called after rce_qmm_moe_ffn_device on the same out it
+ * completes moe_ffn_forward: the routed combine first, then the shared term,
+ * the order in which the reference adds them.  gate/up [n_ff x d_model],
+ * down [d_model x n_ff]; gate_inp device f32 [d_model].  The matmuls run
+ * through mm_batched's dispatch.  Asynchronous on `stream`; uses the
+ * stream's MoE workspace. */
+int rce_qmm_moe_shared_expert_device(rce_qmm_ctx *ctx, const float *d_x, size_t ldx, size_t t_rows,
+                                     const rce_qmm_weight *gate, const rce_qmm_weight *up,
+                                     const rce_qmm_weight *down, const float *d_gate_inp, float *d_out,
+                                     size_t ldo, void *stream);
 
 /* Host-buffer rce_qmm_moe_ffn_device, synchronous (the MoE FFN call of the
  * reference's runtimes, rce-qwen36-moe/src/lib.rs:666-705, routed by

@@ -85,6 +85,11 @@ def lib():
             L.oracle_moe_ffn.restype = ctypes.c_int
             L.oracle_moe_ffn.argtypes = [_f32p, _sz, _sz, _sz, _f32p, ctypes.c_int, ctypes.c_int,
                                          _u8p, _u8p, _u8p, _sz, _sz, _sz, ctypes.c_int, _f32p, ctypes.c_int]
+            L.oracle_sigmoid.restype = ctypes.c_float
+            L.oracle_sigmoid.argtypes = [ctypes.c_float]
+            L.oracle_moe_shared_expert.restype = ctypes.c_int
+            L.oracle_moe_shared_expert.argtypes = [_f32p, _sz, _sz, _sz, _f32p, _u8p, _u8p, _u8p, ctypes.c_int,
+                                                   _f32p, ctypes.c_int]
             L.oracle_quantize_block.argtypes = [_f32p, ctypes.c_int, _i32p, _f32p]
             L.oracle_spec_matmul_q.argtypes = [_f32p, _sz, _i32p, _f32p, _sz, _sz, ctypes.c_int, _f32p]
             L.oracle_spec_matmul_q4k.argtypes = [_f32p, _sz, _i32p, _f32p, _f32p, _sz, _sz, _f32p]
@@ -222,6 +227,25 @@ def moe_ffn(x, router_logits, top_k, gate, up, down, dtype, d_ff, nthreads=1) ->
     if rc != 0:
         raise ValueError("oracle moe_ffn failed")
     return out
+
+
+def sigmoid(x: float) -> float:
+    return lib().oracle_sigmoid(float(x))
+
+
+def moe_shared_expert(x, out, gate_inp, gate, up, down, dtype, n_ff, nthreads=1) -> np.ndarray:
+    """out + sigmoid(gate_inp . x) * SwiGLU(x) with the shared expert's weights
+    (moe_ffn_forward, rce-qwen36-moe/src/lib.rs:694-705); returns a new array."""
+    x = _f32(x)
+    t_rows, d_model = x.shape
+    res = np.array(_f32(out), dtype=np.float32, copy=True)
+    gi = _f32(gate_inp)
+    gate, up, down = _u8(gate), _u8(up), _u8(down)
+    rc = lib().oracle_moe_shared_expert(_p(x, _f32p), t_rows, d_model, n_ff, _p(gi, _f32p), _p(gate, _u8p),
+                                        _p(up, _u8p), _p(down, _u8p), int(dtype), _p(res, _f32p), int(nthreads))
+    if rc != 0:
+        raise ValueError("oracle moe_shared_expert failed")
+    return res
 
 
 def quantize_block(x, q4: bool):

@@ -596,6 +596,53 @@ int oracle_moe_ffn(const float *x, size_t t_rows, size_t d_model, size_t d_ff,
     return rc;
 }
 
+/* sigmoid (rce-qwen36-moe/src/lib.rs:465-467). */
+float oracle_sigmoid(float x) {
+    if (x >= 0.0f) {
+        float den = 1.0f + expf(-x);
+        return 1.0f / den;
+    }
+    float e = expf(x);
+    float den = 1.0f + e;
+    return e / den;
+}
+
+/* The always-on shared expert of moe_ffn_forward (rce-qwen36-moe/src/lib.rs:
+ * 694-705), added into out [t_rows][d_model] (which holds the routed
+ * experts' combine): sh = swiglu_expert_serial(x, gate, up, down) with the
+ * shared weights ([n_ff, d_model], [n_ff, d_model], [d_model, n_ff]),
+ * g = sum_i gate_inp[i] * x[i] left to right, out[i] += sigmoid(g) * sh[i]. */
+int oracle_moe_shared_expert(const float *x, size_t t_rows, size_t d_model, size_t n_ff, const float *gate_inp,
+                             const uint8_t *gate, const uint8_t *up, const uint8_t *down, int dtype, float *out,
+                             int nthreads) {
+    float *g = malloc(n_ff * sizeof(float)), *u = malloc(n_ff * sizeof(float));
+    float *sh = malloc(d_model * sizeof(float));
+    int rc = (g && u && sh) ? 0 : -1;
+    for (size_t t = 0; t < t_rows && rc == 0; t++) {
+        const float *xt = x + t * d_model;
+        float *ot = out + t * d_model;
+        rc |= oracle_mm_1d(xt, gate, dtype, n_ff, d_model, g, nthreads);
+        rc |= oracle_mm_1d(xt, up, dtype, n_ff, d_model, u, nthreads);
+        for (size_t i = 0; i < n_ff; i++) {
+            float s = oracle_silu(g[i]);
+            g[i] = s * u[i];
+        }
+        rc |= oracle_mm_1d(g, down, dtype, d_model, n_ff, sh, nthreads);
+        float acc = 0.0f;
+        for (size_t i = 0; i < d_model; i++) {
+            float p = gate_inp[i] * xt[i];
+            acc = acc + p;
+        }
+        const float alpha = oracle_sigmoid(acc);
+        for (size_t i = 0; i < d_model; i++) {
+            float p = alpha * sh[i];
+            ot[i] = ot[i] + p;
+        }
+    }
+    free(g); free(u); free(sh);
+    return rc;
+}
+
 /* quantize_block (rce-vm-backend-cpu/src/ml/nn.rs:541-563): GGUF's reference
  * quantizer for one block of 32.  q4: d = max / -8, q = min(15, floor(x id +
  * 8.5)) - 8; otherwise d = amax / 127, q = round-half-away(x id).  The scale

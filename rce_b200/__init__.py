@@ -19,7 +19,7 @@ from .qmm import (  # noqa: F401
     mm_multi_device,
 )
 from .moe import (RouterDecision, decisions, moe_ffn, moe_ffn_device, moe_route_device, moe_router,  # noqa: F401
-                  moe_router_device, split_experts)
+                  moe_router_device, moe_shared_expert_device, split_experts)
 from .shard import PeerGroup, row_shards, torch_exchange  # noqa: F401
 
 __version__ = "0.1.0"

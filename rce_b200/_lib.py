@@ -76,6 +76,7 @@ SIGNATURES = {
                                        _sz, _vp, _vp, _vp]),
     "rce_qmm_moe_router_device": (_int, [_vp, _vp, _sz, _sz, _vp, _int, _int, _vp, _sz, _vp, _vp, _vp]),
     "rce_qmm_moe_ffn": (_int, [_vp, _vp, _sz, _vp, _vp, _int, _int, _int, _int, _vp, _vp, _vp, _vp, _vp, _vp]),
+    "rce_qmm_moe_shared_expert_device": (_int, [_vp, _vp, _sz, _sz, _vp, _vp, _vp, _vp, _vp, _sz, _vp]),
     "rce_qmm_synchronize": (_int, [_vp]),
 }
 

@@ -1069,6 +1069,51 @@ int rce_qmm_moe_ffn_device(rce_qmm_ctx *ctx, const float *d_x, size_t ldx, size_
     return ok();
 }
 
+int rce_qmm_moe_shared_expert_device(rce_qmm_ctx *ctx, const float *d_x, size_t ldx, size_t t_rows,
+                                     const rce_qmm_weight *gate, const rce_qmm_weight *up,
+                                     const rce_qmm_weight *down, const float *d_gate_inp, float *d_out,
+                                     size_t ldo, void *stream) {
+    if (!ctx) return fail(RCE_QMM_ERR_INVALID, "moe_shared_expert_device: null ctx");
+    for (const rce_qmm_weight *w : {gate, up, down}) {
+        const int rc = check_weight(w);
+        if (rc) return rc;
+        if (w->ctx != ctx) return fail(RCE_QMM_ERR_INVALID, "moe_shared_expert_device: weight of another context");
+    }
+    const int64_t d_model = gate->g.n_cols, n_ff = gate->g.n_rows;
+    if (up->g.n_rows != n_ff || up->g.n_cols != d_model || down->g.n_rows != d_model || down->g.n_cols != n_ff)
+        return fail(RCE_QMM_ERR_INVALID,
+                    "moe_shared_expert_device: gate/up must be [%lld x %lld] and down [%lld x %lld]",
+                    (long long)n_ff, (long long)d_model, (long long)d_model, (long long)n_ff);
+    if (t_rows == 0) return ok();
+    if (!d_x || !d_gate_inp || !d_out) return fail(RCE_QMM_ERR_INVALID, "moe_shared_expert_device: null buffer");
+    if (ldx < (size_t)d_model || ldo < (size_t)d_model)
+        return fail(RCE_QMM_ERR_INVALID, "moe_shared_expert_device: ldx %zu / ldo %zu < d_model %lld", ldx, ldo,
+                    (long long)d_model);
+    if (t_rows > (size_t)INT32_MAX) return fail(RCE_QMM_ERR_INVALID, "moe_shared_expert_device: too many tokens");
+    DeviceGuard dg(ctx->device);
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    // workspace: g and u [t][n_ff] (h = silu(g) * u written over g), sh [t][d_model]
+    auto al = [](size_t v) { return (v + 255) / 256 * 256; };
+    const size_t o_u = al(t_rows * (size_t)n_ff * 4), o_sh = o_u + al(t_rows * (size_t)n_ff * 4);
+    void *wsv = nullptr;
+    int32_t *host_off = nullptr;
+    int rc = stream_moe_ws(ctx, s, o_sh + al(t_rows * (size_t)d_model * 4), 1, &wsv, &host_off);
+    if (rc) return rc;
+    float *gb = static_cast<float *>(wsv);
+    float *ub = reinterpret_cast<float *>(static_cast<uint8_t *>(wsv) + o_u);
+    float *sh = reinterpret_cast<float *>(static_cast<uint8_t *>(wsv) + o_sh);
+    rc = run_matmul(ctx, gate, d_x, ldx, t_rows, gb, (size_t)n_ff, s);
+    if (rc) return rc;
+    rc = run_matmul(ctx, up, d_x, ldx, t_rows, ub, (size_t)n_ff, s);
+    if (rc) return rc;
+    CUDA_TRY(rce::launch_swiglu(gb, ub, gb, t_rows * (size_t)n_ff, s));
+    rc = run_matmul(ctx, down, gb, (size_t)n_ff, t_rows, sh, (size_t)d_model, s);
+    if (rc) return rc;
+    CUDA_TRY(rce::launch_moe_shared_combine(d_x, ldx, (int)t_rows, (int)d_model, d_gate_inp, sh, (size_t)d_model,
+                                            d_out, ldo, s));
+    return ok();
+}
+
 int rce_qmm_moe_ffn(rce_qmm_ctx *ctx, const float *x, size_t t_rows, const float *router_logits,
                     const rce_qmm_weight *router_w, int n_experts, int top_k, int expert_begin, int expert_end,
                     const rce_qmm_weight *const *gate, const rce_qmm_weight *const *up,

@@ -195,6 +195,9 @@ cudaError_t launch_moe_gather_prep(const float *x, size_t ldx, const int32_t *to
                                    int zero_rows, cudaStream_t s);
 cudaError_t launch_moe_h_prep(const float *h, size_t ld, const int32_t *n_rows, int max_rows, int d_ff, void *xh,
                               float *inv, cudaStream_t s);
+// The shared expert's gate and add: out[t] += sigmoid(gate_inp . x[t]) * sh[t].
+cudaError_t launch_moe_shared_combine(const float *x, size_t ldx, int t_rows, int d_model, const float *gate_inp,
+                                      const float *sh, size_t ldsh, float *out, size_t ldo, cudaStream_t s);
 cudaError_t launch_moe_combine(const float *y, int d_model, const int32_t *pos, const float *w, int t_rows, int top_k,
                                float *out, size_t ldo, cudaStream_t s);
 

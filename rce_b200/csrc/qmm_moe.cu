@@ -180,7 +180,43 @@ __global__ void combine_kernel(const float *y, int d_model, const int32_t *pos, 
     }
 }
 
+// sigmoid as moe_ffn_forward's shared-expert gate computes it
+// (rce-qwen36-moe/src/lib.rs:465-467), each operation rounded on its own.
+__device__ __forceinline__ float sigmoid_ref(float x) {
+    if (x >= 0.f) return __fdiv_rn(1.f, __fadd_rn(1.f, expf(-x)));
+    const float e = expf(x);
+    return __fdiv_rn(e, __fadd_rn(1.f, e));
+}
+
+// The shared expert's contribution, token t = blockIdx.x: g = sum_i
+// gate_inp[i] * x[t][i] left to right (one thread: the reference's order),
+// then out[t][i] += sigmoid(g) * sh[t][i] (moe_ffn_forward,
+// rce-qwen36-moe/src/lib.rs:697-704).
+__global__ void shared_combine_kernel(const float *x, size_t ldx, int d_model, const float *gate_inp,
+                                      const float *sh, size_t ldsh, float *out, size_t ldo) {
+    __shared__ float alpha;
+    const int t = blockIdx.x;
+    if (threadIdx.x == 0) {
+        const float *xt = x + (size_t)t * ldx;
+        float acc = 0.f;
+        for (int i = 0; i < d_model; i++) acc = __fadd_rn(acc, __fmul_rn(gate_inp[i], xt[i]));
+        alpha = sigmoid_ref(acc);
+    }
+    __syncthreads();
+    const float a = alpha;
+    const float *st = sh + (size_t)t * ldsh;
+    float *ot = out + (size_t)t * ldo;
+    for (int i = threadIdx.x; i < d_model; i += blockDim.x) ot[i] = __fadd_rn(ot[i], __fmul_rn(a, st[i]));
+}
+
 }  // namespace
+
+cudaError_t launch_moe_shared_combine(const float *x, size_t ldx, int t_rows, int d_model, const float *gate_inp,
+                                      const float *sh, size_t ldsh, float *out, size_t ldo, cudaStream_t s) {
+    if (t_rows <= 0) return cudaSuccess;
+    shared_combine_kernel<<<t_rows, 256, 0, s>>>(x, ldx, d_model, gate_inp, sh, ldsh, out, ldo);
+    return cudaGetLastError();
+}
 
 cudaError_t launch_moe_route(const float *logits, size_t ld, int t_rows, int n_experts, int top_k, int normalize,
                              int32_t *idx, float *w, cudaStream_t s) {

@@ -115,15 +115,40 @@ def _handles(ws: Sequence[Optional[QuantWeight]], lo: int, hi: int):
     return arr
 
 
+def moe_shared_expert_device(x, gate: QuantWeight, up: QuantWeight, down: QuantWeight, gate_inp, out,
+                             stream=None):
+    """Add the always-on shared expert of moe_ffn_forward
+    (rce-qwen36-moe/src/lib.rs:684-705) into out [T, d_model] (CUDA f32, in
+    place): out[t] += sigmoid(gate_inp . x[t]) * W_down (silu(W_gate x[t]) *
+    (W_up x[t])), gate_inp a CUDA f32 vector [d_model].  Returns out."""
+    import torch
+
+    _f32_2d(x, "x")
+    _f32_2d(out, "out")
+    t_rows, d_model = x.shape
+    if tuple(out.shape) != (t_rows, d_model):
+        raise ValueError("out must be [T, d_model]")
+    if gate_inp.dtype != torch.float32 or not gate_inp.is_cuda or gate_inp.numel() != d_model \
+            or not gate_inp.is_contiguous():
+        raise ValueError("gate_inp must be a contiguous CUDA f32 vector of d_model values")
+    check(lib().rce_qmm_moe_shared_expert_device(gate.ctx.handle, ctypes.c_void_p(x.data_ptr()), x.stride(0), t_rows,
+                                                 gate.handle, up.handle, down.handle,
+                                                 ctypes.c_void_p(gate_inp.data_ptr()), ctypes.c_void_p(out.data_ptr()),
+                                                 out.stride(0), _stream_handle(stream, x.device)))
+    return out
+
+
 def moe_ffn_device(x, logits, top_k: int, gate: Sequence[QuantWeight], up: Sequence[QuantWeight],
                    down: Sequence[QuantWeight], expert_range: Optional[Tuple[int, int]] = None, out=None,
-                   stream=None, return_routes: bool = False):
+                   stream=None, return_routes: bool = False, shared=None):
     """The expert-grouped SwiGLU FFN over T tokens (x [T, d_model], router
     logits [T, n_experts], CUDA f32): route (softmax, top_k, renormalise),
     per routed expert y = W_down (silu(W_gate x) * (W_up x)), and combine in
     route order.  ``expert_range=(lo, hi)`` computes only the contributions
     of experts lo..hi-1 (the others add nothing; the weights of the others
-    may be None), for experts placed across GPUs."""
+    may be None), for experts placed across GPUs.  ``shared=(gate, up, down,
+    gate_inp)`` then adds the sigmoid-gated shared expert
+    (moe_shared_expert_device), completing moe_ffn_forward."""
     import torch
 
     _f32_2d(x, "x")
@@ -145,6 +170,9 @@ def moe_ffn_device(x, logits, top_k: int, gate: Sequence[QuantWeight], up: Seque
                                        _handles(gate, lo, hi), _handles(up, lo, hi), _handles(down, lo, hi),
                                        ctypes.c_void_p(out.data_ptr()), out.stride(0), ctypes.c_void_p(idx.data_ptr()),
                                        ctypes.c_void_p(w.data_ptr()), _stream_handle(stream, x.device)))
+    if shared is not None:
+        sg, su, sd, sgi = shared
+        moe_shared_expert_device(x, sg, su, sd, sgi, out, stream=stream)
     if return_routes:
         return out, idx, w
     return out

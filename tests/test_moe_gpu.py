@@ -351,3 +351,62 @@ def test_host_moe_ffn(ctx):
     assert err.max() <= 1e-5
     with pytest.raises(ValueError):
         R.moe_ffn(x, top_k, g, u, d)  # neither logits nor a gate weight
+
+
+# ---- the shared expert of moe_ffn_forward (rce-qwen36-moe/src/lib.rs:684-705)
+
+@pytest.mark.parametrize("exact", [True, False])
+def test_ffn_with_shared_expert_matches_oracle(ctx, exact):
+    import torch
+
+    # routed experts (top-2 of 4) plus the always-on shared expert with its
+    # sigmoid gate; the exact path against the oracle's moe_ffn_forward at
+    # the exact path's bar, the default (tensor-core) path at the GEMM bar
+    dt, n_e, d_model, d_ff, n_ff_s, t = Q4_K, 4, 512, 1024, 512, 40
+    gate, up, down, x, logits = _setup(dt, n_e, d_model, d_ff, t, 61)
+    rng = np.random.default_rng(62)
+    sg = synth.weights(dt, n_ff_s, d_model, rng)
+    su = synth.weights(dt, n_ff_s, d_model, rng)
+    sd = synth.weights(dt, d_model, n_ff_s, rng)
+    gate_inp = (rng.standard_normal(d_model) * 0.05).astype(np.float32)
+    g, u, d = _device(ctx, dt, gate, up, down, d_model, d_ff)
+    wsg = R.QuantWeight.from_owned_bytes(sg, dt, n_ff_s, d_model, ctx=ctx)
+    wsu = R.QuantWeight.from_owned_bytes(su, dt, n_ff_s, d_model, ctx=ctx)
+    wsd = R.QuantWeight.from_owned_bytes(sd, dt, d_model, n_ff_s, ctx=ctx)
+    routed = O.moe_ffn(x, logits, 2, np.stack(gate), np.stack(up), np.stack(down), dt, d_ff, nthreads=8)
+    want = O.moe_shared_expert(x, routed, gate_inp, sg, su, sd, dt, n_ff_s, nthreads=8)
+    saved = ctx.prefill_min_tokens
+    if exact:
+        ctx.prefill_min_tokens = 0
+    try:
+        got = R.moe_ffn_device(torch.from_numpy(x).cuda(), torch.from_numpy(logits).cuda(), 2, g, u, d,
+                               shared=(wsg, wsu, wsd, torch.from_numpy(gate_inp).cuda())).cpu().numpy()
+    finally:
+        ctx.prefill_min_tokens = saved
+    assert ctx.device_error() == 0
+    # the shared term matters: the output differs from the routed part alone
+    assert np.abs(want - routed).max() > 1e-2 * np.abs(want).max()
+    if exact:
+        err = np.abs(got - want).max(axis=1) / np.abs(want).max(axis=1)
+        print(f"MoE + shared expert, exact path: per-token normwise {err.max():.3e}")
+        assert err.max() <= 1e-5
+    else:
+        tensor = np.abs(got.astype(np.float64) - want).max() / np.abs(want).max()
+        print(f"MoE + shared expert, tensor-core path: max-norm {tensor:.3e}")
+        assert tensor <= 1e-3
+
+
+def test_shared_expert_bad_arguments(ctx):
+    import torch
+
+    dt, d_model, n_ff_s = Q4_K, 256, 512
+    rng = np.random.default_rng(63)
+    wsg = R.QuantWeight.from_owned_bytes(synth.weights(dt, n_ff_s, d_model, rng), dt, n_ff_s, d_model, ctx=ctx)
+    wsd = R.QuantWeight.from_owned_bytes(synth.weights(dt, d_model, n_ff_s, rng), dt, d_model, n_ff_s, ctx=ctx)
+    x = torch.zeros((4, d_model), device="cuda")
+    out = torch.zeros((4, d_model), device="cuda")
+    gi = torch.zeros(d_model, device="cuda")
+    with pytest.raises(R.QmmError):
+        R.moe_shared_expert_device(x, wsg, wsd, wsd, gi, out)  # up with down's shape
+    with pytest.raises(ValueError):
+        R.moe_shared_expert_device(x, wsg, wsg, wsd, gi[:10], out)  # gate_inp of the wrong length
