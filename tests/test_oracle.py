@@ -218,6 +218,43 @@ def test_moe_ffn_equals_explicit_composition():
         assert np.array_equal(got[i], O.moe_combine(wt, np.stack(outs)))
 
 
+def test_sigmoid_two_branches():
+    # sigmoid (rce-qwen36-moe/src/lib.rs:465-467): 1 / (1 + e^-x) for x >= 0,
+    # e^x / (1 + e^x) below, each step in binary32 (the exponential within
+    # one unit in the last place of numpy's)
+    for x in [0.0, 0.25, 3.5, 20.0, -0.25, -3.5, -20.0, -90.0]:
+        xf = np.float32(x)
+        if xf >= 0:
+            want = np.float32(1.0) / (np.float32(1.0) + np.exp(-xf))
+        else:
+            e = np.exp(xf)
+            want = e / (np.float32(1.0) + e)
+        got = np.float32(O.sigmoid(x))
+        assert abs(int(got.view(np.int32)) - int(np.float32(want).view(np.int32))) <= 1, x
+
+
+def test_shared_expert_equals_explicit_composition():
+    # moe_ffn_forward's shared expert (rce-qwen36-moe/src/lib.rs:694-705)
+    rng = np.random.default_rng(5)
+    d, f, t = 256, 512, 3
+    from rce_b200 import synth
+    sg, su, sd = synth.q4_k(f, d, rng), synth.q4_k(f, d, rng), synth.q4_k(d, f, rng)
+    gi = (rng.standard_normal(d) * 0.1).astype(np.float32)
+    x = rng.standard_normal((t, d), dtype=np.float32)
+    base = rng.standard_normal((t, d), dtype=np.float32)
+    got = O.moe_shared_expert(x, base, gi, sg, su, sd, Q4_K, f)
+    for i in range(t):
+        g = O.mm_1d(x[i], sg, Q4_K, f, d)
+        u = O.mm_1d(x[i], su, Q4_K, f, d)
+        h = np.array([O.silu(float(v)) for v in g], np.float32) * u
+        sh = O.mm_1d(h.astype(np.float32), sd, Q4_K, d, f)
+        acc = np.float32(0.0)
+        for j in range(d):
+            acc = np.float32(acc + np.float32(gi[j] * x[i, j]))
+        alpha = np.float32(O.sigmoid(float(acc)))
+        assert np.array_equal(got[i], (base[i] + alpha * sh).astype(np.float32))
+
+
 # ---- quantize_block (rce-vm-backend-cpu/src/ml/nn.rs:541-563) ---------------
 
 def test_quantize_block_known_answers():
