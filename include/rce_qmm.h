@@ -16,7 +16,8 @@
  *   QmmLeaf::execute     rce-op-qmm/src/lib.rs:2096-2130
  *   moe_router / moe_combine
  *                        rce-op-moe/src/lib.rs:35-73, 98-110
- *   moe_ffn_forward      rce-qwen36-moe/src/lib.rs:666-705 (routed experts)
+ *   moe_ffn_forward      rce-qwen36-moe/src/lib.rs:666-705 (routed experts; the
+ *                        shared expert, :684-705, rce_qmm_moe_shared_expert_device)
  *
  * Conventions (after the reference's own C ABI, rce-c/src/lib.rs:8-100):
  *   - every function returns RCE_QMM_OK (0) or an error code; the message of
