@@ -5,6 +5,7 @@
 // launch is an error returned to the caller.
 #include <cuda_runtime.h>
 
+#include <atomic>
 #include <cstdarg>
 #include <cstdio>
 #include <cstring>
@@ -64,6 +65,11 @@ struct DeviceGuard {
         if (changed) cudaSetDevice(prev);
     }
 };
+
+uint64_t next_serial() {
+    static std::atomic<uint64_t> n{0};
+    return ++n;
+}
 
 int thread_state(rce_qmm_ctx *ctx, RceThreadState **out) {
     std::lock_guard<std::mutex> lk(ctx->mu);
@@ -236,6 +242,7 @@ int register_common(rce_qmm_ctx *ctx, const void *src, bool src_on_device, size_
     }
     rce_qmm_weight *w = new rce_qmm_weight;
     w->ctx = ctx;
+    w->serial = next_serial();
     w->dtype = dtype;
     w->g = g;
     w->dev = dev;
@@ -298,6 +305,8 @@ int rce_qmm_ctx_destroy(rce_qmm_ctx *ctx) {
     for (auto &kv : ctx->threads) {
         RceThreadState &ts = kv.second;
         if (ts.stream) cudaStreamSynchronize(ts.stream);
+        for (auto &g : ts.graphs) cudaGraphExecDestroy(g.second);
+        ts.graphs.clear();
         if (ts.d_in) cudaFree(ts.d_in);
         if (ts.d_out) cudaFree(ts.d_out);
         if (ts.h_pin) cudaFreeHost(ts.h_pin);
@@ -369,6 +378,7 @@ int rce_qmm_weight_sub_view(const rce_qmm_weight *parent, size_t byte_offset, si
                     byte_len, (long long)n_rows);
     rce_qmm_weight *w = new rce_qmm_weight;
     w->ctx = parent->ctx;
+    w->serial = next_serial();
     w->dtype = parent->dtype;
     w->g = rce::make_geometry(parent->dtype, n_rows, n_cols);
     w->dev = parent->dev + (size_t)(row0 / rce::TILE_ROWS) * pg.n_chunks * rce::chunk_bytes(parent->dtype);
@@ -491,6 +501,37 @@ int rce_qmm_mm_batched_device_multi(rce_qmm_ctx *ctx, const float *d_a, size_t l
     return ok();
 }
 
+constexpr size_t kMaxHostGraphs = 1024;  // per thread; all are dropped when full
+
+void clear_graphs(RceThreadState *ts) {
+    for (auto &kv : ts->graphs) cudaGraphExecDestroy(kv.second);
+    ts->graphs.clear();
+}
+
+// Records rce_qmm_mm_batched's device steps for w and t_rows on the thread's
+// staging buffers (copy in, matmul, copy out) as an executable graph.
+int record_host_call(rce_qmm_ctx *ctx, RceThreadState *ts, const rce_qmm_weight *w, size_t t_rows,
+                     cudaGraphExec_t *exec) {
+    *exec = nullptr;
+    const size_t k = (size_t)w->g.n_cols, n = (size_t)w->g.n_rows;
+    cudaGraph_t graph = nullptr;
+    CUDA_TRY(cudaStreamBeginCapture(ts->stream, cudaStreamCaptureModeThreadLocal));
+    cudaError_t e = cudaMemcpyAsync(ts->d_in, ts->h_pin, t_rows * k * sizeof(float), cudaMemcpyHostToDevice, ts->stream);
+    int rc = e == cudaSuccess ? run_matmul(ctx, w, ts->d_in, k, t_rows, ts->d_out, n, ts->stream) : 0;
+    if (e == cudaSuccess && rc == 0)
+        e = cudaMemcpyAsync(ts->h_pin, ts->d_out, t_rows * n * sizeof(float), cudaMemcpyDeviceToHost, ts->stream);
+    const cudaError_t ee = cudaStreamEndCapture(ts->stream, &graph);
+    if (e == cudaSuccess) e = ee;
+    if (e == cudaSuccess && rc == 0) e = cudaGraphInstantiate(exec, graph, 0);
+    if (graph) cudaGraphDestroy(graph);
+    if (e != cudaSuccess || rc != 0) {
+        *exec = nullptr;
+        cudaGetLastError();  // (the direct path runs instead)
+        return 1;
+    }
+    return 0;
+}
+
 int rce_qmm_mm_batched(rce_qmm_ctx *ctx, const float *a, size_t t_rows, const rce_qmm_weight *w, float *out,
                        size_t out_len) {
     if (!ctx) return fail(RCE_QMM_ERR_INVALID, "mm_batched: null ctx");
@@ -507,14 +548,34 @@ int rce_qmm_mm_batched(rce_qmm_ctx *ctx, const float *a, size_t t_rows, const rc
     rc = thread_state(ctx, &ts);
     if (rc) return rc;
     const size_t in_f = t_rows * k, out_f = t_rows * n;
+    const void *bufs[3] = {ts->d_in, ts->d_out, ts->h_pin};
     if ((rc = grow_device(&ts->d_in, &ts->d_in_cap, in_f))) return rc;
     if ((rc = grow_device(&ts->d_out, &ts->d_out_cap, out_f))) return rc;
     if ((rc = grow_pinned(ts, (in_f > out_f ? in_f : out_f) * sizeof(float)))) return rc;
+    if (bufs[0] != ts->d_in || bufs[1] != ts->d_out || bufs[2] != ts->h_pin) clear_graphs(ts);
     std::memcpy(ts->h_pin, a, in_f * sizeof(float));
-    CUDA_TRY(cudaMemcpyAsync(ts->d_in, ts->h_pin, in_f * sizeof(float), cudaMemcpyHostToDevice, ts->stream));
-    rc = run_matmul(ctx, w, ts->d_in, k, t_rows, ts->d_out, n, ts->stream);
-    if (rc) return rc;
-    CUDA_TRY(cudaMemcpyAsync(ts->h_pin, ts->d_out, out_f * sizeof(float), cudaMemcpyDeviceToHost, ts->stream));
+    // the decode route (no workspace: the graph stays valid) replays a cached
+    // graph of the three steps; the first call of a (weight, batch) records it
+    const bool decode = ctx->prefill_min_tokens == 0 || t_rows < (size_t)ctx->prefill_min_tokens;
+    cudaGraphExec_t exec = nullptr;
+    if (decode && t_rows < 256) {
+        const uint64_t key = (w->serial << 8) | (uint64_t)t_rows;
+        auto it = ts->graphs.find(key);
+        if (it != ts->graphs.end()) {
+            exec = it->second;
+        } else if (record_host_call(ctx, ts, w, t_rows, &exec) == 0 && exec) {
+            if (ts->graphs.size() >= kMaxHostGraphs) clear_graphs(ts);
+            ts->graphs[key] = exec;
+        }
+    }
+    if (exec) {
+        CUDA_TRY(cudaGraphLaunch(exec, ts->stream));
+    } else {
+        CUDA_TRY(cudaMemcpyAsync(ts->d_in, ts->h_pin, in_f * sizeof(float), cudaMemcpyHostToDevice, ts->stream));
+        rc = run_matmul(ctx, w, ts->d_in, k, t_rows, ts->d_out, n, ts->stream);
+        if (rc) return rc;
+        CUDA_TRY(cudaMemcpyAsync(ts->h_pin, ts->d_out, out_f * sizeof(float), cudaMemcpyDeviceToHost, ts->stream));
+    }
     CUDA_TRY(cudaStreamSynchronize(ts->stream));
     if ((rc = take_kernel_error(ctx))) return rc;
     std::memcpy(out, ts->h_pin, out_f * sizeof(float));

@@ -3,6 +3,7 @@
 #pragma once
 #include <cuda_runtime.h>
 
+#include <cstdint>
 #include <mutex>
 #include <thread>
 #include <unordered_map>
@@ -26,6 +27,10 @@ struct RceThreadState {
     size_t d_out_cap = 0;
     void *h_pin = nullptr;
     size_t h_cap = 0;
+    // Host-buffer decode calls replayed as CUDA graphs (copy in, matmul, copy
+    // out: one launch instead of three API calls), keyed by weight serial and
+    // batch; valid while the staging buffers above stay where they are.
+    std::unordered_map<uint64_t, cudaGraphExec_t> graphs;
 };
 
 struct rce_qmm_ctx {
@@ -45,6 +50,7 @@ struct rce_qmm_ctx {
 
 struct rce_qmm_weight {
     rce_qmm_ctx *ctx = nullptr;
+    uint64_t serial = 0;  // unique per handle (a freed handle's address may be reused; its serial is not)
     int dtype = 0;
     rce::Geometry g;
     uint8_t *dev = nullptr;

@@ -225,3 +225,31 @@ def test_device_path_and_strided_rows(ctx):
     o = out.cpu().numpy()
     assert np.all(np.isnan(o[:, n:]))
     assert_close(o[:, :n], O.mm_batched(x, m, w, Q4_K, n, k))
+
+
+def test_host_calls_replay_and_never_reuse_a_freed_weights_graph(ctx):
+    # host-buffer decode calls are replayed from a per-thread cache of CUDA
+    # graphs keyed by weight handle serial: repeated calls give the same bits,
+    # a weight freed and another registered (often at the same handle
+    # address) gets its own results, and growing the staging buffers (a
+    # larger matrix) drops the cache without changing any result
+    from rce_b200 import synth
+
+    rng = np.random.default_rng(91)
+    n, k = 512, 1024
+    x = rng.standard_normal((1, k), dtype=np.float32)
+    for _ in range(3):
+        wb = synth.q4_k(n, k, rng)
+        qw = register(ctx, wb, Q4_K, n, k)
+        first = R.mm_1d(x[0], qw)
+        assert_close(first, O.mm_batched(x, 1, wb, Q4_K, n, k))
+        for _ in range(3):
+            assert np.array_equal(R.mm_1d(x[0], qw).view(np.uint32), first.view(np.uint32))
+        qw.close()
+    big_b = synth.q4_k(4096, 4096, rng)
+    big = register(ctx, big_b, Q4_K, 4096, 4096)
+    xb = rng.standard_normal((2, 4096), dtype=np.float32)
+    assert_close(R.mm_batched(xb, 2, big).reshape(2, 4096), O.mm_batched(xb, 2, big_b, Q4_K, 4096, 4096, nthreads=8))
+    wb = synth.q4_k(n, k, rng)
+    qw = register(ctx, wb, Q4_K, n, k)
+    assert_close(R.mm_1d(x[0], qw), O.mm_batched(x, 1, wb, Q4_K, n, k))
