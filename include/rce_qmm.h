@@ -129,7 +129,13 @@ int rce_qmm_mm_1d(rce_qmm_ctx *ctx, const float *a, size_t a_len, const rce_qmm_
 int rce_qmm_mm_1d_serial(rce_qmm_ctx *ctx, const float *a, size_t a_len, const rce_qmm_weight *w,
                          float *out, size_t out_len);
 /* out[T, n_rows] = a[T, n_cols] . W^T (mm_batched, rce-op-qmm/src/lib.rs:967).
- * Host buffers, synchronous. */
+ * Host buffers, synchronous.  Below the context's prefill_min_tokens
+ * (default 16) every token's row is bit-identical to mm_1d's, the reference's
+ * mm_batched guarantee (lib.rs:2575-2616); from there on the tensor-core GEMM
+ * (fp16 weights, activations as two fp16 terms up to 64 tokens, one above)
+ * holds each output row within 1e-3 of the f32 result but not bit for bit.
+ * Callers that need the identity at every batch size set prefill_min_tokens
+ * to 0 (rce_qmm_ctx_set_prefill_min_tokens). */
 int rce_qmm_mm_batched(rce_qmm_ctx *ctx, const float *a, size_t t_rows, const rce_qmm_weight *w,
                        float *out, size_t out_len);
 /* Device variant: d_a is [t_rows][lda] f32, d_out [t_rows][ldo] f32. */
