@@ -509,7 +509,8 @@ void clear_graphs(RceThreadState *ts) {
 }
 
 // Records rce_qmm_mm_batched's device steps for w and t_rows on the thread's
-// staging buffers (copy in, matmul, copy out) as an executable graph.
+// staging buffers (copy in, matmul into the pinned buffer) as an executable
+// graph.
 int record_host_call(rce_qmm_ctx *ctx, RceThreadState *ts, const rce_qmm_weight *w, size_t t_rows,
                      cudaGraphExec_t *exec) {
     *exec = nullptr;
@@ -517,9 +518,11 @@ int record_host_call(rce_qmm_ctx *ctx, RceThreadState *ts, const rce_qmm_weight 
     cudaGraph_t graph = nullptr;
     CUDA_TRY(cudaStreamBeginCapture(ts->stream, cudaStreamCaptureModeThreadLocal));
     cudaError_t e = cudaMemcpyAsync(ts->d_in, ts->h_pin, t_rows * k * sizeof(float), cudaMemcpyHostToDevice, ts->stream);
-    int rc = e == cudaSuccess ? run_matmul(ctx, w, ts->d_in, k, t_rows, ts->d_out, n, ts->stream) : 0;
-    if (e == cudaSuccess && rc == 0)
-        e = cudaMemcpyAsync(ts->h_pin, ts->d_out, t_rows * n * sizeof(float), cudaMemcpyDeviceToHost, ts->stream);
+    // the matmul writes its (small, decode-sized) output straight into the
+    // pinned staging buffer (mapped into the device's address space): no
+    // device-to-host copy after it
+    int rc = e == cudaSuccess ? run_matmul(ctx, w, ts->d_in, k, t_rows, static_cast<float *>(ts->h_pin), n, ts->stream)
+                              : 0;
     const cudaError_t ee = cudaStreamEndCapture(ts->stream, &graph);
     if (e == cudaSuccess) e = ee;
     if (e == cudaSuccess && rc == 0) e = cudaGraphInstantiate(exec, graph, 0);
