@@ -546,6 +546,12 @@ __host__ __device__ inline int act_kps_log(int bn, int terms, bool tmem_a) {
 // Token tiles up to this width carry two-term activations (N = 2 bn <= 256).
 constexpr int kTwoTermMaxTile = 128;
 
+// Activation stages per k-block: the 512-token tile's k-block is two stages
+// of 256 rows (one tensor-map box and one N = 256 accumulator half each), so
+// that with the same shared memory three of four halves can be in flight
+// while the MMAs read the fourth (with whole-k-block stages, one of two).
+__host__ __device__ inline int act_halves(int bn, int terms) { return terms * bn > 256 ? 2 : 1; }
+
 __host__ __device__ inline GemmSmem gemm_smem(int dt, int bn, int terms, bool tmem_a, int kps_log) {
     // Rings as deep as 227 KB allow: the dequantiser <-> MMA hand-off takes
     // a few thousand cycles, so the A ring should span several k-blocks;
@@ -557,6 +563,8 @@ __host__ __device__ inline GemmSmem gemm_smem(int dt, int bn, int terms, bool tm
     // shared memory) or kMaxB within 64 KB (A in tensor memory): at small
     // token tiles a stage is consumed faster than an L2 round trip
     L.b_stages = brows > 256 ? 2 : (brows > 128 ? 3 : 4);
+    const int halves = act_halves(bn, terms);  // (tmem_a is false there: 512 accumulator columns)
+    L.b_stages *= halves;
     const int by_bytes = (int)(((tmem_a ? 64 : 32) * 1024) / (brows * kBK * 2));
     const int max_b = tmem_a ? kMaxB : 8;
     if (by_bytes > L.b_stages) L.b_stages = by_bytes < max_b ? by_bytes : max_b;
@@ -566,7 +574,7 @@ __host__ __device__ inline GemmSmem gemm_smem(int dt, int bn, int terms, bool tm
         L.b_stages = n < 2 ? 2 : (n > kMaxB ? kMaxB : n);
     }
     const size_t a_stage = (size_t)kBM * kBK * 2;
-    const size_t b_bytes = (size_t)L.b_stages * kps * brows * kBK * 2;
+    const size_t b_bytes = (size_t)L.b_stages * kps * (brows / halves) * kBK * 2;
     const size_t slot = (size_t)8 * chunk_bytes(dt);
     const size_t misc = kBars * 8 + 16 + 1024;
     L.pslots = 2;
@@ -590,6 +598,14 @@ __host__ __device__ inline GemmSmem gemm_smem(int dt, int bn, int terms, bool tm
         L.total = o + 1024;
         return L;
     }
+    // the 512-token tile with the larger chunks of Q8_0 / Q6_K: fewer
+    // activation halves (at least one k-block's two) until two A stages fit
+    size_t b_now = b_bytes;
+    while (halves == 2 && L.b_stages > 2 && avail < 2 * a_stage) {
+        L.b_stages--;
+        b_now = (size_t)L.b_stages * kps * (brows / halves) * kBK * 2;
+        avail = kLimit > b_now + misc + 2 * slot ? kLimit - b_now - misc - 2 * slot : 0;
+    }
     int na = (int)(avail / a_stage);
     if (na > kMaxASmem) na = kMaxASmem;
     // leftover room buys a third and fourth weight slot
@@ -608,7 +624,7 @@ __host__ __device__ inline GemmSmem gemm_smem(int dt, int bn, int terms, bool tm
     L.a = o;  // 1024-aligned stages
     o += (size_t)L.a_stages * a_stage;
     L.b = o;
-    o += b_bytes;
+    o += b_now;
     L.packed = o;
     o += (size_t)L.pslots * slot;
     o = (o + 15) / 16 * 16;
@@ -873,6 +889,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int KL = p.kps_log, KPS = 1 << KL;  // k-blocks per activation stage
     const GemmSmem L = gemm_smem(DT, bn, terms, TA, KL);
     const int NB = L.b_stages, NP = L.pslots;
+    const int BH = act_halves(bn, terms);  // activation stages per k-block (1, or 2 at 512 tokens)
+    const size_t b_sbytes = (size_t)terms * bn / BH * kBK * 2;  // bytes of one activation stage
     uint8_t *a_st = smem + L.a;
     uint8_t *b_st = smem + L.b;
     uint8_t *pk = smem + L.packed;
@@ -1019,6 +1037,26 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
             if (!ok)
                 for (int u = max(0, cs - NB); u < cs; u++) mbar_wait(BF(u % NB), (u / NB) & 1);
+        } else if (lane == 0 && BH == 2) {
+            // the 512-token tile: stage f holds rows 256 (f % 2) .. + 255 of
+            // k-block f / 2 (one term)
+            int f = 0, st = 0;
+            uint32_t ph = 0;
+            for (; f < 2 * nkb; f++) {
+                if (f >= NB && !mbar_wait(BE(st), ph ^ 1)) {
+                    ok = false;
+                    break;
+                }
+                mbar_expect_tx(BF(st), (uint32_t)b_sbytes);
+                tma_2d(smem_u32(b_st + (size_t)st * b_sbytes), &xmap, (4 * ch0 + (f >> 1)) * kBK,
+                       t_begin + tok0 + 256 * (f & 1), BF(st));
+                if (++st == NB) {
+                    st = 0;
+                    ph ^= 1;
+                }
+            }
+            if (!ok)
+                for (int u = max(0, f - NB); u < f; u++) mbar_wait(BF(u % NB), (u / NB) & 1);
         } else if (lane == 0) {
             int kb = 0, st = 0;
             uint32_t ph = 0;
@@ -1028,7 +1066,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                     break;
                 }
                 mbar_expect_tx(BF(st), (uint32_t)(terms * b_rows * kBK * 2));
-                uint8_t *dst = b_st + (size_t)st * terms * bn * kBK * 2;
+                uint8_t *dst = b_st + (size_t)st * b_sbytes;
                 for (int r0 = 0; r0 < b_rows; r0 += p.box_rows) {  // a tensor-map box is at most 256 rows
                     const int kx = (4 * ch0 + kb) * kBK;
                     tma_2d(smem_u32(dst + (size_t)r0 * kBK * 2), &xmap, kx, t_begin + tok0 + r0, BF(st));
@@ -1079,13 +1117,50 @@ __global__ void __launch_bounds__(kThreads, 1)
         const uint32_t acc = tmem + (uint32_t)w * acc_cols;
         {
             const uint64_t da0 = sw128_desc(smem_u32(a_st)), db0 = sw128_desc(smem_u32(b_st));
-            const uint64_t a_step = (uint64_t)(kBM * kBK * 2) >> 4, b_step = (uint64_t)(terms * bn * kBK * 2) >> 4;
+            const uint64_t a_step = (uint64_t)(kBM * kBK * 2) >> 4, b_step = (uint64_t)b_sbytes >> 4;
             const uint64_t h_step = (uint64_t)(256 * kBK * 2) >> 4;
             // A stage of k-block kb = w; activation stage sb of stage index bi (k-blocks bi * KPS ..)
             int sa = w, sb = 0, bi = 0;
             uint32_t aph = 0, bph = 0;
             const uint64_t bs_step = b_step << KL;
-            for (int kb = w; kb < nkb; kb += MW) {
+            // the 512-token tile (one issuer, A in shared memory): half h of
+            // k-block kb is activation stage 2 kb + h, released once its
+            // four MMAs are done; each half's N covers only its live tokens
+            const int nlive = (live + 15) / 16 * 16;
+            const int n0 = min(256, nlive), n1 = min(256, max(0, nlive - 256));
+            const uint32_t id0 = idesc_f16(max(n0, 16)), id1 = idesc_f16(max(n1, 16));
+            for (int kb = 0; BH == 2 && kb < nkb; kb++) {
+                if (!__all_sync(0xffffffffu, mbar_wait(AF(sa), aph))) {
+                    ok = false;
+                    break;
+                }
+                const uint64_t da = da0 + (uint64_t)sa * a_step;
+                for (int h = 0; h < 2 && ok; h++) {
+                    if (!__all_sync(0xffffffffu, mbar_wait(BF(sb), bph))) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    const uint64_t db = db0 + (uint64_t)sb * b_step;
+                    if ((h ? n1 : n0) > 0)
+#pragma unroll
+                        for (int k = 0; k < kBK / 16; k++)
+                            umma_f16(acc + (uint32_t)(h * 256), da + 2 * k, db + 2 * k, h ? id1 : id0,
+                                     (kb || k) ? 1u : 0u);
+                    umma_commit(BE(sb));
+                    if (++sb == NB) {
+                        sb = 0;
+                        bph ^= 1;
+                    }
+                }
+                if (!ok) break;
+                umma_commit(AE(sa));
+                if (++sa == NA) {
+                    sa = 0;
+                    aph ^= 1;
+                }
+            }
+            for (int kb = w; BH == 1 && kb < nkb; kb += MW) {
                 for (; bi < (kb >> KL); bi++)
                     if (++sb == NB) {
                         sb = 0;
@@ -1379,10 +1454,10 @@ cudaError_t act_map4(CUtensorMap *map, const void *xh, int rows, int64_t k, int 
 }  // namespace
 
 int gemm_bn(int dt, int t_rows) {
-    // 512 tokens: two N = 256 accumulators fill tensor memory, so each weight
-    // tile is dequantised once per 512 tokens (the larger chunks of Q8_0 and
-    // Q6_K leave no room for the 2 x 64 KB activation stages)
-    if (t_rows >= 512 && dt != GGUF_Q8_0 && dt != GGUF_Q6_K) return 512;
+    // over 256 tokens: 512-token tiles, whose two N = 256 accumulators fill
+    // tensor memory, so each weight tile is dequantised once per 512 tokens
+    // (a tile's MMAs cover only its live tokens)
+    if (t_rows > 256) return 512;
     if (t_rows >= 256) return 256;
     int bn = (t_rows + 15) / 16 * 16;
     return bn < 16 ? 16 : bn;

@@ -102,7 +102,7 @@ def gemm_operand_model(dt, w, x, n, k):
 
 @pytest.mark.parametrize("dt", KQ)
 @pytest.mark.parametrize("n,k,m", [(1024, 4096, 16), (2048, 4096, 128), (1024, 14336, 64), (512, 2048, 300),
-                                   (256, 1024, 520)])
+                                   (2048, 4096, 384), (256, 1024, 520)])
 def test_prefill_gemm_against_oracle(ctx, dt, n, k, m):
     rng = np.random.default_rng(2000 + m)
     w = synth.weights(dt, n, k, rng)
