@@ -432,7 +432,7 @@ def baseline_configs_section(args, dev, stream, ctx, hbm):
     return out
 
 
-def moe_section(args, rank, world, dev, stream, ctx):
+def moe_section(args, rank, world, dev, stream, ctx, calls=0):
     """Mixtral-shaped MoE FFN: 8 experts of Q4_K gate/up 14336x4096 and down
     4096x14336, 256 tokens, top-2 from softmax of N(0,1) router logits.
     Experts are placed world-ways (8/world per GPU); every GPU routes all
@@ -466,6 +466,12 @@ def moe_section(args, rank, world, dev, stream, ctx):
         if world > 1:
             dist.all_reduce(out)
 
+    if calls:  # profiling: the calls only, no timing
+        with torch.cuda.stream(stream):
+            for _ in range(calls):
+                one()
+        stream.synchronize()
+        return None
     with torch.cuda.stream(stream):
         for _ in range(3):
             one()
@@ -537,6 +543,8 @@ def main():
     ap.add_argument("--no-group", action="store_true",
                     help="one launch per matrix (no grouped q/k/v and gate/up launches)")
     ap.add_argument("--profile", action="store_true", help="short run for ncu: warm-up + steps only")
+    ap.add_argument("--profile-moe", action="store_true",
+                    help="for ncu: only the configs[4] MoE FFN on one GPU, warm-up + steps calls (five launches each)")
     ap.add_argument("--profile-prefill", type=int, default=0, metavar="M",
                     help="for ncu: only the configs[2] prefill matmul at M tokens, warm-up + steps launches")
     ap.add_argument("--profile-gemv", default="", metavar="FORMAT",
@@ -584,6 +592,11 @@ def main():
             R.mm_batched_device(x, w, y)
         torch.cuda.synchronize(dev)
         print(json.dumps({"profile_gemv": args.profile_gemv, "launches": args.warmup + args.steps}))
+        return
+    if args.profile_moe:
+        stream = torch.cuda.Stream(dev)
+        moe_section(args, 0, 1, dev, stream, R.default_context(dev.index), calls=args.warmup + args.steps)
+        print(json.dumps({"profile_moe": True, "calls": args.warmup + args.steps}))
         return
     if args.profile_prefill:
         from rce_b200 import synth
