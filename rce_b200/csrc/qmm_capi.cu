@@ -511,13 +511,38 @@ void clear_graphs(RceThreadState *ts) {
 // Records rce_qmm_mm_batched's device steps for w and t_rows on the thread's
 // staging buffers (copy in, matmul into the pinned buffer) as an executable
 // graph.
+// Copies a host call's activations from the pinned staging buffer (mapped
+// into the device's address space) to the device buffer.  It releases its
+// dependent grid at once, so the matmul launched after it (programmatic
+// stream serialisation) starts streaming its weights while the activations
+// cross the bus; the matmul reads them only after its grid-dependency wait.
+__global__ void __launch_bounds__(256) stage_in_kernel(const float *src, float *dst, size_t n) {
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+    const size_t stride = (size_t)gridDim.x * blockDim.x;
+    size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if ((reinterpret_cast<uintptr_t>(src) & 15) == 0 && (reinterpret_cast<uintptr_t>(dst) & 15) == 0) {
+        const size_t n4 = n / 4;
+        for (size_t j = i; j < n4; j += stride)
+            reinterpret_cast<float4 *>(dst)[j] = reinterpret_cast<const float4 *>(src)[j];
+        for (size_t j = 4 * n4 + i; j < n; j += stride) dst[j] = src[j];
+    } else {
+        for (; i < n; i += stride) dst[i] = src[i];
+    }
+}
+
 int record_host_call(rce_qmm_ctx *ctx, RceThreadState *ts, const rce_qmm_weight *w, size_t t_rows,
                      cudaGraphExec_t *exec) {
     *exec = nullptr;
     const size_t k = (size_t)w->g.n_cols, n = (size_t)w->g.n_rows;
     cudaGraph_t graph = nullptr;
     CUDA_TRY(cudaStreamBeginCapture(ts->stream, cudaStreamCaptureModeThreadLocal));
-    cudaError_t e = cudaMemcpyAsync(ts->d_in, ts->h_pin, t_rows * k * sizeof(float), cudaMemcpyHostToDevice, ts->stream);
+    // the activations in by a kernel (not a copy node), so that the matmul's
+    // weight stream overlaps their transfer
+    const size_t in_f = t_rows * k;
+    unsigned blocks = (unsigned)((in_f / 4 + 255) / 256);
+    blocks = blocks < 1 ? 1 : (blocks > 8 ? 8 : blocks);
+    stage_in_kernel<<<blocks, 256, 0, ts->stream>>>(static_cast<const float *>(ts->h_pin), ts->d_in, in_f);
+    cudaError_t e = cudaGetLastError();
     // the matmul writes its (small, decode-sized) output straight into the
     // pinned staging buffer (mapped into the device's address space): no
     // device-to-host copy after it
