@@ -509,7 +509,8 @@ void clear_graphs(RceThreadState *ts) {
 }
 
 // Records rce_qmm_mm_batched's device steps for w and t_rows on the thread's
-// staging buffers (copy in, matmul into the pinned buffer) as an executable
+// staging buffers (activations in by stage_in_kernel, matmul into the pinned
+// buffer) as an executable
 // graph.
 // Copies a host call's activations from the pinned staging buffer (mapped
 // into the device's address space) to the device buffer.  It releases its
