@@ -508,10 +508,6 @@ void clear_graphs(RceThreadState *ts) {
     ts->graphs.clear();
 }
 
-// Records rce_qmm_mm_batched's device steps for w and t_rows on the thread's
-// staging buffers (activations in by stage_in_kernel, matmul into the pinned
-// buffer) as an executable
-// graph.
 // Copies a host call's activations from the pinned staging buffer (mapped
 // into the device's address space) to the device buffer.  It releases its
 // dependent grid at once, so the matmul launched after it (programmatic
@@ -531,6 +527,9 @@ __global__ void __launch_bounds__(256) stage_in_kernel(const float *src, float *
     }
 }
 
+// Records rce_qmm_mm_batched's device steps for w and t_rows on the thread's
+// staging buffers (activations in by stage_in_kernel, matmul into the pinned
+// buffer) as an executable graph.
 int record_host_call(rce_qmm_ctx *ctx, RceThreadState *ts, const rce_qmm_weight *w, size_t t_rows,
                      cudaGraphExec_t *exec) {
     *exec = nullptr;
