@@ -48,9 +48,11 @@ SIGNATURES = {
     "rce_qmm_weight_info": (_int, [_vp, _c.POINTER(_int), _c.POINTER(_i64), _c.POINTER(_i64), _c.POINTER(_sz)]),
     "rce_qmm_weight_device_storage": (_int, [_vp, _vpp, _c.POINTER(_sz)]),
     "rce_qmm_weight_read_bytes": (_int, [_vp, _vp, _sz]),
-    "rce_qmm_mm_1d": (_int, [_vp, _f32p, _sz, _vp, _f32p, _sz]),
+    # (the per-token host calls take plain addresses: building a typed
+    # pointer costs several microseconds a call)
+    "rce_qmm_mm_1d": (_int, [_vp, _vp, _sz, _vp, _vp, _sz]),
     "rce_qmm_mm_1d_serial": (_int, [_vp, _f32p, _sz, _vp, _f32p, _sz]),
-    "rce_qmm_mm_batched": (_int, [_vp, _f32p, _sz, _vp, _f32p, _sz]),
+    "rce_qmm_mm_batched": (_int, [_vp, _vp, _sz, _vp, _vp, _sz]),
     "rce_qmm_mm_batched_device": (_int, [_vp, _vp, _sz, _sz, _vp, _vp, _sz, _vp]),
     "rce_qmm_mm_batched_device_noalloc": (_int, [_vp, _vp, _sz, _sz, _vp, _vp, _sz, _vp]),
     "rce_qmm_mm_batched_device_multi": (_int, [_vp, _vp, _sz, _sz, _vp, _sz, _vp, _vp, _vp]),
@@ -97,6 +99,9 @@ class Unsupported(QmmError):
 def lib():
     """Load librce_qmm.so once; raise if it is missing (no CPU fallback)."""
     global _lib
+    loaded = _lib
+    if loaded is not None:  # (no lock once loaded: this runs on every call)
+        return loaded
     with _lock:
         if _lib is None:
             if not os.path.exists(LIB_PATH):

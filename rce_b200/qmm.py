@@ -110,6 +110,12 @@ def _fptr(arr: np.ndarray):
     return arr.ctypes.data_as(ctypes.POINTER(ctypes.c_float))
 
 
+def _addr(arr: np.ndarray) -> int:
+    """The array's data address (for the hot host calls, whose pointer
+    arguments are declared void *: cheaper than a typed ctypes pointer)."""
+    return arr.ctypes.data
+
+
 class QuantWeight:
     """A weight in its native GGUF dtype, registered once on the device.
 
@@ -250,7 +256,7 @@ def mm_1d(a, w: QuantWeight, out: Optional[np.ndarray] = None) -> np.ndarray:
         out = np.empty(w.n_rows, dtype=np.float32)
     if out.dtype != np.float32 or not out.flags.c_contiguous or out.size < w.n_rows:
         raise ValueError("output buffer too small")
-    check(lib().rce_qmm_mm_1d(w.ctx.handle, _fptr(a), a.size, w.handle, _fptr(out), out.size))
+    check(lib().rce_qmm_mm_1d(w.ctx.handle, _addr(a), a.size, w.handle, _addr(out), out.size))
     return out
 
 
@@ -275,7 +281,7 @@ def mm_batched(a, t_rows: int, w: QuantWeight, out: Optional[np.ndarray] = None)
         out = np.empty(t_rows * w.n_rows, dtype=np.float32)
     if out.dtype != np.float32 or not out.flags.c_contiguous or out.size < t_rows * w.n_rows:
         raise ValueError("output buffer too small")
-    check(lib().rce_qmm_mm_batched(w.ctx.handle, _fptr(a), int(t_rows), w.handle, _fptr(out), out.size))
+    check(lib().rce_qmm_mm_batched(w.ctx.handle, _addr(a), int(t_rows), w.handle, _addr(out), out.size))
     return out
 
 
